@@ -1,0 +1,55 @@
+"""ctypes binding of libda3b.so (the native library built in-tree by build.py).
+
+The library is the product: every compute call goes through it. If it is missing
+the import raises instead of falling back to anything else.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libda3b.so")
+
+_lib = None
+
+c_int = ctypes.c_int
+c_float = ctypes.c_float
+c_void_p = ctypes.c_void_p
+c_char_p = ctypes.c_char_p
+c_size_t = ctypes.c_size_t
+
+# name -> (restype, argtypes); one entry per symbol of include/da3b.h and include/da3cpp/da3_c.h
+SIGNATURES = {
+    "da3b_abi_version": (c_int, []),
+    "da3b_device_status": (c_int, []),
+    "da3b_dequant_q8_0": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
+    "da3b_linear_f16": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int,
+                                c_void_p, c_int, c_void_p]),
+    "da3b_linear_resid_f32": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p,
+                                      c_void_p, c_int, c_void_p]),
+    "da3b_pack_conv_weight": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "da3b_conv_nhwc": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p,
+                               c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
+}
+
+
+def load() -> ctypes.CDLL:
+    """Load libda3b.so (raises OSError when it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise OSError(f"libda3b.so not built at {LIB_PATH}; run `python da3cpplib_b200/build.py`")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed with status {rc}")

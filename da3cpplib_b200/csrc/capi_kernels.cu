@@ -1,0 +1,113 @@
+// Kernel-level C ABI (include/da3b.h): thin validated wrappers over the launchers.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "da3b.h"
+#include "ops.h"
+
+namespace da3b {
+
+// w_f32: torch conv layout [OC][IC][k][k]; out: [OC][k*k][icp] f16, zero padded.
+__global__ void k_pack_conv(const float* __restrict__ w, int OC, int IC, int ks, int icp, __half* __restrict__ out) {
+  const long total = static_cast<long>(OC) * ks * ks * icp;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int ic = static_cast<int>(i % icp);
+    const int tap = static_cast<int>((i / icp) % (ks * ks));
+    const int oc = static_cast<int>(i / (static_cast<long>(icp) * ks * ks));
+    float v = 0.f;
+    if (ic < IC) v = w[(static_cast<size_t>(oc) * IC + ic) * ks * ks + tap];
+    out[i] = __float2half_rn(v);
+  }
+}
+
+int pack_conv_weight(const float* w, int OC, int IC, int ks, __half* out, cudaStream_t s) {
+  const int icp = conv_icp(IC);
+  const long total = static_cast<long>(OC) * ks * ks * icp;
+  const int threads = 256;
+  long blocks = (total + threads - 1) / threads;
+  if (blocks > 65535) blocks = 65535;
+  k_pack_conv<<<static_cast<unsigned>(blocks), threads, 0, s>>>(w, OC, IC, ks, icp, out);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace da3b
+
+using namespace da3b;
+
+extern "C" {
+
+DA3B_API int da3b_abi_version(void) { return 1; }
+
+DA3B_API int da3b_device_status(void) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  int* w = device_status_word();
+  if (!w) return -2;
+  int st = 0;
+  if (read_and_reset_status(w, &st)) return -3;
+  return st;
+}
+
+DA3B_API int da3b_dequant_q8_0(const void* q8, int rows, int K, void* w_f16, int ldw, void* stream) {
+  if (!q8 || !w_f16) return -100;
+  return dequant_q8_0(q8, rows, K, static_cast<__half*>(w_f16), ldw, static_cast<cudaStream_t>(stream));
+}
+
+DA3B_API int da3b_linear_f16(const void* x, int M, int K, int lda, const void* w, int N, int ldw, const float* bias,
+                             int act, void* out, int ldo, void* stream) {
+  if (!x || !w || !out || act < 0 || act > 2) return -100;
+  int* st = device_status_word();
+  if (!st) return -101;
+  EpiArgs e = epi_default();
+  e.kind = kEpiF16;
+  e.act = act;
+  e.bias = bias;
+  e.out = static_cast<__half*>(out);
+  e.ld_out = ldo;
+  return gemm_linear(static_cast<const __half*>(x), M, K, lda, static_cast<const __half*>(w), N, ldw, 0, e, st,
+                     static_cast<cudaStream_t>(stream));
+}
+
+DA3B_API int da3b_linear_resid_f32(const void* x, int M, int K, int lda, const void* w, int N, int ldw,
+                                   const float* bias, const float* scale, float* resid, int ldr, void* stream) {
+  if (!x || !w || !resid) return -100;
+  int* st = device_status_word();
+  if (!st) return -101;
+  EpiArgs e = epi_default();
+  e.kind = kEpiResid;
+  e.bias = bias;
+  e.scale = scale;
+  e.resid = resid;
+  e.ld_resid = ldr;
+  return gemm_linear(static_cast<const __half*>(x), M, K, lda, static_cast<const __half*>(w), N, ldw, 0, e, st,
+                     static_cast<cudaStream_t>(stream));
+}
+
+DA3B_API int da3b_pack_conv_weight(const float* w_f32, int OC, int IC, int ksize, void* w_packed, void* stream) {
+  if (!w_f32 || !w_packed || OC <= 0 || IC <= 0 || ksize <= 0) return -100;
+  return pack_conv_weight(w_f32, OC, IC, ksize, static_cast<__half*>(w_packed), static_cast<cudaStream_t>(stream));
+}
+
+DA3B_API int da3b_conv_nhwc(const void* x, int B, int H, int W, int IC, const void* w_packed, int OC, int ksize,
+                            const float* bias, const void* res1, const void* res2, int act, void* out, void* out_relu,
+                            void* stream) {
+  if (!x || !w_packed || !out || act < 0 || act > 2) return -100;
+  int* st = device_status_word();
+  if (!st) return -101;
+  EpiArgs e = epi_default();
+  e.kind = kEpiF16;
+  e.act = act;
+  e.bias = bias;
+  e.out = static_cast<__half*>(out);
+  e.ld_out = OC;
+  e.out_relu = static_cast<__half*>(out_relu);
+  e.res1 = static_cast<const __half*>(res1);
+  e.ld_res1 = OC;
+  e.res2 = static_cast<const __half*>(res2);
+  e.ld_res2 = OC;
+  return conv_nhwc(static_cast<const __half*>(x), B, H, W, IC, static_cast<const __half*>(w_packed), OC, ksize, 0, e,
+                   st, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,558 @@
+// Persistent warp-specialised tcgen05 GEMM / implicit-GEMM convolution for sm_100a.
+//
+// Roles (192 threads, one CTA per SM, grid = min(#tiles, #SMs)):
+//   warp 0       TMA producer: streams A/B k-blocks into a kStages-deep ring of
+//                128B-swizzled shared-memory stages (mbarrier full/empty pairs);
+//   warp 1       MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, K=16) into
+//                one of two TMEM accumulators, commits stage releases and
+//                "accumulator full" events;
+//   warps 2..5   epilogue: tcgen05.ld the accumulator (each warp owns its 32-lane
+//                TMEM quarter), apply the fused epilogue, store to global, and
+//                release the accumulator so the MMA of the next tile overlaps.
+// Tiles are visited m-major (all N tiles of one 128-row A panel back to back) so an
+// A panel is read from HBM about once while the weights stay resident in L2.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "gemm.h"
+#include "ops.h"
+#include "ptx.cuh"
+
+namespace da3b {
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kABytes = 128 * 64 * 2;
+  static constexpr int kBBytes = BN * 64 * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
+  static constexpr int kAccCols = (BN < 32) ? 32 : BN;
+  static constexpr int kTmemCols = (2 * kAccCols <= 64) ? 64 : (2 * kAccCols <= 128 ? 128 : (2 * kAccCols <= 256 ? 256 : 512));
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
+};
+
+__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  if (act == kActRelu) return fmaxf(v, 0.0f);
+  if (act == kActGelu) return gelu_erf(v);
+  return v;
+}
+
+__device__ __forceinline__ float out_act(float l, int a, float scale) {
+  switch (a) {
+    case kOutRelu: return fmaxf(l, 0.0f);
+    case kOutSigmoidScale: return scale / (1.0f + expf(-l));
+    case kOutExp: return expf(l);
+    case kOutExpP1: return expf(l) + 1.0f;
+    default: return l;
+  }
+}
+
+__device__ __forceinline__ void load_h8(const __half* p, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store_h8(__half* p, const float* v) {
+  uint4 u;
+  __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+__device__ __forceinline__ int remap_row(const EpiArgs& e, int row) {
+  return e.rm_div > 0 ? (row / e.rm_div) * e.rm_mul + e.rm_add + row % e.rm_div : row;
+}
+
+// Epilogue for 32 accumulator columns [n_base, n_base+32) of one output row.
+// `row` is the GEMM row (linear row, or output pixel index in conv mode).
+__device__ __forceinline__ void epilogue32(const GemmGeom& g, const EpiArgs& e, int row, int n_base, float (&v)[32]) {
+  const int nvalid = min(32, g.N - n_base);
+  if (nvalid <= 0) return;
+  switch (e.kind) {
+    case kEpiF16: {
+      const int orow = remap_row(e, row);
+      for (int j0 = 0; j0 < nvalid; j0 += 8) {  // N % 8 == 0 is enforced by the host
+        float t[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t[i] = v[j0 + i] + (e.bias ? __ldg(e.bias + n_base + j0 + i) : 0.0f);
+        if (e.res1) {
+          const int r1 = e.res1_mod > 0 ? orow % e.res1_mod : orow;
+          float s[8];
+          load_h8(e.res1 + static_cast<size_t>(r1) * e.ld_res1 + n_base + j0, s);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) t[i] += s[i];
+        }
+        if (e.res2) {
+          float s[8];
+          load_h8(e.res2 + static_cast<size_t>(orow) * e.ld_res2 + n_base + j0, s);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) t[i] += s[i];
+        }
+        if (e.out_relu) {
+          float q[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) q[i] = fmaxf(t[i], 0.0f);
+          store_h8(e.out_relu + static_cast<size_t>(orow) * e.ld_out + n_base + j0, q);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t[i] = apply_act(t[i], e.act);
+        store_h8(e.out + static_cast<size_t>(orow) * e.ld_out + n_base + j0, t);
+      }
+      break;
+    }
+    case kEpiResid: {
+      const int orow = remap_row(e, row);
+      float* p = e.resid + static_cast<size_t>(orow) * e.ld_resid + n_base;
+      for (int j0 = 0; j0 < nvalid; j0 += 4) {
+        float4 x = *reinterpret_cast<float4*>(p + j0);
+        float t[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int n = n_base + j0 + i;
+          const float a = v[j0 + i] + (e.bias ? __ldg(e.bias + n) : 0.0f);
+          t[i] = e.scale ? __ldg(e.scale + n) * a : a;
+        }
+        x.x += t[0]; x.y += t[1]; x.z += t[2]; x.w += t[3];
+        *reinterpret_cast<float4*>(p + j0) = x;
+      }
+      break;
+    }
+    case kEpiTokens: {
+      const int orow = remap_row(e, row);
+      const int prow = 1 + row % e.rm_div;
+      float* p = e.resid + static_cast<size_t>(orow) * e.ld_resid + n_base;
+      const float* pp = e.pos + static_cast<size_t>(prow) * g.N + n_base;
+      for (int j0 = 0; j0 < nvalid; j0 += 4) {
+        float4 x;
+        x.x = v[j0 + 0] + __ldg(e.bias + n_base + j0 + 0) + __ldg(pp + j0 + 0);
+        x.y = v[j0 + 1] + __ldg(e.bias + n_base + j0 + 1) + __ldg(pp + j0 + 1);
+        x.z = v[j0 + 2] + __ldg(e.bias + n_base + j0 + 2) + __ldg(pp + j0 + 2);
+        x.w = v[j0 + 3] + __ldg(e.bias + n_base + j0 + 3) + __ldg(pp + j0 + 3);
+        *reinterpret_cast<float4*>(p + j0) = x;
+      }
+      break;
+    }
+    case kEpiConvT: {
+      const int hw = e.ct_hin * e.ct_win;
+      const int b = row / hw, rem = row % hw;
+      const int y = rem / e.ct_win, x = rem % e.ct_win;
+      const int S = e.ct_s;
+      const int hout = e.ct_hin * S, wout = e.ct_win * S;
+      for (int j0 = 0; j0 < nvalid; j0 += 8) {
+        const int n = n_base + j0;
+        const int grp = n / e.ct_oc, oc = n % e.ct_oc;
+        const int ky = grp / S, kx = grp % S;
+        const size_t opix = (static_cast<size_t>(b) * hout + (S * y + ky)) * wout + (S * x + kx);
+        float t[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t[i] = v[j0 + i] + (e.bias ? __ldg(e.bias + oc + i) : 0.0f);
+        store_h8(e.out + opix * e.ld_out + oc, t);
+      }
+      break;
+    }
+    case kEpiOut2: {
+      // out2a channels (N == 32) -> [channels-last LayerNorm] -> relu -> out2b 1x1 -> activation
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += e.bias ? __ldg(e.bias + j) : 0.0f;
+      if (e.o2_ln_g) {
+        float mean = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mean += v[j];
+        mean *= (1.0f / 32.0f);
+        float var = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) { const float d = v[j] - mean; var += d * d; }
+        var *= (1.0f / 32.0f);
+        const float rstd = rsqrtf(var + e.o2_ln_eps);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = (v[j] - mean) * rstd * __ldg(e.o2_ln_g + j) + __ldg(e.o2_ln_b + j);
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+      for (int od = 0; od < e.o2_dim; ++od) {
+        float l = __ldg(e.o2_b + od);
+        const float* w = e.o2_w + od * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) l = fmaf(v[j], __ldg(w + j), l);
+        e.o2_out[od][row] = out_act(l, e.o2_act[od], e.o2_scale);
+      }
+      break;
+    }
+    default: break;
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    k_tc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmGeom g,
+              const EpiArgs e, int* status) {
+  using Cfg = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + Cfg::kStages * Cfg::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  uint64_t* empty = full + Cfg::kStages;
+  uint64_t* tfull = empty + Cfg::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = g.num_m_tiles * g.num_n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int mt = t / g.num_n_tiles, nt = t % g.num_n_tiles;
+        const int n0 = nt * BN;
+        int cb = 0, cx = 0, cy = 0;
+        if (g.mode == kModeConv) {
+          const int per_img = g.tiles_x * g.tiles_y;
+          cb = mt / per_img;
+          const int rem = mt % per_img;
+          cy = (rem / g.tiles_x) * g.bh;
+          cx = (rem % g.tiles_x) * g.bw;
+        }
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, status, kStatusTimeoutEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          uint8_t* a_dst = sA + stage * Cfg::kABytes;
+          uint8_t* b_dst = sB + stage * Cfg::kBBytes;
+          if (g.mode == kModeConv) {
+            const int tap = kb / g.ic_chunks;
+            const int ic0 = (kb % g.ic_chunks) * 64;
+            const int dy = tap / g.ksize - g.pad, dx = tap % g.ksize - g.pad;
+            tma_load_4d(a_dst, &tmA, &full[stage], ic0, cx + dx, cy + dy, cb);
+            tma_load_2d(b_dst, &tmB, &full[stage], tap * g.icp + ic0, n0);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * 64, mt * 128);
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * 64, n0);
+          }
+          if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = umma_idesc_f16(128, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, status, kStatusTimeoutAccumFree)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccCols;
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, status, kStatusTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_sw128(smem_u32(sA + stage * Cfg::kABytes));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * Cfg::kBBytes));
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[stage]);
+          if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      const int mt = t / g.num_n_tiles, nt = t % g.num_n_tiles;
+      int row = -1;
+      if (g.mode == kModeConv) {
+        const int per_img = g.tiles_x * g.tiles_y;
+        const int b = mt / per_img, rem = mt % per_img;
+        const int y = (rem / g.tiles_x) * g.bh + r / g.bw;
+        const int x = (rem % g.tiles_x) * g.bw + r % g.bw;
+        if (y < g.H && x < g.W) row = (b * g.H + y) * g.W + x;
+      } else {
+        const int m = mt * 128 + r;
+        if (m < g.M) row = m;
+      }
+      if (!mbar_wait(&tfull[acc], acc_phase, status, kStatusTimeoutAccum)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t raw[32];
+        tmem_ld32(tbase + c, raw);
+        tmem_wait_ld();
+        if (row >= 0) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
+          epilogue32(g, e, row, nt * BN + c, v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+typedef CUresult (*PFN_tmapEncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                        const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                        CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                        CUtensorMapFloatOOBfill);
+
+static PFN_tmapEncodeTiled tmap_encoder() {
+  static PFN_tmapEncodeTiled fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_tmapEncodeTiled>(p);
+  }
+  return fn;
+}
+
+// 2-D f16 tensor map over a row-major [rows][cols] matrix with leading dimension ld
+// (elements), box = 64 columns x box_rows rows, 128B swizzle, zero fill out of range.
+int make_tmap_2d(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows) {
+  PFN_tmapEncodeTiled enc = tmap_encoder();
+  if (!enc) return -1;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 2) % 16 || box_rows > 256 || box_rows < 1) return -2;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -3;
+}
+
+// 4-D f16 tensor map over an NHWC tensor [B][H][W][C] (row pitch C), box =
+// 64 channels x bw x bh x 1, 128B swizzle, zero fill out of range (conv padding).
+int make_tmap_nhwc(CUtensorMap* map, const void* ptr, int B, int H, int W, int C, int bw, int bh) {
+  PFN_tmapEncodeTiled enc = tmap_encoder();
+  if (!enc) return -1;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (C * 2) % 16) return -2;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(C) * 2, static_cast<cuuint64_t>(C) * 2 * W,
+                           static_cast<cuuint64_t>(C) * 2 * W * H};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(bw), static_cast<cuuint32_t>(bh), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -3;
+}
+
+static int g_num_sms = 0;
+static int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+template <int BN>
+static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeom& g, const EpiArgs& e, int* status,
+                     cudaStream_t stream, int max_ctas) {
+  using Cfg = GemmCfg<BN>;
+  static uint64_t attr_set = 0;  // one bit per device ordinal
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!((attr_set >> (dev & 63)) & 1)) {
+    if (cudaFuncSetAttribute(k_tc_gemm<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
+        cudaSuccess)
+      return -10;
+    attr_set |= uint64_t(1) << (dev & 63);
+  }
+  const int tiles = g.num_m_tiles * g.num_n_tiles;
+  int grid = num_sms();
+  if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
+  if (tiles < grid) grid = tiles;
+  if (grid <= 0) return 0;
+  k_tc_gemm<BN><<<grid, 192, Cfg::kSmemBytes, stream>>>(ta, tb, g, e, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+}
+
+// Launch with a validated geometry. BN in {32, 64, 128, 256}.
+int gemm_launch(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeom& g, const EpiArgs& e,
+                int* status, cudaStream_t stream, int max_ctas) {
+  switch (bn) {
+    case 32: return launch_bn<32>(ta, tb, g, e, status, stream, max_ctas);
+    case 64: return launch_bn<64>(ta, tb, g, e, status, stream, max_ctas);
+    case 128: return launch_bn<128>(ta, tb, g, e, status, stream, max_ctas);
+    case 256: return launch_bn<256>(ta, tb, g, e, status, stream, max_ctas);
+    default: return -12;
+  }
+}
+
+EpiArgs epi_default() {
+  EpiArgs e;
+  memset(&e, 0, sizeof(e));
+  e.kind = kEpiF16;
+  e.o2_ln_eps = 1e-5f;
+  e.o2_scale = 1.0f;
+  return e;
+}
+
+int pick_bn(int N) {
+  if (N <= 32) return 32;
+  if (N <= 64) return 64;
+  if (N <= 128) return 128;
+  return 256;
+}
+
+static int check_epi(const EpiArgs& e, int N) {
+  if (e.kind == kEpiF16 || e.kind == kEpiConvT) {
+    if (N % 8 || !e.out || e.ld_out % 8 || (reinterpret_cast<uintptr_t>(e.out) & 15)) return -20;
+    if (e.out_relu && (reinterpret_cast<uintptr_t>(e.out_relu) & 15)) return -21;
+    if (e.res1 && (e.ld_res1 % 8 || (reinterpret_cast<uintptr_t>(e.res1) & 15))) return -22;
+    if (e.res2 && (e.ld_res2 % 8 || (reinterpret_cast<uintptr_t>(e.res2) & 15))) return -23;
+  }
+  if (e.kind == kEpiResid || e.kind == kEpiTokens) {
+    if (N % 4 || !e.resid || e.ld_resid % 4 || (reinterpret_cast<uintptr_t>(e.resid) & 15)) return -24;
+    if (e.kind == kEpiTokens && (!e.pos || !e.bias || e.rm_div <= 0)) return -25;
+  }
+  if (e.kind == kEpiConvT && (e.ct_oc % 8 || e.ct_s <= 0 || e.ct_hin <= 0 || e.ct_win <= 0)) return -26;
+  if (e.kind == kEpiOut2) {
+    if (N != 32 || e.o2_dim < 1 || e.o2_dim > 8 || !e.o2_w || !e.o2_b) return -27;
+    for (int i = 0; i < e.o2_dim; ++i)
+      if (!e.o2_out[i]) return -28;
+  }
+  return 0;
+}
+
+int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, int ldw, int bn, const EpiArgs& e,
+                int* status, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return M == 0 ? 0 : -30;
+  if (lda < K || ldw < K || lda % 8 || ldw % 8) return -31;
+  if (bn <= 0) bn = pick_bn(N);
+  if (e.kind == kEpiOut2) bn = 32;
+  int rc = check_epi(e, N);
+  if (rc) return rc;
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap_2d(&ta, A, M, K, lda, 128))) return rc - 100;
+  if ((rc = make_tmap_2d(&tb, W, N, K, ldw, bn))) return rc - 200;
+  GemmGeom g;
+  memset(&g, 0, sizeof(g));
+  g.mode = kModeLinear;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.num_kb = (K + 63) / 64;
+  g.num_m_tiles = (M + 127) / 128;
+  g.num_n_tiles = (N + bn - 1) / bn;
+  return gemm_launch(bn, ta, tb, g, e, status, stream, 0);
+}
+
+// Pixel block of one 128-row M tile: the (bw, bh) with bw * bh == 128 that wastes
+// the fewest padded pixels on an H x W map.
+static void pick_block(int H, int W, int* bw, int* bh) {
+  static const int cand[6][2] = {{16, 8}, {8, 16}, {32, 4}, {4, 32}, {64, 2}, {128, 1}};
+  long best = -1;
+  for (auto& c : cand) {
+    const long cover = static_cast<long>((W + c[0] - 1) / c[0]) * c[0] * ((H + c[1] - 1) / c[1]) * c[1];
+    if (best < 0 || cover < best) {
+      best = cover;
+      *bw = c[0];
+      *bh = c[1];
+    }
+  }
+}
+
+int conv_nhwc(const __half* X, int B, int H, int W, int IC, const __half* Wp, int OC, int ksize, int bn,
+              const EpiArgs& e, int* status, cudaStream_t stream) {
+  if (B <= 0 || H <= 0 || W <= 0 || IC <= 0 || OC <= 0 || (ksize != 1 && ksize != 3)) return -40;
+  if (IC % 8) return -41;
+  if (bn <= 0) bn = pick_bn(OC);
+  if (e.kind == kEpiOut2) bn = 32;
+  int rc = check_epi(e, OC);
+  if (rc) return rc;
+  int bw = 16, bh = 8;
+  pick_block(H, W, &bw, &bh);
+  const int icp = conv_icp(IC);
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap_nhwc(&ta, X, B, H, W, IC, bw, bh))) return rc - 100;
+  if ((rc = make_tmap_2d(&tb, Wp, OC, ksize * ksize * icp, ksize * ksize * icp, bn))) return rc - 200;
+  GemmGeom g;
+  memset(&g, 0, sizeof(g));
+  g.mode = kModeConv;
+  g.M = B * H * W;
+  g.N = OC;
+  g.K = IC;
+  g.ic_chunks = icp / 64;
+  g.icp = icp;
+  g.ksize = ksize;
+  g.pad = ksize / 2;
+  g.num_kb = ksize * ksize * g.ic_chunks;
+  g.B = B;
+  g.H = H;
+  g.W = W;
+  g.bw = bw;
+  g.bh = bh;
+  g.tiles_x = (W + bw - 1) / bw;
+  g.tiles_y = (H + bh - 1) / bh;
+  g.num_m_tiles = B * g.tiles_x * g.tiles_y;
+  g.num_n_tiles = (OC + bn - 1) / bn;
+  return gemm_launch(bn, ta, tb, g, e, status, stream, 0);
+}
+
+}  // namespace da3b

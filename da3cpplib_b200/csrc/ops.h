@@ -1,0 +1,39 @@
+// Host-side launchers of the device kernels (internal to libda3b).
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gemm.h"
+
+namespace da3b {
+
+// ------------------------------------------------------------------ GEMM engine (gemm.cu)
+int make_tmap_2d(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows);
+int make_tmap_nhwc(CUtensorMap* map, const void* ptr, int B, int H, int W, int C, int bw, int bh);
+int gemm_launch(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeom& g, const EpiArgs& e,
+                int* status, cudaStream_t stream, int max_ctas);
+
+// C[M][N] = A[M][K] * W[N][K]^T with a fused epilogue. bn <= 0 picks the N tile.
+int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, int ldw, int bn, const EpiArgs& e,
+                int* status, cudaStream_t stream);
+// Implicit-GEMM KxK stride-1 "same" convolution: X NHWC [B][H][W][IC] f16,
+// Wp packed [OC][ksize*ksize][icp] f16 (icp = IC rounded up to 64, zero padded).
+// The epilogue sees output pixel indices (b*H + y)*W + x as rows.
+int conv_nhwc(const __half* X, int B, int H, int W, int IC, const __half* Wp, int OC, int ksize, int bn,
+              const EpiArgs& e, int* status, cudaStream_t stream);
+int pick_bn(int N);
+inline int conv_icp(int IC) { return (IC + 63) / 64 * 64; }
+
+EpiArgs epi_default();
+
+// ------------------------------------------------------------------ elementwise (elementwise.cu)
+int dequant_q8_0(const void* q8, int rows, int K, __half* out, int ldo, cudaStream_t s);
+int f32_to_f16(const float* in, __half* out, size_t n, cudaStream_t s);
+
+// Per-device status word (allocated on first use for the current device).
+int* device_status_word();
+int read_and_reset_status(int* word, int* out_status);
+
+}  // namespace da3b

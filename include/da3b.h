@@ -1,0 +1,81 @@
+/*
+ * da3b.h — kernel-level C ABI of libda3b (B200 / sm_100a).
+ *
+ * These entry points are the drop-in replacement for the reference's GPU plugin
+ * point: in DA3cpplib every hot op of the depth path is a ggml graph node
+ * (ggml_mul_mat for the Q8_0 linears, ggml_flash_attn_ext, ggml_conv_2d /
+ * ggml_conv_transpose_2d_p0 / ggml_interpolate for the DPT head), and its own
+ * CUDA kernels enter ggml through a GGML_OP_CUSTOM descriptor
+ * {magic, launch(dst, stream, user), user}
+ * (scripts/patches/ggml/0001-da3-custom-cuda-ops.patch:24-38,
+ *  src/cuda_head_kernels.hpp:28-49, src/cuda_head_kernels.cu:20-25).
+ * Here each op is a flat extern "C" function taking raw device pointers, sizes
+ * and a cudaStream_t (passed as void*), returning 0 on success or a negative
+ * error code. No function allocates on the caller's behalf except where stated.
+ *
+ * Layouts: activations are row-major f16 ([rows][cols], cols fastest) or NHWC
+ * f16 ([B][H][W][C]); weights are f16 [N][K] (K fastest); biases are f32.
+ */
+#ifndef DA3B_H
+#define DA3B_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define DA3B_API __attribute__((visibility("default")))
+#else
+#define DA3B_API
+#endif
+
+/* Version of this kernel-level ABI. */
+DA3B_API int da3b_abi_version(void);
+
+/* Waits for the current device, then returns (and clears) the device-side status
+ * word that bounded waits inside the kernels write on a timeout (0 = ok). Returns
+ * a negative value if the device itself reports an error. */
+DA3B_API int da3b_device_status(void);
+
+/* Q8_0 weight repack: GGUF Q8_0 rows (K/32 blocks of {f16 d, int8 q[32]}) on the
+ * device -> f16 plane w[r][k] = d*q with leading dimension ldw (>= K, multiple of
+ * 32, zero padded). Replaces the per-call Q8_0 dequantisation inside ggml_mul_mat
+ * (src/ggml_extend.hpp:6-10) by a load-time repack. */
+DA3B_API int da3b_dequant_q8_0(const void* q8, int rows, int K, void* w_f16, int ldw, void* stream);
+
+/* Linear layer y = act(x W^T + b) (+res): the replacement of `linear()`
+ * (src/ggml_extend.hpp:6-10 -> ggml_mul_mat(W_q8_0, x) + bias) on the tcgen05 path.
+ * x: f16 [M][K] (lda), W: f16 [N][K] (ldw, from da3b_dequant_q8_0), bias f32 [N]
+ * or NULL, act: 0 none, 1 relu, 2 erf-GELU (src/ggml_extend.hpp:22-25),
+ * out: f16 [M][N] (ldo). */
+DA3B_API int da3b_linear_f16(const void* x, int M, int K, int lda, const void* w, int N, int ldw,
+                             const float* bias, int act, void* out, int ldo, void* stream);
+
+/* Residual linear: resid[m][n] += scale[n] * ((x W^T)[m][n] + bias[n]) in f32 —
+ * the ViT block's `x + ls * linear(...)` (src/vit_block.cpp:33-35, :56-57).
+ * scale may be NULL (no LayerScale). */
+DA3B_API int da3b_linear_resid_f32(const void* x, int M, int K, int lda, const void* w, int N, int ldw,
+                                   const float* bias, const float* scale, float* resid, int ldr, void* stream);
+
+/* Packs a ggml conv2d weight (ne [KW,KH,IC,OC] f32 == torch [OC][IC][KH][KW]) into
+ * the implicit-GEMM layout f16 [OC][KH*KW][icp], icp = IC rounded up to 64. */
+DA3B_API int da3b_pack_conv_weight(const float* w_f32, int OC, int IC, int ksize, void* w_packed, void* stream);
+
+/* KxK stride-1 "same" convolution (K = 1 or 3) on NHWC f16, implicit GEMM:
+ *   v = conv(x, w) + bias + res1 + res2;  out = act(v);  out_relu = relu(v) (optional)
+ * Replaces conv2d / residual_conv_unit pieces of src/dpt_blocks.cpp:18-114 and the
+ * fused kernels k_conv3x3_igemm / k_conv1x1_igemm (src/cuda_head_kernels.cu:34-164).
+ * x: [B][H][W][IC], w: packed (da3b_pack_conv_weight), res1/res2/out/out_relu:
+ * [B][H][W][OC] or NULL. */
+DA3B_API int da3b_conv_nhwc(const void* x, int B, int H, int W, int IC, const void* w_packed, int OC,
+                            int ksize, const float* bias, const void* res1, const void* res2, int act,
+                            void* out, void* out_relu, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DA3B_H */

@@ -1,0 +1,122 @@
+"""tcgen05 GEMM / implicit-GEMM conv engine vs. a plain PyTorch fp32 reference.
+
+Tolerance: |out - ref| <= 2e-3 * max|ref| + 2e-3 (f16 operands are exact in both
+paths; the difference is f32 summation order plus the f16 rounding of the output).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+V = ctypes.c_void_p
+
+
+def ptr(t):
+    return V(t.data_ptr()) if t is not None else None
+
+
+def stream():
+    return V(torch.cuda.current_stream().cuda_stream)
+
+
+def close(out, ref, rel=2e-3, abs_=2e-3):
+    out = out.float()
+    ref = ref.float()
+    err = (out - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert err <= rel * scale + abs_, f"max err {err} vs scale {scale}"
+
+
+@pytest.fixture(autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    yield
+    torch.cuda.synchronize()
+
+
+def test_dequant_q8_0_exact(lib):
+    rng = np.random.default_rng(1)
+    rows, K, ldw = 96, 384, 448
+    q = rng.integers(-127, 128, size=(rows, K // 32, 32), dtype=np.int8)
+    d = rng.uniform(1e-3, 1e-2, size=(rows, K // 32)).astype(np.float16)
+    raw = np.zeros((rows, K // 32, 34), dtype=np.uint8)
+    raw[:, :, :2] = d.view(np.uint8).reshape(rows, K // 32, 2)
+    raw[:, :, 2:] = q.view(np.uint8)
+    q8 = torch.from_numpy(raw.reshape(-1)).cuda()
+    w = torch.full((rows, ldw), 7.0, dtype=torch.float16, device="cuda")
+    assert lib.da3b_dequant_q8_0(ptr(q8), rows, K, ptr(w), ldw, stream()) == 0
+    torch.cuda.synchronize()
+    ref = (d.astype(np.float32)[:, :, None] * q.astype(np.float32)).reshape(rows, K).astype(np.float16)
+    got = w.cpu().numpy()
+    assert np.array_equal(got[:, :K].view(np.uint16), ref.view(np.uint16))
+    assert np.all(got[:, K:] == 0)
+    assert lib.da3b_device_status() == 0
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 64, 32), (127, 384, 1152), (128, 128, 64), (300, 200, 48),
+                                   (1370, 768, 2304), (2740, 1024, 4096), (1370, 4096, 1024), (257, 640, 96)])
+@pytest.mark.parametrize("act", [0, 2])
+def test_linear_f16(lib, M, K, N, act):
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + K + N)
+    lda = (K + 7) // 8 * 8
+    x = torch.randn(M, lda, device="cuda", generator=g).half()
+    w = (torch.randn(N, lda, device="cuda", generator=g) * 0.05).half()
+    b = torch.randn(N, device="cuda", generator=g).float()
+    out = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    rc = lib.da3b_linear_f16(ptr(x), M, K, lda, ptr(w), N, lda, ptr(b), act, ptr(out), N, stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert lib.da3b_device_status() == 0
+    ref = x[:, :K].float() @ w[:, :K].float().t() + b
+    if act == 2:
+        ref = torch.nn.functional.gelu(ref)
+    close(out, ref)
+
+
+@pytest.mark.parametrize("M,K,N", [(1370, 1024, 1024), (100, 384, 384), (4111, 4096, 1024)])
+def test_linear_resid(lib, M, K, N):
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).half()
+    b = torch.randn(N, device="cuda", generator=g).float()
+    s = torch.randn(N, device="cuda", generator=g).float()
+    r0 = torch.randn(M, N, device="cuda", generator=g).float()
+    r = r0.clone()
+    rc = lib.da3b_linear_resid_f32(ptr(x), M, K, K, ptr(w), N, K, ptr(b), ptr(s), ptr(r), N, stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert lib.da3b_device_status() == 0
+    ref = r0 + s * (x.float() @ w.float().t() + b)
+    err = (r - ref).abs().max().item()
+    assert err <= 1e-3 * ref.abs().max().item() + 1e-4
+
+
+@pytest.mark.parametrize("B,H,W,IC,OC,ks", [(2, 5, 5, 32, 32, 3), (1, 37, 37, 64, 64, 3), (2, 19, 19, 256, 256, 3),
+                                             (1, 74, 74, 48, 64, 3), (1, 37, 37, 128, 256, 1),
+                                             (1, 148, 148, 256, 256, 3), (3, 9, 30, 96, 128, 3)])
+def test_conv_nhwc(lib, B, H, W, IC, OC, ks):
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + H + IC + OC)
+    x = torch.randn(B, H, W, IC, device="cuda", generator=g).half()
+    w = torch.randn(OC, IC, ks, ks, device="cuda", generator=g).float() * 0.05
+    b = torch.randn(OC, device="cuda", generator=g).float()
+    r1 = torch.randn(B, H, W, OC, device="cuda", generator=g).half()
+    r2 = torch.randn(B, H, W, OC, device="cuda", generator=g).half()
+    icp = (IC + 63) // 64 * 64
+    wp = torch.empty(OC, ks * ks, icp, dtype=torch.float16, device="cuda")
+    assert lib.da3b_pack_conv_weight(ptr(w), OC, IC, ks, ptr(wp), stream()) == 0
+    out = torch.empty(B, H, W, OC, dtype=torch.float16, device="cuda")
+    outr = torch.empty_like(out)
+    rc = lib.da3b_conv_nhwc(ptr(x), B, H, W, IC, ptr(wp), OC, ks, ptr(b), ptr(r1), ptr(r2), 0, ptr(out), ptr(outr),
+                            stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert lib.da3b_device_status() == 0
+    ref = torch.nn.functional.conv2d(x.permute(0, 3, 1, 2).float(), w.half().float(), b, padding=ks // 2)
+    ref = ref.permute(0, 2, 3, 1) + r1.float() + r2.float()
+    close(out, ref)
+    close(outr, ref.clamp_min(0))
