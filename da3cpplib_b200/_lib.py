@@ -31,6 +31,38 @@ SIGNATURES = {
     "da3b_pack_conv_weight": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "da3b_conv_nhwc": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p,
                                c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
+    "da3b_load": (c_void_p, [c_char_p, c_int]),
+    "da3b_processed_size": (c_int, [c_void_p, c_int, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int),
+                                    ctypes.POINTER(c_int)]),
+    "da3b_infer_device": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                  c_void_p]),
+    "da3b_infer_host": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "da3b_ref_views": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int]),
+    "da3b_launches": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int]),
+    "da3b_debug_feature": (c_int, [c_void_p, c_int, c_void_p, c_size_t, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    "da3b_set_graphs": (c_int, [c_void_p, c_int]),
+    "da3b_set_raw_logits": (c_int, [c_void_p, c_int]),
+    "da3b_set_act_quant": (c_int, [c_void_p, c_int]),
+    "da3b_model_dims": (c_int, [c_void_p, ctypes.POINTER(c_int)]),
+    # reference-compatible C ABI (include/da3cpp/da3_c.h)
+    "da_capi_abi_version": (c_int, []),
+    "da_capi_load": (c_void_p, [c_char_p, c_int]),
+    "da_capi_load_nested": (c_void_p, [c_char_p, c_char_p, c_int]),
+    "da_capi_free": (None, [c_void_p]),
+    "da_capi_info_json": (c_void_p, [c_void_p]),
+    "da_capi_free_string": (None, [c_void_p]),
+    "da_capi_last_error": (c_char_p, [c_void_p]),
+    "da_capi_depth_path": (c_void_p, [c_void_p, c_char_p, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    "da_capi_pose_path": (c_int, [c_void_p, c_char_p, c_void_p, c_void_p]),
+    "da_capi_depth_pose_multi": (c_void_p, [c_void_p, ctypes.POINTER(c_char_p), c_int, ctypes.POINTER(c_int),
+                                            ctypes.POINTER(c_int), ctypes.POINTER(c_int), c_void_p, c_void_p]),
+    "da_capi_depth_dense": (c_int, [c_void_p, c_char_p, ctypes.POINTER(c_int), ctypes.POINTER(c_int), c_void_p,
+                                    c_void_p, c_void_p, c_void_p, c_void_p, ctypes.POINTER(c_int)]),
+    "da_capi_points": (c_int, [c_void_p, c_char_p, c_float, ctypes.POINTER(c_int), c_void_p, c_void_p]),
+    "da_capi_export_glb": (c_int, [c_void_p, c_char_p, c_char_p]),
+    "da_capi_export_colmap": (c_int, [c_void_p, c_char_p, c_char_p, c_int]),
+    "da_capi_free_floats": (None, [c_void_p]),
+    "da_capi_free_bytes": (None, [c_void_p]),
 }
 
 

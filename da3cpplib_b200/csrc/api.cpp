@@ -1,0 +1,536 @@
+// Public boundary of libda3b: the DA3cpplib-compatible C++ API (da3::), its C ABI
+// (da_capi_*), and the model-level batched entry points (da3b_*). Everything here is
+// host code; inference runs through Engine on the GPU.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+#include <cmath>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "da3b.h"
+#include "da3cpp/da3.h"
+#include "da3cpp/da3_c.h"
+#include "engine.h"
+
+#define DA_LOG(...)                     \
+  do {                                  \
+    fprintf(stderr, "[da3b] ");         \
+    fprintf(stderr, __VA_ARGS__);       \
+    fprintf(stderr, "\n");              \
+  } while (0)
+
+struct da_ctx {
+  std::unique_ptr<da3b::Engine> engine;
+  std::string last_error;
+  cudaStream_t stream = nullptr;
+  ~da_ctx() {
+    if (engine) cudaSetDevice(engine->device());
+    if (stream) cudaStreamDestroy(stream);
+  }
+};
+
+namespace {
+
+int default_device() {
+  if (const char* d = getenv("DA3B_DEVICE")) return atoi(d);
+  return 0;
+}
+
+// Processed size (src/preprocess.cpp:26-41 legacy, :157-197 real policy).
+void processed_size(const da3b::Config& c, int w, int h, bool legacy, int* ow, int* oh) {
+  const int patch = c.patch_size;
+  if (legacy) {
+    int dw = (w / patch) * patch, dh = (h / patch) * patch;
+    *ow = dw == 0 ? patch : dw;
+    *oh = dh == 0 ? patch : dh;
+    return;
+  }
+  const int target = c.img_resize_target > 0 ? c.img_resize_target : 504;
+  const bool upper = c.img_resize_mode.rfind("lower", 0) != 0;
+  int cw = w, ch = h;
+  const int bound = upper ? std::max(cw, ch) : std::min(cw, ch);
+  if (bound != target) {
+    const double scale = static_cast<double>(target) / bound;
+    cw = std::max(1, static_cast<int>(std::nearbyint(cw * scale)));
+    ch = std::max(1, static_cast<int>(std::nearbyint(ch * scale)));
+  }
+  auto nearest = [](int x, int p) {
+    const int down = (x / p) * p, up = down + p;
+    return (std::abs(up - x) <= std::abs(x - down)) ? up : down;
+  };
+  *ow = std::max(1, nearest(cw, patch));
+  *oh = std::max(1, nearest(ch, patch));
+}
+
+bool read_ppm(const char* path, int* w, int* h, std::vector<uint8_t>& rgb, std::string* err) {
+  FILE* f = fopen(path, "rb");
+  if (!f) { *err = std::string("cannot open image ") + path; return false; }
+  char magic[3] = {0, 0, 0};
+  int maxv = 0;
+  bool ok = fscanf(f, "%2s", magic) == 1 && strcmp(magic, "P6") == 0 && fscanf(f, "%d %d %d", w, h, &maxv) == 3 &&
+            maxv == 255 && *w > 0 && *h > 0;
+  if (ok) {
+    fgetc(f);
+    rgb.resize(static_cast<size_t>(*w) * *h * 3);
+    ok = fread(rgb.data(), 1, rgb.size(), f) == rgb.size();
+  }
+  fclose(f);
+  if (!ok) *err = std::string("image decode supports binary PPM (P6, 8-bit) only: ") + path;
+  return ok;
+}
+
+bool is_mono(const da3b::Engine& e) {
+  return e.model().file.tensor("head.scratch.sky_out2b.weight") != nullptr && e.output_dim() == 1;
+}
+
+// Single-image inference at the processed size (H2D, forward, D2H).
+bool run_one(da_ctx* c, const uint8_t* rgb, int w, int h, bool legacy, std::vector<float>& depth,
+             std::vector<float>* conf, int* oh, int* ow) {
+  da3b::Engine& e = *c->engine;
+  int W = 0, H = 0;
+  processed_size(e.config(), w, h, legacy, &W, &H);
+  if (W != w || H != h) {
+    c->last_error = "input " + std::to_string(w) + "x" + std::to_string(h) + " needs a resize to " +
+                    std::to_string(W) + "x" + std::to_string(H) + ", which this build does not run on the GPU";
+    return false;
+  }
+  depth.resize(static_cast<size_t>(H) * W);
+  const bool want_conf = conf && e.output_dim() >= 2;
+  if (want_conf) conf->resize(static_cast<size_t>(H) * W);
+  cudaSetDevice(e.device());
+  const int rc = e.run(rgb, 1, 1, H, W, depth.data(), want_conf ? conf->data() : nullptr, nullptr, c->stream);
+  if (rc != 0 || cudaStreamSynchronize(c->stream) != cudaSuccess || e.status() != 0) {
+    c->last_error = "depth: forward failed: " + e.last_error();
+    return false;
+  }
+  *oh = H;
+  *ow = W;
+  return true;
+}
+
+da_ctx* make_ctx(const char* path, int device, std::string* err) {
+  if (!path) { *err = "null path"; return nullptr; }
+  auto e = da3b::Engine::create(path, device, err);
+  if (!e) return nullptr;
+  auto* c = new da_ctx();
+  c->engine = std::move(e);
+  cudaSetDevice(device);
+  cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  return c;
+}
+
+}  // namespace
+
+// ====================================================================== da3:: C++ API
+namespace da3 {
+
+struct Model {
+  std::unique_ptr<da_ctx> ctx;
+};
+
+std::shared_ptr<Model> load_model(const Params& params) {
+  if (params.model_path.empty()) return nullptr;
+  if (params.tensorrt.enabled && !params.tensorrt.fallback_to_ggml) {
+    DA_LOG("load_model: TensorRT is not part of this library and fallback is disabled");
+    return nullptr;
+  }
+  std::string err;
+  da_ctx* c = make_ctx(params.model_path.c_str(), params.device >= 0 ? params.device : default_device(), &err);
+  if (!c) {
+    DA_LOG("load_model: %s", err.c_str());
+    return nullptr;
+  }
+  auto m = std::make_shared<Model>();
+  m->ctx.reset(c);
+  return m;
+}
+
+ModelInfo model_info(const Model& model) {
+  ModelInfo info;
+  if (!model.ctx || !model.ctx->engine) return info;
+  const da3b::Engine& e = *model.ctx->engine;
+  const da3b::Config& c = e.config();
+  info.checkpoint_name = c.checkpoint_name;
+  info.patch_size = c.patch_size;
+  info.resize_target = c.img_resize_target;
+  for (int i = 0; i < 3; ++i) {
+    info.mean[i] = c.img_mean[i];
+    info.std[i] = c.img_std[i];
+  }
+  std::string n = c.checkpoint_name;
+  std::transform(n.begin(), n.end(), n.begin(), [](unsigned char ch) { return static_cast<char>(tolower(ch)); });
+  info.is_metric = c.head_max_depth > 0.f || n.find("metric") != std::string::npos ||
+                   n.find("nested") != std::string::npos || n.find("mono") != std::string::npos;
+  info.has_aux_ray_head = e.has_aux();
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, e.device()) == cudaSuccess) info.device_name = prop.name;
+  info.gpu_active = true;
+  if (c.is_da2()) info.kind = c.head_max_depth > 0.f ? ModelKind::da2_metric : ModelKind::da2_relative;
+  else if (is_mono(e)) info.kind = ModelKind::da3_mono;
+  else {
+    info.kind = ModelKind::da3;
+    info.has_camera_pose = true;
+  }
+  return info;
+}
+
+bool infer(Model& model, const Image& image, Result& result, const InferOptions& options) {
+  result = {};
+  if (!model.ctx || !model.ctx->engine) return false;
+  if (image.width <= 0 || image.height <= 0 ||
+      image.data.size() != static_cast<size_t>(image.width) * image.height * 3)
+    return false;
+  da_ctx* c = model.ctx.get();
+  const da3b::Engine& e = *c->engine;
+  if (options.with_pose || options.ray_pose) {
+    DA_LOG("infer: camera pose is outside the depth path of this library");
+    return false;
+  }
+  if (is_mono(e)) {
+    DA_LOG("infer: DA3 mono (sky head) checkpoints are not supported");
+    return false;
+  }
+  // DA2 always uses preprocess_real (src/engine.cpp:121-130); DA3 uses it unless
+  // legacy_resize (src/api.cpp:151-157).
+  const bool legacy = !e.config().is_da2() && options.legacy_resize;
+  int H = 0, W = 0;
+  if (!run_one(c, image.data.data(), image.width, image.height, legacy, result.depth, &result.confidence, &H, &W)) {
+    DA_LOG("infer: %s", c->last_error.c_str());
+    result = {};
+    return false;
+  }
+  result.height = H;
+  result.width = W;
+  result.is_metric = model_info(model).is_metric;
+  return !result.depth.empty();
+}
+
+bool infer_file(Model& model, const std::string& image_path, Result& result, const InferOptions& options) {
+  Image img;
+  std::string err;
+  if (!read_ppm(image_path.c_str(), &img.width, &img.height, img.data, &err)) {
+    DA_LOG("infer_file: %s", err.c_str());
+    result = {};
+    return false;
+  }
+  return infer(model, img, result, options);
+}
+
+bool infer_preprocessed(Model& model, int height, int width, const UploadCallback& upload, Result& result) {
+  result = {};
+  (void)model;
+  (void)height;
+  (void)width;
+  (void)upload;
+  DA_LOG("infer_preprocessed: the f32 planar device input path is not implemented in this build");
+  return false;
+}
+
+bool infer_batch(Model& model, const std::vector<Image>& images, std::vector<Result>& results) {
+  results.clear();
+  if (!model.ctx || !model.ctx->engine || images.empty()) return false;
+  da_ctx* c = model.ctx.get();
+  da3b::Engine& e = *c->engine;
+  const int w = images[0].width, h = images[0].height, n = static_cast<int>(images.size());
+  std::vector<uint8_t> rgb(static_cast<size_t>(n) * w * h * 3);
+  for (int i = 0; i < n; ++i) {
+    if (images[i].width != w || images[i].height != h ||
+        images[i].data.size() != static_cast<size_t>(w) * h * 3)
+      return false;
+    memcpy(&rgb[static_cast<size_t>(i) * w * h * 3], images[i].data.data(), images[i].data.size());
+  }
+  const size_t HW = static_cast<size_t>(w) * h;
+  std::vector<float> depth(n * HW), conf(e.output_dim() >= 2 ? n * HW : 0);
+  if (da3b_infer_host(c, rgb.data(), n, 1, h, w, depth.data(), conf.empty() ? nullptr : conf.data(), nullptr) != 0) {
+    DA_LOG("infer_batch: %s", c->last_error.c_str());
+    return false;
+  }
+  const bool metric = model_info(model).is_metric;
+  results.resize(n);
+  for (int i = 0; i < n; ++i) {
+    Result& r = results[i];
+    r.width = w;
+    r.height = h;
+    r.is_metric = metric;
+    r.depth.assign(depth.begin() + i * HW, depth.begin() + (i + 1) * HW);
+    if (!conf.empty()) r.confidence.assign(conf.begin() + i * HW, conf.begin() + (i + 1) * HW);
+  }
+  return true;
+}
+
+}  // namespace da3
+
+// ====================================================================== C ABI
+extern "C" {
+
+DA_CAPI int da_capi_abi_version(void) { return 4; }
+
+DA_CAPI da_ctx* da_capi_load(const char* path, int n_threads) {
+  (void)n_threads;
+  std::string err;
+  da_ctx* c = make_ctx(path, default_device(), &err);
+  if (!c) DA_LOG("da_capi_load: %s", err.c_str());
+  return c;
+}
+
+DA_CAPI da_ctx* da_capi_load_nested(const char* anyview, const char* metric, int n_threads) {
+  (void)anyview;
+  (void)metric;
+  (void)n_threads;
+  DA_LOG("da_capi_load_nested: nested metric models are outside the supported depth path");
+  return nullptr;
+}
+
+DA_CAPI void da_capi_free(da_ctx* c) { delete c; }
+
+DA_CAPI char* da_capi_info_json(da_ctx* c) {
+  if (!c || !c->engine) return nullptr;
+  const da3b::Config& cfg = c->engine->config();
+  std::string name;
+  for (char ch : cfg.checkpoint_name) {
+    if (ch == '"' || ch == '\\') name += '\\';
+    if (static_cast<unsigned char>(ch) >= 0x20) name += ch;
+  }
+  const std::string j = "{\"checkpoint\":\"" + name + "\",\"embed_dim\":" + std::to_string(cfg.embed_dim) +
+                        ",\"depth\":" + std::to_string(cfg.depth) + ",\"num_heads\":" + std::to_string(cfg.num_heads) +
+                        ",\"tensorrt_enabled\":false,\"tensorrt_active\":false}";
+  char* p = static_cast<char*>(malloc(j.size() + 1));
+  if (p) memcpy(p, j.c_str(), j.size() + 1);
+  return p;
+}
+
+DA_CAPI void da_capi_free_string(char* s) { free(s); }
+DA_CAPI const char* da_capi_last_error(da_ctx* c) { return c ? c->last_error.c_str() : ""; }
+DA_CAPI void da_capi_free_floats(float* p) { free(p); }
+DA_CAPI void da_capi_free_bytes(unsigned char* p) { free(p); }
+
+// src/da_capi.cpp:97-117: DA2 -> depth_relative (preprocess_real); DA3 -> depth
+// (legacy floor-to-patch preprocess).
+DA_CAPI float* da_capi_depth_path(da_ctx* c, const char* image_path, int* out_h, int* out_w) {
+  if (!c || !c->engine || !image_path) {
+    if (c) c->last_error = "depth: bad args";
+    return nullptr;
+  }
+  int w = 0, h = 0;
+  std::vector<uint8_t> rgb;
+  if (!read_ppm(image_path, &w, &h, rgb, &c->last_error)) return nullptr;
+  std::vector<float> depth;
+  int H = 0, W = 0;
+  const bool legacy = !c->engine->config().is_da2();
+  if (!run_one(c, rgb.data(), w, h, legacy, depth, nullptr, &H, &W)) return nullptr;
+  float* p = static_cast<float*>(malloc(depth.size() * sizeof(float)));
+  if (!p) {
+    c->last_error = "depth: oom";
+    return nullptr;
+  }
+  memcpy(p, depth.data(), depth.size() * sizeof(float));
+  if (out_h) *out_h = H;
+  if (out_w) *out_w = W;
+  return p;
+}
+
+DA_CAPI int da_capi_pose_path(da_ctx* c, const char* image_path, float out_ext[12], float out_intr[9]) {
+  (void)image_path;
+  (void)out_ext;
+  (void)out_intr;
+  if (c) c->last_error = "pose: camera pose is outside the depth path of this library";
+  return -1;
+}
+
+// src/da_capi.cpp:130-155: legacy preprocess, one backbone pass over all views.
+DA_CAPI float* da_capi_depth_pose_multi(da_ctx* c, const char** paths, int n, int* out_h, int* out_w, int* out_n,
+                                        float* out_ext, float* out_intr) {
+  (void)out_ext;
+  (void)out_intr;
+  if (!c || !c->engine || !paths || n <= 0) {
+    if (c) c->last_error = "depth_multi: bad args";
+    return nullptr;
+  }
+  int w0 = 0, h0 = 0;
+  std::vector<uint8_t> all;
+  for (int i = 0; i < n; ++i) {
+    int w = 0, h = 0;
+    std::vector<uint8_t> rgb;
+    if (!paths[i] || !read_ppm(paths[i], &w, &h, rgb, &c->last_error)) return nullptr;
+    if (i == 0) { w0 = w; h0 = h; }
+    else if (w != w0 || h != h0) { c->last_error = "depth_multi: views differ in H,W"; return nullptr; }
+    all.insert(all.end(), rgb.begin(), rgb.end());
+  }
+  int W = 0, H = 0;
+  processed_size(c->engine->config(), w0, h0, true, &W, &H);
+  if (W != w0 || H != h0) {
+    c->last_error = "depth_multi: views need a resize, which this build does not run on the GPU";
+    return nullptr;
+  }
+  const size_t per = static_cast<size_t>(H) * W;
+  float* p = static_cast<float*>(malloc(static_cast<size_t>(n) * per * sizeof(float)));
+  if (!p) { c->last_error = "depth_multi: oom"; return nullptr; }
+  if (da3b_infer_host(c, all.data(), n, n, H, W, p, nullptr, nullptr) != 0) {
+    free(p);
+    return nullptr;
+  }
+  if (out_h) *out_h = H;
+  if (out_w) *out_w = W;
+  if (out_n) *out_n = n;
+  return p;
+}
+
+DA_CAPI int da_capi_depth_dense(da_ctx* c, const char* image_path, int* out_h, int* out_w, float** out_depth,
+                                float** out_conf, float** out_sky, float out_ext[12], float out_intr[9],
+                                int* out_is_metric) {
+  (void)out_ext;
+  (void)out_intr;
+  if (!c || !c->engine || !image_path) {
+    if (c) c->last_error = "depth_dense: bad args";
+    return -1;
+  }
+  int w = 0, h = 0;
+  std::vector<uint8_t> rgb;
+  if (!read_ppm(image_path, &w, &h, rgb, &c->last_error)) return -1;
+  std::vector<float> depth, conf;
+  int H = 0, W = 0;
+  if (!run_one(c, rgb.data(), w, h, false, depth, &conf, &H, &W)) return -1;
+  auto dup = [](const std::vector<float>& v) -> float* {
+    if (v.empty()) return nullptr;
+    float* p = static_cast<float*>(malloc(v.size() * sizeof(float)));
+    if (p) memcpy(p, v.data(), v.size() * sizeof(float));
+    return p;
+  };
+  if (out_depth) *out_depth = dup(depth);
+  if (out_conf) *out_conf = dup(conf);
+  if (out_sky) *out_sky = nullptr;
+  if (out_h) *out_h = H;
+  if (out_w) *out_w = W;
+  if (out_is_metric) *out_is_metric = c->engine->config().head_max_depth > 0.f ? 1 : 0;
+  return 0;
+}
+
+DA_CAPI int da_capi_points(da_ctx* c, const char*, float, int*, float**, unsigned char**) {
+  if (c) c->last_error = "points: point clouds are outside the depth path of this library";
+  return -1;
+}
+DA_CAPI int da_capi_export_glb(da_ctx* c, const char*, const char*) {
+  if (c) c->last_error = "export_glb: exporters are outside the depth path of this library";
+  return -1;
+}
+DA_CAPI int da_capi_export_colmap(da_ctx* c, const char*, const char*, int) {
+  if (c) c->last_error = "export_colmap: exporters are outside the depth path of this library";
+  return -1;
+}
+
+// ---------------------------------------------------------------------- da3b_*
+DA3B_API da_ctx* da3b_load(const char* gguf_path, int device) {
+  std::string err;
+  da_ctx* c = make_ctx(gguf_path, device, &err);
+  if (!c) DA_LOG("da3b_load: %s", err.c_str());
+  return c;
+}
+
+DA3B_API int da3b_processed_size(da_ctx* c, int w, int h, int legacy, int* out_h, int* out_w, int* needs_resize) {
+  if (!c || !c->engine || w <= 0 || h <= 0) return -1;
+  int W = 0, H = 0;
+  processed_size(c->engine->config(), w, h, legacy != 0, &W, &H);
+  if (out_h) *out_h = H;
+  if (out_w) *out_w = W;
+  if (needs_resize) *needs_resize = (W != w || H != h) ? 1 : 0;
+  return 0;
+}
+
+DA3B_API int da3b_infer_device(da_ctx* c, const void* rgb_dev, int n_views, int views_per_scene, int h, int w,
+                               void* depth_dev, void* conf_dev, void* rays_dev, void* stream) {
+  if (!c || !c->engine || !rgb_dev || !depth_dev) return -1;
+  cudaSetDevice(c->engine->device());
+  const int rc = c->engine->run(static_cast<const uint8_t*>(rgb_dev), n_views, views_per_scene, h, w,
+                                static_cast<float*>(depth_dev), static_cast<float*>(conf_dev),
+                                static_cast<float*>(rays_dev), static_cast<cudaStream_t>(stream));
+  if (rc) c->last_error = c->engine->last_error();
+  return rc;
+}
+
+DA3B_API int da3b_infer_host(da_ctx* c, const void* rgb_host, int n_views, int views_per_scene, int h, int w,
+                             float* depth_host, float* conf_host, float* rays_host) {
+  if (!c || !c->engine || !rgb_host || !depth_host) return -1;
+  cudaSetDevice(c->engine->device());
+  int rc = c->engine->run(static_cast<const uint8_t*>(rgb_host), n_views, views_per_scene, h, w, depth_host,
+                          conf_host, rays_host, c->stream);
+  if (rc) {
+    c->last_error = c->engine->last_error();
+    return rc;
+  }
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
+    c->last_error = std::string("CUDA error: ") + cudaGetErrorString(cudaGetLastError());
+    return -20;
+  }
+  const int st = c->engine->status();
+  if (st != 0) {
+    c->last_error = "device status " + std::to_string(st) + " (a bounded wait timed out)";
+    return -21;
+  }
+  return 0;
+}
+
+DA3B_API int da3b_ref_views(da_ctx* c, int* out, int n) {
+  if (!c || !c->engine || !out) return -1;
+  const std::vector<int> v = c->engine->last_ref_views(c->stream);
+  for (int i = 0; i < n && i < static_cast<int>(v.size()); ++i) out[i] = v[i];
+  return static_cast<int>(v.size());
+}
+
+DA3B_API int da3b_launches(da_ctx* c, int n_views, int views_per_scene, int h, int w, int rays) {
+  if (!c || !c->engine) return -1;
+  return c->engine->launches(n_views, views_per_scene, h, w, rays != 0);
+}
+
+DA3B_API int da3b_debug_feature(da_ctx* c, int layer, void* out, size_t capacity, int* rows, int* cols) {
+  if (!c || !c->engine || !out) return -1;
+  int r = 0, k = 0;
+  const __half* p = c->engine->debug_feat(layer, &r, &k);
+  if (!p) return -2;
+  if (rows) *rows = r;
+  if (cols) *cols = k;
+  const size_t n = static_cast<size_t>(r) * k;
+  if (n > capacity) return -3;
+  cudaSetDevice(c->engine->device());
+  cudaStreamSynchronize(c->stream);
+  return cudaMemcpy(out, p, n * 2, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -4;
+}
+
+DA3B_API int da3b_set_graphs(da_ctx* c, int on) {
+  if (!c || !c->engine) return -1;
+  c->engine->set_use_graph(on != 0);
+  return 0;
+}
+
+DA3B_API int da3b_set_act_quant(da_ctx* c, int on) {
+  if (!c || !c->engine) return -1;
+  c->engine->set_act_quant(on != 0);
+  return 0;
+}
+
+DA3B_API int da3b_set_raw_logits(da_ctx* c, int on) {
+  if (!c || !c->engine) return -1;
+  c->engine->set_raw_logits(on != 0);
+  return 0;
+}
+
+DA3B_API int da3b_model_dims(da_ctx* c, int* out) {
+  if (!c || !c->engine || !out) return -1;
+  const da3b::Config& cfg = c->engine->config();
+  out[0] = cfg.embed_dim;
+  out[1] = cfg.depth;
+  out[2] = cfg.num_heads;
+  out[3] = cfg.patch_size;
+  out[4] = cfg.cat_token ? 1 : 0;
+  out[5] = c->engine->output_dim();
+  out[6] = c->engine->has_aux() ? 1 : 0;
+  out[7] = cfg.is_da2() ? 1 : 0;
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,87 @@
+// Depth-path engine: one device model, per-shape plans (pre-allocated buffers,
+// per-resolution tables, a captured CUDA graph), and the forward launch sequence.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <map>
+#include <memory>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "model.h"
+
+namespace da3b {
+
+struct Plan;
+
+// Output activation family of the depth head (src/dpt_head.cpp:402-439, src/engine.cpp:218-225).
+enum class HeadKind { Da2Relative, Da2Metric, Da3 };
+
+class Engine {
+ public:
+  ~Engine();
+  static std::unique_ptr<Engine> create(const std::string& gguf_path, int device, std::string* err);
+
+  const Config& config() const { return model_->cfg; }
+  const DeviceModel& model() const { return *model_; }
+  int device() const { return device_; }
+  HeadKind head_kind() const;
+  bool has_aux() const { return model_->head.aux; }
+  int output_dim() const { return model_->head.od; }
+
+  // Depth inference of n_views RGB8 images [n_views][H][W][3] already on the device
+  // (H, W multiples of the patch size). Views are grouped into scenes of
+  // views_per_scene consecutive images that share global attention (1 = single
+  // image). Outputs are f32 planes [n_views][H][W] (conf may be null; for DA2 it is
+  // unused); rays (may be null) receives the aux ray head [7][n_views][8*gh][8*gw].
+  // Returns 0, or a negative error code with last_error() set. Asynchronous on `s`
+  // except on the first call for a shape (plan creation synchronises).
+  int run(const uint8_t* rgb_dev, int n_views, int views_per_scene, int H, int W, float* depth_dev,
+          float* conf_dev, float* rays_dev, cudaStream_t s);
+
+  // Selected reference view per scene of the last run with views_per_scene >= 3 (host copy).
+  std::vector<int> last_ref_views(cudaStream_t s);
+  // Kernel launches of one forward of the given shape (after a run of that shape).
+  int launches(int n_views, int views_per_scene, int H, int W, bool rays) const;
+  // Device-side status word (0 = ok), read after a synchronisation.
+  int status();
+  const std::string& last_error() const { return err_; }
+  void set_use_graph(bool on) { use_graph_ = on; }
+  // true: the fused out2b epilogue writes raw logits (no output activation); used
+  // by parity tests. Changing it drops the cached plans.
+  void set_raw_logits(bool on);
+  // true (default): activations entering a Q8_0 linear are rounded through Q8_0
+  // exactly as ggml quantises them before its Q8_0 matmuls, so results follow the
+  // reference's numerics; false: plain f16 activations. Drops the cached plans.
+  void set_act_quant(bool on);
+
+  // Debug captures for parity tests: feats of out-layer o ([n_views*Np][C] f16) of
+  // the last run; returns nullptr if unavailable.
+  const __half* debug_feat(int o, int* rows, int* cols) const;
+  const float* debug_x(int* rows, int* cols) const;
+
+ private:
+  Engine() = default;
+  Plan* plan_for(int n_views, int S, int H, int W, bool rays);
+  int forward(Plan& p, cudaStream_t s);
+  int backbone(Plan& p, cudaStream_t s);
+  int head(Plan& p, cudaStream_t s);
+  int pyramid(Plan& p, const void* fuse_weights, __half* u_out, cudaStream_t s);
+
+  std::unique_ptr<DeviceModel> model_;
+  int device_ = 0;
+  int* status_ = nullptr;
+  bool use_graph_ = true;
+  bool raw_logits_ = false;
+  bool act_quant_ = true;
+  std::string err_;
+  std::map<std::tuple<int, int, int, int, bool>, std::unique_ptr<Plan>> plans_;
+  Plan* last_ = nullptr;
+  const float* last_x_ = nullptr;
+  const __half* last_feat_[4] = {nullptr, nullptr, nullptr, nullptr};
+};
+
+}  // namespace da3b

@@ -70,6 +70,21 @@ __device__ __forceinline__ void store_h8(__half* p, const float* v) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
+// Q8_0 round trip of one 32-element block with ggml's reference quantiser
+// (quantize_row_q8_0_ref: d = amax/127, q = roundf(x * (1/d)), d stored as f16) followed
+// by dequantisation d*q: the values a ggml Q8_0 x Q8_0 dot product sees on the
+// activation side.
+__device__ __forceinline__ void q8_roundtrip32(float (&t)[32]) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(t[i]));
+  const float d = amax / 127.0f;
+  const float id = d != 0.f ? 1.0f / d : 0.0f;
+  const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) t[i] = dh * roundf(t[i] * id);
+}
+
 __device__ __forceinline__ int remap_row(const EpiArgs& e, int row) {
   return e.rm_div > 0 ? (row / e.rm_div) * e.rm_mul + e.rm_add + row % e.rm_div : row;
 }
@@ -82,6 +97,15 @@ __device__ __forceinline__ void epilogue32(const GemmGeom& g, const EpiArgs& e, 
   switch (e.kind) {
     case kEpiF16: {
       const int orow = remap_row(e, row);
+      if (e.q8) {  // full 32-column block (host enforces N % 32 == 0, no addends)
+        float t[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) t[i] = apply_act(v[i] + (e.bias ? __ldg(e.bias + n_base + i) : 0.0f), e.act);
+        q8_roundtrip32(t);
+#pragma unroll
+        for (int j0 = 0; j0 < 32; j0 += 8) store_h8(e.out + static_cast<size_t>(orow) * e.ld_out + n_base + j0, t + j0);
+        break;
+      }
       for (int j0 = 0; j0 < nvalid; j0 += 8) {  // N % 8 == 0 is enforced by the host
         float t[8];
 #pragma unroll
@@ -466,6 +490,7 @@ static int check_epi(const EpiArgs& e, int N) {
     if (e.out_relu && (reinterpret_cast<uintptr_t>(e.out_relu) & 15)) return -21;
     if (e.res1 && (e.ld_res1 % 8 || (reinterpret_cast<uintptr_t>(e.res1) & 15))) return -22;
     if (e.res2 && (e.ld_res2 % 8 || (reinterpret_cast<uintptr_t>(e.res2) & 15))) return -23;
+    if (e.q8 && (N % 32 || e.res1 || e.res2 || e.out_relu || e.kind != kEpiF16)) return -29;
   }
   if (e.kind == kEpiResid || e.kind == kEpiTokens) {
     if (N % 4 || !e.resid || e.ld_resid % 4 || (reinterpret_cast<uintptr_t>(e.resid) & 15)) return -24;

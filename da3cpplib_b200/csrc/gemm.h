@@ -51,6 +51,8 @@ struct GemmGeom {
 struct EpiArgs {
   int kind;          // EpiKind
   int act;           // Act (kEpiF16)
+  int q8;            // kEpiF16: round-trip each 32-column block through Q8_0 (ggml's
+                     // activation quantisation before a Q8_0 matmul); needs N % 32 == 0
   const float* bias;   // [N] or null
   const float* scale;  // [N] LayerScale (kEpiResid) or null
   float* resid;        // f32 [rows][ld_resid] (kEpiResid / kEpiTokens)

@@ -1,0 +1,501 @@
+// Memory-bound kernels of the depth path (coalesced, vectorised, one pass each).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.h"
+
+namespace da3b {
+
+static inline unsigned grid_for(long n, int threads, long cap = 1L << 20) {
+  long b = (n + threads - 1) / threads;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return static_cast<unsigned>(b);
+}
+
+// ---------------------------------------------------------------- preprocess + patchify
+// RGB8 [B][H][W][3] -> normalised, patch-major A matrix of the patch-embed GEMM:
+// row = b*Np + (py*gw + px), column k = c*P*P + ky*P + kx (the flattening of the
+// conv weight [D][3][P][P]), zero for k >= 3*P*P. Normalisation is the reference's
+// (v/255 - mean[c]) / std[c] in f32 (src/preprocess.cpp:192-196), stored as f16.
+__global__ void k_patchify(const uint8_t* __restrict__ rgb, int B, int H, int W, int P, int gh, int gw,
+                           float m0, float m1, float m2, float s0, float s1, float s2, __half* __restrict__ out,
+                           int ldk) {
+  const long total = static_cast<long>(B) * gh * gw * (ldk / 2);
+  const int kk = 3 * P * P;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int k2 = static_cast<int>(i % (ldk / 2)) * 2;
+    const long row = i / (ldk / 2);
+    const int p = static_cast<int>(row % (gh * gw));
+    const int b = static_cast<int>(row / (gh * gw));
+    const int py = p / gw, px = p % gw;
+    float v[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int k = k2 + j;
+      if (k < kk) {
+        const int c = k / (P * P), r = k % (P * P), ky = r / P, kx = r % P;
+        const int y = py * P + ky, x = px * P + kx;
+        const float u = static_cast<float>(rgb[((static_cast<size_t>(b) * H + y) * W + x) * 3 + c]) / 255.f;
+        const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2);
+        const float sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
+        v[j] = (u - mean) / sd;
+      } else {
+        v[j] = 0.f;
+      }
+    }
+    *reinterpret_cast<__half2*>(out + row * ldk + k2) = __floats2half2_rn(v[0], v[1]);
+  }
+}
+
+int patchify(const uint8_t* rgb, int B, int H, int W, int P, const float* mean, const float* sd, __half* out, int ldk,
+             cudaStream_t s) {
+  if (H % P || W % P || ldk % 2 || ldk < 3 * P * P) return -1;
+  const int gh = H / P, gw = W / P;
+  const long total = static_cast<long>(B) * gh * gw * (ldk / 2);
+  k_patchify<<<grid_for(total, 256), 256, 0, s>>>(rgb, B, H, W, P, gh, gw, mean[0], mean[1], mean[2], sd[0], sd[1],
+                                                  sd[2], out, ldk);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+// x[b*ntok + 0][:] = cls + pos[0]  (token 0 of every image; src/dino_backbone.cpp:123-126)
+__global__ void k_cls_rows(float* __restrict__ x, int B, int ntok, int D, const float* __restrict__ cls,
+                           const float* __restrict__ pos) {
+  const long total = static_cast<long>(B) * D;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int b = static_cast<int>(i / D), e = static_cast<int>(i % D);
+    x[static_cast<size_t>(b) * ntok * D + e] = cls[e] + pos[e];
+  }
+}
+int cls_rows(float* x, int B, int ntok, int D, const float* cls, const float* pos, cudaStream_t s) {
+  k_cls_rows<<<grid_for(static_cast<long>(B) * D, 256), 256, 0, s>>>(x, B, ntok, D, cls, pos);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// Token 0 of every view := camera_token[slot] with slot 0 for the first view of
+// each scene and slot 1 for the others (src/dino_backbone.cpp:533-546).
+__global__ void k_cam_rows(float* __restrict__ x, int nviews_total, int views_per_scene, int ntok, int D,
+                           const float* __restrict__ cam) {
+  const long total = static_cast<long>(nviews_total) * D;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int v = static_cast<int>(i / D), e = static_cast<int>(i % D);
+    const int slot = (v % views_per_scene) == 0 ? 0 : 1;
+    x[static_cast<size_t>(v) * ntok * D + e] = cam[slot * D + e];
+  }
+}
+int cam_rows(float* x, int nviews_total, int views_per_scene, int ntok, int D, const float* cam, cudaStream_t s) {
+  k_cam_rows<<<grid_for(static_cast<long>(nviews_total) * D, 256), 256, 0, s>>>(x, nviews_total, views_per_scene,
+                                                                                ntok, D, cam);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// ---------------------------------------------------------------- LayerNorm
+// One warp per output row; VPL = D / 32 values per lane held in registers.
+// Two-pass mean / variance in f32, y = (x - mean) * rsqrt(var + eps) * g + b
+// (ggml_norm + mul + add, src/ggml_extend.hpp:12-17).
+template <typename Tin, int VPL>
+__global__ void k_layernorm(const Tin* __restrict__ in, int ld_in, int rows, int D, const float* __restrict__ g,
+                            const float* __restrict__ bta, float eps, __half* __restrict__ out, int ld_out, int col_off,
+                            int rm_div, int rm_mul, int rm_add, int q8) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int in_row = rm_div > 0 ? (warp / rm_div) * rm_mul + rm_add + warp % rm_div : warp;
+  const Tin* src = in + static_cast<size_t>(in_row) * ld_in;
+  float v[VPL];
+  // element j of lane: index = (j / 4) * 128 + lane * 4 + (j % 4)   (vectors of 4)
+#pragma unroll
+  for (int j = 0; j < VPL; j += 4) {
+    const int idx = (j / 4) * 128 + lane * 4;
+    if (sizeof(Tin) == 4) {
+      const float4 f = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + idx);
+      v[j] = f.x; v[j + 1] = f.y; v[j + 2] = f.z; v[j + 3] = f.w;
+    } else {
+      const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(src) + idx);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+      v[j] = a.x; v[j + 1] = a.y; v[j + 2] = b.x; v[j + 3] = b.y;
+    }
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) s += v[j];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / D;
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const float d = v[j] - mean;
+    q += d * d;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = rsqrtf(q / D + eps);
+  __half* dst = out + static_cast<size_t>(warp) * ld_out + col_off;
+#pragma unroll
+  for (int j = 0; j < VPL; j += 4) {
+    const int idx = (j / 4) * 128 + lane * 4;
+    float r[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[i] = (v[j + i] - mean) * rstd * __ldg(g + idx + i) + (bta ? __ldg(bta + idx + i) : 0.f);
+    if (q8) {
+      // Q8_0 round trip over the 32-element block held by 8 consecutive lanes
+      // (ggml quantize_row_q8_0_ref semantics, as in the GEMM epilogue).
+      float amax = fmaxf(fmaxf(fabsf(r[0]), fabsf(r[1])), fmaxf(fabsf(r[2]), fabsf(r[3])));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+      const float d = amax / 127.0f;
+      const float id = d != 0.f ? 1.0f / d : 0.0f;
+      const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) r[i] = dh * roundf(r[i] * id);
+    }
+    uint2 u;
+    *reinterpret_cast<__half2*>(&u.x) = __floats2half2_rn(r[0], r[1]);
+    *reinterpret_cast<__half2*>(&u.y) = __floats2half2_rn(r[2], r[3]);
+    *reinterpret_cast<uint2*>(dst + idx) = u;
+  }
+}
+
+template <typename Tin>
+static int ln_dispatch(const Tin* in, int ld_in, int rows, int D, const float* g, const float* b, float eps,
+                       __half* out, int ld_out, int col_off, int rm_div, int rm_mul, int rm_add, int q8,
+                       cudaStream_t s) {
+  if (rows <= 0) return 0;
+  const unsigned blocks = static_cast<unsigned>((static_cast<long>(rows) * 32 + 255) / 256);
+#define DA3B_LN(VPL)                                                                                           \
+  k_layernorm<Tin, VPL><<<blocks, 256, 0, s>>>(in, ld_in, rows, D, g, b, eps, out, ld_out, col_off, rm_div, rm_mul, \
+                                               rm_add, q8)
+  switch (D) {
+    case 128: DA3B_LN(4); break;
+    case 256: DA3B_LN(8); break;
+    case 384: DA3B_LN(12); break;
+    case 512: DA3B_LN(16); break;
+    case 768: DA3B_LN(24); break;
+    case 1024: DA3B_LN(32); break;
+    case 1536: DA3B_LN(48); break;
+    case 2048: DA3B_LN(64); break;
+    default: return -1;
+  }
+#undef DA3B_LN
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+int layernorm_f32(const float* in, int ld_in, int rows, int D, const float* g, const float* b, float eps, __half* out,
+                  int ld_out, int col_off, int rm_div, int rm_mul, int rm_add, cudaStream_t s, int q8) {
+  return ln_dispatch<float>(in, ld_in, rows, D, g, b, eps, out, ld_out, col_off, rm_div, rm_mul, rm_add, q8, s);
+}
+int layernorm_f16(const __half* in, int ld_in, int rows, int D, const float* g, const float* b, float eps,
+                  __half* out, int ld_out, int col_off, int rm_div, int rm_mul, int rm_add, cudaStream_t s) {
+  return ln_dispatch<__half>(in, ld_in, rows, D, g, b, eps, out, ld_out, col_off, rm_div, rm_mul, rm_add, 0, s);
+}
+
+// f32 rows -> f16 rows with the same row remap as the LayerNorm (DA3 local_x half of feats).
+__global__ void k_cast_rows(const float* __restrict__ in, int ld_in, int rows, int D, __half* __restrict__ out,
+                            int ld_out, int col_off, int rm_div, int rm_mul, int rm_add) {
+  const long total = static_cast<long>(rows) * (D / 4);
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / (D / 4)), c = static_cast<int>(i % (D / 4)) * 4;
+    const int ir = rm_div > 0 ? (r / rm_div) * rm_mul + rm_add + r % rm_div : r;
+    const float4 f = *reinterpret_cast<const float4*>(in + static_cast<size_t>(ir) * ld_in + c);
+    uint2 u;
+    *reinterpret_cast<__half2*>(&u.x) = __floats2half2_rn(f.x, f.y);
+    *reinterpret_cast<__half2*>(&u.y) = __floats2half2_rn(f.z, f.w);
+    *reinterpret_cast<uint2*>(out + static_cast<size_t>(r) * ld_out + col_off + c) = u;
+  }
+}
+int cast_rows(const float* in, int ld_in, int rows, int D, __half* out, int ld_out, int col_off, int rm_div, int rm_mul,
+              int rm_add, cudaStream_t s) {
+  if (D % 4) return -1;
+  k_cast_rows<<<grid_for(static_cast<long>(rows) * (D / 4), 256), 256, 0, s>>>(in, ld_in, rows, D, out, ld_out,
+                                                                               col_off, rm_div, rm_mul, rm_add);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+// ---------------------------------------------------------------- QK-norm + 2-D RoPE
+// In place on qkv [M][3D] (head_dim 64): one warp per (token, head), lane owns dims
+// 2l, 2l+1. q/k LayerNorm over 64 (eps 1e-5, src/vit_block.cpp:5-11) then
+// rotate-half RoPE per 32-dim half (src/rope2d.cpp:36-52; partner lane = l ^ 8).
+// Table row = token % ntok (pos_local or the tiled pos_nodiff of global layers).
+__global__ void k_qk_norm_rope(__half* __restrict__ qkv, int M, int H, int D, int ntok, const float* __restrict__ qg,
+                               const float* __restrict__ qb, const float* __restrict__ kg,
+                               const float* __restrict__ kb, const float* __restrict__ cs,
+                               const float* __restrict__ sn) {
+  const long warp = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= static_cast<long>(M) * H * 2) return;
+  const int which = static_cast<int>(warp & 1);          // 0 = q, 1 = k
+  const long th = warp >> 1;
+  const int m = static_cast<int>(th / H), h = static_cast<int>(th % H);
+  __half2* p = reinterpret_cast<__half2*>(qkv + static_cast<size_t>(m) * 3 * D + which * D + h * 64) + lane;
+  float2 v = __half22float2(*p);
+  const float* g = which ? kg : qg;
+  const float* b = which ? kb : qb;
+  if (g) {
+    float s = v.x + v.y;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s * (1.0f / 64.0f);
+    const float dx = v.x - mean, dy = v.y - mean;
+    float q = dx * dx + dy * dy;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    const float rstd = rsqrtf(q * (1.0f / 64.0f) + 1e-5f);
+    v.x = dx * rstd * g[2 * lane] + (b ? b[2 * lane] : 0.f);
+    v.y = dy * rstd * g[2 * lane + 1] + (b ? b[2 * lane + 1] : 0.f);
+  }
+  if (cs) {
+    const float px = __shfl_xor_sync(0xffffffffu, v.x, 8);
+    const float py = __shfl_xor_sync(0xffffffffu, v.y, 8);
+    const bool lo = (lane & 8) == 0;  // first quarter of its half: rot = -partner
+    const float rx = lo ? -px : px, ry = lo ? -py : py;
+    const int t = m % ntok;
+    const float c0 = cs[t * 64 + 2 * lane], c1 = cs[t * 64 + 2 * lane + 1];
+    const float s0 = sn[t * 64 + 2 * lane], s1 = sn[t * 64 + 2 * lane + 1];
+    v.x = v.x * c0 + rx * s0;
+    v.y = v.y * c1 + ry * s1;
+  }
+  *p = __floats2half2_rn(v.x, v.y);
+}
+int qk_norm_rope(__half* qkv, int M, int H, int D, int ntok, const float* qg, const float* qb, const float* kg,
+                 const float* kb, const float* cs, const float* sn, cudaStream_t s) {
+  if (!qg && !cs) return 0;
+  const long warps = static_cast<long>(M) * H * 2;
+  k_qk_norm_rope<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, s>>>(qkv, M, H, D, ntok, qg, qb, kg, kb,
+                                                                                 cs, sn);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// ---------------------------------------------------------------- bilinear upsample
+// Align-corners bilinear resize of NHWC f16, ggml CPU formula: sf = (dst-1)/(src-1),
+// src = i / sf, lerp between floor and floor+1 with clamps (src/dpt_blocks.cpp:87-90).
+// Optional f16 addend pe[(y*W + x)][c] (the 0.1 * UV embedding, src/dpt_head.cpp:204-209).
+__global__ void k_upsample_ac(const __half* __restrict__ in, int B, int hs, int ws, int C, __half* __restrict__ out,
+                              int H, int W, const __half* __restrict__ pe) {
+  const int c8 = C / 8;
+  const long total = static_cast<long>(B) * H * W * c8;
+  const float sf0 = (W > 1 && ws > 1) ? static_cast<float>(W - 1) / (ws - 1) : static_cast<float>(W) / ws;
+  const float sf1 = (H > 1 && hs > 1) ? static_cast<float>(H - 1) / (hs - 1) : static_cast<float>(H) / hs;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % c8) * 8;
+    const long pix = i / c8;
+    const int x = static_cast<int>(pix % W);
+    const int y = static_cast<int>((pix / W) % H);
+    const int b = static_cast<int>(pix / (static_cast<long>(W) * H));
+    const float fy = static_cast<float>(y) / sf1, fx = static_cast<float>(x) / sf0;
+    int y0 = static_cast<int>(floorf(fy)), x0 = static_cast<int>(floorf(fx));
+    int y1 = y0 + 1, x1 = x0 + 1;
+    const float dy = fminf(fmaxf(fy - floorf(fy), 0.f), 1.f), dx = fminf(fmaxf(fx - floorf(fx), 0.f), 1.f);
+    y0 = max(0, min(y0, hs - 1)); y1 = max(0, min(y1, hs - 1));
+    x0 = max(0, min(x0, ws - 1)); x1 = max(0, min(x1, ws - 1));
+    const __half* base = in + static_cast<size_t>(b) * hs * ws * C + c;
+    const uint4 ua = *reinterpret_cast<const uint4*>(base + (static_cast<size_t>(y0) * ws + x0) * C);
+    const uint4 ub = *reinterpret_cast<const uint4*>(base + (static_cast<size_t>(y0) * ws + x1) * C);
+    const uint4 uc = *reinterpret_cast<const uint4*>(base + (static_cast<size_t>(y1) * ws + x0) * C);
+    const uint4 ud = *reinterpret_cast<const uint4*>(base + (static_cast<size_t>(y1) * ws + x1) * C);
+    const __half2* ha = reinterpret_cast<const __half2*>(&ua);
+    const __half2* hb = reinterpret_cast<const __half2*>(&ub);
+    const __half2* hc = reinterpret_cast<const __half2*>(&uc);
+    const __half2* hd = reinterpret_cast<const __half2*>(&ud);
+    const float wa = (1 - dx) * (1 - dy), wb = dx * (1 - dy), wc = (1 - dx) * dy, wd = dx * dy;
+    uint4 uo;
+    __half2* ho = reinterpret_cast<__half2*>(&uo);
+    uint4 up;
+    if (pe) up = *reinterpret_cast<const uint4*>(pe + (static_cast<size_t>(y) * W + x) * C + c);
+    const __half2* hp = reinterpret_cast<const __half2*>(&up);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 a = __half22float2(ha[k]), bb = __half22float2(hb[k]), cc = __half22float2(hc[k]),
+                   d = __half22float2(hd[k]);
+      float rx = a.x * wa + bb.x * wb + cc.x * wc + d.x * wd;
+      float ry = a.y * wa + bb.y * wb + cc.y * wc + d.y * wd;
+      if (pe) {
+        const float2 q = __half22float2(hp[k]);
+        rx += q.x;
+        ry += q.y;
+      }
+      ho[k] = __floats2half2_rn(rx, ry);
+    }
+    *reinterpret_cast<uint4*>(out + pix * C + c) = uo;
+  }
+}
+int upsample_ac(const __half* in, int B, int hs, int ws, int C, __half* out, int H, int W, const __half* pe,
+                cudaStream_t s) {
+  if (C % 8) return -1;
+  const long total = static_cast<long>(B) * H * W * (C / 8);
+  k_upsample_ac<<<grid_for(total, 256), 256, 0, s>>>(in, B, hs, ws, C, out, H, W, pe);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+// ---------------------------------------------------------------- im2col (3x3, stride 2, pad 1)
+// NHWC [B][h][w][C] -> [B*ho*wo][9*icp], column = tap*icp + c (the packed conv weight
+// layout [OC][9][icp]); columns c >= C are left untouched (zeroed once by the caller).
+__global__ void k_im2col_s2(const __half* __restrict__ in, int B, int h, int w, int C, int icp, int ho, int wo,
+                            __half* __restrict__ out) {
+  const int c8 = C / 8;
+  const long total = static_cast<long>(B) * ho * wo * 9 * c8;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % c8) * 8;
+    const int tap = static_cast<int>((i / c8) % 9);
+    const long pix = i / (static_cast<long>(c8) * 9);
+    const int ox = static_cast<int>(pix % wo), oy = static_cast<int>((pix / wo) % ho);
+    const int b = static_cast<int>(pix / (static_cast<long>(wo) * ho));
+    const int iy = oy * 2 + tap / 3 - 1, ix = ox * 2 + tap % 3 - 1;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (iy >= 0 && iy < h && ix >= 0 && ix < w)
+      v = *reinterpret_cast<const uint4*>(in + ((static_cast<size_t>(b) * h + iy) * w + ix) * C + c);
+    *reinterpret_cast<uint4*>(out + pix * 9 * icp + tap * icp + c) = v;
+  }
+}
+int im2col_s2(const __half* in, int B, int h, int w, int C, int icp, __half* out, cudaStream_t s) {
+  if (C % 8 || icp < C) return -1;
+  const int ho = (h + 2 - 3) / 2 + 1, wo = (w + 2 - 3) / 2 + 1;
+  const long total = static_cast<long>(B) * ho * wo * 9 * (C / 8);
+  k_im2col_s2<<<grid_for(total, 256), 256, 0, s>>>(in, B, h, w, C, icp, ho, wo, out);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+// ---------------------------------------------------------------- reference-view selection
+// One block per scene: saddle-balanced choice over the views' token-0 features after
+// the local blocks [0, alt_start-1) (src/dino_backbone.cpp:372-412), in double.
+__global__ void k_select_ref_view(const float* __restrict__ x, int S, int ntok, int D, int* __restrict__ b_idx) {
+  extern __shared__ double sh[];
+  const int scene = blockIdx.x;
+  double* nrm = sh;              // [S]
+  double* sim = sh + S;          // [S]
+  double* var = sh + 2 * S;      // [S]
+  double* red = sh + 3 * S;      // [blockDim.x]
+  const float* base = x + static_cast<size_t>(scene) * S * ntok * D;
+  auto reduce = [&](double v) -> double {
+    red[threadIdx.x] = v;
+    __syncthreads();
+    for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+      if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+      __syncthreads();
+    }
+    const double r = red[0];
+    __syncthreads();
+    return r;
+  };
+  for (int v = 0; v < S; ++v) {
+    const float* cv = base + static_cast<size_t>(v) * ntok * D;
+    double a = 0;
+    for (int e = threadIdx.x; e < D; e += blockDim.x) a += static_cast<double>(cv[e]) * cv[e];
+    const double n = sqrt(reduce(a));
+    if (threadIdx.x == 0) nrm[v] = n;
+    __syncthreads();
+  }
+  for (int v = 0; v < S; ++v) {
+    const float* cv = base + static_cast<size_t>(v) * ntok * D;
+    const double iv = nrm[v] > 0 ? 1.0 / nrm[v] : 0.0;
+    double s = 0;
+    for (int w = 0; w < S; ++w) {
+      if (w == v) continue;
+      const float* cw = base + static_cast<size_t>(w) * ntok * D;
+      const double iw = nrm[w] > 0 ? 1.0 / nrm[w] : 0.0;
+      double a = 0;
+      for (int e = threadIdx.x; e < D; e += blockDim.x) a += (cv[e] * iv) * (cw[e] * iw);
+      s += reduce(a);
+    }
+    double m = 0;
+    for (int e = threadIdx.x; e < D; e += blockDim.x) m += cv[e] * iv;
+    const double mean = reduce(m) / D;
+    double q = 0;
+    for (int e = threadIdx.x; e < D; e += blockDim.x) {
+      const double d = cv[e] * iv - mean;
+      q += d * d;
+    }
+    const double vv = reduce(q) / (D - 1);
+    if (threadIdx.x == 0) {
+      sim[v] = s / (S - 1);
+      var[v] = vv;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    double* arrs[3] = {sim, nrm, var};
+    for (int k = 0; k < 3; ++k) {
+      double mn = arrs[k][0], mx = arrs[k][0];
+      for (int v = 0; v < S; ++v) { mn = fmin(mn, arrs[k][v]); mx = fmax(mx, arrs[k][v]); }
+      for (int v = 0; v < S; ++v) arrs[k][v] = (arrs[k][v] - mn) / (mx - mn + 1e-8);
+    }
+    int best = 0;
+    double bb = 1e300;
+    for (int v = 0; v < S; ++v) {
+      const double bal = fabs(sim[v] - 0.5) + fabs(nrm[v] - 0.5) + fabs(var[v] - 0.5);
+      if (bal < bb) { bb = bal; best = v; }
+    }
+    b_idx[scene] = best;
+  }
+}
+int select_ref_view(const float* x, int scenes, int S, int ntok, int D, int* b_idx, cudaStream_t s) {
+  const int threads = 256;
+  const size_t shm = (3 * S + threads) * sizeof(double);
+  k_select_ref_view<<<scenes, threads, shm, s>>>(x, S, ntok, D, b_idx);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// Processing position q of a scene holds original view order[q]: order[0] = b,
+// order[q] = q-1 for 1 <= q <= b, q otherwise (src/dino_backbone.cpp:435-441).
+__device__ __forceinline__ int view_at(int q, int b) { return q == 0 ? b : (q <= b ? q - 1 : q); }
+
+// dst[scene][q] = src[scene][order[q]] for rows of `row_elems` floats per view.
+__global__ void k_permute_views(const float* __restrict__ src, float* __restrict__ dst, int scenes, int S,
+                                long view_elems, const int* __restrict__ b_idx) {
+  const long per_scene = static_cast<long>(S) * view_elems;
+  const long total4 = static_cast<long>(scenes) * per_scene / 4;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total4;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const long e = i * 4;
+    const int scene = static_cast<int>(e / per_scene);
+    const long r = e % per_scene;
+    const int q = static_cast<int>(r / view_elems);
+    const long off = r % view_elems;
+    const int v = view_at(q, b_idx[scene]);
+    *reinterpret_cast<float4*>(dst + e) =
+        *reinterpret_cast<const float4*>(src + static_cast<size_t>(scene) * per_scene + v * view_elems + off);
+  }
+}
+int permute_views(const float* src, float* dst, int scenes, int S, long view_elems, const int* b_idx, cudaStream_t s) {
+  if (view_elems % 4) return -1;
+  const long total4 = static_cast<long>(scenes) * S * view_elems / 4;
+  k_permute_views<<<grid_for(total4, 256), 256, 0, s>>>(src, dst, scenes, S, view_elems, b_idx);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+// Inverse for f16 feature rows: dst[scene][t] = src[scene][q] with view_at(q) == t.
+__global__ void k_unpermute_views_h(const __half* __restrict__ src, __half* __restrict__ dst, int scenes, int S,
+                                    long view_elems, const int* __restrict__ b_idx) {
+  const long per_scene = static_cast<long>(S) * view_elems;
+  const long total8 = static_cast<long>(scenes) * per_scene / 8;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total8;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const long e = i * 8;
+    const int scene = static_cast<int>(e / per_scene);
+    const long r = e % per_scene;
+    const int t = static_cast<int>(r / view_elems);
+    const long off = r % view_elems;
+    const int b = b_idx[scene];
+    const int q = t < b ? t + 1 : (t == b ? 0 : t);
+    *reinterpret_cast<uint4*>(dst + e) =
+        *reinterpret_cast<const uint4*>(src + static_cast<size_t>(scene) * per_scene + q * view_elems + off);
+  }
+}
+int unpermute_views_h(const __half* src, __half* dst, int scenes, int S, long view_elems, const int* b_idx,
+                      cudaStream_t s) {
+  if (view_elems % 8) return -1;
+  const long total8 = static_cast<long>(scenes) * S * view_elems / 8;
+  k_unpermute_views_h<<<grid_for(total8, 256), 256, 0, s>>>(src, dst, scenes, S, view_elems, b_idx);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+}  // namespace da3b

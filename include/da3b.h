@@ -74,6 +74,56 @@ DA3B_API int da3b_conv_nhwc(const void* x, int B, int H, int W, int IC, const vo
                             int ksize, const float* bias, const void* res1, const void* res2, int act,
                             void* out, void* out_relu, void* stream);
 
+
+/* ======================================================================
+ * Model-level entry points (batched depth path). A context is the same
+ * da_ctx as the reference-compatible C ABI in da3cpp/da3_c.h.
+ * ====================================================================== */
+typedef struct da_ctx da_ctx;
+
+/* Loads a GGUF (DA3cpplib weight layout) onto CUDA device `device`: the
+ * replacement of Engine::load + ModelLoader::offload_weights
+ * (src/engine.cpp:24-66, src/model_loader.cpp:166-220). NULL on failure. */
+DA3B_API da_ctx* da3b_load(const char* gguf_path, int device);
+
+/* Processed size of a w x h input under the reference preprocessing policy
+ * (preprocess_real, src/preprocess.cpp:157-197; legacy=1: floor-to-patch,
+ * src/preprocess.cpp:26-41). *needs_resize = 1 when the image must be resampled. */
+DA3B_API int da3b_processed_size(da_ctx* ctx, int w, int h, int legacy, int* out_h, int* out_w, int* needs_resize);
+
+/* Depth of n_views RGB8 images [n_views][h][w][3] (device memory), h and w at the
+ * processed size. views_per_scene consecutive views share global attention (1 =
+ * independent images, the path of Engine::depth_native_fused / depth_relative,
+ * src/engine.cpp:121-130, :189-229; > 1 = Engine::depth_pose_multi's backbone,
+ * src/engine.cpp:352-384). Outputs (device memory, f32): depth [n][h][w], conf
+ * [n][h][w] (DA3 only, may be NULL), rays [7][n][8h/14][8w/14] (aux ray head, may
+ * be NULL). Asynchronous on `stream` after the first call of a shape. */
+DA3B_API int da3b_infer_device(da_ctx* ctx, const void* rgb_dev, int n_views, int views_per_scene, int h, int w,
+                               void* depth_dev, void* conf_dev, void* rays_dev, void* stream);
+
+/* Same with host buffers (copies included); returns after the results are on the host. */
+DA3B_API int da3b_infer_host(da_ctx* ctx, const void* rgb_host, int n_views, int views_per_scene, int h, int w,
+                             float* depth_host, float* conf_host, float* rays_host);
+
+/* Reference view chosen per scene by the last multi-view run (views_per_scene >= 3). */
+DA3B_API int da3b_ref_views(da_ctx* ctx, int* out, int n);
+/* Kernel launches of one forward of that shape (after one run of it). */
+DA3B_API int da3b_launches(da_ctx* ctx, int n_views, int views_per_scene, int h, int w, int rays);
+/* Out-layer feature map of the last run (f16 [rows][cols], token 0 dropped) copied to host. */
+DA3B_API int da3b_debug_feature(da_ctx* ctx, int layer, void* out_f16, size_t capacity, int* rows, int* cols);
+/* 1 = replay captured CUDA graphs (default), 0 = eager launches. */
+DA3B_API int da3b_set_graphs(da_ctx* ctx, int on);
+/* 1 (default) = activations entering each Q8_0 linear are rounded through Q8_0 the
+ * way ggml quantises them before its Q8_0 x Q8_0 dot products (ggml_mul_mat on
+ * CPU, src/ggml_extend.hpp:6-10), so results follow the reference's numerics;
+ * 0 = plain f16 activations. */
+DA3B_API int da3b_set_act_quant(da_ctx* ctx, int on);
+/* 1 = the depth / confidence / ray outputs are the raw head logits (no output
+ * activation), for parity checks against pre-activation reference values. */
+DA3B_API int da3b_set_raw_logits(da_ctx* ctx, int on);
+/* out[8] = {embed_dim, depth, num_heads, patch_size, cat_token, output_dim, has_aux, is_da2} */
+DA3B_API int da3b_model_dims(da_ctx* ctx, int* out);
+
 #ifdef __cplusplus
 }
 #endif

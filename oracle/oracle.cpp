@@ -1,0 +1,1214 @@
+// CPU ORACLE — test infrastructure only; never linked into or called by libda3b.
+//
+// A CPU restatement of DA3cpplib's depth hot path (preprocess -> DINOv2 backbone ->
+// DPT head -> output activation), written to follow the reference's arithmetic:
+// ggml CPU semantics for every graph op the reference builds (Q8_0 matmul with
+// activations quantised to Q8_0 per 32-block, ggml_norm with double sums, online-
+// softmax flash attention in f32, align-corners bilinear interpolation), and the
+// reference's own host code for pos-embed interpolation, RoPE tables, UV embedding,
+// preprocessing and output activations. Citations are path:line in DA3cpplib.
+//
+// PARITY UNPINNED against the reference itself: DA3cpplib cannot be built here (its
+// ggml submodule is empty) and its tests ship no golden vectors for this path. The
+// Q8_0 quantiser is pinned bit-exactly against gguf-py's published quantiser, and the
+// DA2 architecture against an independent implementation (tests/test_oracle_*.py).
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <algorithm>
+#include <cmath>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define OR_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+// ------------------------------------------------------------------ fp16
+float h2f(uint16_t h) {
+  const uint32_t s = (h >> 15) & 1, e = (h >> 10) & 0x1f, m = h & 0x3ff;
+  uint32_t bits;
+  if (e == 0) {
+    if (m == 0) {
+      bits = s << 31;
+    } else {  // subnormal
+      int ee = -1;
+      uint32_t mm = m;
+      do { ++ee; mm <<= 1; } while (!(mm & 0x400));
+      bits = (s << 31) | ((127 - 15 - ee) << 23) | ((mm & 0x3ff) << 13);
+    }
+  } else if (e == 31) {
+    bits = (s << 31) | 0x7f800000u | (m << 13);
+  } else {
+    bits = (s << 31) | ((e - 15 + 127) << 23) | (m << 13);
+  }
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+uint16_t f2h(float f) {  // round to nearest even
+  uint32_t x;
+  memcpy(&x, &f, 4);
+  const uint32_t sign = (x >> 16) & 0x8000;
+  const uint32_t absx = x & 0x7fffffffu;
+  if (absx >= 0x7f800000u) return sign | 0x7c00 | (absx > 0x7f800000u ? 0x200 : 0);
+  if (absx >= 0x477ff000u) return sign | 0x7c00;  // overflow
+  if (absx < 0x38800000u) {                        // subnormal / zero
+    if (absx < 0x33000000u) return sign;
+    const uint32_t e = absx >> 23;
+    const uint32_t m = (absx & 0x7fffff) | 0x800000;
+    const int shift = 126 - e;  // 14 + (113 - e)
+    const uint32_t r = m >> shift;
+    const uint32_t rem = m & ((1u << shift) - 1), half = 1u << (shift - 1);
+    return sign | (r + ((rem > half) || (rem == half && (r & 1))));
+  }
+  const uint32_t e = (absx >> 23) - 127 + 15;
+  const uint32_t m = absx & 0x7fffff;
+  uint32_t h = (e << 10) | (m >> 13);
+  const uint32_t rem = m & 0x1fff;
+  if (rem > 0x1000 || (rem == 0x1000 && (h & 1))) ++h;
+  return sign | h;
+}
+
+struct Tensor {
+  const void* data = nullptr;
+  int type = 0;  // ggml type id: 0 f32, 1 f16, 8 q8_0
+  int64_t ne[4] = {1, 1, 1, 1};
+  int64_t nel() const { return ne[0] * ne[1] * ne[2] * ne[3]; }
+};
+
+}  // namespace
+
+extern "C" {
+typedef struct {
+  const char* name;
+  const void* data;
+  int type;
+  int64_t ne[4];
+} or_tensor;
+
+typedef struct {
+  int patch_size, embed_dim, depth, num_heads, head_dim, mlp_hidden, pos_embed_grid;
+  int alt_start, rope_start, qknorm_start;
+  float rope_freq, ln_eps, interp_offset;
+  int cat_token, head_pos_embed, is_da2;
+  int head_features;
+  int n_out_layers;
+  int out_layers[4];
+  int head_out_channels[4];
+  float img_mean[3], img_std[3];
+  int resize_target, resize_upper;
+  float head_max_depth;
+  int act_quant;
+  int n_threads;
+} or_config;
+}
+
+namespace {
+
+// ------------------------------------------------------------------ Q8_0
+// ggml quantize_row_q8_0 reference: d = amax/127, id = d ? 1/d : 0, q = roundf(x*id),
+// d stored as fp16 (third-party ggml, ggml-quants.c; same algorithm as gguf-py
+// quants.py:378-401).
+struct QBlocks {
+  std::vector<float> d;     // fp16-rounded scale per block, as f32
+  std::vector<int8_t> q;    // 32 per block
+};
+
+void quantize_row(const float* x, int K, float* d_out, int8_t* q_out) {
+  for (int b = 0; b < K / 32; ++b) {
+    float amax = 0.f;
+    for (int i = 0; i < 32; ++i) amax = std::max(amax, std::fabs(x[b * 32 + i]));
+    const float d = amax / 127.0f;
+    const float id = d != 0.f ? 1.0f / d : 0.0f;
+    d_out[b] = h2f(f2h(d));
+    for (int i = 0; i < 32; ++i) q_out[b * 32 + i] = static_cast<int8_t>(roundf(x[b * 32 + i] * id));
+  }
+}
+
+class Oracle {
+ public:
+  or_config c;
+  std::map<std::string, Tensor> t;
+  std::map<std::string, std::vector<float>> f32cache;
+  std::map<std::string, std::vector<float>> caps;  // captures for parity tests
+
+  bool has(const std::string& n) const { return t.count(n) > 0; }
+  const Tensor& T(const std::string& n) const {
+    static Tensor empty;
+    auto it = t.find(n);
+    return it == t.end() ? empty : it->second;
+  }
+  // f32 view of an f32/f16/q8_0 tensor (converted once and cached).
+  const float* F(const std::string& n) {
+    auto it = t.find(n);
+    if (it == t.end()) return nullptr;
+    const Tensor& x = it->second;
+    if (x.type == 0) return static_cast<const float*>(x.data);
+    auto c2 = f32cache.find(n);
+    if (c2 != f32cache.end()) return c2->second.data();
+    std::vector<float> v(x.nel());
+    if (x.type == 1) {
+      const uint16_t* h = static_cast<const uint16_t*>(x.data);
+      for (int64_t i = 0; i < x.nel(); ++i) v[i] = h2f(h[i]);
+    } else if (x.type == 8) {
+      const uint8_t* p = static_cast<const uint8_t*>(x.data);
+      for (int64_t b = 0; b < x.nel() / 32; ++b) {
+        uint16_t dh;
+        memcpy(&dh, p + b * 34, 2);
+        const float d = h2f(dh);
+        const int8_t* q = reinterpret_cast<const int8_t*>(p + b * 34 + 2);
+        for (int i = 0; i < 32; ++i) v[b * 32 + i] = d * q[i];
+      }
+    }
+    return f32cache.emplace(n, std::move(v)).first->second.data();
+  }
+
+  // ---------------------------------------------------------------- linear
+  // y[M][N] = x[M][K] W^T + b  — ggml_mul_mat(W, x) + ggml_add (src/ggml_extend.hpp:6-10).
+  // Q8_0 W with act_quant: activations quantised to Q8_0, per-block int32 dot,
+  // sumf += isum * (d_w * d_x) in block order (ggml vec_dot_q8_0_q8_0).
+  void linear(const float* x, int M, int K, const std::string& wn, const std::string& bn, float* y) {
+    const Tensor& W = T(wn);
+    const int N = static_cast<int>(W.ne[1]);
+    const float* bias = bn.empty() ? nullptr : F(bn);
+    if (W.type == 8 && c.act_quant) {
+      const int nb = K / 32;
+      std::vector<float> dx(static_cast<size_t>(M) * nb);
+      std::vector<int8_t> qx(static_cast<size_t>(M) * K);
+#pragma omp parallel for schedule(static)
+      for (int m = 0; m < M; ++m) quantize_row(x + static_cast<size_t>(m) * K, K, &dx[static_cast<size_t>(m) * nb], &qx[static_cast<size_t>(m) * K]);
+      const uint8_t* wp = static_cast<const uint8_t*>(W.data);
+      std::vector<float> dw(static_cast<size_t>(N) * nb);
+      std::vector<int8_t> qw(static_cast<size_t>(N) * K);
+      for (int n = 0; n < N; ++n)
+        for (int b = 0; b < nb; ++b) {
+          const uint8_t* blk = wp + (static_cast<size_t>(n) * nb + b) * 34;
+          uint16_t dh;
+          memcpy(&dh, blk, 2);
+          dw[static_cast<size_t>(n) * nb + b] = h2f(dh);
+          memcpy(&qw[static_cast<size_t>(n) * K + b * 32], blk + 2, 32);
+        }
+      const int NB = 16;
+#pragma omp parallel for schedule(dynamic, 1) collapse(2)
+      for (int n0 = 0; n0 < N; n0 += NB)
+        for (int m0 = 0; m0 < M; m0 += 64)
+          for (int m = m0; m < std::min(M, m0 + 64); ++m) {
+            const int8_t* xq = &qx[static_cast<size_t>(m) * K];
+            const float* xd = &dx[static_cast<size_t>(m) * nb];
+            for (int n = n0; n < std::min(N, n0 + NB); ++n) {
+              const int8_t* wq = &qw[static_cast<size_t>(n) * K];
+              const float* wd = &dw[static_cast<size_t>(n) * nb];
+              float sumf = 0.f;
+              for (int b = 0; b < nb; ++b) {
+                int isum = 0;
+                const int8_t* a = wq + b * 32;
+                const int8_t* q = xq + b * 32;
+                for (int i = 0; i < 32; ++i) isum += static_cast<int>(a[i]) * static_cast<int>(q[i]);
+                sumf += static_cast<float>(isum) * (wd[b] * xd[b]);
+              }
+              y[static_cast<size_t>(m) * N + n] = sumf + (bias ? bias[n] : 0.f);
+            }
+          }
+      return;
+    }
+    const float* w = F(wn);
+    sgemm_nt(x, M, K, w, N, y);
+    if (bias)
+      for (int m = 0; m < M; ++m)
+        for (int n = 0; n < N; ++n) y[static_cast<size_t>(m) * N + n] += bias[n];
+  }
+
+  // y[M][N] = x[M][K] * w[N][K]^T in f32.
+  static void sgemm_nt(const float* x, int M, int K, const float* w, int N, float* y) {
+#pragma omp parallel for schedule(dynamic, 1) collapse(2)
+    for (int m0 = 0; m0 < M; m0 += 32)
+      for (int n0 = 0; n0 < N; n0 += 32)
+        for (int m = m0; m < std::min(M, m0 + 32); ++m)
+          for (int n = n0; n < std::min(N, n0 + 32); ++n) {
+            const float* a = x + static_cast<size_t>(m) * K;
+            const float* b = w + static_cast<size_t>(n) * K;
+            float s = 0.f;
+            for (int k = 0; k < K; ++k) s += a[k] * b[k];
+            y[static_cast<size_t>(m) * N + n] = s;
+          }
+  }
+
+  // ggml_norm (double sums) * w + b  (src/ggml_extend.hpp:12-17).
+  static void layernorm_rows(const float* x, int M, int D, const float* w, const float* b, float eps, float* y) {
+#pragma omp parallel for schedule(static)
+    for (int m = 0; m < M; ++m) {
+      const float* r = x + static_cast<size_t>(m) * D;
+      float* o = y + static_cast<size_t>(m) * D;
+      double sum = 0.0;
+      for (int i = 0; i < D; ++i) sum += r[i];
+      const float mean = static_cast<float>(sum / D);
+      double sum2 = 0.0;
+      for (int i = 0; i < D; ++i) {
+        const float v = r[i] - mean;
+        o[i] = v;
+        sum2 += static_cast<double>(v * v);
+      }
+      const float var = static_cast<float>(sum2 / D);
+      const float scale = 1.0f / sqrtf(var + eps);
+      for (int i = 0; i < D; ++i) {
+        o[i] *= scale;
+        o[i] = o[i] * w[i];
+        if (b) o[i] += b[i];
+      }
+    }
+  }
+
+  // Host double-precision LayerNorm used for DA2 features (src/dino_backbone.cpp:174-181).
+  static void layernorm_host(const float* row, int D, const float* w, const float* b, float eps, float* o) {
+    double mean = 0;
+    for (int e = 0; e < D; ++e) mean += row[e];
+    mean /= D;
+    double var = 0;
+    for (int e = 0; e < D; ++e) {
+      const double d = row[e] - mean;
+      var += d * d;
+    }
+    var /= D;
+    const double inv = 1.0 / std::sqrt(var + static_cast<double>(eps));
+    for (int e = 0; e < D; ++e) o[e] = static_cast<float>((row[e] - mean) * inv) * w[e] + b[e];
+  }
+
+  // ---------------------------------------------------------------- RoPE
+  // build_rope_tables (src/rope2d.cpp:4-27): head_dim split into y-half and x-half,
+  // rotate-half within each half, inv_freq = freq^(-2j/half).
+  struct Rope {
+    std::vector<float> cos, sin;
+    int hd = 0;
+  };
+  Rope rope_tables(const std::vector<float>& pos_yx, int tokens) const {
+    Rope r;
+    const int hd = c.head_dim, half = hd / 2, quart = half / 2;
+    r.hd = hd;
+    r.cos.assign(static_cast<size_t>(hd) * tokens, 0.f);
+    r.sin.assign(static_cast<size_t>(hd) * tokens, 0.f);
+    for (int tk = 0; tk < tokens; ++tk) {
+      const float y = pos_yx[2 * tk], x = pos_yx[2 * tk + 1];
+      for (int j = 0; j < quart; ++j) {
+        const float invf = std::pow(c.rope_freq, -2.f * static_cast<float>(j) / static_cast<float>(half));
+        const float ay = y * invf, ax = x * invf;
+        float* cs = &r.cos[static_cast<size_t>(tk) * hd];
+        float* sn = &r.sin[static_cast<size_t>(tk) * hd];
+        cs[j] = cs[j + quart] = std::cos(ay);
+        sn[j] = sn[j + quart] = std::sin(ay);
+        cs[half + j] = cs[half + j + quart] = std::cos(ax);
+        sn[half + j] = sn[half + j + quart] = std::sin(ax);
+      }
+    }
+    return r;
+  }
+  // apply_rope (src/rope2d.cpp:36-52): x*cos + rot(x)*sin, rot = [-h1, h0] per half.
+  static void apply_rope(float* v, const float* cs, const float* sn, int hd) {
+    const int half = hd / 2, quart = half / 2;
+    float rot[256];
+    for (int h = 0; h < 2; ++h)
+      for (int j = 0; j < quart; ++j) {
+        rot[h * half + j] = -v[h * half + quart + j];
+        rot[h * half + quart + j] = v[h * half + j];
+      }
+    for (int i = 0; i < hd; ++i) v[i] = v[i] * cs[i] + rot[i] * sn[i];
+  }
+
+  // ---------------------------------------------------------------- attention
+  // attention (src/attention.cpp:44-96), flash path: per head, online softmax in f32
+  // with expf, scale = 1/sqrt(head_dim) (ggml CPU flash_attn_ext with f32 K/V).
+  void attention(const float* xn, int nseq, int seqlen, int blk, const Rope* rope, float* out) {
+    const int D = c.embed_dim, H = c.num_heads, hd = c.head_dim;
+    const int M = nseq * seqlen;
+    const std::string p = "vit.blk." + std::to_string(blk) + ".";
+    std::vector<float> qkv(static_cast<size_t>(M) * 3 * D);
+    linear(xn, M, D, p + "attn_qkv.weight", has(p + "attn_qkv.bias") ? p + "attn_qkv.bias" : "", qkv.data());
+    const bool qkn = has(p + "attn_qnorm.weight");
+    const float *qw = F(p + "attn_qnorm.weight"), *qb = F(p + "attn_qnorm.bias");
+    const float *kw = F(p + "attn_knorm.weight"), *kb = F(p + "attn_knorm.bias");
+    // QK-norm (eps 1e-5, src/vit_block.cpp:5-11) then RoPE, per (token, head).
+#pragma omp parallel for schedule(static)
+    for (int m = 0; m < M; ++m) {
+      const int tk = m % seqlen;
+      for (int h = 0; h < H; ++h) {
+        float* q = &qkv[static_cast<size_t>(m) * 3 * D + h * hd];
+        float* k = q + D;
+        if (qkn) {
+          layernorm_rows(q, 1, hd, qw, qb, 1e-5f, q);
+          layernorm_rows(k, 1, hd, kw, kb, 1e-5f, k);
+        }
+        if (rope) {
+          apply_rope(q, &rope->cos[static_cast<size_t>(tk) * hd], &rope->sin[static_cast<size_t>(tk) * hd], hd);
+          apply_rope(k, &rope->cos[static_cast<size_t>(tk) * hd], &rope->sin[static_cast<size_t>(tk) * hd], hd);
+        }
+      }
+    }
+    const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
+    std::vector<float> o(static_cast<size_t>(M) * D);
+#pragma omp parallel for schedule(dynamic, 4) collapse(2)
+    for (int s = 0; s < nseq; ++s)
+      for (int qi = 0; qi < seqlen; ++qi)
+        for (int h = 0; h < H; ++h) {
+          const float* q = &qkv[(static_cast<size_t>(s) * seqlen + qi) * 3 * D + h * hd];
+          float acc[256];
+          for (int d = 0; d < hd; ++d) acc[d] = 0.f;
+          float Mx = -INFINITY, S = 0.f;
+          for (int ki = 0; ki < seqlen; ++ki) {
+            const float* k = &qkv[(static_cast<size_t>(s) * seqlen + ki) * 3 * D + D + h * hd];
+            const float* v = k + D;
+            float sc = 0.f;
+            for (int d = 0; d < hd; ++d) sc += q[d] * k[d];
+            sc *= scale;
+            float ms = 1.f, vs = 1.f;
+            if (sc > Mx) {
+              const float Mold = Mx;
+              Mx = sc;
+              ms = expf(Mold - Mx);
+              for (int d = 0; d < hd; ++d) acc[d] *= ms;
+            } else {
+              vs = expf(sc - Mx);
+            }
+            for (int d = 0; d < hd; ++d) acc[d] += v[d] * vs;
+            S = S * ms + vs;
+          }
+          float* od = &o[(static_cast<size_t>(s) * seqlen + qi) * D + h * hd];
+          const float inv = S == 0.f ? 0.f : 1.0f / S;
+          for (int d = 0; d < hd; ++d) od[d] = acc[d] * inv;
+        }
+    linear(o.data(), M, D, p + "attn_proj.weight", has(p + "attn_proj.bias") ? p + "attn_proj.bias" : "", out);
+  }
+
+  // vit_block (src/vit_block.cpp:30-58): x += ls1*Attn(LN1 x); x += ls2*fc2(gelu(fc1(LN2 x))).
+  void vit_block(float* x, int nseq, int seqlen, int blk, const Rope* rope) {
+    const int D = c.embed_dim, M = nseq * seqlen, Hm = c.mlp_hidden;
+    const std::string p = "vit.blk." + std::to_string(blk) + ".";
+    std::vector<float> xn(static_cast<size_t>(M) * D), a(static_cast<size_t>(M) * D);
+    layernorm_rows(x, M, D, F(p + "norm1.weight"), F(p + "norm1.bias"), c.ln_eps, xn.data());
+    attention(xn.data(), nseq, seqlen, blk, rope, a.data());
+    const float* ls1 = F(p + "ls1");
+    for (size_t i = 0; i < a.size(); ++i) x[i] += ls1 ? a[i] * ls1[i % D] : a[i];
+    layernorm_rows(x, M, D, F(p + "norm2.weight"), F(p + "norm2.bias"), c.ln_eps, xn.data());
+    std::vector<float> h(static_cast<size_t>(M) * Hm);
+    linear(xn.data(), M, D, p + "mlp_fc1.weight", p + "mlp_fc1.bias", h.data());
+#pragma omp parallel for schedule(static)
+    for (size_t i = 0; i < h.size(); ++i) h[i] = 0.5f * h[i] * (1.0f + erff(h[i] * 0.70710678118654752440f));
+    linear(h.data(), M, Hm, p + "mlp_fc2.weight", p + "mlp_fc2.bias", a.data());
+    const float* ls2 = F(p + "ls2");
+    for (size_t i = 0; i < a.size(); ++i) x[i] += ls2 ? a[i] * ls2[i % D] : a[i];
+  }
+
+  // ---------------------------------------------------------------- embeddings
+  static float cubic(float x) {  // a = -0.75 (src/dino_backbone.cpp:12-17)
+    const float a = -0.75f;
+    x = std::fabs(x);
+    if (x < 1) return ((a + 2) * x - (a + 3)) * x * x + 1;
+    if (x < 2) return (((x - 5) * x + 8) * x - 4) * a;
+    return 0;
+  }
+  // interp_pos_embed (src/dino_backbone.cpp:18-56): always bicubic with the offset.
+  std::vector<float> interp_pos_embed(int gh, int gw) {
+    const int E = c.embed_dim, Mg = c.pos_embed_grid;
+    const float* p = F("vit.pos_embed");
+    std::vector<float> out(static_cast<size_t>(1 + gh * gw) * E);
+    for (int ch = 0; ch < E; ++ch) out[ch] = p[ch];
+    const float sx = static_cast<float>(gw + c.interp_offset) / Mg, sy = static_cast<float>(gh + c.interp_offset) / Mg;
+    for (int oy = 0; oy < gh; ++oy) {
+      const float iy = (oy + 0.5f) / sy - 0.5f;
+      const int y0 = static_cast<int>(std::floor(iy));
+      const float fy = iy - y0;
+      for (int ox = 0; ox < gw; ++ox) {
+        const float ix = (ox + 0.5f) / sx - 0.5f;
+        const int x0 = static_cast<int>(std::floor(ix));
+        const float fx = ix - x0;
+        const int orow = 1 + oy * gw + ox;
+        for (int ch = 0; ch < E; ++ch) {
+          float acc = 0;
+          for (int m = -1; m <= 2; ++m) {
+            const float wy = cubic(fy - m);
+            const int yy = std::min(std::max(y0 + m, 0), Mg - 1);
+            for (int n = -1; n <= 2; ++n) {
+              const float wx = cubic(fx - n);
+              const int xx = std::min(std::max(x0 + n, 0), Mg - 1);
+              acc += wy * wx * p[static_cast<size_t>(1 + yy * Mg + xx) * E + ch];
+            }
+          }
+          out[static_cast<size_t>(orow) * E + ch] = acc;
+        }
+      }
+    }
+    return out;
+  }
+
+  // Patch embed conv k14 s14 + bias, CLS concat, + pos-embed (src/dino_backbone.cpp:117-126).
+  void embed(const float* chw, int H, int W, const std::vector<float>& pos, float* x) {
+    const int P = c.patch_size, E = c.embed_dim, gh = H / P, gw = W / P;
+    const float* pw = F("vit.patch_embed.weight");  // [E][3][P][P]
+    const float* pb = F("vit.patch_embed.bias");
+    const float* cls = F("vit.cls_token");
+    for (int e = 0; e < E; ++e) x[e] = cls[e] + pos[e];
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < gh * gw; ++t) {
+      const int py = t / gw, px = t % gw;
+      for (int e = 0; e < E; ++e) {
+        float s = 0.f;
+        for (int ch = 0; ch < 3; ++ch)
+          for (int ky = 0; ky < P; ++ky) {
+            const float* img = chw + (static_cast<size_t>(ch) * H + py * P + ky) * W + px * P;
+            const float* w = pw + ((static_cast<size_t>(e) * 3 + ch) * P + ky) * P;
+            for (int kx = 0; kx < P; ++kx) s += w[kx] * img[kx];
+          }
+        x[static_cast<size_t>(1 + t) * E + e] = s + pb[e] + pos[static_cast<size_t>(1 + t) * E + e];
+      }
+    }
+  }
+
+  // ---------------------------------------------------------------- head ops (NCHW per image)
+  struct Map {
+    int C = 0, H = 0, W = 0;
+    std::vector<float> v;  // [C][H][W]
+    Map() {}
+    Map(int c_, int h_, int w_) : C(c_), H(h_), W(w_), v(static_cast<size_t>(c_) * h_ * w_, 0.f) {}
+    float* ch(int cc) { return &v[static_cast<size_t>(cc) * H * W]; }
+    const float* ch(int cc) const { return &v[static_cast<size_t>(cc) * H * W]; }
+  };
+
+  // conv2d with ggml kernel [KW,KH,IC,OC] (= torch [OC][IC][KH][KW]) f32, stride s, pad p,
+  // optional bias (src/dpt_blocks.cpp:18-66, direct f32 semantics).
+  Map conv2d(const Map& x, const std::string& wn, const std::string& bn, int stride, int pad) {
+    const Tensor& Wt = T(wn);
+    const int ks = static_cast<int>(Wt.ne[0]), IC = static_cast<int>(Wt.ne[2]), OC = static_cast<int>(Wt.ne[3]);
+    const float* w = F(wn);
+    const float* b = (!bn.empty() && has(bn)) ? F(bn) : nullptr;
+    const int Ho = (x.H + 2 * pad - ks) / stride + 1, Wo = (x.W + 2 * pad - ks) / stride + 1;
+    Map y(OC, Ho, Wo);
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int oc = 0; oc < OC; ++oc) {
+      float* out = y.ch(oc);
+      for (int i = 0; i < Ho * Wo; ++i) out[i] = 0.f;
+      for (int ic = 0; ic < IC; ++ic) {
+        const float* in = x.ch(ic);
+        for (int ky = 0; ky < ks; ++ky)
+          for (int kx = 0; kx < ks; ++kx) {
+            const float wv = w[((static_cast<size_t>(oc) * IC + ic) * ks + ky) * ks + kx];
+            for (int oy = 0; oy < Ho; ++oy) {
+              const int iy = oy * stride + ky - pad;
+              if (iy < 0 || iy >= x.H) continue;
+              const float* row = in + static_cast<size_t>(iy) * x.W;
+              float* orow = out + static_cast<size_t>(oy) * Wo;
+              if (stride == 1) {
+                const int x0 = std::max(0, pad - kx), x1 = std::min(Wo, x.W + pad - kx);
+                const float* r2 = row + kx - pad;
+                for (int ox = x0; ox < x1; ++ox) orow[ox] += wv * r2[ox];
+              } else {
+                for (int ox = 0; ox < Wo; ++ox) {
+                  const int ix = ox * stride + kx - pad;
+                  if (ix >= 0 && ix < x.W) orow[ox] += wv * row[ix];
+                }
+              }
+            }
+          }
+      }
+      if (b)
+        for (int i = 0; i < Ho * Wo; ++i) out[i] += b[oc];
+    }
+    return y;
+  }
+
+  // conv_transpose2d_p0 with stride == kernel; ggml kernel [KW,KH,OC,IC]
+  // (= torch [IC][OC][KH][KW]) (src/dpt_blocks.cpp:68-85).
+  Map convT(const Map& x, const std::string& wn, const std::string& bn, int S) {
+    const Tensor& Wt = T(wn);
+    const int OC = static_cast<int>(Wt.ne[2]), IC = static_cast<int>(Wt.ne[3]);
+    const float* w = F(wn);
+    const float* b = has(bn) ? F(bn) : nullptr;
+    Map y(OC, x.H * S, x.W * S);
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int oc = 0; oc < OC; ++oc)
+      for (int ky = 0; ky < S; ++ky)
+        for (int kx = 0; kx < S; ++kx) {
+          float* out = y.ch(oc);
+          for (int iy = 0; iy < x.H; ++iy)
+            for (int ix = 0; ix < x.W; ++ix) out[static_cast<size_t>(iy * S + ky) * y.W + ix * S + kx] = b ? b[oc] : 0.f;
+          for (int ic = 0; ic < IC; ++ic) {
+            const float wv = w[((static_cast<size_t>(ic) * OC + oc) * S + ky) * S + kx];
+            const float* in = x.ch(ic);
+            for (int iy = 0; iy < x.H; ++iy)
+              for (int ix = 0; ix < x.W; ++ix)
+                out[static_cast<size_t>(iy * S + ky) * y.W + ix * S + kx] += wv * in[static_cast<size_t>(iy) * x.W + ix];
+          }
+        }
+    return y;
+  }
+
+  // ggml_interpolate bilinear + align corners (src/dpt_blocks.cpp:87-90): ggml CPU
+  // upscale with pixel_offset 0 and sf = (dst-1)/(src-1), y = i / sf.
+  static Map interp_ac(const Map& x, int ow, int oh) {
+    Map y(x.C, oh, ow);
+    const float sf0 = (ow > 1 && x.W > 1) ? static_cast<float>(ow - 1) / (x.W - 1) : static_cast<float>(ow) / x.W;
+    const float sf1 = (oh > 1 && x.H > 1) ? static_cast<float>(oh - 1) / (x.H - 1) : static_cast<float>(oh) / x.H;
+#pragma omp parallel for schedule(static)
+    for (int cc = 0; cc < x.C; ++cc) {
+      const float* in = x.ch(cc);
+      float* out = y.ch(cc);
+      for (int i1 = 0; i1 < oh; ++i1) {
+        const float fy = static_cast<float>(i1) / sf1;
+        int64_t y0 = static_cast<int64_t>(floorf(fy)), y1 = y0 + 1;
+        y0 = std::max<int64_t>(0, std::min<int64_t>(y0, x.H - 1));
+        y1 = std::max<int64_t>(0, std::min<int64_t>(y1, x.H - 1));
+        float dy = fy - floorf(fy);
+        dy = std::max(0.0f, std::min(dy, 1.0f));
+        for (int i0 = 0; i0 < ow; ++i0) {
+          const float fx = static_cast<float>(i0) / sf0;
+          int64_t x0 = static_cast<int64_t>(floorf(fx)), x1 = x0 + 1;
+          x0 = std::max<int64_t>(0, std::min<int64_t>(x0, x.W - 1));
+          x1 = std::max<int64_t>(0, std::min<int64_t>(x1, x.W - 1));
+          float dx = fx - floorf(fx);
+          dx = std::max(0.0f, std::min(dx, 1.0f));
+          const float a = in[y0 * x.W + x0], b = in[y0 * x.W + x1], cc2 = in[y1 * x.W + x0], d = in[y1 * x.W + x1];
+          out[static_cast<size_t>(i1) * ow + i0] =
+              a * (1 - dx) * (1 - dy) + b * dx * (1 - dy) + cc2 * (1 - dx) * dy + d * dx * dy;
+        }
+      }
+    }
+    return y;
+  }
+
+  static void relu_inplace(Map& m) {
+    for (auto& v : m.v) v = std::max(v, 0.0f);
+  }
+  static void add_inplace(Map& a, const Map& b) {
+    for (size_t i = 0; i < a.v.size(); ++i) a.v[i] += b.v[i];
+  }
+
+  // residual_conv_unit (src/dpt_blocks.cpp:92-114).
+  Map rcu(const Map& x, const std::string& p) {
+    Map o = x;
+    relu_inplace(o);
+    o = conv2d(o, p + "c1.weight", p + "c1.bias", 1, 1);
+    relu_inplace(o);
+    o = conv2d(o, p + "c2.weight", p + "c2.bias", 1, 1);
+    add_inplace(o, x);
+    return o;
+  }
+  // feature_fusion (src/dpt_blocks.cpp:116-143).
+  Map fusion(const Map& top, const Map* lateral, const std::string& p, int ow, int oh) {
+    Map y = top;
+    if (lateral && has(p + "rc1.c1.weight")) {
+      Map r = rcu(*lateral, p + "rc1.");
+      add_inplace(y, r);
+    }
+    y = rcu(y, p + "rc2.");
+    const int w2 = ow > 0 ? ow : y.W * 2, h2 = oh > 0 ? oh : y.H * 2;
+    y = interp_ac(y, w2, h2);
+    return conv2d(y, p + "out.weight", p + "out.bias", 1, 0);
+  }
+
+  // uv_pos_embed (src/uv_posembed.cpp:15-73) * ratio, as [C][H][W].
+  static Map uv_embed(int pw, int ph, int C, float aspect, float ratio) {
+    Map m(C, ph, pw);
+    const double diag = std::sqrt(static_cast<double>(aspect) * aspect + 1.0);
+    const double span_x = aspect / diag, span_y = 1.0 / diag;
+    const double left_x = -span_x * (pw - 1) / pw, right_x = span_x * (pw - 1) / pw;
+    const double top_y = -span_y * (ph - 1) / ph, bottom_y = span_y * (ph - 1) / ph;
+    std::vector<double> xc(pw), yc(ph);
+    for (int i = 0; i < pw; ++i) xc[i] = pw == 1 ? left_x : left_x + i * ((right_x - left_x) / (pw - 1));
+    for (int i = 0; i < ph; ++i) yc[i] = ph == 1 ? top_y : top_y + i * ((bottom_y - top_y) / (ph - 1));
+    const int D = C / 2, Fq = D / 2;
+    std::vector<double> om(Fq);
+    for (int j = 0; j < Fq; ++j) om[j] = 1.0 / std::pow(100.0, static_cast<double>(j) / (static_cast<double>(D) / 2.0));
+    for (int y = 0; y < ph; ++y)
+      for (int x = 0; x < pw; ++x)
+        for (int j = 0; j < Fq; ++j) {
+          const double ox = xc[x] * om[j], oy = yc[y] * om[j];
+          const size_t pix = static_cast<size_t>(y) * pw + x, hw = static_cast<size_t>(pw) * ph;
+          m.v[(j)*hw + pix] = ratio * static_cast<float>(std::sin(ox));
+          m.v[(Fq + j) * hw + pix] = ratio * static_cast<float>(std::cos(ox));
+          m.v[(D + j) * hw + pix] = ratio * static_cast<float>(std::sin(oy));
+          m.v[(D + Fq + j) * hw + pix] = ratio * static_cast<float>(std::cos(oy));
+        }
+    return m;
+  }
+
+  // DptHead::build_depth_graph (src/dpt_head.cpp:75-275) for one image. feats[s]:
+  // [Npatch][C] token-major. Returns main logits [od][H][W]; aux logits [7][Ha][Wa]
+  // when the aux tensors exist and want_aux.
+  Map head(const std::vector<const float*>& feats, int Cf, int H, int W, bool want_aux, Map* aux_out, const std::string& cap) {
+    const int P = c.patch_size, pw = W / P, ph = H / P, N = pw * ph;
+    const float aspect = static_cast<float>(W) / H;
+    const bool hn = has("head.norm.weight");
+    Map l[4];
+    for (int s = 0; s < 4; ++s) {
+      std::vector<float> f(feats[s], feats[s] + static_cast<size_t>(N) * Cf);
+      if (hn) layernorm_rows(f.data(), N, Cf, F("head.norm.weight"), F("head.norm.bias"), 1e-5f, f.data());
+      Map x(Cf, ph, pw);
+      for (int tk = 0; tk < N; ++tk)
+        for (int ch = 0; ch < Cf; ++ch) x.v[static_cast<size_t>(ch) * N + tk] = f[static_cast<size_t>(tk) * Cf + ch];
+      const std::string ss = std::to_string(s);
+      x = conv2d(x, "head.proj." + ss + ".weight", "head.proj." + ss + ".bias", 1, 0);
+      if (c.head_pos_embed) add_inplace(x, uv_embed(pw, ph, x.C, aspect, 0.1f));
+      if (s == 0) x = convT(x, "head.resize.0.weight", "head.resize.0.bias", 4);
+      else if (s == 1) x = convT(x, "head.resize.1.weight", "head.resize.1.bias", 2);
+      else if (s == 3) x = conv2d(x, "head.resize.3.weight", "head.resize.3.bias", 2, 1);
+      l[s] = std::move(x);
+      caps[cap + "stage" + ss] = l[s].v;
+    }
+    Map rn[4];
+    for (int s = 0; s < 4; ++s) rn[s] = conv2d(l[s], "head.scratch.layer" + std::to_string(s + 1) + "_rn.weight", "", 1, 1);
+    auto pyramid = [&](const std::string& sfx) {
+      Map o = fusion(rn[3], nullptr, "head.scratch.rn4" + sfx + ".", pw, ph);
+      o = fusion(o, &rn[2], "head.scratch.rn3" + sfx + ".", 2 * pw, 2 * ph);
+      o = fusion(o, &rn[1], "head.scratch.rn2" + sfx + ".", 4 * pw, 4 * ph);
+      o = fusion(o, &rn[0], "head.scratch.rn1" + sfx + ".", 0, 0);
+      return o;
+    };
+    Map out = pyramid("");
+    out = conv2d(out, "head.scratch.out1.weight", "head.scratch.out1.bias", 1, 1);
+    caps[cap + "out1"] = out.v;
+    out = interp_ac(out, W, H);
+    if (c.head_pos_embed) add_inplace(out, uv_embed(W, H, out.C, aspect, 0.1f));
+    out = conv2d(out, "head.scratch.out2a.weight", "head.scratch.out2a.bias", 1, 1);
+    relu_inplace(out);
+    out = conv2d(out, "head.scratch.out2b.weight", "head.scratch.out2b.bias", 1, 0);
+    if (want_aux && aux_out && has("head.scratch.rn1_aux.out.weight")) {
+      Map a = pyramid("_aux");
+      for (int i = 0; i < 5; ++i) {
+        const std::string p = "head.scratch.out1_aux." + std::to_string(i) + ".";
+        a = conv2d(a, p + "weight", p + "bias", 1, 1);
+      }
+      if (c.head_pos_embed) add_inplace(a, uv_embed(a.W, a.H, a.C, aspect, 0.1f));
+      a = conv2d(a, "head.scratch.out2a_aux.weight", "head.scratch.out2a_aux.bias", 1, 1);
+      // channels-last LayerNorm over C (eps 1e-5) (src/dpt_head.cpp:56-66, :268-269)
+      {
+        const float* g = F("head.scratch.out2_aux_ln.weight");
+        const float* b = F("head.scratch.out2_aux_ln.bias");
+        const int HW = a.H * a.W;
+        std::vector<float> px(a.C);
+        for (int p = 0; p < HW; ++p) {
+          for (int ch = 0; ch < a.C; ++ch) px[ch] = a.v[static_cast<size_t>(ch) * HW + p];
+          layernorm_rows(px.data(), 1, a.C, g, b, 1e-5f, px.data());
+          for (int ch = 0; ch < a.C; ++ch) a.v[static_cast<size_t>(ch) * HW + p] = px[ch];
+        }
+      }
+      relu_inplace(a);
+      a = conv2d(a, "head.scratch.out2b_aux.weight", "head.scratch.out2b_aux.bias", 1, 0);
+      *aux_out = std::move(a);
+    }
+    return out;
+  }
+
+  // ---------------------------------------------------------------- backbone
+  // Positions (src/dino_backbone.cpp:92-95): token 0 at (0,0); patch t: local (row+1, col+1),
+  // nodiff (1,1).
+  void positions(int gh, int gw, std::vector<float>& local, std::vector<float>& nodiff) const {
+    const int Nt = 1 + gh * gw;
+    local.assign(2 * Nt, 0.f);
+    nodiff.assign(2 * Nt, 0.f);
+    for (int tk = 1; tk < Nt; ++tk) {
+      const int idx = tk - 1, row = idx / gw, col = idx % gw;
+      local[2 * tk] = static_cast<float>(row + 1);
+      local[2 * tk + 1] = static_cast<float>(col + 1);
+      nodiff[2 * tk] = nodiff[2 * tk + 1] = 1.f;
+    }
+  }
+
+  // Multi-view backbone (S >= 1 views already in processing order), returning per
+  // out-layer features [S][Npatch][C] (src/dino_backbone.cpp:80-213, 462-616).
+  // upto >= 0 stops after block upto-1 and returns x (pass A helper).
+  void backbone(const std::vector<std::vector<float>>& views, int H, int W, std::vector<std::vector<float>>& feats,
+                int upto, std::vector<float>* x_out) {
+    const int P = c.patch_size, gh = H / P, gw = W / P, Np = gh * gw, Nt = 1 + Np, E = c.embed_dim;
+    const int S = static_cast<int>(views.size());
+    std::vector<float> pos = interp_pos_embed(gh, gw);
+    std::vector<float> x(static_cast<size_t>(S) * Nt * E);
+    for (int s = 0; s < S; ++s) embed(views[s].data(), H, W, pos, &x[static_cast<size_t>(s) * Nt * E]);
+    std::vector<float> pl, pn;
+    positions(gh, gw, pl, pn);
+    Rope r_local = rope_tables(pl, Nt);
+    std::vector<float> png(2 * static_cast<size_t>(Nt) * S);
+    for (int s = 0; s < S; ++s)
+      for (int tk = 0; tk < Nt; ++tk) {
+        png[2 * (static_cast<size_t>(s) * Nt + tk)] = pn[2 * tk];
+        png[2 * (static_cast<size_t>(s) * Nt + tk) + 1] = pn[2 * tk + 1];
+      }
+    Rope r_global = rope_tables(png, Nt * S);
+    const float* cam = F("vit.camera_token");
+    std::vector<float> local_x = x;
+    const int NL = c.n_out_layers;
+    feats.assign(NL, std::vector<float>());
+    const int depth = upto >= 0 ? upto : c.depth;
+    for (int i = 0; i < depth; ++i) {
+      if (c.alt_start >= 0 && i == c.alt_start) {
+        for (int s = 0; s < S; ++s)  // token 0 <- camera_token[ref slot 0 | src slot 1]
+          for (int e = 0; e < E; ++e) x[static_cast<size_t>(s) * Nt * E + e] = cam ? cam[(s == 0 ? 0 : E) + e] : 0.f;
+      }
+      const bool global = c.alt_start >= 0 && i >= c.alt_start && (i % 2 == 1);
+      const bool use_rope = c.rope_start >= 0 && i >= c.rope_start;
+      if (global) vit_block(x.data(), 1, S * Nt, i, use_rope ? &r_global : nullptr);
+      else vit_block(x.data(), S, Nt, i, use_rope ? &r_local : nullptr);
+      if (!global) local_x = x;
+      for (int o = 0; o < NL; ++o)
+        if (c.out_layers[o] == i) {
+          const int Cf = c.cat_token ? 2 * E : E;
+          std::vector<float> f(static_cast<size_t>(S) * Np * Cf);
+          const float* nw = F("vit.norm.weight");
+          const float* nb = F("vit.norm.bias");
+#pragma omp parallel for schedule(static)
+          for (int row = 0; row < S * Np; ++row) {
+            const int s = row / Np, tk = 1 + row % Np;
+            const float* xr = &x[(static_cast<size_t>(s) * Nt + tk) * E];
+            float* dst = &f[static_cast<size_t>(row) * Cf];
+            if (c.cat_token) {
+              const float* lr = &local_x[(static_cast<size_t>(s) * Nt + tk) * E];
+              for (int e = 0; e < E; ++e) dst[e] = lr[e];
+              layernorm_rows(xr, 1, E, nw, nb, c.ln_eps, dst + E);  // in-graph ggml_norm (:301)
+            } else {
+              layernorm_host(xr, E, nw, nb, c.ln_eps, dst);  // host double LN (:174-181)
+            }
+          }
+          feats[o] = std::move(f);
+        }
+    }
+    if (x_out) *x_out = x;
+  }
+
+  // select_reference_view_saddle (src/dino_backbone.cpp:372-412).
+  static int select_saddle(const std::vector<std::vector<float>>& cls, int E) {
+    const int S = static_cast<int>(cls.size());
+    if (S <= 1) return 0;
+    std::vector<double> nrm(S), sim(S), fn(S), fv(S);
+    std::vector<std::vector<double>> cn(S, std::vector<double>(E));
+    for (int v = 0; v < S; ++v) {
+      double n = 0;
+      for (int e = 0; e < E; ++e) n += static_cast<double>(cls[v][e]) * cls[v][e];
+      n = std::sqrt(n);
+      nrm[v] = n;
+      const double inv = n > 0 ? 1.0 / n : 0.0;
+      for (int e = 0; e < E; ++e) cn[v][e] = cls[v][e] * inv;
+    }
+    for (int v = 0; v < S; ++v) {
+      double s = 0;
+      for (int w = 0; w < S; ++w) {
+        if (w == v) continue;
+        double dot = 0;
+        for (int e = 0; e < E; ++e) dot += cn[v][e] * cn[w][e];
+        s += dot;
+      }
+      sim[v] = s / (S - 1);
+      fn[v] = nrm[v];
+      double mean = 0;
+      for (int e = 0; e < E; ++e) mean += cn[v][e];
+      mean /= E;
+      double var = 0;
+      for (int e = 0; e < E; ++e) var += (cn[v][e] - mean) * (cn[v][e] - mean);
+      fv[v] = var / (E - 1);
+    }
+    auto norm01 = [](std::vector<double>& m) {
+      double mn = m[0], mx = m[0];
+      for (double v : m) { mn = std::min(mn, v); mx = std::max(mx, v); }
+      for (double& v : m) v = (v - mn) / (mx - mn + 1e-8);
+    };
+    norm01(sim);
+    norm01(fn);
+    norm01(fv);
+    int best = 0;
+    double bb = 1e300;
+    for (int v = 0; v < S; ++v) {
+      const double bal = std::fabs(sim[v] - 0.5) + std::fabs(fn[v] - 0.5) + std::fabs(fv[v] - 0.5);
+      if (bal < bb) { bb = bal; best = v; }
+    }
+    return best;
+  }
+};
+
+// ------------------------------------------------------------------ preprocessing
+// (src/preprocess.cpp:8-197)
+struct Img {
+  int w = 0, h = 0;
+  std::vector<uint8_t> rgb;
+};
+uint8_t sat_u8(float v) {
+  long r = lrintf(v);
+  return static_cast<uint8_t>(r < 0 ? 0 : (r > 255 ? 255 : r));
+}
+float cubic_w(float x) {
+  const float a = -0.75f;
+  x = std::fabs(x);
+  if (x < 1) return ((a + 2) * x - (a + 3)) * x * x + 1;
+  if (x < 2) return (((x - 5) * x + 8) * x - 4) * a;
+  return 0.f;
+}
+void resize_bilinear(const Img& s, int dw, int dh, std::vector<float>& dst) {
+  dst.assign(static_cast<size_t>(dw) * dh * 3, 0.f);
+  const float sx = static_cast<float>(s.w) / dw, sy = static_cast<float>(s.h) / dh;
+  for (int y = 0; y < dh; ++y) {
+    const float fy = (y + 0.5f) * sy - 0.5f;
+    const int y0 = static_cast<int>(std::floor(fy));
+    const float wy = fy - y0;
+    const int y0c = std::clamp(y0, 0, s.h - 1), y1c = std::clamp(y0 + 1, 0, s.h - 1);
+    for (int x = 0; x < dw; ++x) {
+      const float fx = (x + 0.5f) * sx - 0.5f;
+      const int x0 = static_cast<int>(std::floor(fx));
+      const float wx = fx - x0;
+      const int x0c = std::clamp(x0, 0, s.w - 1), x1c = std::clamp(x0 + 1, 0, s.w - 1);
+      for (int ch = 0; ch < 3; ++ch) {
+        auto P = [&](int yy, int xx) { return static_cast<float>(s.rgb[(static_cast<size_t>(yy) * s.w + xx) * 3 + ch]); };
+        const float top = P(y0c, x0c) * (1 - wx) + P(y0c, x1c) * wx;
+        const float bot = P(y1c, x0c) * (1 - wx) + P(y1c, x1c) * wx;
+        dst[(static_cast<size_t>(y) * dw + x) * 3 + ch] = top * (1 - wy) + bot * wy;
+      }
+    }
+  }
+}
+Img resize_cubic(const Img& src, int dw, int dh) {
+  Img dst;
+  dst.w = dw;
+  dst.h = dh;
+  dst.rgb.assign(static_cast<size_t>(dw) * dh * 3, 0);
+  const int sw = src.w, sh = src.h;
+  const double sx = static_cast<double>(sw) / dw, sy = static_cast<double>(sh) / dh;
+  std::vector<int> xi(static_cast<size_t>(dw) * 4);
+  std::vector<float> xw(static_cast<size_t>(dw) * 4);
+  for (int x = 0; x < dw; ++x) {
+    const double fx = (x + 0.5) * sx - 0.5;
+    const int ix = static_cast<int>(std::floor(fx));
+    const float t = static_cast<float>(fx - ix);
+    const float w[4] = {cubic_w(t + 1), cubic_w(t), cubic_w(t - 1), cubic_w(t - 2)};
+    for (int k = 0; k < 4; ++k) {
+      xi[x * 4 + k] = std::clamp(ix - 1 + k, 0, sw - 1);
+      xw[x * 4 + k] = w[k];
+    }
+  }
+  std::vector<float> tmp(static_cast<size_t>(sh) * dw * 3);
+  for (int y = 0; y < sh; ++y)
+    for (int x = 0; x < dw; ++x)
+      for (int ch = 0; ch < 3; ++ch) {
+        float acc = 0;
+        for (int k = 0; k < 4; ++k) acc += xw[x * 4 + k] * static_cast<float>(src.rgb[(static_cast<size_t>(y) * sw + xi[x * 4 + k]) * 3 + ch]);
+        tmp[(static_cast<size_t>(y) * dw + x) * 3 + ch] = acc;
+      }
+  for (int y = 0; y < dh; ++y) {
+    const double fy = (y + 0.5) * sy - 0.5;
+    const int iy = static_cast<int>(std::floor(fy));
+    const float t = static_cast<float>(fy - iy);
+    const float w[4] = {cubic_w(t + 1), cubic_w(t), cubic_w(t - 1), cubic_w(t - 2)};
+    int yi[4];
+    for (int k = 0; k < 4; ++k) yi[k] = std::clamp(iy - 1 + k, 0, sh - 1);
+    for (int x = 0; x < dw; ++x)
+      for (int ch = 0; ch < 3; ++ch) {
+        float acc = 0;
+        for (int k = 0; k < 4; ++k) acc += w[k] * tmp[(static_cast<size_t>(yi[k]) * dw + x) * 3 + ch];
+        dst.rgb[(static_cast<size_t>(y) * dw + x) * 3 + ch] = sat_u8(acc);
+      }
+  }
+  return dst;
+}
+struct AreaTap {
+  int di, si;
+  float alpha;
+};
+std::vector<AreaTap> area_tab(int ssize, int dsize) {
+  std::vector<AreaTap> tab;
+  const double scale = static_cast<double>(ssize) / dsize;
+  for (int dx = 0; dx < dsize; ++dx) {
+    const double fsx1 = dx * scale, fsx2 = fsx1 + scale;
+    const double cw = std::min(scale, static_cast<double>(ssize) - fsx1);
+    int sx1 = static_cast<int>(std::ceil(fsx1)), sx2 = static_cast<int>(std::floor(fsx2));
+    sx2 = std::min(sx2, ssize - 1);
+    sx1 = std::min(sx1, sx2);
+    if (sx1 - fsx1 > 1e-3) tab.push_back({dx, sx1 - 1, static_cast<float>((sx1 - fsx1) / cw)});
+    for (int sx = sx1; sx < sx2; ++sx) tab.push_back({dx, sx, static_cast<float>(1.0 / cw)});
+    if (fsx2 - sx2 > 1e-3) tab.push_back({dx, sx2, static_cast<float>(std::min(std::min(fsx2 - sx2, 1.0), cw) / cw)});
+  }
+  return tab;
+}
+Img resize_area(const Img& src, int dw, int dh) {
+  const int sw = src.w, sh = src.h;
+  if (dw >= sw && dh >= sh) {
+    Img up;
+    std::vector<float> hwc;
+    resize_bilinear(src, dw, dh, hwc);
+    up.w = dw;
+    up.h = dh;
+    up.rgb.resize(hwc.size());
+    for (size_t i = 0; i < hwc.size(); ++i) up.rgb[i] = sat_u8(hwc[i]);
+    return up;
+  }
+  auto xt = area_tab(sw, dw), yt = area_tab(sh, dh);
+  std::vector<float> tmp(static_cast<size_t>(sh) * dw * 3, 0.f);
+  for (int y = 0; y < sh; ++y)
+    for (const auto& t : xt)
+      for (int ch = 0; ch < 3; ++ch)
+        tmp[(static_cast<size_t>(y) * dw + t.di) * 3 + ch] += t.alpha * static_cast<float>(src.rgb[(static_cast<size_t>(y) * sw + t.si) * 3 + ch]);
+  std::vector<float> acc(static_cast<size_t>(dh) * dw * 3, 0.f);
+  for (const auto& t : yt)
+    for (int x = 0; x < dw; ++x)
+      for (int ch = 0; ch < 3; ++ch)
+        acc[(static_cast<size_t>(t.di) * dw + x) * 3 + ch] += t.alpha * tmp[(static_cast<size_t>(t.si) * dw + x) * 3 + ch];
+  Img dst;
+  dst.w = dw;
+  dst.h = dh;
+  dst.rgb.resize(acc.size());
+  for (size_t i = 0; i < acc.size(); ++i) dst.rgb[i] = sat_u8(acc[i]);
+  return dst;
+}
+int nearest_multiple(int x, int p) {
+  const int down = (x / p) * p, up = down + p;
+  return (std::abs(up - x) <= std::abs(x - down)) ? up : down;
+}
+// preprocess_real / legacy preprocess -> CHW f32 normalised.
+bool preprocess(const Img& img, const or_config& c, bool legacy, std::vector<float>& chw, int& H, int& W) {
+  if (img.w <= 0 || img.h <= 0) return false;
+  const int patch = c.patch_size;
+  if (legacy) {
+    int dw = (img.w / patch) * patch, dh = (img.h / patch) * patch;
+    if (dw == 0) dw = patch;
+    if (dh == 0) dh = patch;
+    std::vector<float> hwc;
+    resize_bilinear(img, dw, dh, hwc);
+    W = dw;
+    H = dh;
+    chw.assign(static_cast<size_t>(3) * dh * dw, 0.f);
+    for (int ch = 0; ch < 3; ++ch)
+      for (int y = 0; y < dh; ++y)
+        for (int x = 0; x < dw; ++x) {
+          const float v = hwc[(static_cast<size_t>(y) * dw + x) * 3 + ch] / 255.f;
+          chw[(static_cast<size_t>(ch) * dh + y) * dw + x] = (v - c.img_mean[ch]) / c.img_std[ch];
+        }
+    return true;
+  }
+  const int target = c.resize_target > 0 ? c.resize_target : 504;
+  Img cur = img;
+  {
+    const int bound = c.resize_upper ? std::max(cur.w, cur.h) : std::min(cur.w, cur.h);
+    if (bound != target) {
+      const double scale = static_cast<double>(target) / bound;
+      const int nw = std::max(1, static_cast<int>(std::nearbyint(cur.w * scale)));
+      const int nh = std::max(1, static_cast<int>(std::nearbyint(cur.h * scale)));
+      cur = scale > 1.0 ? resize_cubic(cur, nw, nh) : resize_area(cur, nw, nh);
+    }
+  }
+  {
+    const int nw = std::max(1, nearest_multiple(cur.w, patch)), nh = std::max(1, nearest_multiple(cur.h, patch));
+    if (nw != cur.w || nh != cur.h) {
+      const bool upscale = nw > cur.w || nh > cur.h;
+      cur = upscale ? resize_cubic(cur, nw, nh) : resize_area(cur, nw, nh);
+    }
+  }
+  H = cur.h;
+  W = cur.w;
+  chw.assign(static_cast<size_t>(3) * H * W, 0.f);
+  for (int ch = 0; ch < 3; ++ch)
+    for (int y = 0; y < H; ++y)
+      for (int x = 0; x < W; ++x) {
+        const float v = static_cast<float>(cur.rgb[(static_cast<size_t>(y) * W + x) * 3 + ch]) / 255.f;
+        chw[(static_cast<size_t>(ch) * H + y) * W + x] = (v - c.img_mean[ch]) / c.img_std[ch];
+      }
+  return true;
+}
+
+struct Handle {
+  Oracle o;
+  std::vector<float> depth, conf, logits, aux, chw;
+  std::vector<std::vector<float>> feats;
+  int H = 0, W = 0, od = 0, aux_h = 0, aux_w = 0, b_idx = 0;
+};
+
+}  // namespace
+
+// ====================================================================== C ABI
+OR_API void* or_create(const or_config* cfg, const or_tensor* ts, int n) {
+  auto* h = new Handle();
+  h->o.c = *cfg;
+  for (int i = 0; i < n; ++i) {
+    Tensor t;
+    t.data = ts[i].data;
+    t.type = ts[i].type;
+    for (int k = 0; k < 4; ++k) t.ne[k] = ts[i].ne[k] > 0 ? ts[i].ne[k] : 1;
+    h->o.t[ts[i].name] = t;
+  }
+#ifdef _OPENMP
+  if (cfg->n_threads > 0) omp_set_num_threads(cfg->n_threads);
+#endif
+  return h;
+}
+
+OR_API void or_destroy(void* p) { delete static_cast<Handle*>(p); }
+
+OR_API void or_quantize_q8_0(const float* x, int64_t n, uint8_t* out) {
+  for (int64_t b = 0; b < n / 32; ++b) {
+    float d;
+    int8_t q[32];
+    quantize_row(x + b * 32, 32, &d, q);
+    // re-derive the exact stored fp16 scale (quantize_row returns it widened)
+    const uint16_t dh = f2h(d);
+    memcpy(out + b * 34, &dh, 2);
+    memcpy(out + b * 34 + 2, q, 32);
+  }
+}
+
+OR_API int or_preprocess(void* p, const uint8_t* rgb, int w, int hgt, int legacy, float* out, int* H, int* W) {
+  auto* h = static_cast<Handle*>(p);
+  Img img;
+  img.w = w;
+  img.h = hgt;
+  img.rgb.assign(rgb, rgb + static_cast<size_t>(w) * hgt * 3);
+  std::vector<float> chw;
+  if (!preprocess(img, h->o.c, legacy != 0, chw, *H, *W)) return -1;
+  if (out) memcpy(out, chw.data(), chw.size() * 4);
+  return 0;
+}
+
+// Single image: RGB8 HWC -> depth (+conf) at the processed size.
+// DA2 route: preprocess_real -> forward -> depth_relative (src/engine.cpp:121-130,
+// src/dpt_head.cpp:402-439); DA3 route: preprocess_real -> fused feats -> head ->
+// exp / exp+1 (src/engine.cpp:189-229). legacy=1 uses the floor-to-patch preprocess.
+OR_API int or_infer(void* p, const uint8_t* rgb, int w, int hgt, int legacy, int want_aux) {
+  auto* h = static_cast<Handle*>(p);
+  Oracle& o = h->o;
+  Img img;
+  img.w = w;
+  img.h = hgt;
+  img.rgb.assign(rgb, rgb + static_cast<size_t>(w) * hgt * 3);
+  int H = 0, W = 0;
+  if (!preprocess(img, o.c, legacy != 0, h->chw, H, W)) return -1;
+  h->H = H;
+  h->W = W;
+  std::vector<std::vector<float>> views{h->chw};
+  o.backbone(views, H, W, h->feats, -1, nullptr);
+  if (static_cast<int>(h->feats.size()) < 4) return -2;
+  const int Cf = (o.c.cat_token ? 2 : 1) * o.c.embed_dim;
+  std::vector<const float*> f4 = {h->feats[0].data(), h->feats[1].data(), h->feats[2].data(), h->feats[3].data()};
+  Oracle::Map aux;
+  Oracle::Map lg = o.head(f4, Cf, H, W, want_aux != 0, &aux, "");
+  h->od = lg.C;
+  h->logits = lg.v;
+  const size_t HW = static_cast<size_t>(H) * W;
+  h->depth.assign(HW, 0.f);
+  h->conf.clear();
+  if (o.c.is_da2) {
+    for (size_t i = 0; i < HW; ++i)
+      h->depth[i] = o.c.head_max_depth > 0.f ? (1.0f / (1.0f + std::exp(-lg.v[i]))) * o.c.head_max_depth : std::max(0.0f, lg.v[i]);
+  } else {
+    for (size_t i = 0; i < HW; ++i) h->depth[i] = std::exp(lg.v[i]);
+    if (lg.C >= 2) {
+      h->conf.resize(HW);
+      for (size_t i = 0; i < HW; ++i) h->conf[i] = std::exp(lg.v[HW + i]) + 1.0f;
+    }
+  }
+  h->aux = aux.v;
+  h->aux_h = aux.H;
+  h->aux_w = aux.W;
+  return 0;
+}
+
+// Multi-view (S views, same size): src/engine.cpp:352-384 + forward_mv
+// (src/dino_backbone.cpp:414-460) with the per-view depth head (+ aux rays).
+// Outputs are concatenated per view in the original order.
+OR_API int or_infer_mv(void* p, const uint8_t* const* rgbs, int S, int w, int hgt, int legacy, int want_aux) {
+  auto* h = static_cast<Handle*>(p);
+  Oracle& o = h->o;
+  std::vector<std::vector<float>> views(S);
+  int H = 0, W = 0;
+  for (int s = 0; s < S; ++s) {
+    Img img;
+    img.w = w;
+    img.h = hgt;
+    img.rgb.assign(rgbs[s], rgbs[s] + static_cast<size_t>(w) * hgt * 3);
+    int h2 = 0, w2 = 0;
+    if (!preprocess(img, o.c, legacy != 0, views[s], h2, w2)) return -1;
+    if (s == 0) { H = h2; W = w2; }
+    else if (h2 != H || w2 != W) return -2;
+  }
+  h->H = H;
+  h->W = W;
+  const int E = o.c.embed_dim, P = o.c.patch_size, Nt = 1 + (H / P) * (W / P);
+  int b_idx = 0;
+  std::vector<int> order(S);
+  for (int s = 0; s < S; ++s) order[s] = s;
+  if (S >= 3 && o.c.alt_start >= 0) {
+    std::vector<float> xa;
+    std::vector<std::vector<float>> dummy;
+    o.backbone(views, H, W, dummy, o.c.alt_start - 1, &xa);
+    std::vector<std::vector<float>> cls(S, std::vector<float>(E));
+    for (int s = 0; s < S; ++s)
+      for (int e = 0; e < E; ++e) cls[s][e] = xa[static_cast<size_t>(s) * Nt * E + e];
+    b_idx = Oracle::select_saddle(cls, E);
+    order[0] = b_idx;
+    for (int q = 1; q < S; ++q) order[q] = q <= b_idx ? q - 1 : q;
+  }
+  h->b_idx = b_idx;
+  std::vector<std::vector<float>> rv(S);
+  for (int q = 0; q < S; ++q) rv[q] = views[order[q]];
+  std::vector<std::vector<float>> feats;
+  o.backbone(rv, H, W, feats, -1, nullptr);
+  const int Cf = (o.c.cat_token ? 2 : 1) * E;
+  const int Np = Nt - 1;
+  const size_t HW = static_cast<size_t>(H) * W;
+  h->depth.assign(HW * S, 0.f);
+  h->conf.assign(HW * S, 0.f);
+  h->logits.clear();
+  h->aux.clear();
+  h->feats.assign(4, std::vector<float>(static_cast<size_t>(S) * Np * Cf));
+  for (int t = 0; t < S; ++t) {
+    // original view t sits at processing position q with order[q] == t
+    int q = 0;
+    while (order[q] != t) ++q;
+    std::vector<const float*> f4;
+    for (int l = 0; l < 4; ++l) {
+      f4.push_back(&feats[l][static_cast<size_t>(q) * Np * Cf]);
+      memcpy(&h->feats[l][static_cast<size_t>(t) * Np * Cf], f4.back(), static_cast<size_t>(Np) * Cf * 4);
+    }
+    Oracle::Map aux;
+    Oracle::Map lg = o.head(f4, Cf, H, W, want_aux != 0, &aux, "v" + std::to_string(t) + ".");
+    h->od = lg.C;
+    for (size_t i = 0; i < HW; ++i) {
+      h->depth[t * HW + i] = std::exp(lg.v[i]);
+      if (lg.C >= 2) h->conf[t * HW + i] = std::exp(lg.v[HW + i]) + 1.0f;
+    }
+    h->logits.insert(h->logits.end(), lg.v.begin(), lg.v.end());
+    h->aux.insert(h->aux.end(), aux.v.begin(), aux.v.end());
+    h->aux_h = aux.H;
+    h->aux_w = aux.W;
+  }
+  return 0;
+}
+
+// Accessors: name in {"depth","conf","logits","aux","chw","feat0".."feat3"} or a
+// capture key ("stage0".."stage3","out1", "v<k>.stage0"...). Returns element count.
+OR_API int64_t or_get(void* p, const char* name, const float** out) {
+  auto* h = static_cast<Handle*>(p);
+  std::string n(name);
+  const std::vector<float>* v = nullptr;
+  if (n == "depth") v = &h->depth;
+  else if (n == "conf") v = &h->conf;
+  else if (n == "logits") v = &h->logits;
+  else if (n == "aux") v = &h->aux;
+  else if (n == "chw") v = &h->chw;
+  else if (n.size() == 5 && n.compare(0, 4, "feat") == 0) {
+    const int l = n[4] - '0';
+    if (l >= 0 && l < static_cast<int>(h->feats.size())) v = &h->feats[l];
+  } else {
+    auto it = h->o.caps.find(n);
+    if (it != h->o.caps.end()) v = &it->second;
+  }
+  if (!v) { *out = nullptr; return -1; }
+  *out = v->data();
+  return static_cast<int64_t>(v->size());
+}
+
+OR_API void or_dims(void* p, int* H, int* W, int* od, int* aux_h, int* aux_w, int* b_idx) {
+  auto* h = static_cast<Handle*>(p);
+  *H = h->H;
+  *W = h->W;
+  *od = h->od;
+  *aux_h = h->aux_h;
+  *aux_w = h->aux_w;
+  *b_idx = h->b_idx;
+}

@@ -1,0 +1,234 @@
+"""Python driver of the CPU oracle (oracle.cpp) — test infrastructure only.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this
+module, and only as the checker / the timed CPU restatement of the reference. The
+GGUF is parsed here with gguf-py (independently of libda3b's own C++ reader) and
+the tensors are handed to the oracle as raw host pointers.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+SRC = os.path.join(HERE, "oracle.cpp")
+LIB = os.path.join(HERE, "liboracle.so")
+# x86-64-v3 (AVX2/FMA): portable to the GPU hosts; -ffp-contract=off keeps f32
+# arithmetic in the written order (no fused multiply-add reassociation).
+CXXFLAGS = ["-O3", "-march=x86-64-v3", "-ffp-contract=off", "-fopenmp", "-fPIC", "-shared", "-std=c++17",
+            "-fvisibility=hidden"]
+
+
+def build(force: bool = False) -> str:
+    if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < os.path.getmtime(SRC):
+        cmd = ["g++"] + CXXFLAGS + [SRC, "-o", LIB + ".tmp"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"oracle build failed:\n{r.stderr}")
+        os.replace(LIB + ".tmp", LIB)
+    return LIB
+
+
+class OrTensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("data", ctypes.c_void_p), ("type", ctypes.c_int),
+                ("ne", ctypes.c_int64 * 4)]
+
+
+class OrConfig(ctypes.Structure):
+    _fields_ = [
+        ("patch_size", ctypes.c_int), ("embed_dim", ctypes.c_int), ("depth", ctypes.c_int),
+        ("num_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("mlp_hidden", ctypes.c_int),
+        ("pos_embed_grid", ctypes.c_int), ("alt_start", ctypes.c_int), ("rope_start", ctypes.c_int),
+        ("qknorm_start", ctypes.c_int), ("rope_freq", ctypes.c_float), ("ln_eps", ctypes.c_float),
+        ("interp_offset", ctypes.c_float), ("cat_token", ctypes.c_int), ("head_pos_embed", ctypes.c_int),
+        ("is_da2", ctypes.c_int), ("head_features", ctypes.c_int), ("n_out_layers", ctypes.c_int),
+        ("out_layers", ctypes.c_int * 4), ("head_out_channels", ctypes.c_int * 4),
+        ("img_mean", ctypes.c_float * 3), ("img_std", ctypes.c_float * 3), ("resize_target", ctypes.c_int),
+        ("resize_upper", ctypes.c_int), ("head_max_depth", ctypes.c_float), ("act_quant", ctypes.c_int),
+        ("n_threads", ctypes.c_int),
+    ]
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        L = ctypes.CDLL(build())
+        L.or_create.restype = ctypes.c_void_p
+        L.or_create.argtypes = [ctypes.POINTER(OrConfig), ctypes.POINTER(OrTensor), ctypes.c_int]
+        L.or_destroy.argtypes = [ctypes.c_void_p]
+        L.or_quantize_q8_0.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+        L.or_preprocess.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                    ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]
+        L.or_infer.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.or_infer_mv.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.or_get.restype = ctypes.c_int64
+        L.or_get.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.POINTER(ctypes.c_float))]
+        L.or_dims.argtypes = [ctypes.c_void_p] + [ctypes.POINTER(ctypes.c_int)] * 6
+        _lib = L
+    return _lib
+
+
+def read_gguf(path):
+    """(kv dict, list of (name, ndarray raw, ggml type, ne[4])) via gguf-py."""
+    from gguf import GGUFReader
+
+    r = GGUFReader(path)
+    kv = {}
+    for name, f in r.fields.items():
+        if not f.data:
+            continue
+        tname = f.types[0].name if f.types else ""
+        if tname == "STRING":
+            kv[name] = bytes(f.parts[f.data[0]]).decode()
+        elif tname == "ARRAY":
+            vals = [f.parts[i] for i in f.data]
+            if f.types[-1].name == "STRING":
+                kv[name] = [bytes(v).decode() for v in vals]
+            else:
+                kv[name] = [v.tolist()[0] for v in vals]
+        else:
+            kv[name] = f.parts[f.data[0]].tolist()[0]
+    tensors = []
+    for t in r.tensors:
+        ne = [int(v) for v in t.shape] + [1] * (4 - len(t.shape))
+        tensors.append((t.name, np.ascontiguousarray(t.data), int(t.tensor_type), ne))
+    return kv, tensors
+
+
+def config_from_kv(kv, act_quant=True, n_threads=0):
+    P = "depthanything3."
+    c = OrConfig()
+    g = lambda k, d: kv.get(P + k, d)
+    c.patch_size = g("patch_size", 14)
+    c.embed_dim = g("vit.embed_dim", 0)
+    c.depth = g("vit.depth", 0)
+    c.num_heads = g("vit.num_heads", 0)
+    c.head_dim = g("vit.head_dim", 0)
+    c.mlp_hidden = g("vit.mlp_hidden", 0)
+    c.pos_embed_grid = g("vit.pos_embed_grid", 0)
+    c.alt_start = g("vit.alt_start", -1)
+    c.rope_start = g("vit.rope_start", -1)
+    c.qknorm_start = g("vit.qknorm_start", -1)
+    c.rope_freq = g("vit.rope_freq", 100.0)
+    c.ln_eps = g("vit.ln_eps", 1e-6)
+    c.interp_offset = g("vit.interpolate_offset", 0.1)
+    c.cat_token = int(bool(g("vit.cat_token", True)))
+    c.head_pos_embed = int(bool(g("head.pos_embed", True)))
+    c.is_da2 = int(g("arch", "depthanything3") == "depthanything2")
+    c.head_features = g("head.features", 0)
+    ol = g("vit.out_layers", [])
+    c.n_out_layers = len(ol)
+    for i, v in enumerate(ol[:4]):
+        c.out_layers[i] = v
+    for i, v in enumerate(g("head.out_channels", [])[:4]):
+        c.head_out_channels[i] = v
+    for i, v in enumerate(g("img.mean", [0.485, 0.456, 0.406])[:3]):
+        c.img_mean[i] = v
+    for i, v in enumerate(g("img.std", [0.229, 0.224, 0.225])[:3]):
+        c.img_std[i] = v
+    c.resize_target = g("img.resize_target", 504)
+    c.resize_upper = int(not str(g("img.resize_mode", "upper_bound")).startswith("lower"))
+    c.head_max_depth = g("head.max_depth", 0.0)
+    c.act_quant = int(act_quant)
+    c.n_threads = int(n_threads)
+    return c
+
+
+class Oracle:
+    """CPU restatement of the reference depth path over a GGUF file."""
+
+    def __init__(self, gguf_path, act_quant=True, n_threads=0):
+        L = lib()
+        self.kv, self._tensors = read_gguf(gguf_path)
+        self.cfg = config_from_kv(self.kv, act_quant, n_threads)
+        arr = (OrTensor * len(self._tensors))()
+        self._names = []
+        for i, (name, data, typ, ne) in enumerate(self._tensors):
+            nb = name.encode()
+            self._names.append(nb)
+            arr[i].name = nb
+            arr[i].data = data.ctypes.data
+            arr[i].type = typ
+            for k in range(4):
+                arr[i].ne[k] = ne[k]
+        self._arr = arr
+        self.h = L.or_create(ctypes.byref(self.cfg), arr, len(self._tensors))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().or_destroy(self.h)
+            self.h = None
+
+    def tensor(self, name):
+        for n, d, t, ne in self._tensors:
+            if n == name:
+                return d, t, ne
+        return None
+
+    def get(self, name):
+        p = ctypes.POINTER(ctypes.c_float)()
+        n = lib().or_get(self.h, name.encode(), ctypes.byref(p))
+        if n < 0:
+            return None
+        if n == 0:
+            return np.zeros(0, dtype=np.float32)
+        return np.ctypeslib.as_array(p, shape=(n,)).copy()
+
+    def dims(self):
+        v = [ctypes.c_int() for _ in range(6)]
+        lib().or_dims(self.h, *[ctypes.byref(x) for x in v])
+        return tuple(x.value for x in v)
+
+    def preprocess(self, rgb, legacy=False):
+        rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+        h, w = rgb.shape[:2]
+        H, W = ctypes.c_int(), ctypes.c_int()
+        buf = np.zeros(3 * (h + 64) * (w + 64) * 4, dtype=np.float32)
+        rc = lib().or_preprocess(self.h, rgb.ctypes.data, w, h, int(legacy), buf.ctypes.data, ctypes.byref(H),
+                                 ctypes.byref(W))
+        assert rc == 0
+        return buf[: 3 * H.value * W.value].reshape(3, H.value, W.value).copy()
+
+    def infer(self, rgb, legacy=False, aux=False):
+        rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+        h, w = rgb.shape[:2]
+        rc = lib().or_infer(self.h, rgb.ctypes.data, w, h, int(legacy), int(aux))
+        if rc != 0:
+            raise RuntimeError(f"oracle infer failed {rc}")
+        H, W, od, ah, aw, _ = self.dims()
+        out = {"H": H, "W": W, "depth": self.get("depth").reshape(H, W), "logits": self.get("logits").reshape(od, H, W)}
+        conf = self.get("conf")
+        if conf is not None and conf.size:
+            out["conf"] = conf.reshape(H, W)
+        if aux and ah > 0:
+            out["aux"] = self.get("aux").reshape(7, ah, aw)
+        return out
+
+    def infer_mv(self, rgbs, legacy=True, aux=False):
+        rgbs = [np.ascontiguousarray(r, dtype=np.uint8) for r in rgbs]
+        S = len(rgbs)
+        h, w = rgbs[0].shape[:2]
+        ptrs = (ctypes.c_void_p * S)(*[r.ctypes.data for r in rgbs])
+        rc = lib().or_infer_mv(self.h, ptrs, S, w, h, int(legacy), int(aux))
+        if rc != 0:
+            raise RuntimeError(f"oracle infer_mv failed {rc}")
+        H, W, od, ah, aw, b_idx = self.dims()
+        out = {"H": H, "W": W, "b_idx": b_idx, "depth": self.get("depth").reshape(S, H, W),
+               "conf": self.get("conf").reshape(S, H, W), "logits": self.get("logits").reshape(S, od, H, W)}
+        if aux and ah > 0:
+            out["aux"] = self.get("aux").reshape(S, 7, ah, aw)
+        return out
+
+
+def quantize_q8_0(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    out = np.zeros(x.size // 32 * 34, dtype=np.uint8)
+    lib().or_quantize_q8_0(x.ctypes.data, x.size, out.ctypes.data)
+    return out
