@@ -4,6 +4,7 @@
 #include <stdint.h>
 
 #include "da3b.h"
+#include "kernels.h"
 #include "ops.h"
 
 namespace da3b {
@@ -82,6 +83,12 @@ DA3B_API int da3b_linear_resid_f32(const void* x, int M, int K, int lda, const v
   e.ld_resid = ldr;
   return gemm_linear(static_cast<const __half*>(x), M, K, lda, static_cast<const __half*>(w), N, ldw, 0, e, st,
                      static_cast<cudaStream_t>(stream));
+}
+
+DA3B_API int da3b_attention(const void* qkv, int nseq, int seqlen, int heads, void* out, void* stream) {
+  if (!qkv || !out || heads <= 0) return -100;
+  return flash_attn(static_cast<const __half*>(qkv), nseq, seqlen, heads, heads * 64, static_cast<__half*>(out),
+                    static_cast<cudaStream_t>(stream), 0);
 }
 
 DA3B_API int da3b_pack_conv_weight(const float* w_f32, int OC, int IC, int ksize, void* w_packed, void* stream) {

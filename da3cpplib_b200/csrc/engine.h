@@ -53,9 +53,10 @@ class Engine {
   // true: the fused out2b epilogue writes raw logits (no output activation); used
   // by parity tests. Changing it drops the cached plans.
   void set_raw_logits(bool on);
-  // true (default): activations entering a Q8_0 linear are rounded through Q8_0
-  // exactly as ggml quantises them before its Q8_0 matmuls, so results follow the
-  // reference's numerics; false: plain f16 activations. Drops the cached plans.
+  // true: activations entering a Q8_0 linear are rounded through Q8_0 as ggml
+  // quantises them before its Q8_0 matmuls; false (default): plain f16 activations,
+  // which sit closer to the reference's outputs (two independent Q8_0 roundings
+  // disagree by more than one rounding does). Drops the cached plans.
   void set_act_quant(bool on);
 
   // Debug captures for parity tests: feats of out-layer o ([n_views*Np][C] f16) of
@@ -76,7 +77,7 @@ class Engine {
   int* status_ = nullptr;
   bool use_graph_ = true;
   bool raw_logits_ = false;
-  bool act_quant_ = true;
+  bool act_quant_ = false;
   std::string err_;
   std::map<std::tuple<int, int, int, int, bool>, std::unique_ptr<Plan>> plans_;
   Plan* last_ = nullptr;

@@ -1,13 +1,14 @@
 // Persistent warp-specialised tcgen05 GEMM / implicit-GEMM convolution for sm_100a.
 //
-// Roles (192 threads, one CTA per SM, grid = min(#tiles, #SMs)):
+// Roles (320 threads, one CTA per SM, grid = min(#tiles, #SMs)):
 //   warp 0       TMA producer: streams A/B k-blocks into a kStages-deep ring of
 //                128B-swizzled shared-memory stages (mbarrier full/empty pairs);
 //   warp 1       MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, K=16) into
 //                one of two TMEM accumulators, commits stage releases and
 //                "accumulator full" events;
-//   warps 2..5   epilogue: tcgen05.ld the accumulator (each warp owns its 32-lane
-//                TMEM quarter), apply the fused epilogue, store to global, and
+//   warps 2..9   epilogue: tcgen05.ld the accumulator (warp w may read TMEM lanes
+//                32*(w%4)..+31; two warps share each lane quarter and split the
+//                tile's columns), apply the fused epilogue, store to global, and
 //                release the accumulator so the MMA of the next tile overlaps.
 // Tiles are visited m-major (all N tiles of one 128-row A panel back to back) so an
 // A panel is read from HBM about once while the weights stay resident in L2.
@@ -85,6 +86,17 @@ __device__ __forceinline__ void q8_roundtrip32(float (&t)[32]) {
   for (int i = 0; i < 32; ++i) t[i] = dh * roundf(t[i] * id);
 }
 
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+
+// 8 consecutive f32 (32-byte aligned) from global memory.
+__device__ __forceinline__ void load_f8(const float* p, float* v) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
 __device__ __forceinline__ int remap_row(const EpiArgs& e, int row) {
   return e.rm_div > 0 ? (row / e.rm_div) * e.rm_mul + e.rm_add + row % e.rm_div : row;
 }
@@ -99,8 +111,15 @@ __device__ __forceinline__ void epilogue32(const GemmGeom& g, const EpiArgs& e, 
       const int orow = remap_row(e, row);
       if (e.q8) {  // full 32-column block (host enforces N % 32 == 0, no addends)
         float t[32];
+        if (e.bias) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) t[i] = apply_act(v[i] + (e.bias ? __ldg(e.bias + n_base + i) : 0.0f), e.act);
+          for (int j0 = 0; j0 < 32; j0 += 8) load_f8(e.bias + n_base + j0, t + j0);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) t[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) t[i] = apply_act(v[i] + t[i], e.act);
         q8_roundtrip32(t);
 #pragma unroll
         for (int j0 = 0; j0 < 32; j0 += 8) store_h8(e.out + static_cast<size_t>(orow) * e.ld_out + n_base + j0, t + j0);
@@ -108,8 +127,14 @@ __device__ __forceinline__ void epilogue32(const GemmGeom& g, const EpiArgs& e, 
       }
       for (int j0 = 0; j0 < nvalid; j0 += 8) {  // N % 8 == 0 is enforced by the host
         float t[8];
+        if (e.bias) {
+          load_f8(e.bias + n_base + j0, t);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) t[i] = v[j0 + i] + (e.bias ? __ldg(e.bias + n_base + j0 + i) : 0.0f);
+          for (int i = 0; i < 8; ++i) t[i] += v[j0 + i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) t[i] = v[j0 + i];
+        }
         if (e.res1) {
           const int r1 = e.res1_mod > 0 ? orow % e.res1_mod : orow;
           float s[8];
@@ -138,17 +163,26 @@ __device__ __forceinline__ void epilogue32(const GemmGeom& g, const EpiArgs& e, 
     case kEpiResid: {
       const int orow = remap_row(e, row);
       float* p = e.resid + static_cast<size_t>(orow) * e.ld_resid + n_base;
-      for (int j0 = 0; j0 < nvalid; j0 += 4) {
-        float4 x = *reinterpret_cast<float4*>(p + j0);
-        float t[4];
+      for (int j0 = 0; j0 < nvalid; j0 += 8) {
+        float bb[8], sc[8];
+        if (e.bias) load_f8(e.bias + n_base + j0, bb);
+        else {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int n = n_base + j0 + i;
-          const float a = v[j0 + i] + (e.bias ? __ldg(e.bias + n) : 0.0f);
-          t[i] = e.scale ? __ldg(e.scale + n) * a : a;
+          for (int i = 0; i < 8; ++i) bb[i] = 0.f;
         }
-        x.x += t[0]; x.y += t[1]; x.z += t[2]; x.w += t[3];
-        *reinterpret_cast<float4*>(p + j0) = x;
+        if (e.scale) load_f8(e.scale + n_base + j0, sc);
+        else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sc[i] = 1.f;
+        }
+        float4 x0 = *reinterpret_cast<float4*>(p + j0);
+        float4 x1 = *reinterpret_cast<float4*>(p + j0 + 4);
+        x0.x += sc[0] * (v[j0 + 0] + bb[0]); x0.y += sc[1] * (v[j0 + 1] + bb[1]);
+        x0.z += sc[2] * (v[j0 + 2] + bb[2]); x0.w += sc[3] * (v[j0 + 3] + bb[3]);
+        x1.x += sc[4] * (v[j0 + 4] + bb[4]); x1.y += sc[5] * (v[j0 + 5] + bb[5]);
+        x1.z += sc[6] * (v[j0 + 6] + bb[6]); x1.w += sc[7] * (v[j0 + 7] + bb[7]);
+        *reinterpret_cast<float4*>(p + j0) = x0;
+        *reinterpret_cast<float4*>(p + j0 + 4) = x1;
       }
       break;
     }
@@ -218,7 +252,7 @@ __device__ __forceinline__ void epilogue32(const GemmGeom& g, const EpiArgs& e, 
 }
 
 template <int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmGeom g,
               const EpiArgs e, int* status) {
   using Cfg = GemmCfg<BN>;
@@ -243,7 +277,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kEpiWarps);
     }
     fence_mbar_init();
     prefetch_tmap(&tmA);
@@ -325,6 +359,10 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int r = q * 32 + lane;
+    // column range of this warp: halves of the tile when BN >= 64
+    const int half = (warp - 2) / 4;
+    const int c_begin = BN >= 64 ? half * (BN / 2) : (half == 0 ? 0 : BN);
+    const int c_end = BN >= 64 ? c_begin + BN / 2 : (half == 0 ? BN : BN);
     int it = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
@@ -345,7 +383,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = c_begin; c < c_end; c += 32) {
         uint32_t raw[32];
         tmem_ld32(tbase + c, raw);
         tmem_wait_ld();
@@ -452,7 +490,7 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeo
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
   if (tiles < grid) grid = tiles;
   if (grid <= 0) return 0;
-  k_tc_gemm<BN><<<grid, 192, Cfg::kSmemBytes, stream>>>(ta, tb, g, e, status);
+  k_tc_gemm<BN><<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, g, e, status);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }
 
@@ -485,6 +523,7 @@ int pick_bn(int N) {
 }
 
 static int check_epi(const EpiArgs& e, int N) {
+  if ((reinterpret_cast<uintptr_t>(e.bias) & 15) || (reinterpret_cast<uintptr_t>(e.scale) & 15)) return -19;
   if (e.kind == kEpiF16 || e.kind == kEpiConvT) {
     if (N % 8 || !e.out || e.ld_out % 8 || (reinterpret_cast<uintptr_t>(e.out) & 15)) return -20;
     if (e.out_relu && (reinterpret_cast<uintptr_t>(e.out_relu) & 15)) return -21;
@@ -493,7 +532,7 @@ static int check_epi(const EpiArgs& e, int N) {
     if (e.q8 && (N % 32 || e.res1 || e.res2 || e.out_relu || e.kind != kEpiF16)) return -29;
   }
   if (e.kind == kEpiResid || e.kind == kEpiTokens) {
-    if (N % 4 || !e.resid || e.ld_resid % 4 || (reinterpret_cast<uintptr_t>(e.resid) & 15)) return -24;
+    if (N % 8 || !e.resid || e.ld_resid % 4 || (reinterpret_cast<uintptr_t>(e.resid) & 15)) return -24;
     if (e.kind == kEpiTokens && (!e.pos || !e.bias || e.rm_div <= 0)) return -25;
   }
   if (e.kind == kEpiConvT && (e.ct_oc % 8 || e.ct_s <= 0 || e.ct_hin <= 0 || e.ct_win <= 0)) return -26;

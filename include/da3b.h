@@ -60,6 +60,12 @@ DA3B_API int da3b_linear_f16(const void* x, int M, int K, int lda, const void* w
 DA3B_API int da3b_linear_resid_f32(const void* x, int M, int K, int lda, const void* w, int N, int ldw,
                                    const float* bias, const float* scale, float* resid, int ldr, void* stream);
 
+/* Bidirectional attention softmax(q k^T / 8) v over head_dim 64 — the replacement of
+ * ggml_flash_attn_ext with F32 precision in attention() (src/attention.cpp:44-96).
+ * qkv: f16 [nseq*seqlen][3*heads*64] (q | k | v, head h at columns h*64 of each third,
+ * the layout of the QKV linear's output), out: f16 [nseq*seqlen][heads*64]. */
+DA3B_API int da3b_attention(const void* qkv, int nseq, int seqlen, int heads, void* out, void* stream);
+
 /* Packs a ggml conv2d weight (ne [KW,KH,IC,OC] f32 == torch [OC][IC][KH][KW]) into
  * the implicit-GEMM layout f16 [OC][KH*KW][icp], icp = IC rounded up to 64. */
 DA3B_API int da3b_pack_conv_weight(const float* w_f32, int OC, int IC, int ksize, void* w_packed, void* stream);
@@ -113,10 +119,10 @@ DA3B_API int da3b_launches(da_ctx* ctx, int n_views, int views_per_scene, int h,
 DA3B_API int da3b_debug_feature(da_ctx* ctx, int layer, void* out_f16, size_t capacity, int* rows, int* cols);
 /* 1 = replay captured CUDA graphs (default), 0 = eager launches. */
 DA3B_API int da3b_set_graphs(da_ctx* ctx, int on);
-/* 1 (default) = activations entering each Q8_0 linear are rounded through Q8_0 the
- * way ggml quantises them before its Q8_0 x Q8_0 dot products (ggml_mul_mat on
- * CPU, src/ggml_extend.hpp:6-10), so results follow the reference's numerics;
- * 0 = plain f16 activations. */
+/* 1 = activations entering each Q8_0 linear are rounded through Q8_0 the way ggml
+ * quantises them before its Q8_0 x Q8_0 dot products (ggml_mul_mat,
+ * src/ggml_extend.hpp:6-10); 0 (default) = plain f16 activations, which stay closer
+ * to the reference's outputs than a second, independent Q8_0 rounding does. */
 DA3B_API int da3b_set_act_quant(da_ctx* ctx, int on);
 /* 1 = the depth / confidence / ray outputs are the raw head logits (no output
  * activation), for parity checks against pre-activation reference values. */

@@ -120,3 +120,18 @@ def test_conv_nhwc(lib, B, H, W, IC, OC, ks):
     ref = ref.permute(0, 2, 3, 1) + r1.float() + r2.float()
     close(out, ref)
     close(outr, ref.clamp_min(0))
+
+
+@pytest.mark.parametrize("nseq,seqlen,heads", [(1, 1, 1), (2, 37, 2), (3, 1370, 6), (1, 1297 * 3, 4), (2, 200, 16)])
+def test_attention(lib, nseq, seqlen, heads):
+    g = torch.Generator(device="cuda").manual_seed(seqlen + heads)
+    D = heads * 64
+    qkv = (torch.randn(nseq * seqlen, 3 * D, device="cuda", generator=g) * 1.5).half()
+    out = torch.empty(nseq * seqlen, D, dtype=torch.float16, device="cuda")
+    assert lib.da3b_attention(ptr(qkv), nseq, seqlen, heads, ptr(out), stream()) == 0
+    torch.cuda.synchronize()
+    assert lib.da3b_device_status() == 0
+    q, k, v = qkv.float().view(nseq, seqlen, 3, heads, 64).permute(2, 0, 3, 1, 4)
+    ref = torch.softmax(q @ k.transpose(-1, -2) / 8.0, dim=-1) @ v          # [nseq, heads, seqlen, 64]
+    ref = ref.permute(0, 2, 1, 3).reshape(nseq * seqlen, D)
+    close(out, ref, rel=5e-3, abs_=5e-3)
