@@ -1,0 +1,300 @@
+// tcgen05 flash attention for sm_100a (head_dim 64, bidirectional).
+//
+// Replaces ggml_flash_attn_ext (F32 precision) of attention() (src/attention.cpp:44-96)
+// on the tensor cores. One CTA = 128 query rows of one (sequence, head); two CTAs per
+// SM (97 KB smem, 256 TMEM columns each) so one CTA's softmax overlaps the other's MMAs.
+//   warp 0     TMA: Q tile once; per key tile of 64, the K tile [64 keys][64] and the
+//              transposed V tile [64 dims][64 keys] (vt, written by the QKV GEMM
+//              epilogue) into a 3-stage ring;
+//   warp 1     one thread issues S_j = Q K_j^T (M=128, N=64, K=64) into one of two
+//              TMEM S buffers, and once the softmax published P_j, O_j = P_j V_j
+//              (M=128, N=64, K=64) into one of two TMEM O buffers;
+//   warps 2-5  softmax: thread = query row (its TMEM lane); S_j read once into registers
+//              (row max, then p = 2^(s*c - m*c)), P_j as f16 into one of two 128B-swizzled
+//              smem tiles, then o = o*alpha + O_{j-1} in registers (one tile behind, so
+//              the softmax never waits for the P V product it just enabled). Keys past
+//              the sequence are masked; rows past it are not stored.
+// Every wait is bounded (ptx.cuh); on a timeout the kernel records a status and exits.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "kernels.h"
+#include "ops.h"
+#include "ptx.cuh"
+
+namespace da3b {
+
+namespace {
+
+constexpr int kKT = 64;                  // keys per tile
+constexpr int kStagesKV = 3;
+constexpr int kQBytes = 128 * 64 * 2;    // Q tile [128][64]
+constexpr int kKBytes = kKT * 64 * 2;    // K tile [64 keys][64]
+constexpr int kVBytes = 64 * kKT * 2;    // V^T tile [64 dims][64 keys]
+constexpr int kPBytes = 128 * kKT * 2;   // P tile [128][64 keys] (double buffered)
+constexpr int kSmem = 1024 + kQBytes + kStagesKV * (kKBytes + kVBytes) + 2 * kPBytes + 256;
+constexpr uint32_t kTmemCols = 256;      // S[0..1]: cols [0,128), O[0..1]: cols [128,256)
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__global__ void __launch_bounds__(192, 2)
+    k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+              const __grid_constant__ CUtensorMap tmV, int seqlen, int H, int D, __half* __restrict__ out, float sl2,
+              int q8, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kQBytes;
+  uint8_t* sV = sK + kStagesKV * kKBytes;
+  uint8_t* sP = sV + kStagesKV * kVBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + kStagesKV;
+  uint64_t* s_full = kv_empty + kStagesKV;  // [2]
+  uint64_t* p_full = s_full + 2;            // [2] P_j written and S_j consumed
+  uint64_t* o_full = p_full + 2;            // [2]
+  uint64_t* o_free = o_full + 2;            // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, h = blockIdx.y, sq = blockIdx.z;
+  const int q0 = qt * 128;
+  const int row_base = sq * seqlen;               // first token row of this sequence
+  const int nkt = (seqlen + kKT - 1) / kKT;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStagesKV; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 4);
+      mbar_init(&o_full[b], 1);
+      mbar_init(&o_free[b], 4);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- TMA
+      mbar_arrive_expect_tx(q_full, kQBytes);
+      tma_load_2d(sQ, &tmQ, q_full, h * 64, row_base + q0);
+      int stage = 0;
+      uint32_t phase = 0;
+      const int vrow = (sq * H + h) * 64;
+      for (int j = 0; j < nkt; ++j) {
+        if (!mbar_wait(&kv_empty[stage], phase ^ 1u, status, kStatusTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&kv_full[stage], kKBytes + kVBytes);
+        tma_load_2d(sK + stage * kKBytes, &tmK, &kv_full[stage], D + h * 64, row_base + j * kKT);
+        tma_load_2d(sV + stage * kVBytes, &tmV, &kv_full[stage], j * kKT, vrow);
+        if (++stage == kStagesKV) { stage = 0; phase ^= 1u; }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- MMA
+      // S_j -> S[j&1], O_j -> O[j&1]. S_{j+2} is issued once the softmax consumed S_j;
+      // PV_j once P_j is written and O[j&1] was consumed (tile j-2).
+      constexpr uint32_t idS = umma_idesc_f16(128, kKT);
+      constexpr uint32_t idO = umma_idesc_f16(128, 64);
+      bool ok = mbar_wait(q_full, 0, status, kStatusTimeoutFull);
+      const uint64_t qdesc = umma_desc_sw128(smem_u32(sQ));
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % kStagesKV;
+        if (!mbar_wait(&kv_full[st], (j / kStagesKV) & 1, status, kStatusTimeoutFull)) return false;
+        tc_fence_after();
+        const uint64_t kdesc = umma_desc_sw128(smem_u32(sK + st * kKBytes));
+        const uint32_t tS = tmem + (j & 1) * 64;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) umma_f16(tS, qdesc + 2 * k, kdesc + 2 * k, idS, k > 0 ? 1u : 0u);
+        umma_commit(&s_full[j & 1]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && nkt > 1) ok = issue_s(1);
+      for (int j = 0; j < nkt && ok; ++j) {
+        const int st = j % kStagesKV, b = j & 1;
+        if (!mbar_wait(&p_full[b], (j >> 1) & 1, status, kStatusTimeoutFull)) break;
+        if (j >= 2 && !mbar_wait(&o_free[b], ((j - 2) >> 1) & 1, status, kStatusTimeoutAccumFree)) break;
+        tc_fence_after();
+        const uint64_t pdesc = umma_desc_sw128(smem_u32(sP + b * kPBytes));
+        const uint64_t vdesc = umma_desc_sw128(smem_u32(sV + st * kVBytes));
+        const uint32_t tO = tmem + 128 + b * 64;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) umma_f16(tO, pdesc + 2 * kk, vdesc + 2 * kk, idO, kk > 0 ? 1u : 0u);
+        umma_commit(&o_full[b]);
+        umma_commit(&kv_empty[st]);
+        if (j + 2 < nkt && !issue_s(j + 2)) break;
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ softmax
+    const int qq = warp & 3;
+    const int r = qq * 32 + lane;                    // query row within the tile == TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(qq * 32) << 16;
+    float o[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) o[i] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    bool ok = true;
+    // o += O_t (tile t) rescaled: o (scale of tile t-1) * alpha_t + O_t
+    auto take_o = [&](int t, float alpha_t) -> bool {
+      const int b = t & 1;
+      if (!mbar_wait(&o_full[b], (t >> 1) & 1, status, kStatusTimeoutAccum)) return false;
+      tc_fence_after();
+      uint32_t ra[32], rb[32];
+      tmem_ld32(tmem + 128 + b * 64 + lane_off, ra);
+      tmem_ld32(tmem + 128 + b * 64 + lane_off + 32, rb);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        o[i] = o[i] * alpha_t + __uint_as_float(ra[i]);
+        o[32 + i] = o[32 + i] * alpha_t + __uint_as_float(rb[i]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[b]);
+      return true;
+    };
+    for (int j = 0; j < nkt; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&s_full[b], (j >> 1) & 1, status, kStatusTimeoutAccum)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t tS = tmem + b * 64 + lane_off;
+      float sv[64];
+      {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tS, ra);
+        tmem_ld32(tS + 32, rb);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          sv[i] = __uint_as_float(ra[i]);
+          sv[32 + i] = __uint_as_float(rb[i]);
+        }
+      }
+      const int kvalid = seqlen - j * kKT;  // keys of this tile inside the sequence (>= 1)
+      if (kvalid < kKT) {
+#pragma unroll
+        for (int i = 0; i < kKT; ++i)
+          if (i >= kvalid) sv[i] = -INFINITY;
+      }
+      float mx = m;
+#pragma unroll
+      for (int i = 0; i < kKT; ++i) mx = fmaxf(mx, sv[i]);
+      const float mc = mx * sl2;
+      const float alpha = (m == -INFINITY) ? 0.f : ex2(m * sl2 - mc);
+      m = mx;
+      // p = 2^(s*c - m*c) (masked keys give 2^-inf = 0), row sum, f16 P into the
+      // 128B-swizzled row r of P[b] (the A operand of P V)
+      float rs = 0.f;
+      uint8_t* prow = sP + b * kPBytes + r * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float p0 = ex2(fmaf(sv[ch * 8 + 2 * k], sl2, -mc));
+          const float p1 = ex2(fmaf(sv[ch * 8 + 2 * k + 1], sl2, -mc));
+          rs += p0 + p1;
+          __half2 hp = __floats2half2_rn(p0, p1);
+          pk[k] = *reinterpret_cast<uint32_t*>(&hp);
+        }
+        *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      l = l * alpha + rs;
+      tc_fence_before();
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+      // accumulate the previous tile's P V while the tensor core works on this one
+      if (j > 0 && !take_o(j - 1, alpha_prev)) { ok = false; break; }
+      alpha_prev = alpha;
+    }
+    if (ok) ok = take_o(nkt - 1, alpha_prev);
+    if (ok && q0 + r < seqlen) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) o[i] *= inv;
+      if (q8) {
+        // Q8_0 round trip per 32-dim block (ggml quantize_row_q8_0_ref semantics)
+#pragma unroll
+        for (int bb = 0; bb < 2; ++bb) {
+          float amax = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[32 * bb + i]));
+          const float d = amax / 127.0f;
+          const float id = d != 0.f ? 1.0f / d : 0.0f;
+          const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[32 * bb + i] = dh * roundf(o[32 * bb + i] * id);
+        }
+      }
+      __half* dst = out + static_cast<size_t>(row_base + q0 + r) * D + h * 64;
+#pragma unroll
+      for (int i = 0; i < 64; i += 8) {
+        uint4 u;
+        __half2* hh = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) hh[k] = __floats2half2_rn(o[i + 2 * k], o[i + 2 * k + 1]);
+        *reinterpret_cast<uint4*>(dst + i) = u;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+// qkv: [nseq*seqlen][3D] (q | k | v), vt: [nseq][H][64][ld_vt] (transposed v, zero
+// beyond seqlen within each row), out: [nseq*seqlen][D].
+int attention_tc(const __half* qkv, const __half* vt, int ld_vt, int nseq, int seqlen, int H, int D, __half* out,
+                 int q8, int* status, cudaStream_t s) {
+  if (nseq <= 0 || seqlen <= 0) return 0;
+  if (D != H * 64 || ld_vt < seqlen || ld_vt % 8 || (reinterpret_cast<uintptr_t>(out) & 15)) return -1;
+  CUtensorMap tq, tk, tv;
+  int rc;
+  if ((rc = make_tmap_2d(&tq, qkv, nseq * seqlen, 3 * D, 3 * D, 128))) return rc - 100;
+  if ((rc = make_tmap_2d(&tk, qkv, nseq * seqlen, 3 * D, 3 * D, kKT))) return rc - 100;
+  if ((rc = make_tmap_2d(&tv, vt, nseq * H * 64, seqlen, ld_vt, 64))) return rc - 200;
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!((attr_set >> (dev & 63)) & 1)) {
+    if (cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess) return -3;
+    attr_set |= uint64_t(1) << (dev & 63);
+  }
+  dim3 grid((seqlen + 127) / 128, H, nseq);
+  const float sl2 = 0.125f * 1.4426950408889634f;
+  k_attn_tc<<<grid, 192, kSmem, s>>>(tq, tk, tv, seqlen, H, D, out, sl2, q8, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+}  // namespace da3b

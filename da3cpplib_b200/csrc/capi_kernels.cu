@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "da3b.h"
 #include "kernels.h"
 #include "ops.h"
@@ -85,10 +87,42 @@ DA3B_API int da3b_linear_resid_f32(const void* x, int M, int K, int lda, const v
                      static_cast<cudaStream_t>(stream));
 }
 
+// Scratch for the transposed V of da3b_attention: one grow-only buffer per device,
+// allocated by the library on first use (cudaMalloc) and reused by later calls.
+static std::mutex g_vt_mu;
+static void* g_vt_buf[64] = {nullptr};
+static size_t g_vt_cap[64] = {0};
+
+static __half* vt_scratch(size_t bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_vt_mu);
+  if (g_vt_cap[dev] < bytes) {
+    if (g_vt_buf[dev]) {
+      cudaDeviceSynchronize();
+      cudaFree(g_vt_buf[dev]);
+    }
+    g_vt_buf[dev] = nullptr;
+    g_vt_cap[dev] = 0;
+    if (cudaMalloc(&g_vt_buf[dev], bytes) != cudaSuccess) return nullptr;
+    g_vt_cap[dev] = bytes;
+  }
+  return static_cast<__half*>(g_vt_buf[dev]);
+}
+
 DA3B_API int da3b_attention(const void* qkv, int nseq, int seqlen, int heads, void* out, void* stream) {
-  if (!qkv || !out || heads <= 0) return -100;
-  return flash_attn(static_cast<const __half*>(qkv), nseq, seqlen, heads, heads * 64, static_cast<__half*>(out),
-                    static_cast<cudaStream_t>(stream), 0);
+  if (!qkv || !out || heads <= 0 || nseq < 0 || seqlen < 0) return -100;
+  if (nseq == 0 || seqlen == 0) return 0;
+  int* st = device_status_word();
+  if (!st) return -101;
+  const int D = heads * 64, ld = (seqlen + 7) / 8 * 8;
+  __half* vt = vt_scratch(static_cast<size_t>(nseq) * D * ld * sizeof(__half));
+  if (!vt) return -102;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = transpose_v(static_cast<const __half*>(qkv), nseq, seqlen, heads, D, vt, ld, s);
+  if (rc) return rc;
+  return attention_tc(static_cast<const __half*>(qkv), vt, ld, nseq, seqlen, heads, D, static_cast<__half*>(out), 0,
+                      st, s);
 }
 
 DA3B_API int da3b_pack_conv_weight(const float* w_f32, int OC, int IC, int ksize, void* w_packed, void* stream) {

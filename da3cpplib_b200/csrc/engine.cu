@@ -60,6 +60,8 @@ struct Plan {
   float *x = nullptr, *x2 = nullptr, *pos = nullptr;
   float *rl_cos = nullptr, *rl_sin = nullptr, *rn_cos = nullptr, *rn_sin = nullptr;
   __half *patchA = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *hid = nullptr;
+  __half* vt = nullptr;   // transposed V [nseq][H][64][ld] written by the QKV epilogue
+  int ld_vt_local = 0, ld_vt_global = 0;
   __half* feats[4] = {nullptr, nullptr, nullptr, nullptr};
   __half* ftmp[4] = {nullptr, nullptr, nullptr, nullptr};
   __half* featn[4] = {nullptr, nullptr, nullptr, nullptr};  // head-LayerNormed features (DA3)
@@ -295,6 +297,9 @@ Plan* Engine::plan_for(int V, int S, int H, int W, bool rays) {
     T(p->patchA, V_ * Np * model_->patch_ldk);
     T(p->xn, M_ * D);
     T(p->qkv, M_ * 3 * D);
+    p->ld_vt_local = (p->Ntok + 7) / 8 * 8;
+    p->ld_vt_global = (S * p->Ntok + 7) / 8 * 8;
+    T(p->vt, std::max(V_ * D * p->ld_vt_local, static_cast<size_t>(p->scenes) * D * p->ld_vt_global));
     T(p->attn, M_ * D);
     T(p->hid, M_ * c.mlp_hidden);
     for (int o = 0; o < 4; ++o) T(p->feats[o], V_ * Np * p->Cf);
@@ -471,14 +476,23 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
     // ---- attention half
     const int q8 = act_quant_ ? 1 : 0;
     CK(layernorm_f32(p.x, D, M, D, b.n1g, b.n1b, c.ln_eps, p.xn, D, 0, 0, 0, 0, s, q8));
-    CK(gemm_linear(p.xn, M, D, D, b.qkv.w, b.qkv.N, b.qkv.ldw, 0, epi_f16(p.qkv, 3 * D, b.qkv.b, kActNone), status_, s));
+    const int seqlen = global ? p.S * Nt : Nt, nseq = global ? p.scenes : V;
+    const int ld_vt = global ? p.ld_vt_global : p.ld_vt_local;
+    {
+      EpiArgs e = epi_f16(p.qkv, 3 * D, b.qkv.b, kActNone);
+      e.kind = kEpiQKV;
+      e.vt = p.vt;
+      e.vt_seqlen = seqlen;
+      e.vt_ld = ld_vt;
+      e.vt_d = D;
+      CK(gemm_linear(p.xn, M, D, D, b.qkv.w, b.qkv.N, b.qkv.ldw, 0, e, status_, s));
+    }
     if (b.qng || use_rope) {
       const float* cs = use_rope ? (global ? p.rn_cos : p.rl_cos) : nullptr;
       const float* sn = use_rope ? (global ? p.rn_sin : p.rl_sin) : nullptr;
       CK(qk_norm_rope(p.qkv, M, Hh, D, Nt, b.qng, b.qnb, b.kng, b.knb, cs, sn, s));
     }
-    if (global) CK(flash_attn(p.qkv, p.scenes, p.S * Nt, Hh, D, p.attn, s, q8));
-    else CK(flash_attn(p.qkv, V, Nt, Hh, D, p.attn, s, q8));
+    CK(attention_tc(p.qkv, p.vt, ld_vt, nseq, seqlen, Hh, D, p.attn, q8, status_, s));
     {
       EpiArgs e = epi_default();
       e.kind = kEpiResid;

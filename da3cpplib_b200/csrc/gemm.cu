@@ -219,6 +219,35 @@ __device__ __forceinline__ void epilogue32(const GemmGeom& g, const EpiArgs& e, 
       }
       break;
     }
+    case kEpiQKV: {
+      // q | k thirds: plain f16 rows; v third: transposed store vt[seq][h][d][tok]
+      // (a warp's 32 rows are 32 consecutive tokens: each d is one 64-byte run).
+      if (n_base < 2 * e.vt_d) {
+        for (int j0 = 0; j0 < nvalid; j0 += 8) {
+          float t[8];
+          if (e.bias) {
+            load_f8(e.bias + n_base + j0, t);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) t[i] += v[j0 + i];
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) t[i] = v[j0 + i];
+          }
+          store_h8(e.out + static_cast<size_t>(row) * e.ld_out + n_base + j0, t);
+        }
+      } else {
+        const int seq = row / e.vt_seqlen, tok = row % e.vt_seqlen;
+        const int c0 = n_base - 2 * e.vt_d;  // 32 columns within one head (64 | c0 + 32)
+        const int nh = e.vt_d / 64;
+        __half* dst = e.vt + (static_cast<size_t>(seq) * nh * 64 + c0) * e.vt_ld + tok;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float b = e.bias ? __ldg(e.bias + n_base + i) : 0.0f;
+          dst[static_cast<size_t>(i) * e.vt_ld] = __float2half_rn(v[i] + b);
+        }
+      }
+      break;
+    }
     case kEpiOut2: {
       // out2a channels (N == 32) -> [channels-last LayerNorm] -> relu -> out2b 1x1 -> activation
 #pragma unroll
@@ -536,6 +565,9 @@ static int check_epi(const EpiArgs& e, int N) {
     if (e.kind == kEpiTokens && (!e.pos || !e.bias || e.rm_div <= 0)) return -25;
   }
   if (e.kind == kEpiConvT && (e.ct_oc % 8 || e.ct_s <= 0 || e.ct_hin <= 0 || e.ct_win <= 0)) return -26;
+  if (e.kind == kEpiQKV && (!e.out || !e.vt || e.ld_out % 8 || N != 3 * e.vt_d || e.vt_d % 64 || e.vt_seqlen <= 0 ||
+                            e.vt_ld < e.vt_seqlen || e.vt_ld % 8))
+    return -18;
   if (e.kind == kEpiOut2) {
     if (N != 32 || e.o2_dim < 1 || e.o2_dim > 8 || !e.o2_w || !e.o2_b) return -27;
     for (int i = 0; i < e.o2_dim; ++i)

@@ -20,6 +20,8 @@ enum EpiKind : int {
   kEpiTokens = 2,  // resid_f32[row map] = acc + bias + pos[...]   (patch embed)
   kEpiConvT = 3,   // stride==kernel transposed conv: pixel-shuffle f16 store
   kEpiOut2 = 4,    // out2a(32ch) -> [LN] -> relu -> out2b (<=8ch) -> activation -> f32 planes
+  kEpiQKV = 5,     // QKV linear: q|k columns to out (f16 [rows][ld_out]) and the v third
+                   // transposed per (sequence, head) to vt [seq][H][64][ld_vt] for attention
 };
 
 enum Act : int { kActNone = 0, kActRelu = 1, kActGelu = 2 };
@@ -80,6 +82,9 @@ struct EpiArgs {
   int o2_act[8];          // OutAct per output channel
   float o2_scale;         // kOutSigmoidScale factor
   float* o2_out[8];       // f32 plane per output channel, indexed by output pixel
+  // kEpiQKV
+  __half* vt;             // [nseq][H][64][ld_vt]
+  int vt_seqlen, vt_ld, vt_d;  // tokens per attention sequence, row pitch (>= seqlen, %8), model dim D
 };
 
 }  // namespace da3b

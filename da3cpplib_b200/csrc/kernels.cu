@@ -364,6 +364,32 @@ int im2col_s2(const __half* in, int B, int h, int w, int C, int icp, __half* out
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
+// ---------------------------------------------------------------- V transpose
+// v third of qkv [nseq*seqlen][3D] -> vt [nseq][H][64][ld] (per head, token-contiguous).
+// 32 x 32 tiles through shared memory: coalesced reads along d, writes along tokens.
+__global__ void k_transpose_v(const __half* __restrict__ qkv, int nseq, int seqlen, int H, int D,
+                              __half* __restrict__ vt, int ld) {
+  __shared__ __half tile[32][33];
+  const int tok0 = blockIdx.x * 32, c0 = blockIdx.y * 32, sq = blockIdx.z;  // c0: column within v (0..D)
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;                       // 32 x 8 threads
+  for (int i = ty; i < 32; i += 8) {
+    const int tok = tok0 + i;
+    tile[i][tx] = tok < seqlen ? qkv[(static_cast<size_t>(sq) * seqlen + tok) * 3 * D + 2 * D + c0 + tx]
+                               : __float2half(0.f);
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int c = c0 + i, tok = tok0 + tx;
+    if (tok < seqlen) vt[(static_cast<size_t>(sq) * D + c) * ld + tok] = tile[tx][i];
+  }
+}
+int transpose_v(const __half* qkv, int nseq, int seqlen, int H, int D, __half* vt, int ld, cudaStream_t s) {
+  if (D != H * 64 || ld < seqlen) return -1;
+  dim3 grid((seqlen + 31) / 32, D / 32, nseq);
+  k_transpose_v<<<grid, 256, 0, s>>>(qkv, nseq, seqlen, H, D, vt, ld);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
 // ---------------------------------------------------------------- reference-view selection
 // One block per scene: saddle-balanced choice over the views' token-0 features after
 // the local blocks [0, alt_start-1) (src/dino_backbone.cpp:372-412), in double.

@@ -30,9 +30,12 @@ int permute_views(const float* src, float* dst, int scenes, int S, long view_ele
 int unpermute_views_h(const __half* src, __half* dst, int scenes, int S, long view_elems, const int* b_idx,
                       cudaStream_t s);
 
-// Flash attention over qkv [nseq*seqlen][3D] (q | k | v, heads of 64), output
-// [nseq*seqlen][D] f16 (head h at columns h*64..h*64+63).
-// q8 = 1: Q8_0 round trip of each 32-dim block of the output rows.
-int flash_attn(const __half* qkv, int nseq, int seqlen, int H, int D, __half* out, cudaStream_t s, int q8 = 0);
+// v third of qkv -> vt [nseq][H][64][ld] (the B operand layout of the tcgen05 attention).
+int transpose_v(const __half* qkv, int nseq, int seqlen, int H, int D, __half* vt, int ld, cudaStream_t s);
+// tcgen05 flash attention: q, k from qkv, v from vt (attention_tc.cu).
+int attention_tc(const __half* qkv, const __half* vt, int ld_vt, int nseq, int seqlen, int H, int D, __half* out,
+                 int q8, int* status, cudaStream_t s);
+
+
 
 }  // namespace da3b

