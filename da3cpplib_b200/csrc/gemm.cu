@@ -16,6 +16,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "gemm.h"
@@ -437,6 +438,191 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------- 2-SM variant
+// Same roles over a CTA pair (cluster of 2, cta_group::2): a tile is 256 rows x BN;
+// each CTA TMA-loads its own 128 rows of A and BN/2 rows of B (no multicast) and
+// both loads complete on the leader's (rank 0) stage barrier; the leader's single
+// MMA thread issues M=256 tcgen05.mma over both CTAs' shared memory, which leaves
+// each CTA's 128 rows of the accumulator in its own TMEM; commits are multicast to
+// both CTAs; the peer's epilogue releases the accumulator with a remote arrive on
+// the leader's barrier. Per SM the operand traffic per MMA is 3/4 of the 1-SM tile's.
+template <int BN>
+struct Gemm2Cfg {
+  static constexpr int kABytes = 128 * 64 * 2;
+  static constexpr int kBBytes = (BN / 2) * 64 * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (kStageBytes * 6 <= 200 * 1024) ? 6 : 4;
+  static constexpr int kAccCols = (BN < 32) ? 32 : BN;
+  static constexpr int kTmemCols = (2 * kAccCols <= 64) ? 64 : (2 * kAccCols <= 128 ? 128 : (2 * kAccCols <= 256 ? 256 : 512));
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    k_tc_gemm2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmGeom g,
+               const EpiArgs e, int* status) {
+  using Cfg = Gemm2Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + Cfg::kStages * Cfg::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  uint64_t* empty = full + Cfg::kStages;
+  uint64_t* tfull = empty + Cfg::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int m_pairs = (g.num_m_tiles + 1) >> 1;
+  const int num_tiles = m_pairs * g.num_n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kEpiWarps);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) tmem_alloc2(tmem_slot, Cfg::kTmemCols);
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs) {
+        const int mp = t / g.num_n_tiles, nt = t % g.num_n_tiles;
+        const int mt = 2 * mp + static_cast<int>(rank);  // this CTA's 128-row tile
+        const int n0 = nt * BN + static_cast<int>(rank) * (BN / 2);
+        int cb = 0, cx = 0, cy = 0;
+        if (g.mode == kModeConv) {
+          const int per_img = g.tiles_x * g.tiles_y;
+          cb = mt / per_img;  // may be == B for the odd tail tile: zero-filled
+          const int rem = mt % per_img;
+          cy = (rem / g.tiles_x) * g.bh;
+          cx = (rem % g.tiles_x) * g.bw;
+        }
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, status, kStatusTimeoutEmpty)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
+          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+          uint8_t* a_dst = sA + stage * Cfg::kABytes;
+          uint8_t* b_dst = sB + stage * Cfg::kBBytes;
+          if (g.mode == kModeConv) {
+            const int tap = kb / g.ic_chunks;
+            const int ic0 = (kb % g.ic_chunks) * 64;
+            const int dy = tap / g.ksize - g.pad, dx = tap % g.ksize - g.pad;
+            tma2_load_4d(a_dst, &tmA, fb, ic0, cx + dx, cy + dy, cb);
+            tma2_load_2d(b_dst, &tmB, fb, tap * g.icp + ic0, n0);
+          } else {
+            tma2_load_2d(a_dst, &tmA, fb, kb * 64, mt * 128);
+            tma2_load_2d(b_dst, &tmB, fb, kb * 64, n0);
+          }
+          if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ------------------------------------------------------------ MMA issuer (leader only)
+      constexpr uint32_t idesc = umma_idesc_f16(256, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, status, kStatusTimeoutAccumFree)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccCols;
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, status, kStatusTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_sw128(smem_u32(sA + stage * Cfg::kABytes));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * Cfg::kBBytes));
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma2_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          umma2_commit_mc(&empty[stage], 0x3);
+          if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) umma2_commit_mc(&tfull[acc], 0x3);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int half = (warp - 2) / 4;
+    const int c_begin = BN >= 64 ? half * (BN / 2) : (half == 0 ? 0 : BN);
+    const int c_end = BN >= 64 ? c_begin + BN / 2 : (half == 0 ? BN : BN);
+    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty[1]), 0);
+    int it = 0;
+    for (int t = pair; t < num_tiles; t += npairs, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      const int mp = t / g.num_n_tiles, nt = t % g.num_n_tiles;
+      const int mt = 2 * mp + static_cast<int>(rank);
+      int row = -1;
+      if (g.mode == kModeConv) {
+        const int per_img = g.tiles_x * g.tiles_y;
+        const int b = mt / per_img, rem = mt % per_img;
+        const int y = (rem / g.tiles_x) * g.bh + r / g.bw;
+        const int x = (rem % g.tiles_x) * g.bw + r % g.bw;
+        if (b < g.B && y < g.H && x < g.W) row = (b * g.H + y) * g.W + x;
+      } else {
+        const int m = mt * 128 + r;
+        if (m < g.M) row = m;
+      }
+      if (!mbar_wait(&tfull[acc], acc_phase, status, kStatusTimeoutAccum)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
+#pragma unroll 1
+      for (int c = c_begin; c < c_end; c += 32) {
+        uint32_t raw[32];
+        tmem_ld32(tbase + c, raw);
+        tmem_wait_ld();
+        if (row >= 0) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
+          epilogue32(g, e, row, nt * BN + c, v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc ? tempty_leader1 : tempty_leader0);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc2(tmem_base, Cfg::kTmemCols);
+  }
+}
+
 // ---------------------------------------------------------------- host side
 
 typedef CUresult (*PFN_tmapEncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -523,6 +709,67 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeo
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }
 
+template <int BN>
+static int launch_bn2(const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeom& g, const EpiArgs& e, int* status,
+                      cudaStream_t stream) {
+  using Cfg = Gemm2Cfg<BN>;
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!((attr_set >> (dev & 63)) & 1)) {
+    if (cudaFuncSetAttribute(k_tc_gemm2<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
+        cudaSuccess)
+      return -10;
+    attr_set |= uint64_t(1) << (dev & 63);
+  }
+  const int tiles = ((g.num_m_tiles + 1) / 2) * g.num_n_tiles;
+  int pairs = num_sms() / 2;
+  if (tiles < pairs) pairs = tiles;
+  if (pairs <= 0) return 0;
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, k_tc_gemm2<BN>, ta, tb, g, e, status) != cudaSuccess) return -11;
+  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+}
+
+// 1 = use the 2-SM kernel for problems with enough 256-row tiles (default);
+// the environment variable DA3B_GEMM_2SM=0 keeps every launch on the 1-SM kernel.
+static int use_2sm() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("DA3B_GEMM_2SM");
+    v = (s && s[0] == '0') ? 0 : 1;
+  }
+  return v;
+}
+
+// 2-SM launch (B tensor map box of bn/2 rows). BN in {64, 128, 256}.
+static int gemm_launch2(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeom& g, const EpiArgs& e,
+                        int* status, cudaStream_t stream) {
+  switch (bn) {
+    case 64: return launch_bn2<64>(ta, tb, g, e, status, stream);
+    case 128: return launch_bn2<128>(ta, tb, g, e, status, stream);
+    case 256: return launch_bn2<256>(ta, tb, g, e, status, stream);
+    default: return -12;
+  }
+}
+
+// The 2-SM kernel pays off once every CTA pair gets at least one 256-row tile.
+static bool want_2sm(const GemmGeom& g, int bn) {
+  return use_2sm() && bn >= 64 && ((g.num_m_tiles + 1) / 2) * g.num_n_tiles >= num_sms() / 2;
+}
+
 // Launch with a validated geometry. BN in {32, 64, 128, 256}.
 int gemm_launch(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeom& g, const EpiArgs& e,
                 int* status, cudaStream_t stream, int max_ctas) {
@@ -584,9 +831,6 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
   if (e.kind == kEpiOut2) bn = 32;
   int rc = check_epi(e, N);
   if (rc) return rc;
-  CUtensorMap ta, tb;
-  if ((rc = make_tmap_2d(&ta, A, M, K, lda, 128))) return rc - 100;
-  if ((rc = make_tmap_2d(&tb, W, N, K, ldw, bn))) return rc - 200;
   GemmGeom g;
   memset(&g, 0, sizeof(g));
   g.mode = kModeLinear;
@@ -596,7 +840,11 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
   g.num_kb = (K + 63) / 64;
   g.num_m_tiles = (M + 127) / 128;
   g.num_n_tiles = (N + bn - 1) / bn;
-  return gemm_launch(bn, ta, tb, g, e, status, stream, 0);
+  const bool two = want_2sm(g, bn);
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap_2d(&ta, A, M, K, lda, 128))) return rc - 100;
+  if ((rc = make_tmap_2d(&tb, W, N, K, ldw, two ? bn / 2 : bn))) return rc - 200;
+  return two ? gemm_launch2(bn, ta, tb, g, e, status, stream) : gemm_launch(bn, ta, tb, g, e, status, stream, 0);
 }
 
 // Pixel block of one 128-row M tile: the (bw, bh) with bw * bh == 128 that wastes
@@ -625,9 +873,6 @@ int conv_nhwc(const __half* X, int B, int H, int W, int IC, const __half* Wp, in
   int bw = 16, bh = 8;
   pick_block(H, W, &bw, &bh);
   const int icp = conv_icp(IC);
-  CUtensorMap ta, tb;
-  if ((rc = make_tmap_nhwc(&ta, X, B, H, W, IC, bw, bh))) return rc - 100;
-  if ((rc = make_tmap_2d(&tb, Wp, OC, ksize * ksize * icp, ksize * ksize * icp, bn))) return rc - 200;
   GemmGeom g;
   memset(&g, 0, sizeof(g));
   g.mode = kModeConv;
@@ -648,7 +893,11 @@ int conv_nhwc(const __half* X, int B, int H, int W, int IC, const __half* Wp, in
   g.tiles_y = (H + bh - 1) / bh;
   g.num_m_tiles = B * g.tiles_x * g.tiles_y;
   g.num_n_tiles = (OC + bn - 1) / bn;
-  return gemm_launch(bn, ta, tb, g, e, status, stream, 0);
+  const bool two = want_2sm(g, bn);
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap_nhwc(&ta, X, B, H, W, IC, bw, bh))) return rc - 100;
+  if ((rc = make_tmap_2d(&tb, Wp, OC, ksize * ksize * icp, ksize * ksize * icp, two ? bn / 2 : bn))) return rc - 200;
+  return two ? gemm_launch2(bn, ta, tb, g, e, status, stream) : gemm_launch(bn, ta, tb, g, e, status, stream, 0);
 }
 
 }  // namespace da3b
