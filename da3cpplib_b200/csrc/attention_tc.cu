@@ -2,18 +2,19 @@
 //
 // Replaces ggml_flash_attn_ext (F32 precision) of attention() (src/attention.cpp:44-96)
 // on the tensor cores. One CTA = 128 query rows of one (sequence, head); two CTAs per
-// SM (97 KB smem, 256 TMEM columns each) so one CTA's softmax overlaps the other's MMAs.
+// SM (~103 KB smem, 256 TMEM columns each) so one CTA's softmax overlaps the other's MMAs.
 //   warp 0     TMA: Q tile once; per key tile of 64, the K tile [64 keys][64] and the
 //              transposed V tile [64 dims][64 keys] (vt, written by the QKV GEMM
 //              epilogue) into a 3-stage ring;
 //   warp 1     one thread issues S_j = Q K_j^T (M=128, N=64, K=64) into one of two
-//              TMEM S buffers, and once the softmax published P_j, O_j = P_j V_j
-//              (M=128, N=64, K=64) into one of two TMEM O buffers;
-//   warps 2-5  softmax: thread = query row (its TMEM lane); S_j read once into registers
-//              (row max, then p = 2^(s*c - m*c)), P_j as f16 into one of two 128B-swizzled
-//              smem tiles, then o = o*alpha + O_{j-1} in registers (one tile behind, so
-//              the softmax never waits for the P V product it just enabled). Keys past
-//              the sequence are masked; rows past it are not stored.
+//              TMEM S buffers, and once the softmax published P_j, O += P_j [V_j^T; 1]
+//              (M=128, N=80, K=64) into one TMEM accumulator: column 64 (a row of ones
+//              appended to V^T) accumulates the softmax row sums with the same f16 P;
+//   warps 2-5  softmax: thread = query row (its TMEM lane); S_j read once into registers,
+//              p = 2^(s*c - m*c) as f16 into one of two 128B-swizzled smem tiles. The
+//              max m is only raised when a tile's max exceeds it by more than 2^8; then
+//              O is rescaled in TMEM (once the previous P V landed). O / rowsum at the
+//              end. Keys past the sequence are masked; rows past it are not stored.
 // Every wait is bounded (ptx.cuh); on a timeout the kernel records a status and exits.
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -33,16 +34,13 @@ constexpr int kKT = 64;                  // keys per tile
 constexpr int kStagesKV = 3;
 constexpr int kQBytes = 128 * 64 * 2;    // Q tile [128][64]
 constexpr int kKBytes = kKT * 64 * 2;    // K tile [64 keys][64]
-constexpr int kVBytes = 64 * kKT * 2;    // V^T tile [64 dims][64 keys]
+constexpr int kVRows = 80;               // V^T rows: 64 dims, a row of ones (row sums), 15 zero rows
+constexpr int kVBytes = kVRows * kKT * 2;
 constexpr int kPBytes = 128 * kKT * 2;   // P tile [128][64 keys] (double buffered)
 constexpr int kSmem = 1024 + kQBytes + kStagesKV * (kKBytes + kVBytes) + 2 * kPBytes + 256;
-constexpr uint32_t kTmemCols = 256;      // S[0..1]: cols [0,128), O[0..1]: cols [128,256)
+constexpr uint32_t kTmemCols = 256;      // S[0..1]: cols [0,128), O (80 cols): [128,208)
+constexpr float kRescaleLog2 = 8.0f;     // rescale O only when the row max grows by > 2^8
 
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __global__ void __launch_bounds__(192, 2)
@@ -61,9 +59,8 @@ __global__ void __launch_bounds__(192, 2)
   uint64_t* kv_empty = kv_full + kStagesKV;
   uint64_t* s_full = kv_empty + kStagesKV;  // [2]
   uint64_t* p_full = s_full + 2;            // [2] P_j written and S_j consumed
-  uint64_t* o_full = p_full + 2;            // [2]
-  uint64_t* o_free = o_full + 2;            // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
+  uint64_t* o_full = p_full + 2;            // one completion per P V product
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, h = blockIdx.y, sq = blockIdx.z;
@@ -71,6 +68,15 @@ __global__ void __launch_bounds__(192, 2)
   const int row_base = sq * seqlen;               // first token row of this sequence
   const int nkt = (seqlen + kKT - 1) / kKT;
 
+  // rows 64..79 of every V^T stage: a row of ones (its product with P is the row sum
+  // of P) and zeros; the TMA only ever writes rows 0..63. Swizzling permutes 16-byte
+  // chunks within a row, so a constant row needs no swizzle.
+  for (int i = threadIdx.x; i < kStagesKV * 16 * 8; i += blockDim.x) {
+    const int st = i / 128, r = 64 + (i % 128) / 8, c = i % 8;
+    const uint32_t v = (r == 64) ? 0x3C003C00u : 0u;  // f16 1.0 pairs
+    *reinterpret_cast<uint4*>(sV + st * kVBytes + r * 128 + c * 16) = make_uint4(v, v, v, v);
+  }
+  fence_async_smem();
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kStagesKV; ++s) {
@@ -80,9 +86,8 @@ __global__ void __launch_bounds__(192, 2)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 4);
-      mbar_init(&o_full[b], 1);
-      mbar_init(&o_free[b], 4);
     }
+    mbar_init(o_full, 1);
     fence_mbar_init();
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
@@ -93,6 +98,7 @@ __global__ void __launch_bounds__(192, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const uint32_t tO = tmem + 128;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -104,7 +110,7 @@ __global__ void __launch_bounds__(192, 2)
       const int vrow = (sq * H + h) * 64;
       for (int j = 0; j < nkt; ++j) {
         if (!mbar_wait(&kv_empty[stage], phase ^ 1u, status, kStatusTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&kv_full[stage], kKBytes + kVBytes);
+        mbar_arrive_expect_tx(&kv_full[stage], kKBytes + 64 * kKT * 2);
         tma_load_2d(sK + stage * kKBytes, &tmK, &kv_full[stage], D + h * 64, row_base + j * kKT);
         tma_load_2d(sV + stage * kVBytes, &tmV, &kv_full[stage], j * kKT, vrow);
         if (++stage == kStagesKV) { stage = 0; phase ^= 1u; }
@@ -114,10 +120,10 @@ __global__ void __launch_bounds__(192, 2)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------------- MMA
-      // S_j -> S[j&1], O_j -> O[j&1]. S_{j+2} is issued once the softmax consumed S_j;
-      // PV_j once P_j is written and O[j&1] was consumed (tile j-2).
+      // S_j -> S[j&1]; S_{j+2} is issued once the softmax consumed S_j. O (+ the row
+      // sums in column 64) accumulates over all key tiles: O += P_j [V_j^T; 1; 0].
       constexpr uint32_t idS = umma_idesc_f16(128, kKT);
-      constexpr uint32_t idO = umma_idesc_f16(128, 64);
+      constexpr uint32_t idO = umma_idesc_f16(128, kVRows);
       bool ok = mbar_wait(q_full, 0, status, kStatusTimeoutFull);
       const uint64_t qdesc = umma_desc_sw128(smem_u32(sQ));
       auto issue_s = [&](int j) -> bool {
@@ -135,15 +141,15 @@ __global__ void __launch_bounds__(192, 2)
       if (ok && nkt > 1) ok = issue_s(1);
       for (int j = 0; j < nkt && ok; ++j) {
         const int st = j % kStagesKV, b = j & 1;
+        // P_j published (and, if the softmax rescaled O, that rescale is complete)
         if (!mbar_wait(&p_full[b], (j >> 1) & 1, status, kStatusTimeoutFull)) break;
-        if (j >= 2 && !mbar_wait(&o_free[b], ((j - 2) >> 1) & 1, status, kStatusTimeoutAccumFree)) break;
         tc_fence_after();
         const uint64_t pdesc = umma_desc_sw128(smem_u32(sP + b * kPBytes));
         const uint64_t vdesc = umma_desc_sw128(smem_u32(sV + st * kVBytes));
-        const uint32_t tO = tmem + 128 + b * 64;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_f16(tO, pdesc + 2 * kk, vdesc + 2 * kk, idO, kk > 0 ? 1u : 0u);
-        umma_commit(&o_full[b]);
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(tO, pdesc + 2 * kk, vdesc + 2 * kk, idO, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(o_full);
         umma_commit(&kv_empty[st]);
         if (j + 2 < nkt && !issue_s(j + 2)) break;
       }
@@ -154,33 +160,11 @@ __global__ void __launch_bounds__(192, 2)
     const int qq = warp & 3;
     const int r = qq * 32 + lane;                    // query row within the tile == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(qq * 32) << 16;
-    float o[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) o[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    float m = -INFINITY;                             // max used for the exponentials so far
     bool ok = true;
-    // o += O_t (tile t) rescaled: o (scale of tile t-1) * alpha_t + O_t
-    auto take_o = [&](int t, float alpha_t) -> bool {
-      const int b = t & 1;
-      if (!mbar_wait(&o_full[b], (t >> 1) & 1, status, kStatusTimeoutAccum)) return false;
-      tc_fence_after();
-      uint32_t ra[32], rb[32];
-      tmem_ld32(tmem + 128 + b * 64 + lane_off, ra);
-      tmem_ld32(tmem + 128 + b * 64 + lane_off + 32, rb);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        o[i] = o[i] * alpha_t + __uint_as_float(ra[i]);
-        o[32 + i] = o[32 + i] * alpha_t + __uint_as_float(rb[i]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free[b]);
-      return true;
-    };
     for (int j = 0; j < nkt; ++j) {
       const int b = j & 1;
-      if (!mbar_wait(&s_full[b], (j >> 1) & 1, status, kStatusTimeoutAccum)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[b], (j >> 1) & 1, status, kStatusTimeoutAccum)) { ok = false; break; }
       tc_fence_after();
       const uint32_t tS = tmem + b * 64 + lane_off;
       float sv[64];
@@ -201,65 +185,104 @@ __global__ void __launch_bounds__(192, 2)
         for (int i = 0; i < kKT; ++i)
           if (i >= kvalid) sv[i] = -INFINITY;
       }
-      float mx = m;
+      float mt = sv[0];
 #pragma unroll
-      for (int i = 0; i < kKT; ++i) mx = fmaxf(mx, sv[i]);
-      const float mc = mx * sl2;
-      const float alpha = (m == -INFINITY) ? 0.f : ex2(m * sl2 - mc);
-      m = mx;
-      // p = 2^(s*c - m*c) (masked keys give 2^-inf = 0), row sum, f16 P into the
-      // 128B-swizzled row r of P[b] (the A operand of P V)
-      float rs = 0.f;
+      for (int i = 1; i < kKT; ++i) mt = fmaxf(mt, sv[i]);
+      // The running max of a row is raised only when a tile's max exceeds it by more
+      // than 2^8; the accumulated O (and its row-sum column) is then rescaled in TMEM
+      // once P V_{j-1} has landed. The TMEM read-modify-write is warp-collective, so the
+      // whole warp takes the branch if any of its rows needs it (alpha = 1 elsewhere).
+      const bool need = (j > 0) && ((mt - m) * sl2 > kRescaleLog2);
+      if (j == 0) m = mt;
+      if (__any_sync(0xffffffffu, need)) {
+        if (!mbar_wait_warp(o_full, (j - 1) & 1, status, kStatusTimeoutAccum)) { ok = false; break; }
+        tc_fence_after();
+        const float alpha = need ? ex2_approx((m - mt) * sl2) : 1.0f;
+        uint32_t ra[32], rb[32], rc;
+        tmem_ld32(tO + lane_off, ra);
+        tmem_ld32(tO + lane_off + 32, rb);
+        tmem_ld1(tO + lane_off + 64, rc);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          ra[i] = __float_as_uint(__uint_as_float(ra[i]) * alpha);
+          rb[i] = __float_as_uint(__uint_as_float(rb[i]) * alpha);
+        }
+        rc = __float_as_uint(__uint_as_float(rc) * alpha);
+        tmem_st32(tO + lane_off, ra);
+        tmem_st32(tO + lane_off + 32, rb);
+        tmem_st1(tO + lane_off + 64, rc);
+        tmem_wait_st();
+        if (need) m = mt;
+      }
+      // p = 2^(s*c - m*c) (masked keys: 2^-inf = 0), f16 into the 128B-swizzled row r
+      // of P[b], the A operand of O += P V
+      const float mc = m * sl2;
       uint8_t* prow = sP + b * kPBytes + r * 128;
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         uint32_t pk[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const float p0 = ex2(fmaf(sv[ch * 8 + 2 * k], sl2, -mc));
-          const float p1 = ex2(fmaf(sv[ch * 8 + 2 * k + 1], sl2, -mc));
-          rs += p0 + p1;
+          const float p0 = ex2_approx(fmaf(sv[ch * 8 + 2 * k], sl2, -mc));
+          const float p1 = ex2_approx(fmaf(sv[ch * 8 + 2 * k + 1], sl2, -mc));
           __half2 hp = __floats2half2_rn(p0, p1);
           pk[k] = *reinterpret_cast<uint32_t*>(&hp);
         }
         *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
-      l = l * alpha + rs;
+      // o_full completes once per P V product. Parity waits only tell apart two
+      // consecutive phases, so the warp keeps itself at most one phase behind: before
+      // publishing P_j it waits for P_{j-1} V_{j-1} (P_j V_j cannot be issued yet, and
+      // S_j landing implies P_{j-2} V_{j-2} already completed).
+      if (j > 0 && !mbar_wait_warp(o_full, (j - 1) & 1, status, kStatusTimeoutAccum)) { ok = false; break; }
       tc_fence_before();
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[b]);
-      // accumulate the previous tile's P V while the tensor core works on this one
-      if (j > 0 && !take_o(j - 1, alpha_prev)) { ok = false; break; }
-      alpha_prev = alpha;
     }
-    if (ok) ok = take_o(nkt - 1, alpha_prev);
-    if (ok && q0 + r < seqlen) {
+    // final O and row sum after the last P V product
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) ok = mbar_wait_warp(o_full, (nkt - 1) & 1, status, kStatusTimeoutAccum);
+    if (ok) {
+      tc_fence_after();
+      float o[64];
+      uint32_t ra[32], rb[32], rc;
+      tmem_ld32(tO + lane_off, ra);
+      tmem_ld32(tO + lane_off + 32, rb);
+      tmem_ld1(tO + lane_off + 64, rc);
+      tmem_wait_ld();
+      const float l = __uint_as_float(rc);
       const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) o[i] *= inv;
-      if (q8) {
-        // Q8_0 round trip per 32-dim block (ggml quantize_row_q8_0_ref semantics)
-#pragma unroll
-        for (int bb = 0; bb < 2; ++bb) {
-          float amax = 0.f;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[32 * bb + i]));
-          const float d = amax / 127.0f;
-          const float id = d != 0.f ? 1.0f / d : 0.0f;
-          const float dh = __half2float(__float2half_rn(d));
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[32 * bb + i] = dh * roundf(o[32 * bb + i] * id);
-        }
+      for (int i = 0; i < 32; ++i) {
+        o[i] = __uint_as_float(ra[i]) * inv;
+        o[32 + i] = __uint_as_float(rb[i]) * inv;
       }
-      __half* dst = out + static_cast<size_t>(row_base + q0 + r) * D + h * 64;
+      if (q0 + r < seqlen) {
+        if (q8) {
+          // Q8_0 round trip per 32-dim block (ggml quantize_row_q8_0_ref semantics)
 #pragma unroll
-      for (int i = 0; i < 64; i += 8) {
-        uint4 u;
-        __half2* hh = reinterpret_cast<__half2*>(&u);
+          for (int bb = 0; bb < 2; ++bb) {
+            float amax = 0.f;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) hh[k] = __floats2half2_rn(o[i + 2 * k], o[i + 2 * k + 1]);
-        *reinterpret_cast<uint4*>(dst + i) = u;
+            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[32 * bb + i]));
+            const float d = amax / 127.0f;
+            const float id = d != 0.f ? 1.0f / d : 0.0f;
+            const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[32 * bb + i] = dh * roundf(o[32 * bb + i] * id);
+          }
+        }
+        __half* dst = out + static_cast<size_t>(row_base + q0 + r) * D + h * 64;
+#pragma unroll
+        for (int i = 0; i < 64; i += 8) {
+          uint4 u;
+          __half2* hh = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) hh[k] = __floats2half2_rn(o[i + 2 * k], o[i + 2 * k + 1]);
+          *reinterpret_cast<uint4*>(dst + i) = u;
+        }
       }
     }
   }

@@ -53,6 +53,8 @@ struct GemmGeom {
 struct EpiArgs {
   int kind;          // EpiKind
   int act;           // Act (kEpiF16)
+  int tma_store;     // set by the launcher: 1 = f16 tile via TMA store, 2 = f32 TMA reduce-add
+                     // into resid (2-SM kernel, row-major outputs without row remap)
   int q8;            // kEpiF16: round-trip each 32-column block through Q8_0 (ggml's
                      // activation quantisation before a Q8_0 matmul); needs N % 32 == 0
   const float* bias;   // [N] or null
