@@ -112,11 +112,10 @@ def dist_setup(args):
 
 
 def images_for(rank, world):
-    from da3cpplib_b200 import synth
+    from da3cpplib_b200 import shard, synth
 
-    per = IMAGES_TOTAL // world
-    first = rank * per
-    return np.stack([synth.image(synth.IMAGE_SEED, first + i, H, W) for i in range(per)]), per
+    first, end = shard.shard_range(IMAGES_TOTAL, world, rank)
+    return np.stack([synth.image(synth.IMAGE_SEED, i, H, W) for i in range(first, end)]), end - first
 
 
 def model_path(rank, world):
@@ -208,6 +207,11 @@ def run_gpu(args):
 
     def step(rgb_ptr, depth_ptr):
         model.infer_device(rgb_ptr, per, H, W, depth_ptr, stream=sptr)
+        if args.gather and dist and depth_ptr == depth_dev.data_ptr():
+            # optional NCCL gather of the depth maps to rank 0 (equal-sized slabs)
+            from da3cpplib_b200 import shard
+
+            shard.gather_to_rank0(depth_dev, IMAGES_TOTAL)
 
     # warm-up (plan creation, graph capture)
     for _ in range(max(args.warmup, 3)):
@@ -304,6 +308,7 @@ def run_gpu(args):
             "config": {"workload": "C3: DA2-L ViT-L/14 Q8_0 + DPT head, 64 images 518x518 sharded 64/N",
                        "model": "da2-large-random", "global_batch": IMAGES_TOTAL, "per_gpu_batch": per,
                        "seq_len": 1370, "parallelism": f"dp{world}",
+                       "gather": "depth maps to rank 0 over NCCL each step" if (args.gather and world > 1) else "none",
                        "l2": "flushed (256 MB write) between timed steps"},
             "e2e": {k: (round(v, 2) if isinstance(v, float) else v) for k, v in e2e.items()},
             "roofline": roofline,
@@ -327,6 +332,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", action="store_true",
+                    help="N>1: gather every step's depth maps to rank 0 over NCCL inside the timed region")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -1,0 +1,162 @@
+"""Isolated hot-path kernel sweep (the reference's microbench workload) on one GPU.
+
+Part A: Q8_0 x f16 linears. Weights are GGUF Q8_0 rows (int8 uniform in [-127, 127],
+f16 scales uniform in [1e-3, 1e-2]) repacked once by da3b_dequant_q8_0 (load time,
+timed separately); the timed op is da3b_linear_f16 on f16 N(0, 1) activations,
+M in {1370, 8*1370, 64*1370} x (K, N) in {(384, 1152), (768, 3072), (1024, 4096),
+(4096, 1024), (1536, 6144)}.
+Part B: DPT-head 3x3 stride-1 pad-1 convs, NHWC f16, C_in = C_out in {64, 128, 256},
+spatial 37..296, batch 8 (da3b_conv_nhwc).
+attn: da3b_attention at the C3 shape (64 x 1370 tokens, 16 heads) and the DA3
+multi-view global layer (8 views x 1297 tokens per scene).
+
+Each line: {"part", "case", "ms", "tflops", "frac", "peak"}; frac is against the
+measured dense bf16 burst peak of this GPU pool (MEASURED_PEAKS.json, else the pool's
+fallback figure). Times are CUDA events around `reps` back-to-back launches on the
+launching stream after 3 warm-up launches. Usage:
+    python -m da3cpplib_b200.microbench [--part A|B|attn|all] [--m 87680] [--reps 20]
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+M_SET = (1370, 8 * 1370, 64 * 1370)
+KN_SET = ((384, 1152), (768, 3072), (1024, 4096), (4096, 1024), (1536, 6144))
+CONV_C = (64, 128, 256)
+CONV_HW = (37, 74, 148, 296)
+
+
+def peak_tflops():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
+
+
+def q8_0_weights(torch, N, K, gen):
+    """GGUF Q8_0 bytes [N][K/32][34] on the device: f16 d then 32 int8."""
+    nb = K // 32
+    q = torch.randint(-127, 128, (N, nb, 32), generator=gen, device="cuda", dtype=torch.int8)
+    d = (torch.rand((N, nb), generator=gen, device="cuda") * 9e-3 + 1e-3).half()
+    raw = torch.empty((N, nb, 34), dtype=torch.uint8, device="cuda")
+    raw[:, :, :2] = d.view(torch.uint8).view(N, nb, 2)
+    raw[:, :, 2:] = q.view(torch.uint8)
+    return raw
+
+
+def main(argv=None):
+    import torch
+
+    from . import _lib
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--part", default="all", choices=["A", "B", "attn", "all"])
+    ap.add_argument("--m", type=int, default=0, help="Part A: only this M")
+    ap.add_argument("--kn", default="", help="Part A: only this K,N (e.g. 1024,4096)")
+    ap.add_argument("--act", type=int, default=0, help="Part A activation: 0 none, 2 erf-GELU")
+    ap.add_argument("--c", type=int, default=0, help="Part B: only this channel count")
+    ap.add_argument("--hw", type=int, default=0, help="Part B: only this spatial size")
+    ap.add_argument("--reps", type=int, default=20)
+    args = ap.parse_args(argv)
+
+    L = _lib.load()
+    V = ctypes.c_void_p
+    P = lambda t: V(t.data_ptr())
+    s = torch.cuda.current_stream()
+    S = V(s.cuda_stream)
+    peak, src = peak_tflops()
+    gen = torch.Generator(device="cuda").manual_seed(20260101)
+
+    def timeit(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        for _ in range(args.reps):
+            fn()
+        b.record(s)
+        torch.cuda.synchronize()
+        if L.da3b_device_status() != 0:
+            raise RuntimeError("device status set")
+        return a.elapsed_time(b) / args.reps
+
+    def emit(part, case, ms, flops, extra=None):
+        tf = flops / (ms / 1e3) / 1e12
+        line = {"part": part, "case": case, "ms": round(ms, 4), "tflops": round(tf, 1),
+                "frac": round(tf / peak, 4), "peak": f"{peak} TFLOP/s ({src})"}
+        if extra:
+            line.update(extra)
+        print(json.dumps(line), flush=True)
+
+    if args.part in ("A", "all"):
+        kns = KN_SET if not args.kn else (tuple(int(v) for v in args.kn.split(",")),)
+        ms_set = M_SET if not args.m else (args.m,)
+        for K, N in kns:
+            raw = q8_0_weights(torch, N, K, gen)
+            W = torch.empty((N, K), dtype=torch.float16, device="cuda")
+            dq_ms = timeit(lambda: L.da3b_dequant_q8_0(P(raw), N, K, P(W), K, S))
+            bias = torch.randn(N, generator=gen, device="cuda")
+            for M in ms_set:
+                x = torch.randn((M, K), generator=gen, device="cuda").half()
+                y = torch.empty((M, N), dtype=torch.float16, device="cuda")
+
+                def run():
+                    rc = L.da3b_linear_f16(P(x), M, K, K, P(W), N, K, P(bias), args.act, P(y), N, S)
+                    if rc:
+                        raise RuntimeError(f"da3b_linear_f16 rc={rc}")
+
+                ms = timeit(run)
+                emit("A", f"M={M} K={K} N={N} act={args.act}", ms, 2.0 * M * K * N,
+                     {"dequant_ms_load_time": round(dq_ms, 4),
+                      "l2": "inputs exceed L2" if (M * K + M * N) * 2 > 126e6 else "inputs fit in L2"})
+                del x, y
+            del raw, W
+
+    if args.part in ("B", "all"):
+        for C in (CONV_C if not args.c else (args.c,)):
+            w = torch.randn((C, C, 3, 3), generator=gen, device="cuda") * 0.02
+            icp = (C + 63) // 64 * 64
+            wp = torch.empty((C, 9, icp), dtype=torch.float16, device="cuda")
+            assert L.da3b_pack_conv_weight(P(w), C, C, 3, P(wp), S) == 0
+            b = torch.randn(C, generator=gen, device="cuda")
+            for hw in (CONV_HW if not args.hw else (args.hw,)):
+                B = 8
+                x = torch.randn((B, hw, hw, C), generator=gen, device="cuda").half()
+                o = torch.empty((B, hw, hw, C), dtype=torch.float16, device="cuda")
+
+                def run():
+                    rc = L.da3b_conv_nhwc(P(x), B, hw, hw, C, P(wp), C, 3, P(b), None, None, 0, P(o), None, S)
+                    if rc:
+                        raise RuntimeError(f"da3b_conv_nhwc rc={rc}")
+
+                ms = timeit(run)
+                emit("B", f"B=8 {hw}x{hw} C={C}", ms, 2.0 * B * hw * hw * C * C * 9)
+                del x, o
+
+    if args.part in ("attn", "all"):
+        for nseq, seqlen, heads, tag in ((64, 1370, 16, "C3 per-image"), (2, 8 * 1297, 16, "C4 global, 2 scenes")):
+            D = heads * 64
+            qkv = torch.randn((nseq * seqlen, 3 * D), generator=gen, device="cuda").half()
+            out = torch.empty((nseq * seqlen, D), dtype=torch.float16, device="cuda")
+
+            def run():
+                rc = L.da3b_attention(P(qkv), nseq, seqlen, heads, P(out), S)
+                if rc:
+                    raise RuntimeError(f"da3b_attention rc={rc}")
+
+            ms = timeit(run)
+            emit("attn", f"{tag}: nseq={nseq} seqlen={seqlen} heads={heads}", ms, 4.0 * nseq * seqlen * seqlen * D)
+            del qkv, out
+
+
+if __name__ == "__main__":
+    main()

@@ -1065,6 +1065,48 @@ OR_API int or_preprocess(void* p, const uint8_t* rgb, int w, int hgt, int legacy
   return 0;
 }
 
+// Model-free entry points for the preprocessing pins: the same preprocess with the
+// policy given explicitly, the two uint8 resizers (mode 0 cubic, 1 area), and the raw
+// UV embedding in the reference's [ph][pw][C] order (src/uv_posembed.hpp:4-7).
+OR_API int or_preprocess_cfg(const uint8_t* rgb, int w, int hgt, int patch, int target, int upper, const float* mean,
+                             const float* std_, int legacy, float* out, int64_t cap, int* H, int* W) {
+  or_config c{};
+  c.patch_size = patch;
+  c.resize_target = target;
+  c.resize_upper = upper;
+  for (int i = 0; i < 3; ++i) {
+    c.img_mean[i] = mean[i];
+    c.img_std[i] = std_[i];
+  }
+  Img img;
+  img.w = w;
+  img.h = hgt;
+  img.rgb.assign(rgb, rgb + static_cast<size_t>(w) * hgt * 3);
+  std::vector<float> chw;
+  if (!preprocess(img, c, legacy != 0, chw, *H, *W)) return -1;
+  if (static_cast<int64_t>(chw.size()) > cap) return -2;
+  memcpy(out, chw.data(), chw.size() * 4);
+  return 0;
+}
+
+OR_API int or_resize(const uint8_t* rgb, int w, int hgt, int dw, int dh, int mode, uint8_t* out) {
+  Img img;
+  img.w = w;
+  img.h = hgt;
+  img.rgb.assign(rgb, rgb + static_cast<size_t>(w) * hgt * 3);
+  const Img r = mode == 0 ? resize_cubic(img, dw, dh) : resize_area(img, dw, dh);
+  memcpy(out, r.rgb.data(), r.rgb.size());
+  return 0;
+}
+
+OR_API int or_uv_pos_embed(int pw, int ph, int C, float aspect, float* out) {
+  const Oracle::Map m = Oracle::uv_embed(pw, ph, C, aspect, 1.0f);
+  const size_t hw = static_cast<size_t>(pw) * ph;
+  for (int ch = 0; ch < C; ++ch)
+    for (size_t p = 0; p < hw; ++p) out[p * C + ch] = m.v[ch * hw + p];
+  return 0;
+}
+
 // Single image: RGB8 HWC -> depth (+conf) at the processed size.
 // DA2 route: preprocess_real -> forward -> depth_relative (src/engine.cpp:121-130,
 // src/dpt_head.cpp:402-439); DA3 route: preprocess_real -> fused feats -> head ->

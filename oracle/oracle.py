@@ -22,6 +22,56 @@ CXXFLAGS = ["-O3", "-march=x86-64-v3", "-ffp-contract=off", "-fopenmp", "-fPIC",
             "-fvisibility=hidden"]
 
 
+REF_SRC_DIR = os.environ.get("DA3_REFERENCE_SRC", "/root/reference/src")
+REF_DIR = os.path.join(HERE, "_ref")
+REF_LIB = os.path.join(REF_DIR, "libda3ref.so")
+# DA3cpplib's own host-only sources on the path, compiled unmodified (never copied).
+REF_SOURCES = ["preprocess.cpp", "uv_posembed.cpp"]
+
+
+def build_ref(force: bool = False):
+    """Compile the reference's preprocess.cpp + uv_posembed.cpp with ref_wrap.cpp into
+    oracle/_ref/libda3ref.so. Returns the library path, or None when the reference
+    checkout is absent (the prebuilt library, if shipped, is still used)."""
+    srcs = [os.path.join(REF_SRC_DIR, f) for f in REF_SOURCES]
+    if not all(os.path.exists(s) for s in srcs):
+        return REF_LIB if os.path.exists(REF_LIB) else None
+    wrap = os.path.join(HERE, "ref_wrap.cpp")
+    newest = max(os.path.getmtime(s) for s in srcs + [wrap])
+    if force or not os.path.exists(REF_LIB) or os.path.getmtime(REF_LIB) < newest:
+        os.makedirs(REF_DIR, exist_ok=True)
+        # x86-64 baseline ISA: no FMA, so no contraction; the reference's Release flags
+        # (-O3, C++17) otherwise.
+        cmd = (["g++", "-O3", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden",
+                "-I", os.path.join(HERE, "ref_shim"), "-I", REF_SRC_DIR] + srcs + [wrap, "-o", REF_LIB + ".tmp"])
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"reference build failed:\n{r.stderr}")
+        os.replace(REF_LIB + ".tmp", REF_LIB)
+    return REF_LIB
+
+
+_ref = None
+
+
+def ref_lib():
+    """ctypes handle of oracle/_ref/libda3ref.so, or None when it is unavailable."""
+    global _ref
+    if _ref is None:
+        path = build_ref()
+        if path is None:
+            return None
+        R = ctypes.CDLL(path)
+        R.ref_preprocess.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                     ctypes.c_int64, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                                     ctypes.c_void_p, ctypes.c_int64]
+        R.ref_resize.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 5 + [ctypes.c_void_p]
+        R.ref_uv_pos_embed.argtypes = [ctypes.c_int] * 3 + [ctypes.c_float, ctypes.c_void_p]
+        _ref = R
+    return _ref
+
+
 def build(force: bool = False) -> str:
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < os.path.getmtime(SRC):
         cmd = ["g++"] + CXXFLAGS + [SRC, "-o", LIB + ".tmp"]
@@ -68,6 +118,11 @@ def lib():
         L.or_infer.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.or_infer_mv.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
                                   ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.or_preprocess_cfg.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                        ctypes.c_int64, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]
+        L.or_resize.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 5 + [ctypes.c_void_p]
+        L.or_uv_pos_embed.argtypes = [ctypes.c_int] * 3 + [ctypes.c_float, ctypes.c_void_p]
         L.or_get.restype = ctypes.c_int64
         L.or_get.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.POINTER(ctypes.c_float))]
         L.or_dims.argtypes = [ctypes.c_void_p] + [ctypes.POINTER(ctypes.c_int)] * 6
@@ -231,4 +286,73 @@ def quantize_q8_0(x: np.ndarray) -> np.ndarray:
     x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
     out = np.zeros(x.size // 32 * 34, dtype=np.uint8)
     lib().or_quantize_q8_0(x.ctypes.data, x.size, out.ctypes.data)
+    return out
+
+
+# ---------------------------------------------------------------- preprocessing pins
+IMAGENET_MEAN = (0.485, 0.456, 0.406)
+IMAGENET_STD = (0.229, 0.224, 0.225)
+
+
+def _policy_args(mean, std):
+    m = np.ascontiguousarray(mean, dtype=np.float32)
+    s = np.ascontiguousarray(std, dtype=np.float32)
+    return m, s
+
+
+def preprocess_cfg(rgb, patch=14, target=504, upper=True, legacy=False, mean=IMAGENET_MEAN, std=IMAGENET_STD,
+                   impl="oracle"):
+    """preprocess_real / legacy preprocess with an explicit policy -> CHW f32.
+    impl="oracle" runs the restatement, impl="ref" the reference's own preprocess.cpp."""
+    rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+    h, w = rgb.shape[:2]
+    m, s = _policy_args(mean, std)
+    big = int(max(h, w) * max(1.0, target / min(h, w))) + 2 * patch + 2
+    cap = 3 * big * big
+    out = np.zeros(cap, dtype=np.float32)
+    H, W = ctypes.c_int(), ctypes.c_int()
+    if impl == "ref":
+        R = ref_lib()
+        if R is None:
+            raise RuntimeError("oracle/_ref is not built")
+        rc = R.ref_preprocess(rgb.ctypes.data, w, h, patch, target, int(upper), m.ctypes.data, s.ctypes.data,
+                              int(legacy), out.ctypes.data, cap, ctypes.byref(H), ctypes.byref(W), None, 0)
+    else:
+        rc = lib().or_preprocess_cfg(rgb.ctypes.data, w, h, patch, target, int(upper), m.ctypes.data, s.ctypes.data,
+                                     int(legacy), out.ctypes.data, cap, ctypes.byref(H), ctypes.byref(W))
+    if rc != 0:
+        raise RuntimeError(f"preprocess failed ({impl}): {rc}")
+    return out[: 3 * H.value * W.value].reshape(3, H.value, W.value).copy()
+
+
+def resize_u8(rgb, dw, dh, mode, impl="oracle"):
+    """uint8 HWC resize: mode "cubic" or "area"."""
+    rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+    h, w = rgb.shape[:2]
+    out = np.zeros((dh, dw, 3), dtype=np.uint8)
+    md = {"cubic": 0, "area": 1}[mode]
+    if impl == "ref":
+        R = ref_lib()
+        if R is None:
+            raise RuntimeError("oracle/_ref is not built")
+        rc = R.ref_resize(rgb.ctypes.data, w, h, dw, dh, md, out.ctypes.data)
+    else:
+        rc = lib().or_resize(rgb.ctypes.data, w, h, dw, dh, md, out.ctypes.data)
+    if rc != 0:
+        raise RuntimeError(f"resize failed ({impl}): {rc}")
+    return out
+
+
+def uv_pos_embed(pw, ph, C, aspect, impl="oracle"):
+    """Raw UV embedding, [ph][pw][C]."""
+    out = np.zeros((ph, pw, C), dtype=np.float32)
+    if impl == "ref":
+        R = ref_lib()
+        if R is None:
+            raise RuntimeError("oracle/_ref is not built")
+        rc = R.ref_uv_pos_embed(pw, ph, C, aspect, out.ctypes.data)
+    else:
+        rc = lib().or_uv_pos_embed(pw, ph, C, aspect, out.ctypes.data)
+    if rc != 0:
+        raise RuntimeError(f"uv_pos_embed failed ({impl}): {rc}")
     return out

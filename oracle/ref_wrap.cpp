@@ -1,0 +1,76 @@
+// C ABI over DA3cpplib's own host-only sources, compiled unmodified from the reference
+// checkout into oracle/_ref/ — test infrastructure only, never part of libda3b.
+//
+// Only src/preprocess.cpp (the real/legacy preprocess and the uint8 cubic/area
+// resizers) and src/uv_posembed.cpp are compiled: they need nothing from ggml beyond
+// the opaque type names that model_loader.hpp mentions (oracle/ref_shim/). Everything
+// else on the depth path goes through ggml graphs, whose source is absent from the
+// reference checkout, so it cannot be built here.
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "preprocess.hpp"
+#include "uv_posembed.hpp"
+
+#define REF_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+da::Config make_cfg(int patch, int target, int upper, const float* mean, const float* std_) {
+  da::Config c;
+  c.patch_size = static_cast<uint32_t>(patch);
+  c.img_resize_target = static_cast<uint32_t>(target);
+  c.img_resize_mode = upper ? "upper_bound" : "lower_bound";
+  c.img_mean.assign(mean, mean + 3);
+  c.img_std.assign(std_, std_ + 3);
+  return c;
+}
+da::Image make_img(const uint8_t* rgb, int w, int h) {
+  da::Image im;
+  im.w = w;
+  im.h = h;
+  im.rgb.assign(rgb, rgb + static_cast<size_t>(w) * h * 3);
+  return im;
+}
+}  // namespace
+
+// preprocess_real (legacy = 0) or preprocess (legacy = 1). Writes at most cap floats of
+// CHW output and, when rgb_out is non-null (real path only), the resized uint8 HWC
+// image (cap_rgb bytes at most). Returns 0 on success, -1 when the reference returns
+// false, -2 when an output buffer is too small.
+REF_API int ref_preprocess(const uint8_t* rgb, int w, int h, int patch, int target, int upper, const float* mean,
+                           const float* std_, int legacy, float* chw, int64_t cap, int* H, int* W, uint8_t* rgb_out,
+                           int64_t cap_rgb) {
+  const da::Config c = make_cfg(patch, target, upper, mean, std_);
+  const da::Image im = make_img(rgb, w, h);
+  da::Preprocessed p;
+  std::vector<uint8_t> u8;
+  const bool ok = legacy ? da::preprocess(im, c, p) : da::preprocess_real(im, c, p, rgb_out ? &u8 : nullptr);
+  if (!ok) return -1;
+  *H = p.H;
+  *W = p.W;
+  if (static_cast<int64_t>(p.chw.size()) > cap) return -2;
+  std::memcpy(chw, p.chw.data(), p.chw.size() * sizeof(float));
+  if (rgb_out && !legacy) {
+    if (static_cast<int64_t>(u8.size()) > cap_rgb) return -2;
+    std::memcpy(rgb_out, u8.data(), u8.size());
+  }
+  return 0;
+}
+
+// resize_cubic (mode 0) / resize_area (mode 1) of a uint8 HWC RGB image.
+REF_API int ref_resize(const uint8_t* rgb, int w, int h, int dw, int dh, int mode, uint8_t* out) {
+  const da::Image im = make_img(rgb, w, h);
+  const da::Image r = mode == 0 ? da::resize_cubic(im, dw, dh) : da::resize_area(im, dw, dh);
+  if (r.w != dw || r.h != dh) return -1;
+  std::memcpy(out, r.rgb.data(), r.rgb.size());
+  return 0;
+}
+
+// uv_pos_embed: [ph][pw][C] row-major, raw (not multiplied by the 0.1 ratio).
+REF_API int ref_uv_pos_embed(int pw, int ph, int C, float aspect, float* out) {
+  const std::vector<float> v = da::uv_pos_embed(pw, ph, C, aspect);
+  if (v.size() != static_cast<size_t>(pw) * ph * C) return -1;
+  std::memcpy(out, v.data(), v.size() * sizeof(float));
+  return 0;
+}

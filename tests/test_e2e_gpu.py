@@ -201,3 +201,31 @@ def test_graph_replay_matches_eager(cuda):
     for x in (b, c, d):
         assert np.array_equal(a["depth"], x["depth"]) and np.array_equal(a["conf"], x["conf"])
     assert m.launches(1, 112, 112) > 0
+
+
+@pytest.mark.parametrize("tag", ["sq", "rect"])
+def test_da2_matches_transformers(cuda, tag):
+    """libda3b on the DA2 model built with transformers (f32 weights in the GGUF,
+    tests/golden/make_golden.py) against transformers' own f32 outputs: out-layer
+    features normalised max error <= 1e-2, logits and depth median relative error
+    <= 1e-2 (f16 weights and activations against f32)."""
+    import os
+
+    from da3cpplib_b200 import Model
+
+    gold = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    z = np.load(os.path.join(gold, "da2_hf_tiny.npz"))
+    m = Model(os.path.join(gold, "da2_hf_tiny.gguf"), 0)
+    img = z[tag + "_img"]
+    out = m.infer(img)
+    for i in range(4):
+        ref = z[f"{tag}_feat{i}"]
+        got = m.feature(i)
+        assert got.shape == ref.shape
+        assert nmax(got, ref) <= 1e-2, f"feature {i}: {nmax(got, ref)}"
+    m.set_raw_logits(True)
+    lg = m.infer(img)["depth"][0]
+    m.set_raw_logits(False)
+    assert median_rel(lg, z[tag + "_logits"]) <= 1e-2
+    assert nmax(lg, z[tag + "_logits"]) <= 3e-2
+    assert median_rel(out["depth"][0], z[tag + "_depth"]) <= 1e-2

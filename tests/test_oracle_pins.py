@@ -1,0 +1,113 @@
+"""Pins of the CPU oracle (CPU only).
+
+* Preprocessing and the UV embedding against DA3cpplib's own src/preprocess.cpp and
+  src/uv_posembed.cpp: bit-exact against the committed fixtures generated from
+  oracle/_ref (tests/golden/make_golden.py), and against oracle/_ref live on seeded
+  random cases when that library is present.
+* The Q8_0 quantiser against gguf-py's (bit-exact with ggml's C reference quantiser).
+* The whole DA2 path (patch embed, offset pos-embed interpolation, ViT blocks, attention,
+  out-layer LayerNorm, DPT head, ReLU) against transformers' DepthAnythingForDepthEstimation
+  with the same f32 weights: |diff| <= 1e-4 * max|ref| (f32 summation-order noise).
+"""
+import os
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLD = os.path.join(HERE, "golden")
+
+
+@pytest.fixture(scope="module")
+def orc():
+    from oracle import oracle
+
+    return oracle
+
+
+@pytest.fixture(scope="module")
+def pre():
+    return np.load(os.path.join(GOLD, "preprocess_ref.npz"))
+
+
+def _cases(z, prefix):
+    return sorted({k.split("_")[0] for k in z.files if k.startswith(prefix)})
+
+
+def test_preprocess_matches_reference_fixture(orc, pre):
+    cases = _cases(pre, "pre")
+    assert len(cases) >= 8
+    for c in cases:
+        patch, target, upper, legacy = (int(v) for v in pre[c + "_cfg"])
+        got = orc.preprocess_cfg(pre[c + "_in"], patch, target, bool(upper), bool(legacy))
+        ref = pre[c + "_out"]
+        assert got.shape == ref.shape, c
+        np.testing.assert_array_equal(got, ref, err_msg=c)
+
+
+def test_resize_matches_reference_fixture(orc, pre):
+    for c in _cases(pre, "rs"):
+        dw, dh, mode = (int(v) for v in pre[c + "_cfg"])
+        got = orc.resize_u8(pre[c + "_in"], dw, dh, "cubic" if mode == 0 else "area")
+        np.testing.assert_array_equal(got, pre[c + "_out"], err_msg=c)
+
+
+def test_uv_pos_embed_matches_reference_fixture(orc, pre):
+    for c in _cases(pre, "uv"):
+        pw, ph, C, aspect = pre[c + "_cfg"]
+        got = orc.uv_pos_embed(int(pw), int(ph), int(C), float(aspect))
+        np.testing.assert_allclose(got, pre[c + "_out"], rtol=0, atol=1e-7, err_msg=c)
+
+
+def test_preprocess_matches_reference_live(orc):
+    """Seeded random sizes and policies, oracle vs. the reference's compiled
+    preprocess.cpp (oracle/_ref), bit-exact."""
+    if orc.ref_lib() is None:
+        pytest.skip("oracle/_ref not available (no DA3cpplib checkout and no prebuilt library)")
+    rng = np.random.default_rng(7)
+    for i in range(40):
+        h, w = (int(v) for v in rng.integers(1, 160, size=2))
+        target = int(rng.choice([14, 28, 56, 98, 140, 518]))
+        upper, legacy = bool(rng.integers(0, 2)), bool(i % 7 == 0)
+        img = rng.integers(0, 256, size=(h, w, 3), dtype=np.uint8)
+        a = orc.preprocess_cfg(img, 14, target, upper, legacy)
+        b = orc.preprocess_cfg(img, 14, target, upper, legacy, impl="ref")
+        np.testing.assert_array_equal(a, b, err_msg=f"{h}x{w} target {target} upper {upper} legacy {legacy}")
+    for i in range(20):
+        h, w, dh, dw = (int(v) for v in rng.integers(1, 90, size=4))
+        img = rng.integers(0, 256, size=(h, w, 3), dtype=np.uint8)
+        for mode in ("cubic", "area"):
+            np.testing.assert_array_equal(orc.resize_u8(img, dw, dh, mode), orc.resize_u8(img, dw, dh, mode, "ref"))
+
+
+def test_q8_0_matches_ggufpy(orc):
+    z = np.load(os.path.join(GOLD, "q8_0_ggufpy.npz"))
+    got = orc.quantize_q8_0(z["x"])
+    np.testing.assert_array_equal(got, z["q"])
+
+
+def test_q8_0_matches_ggufpy_live(orc):
+    gguf = pytest.importorskip("gguf")
+    from gguf import quants
+
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((16, 512)) * rng.uniform(1e-3, 50, size=(16, 1))).astype(np.float32)
+    ref = np.ascontiguousarray(quants.quantize(x, gguf.GGMLQuantizationType.Q8_0)).reshape(-1)
+    np.testing.assert_array_equal(orc.quantize_q8_0(x), ref)
+
+
+@pytest.mark.parametrize("tag", ["sq", "rect"])
+def test_da2_matches_transformers(orc, tag):
+    z = np.load(os.path.join(GOLD, "da2_hf_tiny.npz"))
+    o = orc.Oracle(os.path.join(GOLD, "da2_hf_tiny.gguf"), act_quant=False, n_threads=4)
+    r = o.infer(z[tag + "_img"], legacy=True)
+    for i in range(4):
+        ref = z[f"{tag}_feat{i}"]
+        got = o.get(f"feat{i}").reshape(ref.shape)
+        assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max(), f"feature {i}"
+    ref = z[tag + "_logits"]
+    assert r["logits"].shape == (1,) + ref.shape
+    assert np.abs(r["logits"][0] - ref).max() <= 1e-4 * np.abs(ref).max()
+    ref = z[tag + "_depth"]
+    assert np.abs(r["depth"] - ref).max() <= 1e-4 * np.abs(ref).max()
+    assert (ref > 0).mean() > 0.3  # a live (not all-ReLU-zero) output
