@@ -286,8 +286,15 @@ def run_gpu(args):
     gemm_ms = e0.elapsed_time(e1) / reps
     flops = 2.0 * M * K * N
     achieved = flops / (gemm_ms / 1e3) / 1e12
+    # DRAM read+write of one fc1 launch from an ncu capture of the same kernel at
+    # M = 21920 (profiles/gemm_fc1_m21920_k1024_n4096_gelu.txt: 53.57 MB read +
+    # 123.73 MB written), scaled by M to this launch (traffic grows with M; the 8.4 MB
+    # weight is the only fixed part)
+    traffic = int(round((53.567488e6 + 123.73248e6) * M / 21920))
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": tflops, "unit": "TFLOP/s",
-                "frac": round(achieved / tflops, 4), "traffic": None,
+                "frac": round(achieved / tflops, 4), "traffic": traffic,
+                "traffic_note": "bytes per launch, ncu dram__bytes_read+write at M=21920 scaled by M",
+                "algorithmic_bytes": int(2 * (M * K + K * N + M * N)),
                 "kernel": f"k_tc_gemm<256> fc1 M={M} K={K} N={N} (+bias, erf-GELU), {src} bf16 dense peak",
                 "ms_per_launch": round(gemm_ms, 4)}
 
