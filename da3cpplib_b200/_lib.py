@@ -29,6 +29,7 @@ SIGNATURES = {
     "da3b_linear_resid_f32": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p,
                                       c_void_p, c_int, c_void_p]),
     "da3b_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "da3b_attention_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "da3b_pack_conv_weight": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "da3b_conv_nhwc": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p,
                                c_void_p, c_int, c_void_p, c_void_p, c_void_p]),

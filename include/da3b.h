@@ -66,6 +66,37 @@ DA3B_API int da3b_linear_resid_f32(const void* x, int M, int K, int lda, const v
  * the layout of the QKV linear's output), out: f16 [nseq*seqlen][heads*64]. */
 DA3B_API int da3b_attention(const void* qkv, int nseq, int seqlen, int heads, void* out, void* stream);
 
+/* Capacity of the fixed V^T scratch of da3b_attention_noalloc, in bytes (32 MiB):
+ * nseq * heads*64 * round_up(seqlen, 8) * 2 must not exceed it, e.g. 11 ViT-L images
+ * of 1370 tokens, or one 8-view scene of 1297 tokens per view at 16 heads. */
+#define DA3B_NOALLOC_VT_BYTES (32u << 20)
+/* Returned by da3b_attention_noalloc when a call needs more than DA3B_NOALLOC_VT_BYTES
+ * of scratch; nothing is launched. Split the batch (fewer sequences per call). */
+#define DA3B_ERR_NOALLOC_TOO_LARGE (-103)
+
+/* da3b_attention without any device allocation by the library. It has no counterpart
+ * in the reference (DA3cpplib's attention runs inside a ggml graph whose allocator
+ * owns all memory); it exists for callers that cannot let a library allocate device
+ * memory on their call path, for example a host under a fixed device-memory budget
+ * or with its own allocator owning the device, or a latency-critical loop that cannot
+ * take cudaMalloc's implicit device synchronisation on a first or larger call.
+ * Same inputs, outputs and arithmetic as da3b_attention (bit-identical results); the
+ * differences:
+ *  - the V^T scratch is a fixed file-scope device array of DA3B_NOALLOC_VT_BYTES per
+ *    device, created with the library's module; larger calls are rejected with
+ *    DA3B_ERR_NOALLOC_TOO_LARGE before anything is launched;
+ *  - the first call on each device resolves that array's address
+ *    (cudaGetSymbolAddress); make that first call before capturing the stream;
+ *  - the caller owns the status word: status_dev points to a device int that must
+ *    start at zero and that a timed-out wait inside the kernel sets non-zero (the
+ *    library never clears it); the scratch itself needs no initial value;
+ *  - there is ONE scratch per device: calls that overlap in time on the same device
+ *    (different streams, or threads without ordering) race on it and corrupt each
+ *    other's results. Order them on one stream, or synchronise between them.
+ * Returns 0 when launched, a negative code otherwise. */
+DA3B_API int da3b_attention_noalloc(const void* qkv, int nseq, int seqlen, int heads, void* out, int* status_dev,
+                                    void* stream);
+
 /* Packs a ggml conv2d weight (ne [KW,KH,IC,OC] f32 == torch [OC][IC][KH][KW]) into
  * the implicit-GEMM layout f16 [OC][KH*KW][icp], icp = IC rounded up to 64. */
 DA3B_API int da3b_pack_conv_weight(const float* w_f32, int OC, int IC, int ksize, void* w_packed, void* stream);
