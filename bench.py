@@ -253,8 +253,9 @@ def run_gpu(args):
     step(rgb_host.data_ptr(), depth_host.data_ptr())
     torch.cuda.synchronize()
     ms_e2e = timed(rgb_host.data_ptr(), depth_host.data_ptr())
-    e2e = {"value": IMAGES_TOTAL / (ms_e2e / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(imgs.nbytes),
-           "d2h_bytes_per_step": int(per * H * W * 4)}
+    # whole-job bytes per step (every rank copies its own shard in and out)
+    e2e = {"value": IMAGES_TOTAL / (ms_e2e / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(IMAGES_TOTAL * H * W * 3),
+           "d2h_bytes_per_step": int(IMAGES_TOTAL * H * W * 4)}
     # sanity: the host result equals the device-resident result
     if not torch.equal(depth_host, depth_dev.cpu()):
         raise RuntimeError("e2e and device-resident outputs differ")
