@@ -54,6 +54,27 @@ __device__ __forceinline__ float erf_as(float z) {
 // Exact-form GELU 0.5 x (1 + erf(x / sqrt 2)) (ggml_gelu_erf, src/ggml_extend.hpp:22-25).
 __device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erf_as(v * 0.70710678118654752f)); }
 
+// gelu_erf of two values with packed f32x2 arithmetic (sm_100): the same operations in
+// the same order as gelu_erf, so each result is bit-identical to the scalar one, in
+// about half the instructions.
+__device__ __forceinline__ float2 f2c(float c) { return make_float2(c, c); }
+__device__ __forceinline__ float2 gelu_erf2(float2 v) {
+  const float2 z = __fmul2_rn(v, f2c(0.70710678118654752f));
+  const float2 az = make_float2(fabsf(z.x), fabsf(z.y));
+  const float2 d = __ffma2_rn(f2c(0.3275911f), az, f2c(1.0f));
+  const float2 t = make_float2(__fdividef(1.0f, d.x), __fdividef(1.0f, d.y));
+  float2 y = __ffma2_rn(f2c(1.061405429f), t, f2c(-1.453152027f));
+  y = __ffma2_rn(y, t, f2c(1.421413741f));
+  y = __ffma2_rn(y, t, f2c(-0.284496736f));
+  y = __ffma2_rn(y, t, f2c(0.254829592f));
+  y = __fmul2_rn(y, t);
+  const float2 w = __fmul2_rn(__fmul2_rn(make_float2(-az.x, -az.y), az), f2c(1.4426950408889634f));
+  const float2 ex = make_float2(ex2_approx(w.x), ex2_approx(w.y));
+  float2 r = __ffma2_rn(make_float2(-y.x, -y.y), ex, f2c(1.0f));
+  r = make_float2(copysignf(r.x, z.x), copysignf(r.y, z.y));
+  return __fmul2_rn(__fmul2_rn(f2c(0.5f), v), __fadd2_rn(f2c(1.0f), r));
+}
+
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == kActRelu) return fmaxf(v, 0.0f);
   if (act == kActGelu) return gelu_erf(v);
@@ -455,6 +476,123 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 
+// Transposed epilogue of one warp: its 32 accumulator rows (TMEM lanes; `row` is
+// this lane's output row or -1) x columns [c_begin, c_end) of the tile at column n_tile.
+// Each 32x32 f32 chunk is written row-per-lane into the warp's staging buffer (16-byte
+// pieces XOR-swizzled by row & 7: conflict-free both ways) and read back so that lane
+// l holds columns 8*(l&3) .. +7 of row 8k + (l>>2), k = 0..3. All per-element work then
+// runs in that layout, and each global store instruction covers 8 rows x 64 contiguous
+// bytes. kEpiF16: bias, res1/res2, out_relu, activation; kEpiQKV: bias, q|k thirds
+// stored the same way, the v third transposed per (sequence, head) into vt.
+// bsm: this warp's bias slice [c_end - c_begin] in shared memory (zeros without bias).
+template <int BN>
+__device__ __forceinline__ void epi_transposed(const GemmGeom& g, const EpiArgs& e, uint32_t tbase, int c_begin,
+                                               int c_end, int n_tile, int row, int lane, float* stg,
+                                               const float* bsm) {
+  const int s = lane & 3, rsub = lane >> 2;
+  const int orow = (row >= 0 && e.kind == kEpiF16) ? remap_row(e, row) : row;
+#pragma unroll 1
+  for (int c = c_begin; c < c_end; c += 32) {
+    uint32_t raw[32];
+    tmem_ld32(tbase + c, raw);
+    tmem_wait_ld();
+    const int n_base = n_tile + c;
+    if (n_base >= g.N) continue;  // warp-uniform
+    if (e.kind == kEpiQKV && n_base >= 2 * e.vt_d) {
+      // v third: lanes are consecutive tokens, so each of the 32 columns is one
+      // contiguous run of the transposed row
+      if (row >= 0) {
+        const int seq = row / e.vt_seqlen, tok = row % e.vt_seqlen;
+        const int c0 = n_base - 2 * e.vt_d;
+        __half* dst = e.vt + (static_cast<size_t>(seq) * (e.vt_d / 64) * 64 + c0) * e.vt_ld + tok;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          dst[static_cast<size_t>(i) * e.vt_ld] = __float2half_rn(__uint_as_float(raw[i]) + bsm[c - c_begin + i]);
+      }
+      continue;
+    }
+    uint4* wrow = reinterpret_cast<uint4*>(stg + lane * 32);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      wrow[j ^ (lane & 7)] = make_uint4(raw[4 * j], raw[4 * j + 1], raw[4 * j + 2], raw[4 * j + 3]);
+    __syncwarp();
+    const int n = n_base + 8 * s;
+    const bool col_ok = n < g.N;
+    const float4 b0 = *reinterpret_cast<const float4*>(bsm + (c - c_begin) + 8 * s);
+    const float4 b1 = *reinterpret_cast<const float4*>(bsm + (c - c_begin) + 8 * s + 4);
+    // gather all four row groups first: 32 independent values per lane for the math
+    float t[4][8];
+    int rr[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int r = 8 * k + rsub;
+      rr[k] = __shfl_sync(0xffffffffu, orow, r);
+      const uint4* rrow = reinterpret_cast<const uint4*>(stg + r * 32);
+      const uint4 a = rrow[(2 * s) ^ (r & 7)], b = rrow[(2 * s + 1) ^ (r & 7)];
+      t[k][0] = __uint_as_float(a.x) + b0.x;
+      t[k][1] = __uint_as_float(a.y) + b0.y;
+      t[k][2] = __uint_as_float(a.z) + b0.z;
+      t[k][3] = __uint_as_float(a.w) + b0.w;
+      t[k][4] = __uint_as_float(b.x) + b1.x;
+      t[k][5] = __uint_as_float(b.y) + b1.y;
+      t[k][6] = __uint_as_float(b.z) + b1.z;
+      t[k][7] = __uint_as_float(b.w) + b1.w;
+    }
+    __syncwarp();  // every lane has read the staging buffer before the next chunk overwrites it
+    if (e.kind == kEpiF16) {
+      if (e.res1) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (rr[k] < 0 || !col_ok) continue;
+          const int r1 = e.res1_mod > 0 ? rr[k] % e.res1_mod : rr[k];
+          float a1[8];
+          load_h8(e.res1 + static_cast<size_t>(r1) * e.ld_res1 + n, a1);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) t[k][i] += a1[i];
+        }
+      }
+      if (e.res2) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (rr[k] < 0 || !col_ok) continue;
+          float a2[8];
+          load_h8(e.res2 + static_cast<size_t>(rr[k]) * e.ld_res2 + n, a2);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) t[k][i] += a2[i];
+        }
+      }
+      if (e.out_relu) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (rr[k] < 0 || !col_ok) continue;
+          float rl[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) rl[i] = fmaxf(t[k][i], 0.0f);
+          store_h8(e.out_relu + static_cast<size_t>(rr[k]) * e.ld_out + n, rl);
+        }
+      }
+      if (e.act == kActGelu) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) {
+            const float2 gv = gelu_erf2(make_float2(t[k][i], t[k][i + 1]));
+            t[k][i] = gv.x;
+            t[k][i + 1] = gv.y;
+          }
+      } else if (e.act == kActRelu) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) t[k][i] = fmaxf(t[k][i], 0.0f);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (rr[k] >= 0 && col_ok) store_h8(e.out + static_cast<size_t>(rr[k]) * e.ld_out + n, t[k]);
+  }
+}
+
 // ---------------------------------------------------------------- 2-SM variant
 // Same roles over a CTA pair (cluster of 2, cta_group::2): a tile is 256 rows x BN;
 // each CTA TMA-loads its own 128 rows of A and BN/2 rows of B (no multicast) and
@@ -473,7 +611,8 @@ struct Gemm2Cfg {
   static constexpr int kBBytes = (BN / 2) * 64 * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiBufBytes = 4096;
-  static constexpr int kEpiBytes = kStaged ? kEpiWarps * kEpiBufBytes : 0;
+  static constexpr int kBiasBytes = (BN / 2) * 4;  // one warp's bias slice (transposed epilogue)
+  static constexpr int kEpiBytes = kStaged ? kEpiWarps * (kEpiBufBytes + kBiasBytes) : 0;
   static constexpr int kStages = (196 * 1024 - kEpiBytes) / kStageBytes > 6 ? 6 : (196 * 1024 - kEpiBytes) / kStageBytes;
   static constexpr int kAccCols = (BN < 32) ? 32 : BN;
   static constexpr int kTmemCols = (2 * kAccCols <= 64) ? 64 : (2 * kAccCols <= 128 ? 128 : (2 * kAccCols <= 256 ? 256 : 512));
@@ -620,6 +759,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
     const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty[1]), 0);
     uint8_t* ebuf = sEpi + (warp - 2) * Cfg::kEpiBufBytes;
+    float* ebias = reinterpret_cast<float*>(sEpi + kEpiWarps * Cfg::kEpiBufBytes) + (warp - 2) * (BN / 2);
     int it = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++it) {
       const int acc = it & 1;
@@ -637,10 +777,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int m = mt * 128 + r;
         if (m < g.M) row = m;
       }
+      // transposed epilogue: this tile's bias slice is fetched before the accumulator
+      // wait, so its latency hides behind the MMA
+      float4 bq = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int bcol = nt * BN + c_begin + 4 * lane;
+      if (kStaged && e.tma_store == 3 && e.bias && 4 * lane < c_end - c_begin && bcol < g.N)
+        bq = __ldg(reinterpret_cast<const float4*>(e.bias + bcol));
       if (!mbar_wait_warp(&tfull[acc], acc_phase, status, kStatusTimeoutAccum)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
-      if (kStaged && e.tma_store == 1) {
+      if (kStaged && e.tma_store == 3) {
+        if (4 * lane < c_end - c_begin) *reinterpret_cast<float4*>(ebias + 4 * lane) = bq;
+        __syncwarp();
+        epi_transposed<BN>(g, e, tbase, c_begin, c_end, nt * BN, row, lane, reinterpret_cast<float*>(ebuf), ebias);
+      } else if (kStaged && e.tma_store == 1) {
         // f16 out: 64-column slices -> staging -> TMA store (rows / columns past the
         // tensor are clipped by the TMA unit)
 #pragma unroll 1
@@ -735,7 +885,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote(acc ? tempty_leader1 : tempty_leader0);
+      if (lane == 0) mbar_arrive_remote_relaxed(acc ? tempty_leader1 : tempty_leader0);
     }
     if (kStaged) {
       if (lane == 0) bulk_wait_all();  // every TMA store of this warp has completed
@@ -888,6 +1038,7 @@ static int gemm_launch2(int bn, const CUtensorMap& ta, const CUtensorMap& tb, co
                         const EpiArgs& e, int* status, cudaStream_t stream) {
   if (e.tma_store) {
     switch (bn) {
+      case 64: return launch_bn2<64, true>(ta, tb, tc, g, e, status, stream);
       case 128: return launch_bn2<128, true>(ta, tb, tc, g, e, status, stream);
       case 256: return launch_bn2<256, true>(ta, tb, tc, g, e, status, stream);
       default: return -12;
@@ -922,6 +1073,18 @@ static bool make_out_map(CUtensorMap* map, void* ptr, bool f32, int rows, int co
 }
 
 // The 2-SM kernel pays off once every CTA pair gets at least one 256-row tile.
+// Epilogue of the 2-SM kernel for f16 outputs: 0 (default) = transposed epilogue with
+// coalesced stores; 1 = the earlier selection (GELU via staged TMA store, others direct
+// per-row stores). DA3B_GEMM_EPI=1 selects the latter, for A/B timing.
+static int epi_mode_override() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("DA3B_GEMM_EPI");
+    v = (s && s[0] == '1') ? 1 : 0;
+  }
+  return v;
+}
+
 static bool want_2sm(const GemmGeom& g, int bn) {
   return use_2sm() && bn >= 64 && ((g.num_m_tiles + 1) / 2) * g.num_n_tiles >= num_sms() / 2;
 }
@@ -1006,12 +1169,15 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
   memset(&tc, 0, sizeof(tc));
   // Measured on B200 (C3 shapes): the staged TMA store wins for the GELU epilogue and
   // the TMA reduce-add for residual updates; plain f16 outputs are faster stored directly.
-  if (bn >= 128 && e.rm_div == 0) {
-    if (e.kind == kEpiF16 && e.act == kActGelu && !e.res1 && !e.res2 && !e.out_relu &&
-        make_out_map(&tc, e.out, false, M, N, e.ld_out))
+  const int epi_mode = epi_mode_override();
+  if ((e.kind == kEpiF16 && !e.q8) || e.kind == kEpiQKV) {
+    if (epi_mode != 1) e2.tma_store = 3;
+    else if (bn >= 128 && e.rm_div == 0 && e.kind == kEpiF16 && e.act == kActGelu && !e.res1 && !e.res2 &&
+             !e.out_relu && make_out_map(&tc, e.out, false, M, N, e.ld_out))
       e2.tma_store = 1;
-    else if (e.kind == kEpiResid && make_out_map(&tc, e.resid, true, M, N, e.ld_resid))
-      e2.tma_store = 2;
+  } else if (bn >= 128 && e.rm_div == 0 && e.kind == kEpiResid &&
+             make_out_map(&tc, e.resid, true, M, N, e.ld_resid)) {
+    e2.tma_store = 2;
   }
   return gemm_launch2(bn, ta, tb, tc, g, e2, status, stream);
 }
@@ -1069,7 +1235,7 @@ int conv_nhwc(const __half* X, int B, int H, int W, int IC, const __half* Wp, in
   if (!two) return gemm_launch(bn, ta, tb, g, e, status, stream, 0);
   memset(&tc, 0, sizeof(tc));
   EpiArgs e2 = e;
-  e2.tma_store = 0;
+  e2.tma_store = (e.kind == kEpiF16 && !e.q8 && epi_mode_override() != 1) ? 3 : 0;
   return gemm_launch2(bn, ta, tb, tc, g, e2, status, stream);
 }
 

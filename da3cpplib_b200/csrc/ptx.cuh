@@ -213,6 +213,12 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Relaxed form, for handing TMEM accumulator columns back to the MMA issuer: after
+// tcgen05.wait::ld the values are in registers, so nothing needs ordering before the
+// arrive, and the release form would also wait for every global store still in flight.
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 
 // 2-SM (cta_group::2) forms. Every tcgen05 instruction of a kernel uses one cta_group.
 __device__ __forceinline__ void tmem_alloc2(uint32_t* slot, uint32_t ncols) {
