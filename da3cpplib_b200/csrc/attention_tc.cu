@@ -14,7 +14,8 @@
 //              p = 2^(s*c - m*c) as f16 into one of two 128B-swizzled smem tiles. The
 //              max m is only raised when a tile's max exceeds it by more than 2^8; then
 //              O is rescaled in TMEM (once the previous P V landed). O / rowsum at the
-//              end. Keys past the sequence are masked; rows past it are not stored.
+//              end. P V completions alternate between two barriers by tile parity.
+//              Keys past the sequence are masked; rows past it are not stored.
 // Every wait is bounded (ptx.cuh); on a timeout the kernel records a status and exits.
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -59,8 +60,8 @@ __global__ void __launch_bounds__(192, 2)
   uint64_t* kv_empty = kv_full + kStagesKV;
   uint64_t* s_full = kv_empty + kStagesKV;  // [2]
   uint64_t* p_full = s_full + 2;            // [2] P_j written and S_j consumed
-  uint64_t* o_full = p_full + 2;            // one completion per P V product
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
+  uint64_t* o_full = p_full + 2;            // [2] P_j V_j done, j even / odd
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, h = blockIdx.y, sq = blockIdx.z;
@@ -86,8 +87,8 @@ __global__ void __launch_bounds__(192, 2)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 4);
+      mbar_init(&o_full[b], 1);
     }
-    mbar_init(o_full, 1);
     fence_mbar_init();
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
@@ -149,7 +150,7 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           umma_f16(tO, pdesc + 2 * kk, vdesc + 2 * kk, idO, (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(o_full);
+        umma_commit(&o_full[b]);
         umma_commit(&kv_empty[st]);
         if (j + 2 < nkt && !issue_s(j + 2)) break;
       }
@@ -185,9 +186,14 @@ __global__ void __launch_bounds__(192, 2)
         for (int i = 0; i < kKT; ++i)
           if (i >= kvalid) sv[i] = -INFINITY;
       }
-      float mt = sv[0];
+      // row max as a tree of 8 independent chains (not one 63-deep dependency chain)
+      float m8[8];
 #pragma unroll
-      for (int i = 1; i < kKT; ++i) mt = fmaxf(mt, sv[i]);
+      for (int i = 0; i < 8; ++i) m8[i] = sv[i];
+#pragma unroll
+      for (int i = 8; i < kKT; ++i) m8[i & 7] = fmaxf(m8[i & 7], sv[i]);
+      const float mt = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       // The running max of a row is raised only when a tile's max exceeds it by more
       // than 2^8; the accumulated O (and its row-sum column) is then rescaled in TMEM
       // once P V_{j-1} has landed. The TMEM read-modify-write is warp-collective, so the
@@ -195,7 +201,10 @@ __global__ void __launch_bounds__(192, 2)
       const bool need = (j > 0) && ((mt - m) * sl2 > kRescaleLog2);
       if (j == 0) m = mt;
       if (__any_sync(0xffffffffu, need)) {
-        if (!mbar_wait_warp(o_full, (j - 1) & 1, status, kStatusTimeoutAccum)) { ok = false; break; }
+        if (!mbar_wait_warp(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, status, kStatusTimeoutAccum)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const float alpha = need ? ex2_approx((m - mt) * sl2) : 1.0f;
         uint32_t ra[32], rb[32], rc;
@@ -224,18 +233,18 @@ __global__ void __launch_bounds__(192, 2)
         uint32_t pk[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const float p0 = ex2_approx(fmaf(sv[ch * 8 + 2 * k], sl2, -mc));
-          const float p1 = ex2_approx(fmaf(sv[ch * 8 + 2 * k + 1], sl2, -mc));
+          const float2 a = __ffma2_rn(make_float2(sv[ch * 8 + 2 * k], sv[ch * 8 + 2 * k + 1]),
+                                      make_float2(sl2, sl2), make_float2(-mc, -mc));
+          const float p0 = ex2_approx(a.x);
+          const float p1 = ex2_approx(a.y);
           __half2 hp = __floats2half2_rn(p0, p1);
           pk[k] = *reinterpret_cast<uint32_t*>(&hp);
         }
         *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
-      // o_full completes once per P V product. Parity waits only tell apart two
-      // consecutive phases, so the warp keeps itself at most one phase behind: before
-      // publishing P_j it waits for P_{j-1} V_{j-1} (P_j V_j cannot be issued yet, and
-      // S_j landing implies P_{j-2} V_{j-2} already completed).
-      if (j > 0 && !mbar_wait_warp(o_full, (j - 1) & 1, status, kStatusTimeoutAccum)) { ok = false; break; }
+      // No wait on the P V products here: P_{j-2} V_{j-2} (the last reader of P[b])
+      // completed before S_j could land, and the two o_full barriers stay within one
+      // phase of every later wait (P_j V_j cannot be issued before P_j is published).
       tc_fence_before();
       fence_async_smem();
       __syncwarp();
@@ -243,7 +252,7 @@ __global__ void __launch_bounds__(192, 2)
     }
     // final O and row sum after the last P V product
     ok = __all_sync(0xffffffffu, ok);
-    if (ok) ok = mbar_wait_warp(o_full, (nkt - 1) & 1, status, kStatusTimeoutAccum);
+    if (ok) ok = mbar_wait_warp(&o_full[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1, status, kStatusTimeoutAccum);
     if (ok) {
       tc_fence_after();
       float o[64];

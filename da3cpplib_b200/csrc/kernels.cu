@@ -279,59 +279,74 @@ int qk_norm_rope(__half* qkv, int M, int H, int D, int ntok, const float* qg, co
 // Optional f16 addend pe[(y*W + x)][c] (the 0.1 * UV embedding, src/dpt_head.cpp:204-209).
 __global__ void k_upsample_ac(const __half* __restrict__ in, int B, int hs, int ws, int C, __half* __restrict__ out,
                               int H, int W, const __half* __restrict__ pe) {
+  // one output row per blockIdx.y step: its source rows and vertical weight are computed
+  // once; threads stride over (x, 8-channel chunk) of the row with 32-bit indices
   const int c8 = C / 8;
-  const long total = static_cast<long>(B) * H * W * c8;
+  const int per_row = W * c8;
   const float sf0 = (W > 1 && ws > 1) ? static_cast<float>(W - 1) / (ws - 1) : static_cast<float>(W) / ws;
   const float sf1 = (H > 1 && hs > 1) ? static_cast<float>(H - 1) / (hs - 1) : static_cast<float>(H) / hs;
-  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<long>(gridDim.x) * blockDim.x) {
-    const int c = static_cast<int>(i % c8) * 8;
-    const long pix = i / c8;
-    const int x = static_cast<int>(pix % W);
-    const int y = static_cast<int>((pix / W) % H);
-    const int b = static_cast<int>(pix / (static_cast<long>(W) * H));
-    const float fy = static_cast<float>(y) / sf1, fx = static_cast<float>(x) / sf0;
-    int y0 = static_cast<int>(floorf(fy)), x0 = static_cast<int>(floorf(fx));
-    int y1 = y0 + 1, x1 = x0 + 1;
-    const float dy = fminf(fmaxf(fy - floorf(fy), 0.f), 1.f), dx = fminf(fmaxf(fx - floorf(fx), 0.f), 1.f);
-    y0 = max(0, min(y0, hs - 1)); y1 = max(0, min(y1, hs - 1));
-    x0 = max(0, min(x0, ws - 1)); x1 = max(0, min(x1, ws - 1));
-    const __half* base = in + static_cast<size_t>(b) * hs * ws * C + c;
-    const uint4 ua = *reinterpret_cast<const uint4*>(base + (static_cast<size_t>(y0) * ws + x0) * C);
-    const uint4 ub = *reinterpret_cast<const uint4*>(base + (static_cast<size_t>(y0) * ws + x1) * C);
-    const uint4 uc = *reinterpret_cast<const uint4*>(base + (static_cast<size_t>(y1) * ws + x0) * C);
-    const uint4 ud = *reinterpret_cast<const uint4*>(base + (static_cast<size_t>(y1) * ws + x1) * C);
-    const __half2* ha = reinterpret_cast<const __half2*>(&ua);
-    const __half2* hb = reinterpret_cast<const __half2*>(&ub);
-    const __half2* hc = reinterpret_cast<const __half2*>(&uc);
-    const __half2* hd = reinterpret_cast<const __half2*>(&ud);
-    const float wa = (1 - dx) * (1 - dy), wb = dx * (1 - dy), wc = (1 - dx) * dy, wd = dx * dy;
-    uint4 uo;
-    __half2* ho = reinterpret_cast<__half2*>(&uo);
-    uint4 up;
-    if (pe) up = *reinterpret_cast<const uint4*>(pe + (static_cast<size_t>(y) * W + x) * C + c);
-    const __half2* hp = reinterpret_cast<const __half2*>(&up);
+  const long rows = static_cast<long>(B) * H;
+  for (long orow = blockIdx.y; orow < rows; orow += gridDim.y) {
+    const int y = static_cast<int>(orow % H);
+    const int b = static_cast<int>(orow / H);
+    const float fy = static_cast<float>(y) / sf1;
+    int y0 = static_cast<int>(floorf(fy));
+    int y1 = y0 + 1;
+    const float dy = fminf(fmaxf(fy - floorf(fy), 0.f), 1.f);
+    y0 = max(0, min(y0, hs - 1));
+    y1 = max(0, min(y1, hs - 1));
+    const __half* src0 = in + (static_cast<size_t>(b) * hs + y0) * ws * C;
+    const __half* src1 = in + (static_cast<size_t>(b) * hs + y1) * ws * C;
+    __half* dst = out + static_cast<size_t>(orow) * W * C;
+    const __half* prow = pe ? pe + static_cast<size_t>(y) * W * C : nullptr;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < per_row; i += gridDim.x * blockDim.x) {
+      const int x = i / c8;
+      const int c = (i - x * c8) * 8;
+      const float fx = static_cast<float>(x) / sf0;
+      int x0 = static_cast<int>(floorf(fx));
+      int x1 = x0 + 1;
+      const float dx = fminf(fmaxf(fx - floorf(fx), 0.f), 1.f);
+      x0 = max(0, min(x0, ws - 1));
+      x1 = max(0, min(x1, ws - 1));
+      const uint4 ua = *reinterpret_cast<const uint4*>(src0 + x0 * C + c);
+      const uint4 ub = *reinterpret_cast<const uint4*>(src0 + x1 * C + c);
+      const uint4 uc = *reinterpret_cast<const uint4*>(src1 + x0 * C + c);
+      const uint4 ud = *reinterpret_cast<const uint4*>(src1 + x1 * C + c);
+      const __half2* ha = reinterpret_cast<const __half2*>(&ua);
+      const __half2* hb = reinterpret_cast<const __half2*>(&ub);
+      const __half2* hc = reinterpret_cast<const __half2*>(&uc);
+      const __half2* hd = reinterpret_cast<const __half2*>(&ud);
+      const float wa = (1 - dx) * (1 - dy), wb = dx * (1 - dy), wc = (1 - dx) * dy, wd = dx * dy;
+      uint4 uo;
+      __half2* ho = reinterpret_cast<__half2*>(&uo);
+      uint4 up;
+      if (prow) up = *reinterpret_cast<const uint4*>(prow + x * C + c);
+      const __half2* hp = reinterpret_cast<const __half2*>(&up);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float2 a = __half22float2(ha[k]), bb = __half22float2(hb[k]), cc = __half22float2(hc[k]),
-                   d = __half22float2(hd[k]);
-      float rx = a.x * wa + bb.x * wb + cc.x * wc + d.x * wd;
-      float ry = a.y * wa + bb.y * wb + cc.y * wc + d.y * wd;
-      if (pe) {
-        const float2 q = __half22float2(hp[k]);
-        rx += q.x;
-        ry += q.y;
+      for (int k = 0; k < 4; ++k) {
+        const float2 a = __half22float2(ha[k]), bb = __half22float2(hb[k]), cc = __half22float2(hc[k]),
+                     d = __half22float2(hd[k]);
+        float rx = a.x * wa + bb.x * wb + cc.x * wc + d.x * wd;
+        float ry = a.y * wa + bb.y * wb + cc.y * wc + d.y * wd;
+        if (prow) {
+          const float2 q = __half22float2(hp[k]);
+          rx += q.x;
+          ry += q.y;
+        }
+        ho[k] = __floats2half2_rn(rx, ry);
       }
-      ho[k] = __floats2half2_rn(rx, ry);
+      *reinterpret_cast<uint4*>(dst + x * C + c) = uo;
     }
-    *reinterpret_cast<uint4*>(out + pix * C + c) = uo;
   }
 }
 int upsample_ac(const __half* in, int B, int hs, int ws, int C, __half* out, int H, int W, const __half* pe,
                 cudaStream_t s) {
   if (C % 8) return -1;
-  const long total = static_cast<long>(B) * H * W * (C / 8);
-  k_upsample_ac<<<grid_for(total, 256), 256, 0, s>>>(in, B, hs, ws, C, out, H, W, pe);
+  const long rows = static_cast<long>(B) * H;
+  const int per_row = W * (C / 8);
+  const unsigned gx = static_cast<unsigned>((per_row + 255) / 256);
+  const unsigned gy = static_cast<unsigned>(rows < 65535 ? rows : 65535);
+  k_upsample_ac<<<dim3(gx, gy), 256, 0, s>>>(in, B, hs, ws, C, out, H, W, pe);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
