@@ -44,6 +44,25 @@ constexpr float kRescaleLog2 = 8.0f;     // rescale O only when the row max grow
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// 2^x of two values on the FMA/ALU pipes instead of the XU (MUFU) pipe, which one
+// exponential per score otherwise saturates. Cody-Waite reduction x = j + f with
+// j = round(x) (adding 1.5*2^23 leaves j in the low mantissa bits) and f in [-0.5, 0.5];
+// 2^f by a degree-3 polynomial whose coefficients were fitted for this range by
+// relative-error minimax (Lawson-weighted least squares; max relative error 7.5e-5,
+// below the f16 rounding of P); 2^j is added to the exponent field. x is clamped at
+// -125 so the exponent stays normal (the result then rounds to 0 in f16).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  x = make_float2(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f));
+  const float2 t = __fadd2_rn(x, make_float2(12582912.0f, 12582912.0f));
+  const float2 jf = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = __fadd2_rn(x, make_float2(-jf.x, -jf.y));
+  float2 p = __ffma2_rn(make_float2(0.05517166853f, 0.05517166853f), f, make_float2(0.24261112511f, 0.24261112511f));
+  p = __ffma2_rn(p, f, make_float2(0.69326096773f, 0.69326096773f));
+  p = __ffma2_rn(p, f, make_float2(0.99992805719f, 0.99992805719f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 __global__ void __launch_bounds__(192, 2)
     k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
               const __grid_constant__ CUtensorMap tmV, int seqlen, int H, int D, __half* __restrict__ out, float sl2,
@@ -235,8 +254,15 @@ __global__ void __launch_bounds__(192, 2)
         for (int k = 0; k < 4; ++k) {
           const float2 a = __ffma2_rn(make_float2(sv[ch * 8 + 2 * k], sv[ch * 8 + 2 * k + 1]),
                                       make_float2(sl2, sl2), make_float2(-mc, -mc));
-          const float p0 = ex2_approx(a.x);
-          const float p1 = ex2_approx(a.y);
+          float p0, p1;
+          if (k == 0) {  // a quarter of the exponentials on the FMA pipe, the rest on MUFU
+            const float2 e2 = exp2_poly2(a);
+            p0 = e2.x;
+            p1 = e2.y;
+          } else {
+            p0 = ex2_approx(a.x);
+            p1 = ex2_approx(a.y);
+          }
           __half2 hp = __floats2half2_rn(p0, p1);
           pk[k] = *reinterpret_cast<uint32_t*>(&hp);
         }

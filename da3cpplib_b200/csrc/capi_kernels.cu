@@ -125,6 +125,12 @@ DA3B_API int da3b_attention(const void* qkv, int nseq, int seqlen, int heads, vo
                       st, s);
 }
 
+DA3B_API int da3b_upsample_nhwc(const void* in, int B, int hs, int ws, int C, void* out, int H, int W, void* stream) {
+  if (!in || !out || B < 0 || hs <= 0 || ws <= 0 || H <= 0 || W <= 0 || C <= 0 || C % 8) return -100;
+  return upsample_ac(static_cast<const __half*>(in), B, hs, ws, C, static_cast<__half*>(out), H, W, nullptr,
+                     static_cast<cudaStream_t>(stream));
+}
+
 DA3B_API int da3b_pack_conv_weight(const float* w_f32, int OC, int IC, int ksize, void* w_packed, void* stream) {
   if (!w_f32 || !w_packed || OC <= 0 || IC <= 0 || ksize <= 0) return -100;
   return pack_conv_weight(w_f32, OC, IC, ksize, static_cast<__half*>(w_packed), static_cast<cudaStream_t>(stream));

@@ -33,7 +33,13 @@ struct GemmCfg {
   static constexpr int kStages = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
   static constexpr int kAccCols = (BN < 32) ? 32 : BN;
   static constexpr int kTmemCols = (2 * kAccCols <= 64) ? 64 : (2 * kAccCols <= 128 ? 128 : (2 * kAccCols <= 256 ? 256 : 512));
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
+  // epilogue constants of the fused out2a -> out2b stage (N == 32): bias, LayerNorm
+  // gamma/beta, out2b weights [8][32] and biases [8], staged once per CTA
+  static constexpr int kConstFloats = 32 * 3 + 8 * 32 + 8;
+  static constexpr int kConstBytes = (kConstFloats * 4 + 127) / 128 * 128;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kConstBytes + 256;
+  // N <= 32: the two epilogue warp halves take alternate tiles (each all columns)
+  static constexpr bool kSplitTiles = BN < 64;
 };
 
 // erf(z) by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26:
@@ -318,6 +324,36 @@ __device__ __forceinline__ void epilogue32(const GemmGeom& g, const EpiArgs& e, 
   }
 }
 
+// Fused out2a -> [LayerNorm] -> relu -> out2b -> output activation of one pixel (the
+// kEpiOut2 case of epilogue32) with its constants read from shared memory (c, staged
+// once per CTA) instead of global memory per row.
+__device__ __forceinline__ void epi_out2_smem(const EpiArgs& e, int row, float (&v)[32], const float* c) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] += c[j];
+  if (e.o2_ln_g) {
+    float mean = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) mean += v[j];
+    mean *= (1.0f / 32.0f);
+    float var = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) { const float d = v[j] - mean; var += d * d; }
+    var *= (1.0f / 32.0f);
+    const float rstd = rsqrtf(var + e.o2_ln_eps);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (v[j] - mean) * rstd * c[32 + j] + c[64 + j];
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+  for (int od = 0; od < e.o2_dim; ++od) {
+    float l = c[352 + od];
+    const float* w = c + 96 + od * 32;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) l = fmaf(v[j], w[j], l);
+    e.o2_out[od][row] = out_act(l, e.o2_act[od], e.o2_scale);
+  }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmGeom g,
@@ -327,7 +363,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + Cfg::kStages * Cfg::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  float* sConst = reinterpret_cast<float*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes + Cfg::kConstBytes);
   uint64_t* empty = full + Cfg::kStages;
   uint64_t* tfull = empty + Cfg::kStages;
   uint64_t* tempty = tfull + 2;
@@ -337,6 +374,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int lane = threadIdx.x & 31;
   const int num_tiles = g.num_m_tiles * g.num_n_tiles;
 
+  if (e.kind == kEpiOut2) {
+    // [0,32) bias, [32,64) LN gamma, [64,96) LN beta, [96,352) out2b weights, [352,360) out2b bias
+    for (int i = threadIdx.x; i < Cfg::kConstFloats; i += blockDim.x) {
+      float v = 0.f;
+      if (i < 32) v = e.bias ? e.bias[i] : 0.f;
+      else if (i < 64) v = e.o2_ln_g ? e.o2_ln_g[i - 32] : 1.f;
+      else if (i < 96) v = e.o2_ln_b ? e.o2_ln_b[i - 64] : 0.f;
+      else if (i < 352) v = (i - 96) < e.o2_dim * 32 ? e.o2_w[i - 96] : 0.f;
+      else v = (i - 352) < e.o2_dim ? e.o2_b[i - 352] : 0.f;
+      sConst[i] = v;
+    }
+  }
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -344,7 +394,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiWarps);
+      mbar_init(&tempty[a], Cfg::kSplitTiles ? kEpiWarps / 2 : kEpiWarps);
     }
     fence_mbar_init();
     prefetch_tmap(&tmA);
@@ -428,10 +478,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int r = q * 32 + lane;
     // column range of this warp: halves of the tile when BN >= 64
     const int half = (warp - 2) / 4;
-    const int c_begin = BN >= 64 ? half * (BN / 2) : (half == 0 ? 0 : BN);
-    const int c_end = BN >= 64 ? c_begin + BN / 2 : (half == 0 ? BN : BN);
+    const int c_begin = Cfg::kSplitTiles ? 0 : half * (BN / 2);
+    const int c_end = Cfg::kSplitTiles ? BN : c_begin + BN / 2;
     int it = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      if (Cfg::kSplitTiles && (it & 1) != half) continue;  // the other half takes this tile
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       const int mt = t / g.num_n_tiles, nt = t % g.num_n_tiles;
@@ -458,7 +509,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
-          epilogue32(g, e, row, nt * BN + c, v);
+          if (e.kind == kEpiOut2) epi_out2_smem(e, row, v, sConst);
+          else epilogue32(g, e, row, nt * BN + c, v);
         }
       }
       tc_fence_before();

@@ -277,12 +277,14 @@ int qk_norm_rope(__half* qkv, int M, int H, int D, int ntok, const float* qg, co
 // Align-corners bilinear resize of NHWC f16, ggml CPU formula: sf = (dst-1)/(src-1),
 // src = i / sf, lerp between floor and floor+1 with clamps (src/dpt_blocks.cpp:87-90).
 // Optional f16 addend pe[(y*W + x)][c] (the 0.1 * UV embedding, src/dpt_head.cpp:204-209).
+template <int CPT>
 __global__ void k_upsample_ac(const __half* __restrict__ in, int B, int hs, int ws, int C, __half* __restrict__ out,
                               int H, int W, const __half* __restrict__ pe) {
-  // one output row per blockIdx.y step: its source rows and vertical weight are computed
-  // once; threads stride over (x, 8-channel chunk) of the row with 32-bit indices
-  const int c8 = C / 8;
-  const int per_row = W * c8;
+  // one output row per blockIdx.y step (its source rows and vertical weight computed
+  // once); a thread owns one output pixel x and CPT 8-channel chunks of it, with the
+  // channel groups of a pixel on consecutive lanes so that stores stay contiguous
+  const int G = C / (8 * CPT);  // channel groups per pixel
+  const int per_row = W * G;
   const float sf0 = (W > 1 && ws > 1) ? static_cast<float>(W - 1) / (ws - 1) : static_cast<float>(W) / ws;
   const float sf1 = (H > 1 && hs > 1) ? static_cast<float>(H - 1) / (hs - 1) : static_cast<float>(H) / hs;
   const long rows = static_cast<long>(B) * H;
@@ -300,42 +302,44 @@ __global__ void k_upsample_ac(const __half* __restrict__ in, int B, int hs, int 
     __half* dst = out + static_cast<size_t>(orow) * W * C;
     const __half* prow = pe ? pe + static_cast<size_t>(y) * W * C : nullptr;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < per_row; i += gridDim.x * blockDim.x) {
-      const int x = i / c8;
-      const int c = (i - x * c8) * 8;
+      const int x = i / G;
+      const int c0 = (i - x * G) * (8 * CPT);
       const float fx = static_cast<float>(x) / sf0;
       int x0 = static_cast<int>(floorf(fx));
       int x1 = x0 + 1;
       const float dx = fminf(fmaxf(fx - floorf(fx), 0.f), 1.f);
       x0 = max(0, min(x0, ws - 1));
       x1 = max(0, min(x1, ws - 1));
-      const uint4 ua = *reinterpret_cast<const uint4*>(src0 + x0 * C + c);
-      const uint4 ub = *reinterpret_cast<const uint4*>(src0 + x1 * C + c);
-      const uint4 uc = *reinterpret_cast<const uint4*>(src1 + x0 * C + c);
-      const uint4 ud = *reinterpret_cast<const uint4*>(src1 + x1 * C + c);
-      const __half2* ha = reinterpret_cast<const __half2*>(&ua);
-      const __half2* hb = reinterpret_cast<const __half2*>(&ub);
-      const __half2* hc = reinterpret_cast<const __half2*>(&uc);
-      const __half2* hd = reinterpret_cast<const __half2*>(&ud);
       const float wa = (1 - dx) * (1 - dy), wb = dx * (1 - dy), wc = (1 - dx) * dy, wd = dx * dy;
-      uint4 uo;
-      __half2* ho = reinterpret_cast<__half2*>(&uo);
-      uint4 up;
-      if (prow) up = *reinterpret_cast<const uint4*>(prow + x * C + c);
-      const __half2* hp = reinterpret_cast<const __half2*>(&up);
+      const float2 wa2 = make_float2(wa, wa), wb2 = make_float2(wb, wb), wc2 = make_float2(wc, wc),
+                   wd2 = make_float2(wd, wd);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float2 a = __half22float2(ha[k]), bb = __half22float2(hb[k]), cc = __half22float2(hc[k]),
-                     d = __half22float2(hd[k]);
-        float rx = a.x * wa + bb.x * wb + cc.x * wc + d.x * wd;
-        float ry = a.y * wa + bb.y * wb + cc.y * wc + d.y * wd;
-        if (prow) {
-          const float2 q = __half22float2(hp[k]);
-          rx += q.x;
-          ry += q.y;
+      for (int q = 0; q < CPT; ++q) {
+        const int c = c0 + 8 * q;
+        const uint4 ua = *reinterpret_cast<const uint4*>(src0 + x0 * C + c);
+        const uint4 ub = *reinterpret_cast<const uint4*>(src0 + x1 * C + c);
+        const uint4 uc = *reinterpret_cast<const uint4*>(src1 + x0 * C + c);
+        const uint4 ud = *reinterpret_cast<const uint4*>(src1 + x1 * C + c);
+        const __half2* ha = reinterpret_cast<const __half2*>(&ua);
+        const __half2* hb = reinterpret_cast<const __half2*>(&ub);
+        const __half2* hc = reinterpret_cast<const __half2*>(&uc);
+        const __half2* hd = reinterpret_cast<const __half2*>(&ud);
+        uint4 up = make_uint4(0, 0, 0, 0);
+        if (prow) up = *reinterpret_cast<const uint4*>(prow + x * C + c);
+        const __half2* hp = reinterpret_cast<const __half2*>(&up);
+        uint4 uo;
+        __half2* ho = reinterpret_cast<__half2*>(&uo);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float2 r = __fmul2_rn(__half22float2(ha[k]), wa2);
+          r = __ffma2_rn(__half22float2(hb[k]), wb2, r);
+          r = __ffma2_rn(__half22float2(hc[k]), wc2, r);
+          r = __ffma2_rn(__half22float2(hd[k]), wd2, r);
+          if (prow) r = __fadd2_rn(r, __half22float2(hp[k]));
+          ho[k] = __floats2half2_rn(r.x, r.y);
         }
-        ho[k] = __floats2half2_rn(rx, ry);
+        *reinterpret_cast<uint4*>(dst + x * C + c) = uo;
       }
-      *reinterpret_cast<uint4*>(dst + x * C + c) = uo;
     }
   }
 }
@@ -343,10 +347,15 @@ int upsample_ac(const __half* in, int B, int hs, int ws, int C, __half* out, int
                 cudaStream_t s) {
   if (C % 8) return -1;
   const long rows = static_cast<long>(B) * H;
-  const int per_row = W * (C / 8);
-  const unsigned gx = static_cast<unsigned>((per_row + 255) / 256);
+  if (rows <= 0 || W <= 0) return 0;
   const unsigned gy = static_cast<unsigned>(rows < 65535 ? rows : 65535);
-  k_upsample_ac<<<dim3(gx, gy), 256, 0, s>>>(in, B, hs, ws, C, out, H, W, pe);
+  if (C % 32 == 0) {
+    const int per_row = W * (C / 32);
+    k_upsample_ac<4><<<dim3((per_row + 127) / 128, gy), 128, 0, s>>>(in, B, hs, ws, C, out, H, W, pe);
+  } else {
+    const int per_row = W * (C / 8);
+    k_upsample_ac<1><<<dim3((per_row + 127) / 128, gy), 128, 0, s>>>(in, B, hs, ws, C, out, H, W, pe);
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

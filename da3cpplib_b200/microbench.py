@@ -41,6 +41,14 @@ def peak_tflops():
         return 1590.0, "fallback"
 
 
+def peak_hbm():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
 def q8_0_weights(torch, N, K, gen):
     """GGUF Q8_0 bytes [N][K/32][34] on the device: f16 d then 32 int8."""
     nb = K // 32
@@ -58,12 +66,14 @@ def main(argv=None):
     from . import _lib
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("--part", default="all", choices=["A", "B", "attn", "all"])
+    ap.add_argument("--part", default="all", choices=["A", "B", "attn", "up", "all"])
     ap.add_argument("--m", type=int, default=0, help="Part A: only this M")
     ap.add_argument("--kn", default="", help="Part A: only this K,N (e.g. 1024,4096)")
     ap.add_argument("--act", type=int, default=0, help="Part A activation: 0 none, 2 erf-GELU")
     ap.add_argument("--c", type=int, default=0, help="Part B: only this channel count")
     ap.add_argument("--hw", type=int, default=0, help="Part B: only this spatial size")
+    ap.add_argument("--cout", type=int, default=0, help="Part B: output channels (default = input channels)")
+    ap.add_argument("--batch", type=int, default=8, help="Part B / up: images")
     ap.add_argument("--reps", type=int, default=20)
     args = ap.parse_args(argv)
 
@@ -123,24 +133,43 @@ def main(argv=None):
 
     if args.part in ("B", "all"):
         for C in (CONV_C if not args.c else (args.c,)):
-            w = torch.randn((C, C, 3, 3), generator=gen, device="cuda") * 0.02
+            OC = args.cout or C
+            w = torch.randn((OC, C, 3, 3), generator=gen, device="cuda") * 0.02
             icp = (C + 63) // 64 * 64
-            wp = torch.empty((C, 9, icp), dtype=torch.float16, device="cuda")
-            assert L.da3b_pack_conv_weight(P(w), C, C, 3, P(wp), S) == 0
-            b = torch.randn(C, generator=gen, device="cuda")
+            wp = torch.empty((OC, 9, icp), dtype=torch.float16, device="cuda")
+            assert L.da3b_pack_conv_weight(P(w), OC, C, 3, P(wp), S) == 0
+            b = torch.randn(OC, generator=gen, device="cuda")
             for hw in (CONV_HW if not args.hw else (args.hw,)):
-                B = 8
+                B = args.batch
                 x = torch.randn((B, hw, hw, C), generator=gen, device="cuda").half()
-                o = torch.empty((B, hw, hw, C), dtype=torch.float16, device="cuda")
+                o = torch.empty((B, hw, hw, OC), dtype=torch.float16, device="cuda")
 
                 def run():
-                    rc = L.da3b_conv_nhwc(P(x), B, hw, hw, C, P(wp), C, 3, P(b), None, None, 0, P(o), None, S)
+                    rc = L.da3b_conv_nhwc(P(x), B, hw, hw, C, P(wp), OC, 3, P(b), None, None, 0, P(o), None, S)
                     if rc:
                         raise RuntimeError(f"da3b_conv_nhwc rc={rc}")
 
                 ms = timeit(run)
-                emit("B", f"B=8 {hw}x{hw} C={C}", ms, 2.0 * B * hw * hw * C * C * 9)
+                emit("B", f"B={B} {hw}x{hw} Cin={C} Cout={OC}", ms, 2.0 * B * hw * hw * C * OC * 9)
                 del x, o
+
+    if args.part in ("up", "all"):
+        # align-corners bilinear upsample of the DPT tail: 296x296 -> 518x518, 128 channels
+        B, C = args.batch, 128
+        x = torch.randn((B, 296, 296, C), generator=gen, device="cuda").half()
+        o = torch.empty((B, 518, 518, C), dtype=torch.float16, device="cuda")
+
+        def run():
+            rc = L.da3b_upsample_nhwc(P(x), B, 296, 296, C, P(o), 518, 518, S)
+            if rc:
+                raise RuntimeError(f"da3b_upsample_nhwc rc={rc}")
+
+        ms = timeit(run)
+        gbs = (x.numel() + o.numel()) * 2 / (ms / 1e3) / 1e9
+        hbm = peak_hbm()
+        print(json.dumps({"part": "up", "case": f"B={B} 296->518 C={C}", "ms": round(ms, 4), "GB/s": round(gbs, 1),
+                          "frac": round(gbs / hbm[0], 4), "peak": f"{hbm[0]} GB/s ({hbm[1]})"}), flush=True)
+        del x, o
 
     if args.part in ("attn", "all"):
         for nseq, seqlen, heads, tag in ((64, 1370, 16, "C3 per-image"), (2, 8 * 1297, 16, "C4 global, 2 scenes")):

@@ -111,6 +111,10 @@ DA3B_API int da3b_conv_nhwc(const void* x, int B, int H, int W, int IC, const vo
                             int ksize, const float* bias, const void* res1, const void* res2, int act,
                             void* out, void* out_relu, void* stream);
 
+/* Align-corners bilinear resize of NHWC f16 [B][hs][ws][C] to [B][H][W][C] (C a
+ * multiple of 8), the DPT head's upsample: interp_bilinear_ac (src/dpt_blocks.cpp:87-90,
+ * ggml_interpolate with GGML_SCALE_FLAG_ALIGN_CORNERS). */
+DA3B_API int da3b_upsample_nhwc(const void* in, int B, int hs, int ws, int C, void* out, int H, int W, void* stream);
 
 /* ======================================================================
  * Model-level entry points (batched depth path). A context is the same

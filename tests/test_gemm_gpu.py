@@ -135,3 +135,18 @@ def test_attention(lib, nseq, seqlen, heads):
     ref = torch.softmax(q @ k.transpose(-1, -2) / 8.0, dim=-1) @ v          # [nseq, heads, seqlen, 64]
     ref = ref.permute(0, 2, 1, 3).reshape(nseq * seqlen, D)
     close(out, ref, rel=5e-3, abs_=5e-3)
+
+
+@pytest.mark.parametrize("B,hs,ws,C,H,W", [(2, 296, 296, 128, 518, 518), (1, 37, 37, 256, 74, 74), (3, 19, 19, 64, 37, 37),
+                                        (1, 5, 9, 40, 23, 17), (2, 8, 8, 32, 8, 8)])
+def test_upsample_align_corners(lib, B, hs, ws, C, H, W):
+    """da3b_upsample_nhwc vs torch bilinear interpolate with align_corners=True (the
+    ggml ALIGN_CORNERS formula): within f16 output rounding."""
+    g = torch.Generator(device="cuda").manual_seed(hs * 100 + C)
+    x = torch.randn(B, hs, ws, C, device="cuda", generator=g).half()
+    out = torch.empty(B, H, W, C, dtype=torch.float16, device="cuda")
+    assert lib.da3b_upsample_nhwc(ptr(x), B, hs, ws, C, ptr(out), H, W, stream()) == 0
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.interpolate(x.permute(0, 3, 1, 2).float(), size=(H, W), mode="bilinear",
+                                          align_corners=True).permute(0, 2, 3, 1)
+    close(out, ref, rel=2e-3, abs_=2e-3)
