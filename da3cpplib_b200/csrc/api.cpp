@@ -17,6 +17,7 @@
 #include "da3cpp/da3.h"
 #include "da3cpp/da3_c.h"
 #include "engine.h"
+#include "preprocess.h"
 
 #define DA_LOG(...)                     \
   do {                                  \
@@ -29,8 +30,19 @@ struct da_ctx {
   std::unique_ptr<da3b::Engine> engine;
   std::string last_error;
   cudaStream_t stream = nullptr;
+  // preprocess_real on the GPU for inputs that need a resize: original image upload
+  // buffer and processed-size output (grow-only), tap tables and scratch
+  std::unique_ptr<da3b::Resizer> resizer;
+  uint8_t* in_dev = nullptr;
+  size_t in_cap = 0;
+  uint8_t* pre_dev = nullptr;
+  size_t pre_cap = 0;
   ~da_ctx() {
     if (engine) cudaSetDevice(engine->device());
+    if (stream) cudaStreamSynchronize(stream);
+    resizer.reset();
+    if (in_dev) cudaFree(in_dev);
+    if (pre_dev) cudaFree(pre_dev);
     if (stream) cudaStreamDestroy(stream);
   }
 };
@@ -96,9 +108,40 @@ bool run_one(da_ctx* c, const uint8_t* rgb, int w, int h, bool legacy, std::vect
   int W = 0, H = 0;
   processed_size(e.config(), w, h, legacy, &W, &H);
   if (W != w || H != h) {
-    c->last_error = "input " + std::to_string(w) + "x" + std::to_string(h) + " needs a resize to " +
-                    std::to_string(W) + "x" + std::to_string(H) + ", which this build does not run on the GPU";
-    return false;
+    if (legacy) {
+      c->last_error = "input " + std::to_string(w) + "x" + std::to_string(h) + " needs the legacy bilinear resize to " +
+                      std::to_string(W) + "x" + std::to_string(H) + ", which this build does not run on the GPU";
+      return false;
+    }
+    // preprocess_real on the GPU (src/preprocess.cpp:157-197): upload, resize, then the
+    // processed image feeds the forward below
+    cudaSetDevice(e.device());
+    const size_t in_bytes = static_cast<size_t>(w) * h * 3, pre_bytes = static_cast<size_t>(W) * H * 3;
+    auto grow = [&](uint8_t*& p, size_t& cap, size_t need) -> bool {
+      if (need <= cap) return true;
+      if (p) {
+        cudaStreamSynchronize(c->stream);
+        cudaFree(p);
+      }
+      p = nullptr;
+      cap = 0;
+      if (cudaMalloc(&p, need) != cudaSuccess) return false;
+      cap = need;
+      return true;
+    };
+    if (!c->resizer) c->resizer.reset(new da3b::Resizer());
+    const auto& cfg = e.config();
+    int rw = 0, rh = 0;
+    if (!grow(c->in_dev, c->in_cap, in_bytes) || !grow(c->pre_dev, c->pre_cap, pre_bytes) ||
+        cudaMemcpyAsync(c->in_dev, rgb, in_bytes, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+        c->resizer->preprocess_real(c->in_dev, 1, w, h, cfg.patch_size,
+                                    cfg.img_resize_target > 0 ? cfg.img_resize_target : 504,
+                                    cfg.img_resize_mode.rfind("lower", 0) != 0, c->pre_dev, &rw, &rh, c->stream) != 0 ||
+        rw != W || rh != H) {
+      c->last_error = "preprocess: GPU resize to " + std::to_string(W) + "x" + std::to_string(H) + " failed";
+      return false;
+    }
+    rgb = c->pre_dev;
   }
   depth.resize(static_cast<size_t>(H) * W);
   const bool want_conf = conf && e.output_dim() >= 2;

@@ -14,52 +14,6 @@ static inline unsigned grid_for(long n, int threads, long cap = 1L << 20) {
   return static_cast<unsigned>(b);
 }
 
-// ---------------------------------------------------------------- preprocess + patchify
-// RGB8 [B][H][W][3] -> normalised, patch-major A matrix of the patch-embed GEMM:
-// row = b*Np + (py*gw + px), column k = c*P*P + ky*P + kx (the flattening of the
-// conv weight [D][3][P][P]), zero for k >= 3*P*P. Normalisation is the reference's
-// (v/255 - mean[c]) / std[c] in f32 (src/preprocess.cpp:192-196), stored as f16.
-__global__ void k_patchify(const uint8_t* __restrict__ rgb, int B, int H, int W, int P, int gh, int gw,
-                           float m0, float m1, float m2, float s0, float s1, float s2, __half* __restrict__ out,
-                           int ldk) {
-  const long total = static_cast<long>(B) * gh * gw * (ldk / 2);
-  const int kk = 3 * P * P;
-  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<long>(gridDim.x) * blockDim.x) {
-    const int k2 = static_cast<int>(i % (ldk / 2)) * 2;
-    const long row = i / (ldk / 2);
-    const int p = static_cast<int>(row % (gh * gw));
-    const int b = static_cast<int>(row / (gh * gw));
-    const int py = p / gw, px = p % gw;
-    float v[2];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int k = k2 + j;
-      if (k < kk) {
-        const int c = k / (P * P), r = k % (P * P), ky = r / P, kx = r % P;
-        const int y = py * P + ky, x = px * P + kx;
-        const float u = static_cast<float>(rgb[((static_cast<size_t>(b) * H + y) * W + x) * 3 + c]) / 255.f;
-        const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2);
-        const float sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
-        v[j] = (u - mean) / sd;
-      } else {
-        v[j] = 0.f;
-      }
-    }
-    *reinterpret_cast<__half2*>(out + row * ldk + k2) = __floats2half2_rn(v[0], v[1]);
-  }
-}
-
-int patchify(const uint8_t* rgb, int B, int H, int W, int P, const float* mean, const float* sd, __half* out, int ldk,
-             cudaStream_t s) {
-  if (H % P || W % P || ldk % 2 || ldk < 3 * P * P) return -1;
-  const int gh = H / P, gw = W / P;
-  const long total = static_cast<long>(B) * gh * gw * (ldk / 2);
-  k_patchify<<<grid_for(total, 256), 256, 0, s>>>(rgb, B, H, W, P, gh, gw, mean[0], mean[1], mean[2], sd[0], sd[1],
-                                                  sd[2], out, ldk);
-  return cudaGetLastError() == cudaSuccess ? 0 : -2;
-}
-
 // x[b*ntok + 0][:] = cls + pos[0]  (token 0 of every image; src/dino_backbone.cpp:123-126)
 __global__ void k_cls_rows(float* __restrict__ x, int B, int ntok, int D, const float* __restrict__ cls,
                            const float* __restrict__ pos) {

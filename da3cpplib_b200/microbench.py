@@ -66,7 +66,7 @@ def main(argv=None):
     from . import _lib
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("--part", default="all", choices=["A", "B", "attn", "up", "all"])
+    ap.add_argument("--part", default="all", choices=["A", "B", "attn", "up", "pre", "all"])
     ap.add_argument("--m", type=int, default=0, help="Part A: only this M")
     ap.add_argument("--kn", default="", help="Part A: only this K,N (e.g. 1024,4096)")
     ap.add_argument("--act", type=int, default=0, help="Part A activation: 0 none, 2 erf-GELU")
@@ -170,6 +170,26 @@ def main(argv=None):
         print(json.dumps({"part": "up", "case": f"B={B} 296->518 C={C}", "ms": round(ms, 4), "GB/s": round(gbs, 1),
                           "frac": round(gbs / hbm[0], 4), "peak": f"{hbm[0]} GB/s ({hbm[1]})"}), flush=True)
         del x, o
+
+    if args.part in ("pre", "all"):
+        # normalise + patchify of the C3 batch: 64 RGB8 images 518x518 -> f16 operand [64*1369][640]
+        B, H, W, ldk = 64, 518, 518, 640
+        img = torch.randint(0, 256, (B, H, W, 3), generator=gen, device="cuda", dtype=torch.uint8)
+        o = torch.empty((B * (H // 14) * (W // 14), ldk), dtype=torch.float16, device="cuda")
+        mean = (ctypes.c_float * 3)(0.485, 0.456, 0.406)
+        std = (ctypes.c_float * 3)(0.229, 0.224, 0.225)
+
+        def run():
+            rc = L.da3b_patchify(P(img), B, H, W, 14, mean, std, P(o), ldk, S)
+            if rc:
+                raise RuntimeError(f"da3b_patchify rc={rc}")
+
+        ms = timeit(run)
+        gbs = (img.numel() + o.numel() * 2) / (ms / 1e3) / 1e9
+        hbm = peak_hbm()
+        print(json.dumps({"part": "pre", "case": f"patchify B={B} {H}x{W}", "ms": round(ms, 4), "GB/s": round(gbs, 1),
+                          "frac": round(gbs / hbm[0], 4), "peak": f"{hbm[0]} GB/s ({hbm[1]})"}), flush=True)
+        del img, o
 
     if args.part in ("attn", "all"):
         for nseq, seqlen, heads, tag in ((64, 1370, 16, "C3 per-image"), (2, 8 * 1297, 16, "C4 global, 2 scenes")):

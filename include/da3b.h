@@ -116,6 +116,20 @@ DA3B_API int da3b_conv_nhwc(const void* x, int B, int H, int W, int IC, const vo
  * ggml_interpolate with GGML_SCALE_FLAG_ALIGN_CORNERS). */
 DA3B_API int da3b_upsample_nhwc(const void* in, int B, int hs, int ws, int C, void* out, int H, int W, void* stream);
 
+/* uint8 HWC RGB resize of B images [B][sh][sw][3] -> [B][dh][dw][3], bit-exact with
+ * DA3cpplib's resizers: mode 0 = resize_cubic (src/preprocess.cpp:61-99), mode 1 =
+ * resize_area (:122-148, which falls back to its bilinear when both axes grow). src and
+ * dst are device memory. The library keeps per-size tap tables and a float scratch per
+ * device, allocated on first use of a size. */
+DA3B_API int da3b_resize_u8(const void* src, int B, int sw, int sh, void* dst, int dw, int dh, int mode, void* stream);
+
+/* Normalise + patchify: RGB8 [B][H][W][3] (device, H and W multiples of patch) ->
+ * the patch-embed GEMM operand f16 [B*(H/patch)*(W/patch)][ldk], column
+ * c*patch^2 + ky*patch + kx = (v/255 - mean[c]) / std[c] (src/preprocess.cpp:192-196),
+ * zero up to ldk (even, >= 3*patch^2). mean/std are host arrays of 3. */
+DA3B_API int da3b_patchify(const void* rgb, int B, int H, int W, int patch, const float* mean, const float* std_,
+                           void* out, int ldk, void* stream);
+
 /* ======================================================================
  * Model-level entry points (batched depth path). A context is the same
  * da_ctx as the reference-compatible C ABI in da3cpp/da3_c.h.

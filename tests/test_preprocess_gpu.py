@@ -1,0 +1,143 @@
+"""GPU preprocessing through the C ABI.
+
+* da3b_resize_u8 against the CPU oracle's uint8 resizers (which are bit-exact with
+  DA3cpplib's own src/preprocess.cpp): bit-exact, cubic and area, one or two images,
+  odd sizes, and area's bilinear fallback when both axes grow.
+* The preprocess_real chain (bound resize, then patch rounding) composed from it,
+  normalised: bit-exact against the oracle's preprocess.
+* da3b_patchify against numpy's f32 normalisation rounded to f16: bit-exact, including
+  widths whose rows start unaligned and strips with fewer than 16 patches.
+* A model-level run on an image that needs resizing (da_capi_depth_path on a PPM file):
+  the GPU resizes it, and the depth matches the oracle's (median relative error <= 1e-2).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+V = ctypes.c_void_p
+MEAN = (0.485, 0.456, 0.406)
+STD = (0.229, 0.224, 0.225)
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+def _stream():
+    return V(torch.cuda.current_stream().cuda_stream)
+
+
+def _gpu_resize(lib, imgs, dw, dh, mode):
+    src = torch.from_numpy(np.ascontiguousarray(imgs)).cuda()
+    B, sh, sw, _ = imgs.shape
+    dst = torch.empty((B, dh, dw, 3), dtype=torch.uint8, device="cuda")
+    assert lib.da3b_resize_u8(V(src.data_ptr()), B, sw, sh, V(dst.data_ptr()), dw, dh, mode, _stream()) == 0
+    torch.cuda.synchronize()
+    assert lib.da3b_device_status() == 0
+    return dst.cpu().numpy()
+
+
+@pytest.mark.parametrize("B,sh,sw,dh,dw,mode", [
+    (1, 37, 53, 112, 160, 0), (2, 90, 61, 56, 38, 1), (1, 23, 31, 40, 57, 0), (1, 400, 300, 126, 98, 1),
+    (2, 7, 11, 30, 19, 0), (1, 40, 40, 13, 17, 1), (1, 20, 30, 26, 44, 1), (1, 518, 700, 518, 518, 1),
+    (1, 97, 150, 112, 173, 0)])
+def test_resize_u8_bit_exact(lib, cuda, B, sh, sw, dh, dw, mode):
+    from oracle import oracle as orc
+
+    rng = np.random.default_rng(sh * 1000 + sw + mode)
+    imgs = rng.integers(0, 256, size=(B, sh, sw, 3), dtype=np.uint8)
+    got = _gpu_resize(lib, imgs, dw, dh, mode)
+    for b in range(B):
+        ref = orc.resize_u8(imgs[b], dw, dh, "cubic" if mode == 0 else "area")
+        assert np.array_equal(got[b], ref), f"image {b}: {np.count_nonzero(got[b] != ref)} bytes differ"
+
+
+def _policy(w, h, patch, target, upper):
+    """Step sizes of preprocess_real (src/preprocess.cpp:166-190)."""
+    steps = []
+    bound = max(w, h) if upper else min(w, h)
+    if bound != target:
+        scale = target / bound
+        nw, nh = max(1, int(round(w * scale))), max(1, int(round(h * scale)))
+        steps.append((nw, nh, 0 if scale > 1.0 else 1))
+        w, h = nw, nh
+
+    def nearest(x):
+        down = (x // patch) * patch
+        up = down + patch
+        return up if abs(up - x) <= abs(x - down) else down
+
+    nw, nh = max(1, nearest(w)), max(1, nearest(h))
+    if (nw, nh) != (w, h):
+        steps.append((nw, nh, 0 if (nw > w or nh > h) else 1))
+    return steps
+
+
+@pytest.mark.parametrize("h,w,target,upper", [(37, 53, 56, True), (90, 61, 56, True), (37, 53, 42, False),
+                                              (29, 45, 28, True), (15, 100, 84, True), (300, 457, 518, False),
+                                              (640, 480, 504, True)])
+def test_preprocess_real_chain_bit_exact(lib, cuda, h, w, target, upper):
+    from oracle import oracle as orc
+
+    rng = np.random.default_rng(h * 7 + w)
+    img = rng.integers(0, 256, size=(1, h, w, 3), dtype=np.uint8)
+    cur = img
+    for nw, nh, mode in _policy(w, h, 14, target, upper):
+        cur = _gpu_resize(lib, cur, nw, nh, mode)
+    chw = (cur[0].astype(np.float32) / np.float32(255.0) - np.array(MEAN, np.float32)) / np.array(STD, np.float32)
+    ref = orc.preprocess_cfg(img[0], 14, target, upper)
+    assert np.array_equal(chw.transpose(2, 0, 1), ref)
+
+
+@pytest.mark.parametrize("B,H,W", [(2, 518, 518), (1, 56, 70), (3, 42, 238), (1, 504, 504), (2, 14, 14)])
+def test_patchify_bit_exact(lib, cuda, B, H, W):
+    P, ldk = 14, 640
+    rng = np.random.default_rng(H + W)
+    img = rng.integers(0, 256, size=(B, H, W, 3), dtype=np.uint8)
+    src = torch.from_numpy(img).cuda()
+    gh, gw = H // P, W // P
+    out = torch.full((B * gh * gw, ldk), 7.0, dtype=torch.float16, device="cuda")
+    mean = (ctypes.c_float * 3)(*MEAN)
+    std = (ctypes.c_float * 3)(*STD)
+    assert lib.da3b_patchify(V(src.data_ptr()), B, H, W, P, mean, std, V(out.data_ptr()), ldk, _stream()) == 0
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    x = (img.astype(np.float32) / np.float32(255.0) - np.array(MEAN, np.float32)) / np.array(STD, np.float32)
+    ref = x.reshape(B, gh, P, gw, P, 3).transpose(0, 1, 3, 5, 2, 4).reshape(B * gh * gw, 3 * P * P).astype(np.float16)
+    assert np.array_equal(got[:, :3 * P * P].view(np.uint16), ref.view(np.uint16))
+    assert np.all(got[:, 3 * P * P:] == 0)
+
+
+def test_capi_depth_path_resizes_on_gpu(lib, cuda, tmp_path):
+    from da3cpplib_b200 import synth
+    from oracle.oracle import Oracle
+
+    path = synth.ensure_gguf("da2-t", stress=True)     # lower_bound, target 112
+    rng = np.random.default_rng(5)
+    img = rng.integers(0, 256, size=(97, 150, 3), dtype=np.uint8)
+    ppm = tmp_path / "in.ppm"
+    with open(ppm, "wb") as f:
+        f.write(b"P6\n150 97\n255\n" + img.tobytes())
+    ctx = lib.da_capi_load(path.encode(), 1)
+    assert ctx
+    try:
+        h, w = ctypes.c_int(), ctypes.c_int()
+        p = lib.da_capi_depth_path(ctx, str(ppm).encode(), ctypes.byref(h), ctypes.byref(w))
+        assert p, lib.da_capi_last_error(ctx)
+        got = np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_float)), shape=(h.value * w.value,)).copy()
+        lib.da_capi_free_floats(p)
+    finally:
+        lib.da_capi_free(ctx)
+    ref = Oracle(path, act_quant=True).infer(img)
+    assert (h.value, w.value) == (ref["H"], ref["W"]) == (112, 168)
+    r = ref["depth"].reshape(-1)
+    m = np.abs(r) > 1e-6
+    assert np.median(np.abs(got[m] - r[m]) / np.abs(r[m])) <= 1e-2
