@@ -8,7 +8,10 @@
 * da3b_patchify against numpy's f32 normalisation rounded to f16: bit-exact, including
   widths whose rows start unaligned and strips with fewer than 16 patches.
 * A model-level run on an image that needs resizing (da_capi_depth_path on a PPM file):
-  the GPU resizes it, and the depth matches the oracle's (median relative error <= 1e-2).
+  the GPU resizes it, and the depth matches the oracle's: median relative error over
+  pixels with |ref| > 1e-6 <= max(1e-2, 1.5 * floor), floor being the same error between
+  the oracle with and without ggml's activation quantisation on this input (DA2's ReLU
+  leaves few non-zero pixels on a random model), and the zero pattern agrees on >= 99%.
 """
 import ctypes
 
@@ -137,7 +140,16 @@ def test_capi_depth_path_resizes_on_gpu(lib, cuda, tmp_path):
     finally:
         lib.da_capi_free(ctx)
     ref = Oracle(path, act_quant=True).infer(img)
+    reff = Oracle(path, act_quant=False).infer(img)
     assert (h.value, w.value) == (ref["H"], ref["W"]) == (112, 168)
+
+    def median_rel(a, b):
+        a, b = a.reshape(-1), b.reshape(-1)
+        m = np.abs(b) > 1e-6
+        return float(np.median(np.abs(a[m] - b[m]) / np.abs(b[m])))
+
+    floor = median_rel(reff["depth"], ref["depth"])
+    err = median_rel(got, ref["depth"])
+    assert err <= max(1e-2, 1.5 * floor), (err, floor)
     r = ref["depth"].reshape(-1)
-    m = np.abs(r) > 1e-6
-    assert np.median(np.abs(got[m] - r[m]) / np.abs(r[m])) <= 1e-2
+    assert np.mean((np.abs(got) > 1e-6) == (np.abs(r) > 1e-6)) >= 0.99
