@@ -75,6 +75,26 @@ class Model:
             out["rays"] = ray
         return out
 
+    def infer_prepared(self, chw: np.ndarray):
+        """Normalised planar f32 images [n][3][h][w] (host) -> dict of numpy outputs
+        (the input of the reference's infer_preprocessed)."""
+        chw = np.ascontiguousarray(chw, dtype=np.float32)
+        if chw.ndim == 3:
+            chw = chw[None]
+        n, _, h, w = chw.shape
+        depth = np.empty((n, h, w), np.float32)
+        conf = np.empty((n, h, w), np.float32) if self.output_dim >= 2 else None
+        rc = self.lib.da3b_infer_prepared(self.ctx, chw.ctypes.data, n, h, w, depth.ctypes.data,
+                                          conf.ctypes.data if conf is not None else None, None)
+        if rc == 0:
+            rc = self.lib.da3b_device_status()
+        if rc != 0:
+            raise RuntimeError(f"da3b_infer_prepared failed ({rc}): {self.last_error}")
+        out = {"depth": depth}
+        if conf is not None:
+            out["conf"] = conf
+        return out
+
     def infer_device(self, rgb_ptr, n, h, w, depth_ptr, conf_ptr=None, rays_ptr=None, views_per_scene=1,
                      stream=None):
         """Device-pointer variant (no synchronisation)."""

@@ -265,14 +265,37 @@ bool infer_file(Model& model, const std::string& image_path, Result& result, con
   return infer(model, img, result, options);
 }
 
+// src/api.cpp:178-193: DA3 (not DA2, mono or nested) only; the caller fills the device
+// buffer of the normalised planar f32 image [3][height][width] synchronously inside the
+// callback; depth (+ confidence) at that size.
 bool infer_preprocessed(Model& model, int height, int width, const UploadCallback& upload, Result& result) {
   result = {};
-  (void)model;
-  (void)height;
-  (void)width;
-  (void)upload;
-  DA_LOG("infer_preprocessed: the f32 planar device input path is not implemented in this build");
-  return false;
+  if (!model.ctx || !model.ctx->engine || !upload || height <= 0 || width <= 0) return false;
+  da_ctx* c = model.ctx.get();
+  da3b::Engine& e = *c->engine;
+  if (e.config().is_da2() || is_mono(e)) return false;
+  size_t bytes = 0;
+  float* dst = e.prepared_input(1, height, width, &bytes);
+  if (!dst) {
+    DA_LOG("infer_preprocessed: %s", e.last_error().c_str());
+    return false;
+  }
+  upload(UploadTarget{dst, bytes, true});
+  result.depth.resize(static_cast<size_t>(height) * width);
+  const bool want_conf = e.output_dim() >= 2;
+  if (want_conf) result.confidence.resize(result.depth.size());
+  cudaSetDevice(e.device());
+  const int rc = e.run_prepared(1, height, width, result.depth.data(), want_conf ? result.confidence.data() : nullptr,
+                                c->stream);
+  if (rc != 0 || cudaStreamSynchronize(c->stream) != cudaSuccess || e.status() != 0) {
+    DA_LOG("infer_preprocessed: forward failed: %s", e.last_error().c_str());
+    result = {};
+    return false;
+  }
+  result.height = height;
+  result.width = width;
+  result.is_metric = model_info(model).is_metric;
+  return true;
 }
 
 bool infer_batch(Model& model, const std::vector<Image>& images, std::vector<Result>& results) {
@@ -494,6 +517,26 @@ DA3B_API int da3b_infer_device(da_ctx* c, const void* rgb_dev, int n_views, int 
                                 static_cast<float*>(rays_dev), static_cast<cudaStream_t>(stream));
   if (rc) c->last_error = c->engine->last_error();
   return rc;
+}
+
+DA3B_API int da3b_infer_prepared(da_ctx* c, const float* chw, int n_views, int h, int w, float* depth, float* conf,
+                                 void* stream) {
+  if (!c || !c->engine || !chw || !depth || n_views <= 0 || h <= 0 || w <= 0) return -1;
+  da3b::Engine& e = *c->engine;
+  size_t bytes = 0;
+  float* dst = e.prepared_input(n_views, h, w, &bytes);
+  if (!dst) {
+    c->last_error = e.last_error();
+    return -2;
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  if (cudaMemcpyAsync(dst, chw, bytes, cudaMemcpyDefault, s) != cudaSuccess) return -3;
+  const int rc = e.run_prepared(n_views, h, w, depth, conf, s);
+  if (rc) {
+    c->last_error = e.last_error();
+    return rc;
+  }
+  return 0;
 }
 
 DA3B_API int da3b_infer_host(da_ctx* c, const void* rgb_host, int n_views, int views_per_scene, int h, int w,

@@ -79,8 +79,16 @@ struct Plan {
   int launches = 0;
   cudaGraphExec_t graph = nullptr;
   bool warmed = false;
+  // prepared input (infer_preprocessed): normalised planar f32 [V][3][H][W], allocated on
+  // first use, with its own captured graph (the first kernel reads it instead of rgb)
+  float* chw = nullptr;
+  bool prepared = false;
+  cudaGraphExec_t graph_pre = nullptr;
+  bool warmed_pre = false;
   ~Plan() {
     if (graph) cudaGraphExecDestroy(graph);
+    if (graph_pre) cudaGraphExecDestroy(graph_pre);
+    if (chw) cudaFree(chw);
     if (arena.base) cudaFree(arena.base);
   }
 };
@@ -429,7 +437,8 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
   float* mean = const_cast<float*>(c.img_mean.data());
   float* sd = const_cast<float*>(c.img_std.data());
   // ---- tokens: patchify -> patch-embed GEMM (+bias +pos into rows 1..Np) ; CLS row
-  CK(patchify(p.rgb, V, p.H, p.W, c.patch_size, mean, sd, p.patchA, m.patch_ldk, s));
+  if (p.prepared) CK(patchify_chw(p.chw, V, p.H, p.W, c.patch_size, p.patchA, m.patch_ldk, s));
+  else CK(patchify(p.rgb, V, p.H, p.W, c.patch_size, mean, sd, p.patchA, m.patch_ldk, s));
   {
     EpiArgs e = epi_default();
     e.kind = kEpiTokens;
@@ -724,51 +733,99 @@ int Engine::forward(Plan& p, cudaStream_t s) {
 
 int Engine::run(const uint8_t* rgb, int V, int S, int H, int W, float* depth, float* conf, float* rays,
                 cudaStream_t s) {
-  const Config& c = model_->cfg;
-  if (V <= 0 || S <= 0 || V % S || H <= 0 || W <= 0 || H % c.patch_size || W % c.patch_size) {
-    err_ = "bad shape: n_views must be a positive multiple of views_per_scene and H, W multiples of the patch size";
-    return -2;
-  }
-  if (rays && !model_->head.aux) {
-    err_ = "this GGUF has no auxiliary ray head";
-    return -3;
-  }
-  cudaSetDevice(device_);
-  Plan* p = plan_for(V, S, H, W, rays != nullptr);
-  if (!p) return -4;
-  last_ = p;
+  int code = 0;
+  Plan* p = checked_plan(V, S, H, W, rays != nullptr, &code);
+  if (!p) return code;
   const size_t HW = static_cast<size_t>(H) * W;
   if (cudaMemcpyAsync(p->rgb, rgb, static_cast<size_t>(V) * HW * 3, cudaMemcpyDefault, s) != cudaSuccess) {
     err_ = "input copy failed";
     return -5;
   }
-  if (!use_graph_ || !p->warmed) {
+  const int rc = launch(p, false, s);
+  return rc ? rc : copy_out(p, depth, conf, rays, s);
+}
+
+Plan* Engine::checked_plan(int V, int S, int H, int W, bool rays, int* code) {
+  const Config& c = model_->cfg;
+  if (V <= 0 || S <= 0 || V % S || H <= 0 || W <= 0 || H % c.patch_size || W % c.patch_size) {
+    err_ = "bad shape: n_views must be a positive multiple of views_per_scene and H, W multiples of the patch size";
+    if (code) *code = -2;
+    return nullptr;
+  }
+  if (rays && !model_->head.aux) {
+    err_ = "this GGUF has no auxiliary ray head";
+    if (code) *code = -3;
+    return nullptr;
+  }
+  cudaSetDevice(device_);
+  Plan* p = plan_for(V, S, H, W, rays);
+  if (!p) {
+    if (code) *code = -4;
+    return nullptr;
+  }
+  last_ = p;
+  return p;
+}
+
+float* Engine::prepared_input(int V, int H, int W, size_t* bytes) {
+  Plan* p = checked_plan(V, 1, H, W, false, nullptr);
+  if (!p) return nullptr;
+  const size_t n = static_cast<size_t>(V) * 3 * H * W;
+  if (!p->chw && cudaMalloc(&p->chw, n * sizeof(float)) != cudaSuccess) {
+    p->chw = nullptr;
+    err_ = "out of device memory for the prepared input";
+    return nullptr;
+  }
+  if (bytes) *bytes = n * sizeof(float);
+  return p->chw;
+}
+
+int Engine::run_prepared(int V, int H, int W, float* depth, float* conf, cudaStream_t s) {
+  if (!prepared_input(V, H, W, nullptr)) return -4;
+  Plan* p = last_;
+  const int rc = launch(p, true, s);
+  return rc ? rc : copy_out(p, depth, conf, nullptr, s);
+}
+
+// One forward of a plan: eager on its first run (plan warm-up), then replays of the
+// graph captured for this input mode.
+int Engine::launch(Plan* p, bool prepared, cudaStream_t s) {
+  p->prepared = prepared;
+  bool& warmed = prepared ? p->warmed_pre : p->warmed;
+  cudaGraphExec_t& graph = prepared ? p->graph_pre : p->graph;
+  if (!use_graph_ || !warmed) {
     const int rc = forward(*p, s);
     if (rc) return rc;
-    p->warmed = true;
-  } else {
-    if (!p->graph) {
-      cudaStream_t cs;
-      cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking);
-      cudaGraph_t g = nullptr;
-      int rc = 0;
-      if (cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal) != cudaSuccess) rc = -6;
-      if (!rc) rc = forward(*p, cs);
-      if (cudaStreamEndCapture(cs, &g) != cudaSuccess && !rc) rc = -7;
-      if (!rc && cudaGraphInstantiate(&p->graph, g, 0) != cudaSuccess) rc = -8;
-      if (g) cudaGraphDestroy(g);
-      cudaStreamDestroy(cs);
-      if (rc) {
-        if (err_.empty()) err_ = "CUDA graph capture failed";
-        p->graph = nullptr;
-        return rc;
-      }
-    }
-    if (cudaGraphLaunch(p->graph, s) != cudaSuccess) {
-      err_ = "graph launch failed";
-      return -9;
+    warmed = true;
+    return 0;
+  }
+  if (!graph) {
+    cudaStream_t cs;
+    cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking);
+    cudaGraph_t g = nullptr;
+    int rc = 0;
+    if (cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal) != cudaSuccess) rc = -6;
+    if (!rc) rc = forward(*p, cs);
+    if (cudaStreamEndCapture(cs, &g) != cudaSuccess && !rc) rc = -7;
+    if (!rc && cudaGraphInstantiate(&graph, g, 0) != cudaSuccess) rc = -8;
+    if (g) cudaGraphDestroy(g);
+    cudaStreamDestroy(cs);
+    if (rc) {
+      if (err_.empty()) err_ = "CUDA graph capture failed";
+      graph = nullptr;
+      return rc;
     }
   }
+  if (cudaGraphLaunch(graph, s) != cudaSuccess) {
+    err_ = "graph launch failed";
+    return -9;
+  }
+  return 0;
+}
+
+int Engine::copy_out(Plan* p, float* depth, float* conf, float* rays, cudaStream_t s) {
+  const size_t HW = static_cast<size_t>(p->H) * p->W;
+  const int V = p->V;
   if (depth && cudaMemcpyAsync(depth, p->depth, static_cast<size_t>(V) * HW * 4, cudaMemcpyDefault, s) != cudaSuccess)
     return -10;
   if (conf && model_->head.od >= 2 &&

@@ -42,6 +42,12 @@ class Engine {
   int run(const uint8_t* rgb_dev, int n_views, int views_per_scene, int H, int W, float* depth_dev,
           float* conf_dev, float* rays_dev, cudaStream_t s);
 
+  // Prepared-input runs (infer_preprocessed, src/api.cpp:178-193 / src/engine.cpp:230-270):
+  // device buffer for V normalised planar f32 images [V][3][H][W] of the plan of that
+  // shape (allocated on first use; *bytes its size), and the forward reading it.
+  float* prepared_input(int V, int H, int W, size_t* bytes);
+  int run_prepared(int V, int H, int W, float* depth, float* conf, cudaStream_t s);
+
   // Selected reference view per scene of the last run with views_per_scene >= 3 (host copy).
   std::vector<int> last_ref_views(cudaStream_t s);
   // Kernel launches of one forward of the given shape (after a run of that shape).
@@ -67,6 +73,9 @@ class Engine {
  private:
   Engine() = default;
   Plan* plan_for(int n_views, int S, int H, int W, bool rays);
+  Plan* checked_plan(int V, int S, int H, int W, bool rays, int* code);
+  int launch(Plan* p, bool prepared, cudaStream_t s);
+  int copy_out(Plan* p, float* depth, float* conf, float* rays, cudaStream_t s);
   int forward(Plan& p, cudaStream_t s);
   int backbone(Plan& p, cudaStream_t s);
   int head(Plan& p, cudaStream_t s);

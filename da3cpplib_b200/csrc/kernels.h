@@ -8,6 +8,9 @@ namespace da3b {
 
 int patchify(const uint8_t* rgb, int B, int H, int W, int P, const float* mean, const float* sd, __half* out, int ldk,
              cudaStream_t s);
+// Patchify of normalised planar f32 images [B][3][H][W] (no normalisation): the
+// prepared-input path.
+int patchify_chw(const float* chw, int B, int H, int W, int P, __half* out, int ldk, cudaStream_t s);
 int cls_rows(float* x, int B, int ntok, int D, const float* cls, const float* pos, cudaStream_t s);
 int cam_rows(float* x, int nviews_total, int views_per_scene, int ntok, int D, const float* cam, cudaStream_t s);
 // LayerNorm rows (D in {128,256,384,512,768,1024,1536,2048}); input row of output row r

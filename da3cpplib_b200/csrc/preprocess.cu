@@ -397,6 +397,50 @@ int patchify(const uint8_t* rgb, int B, int H, int W, int P, const float* mean, 
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
+namespace {
+
+// planar f32 [B][3][H][W] -> operand rows (8 consecutive columns per thread)
+__global__ void k_patchify_chw(const float* __restrict__ chw, int B, int H, int W, int P, int gh, int gw,
+                               __half* __restrict__ out, int ldk) {
+  const int k8 = ldk / 8, kk = 3 * P * P;
+  const long total = static_cast<long>(B) * gh * gw * k8;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int k0 = static_cast<int>(i % k8) * 8;
+    const long row = i / k8;
+    const int p = static_cast<int>(row % (gh * gw));
+    const int b = static_cast<int>(row / (gh * gw));
+    const int py = p / gw, px = p % gw;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int k = k0 + j;
+      if (k < kk) {
+        const int c = k / (P * P), r = k % (P * P), ky = r / P, kx = r % P;
+        v[j] = chw[((static_cast<size_t>(b) * 3 + c) * H + py * P + ky) * W + px * P + kx];
+      } else {
+        v[j] = 0.f;
+      }
+    }
+    uint4 o;
+    __half2* h2 = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) h2[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+    *reinterpret_cast<uint4*>(out + row * ldk + k0) = o;
+  }
+}
+
+}  // namespace
+
+int patchify_chw(const float* chw, int B, int H, int W, int P, __half* out, int ldk, cudaStream_t s) {
+  if (H % P || W % P || ldk % 8 || ldk < 3 * P * P || (reinterpret_cast<uintptr_t>(out) & 15)) return -1;
+  const int gh = H / P, gw = W / P;
+  if (B <= 0 || gh <= 0 || gw <= 0) return 0;
+  const long total = static_cast<long>(B) * gh * gw * (ldk / 8);
+  k_patchify_chw<<<blocks_for(total), 256, 0, s>>>(chw, B, H, W, P, gh, gw, out, ldk);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
 }  // namespace da3b
 
 // ------------------------------------------------------------------ C ABI

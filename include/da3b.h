@@ -160,6 +160,15 @@ DA3B_API int da3b_infer_device(da_ctx* ctx, const void* rgb_dev, int n_views, in
 DA3B_API int da3b_infer_host(da_ctx* ctx, const void* rgb_host, int n_views, int views_per_scene, int h, int w,
                              float* depth_host, float* conf_host, float* rays_host);
 
+/* Depth from n_views already preprocessed images: normalised planar f32
+ * [n_views][3][h][w] (host or device memory, h and w multiples of the patch size), the
+ * input of infer_preprocessed (src/api.cpp:178-193, Engine::depth_native_prepared at
+ * src/engine.cpp:230-270) without the callback. depth / conf as in da3b_infer_device
+ * (host or device). Asynchronous on `stream` (NULL: the context's stream) after the first
+ * call of a shape. */
+DA3B_API int da3b_infer_prepared(da_ctx* ctx, const float* chw, int n_views, int h, int w, float* depth, float* conf,
+                                 void* stream);
+
 /* Reference view chosen per scene by the last multi-view run (views_per_scene >= 3). */
 DA3B_API int da3b_ref_views(da_ctx* ctx, int* out, int n);
 /* Kernel launches of one forward of that shape (after one run of it). */

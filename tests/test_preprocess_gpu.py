@@ -7,6 +7,8 @@
   normalised: bit-exact against the oracle's preprocess.
 * da3b_patchify against numpy's f32 normalisation rounded to f16: bit-exact, including
   widths whose rows start unaligned and strips with fewer than 16 patches.
+* da3b_infer_prepared (normalised planar f32 input, the reference's infer_preprocessed
+  path) gives depth and confidence bit-identical to the RGB8 path on the same images.
 * A model-level run on an image that needs resizing (da_capi_depth_path on a PPM file):
   the GPU resizes it, and the depth matches the oracle's: median relative error over
   pixels with |ref| > 1e-6 <= max(1e-2, 1.5 * floor), floor being the same error between
@@ -153,3 +155,19 @@ def test_capi_depth_path_resizes_on_gpu(lib, cuda, tmp_path):
     assert err <= max(1e-2, 1.5 * floor), (err, floor)
     r = ref["depth"].reshape(-1)
     assert np.mean((np.abs(got) > 1e-6) == (np.abs(r) > 1e-6)) >= 0.99
+
+
+@pytest.mark.parametrize("name,n", [("da3-t", 2), ("da2-t", 1)])
+def test_infer_prepared_matches_rgb_path(cuda, name, n):
+    from da3cpplib_b200 import Model, synth
+
+    path = synth.ensure_gguf(name, stress=True)
+    m = Model(path, 0)
+    imgs = np.stack([synth.image(synth.IMAGE_SEED, i, 112, 112) for i in range(n)])
+    ref = m.infer(imgs)
+    chw = (imgs.astype(np.float32) / np.float32(255.0) - np.array(MEAN, np.float32)) / np.array(STD, np.float32)
+    got = m.infer_prepared(chw.transpose(0, 3, 1, 2))
+    got2 = m.infer_prepared(chw.transpose(0, 3, 1, 2))      # second call: the captured graph
+    for k in ref:
+        assert np.array_equal(got[k], ref[k]), k
+        assert np.array_equal(got2[k], ref[k]), k
