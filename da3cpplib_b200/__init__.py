@@ -75,6 +75,16 @@ class Model:
             out["rays"] = ray
         return out
 
+    def pose(self, n):
+        """Camera pose of the n views of the last run: (pose_enc [n][9], ext [n][3][4], intr [n][3][3])."""
+        pe = np.empty((n, 9), np.float32)
+        ext = np.empty((n, 3, 4), np.float32)
+        intr = np.empty((n, 3, 3), np.float32)
+        rc = self.lib.da3b_last_pose(self.ctx, n, pe.ctypes.data, ext.ctypes.data, intr.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(f"da3b_last_pose failed ({rc}): {self.last_error}")
+        return pe, ext, intr
+
     def infer_prepared(self, chw: np.ndarray):
         """Normalised planar f32 images [n][3][h][w] (host) -> dict of numpy outputs
         (the input of the reference's infer_preprocessed)."""

@@ -17,6 +17,7 @@
 #include "da3cpp/da3.h"
 #include "da3cpp/da3_c.h"
 #include "engine.h"
+#include "pose.h"
 #include "preprocess.h"
 
 #define DA_LOG(...)                     \
@@ -231,10 +232,11 @@ bool infer(Model& model, const Image& image, Result& result, const InferOptions&
     return false;
   da_ctx* c = model.ctx.get();
   const da3b::Engine& e = *c->engine;
-  if (options.with_pose || options.ray_pose) {
-    DA_LOG("infer: camera pose is outside the depth path of this library");
+  if (options.ray_pose) {
+    DA_LOG("infer: the ray-based pose solver is not part of this build");
     return false;
   }
+  if (options.with_pose && (e.config().is_da2() || !e.has_camera())) return false;
   if (is_mono(e)) {
     DA_LOG("infer: DA3 mono (sky head) checkpoints are not supported");
     return false;
@@ -251,6 +253,17 @@ bool infer(Model& model, const Image& image, Result& result, const InferOptions&
   result.height = H;
   result.width = W;
   result.is_metric = model_info(model).is_metric;
+  if (options.with_pose) {
+    // CamPose::pose on this forward's camera token (src/api.cpp:136-150, src/engine.cpp:271-286)
+    std::vector<float> pe;
+    if (c->engine->poses(pe, c->stream) != 0) {
+      DA_LOG("infer: camera pose failed: %s", c->engine->last_error().c_str());
+      result = {};
+      return false;
+    }
+    da3b::pose_to_ext_intr(pe.data(), H, W, result.extrinsics.data(), result.intrinsics.data());
+    result.has_pose = true;
+  }
   return !result.depth.empty();
 }
 
@@ -401,19 +414,36 @@ DA_CAPI float* da_capi_depth_path(da_ctx* c, const char* image_path, int* out_h,
   return p;
 }
 
+// src/da_capi.cpp:119-129: legacy preprocess, one view, camera-token pose.
 DA_CAPI int da_capi_pose_path(da_ctx* c, const char* image_path, float out_ext[12], float out_intr[9]) {
-  (void)image_path;
-  (void)out_ext;
-  (void)out_intr;
-  if (c) c->last_error = "pose: camera pose is outside the depth path of this library";
-  return -1;
+  if (!c || !c->engine || !image_path) {
+    if (c) c->last_error = "pose: bad args";
+    return -1;
+  }
+  if (c->engine->config().is_da2() || !c->engine->has_camera()) {
+    c->last_error = "pose: this model has no camera pose";
+    return -1;
+  }
+  int w = 0, h = 0;
+  std::vector<uint8_t> rgb;
+  if (!read_ppm(image_path, &w, &h, rgb, &c->last_error)) return -1;
+  std::vector<float> depth, conf, pe;
+  int H = 0, W = 0;
+  if (!run_one(c, rgb.data(), w, h, true, depth, &conf, &H, &W)) return -1;
+  if (c->engine->poses(pe, c->stream) != 0) {
+    c->last_error = "pose: " + c->engine->last_error();
+    return -1;
+  }
+  float ext[12], intr[9];
+  da3b::pose_to_ext_intr(pe.data(), H, W, ext, intr);
+  if (out_ext) memcpy(out_ext, ext, sizeof(ext));
+  if (out_intr) memcpy(out_intr, intr, sizeof(intr));
+  return 0;
 }
 
 // src/da_capi.cpp:130-155: legacy preprocess, one backbone pass over all views.
 DA_CAPI float* da_capi_depth_pose_multi(da_ctx* c, const char** paths, int n, int* out_h, int* out_w, int* out_n,
                                         float* out_ext, float* out_intr) {
-  (void)out_ext;
-  (void)out_intr;
   if (!c || !c->engine || !paths || n <= 0) {
     if (c) c->last_error = "depth_multi: bad args";
     return nullptr;
@@ -440,6 +470,21 @@ DA_CAPI float* da_capi_depth_pose_multi(da_ctx* c, const char** paths, int n, in
   if (da3b_infer_host(c, all.data(), n, n, H, W, p, nullptr, nullptr) != 0) {
     free(p);
     return nullptr;
+  }
+  if (out_ext || out_intr) {
+    // CamPose::pose per view (src/engine.cpp:372-381), original view order
+    std::vector<float> pe;
+    if (!c->engine->has_camera() || c->engine->poses(pe, c->stream) != 0) {
+      c->last_error = "depth_multi: camera pose failed: " + c->engine->last_error();
+      free(p);
+      return nullptr;
+    }
+    for (int i = 0; i < n; ++i) {
+      float ext[12], intr[9];
+      da3b::pose_to_ext_intr(&pe[static_cast<size_t>(i) * 9], H, W, ext, intr);
+      if (out_ext) memcpy(out_ext + static_cast<size_t>(i) * 12, ext, sizeof(ext));
+      if (out_intr) memcpy(out_intr + static_cast<size_t>(i) * 9, intr, sizeof(intr));
+    }
   }
   if (out_h) *out_h = H;
   if (out_w) *out_w = W;
@@ -517,6 +562,30 @@ DA3B_API int da3b_infer_device(da_ctx* c, const void* rgb_dev, int n_views, int 
                                 static_cast<float*>(rays_dev), static_cast<cudaStream_t>(stream));
   if (rc) c->last_error = c->engine->last_error();
   return rc;
+}
+
+DA3B_API int da3b_last_pose(da_ctx* c, int n_views, float* pose_enc, float* ext, float* intr) {
+  if (!c || !c->engine || n_views <= 0) return -1;
+  std::vector<float> pe;
+  const int rc = c->engine->poses(pe, c->stream);
+  if (rc) {
+    c->last_error = c->engine->last_error();
+    return rc - 10;
+  }
+  if (static_cast<int>(pe.size()) != n_views * 9) {
+    c->last_error = "last_pose: the last run had " + std::to_string(pe.size() / 9) + " views";
+    return -2;
+  }
+  int H = 0, W = 0;
+  c->engine->last_size(&H, &W);
+  for (int v = 0; v < n_views; ++v) {
+    if (pose_enc) memcpy(pose_enc + v * 9, &pe[static_cast<size_t>(v) * 9], 9 * sizeof(float));
+    float e[12], k[9];
+    da3b::pose_to_ext_intr(&pe[static_cast<size_t>(v) * 9], H, W, e, k);
+    if (ext) memcpy(ext + v * 12, e, sizeof(e));
+    if (intr) memcpy(intr + v * 9, k, sizeof(k));
+  }
+  return 0;
 }
 
 DA3B_API int da3b_infer_prepared(da_ctx* c, const float* chw, int n_views, int h, int w, float* depth, float* conf,

@@ -83,6 +83,9 @@ struct Plan {
   // first use, with its own captured graph (the first kernel reads it instead of rgb)
   float* chw = nullptr;
   bool prepared = false;
+  // camera tokens of out-layer 3 in processing order [V][Cf] f32 and the camera
+  // decoder's activations [V][hidden] x 2 and pose encodings [V][9] (DA3 with cam.*)
+  float *cam = nullptr, *cam_h1 = nullptr, *cam_h2 = nullptr, *cam_pe = nullptr;
   cudaGraphExec_t graph_pre = nullptr;
   bool warmed_pre = false;
   ~Plan() {
@@ -316,6 +319,12 @@ Plan* Engine::plan_for(int V, int S, int H, int W, bool rays) {
     if (hd.norm_g)
       for (int o = 0; o < 4; ++o) T(p->featn[o], V_ * Np * p->Cf);
     T(p->b_idx, static_cast<size_t>(std::max(1, p->scenes)));
+    if (model_->camdec.present) {
+      T(p->cam, V_ * p->Cf);
+      T(p->cam_h1, V_ * model_->camdec.bb0.N);
+      T(p->cam_h2, V_ * model_->camdec.bb2.N);
+      T(p->cam_pe, V_ * 9);
+    }
     for (int s = 0; s < 4; ++s) T(p->P[s], V_ * Np * oc[s]);
     T(p->L0, V_ * (4 * gh) * (4 * gw) * oc[0]);
     T(p->L1, V_ * (2 * gh) * (2 * gw) * oc[1]);
@@ -463,7 +472,10 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
       bool all_global = true;
       for (int i = j + 1; i <= L; ++i)
         if (!is_global(c, i)) all_global = false;
-      if (all_global) CK(cast_rows(p.x, D, V * Np, D, p.feats[o], p.Cf, 0, Np, Nt, 1, s));
+      if (all_global) {
+        CK(cast_rows(p.x, D, V * Np, D, p.feats[o], p.Cf, 0, Np, Nt, 1, s));
+        if (o == 3 && p.cam) CK(copy_token0(p.x, V, Nt, D, p.cam, p.Cf, 0, s));  // local half of the camera token
+      }
     }
     return 0;
   };
@@ -535,6 +547,7 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
       // DA3: cat[local_x, LN(x)] (src/dino_backbone.cpp:296-306). Token 0 dropped.
       CK(layernorm_f32(p.x, D, V * Np, D, m.norm_g, m.norm_b, c.ln_eps, p.feats[o], p.Cf, c.cat_token ? D : 0, Np, Nt,
                        1, s));
+      if (o == 3 && p.cam) CK(copy_token0(p.x, V, Nt, D, p.cam, p.Cf, c.cat_token ? D : 0, s));  // raw x half
     }
   }
   if (select) {
@@ -836,6 +849,59 @@ int Engine::copy_out(Plan* p, float* depth, float* conf, float* rays, cudaStream
     if (cudaMemcpyAsync(rays, p->raysbuf, n * 4, cudaMemcpyDefault, s) != cudaSuccess) return -12;
   }
   return 0;
+}
+
+// Camera decoder on the camera tokens of the last run (CamPose::pose,
+// src/cam_pose.cpp:20-38): pose encodings [V][9], in the original view order.
+int Engine::poses(std::vector<float>& pe, cudaStream_t s) {
+  const CamDec& cd = model_->camdec;
+  if (!cd.present) {
+    err_ = "this GGUF has no camera decoder (cam.*)";
+    return -1;
+  }
+  if (!last_ || !last_->cam) {
+    err_ = "no run to take camera tokens from";
+    return -2;
+  }
+  Plan& p = *last_;
+  const int V = p.V;
+  if (cd.bb0.K != p.Cf) {
+    err_ = "camera decoder input width does not match the camera token";
+    return -3;
+  }
+  cudaSetDevice(device_);
+  int rc = gemv_rows(p.cam, V, cd.bb0.K, cd.bb0.w, cd.bb0.ldw, cd.bb0.b, cd.bb0.N, 1, p.cam_h1, cd.bb0.N, 0, s);
+  if (!rc) rc = gemv_rows(p.cam_h1, V, cd.bb2.K, cd.bb2.w, cd.bb2.ldw, cd.bb2.b, cd.bb2.N, 1, p.cam_h2, cd.bb2.N, 0, s);
+  if (!rc) rc = gemv_rows(p.cam_h2, V, cd.fc_t.K, cd.fc_t.w, cd.fc_t.ldw, cd.fc_t.b, 3, 0, p.cam_pe, 9, 0, s);
+  if (!rc) rc = gemv_rows(p.cam_h2, V, cd.fc_q.K, cd.fc_q.w, cd.fc_q.ldw, cd.fc_q.b, 4, 0, p.cam_pe, 9, 3, s);
+  if (!rc) rc = gemv_rows(p.cam_h2, V, cd.fc_fov.K, cd.fc_fov.w, cd.fc_fov.ldw, cd.fc_fov.b, 2, 1, p.cam_pe, 9, 7, s);
+  std::vector<float> proc(static_cast<size_t>(V) * 9);
+  if (rc || cudaMemcpyAsync(proc.data(), p.cam_pe, proc.size() * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess) {
+    err_ = "camera decoder launch failed";
+    return -4;
+  }
+  pe.assign(proc.size(), 0.f);
+  const bool select = p.S >= 3 && model_->cfg.alt_start >= 0;
+  std::vector<int> ref(p.scenes, 0);
+  if (select) {
+    if (cudaMemcpy(ref.data(), p.b_idx, ref.size() * sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -5;
+  }
+  for (int sc = 0; sc < p.scenes; ++sc)
+    for (int q = 0; q < p.S; ++q) {
+      // processing position q holds original view: the reference view first, then the
+      // others in order (src/dino_backbone.cpp:427-441)
+      const int b = ref[sc];
+      const int t = !select ? q : (q == 0 ? b : (q <= b ? q - 1 : q));
+      std::copy(&proc[(static_cast<size_t>(sc) * p.S + q) * 9], &proc[(static_cast<size_t>(sc) * p.S + q) * 9] + 9,
+                &pe[(static_cast<size_t>(sc) * p.S + t) * 9]);
+    }
+  return 0;
+}
+
+void Engine::last_size(int* H, int* W) const {
+  *H = last_ ? last_->H : 0;
+  *W = last_ ? last_->W : 0;
 }
 
 std::vector<int> Engine::last_ref_views(cudaStream_t s) {

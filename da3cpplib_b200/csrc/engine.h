@@ -48,6 +48,13 @@ class Engine {
   float* prepared_input(int V, int H, int W, size_t* bytes);
   int run_prepared(int V, int H, int W, float* depth, float* conf, cudaStream_t s);
 
+  // Camera decoder on the last run's camera tokens: pose encodings [n_views][9]
+  // ([t(3), quaternion xyzw (4), fov h/w (2)]) in the original view order.
+  int poses(std::vector<float>& pe, cudaStream_t s);
+  bool has_camera() const { return model_->camdec.present; }
+  // Processed size of the last run (0 x 0 before any).
+  void last_size(int* H, int* W) const;
+
   // Selected reference view per scene of the last run with views_per_scene >= 3 (host copy).
   std::vector<int> last_ref_views(cudaStream_t s);
   // Kernel launches of one forward of the given shape (after a run of that shape).

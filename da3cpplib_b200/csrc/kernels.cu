@@ -503,3 +503,53 @@ int unpermute_views_h(const __half* src, __half* dst, int scenes, int S, long vi
 }
 
 }  // namespace da3b
+
+namespace da3b {
+
+// ---------------------------------------------------------------- camera token / pose MLP
+// dst[v][col_off + e] = x[v*Nt + 0][e]: token 0 of every view (f32), the camera token
+// halves (src/dino_backbone.cpp:197-201).
+__global__ void k_copy_token0(const float* __restrict__ x, int V, int Nt, int D, float* __restrict__ dst, int ld_dst,
+                              int col_off) {
+  const int total = V * D;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int v = i / D, e = i - v * D;
+    dst[static_cast<size_t>(v) * ld_dst + col_off + e] = x[static_cast<size_t>(v) * Nt * D + e];
+  }
+}
+int copy_token0(const float* x, int V, int Nt, int D, float* dst, int ld_dst, int col_off, cudaStream_t s) {
+  if (V <= 0 || D <= 0) return 0;
+  k_copy_token0<<<grid_for(static_cast<long>(V) * D, 256), 256, 0, s>>>(x, V, Nt, D, dst, ld_dst, col_off);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+// y[m][y_off + n] = act(sum_k x[m][k] W[n][k] + b[n]) for a handful of rows m (the
+// camera decoder's M = views): one warp per output column n, f32 activations, f16
+// weights, f32 accumulation.
+__global__ void k_gemv_rows(const float* __restrict__ x, int M, int K, const __half* __restrict__ W, int ldw,
+                            const float* __restrict__ b, int N, int act, float* __restrict__ y, int ldy, int y_off) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= N) return;
+  const __half* w = W + static_cast<size_t>(warp) * ldw;
+  for (int m = 0; m < M; ++m) {
+    const float* xr = x + static_cast<size_t>(m) * K;
+    float acc = 0.f;
+    for (int k = lane; k < K; k += 32) acc = fmaf(__half2float(w[k]), xr[k], acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      float v = acc + (b ? b[warp] : 0.f);
+      if (act == 1) v = fmaxf(v, 0.f);
+      y[static_cast<size_t>(m) * ldy + y_off + warp] = v;
+    }
+  }
+}
+int gemv_rows(const float* x, int M, int K, const __half* W, int ldw, const float* b, int N, int act, float* y,
+              int ldy, int y_off, cudaStream_t s) {
+  if (M <= 0 || N <= 0) return 0;
+  const int threads = 256, warps = threads / 32;
+  k_gemv_rows<<<(N + warps - 1) / warps, threads, 0, s>>>(x, M, K, W, ldw, b, N, act, y, ldy, y_off);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+}  // namespace da3b

@@ -41,4 +41,9 @@ int attention_tc(const __half* qkv, const __half* vt, int ld_vt, int nseq, int s
 
 
 
+// Camera token capture and the camera decoder's small-M GEMV (kernels.cu).
+int copy_token0(const float* x, int V, int Nt, int D, float* dst, int ld_dst, int col_off, cudaStream_t s);
+int gemv_rows(const float* x, int M, int K, const __half* W, int ldw, const float* b, int N, int act, float* y,
+              int ldy, int y_off, cudaStream_t s);
+
 }  // namespace da3b

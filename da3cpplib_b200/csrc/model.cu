@@ -309,6 +309,21 @@ std::unique_ptr<DeviceModel> DeviceModel::load(const std::string& path, std::str
       return nullptr;
     }
   }
+  if (m->file.tensor("cam.bb0.weight")) {
+    CamDec& cd = m->camdec;
+    if (!m->lin_q8("cam.bb0.weight", "cam.bb0.bias", cd.bb0, err) ||
+        !m->lin_q8("cam.bb2.weight", "cam.bb2.bias", cd.bb2, err) ||
+        !m->lin_q8("cam.fc_t.weight", "cam.fc_t.bias", cd.fc_t, err) ||
+        !m->lin_q8("cam.fc_q.weight", "cam.fc_q.bias", cd.fc_q, err) ||
+        !m->lin_q8("cam.fc_fov.weight", "cam.fc_fov.bias", cd.fc_fov, err))
+      return nullptr;
+    if (cd.bb2.K != cd.bb0.N || cd.fc_t.K != cd.bb2.N || cd.fc_q.K != cd.bb2.N || cd.fc_fov.K != cd.bb2.N ||
+        cd.fc_t.N != 3 || cd.fc_q.N != 4 || cd.fc_fov.N != 2) {
+      if (err) *err = "camera decoder shapes do not chain";
+      return nullptr;
+    }
+    cd.present = true;
+  }
   // ---- DPT head (tensor names: src/dpt_head.cpp:108-272)
   Head& h = m->head;
   if (m->file.tensor("head.norm.weight")) {

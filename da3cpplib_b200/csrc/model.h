@@ -78,6 +78,13 @@ struct Head {
   int aux_od = 0;
 };
 
+// Camera decoder of DA3 (src/cam_pose.cpp:20-32): relu(bb0) -> relu(bb2) -> fc_t (3) |
+// fc_q (4) | relu(fc_fov) (2) on the out-layer-3 camera token.
+struct CamDec {
+  bool present = false;
+  Lin bb0, bb2, fc_t, fc_q, fc_fov;
+};
+
 class DeviceModel {
  public:
   ~DeviceModel();
@@ -94,6 +101,7 @@ class DeviceModel {
   float *norm_g = nullptr, *norm_b = nullptr;
   std::vector<Block> blk;
   Head head;
+  CamDec camdec;
   size_t weight_bytes = 0;
 
   // host views used for per-resolution tables

@@ -169,6 +169,13 @@ DA3B_API int da3b_infer_host(da_ctx* ctx, const void* rgb_host, int n_views, int
 DA3B_API int da3b_infer_prepared(da_ctx* ctx, const float* chw, int n_views, int h, int w, float* depth, float* conf,
                                  void* stream);
 
+/* Camera pose of the n_views views of the last run (DA3 checkpoints with a camera
+ * decoder, cam.*): the camera-token MLP of CamPose::pose (src/cam_pose.cpp:8-83) on the
+ * out-layer-3 camera tokens, in the original view order. pose_enc [n][9] = t(3),
+ * quaternion xyzw (4), fov h/w (2); ext [n][12] world-to-camera 3x4; intr [n][9].
+ * Host arrays, each may be NULL. */
+DA3B_API int da3b_last_pose(da_ctx* ctx, int n_views, float* pose_enc, float* ext, float* intr);
+
 /* Reference view chosen per scene by the last multi-view run (views_per_scene >= 3). */
 DA3B_API int da3b_ref_views(da_ctx* ctx, int* out, int n);
 /* Kernel launches of one forward of that shape (after one run of it). */

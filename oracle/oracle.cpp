@@ -722,7 +722,7 @@ class Oracle {
   // out-layer features [S][Npatch][C] (src/dino_backbone.cpp:80-213, 462-616).
   // upto >= 0 stops after block upto-1 and returns x (pass A helper).
   void backbone(const std::vector<std::vector<float>>& views, int H, int W, std::vector<std::vector<float>>& feats,
-                int upto, std::vector<float>* x_out) {
+                int upto, std::vector<float>* x_out, std::vector<std::vector<float>>* cams = nullptr) {
     const int P = c.patch_size, gh = H / P, gw = W / P, Np = gh * gw, Nt = 1 + Np, E = c.embed_dim;
     const int S = static_cast<int>(views.size());
     std::vector<float> pos = interp_pos_embed(gh, gw);
@@ -742,6 +742,7 @@ class Oracle {
     std::vector<float> local_x = x;
     const int NL = c.n_out_layers;
     feats.assign(NL, std::vector<float>());
+    if (cams) cams->assign(NL, std::vector<float>());
     const int depth = upto >= 0 ? upto : c.depth;
     for (int i = 0; i < depth; ++i) {
       if (c.alt_start >= 0 && i == c.alt_start) {
@@ -773,9 +774,70 @@ class Oracle {
             }
           }
           feats[o] = std::move(f);
+          if (cams) {
+            // camera token (src/dino_backbone.cpp:187-201, :598-601): token 0, raw (no norm):
+            // cat(local_x, x) for cat-token models, x alone otherwise; [S][Cf]
+            std::vector<float> cv(static_cast<size_t>(S) * Cf);
+            for (int s2 = 0; s2 < S; ++s2) {
+              const float* xr = &x[static_cast<size_t>(s2) * Nt * E];
+              float* dst = &cv[static_cast<size_t>(s2) * Cf];
+              if (c.cat_token) {
+                const float* lr = &local_x[static_cast<size_t>(s2) * Nt * E];
+                for (int e = 0; e < E; ++e) dst[e] = lr[e];
+                for (int e = 0; e < E; ++e) dst[E + e] = xr[e];
+              } else {
+                for (int e = 0; e < E; ++e) dst[e] = xr[e];
+              }
+            }
+            (*cams)[o] = std::move(cv);
+          }
         }
     }
     if (x_out) *x_out = x;
+  }
+
+  // CamPose::pose (src/cam_pose.cpp:8-83): camera-token MLP -> pose encoding
+  // [t(3), quaternion xyzw (4), fov h/w (2)] -> extrinsics (3x4 world-to-camera) and
+  // intrinsics (3x3) at the processed size H x W. out[0..9) pose_enc, [9..21) ext,
+  // [21..30) intr. Returns false without camera weights or on a width mismatch.
+  bool pose(const float* cam_token, int D, int H, int W, float* out) {
+    if (!has("cam.bb0.weight") || T("cam.bb0.weight").ne[0] != D) return false;
+    auto lin = [&](const std::vector<float>& in, const std::string& n, bool relu) {
+      const Tensor& w = T("cam." + n + ".weight");
+      std::vector<float> y(static_cast<size_t>(w.ne[1]));
+      linear(in.data(), 1, static_cast<int>(w.ne[0]), "cam." + n + ".weight", "cam." + n + ".bias", y.data());
+      if (relu)
+        for (auto& v : y) v = std::max(0.0f, v);
+      return y;
+    };
+    std::vector<float> f(cam_token, cam_token + D);
+    f = lin(f, "bb0", true);
+    f = lin(f, "bb2", true);
+    const std::vector<float> t3 = lin(f, "fc_t", false), q4 = lin(f, "fc_q", false), fv = lin(f, "fc_fov", true);
+    const float pe[9] = {t3[0], t3[1], t3[2], q4[0], q4[1], q4[2], q4[3], fv[0], fv[1]};
+    for (int i = 0; i < 9; ++i) out[i] = pe[i];
+    const float qi = pe[3], qj = pe[4], qk = pe[5], qr = pe[6];
+    const float sc = 2.0f / (qi * qi + qj * qj + qk * qk + qr * qr);
+    const float R[3][3] = {{1.0f - sc * (qj * qj + qk * qk), sc * (qi * qj - qk * qr), sc * (qi * qk + qj * qr)},
+                           {sc * (qi * qj + qk * qr), 1.0f - sc * (qi * qi + qk * qk), sc * (qj * qk - qi * qr)},
+                           {sc * (qi * qk - qj * qr), sc * (qj * qk + qi * qr), 1.0f - sc * (qi * qi + qj * qj)}};
+    const float fy = (H / 2.0f) / std::max(std::tan(pe[7] / 2.0f), 1e-6f);
+    const float fx = (W / 2.0f) / std::max(std::tan(pe[8] / 2.0f), 1e-6f);
+    float* ext = out + 9;
+    float* intr = out + 21;
+    for (int r = 0; r < 3; ++r) {
+      float acc = 0.0f;
+      for (int k = 0; k < 3; ++k) acc += R[k][r] * pe[k];
+      for (int k = 0; k < 3; ++k) ext[r * 4 + k] = R[k][r];
+      ext[r * 4 + 3] = -acc;
+    }
+    for (int i = 0; i < 9; ++i) intr[i] = 0.0f;
+    intr[0] = fx;
+    intr[4] = fy;
+    intr[2] = W / 2.0f;
+    intr[5] = H / 2.0f;
+    intr[8] = 1.0f;
+    return true;
   }
 
   // select_reference_view_saddle (src/dino_backbone.cpp:372-412).
@@ -1015,7 +1077,7 @@ bool preprocess(const Img& img, const or_config& c, bool legacy, std::vector<flo
 
 struct Handle {
   Oracle o;
-  std::vector<float> depth, conf, logits, aux, chw;
+  std::vector<float> depth, conf, logits, aux, chw, pose;
   std::vector<std::vector<float>> feats;
   int H = 0, W = 0, od = 0, aux_h = 0, aux_w = 0, b_idx = 0;
 };
@@ -1123,9 +1185,12 @@ OR_API int or_infer(void* p, const uint8_t* rgb, int w, int hgt, int legacy, int
   h->H = H;
   h->W = W;
   std::vector<std::vector<float>> views{h->chw};
-  o.backbone(views, H, W, h->feats, -1, nullptr);
+  std::vector<std::vector<float>> cams;
+  o.backbone(views, H, W, h->feats, -1, nullptr, &cams);
   if (static_cast<int>(h->feats.size()) < 4) return -2;
   const int Cf = (o.c.cat_token ? 2 : 1) * o.c.embed_dim;
+  h->pose.assign(30, 0.f);
+  if (!o.pose(cams[3].data(), Cf, H, W, h->pose.data())) h->pose.clear();
   std::vector<const float*> f4 = {h->feats[0].data(), h->feats[1].data(), h->feats[2].data(), h->feats[3].data()};
   Oracle::Map aux;
   Oracle::Map lg = o.head(f4, Cf, H, W, want_aux != 0, &aux, "");
@@ -1188,10 +1253,11 @@ OR_API int or_infer_mv(void* p, const uint8_t* const* rgbs, int S, int w, int hg
   h->b_idx = b_idx;
   std::vector<std::vector<float>> rv(S);
   for (int q = 0; q < S; ++q) rv[q] = views[order[q]];
-  std::vector<std::vector<float>> feats;
-  o.backbone(rv, H, W, feats, -1, nullptr);
+  std::vector<std::vector<float>> feats, cams;
+  o.backbone(rv, H, W, feats, -1, nullptr, &cams);
   const int Cf = (o.c.cat_token ? 2 : 1) * E;
   const int Np = Nt - 1;
+  h->pose.assign(static_cast<size_t>(S) * 30, 0.f);
   const size_t HW = static_cast<size_t>(H) * W;
   h->depth.assign(HW * S, 0.f);
   h->conf.assign(HW * S, 0.f);
@@ -1207,6 +1273,7 @@ OR_API int or_infer_mv(void* p, const uint8_t* const* rgbs, int S, int w, int hg
       f4.push_back(&feats[l][static_cast<size_t>(q) * Np * Cf]);
       memcpy(&h->feats[l][static_cast<size_t>(t) * Np * Cf], f4.back(), static_cast<size_t>(Np) * Cf * 4);
     }
+    if (!o.pose(&cams[3][static_cast<size_t>(q) * Cf], Cf, H, W, &h->pose[static_cast<size_t>(t) * 30])) h->pose.clear();
     Oracle::Map aux;
     Oracle::Map lg = o.head(f4, Cf, H, W, want_aux != 0, &aux, "v" + std::to_string(t) + ".");
     h->od = lg.C;
@@ -1222,7 +1289,7 @@ OR_API int or_infer_mv(void* p, const uint8_t* const* rgbs, int S, int w, int hg
   return 0;
 }
 
-// Accessors: name in {"depth","conf","logits","aux","chw","feat0".."feat3"} or a
+// Accessors: name in {"depth","conf","logits","aux","chw","pose","feat0".."feat3"} or a
 // capture key ("stage0".."stage3","out1", "v<k>.stage0"...). Returns element count.
 OR_API int64_t or_get(void* p, const char* name, const float** out) {
   auto* h = static_cast<Handle*>(p);
@@ -1233,6 +1300,7 @@ OR_API int64_t or_get(void* p, const char* name, const float** out) {
   else if (n == "logits") v = &h->logits;
   else if (n == "aux") v = &h->aux;
   else if (n == "chw") v = &h->chw;
+  else if (n == "pose") v = &h->pose;
   else if (n.size() == 5 && n.compare(0, 4, "feat") == 0) {
     const int l = n[4] - '0';
     if (l >= 0 && l < static_cast<int>(h->feats.size())) v = &h->feats[l];

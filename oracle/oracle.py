@@ -264,6 +264,9 @@ class Oracle:
             out["conf"] = conf.reshape(H, W)
         if aux and ah > 0:
             out["aux"] = self.get("aux").reshape(7, ah, aw)
+        pose = self.get("pose")
+        if pose is not None and pose.size:  # [9 pose encoding | 12 extrinsics | 9 intrinsics]
+            out["pose"] = pose.reshape(30)
         return out
 
     def infer_mv(self, rgbs, legacy=True, aux=False):
@@ -279,6 +282,9 @@ class Oracle:
                "conf": self.get("conf").reshape(S, H, W), "logits": self.get("logits").reshape(S, od, H, W)}
         if aux and ah > 0:
             out["aux"] = self.get("aux").reshape(S, 7, ah, aw)
+        pose = self.get("pose")
+        if pose is not None and pose.size:
+            out["pose"] = pose.reshape(S, 30)
         return out
 
 
