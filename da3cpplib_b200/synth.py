@@ -184,19 +184,6 @@ def tensors_for(spec: ModelSpec, seed: int, stress: bool = False):
     add("head.scratch.out2a.bias", n(32))
     add("head.scratch.out2b.weight", lw(spec.output_dim, 32, 1, 1, fan_in=32))
     add("head.scratch.out2b.bias", n(spec.output_dim))
-    if spec.camera_token:
-        # camera decoder (src/cam_pose.cpp:20-32): relu(bb0) -> relu(bb2) -> fc_t | fc_q | relu(fc_fov)
-        Ccam = C
-        add("cam.bb0.weight", _q8_0(lw(Ccam, Ccam, fan_in=Ccam)), GGML_Q8_0)
-        add("cam.bb0.bias", n(Ccam))
-        add("cam.bb2.weight", _q8_0(lw(Ccam, Ccam, fan_in=Ccam)), GGML_Q8_0)
-        add("cam.bb2.bias", n(Ccam))
-        add("cam.fc_t.weight", _q8_0(lw(3, Ccam, fan_in=Ccam)), GGML_Q8_0)
-        add("cam.fc_t.bias", n(3))
-        add("cam.fc_q.weight", _q8_0(lw(4, Ccam, fan_in=Ccam)), GGML_Q8_0)
-        add("cam.fc_q.bias", n(4) + np.array([0, 0, 0, 1], np.float32))
-        add("cam.fc_fov.weight", _q8_0(lw(2, Ccam, fan_in=Ccam)), GGML_Q8_0)
-        add("cam.fc_fov.bias", n(2) + np.float32(1.0))
     if spec.aux:
         pyramid("_aux")
         chans = [F, F // 2, F, F // 2, F, F // 2]
@@ -209,6 +196,20 @@ def tensors_for(spec: ModelSpec, seed: int, stress: bool = False):
         add("head.scratch.out2_aux_ln.bias", n(32))
         add("head.scratch.out2b_aux.weight", lw(7, 32, 1, 1, fan_in=32))
         add("head.scratch.out2b_aux.bias", n(7))
+    if spec.camera_token:
+        # camera decoder (src/cam_pose.cpp:20-32): relu(bb0) -> relu(bb2) -> fc_t | fc_q |
+        # relu(fc_fov); drawn last so every earlier tensor keeps its seeded values
+        Ccam = C
+        add("cam.bb0.weight", _q8_0(lw(Ccam, Ccam, fan_in=Ccam)), GGML_Q8_0)
+        add("cam.bb0.bias", n(Ccam))
+        add("cam.bb2.weight", _q8_0(lw(Ccam, Ccam, fan_in=Ccam)), GGML_Q8_0)
+        add("cam.bb2.bias", n(Ccam))
+        add("cam.fc_t.weight", _q8_0(lw(3, Ccam, fan_in=Ccam)), GGML_Q8_0)
+        add("cam.fc_t.bias", n(3))
+        add("cam.fc_q.weight", _q8_0(lw(4, Ccam, fan_in=Ccam)), GGML_Q8_0)
+        add("cam.fc_q.bias", n(4) + np.array([0, 0, 0, 1], np.float32))
+        add("cam.fc_fov.weight", _q8_0(lw(2, Ccam, fan_in=Ccam)), GGML_Q8_0)
+        add("cam.fc_fov.bias", n(2) + np.float32(1.0))
     return out
 
 
