@@ -17,6 +17,7 @@
 #include "da3cpp/da3.h"
 #include "da3cpp/da3_c.h"
 #include "engine.h"
+#include "kernels.h"
 #include "pose.h"
 #include "preprocess.h"
 
@@ -102,6 +103,54 @@ bool is_mono(const da3b::Engine& e) {
   return e.model().file.tensor("head.scratch.sky_out2b.weight") != nullptr && e.output_dim() == 1;
 }
 
+// Legacy preprocess on the GPU (src/preprocess.cpp:8-41, bit-exact): upload n views,
+// float bilinear to the floor-to-patch size and normalisation straight into the plan's
+// planar f32 input, then the forward from it (scenes of S views).
+bool run_legacy(da_ctx* c, const uint8_t* rgb, int n, int S, int w, int h, std::vector<float>& depth,
+                std::vector<float>* conf, int* oh, int* ow) {
+  da3b::Engine& e = *c->engine;
+  cudaSetDevice(e.device());
+  const auto& cfg = e.config();
+  int W = 0, H = 0;
+  if (da3b::legacy_preprocess(nullptr, n, w, h, cfg.patch_size, cfg.img_mean.data(), cfg.img_std.data(), nullptr, &W,
+                              &H, c->stream) != 0) {
+    c->last_error = "preprocess: bad legacy size";
+    return false;
+  }
+  const size_t in_bytes = static_cast<size_t>(n) * w * h * 3;
+  if (in_bytes > c->in_cap) {
+    if (c->in_dev) {
+      cudaStreamSynchronize(c->stream);
+      cudaFree(c->in_dev);
+    }
+    c->in_dev = nullptr;
+    c->in_cap = 0;
+    if (cudaMalloc(&c->in_dev, in_bytes) != cudaSuccess) {
+      c->last_error = "preprocess: out of device memory";
+      return false;
+    }
+    c->in_cap = in_bytes;
+  }
+  float* chw = e.prepared_input(n, S, H, W, nullptr);
+  if (!chw || cudaMemcpyAsync(c->in_dev, rgb, in_bytes, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+      da3b::legacy_preprocess(c->in_dev, n, w, h, cfg.patch_size, cfg.img_mean.data(), cfg.img_std.data(), chw, &W, &H,
+                              c->stream) != 0) {
+    c->last_error = "preprocess: legacy resize failed " + e.last_error();
+    return false;
+  }
+  depth.resize(static_cast<size_t>(n) * H * W);
+  const bool want_conf = conf && e.output_dim() >= 2;
+  if (want_conf) conf->resize(depth.size());
+  const int rc = e.run_prepared(n, S, H, W, depth.data(), want_conf ? conf->data() : nullptr, c->stream);
+  if (rc != 0 || cudaStreamSynchronize(c->stream) != cudaSuccess || e.status() != 0) {
+    c->last_error = "depth: forward failed: " + e.last_error();
+    return false;
+  }
+  *oh = H;
+  *ow = W;
+  return true;
+}
+
 // Single-image inference at the processed size (H2D, forward, D2H).
 bool run_one(da_ctx* c, const uint8_t* rgb, int w, int h, bool legacy, std::vector<float>& depth,
              std::vector<float>* conf, int* oh, int* ow) {
@@ -109,11 +158,7 @@ bool run_one(da_ctx* c, const uint8_t* rgb, int w, int h, bool legacy, std::vect
   int W = 0, H = 0;
   processed_size(e.config(), w, h, legacy, &W, &H);
   if (W != w || H != h) {
-    if (legacy) {
-      c->last_error = "input " + std::to_string(w) + "x" + std::to_string(h) + " needs the legacy bilinear resize to " +
-                      std::to_string(W) + "x" + std::to_string(H) + ", which this build does not run on the GPU";
-      return false;
-    }
+    if (legacy) return run_legacy(c, rgb, 1, 1, w, h, depth, conf, oh, ow);
     // preprocess_real on the GPU (src/preprocess.cpp:157-197): upload, resize, then the
     // processed image feeds the forward below
     cudaSetDevice(e.device());
@@ -288,7 +333,7 @@ bool infer_preprocessed(Model& model, int height, int width, const UploadCallbac
   da3b::Engine& e = *c->engine;
   if (e.config().is_da2() || is_mono(e)) return false;
   size_t bytes = 0;
-  float* dst = e.prepared_input(1, height, width, &bytes);
+  float* dst = e.prepared_input(1, 1, height, width, &bytes);
   if (!dst) {
     DA_LOG("infer_preprocessed: %s", e.last_error().c_str());
     return false;
@@ -298,8 +343,8 @@ bool infer_preprocessed(Model& model, int height, int width, const UploadCallbac
   const bool want_conf = e.output_dim() >= 2;
   if (want_conf) result.confidence.resize(result.depth.size());
   cudaSetDevice(e.device());
-  const int rc = e.run_prepared(1, height, width, result.depth.data(), want_conf ? result.confidence.data() : nullptr,
-                                c->stream);
+  const int rc = e.run_prepared(1, 1, height, width, result.depth.data(),
+                                want_conf ? result.confidence.data() : nullptr, c->stream);
   if (rc != 0 || cudaStreamSynchronize(c->stream) != cudaSuccess || e.status() != 0) {
     DA_LOG("infer_preprocessed: forward failed: %s", e.last_error().c_str());
     result = {};
@@ -460,16 +505,21 @@ DA_CAPI float* da_capi_depth_pose_multi(da_ctx* c, const char** paths, int n, in
   }
   int W = 0, H = 0;
   processed_size(c->engine->config(), w0, h0, true, &W, &H);
+  float* p = nullptr;
   if (W != w0 || H != h0) {
-    c->last_error = "depth_multi: views need a resize, which this build does not run on the GPU";
-    return nullptr;
-  }
-  const size_t per = static_cast<size_t>(H) * W;
-  float* p = static_cast<float*>(malloc(static_cast<size_t>(n) * per * sizeof(float)));
-  if (!p) { c->last_error = "depth_multi: oom"; return nullptr; }
-  if (da3b_infer_host(c, all.data(), n, n, H, W, p, nullptr, nullptr) != 0) {
-    free(p);
-    return nullptr;
+    std::vector<float> d;
+    if (!run_legacy(c, all.data(), n, n, w0, h0, d, nullptr, &H, &W)) return nullptr;
+    p = static_cast<float*>(malloc(d.size() * sizeof(float)));
+    if (!p) { c->last_error = "depth_multi: oom"; return nullptr; }
+    memcpy(p, d.data(), d.size() * sizeof(float));
+  } else {
+    const size_t per = static_cast<size_t>(H) * W;
+    p = static_cast<float*>(malloc(static_cast<size_t>(n) * per * sizeof(float)));
+    if (!p) { c->last_error = "depth_multi: oom"; return nullptr; }
+    if (da3b_infer_host(c, all.data(), n, n, H, W, p, nullptr, nullptr) != 0) {
+      free(p);
+      return nullptr;
+    }
   }
   if (out_ext || out_intr) {
     // CamPose::pose per view (src/engine.cpp:372-381), original view order
@@ -593,14 +643,14 @@ DA3B_API int da3b_infer_prepared(da_ctx* c, const float* chw, int n_views, int h
   if (!c || !c->engine || !chw || !depth || n_views <= 0 || h <= 0 || w <= 0) return -1;
   da3b::Engine& e = *c->engine;
   size_t bytes = 0;
-  float* dst = e.prepared_input(n_views, h, w, &bytes);
+  float* dst = e.prepared_input(n_views, 1, h, w, &bytes);
   if (!dst) {
     c->last_error = e.last_error();
     return -2;
   }
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
   if (cudaMemcpyAsync(dst, chw, bytes, cudaMemcpyDefault, s) != cudaSuccess) return -3;
-  const int rc = e.run_prepared(n_views, h, w, depth, conf, s);
+  const int rc = e.run_prepared(n_views, 1, h, w, depth, conf, s);
   if (rc) {
     c->last_error = e.last_error();
     return rc;

@@ -780,8 +780,8 @@ Plan* Engine::checked_plan(int V, int S, int H, int W, bool rays, int* code) {
   return p;
 }
 
-float* Engine::prepared_input(int V, int H, int W, size_t* bytes) {
-  Plan* p = checked_plan(V, 1, H, W, false, nullptr);
+float* Engine::prepared_input(int V, int S, int H, int W, size_t* bytes) {
+  Plan* p = checked_plan(V, S, H, W, false, nullptr);
   if (!p) return nullptr;
   const size_t n = static_cast<size_t>(V) * 3 * H * W;
   if (!p->chw && cudaMalloc(&p->chw, n * sizeof(float)) != cudaSuccess) {
@@ -793,8 +793,8 @@ float* Engine::prepared_input(int V, int H, int W, size_t* bytes) {
   return p->chw;
 }
 
-int Engine::run_prepared(int V, int H, int W, float* depth, float* conf, cudaStream_t s) {
-  if (!prepared_input(V, H, W, nullptr)) return -4;
+int Engine::run_prepared(int V, int S, int H, int W, float* depth, float* conf, cudaStream_t s) {
+  if (!prepared_input(V, S, H, W, nullptr)) return -4;
   Plan* p = last_;
   const int rc = launch(p, true, s);
   return rc ? rc : copy_out(p, depth, conf, nullptr, s);

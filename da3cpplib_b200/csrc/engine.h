@@ -42,11 +42,12 @@ class Engine {
   int run(const uint8_t* rgb_dev, int n_views, int views_per_scene, int H, int W, float* depth_dev,
           float* conf_dev, float* rays_dev, cudaStream_t s);
 
-  // Prepared-input runs (infer_preprocessed, src/api.cpp:178-193 / src/engine.cpp:230-270):
-  // device buffer for V normalised planar f32 images [V][3][H][W] of the plan of that
-  // shape (allocated on first use; *bytes its size), and the forward reading it.
-  float* prepared_input(int V, int H, int W, size_t* bytes);
-  int run_prepared(int V, int H, int W, float* depth, float* conf, cudaStream_t s);
+  // Prepared-input runs (infer_preprocessed, src/api.cpp:178-193 / src/engine.cpp:230-270;
+  // the legacy preprocess): device buffer for V normalised planar f32 images [V][3][H][W]
+  // (scenes of S views) of the plan of that shape (allocated on first use; *bytes its
+  // size), and the forward reading it.
+  float* prepared_input(int V, int S, int H, int W, size_t* bytes);
+  int run_prepared(int V, int S, int H, int W, float* depth, float* conf, cudaStream_t s);
 
   // Camera decoder on the last run's camera tokens: pose encodings [n_views][9]
   // ([t(3), quaternion xyzw (4), fov h/w (2)]) in the original view order.

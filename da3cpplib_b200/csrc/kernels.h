@@ -10,6 +10,10 @@ int patchify(const uint8_t* rgb, int B, int H, int W, int P, const float* mean, 
              cudaStream_t s);
 // Patchify of normalised planar f32 images [B][3][H][W] (no normalisation): the
 // prepared-input path.
+// Legacy preprocess (floor-to-patch float bilinear + normalisation) into planar f32
+// [B][3][*out_h][*out_w]; out == nullptr: size query only.
+int legacy_preprocess(const uint8_t* src, int B, int w, int h, int patch, const float* mean, const float* sd,
+                      float* out, int* out_w, int* out_h, cudaStream_t s);
 int patchify_chw(const float* chw, int B, int H, int W, int P, __half* out, int ldk, cudaStream_t s);
 int cls_rows(float* x, int B, int ntok, int D, const float* cls, const float* pos, cudaStream_t s);
 int cam_rows(float* x, int nviews_total, int views_per_scene, int ntok, int D, const float* cam, cudaStream_t s);

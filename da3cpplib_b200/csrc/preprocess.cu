@@ -432,6 +432,56 @@ __global__ void k_patchify_chw(const float* __restrict__ chw, int B, int H, int 
 
 }  // namespace
 
+// Legacy preprocess (src/preprocess.cpp:8-41): float bilinear resize of RGB8 to the
+// floor-to-patch size, then (v / 255 - mean[c]) / std[c] into planar f32 [B][3][dh][dw],
+// with the reference's f32 operations in its order (explicit rounding, no FMA).
+__global__ void k_legacy_pre(const uint8_t* __restrict__ src, int B, int sw, int sh, int dw, int dh, float sx, float sy,
+                             float m0, float m1, float m2, float s0, float s1, float s2, float* __restrict__ out) {
+  const long total = static_cast<long>(B) * 3 * dh * dw;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int x = static_cast<int>(i % dw);
+    const long r = i / dw;
+    const int y = static_cast<int>(r % dh);
+    const long r2 = r / dh;
+    const int c = static_cast<int>(r2 % 3);
+    const long b = r2 / 3;
+    const float fy = __fsub_rn(__fmul_rn(__fadd_rn(static_cast<float>(y), 0.5f), sy), 0.5f);
+    const int y0 = static_cast<int>(floorf(fy));
+    const float wy = __fsub_rn(fy, static_cast<float>(y0));
+    const int y0c = min(max(y0, 0), sh - 1), y1c = min(max(y0 + 1, 0), sh - 1);
+    const float fx = __fsub_rn(__fmul_rn(__fadd_rn(static_cast<float>(x), 0.5f), sx), 0.5f);
+    const int x0 = static_cast<int>(floorf(fx));
+    const float wx = __fsub_rn(fx, static_cast<float>(x0));
+    const int x0c = min(max(x0, 0), sw - 1), x1c = min(max(x0 + 1, 0), sw - 1);
+    const uint8_t* sp = src + static_cast<size_t>(b) * sh * sw * 3 + c;
+    auto P = [&](int yy, int xx) { return static_cast<float>(sp[(static_cast<size_t>(yy) * sw + xx) * 3]); };
+    const float iwx = __fsub_rn(1.f, wx), iwy = __fsub_rn(1.f, wy);
+    const float top = __fadd_rn(__fmul_rn(P(y0c, x0c), iwx), __fmul_rn(P(y0c, x1c), wx));
+    const float bot = __fadd_rn(__fmul_rn(P(y1c, x0c), iwx), __fmul_rn(P(y1c, x1c), wx));
+    const float v = __fdiv_rn(__fadd_rn(__fmul_rn(top, iwy), __fmul_rn(bot, wy)), 255.f);
+    const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2);
+    const float sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
+    out[i] = __fdiv_rn(__fsub_rn(v, mean), sd);
+  }
+}
+
+int legacy_preprocess(const uint8_t* src, int B, int w, int h, int patch, const float* mean, const float* sd,
+                      float* out, int* out_w, int* out_h, cudaStream_t s) {
+  if (B <= 0 || w <= 0 || h <= 0 || patch <= 0) return -1;
+  int dw = (w / patch) * patch, dh = (h / patch) * patch;
+  if (dw == 0) dw = patch;
+  if (dh == 0) dh = patch;
+  *out_w = dw;
+  *out_h = dh;
+  if (!out) return 0;
+  const float sx = static_cast<float>(w) / dw, sy = static_cast<float>(h) / dh;
+  const long total = static_cast<long>(B) * 3 * dh * dw;
+  k_legacy_pre<<<blocks_for(total), 256, 0, s>>>(src, B, w, h, dw, dh, sx, sy, mean[0], mean[1], mean[2], sd[0], sd[1],
+                                                 sd[2], out);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
 int patchify_chw(const float* chw, int B, int H, int W, int P, __half* out, int ldk, cudaStream_t s) {
   if (H % P || W % P || ldk % 8 || ldk < 3 * P * P || (reinterpret_cast<uintptr_t>(out) & 15)) return -1;
   const int gh = H / P, gw = W / P;
@@ -460,6 +510,13 @@ DA3B_API int da3b_resize_u8(const void* src, int B, int sw, int sh, void* dst, i
   if (!g_rs[dev]) g_rs[dev] = new da3b::Resizer();
   return g_rs[dev]->resize(static_cast<const uint8_t*>(src), B, sw, sh, static_cast<uint8_t*>(dst), dw, dh, mode,
                            static_cast<cudaStream_t>(stream));
+}
+
+DA3B_API int da3b_preprocess_legacy(const void* rgb, int B, int w, int h, int patch, const float* mean,
+                                    const float* std_, void* chw_out, int* out_h, int* out_w, void* stream) {
+  if (!rgb || !mean || !std_ || !out_h || !out_w) return -100;
+  return da3b::legacy_preprocess(static_cast<const uint8_t*>(rgb), B, w, h, patch, mean, std_,
+                                 static_cast<float*>(chw_out), out_w, out_h, static_cast<cudaStream_t>(stream));
 }
 
 DA3B_API int da3b_patchify(const void* rgb, int B, int H, int W, int patch, const float* mean, const float* std_,

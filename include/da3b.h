@@ -123,6 +123,13 @@ DA3B_API int da3b_upsample_nhwc(const void* in, int B, int hs, int ws, int C, vo
  * device, allocated on first use of a size. */
 DA3B_API int da3b_resize_u8(const void* src, int B, int sw, int sh, void* dst, int dw, int dh, int mode, void* stream);
 
+/* Legacy preprocess of B RGB8 images [B][h][w][3] (device): the reference's float
+ * bilinear resize to the floor-to-patch size and normalisation (src/preprocess.cpp:8-41),
+ * bit-exact, into planar f32 [B][3][*out_h][*out_w] (device; NULL: size query only).
+ * mean/std are host arrays of 3. */
+DA3B_API int da3b_preprocess_legacy(const void* rgb, int B, int w, int h, int patch, const float* mean,
+                                    const float* std_, void* chw_out, int* out_h, int* out_w, void* stream);
+
 /* Normalise + patchify: RGB8 [B][H][W][3] (device, H and W multiples of patch) ->
  * the patch-embed GEMM operand f16 [B*(H/patch)*(W/patch)][ldk], column
  * c*patch^2 + ky*patch + kx = (v/255 - mean[c]) / std[c] (src/preprocess.cpp:192-196),

@@ -171,3 +171,71 @@ def test_infer_prepared_matches_rgb_path(cuda, name, n):
     for k in ref:
         assert np.array_equal(got[k], ref[k]), k
         assert np.array_equal(got2[k], ref[k]), k
+
+
+@pytest.mark.parametrize("B,h,w", [(2, 120, 125), (1, 37, 53), (3, 14, 29), (1, 518, 700)])
+def test_legacy_preprocess_bit_exact(lib, cuda, B, h, w):
+    """da3b_preprocess_legacy (float bilinear to the floor-to-patch size + normalisation)
+    against the oracle's legacy preprocess: bit-exact."""
+    from oracle import oracle as orc
+
+    rng = np.random.default_rng(h * 31 + w)
+    imgs = rng.integers(0, 256, size=(B, h, w, 3), dtype=np.uint8)
+    src = torch.from_numpy(imgs).cuda()
+    oh, ow = ctypes.c_int(), ctypes.c_int()
+    mean = (ctypes.c_float * 3)(*MEAN)
+    std = (ctypes.c_float * 3)(*STD)
+    assert lib.da3b_preprocess_legacy(V(src.data_ptr()), B, w, h, 14, mean, std, None, ctypes.byref(oh),
+                                      ctypes.byref(ow), _stream()) == 0
+    out = torch.empty((B, 3, oh.value, ow.value), dtype=torch.float32, device="cuda")
+    assert lib.da3b_preprocess_legacy(V(src.data_ptr()), B, w, h, 14, mean, std, V(out.data_ptr()), ctypes.byref(oh),
+                                      ctypes.byref(ow), _stream()) == 0
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for b in range(B):
+        ref = orc.preprocess_cfg(imgs[b], 14, 504, True, legacy=True)
+        assert got[b].shape == ref.shape and np.array_equal(got[b], ref), b
+
+
+def test_capi_multiview_legacy_resize(lib, cuda, tmp_path):
+    """da_capi_depth_pose_multi on three 125x120 views (legacy resize to 112x112 on the
+    GPU): depth and camera poses against the oracle's multi-view run."""
+    from da3cpplib_b200 import synth
+    from oracle.oracle import Oracle
+
+    path = synth.ensure_gguf("da3-t", stress=True)
+    rng = np.random.default_rng(9)
+    imgs = [rng.integers(0, 256, size=(120, 125, 3), dtype=np.uint8) for _ in range(3)]
+    paths = []
+    for i, img in enumerate(imgs):
+        f = tmp_path / f"v{i}.ppm"
+        f.write_bytes(b"P6\n125 120\n255\n" + img.tobytes())
+        paths.append(str(f).encode())
+    ctx = lib.da_capi_load(path.encode(), 1)
+    assert ctx
+    try:
+        n, h, w = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        ext = np.zeros((3, 12), np.float32)
+        intr = np.zeros((3, 9), np.float32)
+        arr = (ctypes.c_char_p * 3)(*paths)
+        p = lib.da_capi_depth_pose_multi(ctx, arr, 3, ctypes.byref(h), ctypes.byref(w), ctypes.byref(n),
+                                         ext.ctypes.data, intr.ctypes.data)
+        assert p, lib.da_capi_last_error(ctx)
+        got = np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_float)), shape=(3 * 112 * 112,)).copy()
+        lib.da_capi_free_floats(p)
+    finally:
+        lib.da_capi_free(ctx)
+    assert (h.value, w.value, n.value) == (112, 112, 3)
+    rq = Oracle(path, act_quant=True).infer_mv(imgs)
+    rf = Oracle(path, act_quant=False).infer_mv(imgs)
+
+    def median_rel(a, b):
+        a, b = a.reshape(-1), b.reshape(-1)
+        m = np.abs(b) > 1e-6
+        return float(np.median(np.abs(a[m] - b[m]) / np.abs(b[m])))
+
+    floor = median_rel(rf["depth"], rq["depth"])
+    assert median_rel(got, rq["depth"]) <= max(1e-2, 1.5 * floor)
+    pe_floor = float(np.max(np.abs(rf["pose"][:, 9:21] - rq["pose"][:, 9:21]) / np.maximum(1, np.abs(rq["pose"][:, 9:21]))))
+    err = float(np.max(np.abs(ext - rq["pose"][:, 9:21]) / np.maximum(1, np.abs(rq["pose"][:, 9:21]))))
+    assert err <= max(8e-2, 8 * pe_floor), (err, pe_floor)
