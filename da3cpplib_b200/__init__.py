@@ -25,10 +25,10 @@ class Model:
         self.ctx = self.lib.da3b_load(gguf_path.encode(), int(device))
         if not self.ctx:
             raise RuntimeError(f"da3b_load failed for {gguf_path}")
-        dims = (ctypes.c_int * 8)()
+        dims = (ctypes.c_int * 10)()
         _lib.check(self.lib.da3b_model_dims(self.ctx, dims), "da3b_model_dims")
         (self.embed_dim, self.depth, self.num_heads, self.patch_size, self.cat_token, self.output_dim,
-         self.has_aux, self.is_da2) = list(dims)
+         self.has_aux, self.is_da2, self.has_sky, self.has_camera) = list(dims)
 
     def close(self):
         if getattr(self, "ctx", None):
@@ -73,6 +73,16 @@ class Model:
             out["conf"] = conf
         if ray is not None:
             out["rays"] = ray
+        if self.has_sky:
+            out["sky"] = self.sky(n, h, w)
+        return out
+
+    def sky(self, n, h, w):
+        """Sky plane [n][h][w] of the last run (n views at h x w; models with a sky head)."""
+        out = np.empty((n, h, w), np.float32)
+        rc = self.lib.da3b_last_sky(self.ctx, n, out.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(f"da3b_last_sky failed ({rc}): {self.last_error}")
         return out
 
     def pose(self, n):
@@ -103,6 +113,8 @@ class Model:
         out = {"depth": depth}
         if conf is not None:
             out["conf"] = conf
+        if self.has_sky:
+            out["sky"] = self.sky(n, h, w)
         return out
 
     def infer_device(self, rgb_ptr, n, h, w, depth_ptr, conf_ptr=None, rays_ptr=None, views_per_scene=1,

@@ -18,6 +18,7 @@
 #include "da3cpp/da3_c.h"
 #include "engine.h"
 #include "kernels.h"
+#include "nested.h"
 #include "pose.h"
 #include "preprocess.h"
 
@@ -30,6 +31,9 @@
 
 struct da_ctx {
   std::unique_ptr<da3b::Engine> engine;
+  // nested metric models (src/engine.cpp:67-77): the metric branch next to the anyview
+  // engine above, on the same device and stream
+  std::unique_ptr<da3b::Engine> metric;
   std::string last_error;
   cudaStream_t stream = nullptr;
   // preprocess_real on the GPU for inputs that need a resize: original image upload
@@ -99,8 +103,17 @@ bool read_ppm(const char* path, int* w, int* h, std::vector<uint8_t>& rgb, std::
   return ok;
 }
 
-bool is_mono(const da3b::Engine& e) {
-  return e.model().file.tensor("head.scratch.sky_out2b.weight") != nullptr && e.output_dim() == 1;
+bool is_mono(const da3b::Engine& e) { return e.has_sky() && e.output_dim() == 1; }
+
+bool is_nested(const da_ctx* c) { return c->metric != nullptr; }
+
+// Metric-scale checkpoints by name (src/da_capi.cpp:41-52, src/api.cpp:21-30).
+bool name_is_metric(const da3b::Config& c) {
+  if (c.head_max_depth > 0.f) return true;
+  std::string n = c.checkpoint_name;
+  std::transform(n.begin(), n.end(), n.begin(), [](unsigned char ch) { return static_cast<char>(tolower(ch)); });
+  return n.find("metric") != std::string::npos || n.find("nested") != std::string::npos ||
+         n.find("mono") != std::string::npos;
 }
 
 // Legacy preprocess on the GPU (src/preprocess.cpp:8-41, bit-exact): upload n views,
@@ -203,6 +216,59 @@ bool run_one(da_ctx* c, const uint8_t* rgb, int w, int h, bool legacy, std::vect
   return true;
 }
 
+// Sky plane of the last forward (relu of the sky logits), host copy.
+bool fetch_sky(da_ctx* c, da3b::Engine& e, size_t n, std::vector<float>& sky) {
+  sky.resize(n);
+  if (e.sky(sky.data(), n, c->stream) != 0 || cudaStreamSynchronize(c->stream) != cudaSuccess) {
+    c->last_error = "sky: " + e.last_error();
+    sky.clear();
+    return false;
+  }
+  return true;
+}
+
+// Nested metric depth of one image (src/engine.cpp:416-451): the legacy preprocess
+// feeds both branches; anyview -> depth, confidence and camera pose; metric -> depth and
+// sky; then the sky fill and the alignment on the host (src/nested.cpp:22-96).
+bool run_nested(da_ctx* c, const uint8_t* rgb, int w, int h, std::vector<float>& depth, float ext[12],
+                float intr[9], int* oh, int* ow) {
+  da3b::Engine& a = *c->engine;
+  da3b::Engine& m = *c->metric;
+  std::vector<float> conf;
+  int H = 0, W = 0;
+  if (!run_legacy(c, rgb, 1, 1, w, h, depth, &conf, &H, &W)) return false;
+  if (conf.size() != depth.size()) {
+    c->last_error = "nested: the anyview model has no confidence channel";
+    return false;
+  }
+  std::vector<float> pe;
+  if (a.poses(pe, c->stream) != 0) {
+    c->last_error = "nested: camera pose failed: " + a.last_error();
+    return false;
+  }
+  float any_ext[12];
+  da3b::pose_to_ext_intr(pe.data(), H, W, any_ext, intr);
+  // same normalised input for the metric branch: device copy of the anyview plan's input
+  size_t bytes = 0, bytes_m = 0;
+  float* src = a.prepared_input(1, 1, H, W, &bytes);
+  float* dst = m.prepared_input(1, 1, H, W, &bytes_m);
+  const size_t n = static_cast<size_t>(H) * W;
+  std::vector<float> mdepth(n), sky;
+  if (!src || !dst || bytes != bytes_m ||
+      cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess ||
+      m.run_prepared(1, 1, H, W, mdepth.data(), nullptr, c->stream) != 0 ||
+      cudaStreamSynchronize(c->stream) != cudaSuccess || m.status() != 0) {
+    c->last_error = "nested: metric branch failed: " + m.last_error();
+    return false;
+  }
+  if (!fetch_sky(c, m, n, sky)) return false;
+  da3b::mono_sky_fill(mdepth.data(), sky.data(), n);
+  da3b::nested_align(depth.data(), conf.data(), any_ext, intr, mdepth.data(), sky.data(), n, depth.data(), ext);
+  *oh = H;
+  *ow = W;
+  return true;
+}
+
 da_ctx* make_ctx(const char* path, int device, std::string* err) {
   if (!path) { *err = "null path"; return nullptr; }
   auto e = da3b::Engine::create(path, device, err);
@@ -240,6 +306,18 @@ std::shared_ptr<Model> load_model(const Params& params) {
   return m;
 }
 
+// src/api.cpp:69-78 / src/engine.cpp:67-77: the anyview model plus the metric branch
+// (a metric-branch GGUF with m_vit.* / m_head.* or any DPT with a sky head).
+std::shared_ptr<Model> load_nested_model(const NestedParams& params) {
+  if (params.anyview_model_path.empty() || params.metric_model_path.empty()) return nullptr;
+  da_ctx* c = da_capi_load_nested(params.anyview_model_path.c_str(), params.metric_model_path.c_str(),
+                                  params.n_threads);
+  if (!c) return nullptr;
+  auto m = std::make_shared<Model>();
+  m->ctx.reset(c);
+  return m;
+}
+
 ModelInfo model_info(const Model& model) {
   ModelInfo info;
   if (!model.ctx || !model.ctx->engine) return info;
@@ -252,15 +330,15 @@ ModelInfo model_info(const Model& model) {
     info.mean[i] = c.img_mean[i];
     info.std[i] = c.img_std[i];
   }
-  std::string n = c.checkpoint_name;
-  std::transform(n.begin(), n.end(), n.begin(), [](unsigned char ch) { return static_cast<char>(tolower(ch)); });
-  info.is_metric = c.head_max_depth > 0.f || n.find("metric") != std::string::npos ||
-                   n.find("nested") != std::string::npos || n.find("mono") != std::string::npos;
+  info.is_metric = name_is_metric(c) || is_nested(model.ctx.get());
   info.has_aux_ray_head = e.has_aux();
   cudaDeviceProp prop;
   if (cudaGetDeviceProperties(&prop, e.device()) == cudaSuccess) info.device_name = prop.name;
   info.gpu_active = true;
-  if (c.is_da2()) info.kind = c.head_max_depth > 0.f ? ModelKind::da2_metric : ModelKind::da2_relative;
+  if (is_nested(model.ctx.get())) {
+    info.kind = ModelKind::da3_nested;
+    info.has_camera_pose = true;
+  } else if (c.is_da2()) info.kind = c.head_max_depth > 0.f ? ModelKind::da2_metric : ModelKind::da2_relative;
   else if (is_mono(e)) info.kind = ModelKind::da3_mono;
   else {
     info.kind = ModelKind::da3;
@@ -277,20 +355,33 @@ bool infer(Model& model, const Image& image, Result& result, const InferOptions&
     return false;
   da_ctx* c = model.ctx.get();
   const da3b::Engine& e = *c->engine;
+  if (is_nested(c)) {
+    // src/api.cpp:123-129: both branches + alignment; options do not apply
+    int H = 0, W = 0;
+    if (!run_nested(c, image.data.data(), image.width, image.height, result.depth, result.extrinsics.data(),
+                    result.intrinsics.data(), &H, &W)) {
+      DA_LOG("infer: %s", c->last_error.c_str());
+      result = {};
+      return false;
+    }
+    result.height = H;
+    result.width = W;
+    result.is_metric = true;
+    result.has_pose = true;
+    return !result.depth.empty();
+  }
   if (options.ray_pose) {
     DA_LOG("infer: the ray-based pose solver is not part of this build");
     return false;
   }
-  if (options.with_pose && (e.config().is_da2() || !e.has_camera())) return false;
-  if (is_mono(e)) {
-    DA_LOG("infer: DA3 mono (sky head) checkpoints are not supported");
-    return false;
-  }
-  // DA2 always uses preprocess_real (src/engine.cpp:121-130); DA3 uses it unless
-  // legacy_resize (src/api.cpp:151-157).
-  const bool legacy = !e.config().is_da2() && options.legacy_resize;
+  if (options.with_pose && (e.config().is_da2() || is_mono(e) || !e.has_camera())) return false;
+  // DA2 and mono always use preprocess_real (src/engine.cpp:105-130); DA3 uses it
+  // unless legacy_resize (src/api.cpp:151-157).
+  const bool mono = is_mono(e);
+  const bool legacy = !e.config().is_da2() && !mono && options.legacy_resize;
   int H = 0, W = 0;
-  if (!run_one(c, image.data.data(), image.width, image.height, legacy, result.depth, &result.confidence, &H, &W)) {
+  if (!run_one(c, image.data.data(), image.width, image.height, legacy, result.depth, &result.confidence, &H, &W) ||
+      (mono && !fetch_sky(c, *c->engine, result.depth.size(), result.sky))) {
     DA_LOG("infer: %s", c->last_error.c_str());
     result = {};
     return false;
@@ -331,7 +422,7 @@ bool infer_preprocessed(Model& model, int height, int width, const UploadCallbac
   if (!model.ctx || !model.ctx->engine || !upload || height <= 0 || width <= 0) return false;
   da_ctx* c = model.ctx.get();
   da3b::Engine& e = *c->engine;
-  if (e.config().is_da2() || is_mono(e)) return false;
+  if (is_nested(c) || e.config().is_da2() || is_mono(e)) return false;
   size_t bytes = 0;
   float* dst = e.prepared_input(1, 1, height, width, &bytes);
   if (!dst) {
@@ -361,6 +452,7 @@ bool infer_batch(Model& model, const std::vector<Image>& images, std::vector<Res
   if (!model.ctx || !model.ctx->engine || images.empty()) return false;
   da_ctx* c = model.ctx.get();
   da3b::Engine& e = *c->engine;
+  if (is_nested(c)) return false;
   const int w = images[0].width, h = images[0].height, n = static_cast<int>(images.size());
   std::vector<uint8_t> rgb(static_cast<size_t>(n) * w * h * 3);
   for (int i = 0; i < n; ++i) {
@@ -375,6 +467,8 @@ bool infer_batch(Model& model, const std::vector<Image>& images, std::vector<Res
     DA_LOG("infer_batch: %s", c->last_error.c_str());
     return false;
   }
+  std::vector<float> sky;
+  if (e.has_sky() && !fetch_sky(c, e, depth.size(), sky)) return false;
   const bool metric = model_info(model).is_metric;
   results.resize(n);
   for (int i = 0; i < n; ++i) {
@@ -384,6 +478,7 @@ bool infer_batch(Model& model, const std::vector<Image>& images, std::vector<Res
     r.is_metric = metric;
     r.depth.assign(depth.begin() + i * HW, depth.begin() + (i + 1) * HW);
     if (!conf.empty()) r.confidence.assign(conf.begin() + i * HW, conf.begin() + (i + 1) * HW);
+    if (!sky.empty()) r.sky.assign(sky.begin() + i * HW, sky.begin() + (i + 1) * HW);
   }
   return true;
 }
@@ -404,11 +499,29 @@ DA_CAPI da_ctx* da_capi_load(const char* path, int n_threads) {
 }
 
 DA_CAPI da_ctx* da_capi_load_nested(const char* anyview, const char* metric, int n_threads) {
-  (void)anyview;
-  (void)metric;
   (void)n_threads;
-  DA_LOG("da_capi_load_nested: nested metric models are outside the supported depth path");
-  return nullptr;
+  if (!anyview || !metric) return nullptr;
+  std::string err;
+  const int dev = default_device();
+  da_ctx* c = make_ctx(anyview, dev, &err);
+  if (!c) {
+    DA_LOG("da_capi_load_nested: anyview: %s", err.c_str());
+    return nullptr;
+  }
+  c->metric = da3b::Engine::create(metric, dev, &err);
+  if (!c->metric) {
+    DA_LOG("da_capi_load_nested: metric: %s", err.c_str());
+    delete c;
+    return nullptr;
+  }
+  if (!c->metric->has_sky() || c->engine->config().is_da2() || !c->engine->has_camera() ||
+      c->engine->output_dim() < 2) {
+    DA_LOG("da_capi_load_nested: needs a DA3 anyview model with camera decoder and confidence, and a metric "
+           "model with a sky head");
+    delete c;
+    return nullptr;
+  }
+  return c;
 }
 
 DA_CAPI void da_capi_free(da_ctx* c) { delete c; }
@@ -434,8 +547,8 @@ DA_CAPI const char* da_capi_last_error(da_ctx* c) { return c ? c->last_error.c_s
 DA_CAPI void da_capi_free_floats(float* p) { free(p); }
 DA_CAPI void da_capi_free_bytes(unsigned char* p) { free(p); }
 
-// src/da_capi.cpp:97-117: DA2 -> depth_relative (preprocess_real); DA3 -> depth
-// (legacy floor-to-patch preprocess).
+// src/da_capi.cpp:97-117: nested -> both branches + alignment; DA2 -> depth_relative
+// (preprocess_real); DA3 -> depth (legacy floor-to-patch preprocess).
 DA_CAPI float* da_capi_depth_path(da_ctx* c, const char* image_path, int* out_h, int* out_w) {
   if (!c || !c->engine || !image_path) {
     if (c) c->last_error = "depth: bad args";
@@ -447,7 +560,12 @@ DA_CAPI float* da_capi_depth_path(da_ctx* c, const char* image_path, int* out_h,
   std::vector<float> depth;
   int H = 0, W = 0;
   const bool legacy = !c->engine->config().is_da2();
-  if (!run_one(c, rgb.data(), w, h, legacy, depth, nullptr, &H, &W)) return nullptr;
+  if (is_nested(c)) {
+    float ext[12], intr[9];
+    if (!run_nested(c, rgb.data(), w, h, depth, ext, intr, &H, &W)) return nullptr;
+  } else if (!run_one(c, rgb.data(), w, h, legacy, depth, nullptr, &H, &W)) {
+    return nullptr;
+  }
   float* p = static_cast<float*>(malloc(depth.size() * sizeof(float)));
   if (!p) {
     c->last_error = "depth: oom";
@@ -474,6 +592,14 @@ DA_CAPI int da_capi_pose_path(da_ctx* c, const char* image_path, float out_ext[1
   if (!read_ppm(image_path, &w, &h, rgb, &c->last_error)) return -1;
   std::vector<float> depth, conf, pe;
   int H = 0, W = 0;
+  if (is_nested(c)) {
+    // src/da_capi.cpp:123-124: the nested pose is the anyview pose, translation scaled
+    float ext[12], intr[9];
+    if (!run_nested(c, rgb.data(), w, h, depth, ext, intr, &H, &W)) return -1;
+    if (out_ext) memcpy(out_ext, ext, sizeof(ext));
+    if (out_intr) memcpy(out_intr, intr, sizeof(intr));
+    return 0;
+  }
   if (!run_one(c, rgb.data(), w, h, true, depth, &conf, &H, &W)) return -1;
   if (c->engine->poses(pe, c->stream) != 0) {
     c->last_error = "pose: " + c->engine->last_error();
@@ -542,33 +668,81 @@ DA_CAPI float* da_capi_depth_pose_multi(da_ctx* c, const char** paths, int n, in
   return p;
 }
 
+// src/da_capi.cpp:202-285: nested -> aligned depth and pose (no conf / sky); DA2 ->
+// depth only; mono -> depth and sky; DA3 -> depth, confidence and camera pose. Every
+// path but nested uses preprocess_real.
 DA_CAPI int da_capi_depth_dense(da_ctx* c, const char* image_path, int* out_h, int* out_w, float** out_depth,
                                 float** out_conf, float** out_sky, float out_ext[12], float out_intr[9],
                                 int* out_is_metric) {
-  (void)out_ext;
-  (void)out_intr;
   if (!c || !c->engine || !image_path) {
     if (c) c->last_error = "depth_dense: bad args";
     return -1;
   }
+  if (out_depth) *out_depth = nullptr;
+  if (out_conf) *out_conf = nullptr;
+  if (out_sky) *out_sky = nullptr;
+  if (out_ext) memset(out_ext, 0, 12 * sizeof(float));
+  if (out_intr) memset(out_intr, 0, 9 * sizeof(float));
   int w = 0, h = 0;
   std::vector<uint8_t> rgb;
   if (!read_ppm(image_path, &w, &h, rgb, &c->last_error)) return -1;
-  std::vector<float> depth, conf;
+  da3b::Engine& e = *c->engine;
+  std::vector<float> depth, second;
+  float ext[12] = {0}, intr[9] = {0};
+  bool has_pose = false;
   int H = 0, W = 0;
-  if (!run_one(c, rgb.data(), w, h, false, depth, &conf, &H, &W)) return -1;
-  auto dup = [](const std::vector<float>& v) -> float* {
-    if (v.empty()) return nullptr;
-    float* p = static_cast<float*>(malloc(v.size() * sizeof(float)));
-    if (p) memcpy(p, v.data(), v.size() * sizeof(float));
-    return p;
-  };
-  if (out_depth) *out_depth = dup(depth);
-  if (out_conf) *out_conf = dup(conf);
-  if (out_sky) *out_sky = nullptr;
+  int metric = name_is_metric(e.config()) ? 1 : 0;
+  if (is_nested(c)) {
+    if (!run_nested(c, rgb.data(), w, h, depth, ext, intr, &H, &W)) return -1;
+    has_pose = true;
+    metric = 1;
+  } else {
+    const bool mono = is_mono(e);
+    if (!run_one(c, rgb.data(), w, h, false, depth, mono ? nullptr : &second, &H, &W)) return -1;
+    if (e.config().is_da2()) {
+      second.clear();
+      metric = e.config().head_max_depth > 0.f ? 1 : 0;
+    } else if (mono) {
+      if (!fetch_sky(c, e, depth.size(), second)) return -1;
+    } else {
+      std::vector<float> pe;
+      if (!e.has_camera() || e.poses(pe, c->stream) != 0) {
+        c->last_error = "depth_dense: depth+pose failed: " + e.last_error();
+        return -1;
+      }
+      da3b::pose_to_ext_intr(pe.data(), H, W, ext, intr);
+      has_pose = true;
+    }
+    if (!mono && second.size() != depth.size()) second.clear();
+    if (mono) {
+      if (out_sky && !second.empty()) {
+        *out_sky = static_cast<float*>(malloc(second.size() * sizeof(float)));
+        if (!*out_sky) { c->last_error = "depth_dense: oom"; return -1; }
+        memcpy(*out_sky, second.data(), second.size() * sizeof(float));
+      }
+    } else if (out_conf && !second.empty()) {
+      *out_conf = static_cast<float*>(malloc(second.size() * sizeof(float)));
+      if (!*out_conf) { c->last_error = "depth_dense: oom"; return -1; }
+      memcpy(*out_conf, second.data(), second.size() * sizeof(float));
+    }
+  }
+  if (out_depth) {
+    *out_depth = static_cast<float*>(malloc(depth.size() * sizeof(float)));
+    if (!*out_depth) {
+      if (out_conf && *out_conf) { free(*out_conf); *out_conf = nullptr; }
+      if (out_sky && *out_sky) { free(*out_sky); *out_sky = nullptr; }
+      c->last_error = "depth_dense: oom";
+      return -1;
+    }
+    memcpy(*out_depth, depth.data(), depth.size() * sizeof(float));
+  }
+  if (has_pose) {
+    if (out_ext) memcpy(out_ext, ext, sizeof(ext));
+    if (out_intr) memcpy(out_intr, intr, sizeof(intr));
+  }
   if (out_h) *out_h = H;
   if (out_w) *out_w = W;
-  if (out_is_metric) *out_is_metric = c->engine->config().head_max_depth > 0.f ? 1 : 0;
+  if (out_is_metric) *out_is_metric = metric;
   return 0;
 }
 
@@ -636,6 +810,29 @@ DA3B_API int da3b_last_pose(da_ctx* c, int n_views, float* pose_enc, float* ext,
     if (intr) memcpy(intr + v * 9, k, sizeof(k));
   }
   return 0;
+}
+
+DA3B_API int da3b_last_sky(da_ctx* c, int n_views, float* sky) {
+  if (!c || !c->engine || !sky || n_views <= 0) return -1;
+  da3b::Engine& e = *c->engine;
+  int H = 0, W = 0;
+  e.last_size(&H, &W);
+  const size_t n = static_cast<size_t>(n_views) * H * W;
+  if (e.sky(sky, n, c->stream) != 0 || cudaStreamSynchronize(c->stream) != cudaSuccess) {
+    c->last_error = "last_sky: " + e.last_error();
+    return -2;
+  }
+  return 0;
+}
+
+DA3B_API float da3b_nested_align(const float* any_depth, const float* any_conf, const float* any_ext,
+                                 const float* any_intr, float* metric_depth, const float* sky, int64_t n,
+                                 float* out_depth, float* out_ext) {
+  if (!any_depth || !any_conf || !any_ext || !any_intr || !metric_depth || !sky || !out_depth || !out_ext || n < 0)
+    return -1.0f;
+  da3b::mono_sky_fill(metric_depth, sky, static_cast<size_t>(n));
+  return da3b::nested_align(any_depth, any_conf, any_ext, any_intr, metric_depth, sky, static_cast<size_t>(n),
+                            out_depth, out_ext);
 }
 
 DA3B_API int da3b_infer_prepared(da_ctx* c, const float* chw, int n_views, int h, int w, float* depth, float* conf,
@@ -735,6 +932,8 @@ DA3B_API int da3b_model_dims(da_ctx* c, int* out) {
   out[5] = c->engine->output_dim();
   out[6] = c->engine->has_aux() ? 1 : 0;
   out[7] = cfg.is_da2() ? 1 : 0;
+  out[8] = c->engine->has_sky() ? 1 : 0;
+  out[9] = c->engine->has_camera() ? 1 : 0;
   return 0;
 }
 

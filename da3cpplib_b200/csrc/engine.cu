@@ -55,7 +55,7 @@ struct Plan {
   Arena arena;
   // inputs / outputs owned by the plan (the captured graph reads / writes these)
   uint8_t* rgb = nullptr;
-  float *depth = nullptr, *conf = nullptr, *raysbuf = nullptr;
+  float *depth = nullptr, *conf = nullptr, *raysbuf = nullptr, *sky = nullptr;
   // backbone
   float *x = nullptr, *x2 = nullptr, *pos = nullptr;
   float *rl_cos = nullptr, *rl_sin = nullptr, *rn_cos = nullptr, *rn_sin = nullptr;
@@ -298,6 +298,7 @@ Plan* Engine::plan_for(int V, int S, int H, int W, bool rays) {
     T(p->depth, V_ * H * W);
     T(p->conf, V_ * H * W);
     if (p->rays) T(p->raysbuf, static_cast<size_t>(hd.aux_od) * V_ * (8 * gh) * (8 * gw));
+    if (hd.sky) T(p->sky, V_ * H * W);
     T(p->x, M_ * D);
     if (S >= 3 && c.alt_start >= 0) T(p->x2, M_ * D);
     T(p->pos, static_cast<size_t>(p->Ntok) * D);
@@ -690,6 +691,19 @@ int Engine::head(Plan& p, cudaStream_t s) {
     e.o2_scale = c.head_max_depth;
     CK(conv_nhwc(p.O1u, V, p.H, p.W, h.out2a.IC, h.out2a.w, 32, 3, 32, e, status_, s));
   }
+  // ---- sky head (metric / mono DPT, src/dpt_head.cpp:205-222 and the relu at
+  // src/dpt_head.cpp:334-338) on the same upsampled feature map
+  if (h.sky) {
+    EpiArgs e = epi_default();
+    e.kind = kEpiOut2;
+    e.bias = h.sky_out2a.b;
+    e.o2_w = h.sky_out2b_w;
+    e.o2_b = h.sky_out2b_b;
+    e.o2_dim = 1;
+    e.o2_act[0] = raw_logits_ ? kOutIdentity : kOutRelu;
+    e.o2_out[0] = p.sky;
+    CK(conv_nhwc(p.O1u, V, p.H, p.W, h.sky_out2a.IC, h.sky_out2a.w, 32, 3, 32, e, status_, s));
+  }
   // ---- aux ray head (DualDPT, src/dpt_head.cpp:225-272)
   if (p.rays) {
     if (int rc = pyramid(p, h.fa, p.auxA, s)) return rc;
@@ -853,6 +867,27 @@ int Engine::copy_out(Plan* p, float* depth, float* conf, float* rays, cudaStream
 
 // Camera decoder on the camera tokens of the last run (CamPose::pose,
 // src/cam_pose.cpp:20-38): pose encodings [V][9], in the original view order.
+int Engine::sky(float* dst, size_t count, cudaStream_t s) {
+  if (!model_->head.sky) {
+    err_ = "this GGUF has no sky head (head.scratch.sky_out2*)";
+    return -60;
+  }
+  if (!last_) {
+    err_ = "no forward has run yet";
+    return -61;
+  }
+  const size_t n = static_cast<size_t>(last_->V) * last_->H * last_->W;
+  if (count != n) {
+    err_ = "the last run produced " + std::to_string(n) + " sky values, not " + std::to_string(count);
+    return -63;
+  }
+  if (cudaMemcpyAsync(dst, last_->sky, n * 4, cudaMemcpyDefault, s) != cudaSuccess) {
+    err_ = "sky copy failed";
+    return -62;
+  }
+  return 0;
+}
+
 int Engine::poses(std::vector<float>& pe, cudaStream_t s) {
   const CamDec& cd = model_->camdec;
   if (!cd.present) {

@@ -49,6 +49,11 @@ class Engine {
   float* prepared_input(int V, int S, int H, int W, size_t* bytes);
   int run_prepared(int V, int S, int H, int W, float* depth, float* conf, cudaStream_t s);
 
+  // Sky head (metric / mono DPT) of the last run: relu(sky logits) as f32 [n_views][H][W]
+  // into dst (host or device; count must equal n_views * H * W), asynchronous on s.
+  int sky(float* dst, size_t count, cudaStream_t s);
+  bool has_sky() const { return model_->head.sky; }
+
   // Camera decoder on the last run's camera tokens: pose encodings [n_views][9]
   // ([t(3), quaternion xyzw (4), fov h/w (2)]) in the original view order.
   int poses(std::vector<float>& pe, cudaStream_t s);

@@ -130,6 +130,18 @@ bool GgufFile::open(const std::string& path, std::string* err) {
     t.data = base + data_off + t.offset;
     tensors_[t.name] = t;
   }
+  // Nested metric-branch files keep their tensors under m_vit.* / m_head.*; they are
+  // also reachable as vit.* / head.* so one loader serves both layouts
+  // (src/model_loader.cpp:146-154).
+  for (const auto& t : infos) {
+    std::string alias;
+    if (t.name.rfind("m_vit.", 0) == 0) alias = t.name.substr(2);
+    else if (t.name.rfind("m_head.", 0) == 0) alias = t.name.substr(2);
+    if (alias.empty()) continue;
+    GgufTensor a = tensors_[t.name];
+    a.name = alias;
+    tensors_[alias] = a;
+  }
   return true;
 }
 

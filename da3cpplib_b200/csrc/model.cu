@@ -49,33 +49,34 @@ unsigned blocks_for(long n) {
 
 bool read_config(const GgufFile& f, Config& c, std::string* err) {
   const std::string P = "depthanything3.";
-  if (f.kv(P + "m_vit.embed_dim")) {
-    if (err) *err = "nested metric-branch GGUF (m_vit.*) is outside the supported depth path";
-    return false;
-  }
+  // A nested metric-branch file carries its structure under m_vit.* / m_head.*; its
+  // head has no UV pos-embed unless m_head.pos_embed says so (src/model_loader.cpp:84-127).
+  const bool metric = f.kv(P + "m_vit.embed_dim") != nullptr;
+  const std::string V = P + (metric ? "m_vit." : "vit."), Hd = P + (metric ? "m_head." : "head.");
   c.patch_size = static_cast<int>(f.get_u32(P + "patch_size", 14));
-  c.embed_dim = static_cast<int>(f.get_u32(P + "vit.embed_dim", 0));
-  c.depth = static_cast<int>(f.get_u32(P + "vit.depth", 0));
-  c.num_heads = static_cast<int>(f.get_u32(P + "vit.num_heads", 0));
-  c.head_dim = static_cast<int>(f.get_u32(P + "vit.head_dim", 0));
-  c.mlp_hidden = static_cast<int>(f.get_u32(P + "vit.mlp_hidden", 0));
-  c.num_register = static_cast<int>(f.get_u32(P + "vit.num_register_tokens", 0));
-  c.pos_embed_grid = static_cast<int>(f.get_u32(P + "vit.pos_embed_grid", 0));
-  c.alt_start = f.get_i32(P + "vit.alt_start", -1);
-  c.rope_start = f.get_i32(P + "vit.rope_start", -1);
-  c.qknorm_start = f.get_i32(P + "vit.qknorm_start", -1);
-  c.init_values = f.get_f32(P + "vit.init_values", 0.f);
-  c.rope_freq = f.get_f32(P + "vit.rope_freq", 100.f);
-  c.ln_eps = f.get_f32(P + "vit.ln_eps", 1e-6f);
-  c.interp_offset = f.get_f32(P + "vit.interpolate_offset", 0.1f);
-  c.cat_token = f.get_bool(P + "vit.cat_token", true);
-  c.qkv_bias = f.get_bool(P + "vit.qkv_bias", true);
-  c.interp_antialias = f.get_bool(P + "vit.interpolate_antialias", false);
-  c.ffn_type = f.get_str(P + "vit.ffn_type", "mlp");
-  c.head_features = static_cast<int>(f.get_u32(P + "head.features", 0));
-  c.out_layers = f.get_i32_arr(P + "vit.out_layers");
-  c.head_out_channels = f.get_i32_arr(P + "head.out_channels");
-  c.head_pos_embed = f.get_bool(P + "head.pos_embed", true);
+  c.embed_dim = static_cast<int>(f.get_u32(V + "embed_dim", 0));
+  c.depth = static_cast<int>(f.get_u32(V + "depth", 0));
+  c.num_heads = static_cast<int>(f.get_u32(V + "num_heads", 0));
+  c.head_dim = static_cast<int>(f.get_u32(V + "head_dim", 0));
+  c.mlp_hidden = static_cast<int>(f.get_u32(V + "mlp_hidden", 0));
+  c.num_register = static_cast<int>(f.get_u32(V + "num_register_tokens", 0));
+  c.pos_embed_grid = static_cast<int>(f.get_u32(V + "pos_embed_grid", 0));
+  c.alt_start = f.get_i32(V + "alt_start", -1);
+  c.rope_start = f.get_i32(V + "rope_start", -1);
+  c.qknorm_start = f.get_i32(V + "qknorm_start", -1);
+  c.init_values = f.get_f32(V + "init_values", 0.f);
+  c.rope_freq = f.get_f32(V + "rope_freq", 100.f);
+  c.ln_eps = f.get_f32(V + "ln_eps", 1e-6f);
+  c.interp_offset = f.get_f32(V + "interpolate_offset", 0.1f);
+  c.cat_token = f.get_bool(V + "cat_token", true);
+  c.qkv_bias = f.get_bool(V + "qkv_bias", true);
+  c.interp_antialias = f.get_bool(V + "interpolate_antialias", false);
+  c.ffn_type = f.get_str(V + "ffn_type", "mlp");
+  c.head_features = static_cast<int>(f.get_u32(Hd + "features", 0));
+  c.out_layers = f.get_i32_arr(V + "out_layers");
+  c.head_out_channels = f.get_i32_arr(Hd + "out_channels");
+  c.head_pos_embed = f.get_bool(Hd + "pos_embed", !metric);
+  c.metric_branch = metric;
   c.img_mean = f.get_f32_arr(P + "img.mean");
   c.img_std = f.get_f32_arr(P + "img.std");
   c.img_resize_target = static_cast<int>(f.get_u32(P + "img.resize_target", 504));
@@ -350,6 +351,17 @@ std::unique_ptr<DeviceModel> DeviceModel::load(const std::string& path, std::str
     h.od = static_cast<int>(t->ne[3]);
     if (!(h.out2b_w = m->up_f32("head.scratch.out2b.weight", true, err))) return nullptr;
     if (!(h.out2b_b = m->up_f32("head.scratch.out2b.bias", true, err))) return nullptr;
+  }
+  if (m->file.tensor("head.scratch.sky_out2b.weight")) {
+    if (!m->conv("head.scratch.sky_out2a.weight", "head.scratch.sky_out2a.bias", h.sky_out2a, err)) return nullptr;
+    const GgufTensor* t = m->file.tensor("head.scratch.sky_out2b.weight");
+    if (h.sky_out2a.OC != 32 || h.sky_out2a.ks != 3 || h.sky_out2a.IC != h.out2a.IC || t->ne[2] != 32 || t->ne[3] != 1) {
+      if (err) *err = "sky head must be 3x3 feat/2 -> 32 then 1x1 32 -> 1";
+      return nullptr;
+    }
+    if (!(h.sky_out2b_w = m->up_f32("head.scratch.sky_out2b.weight", true, err))) return nullptr;
+    if (!(h.sky_out2b_b = m->up_f32("head.scratch.sky_out2b.bias", true, err))) return nullptr;
+    h.sky = true;
   }
   h.aux = m->file.tensor("head.scratch.rn1_aux.out.weight") != nullptr;
   if (h.aux) {

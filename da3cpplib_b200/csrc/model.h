@@ -29,6 +29,7 @@ struct Config {
   std::string checkpoint_name;
   float head_max_depth = 0.f;
   std::string arch = "depthanything3";
+  bool metric_branch = false;  // read from m_vit.* / m_head.* keys (nested metric GGUF)
 
   bool is_da2() const { return arch == "depthanything2"; }
 };
@@ -76,6 +77,11 @@ struct Head {
   Conv out1_aux[5], out2a_aux;
   float *aux_ln_g = nullptr, *aux_ln_b = nullptr, *out2b_aux_w = nullptr, *out2b_aux_b = nullptr;
   int aux_od = 0;
+  // Sky head of the metric / mono DPT (src/dpt_head.cpp:205-222): 3x3 feat/2 -> 32,
+  // relu, 1x1 32 -> 1 on the upsampled feature map.
+  bool sky = false;
+  Conv sky_out2a;
+  float *sky_out2b_w = nullptr, *sky_out2b_b = nullptr;
 };
 
 // Camera decoder of DA3 (src/cam_pose.cpp:20-32): relu(bb0) -> relu(bb2) -> fc_t (3) |

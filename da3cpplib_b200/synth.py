@@ -61,6 +61,7 @@ class ModelSpec:
     max_depth: float = 0.0
     head_dim: int = 64
     checkpoint_name: str = ""
+    sky: bool = False            # metric / mono DPT sky head (head.scratch.sky_out2*)
 
 
 SPECS = {
@@ -89,6 +90,17 @@ SPECS = {
                        cat_token=True, head_pos_embed=True, head_norm=True, output_dim=2, alt_start=4, rope_start=4,
                        qknorm_start=4, camera_token=True, aux=True, resize_mode="upper_bound", resize_target=504,
                        checkpoint_name="da3-small-random"),
+    # DA3 mono / metric DPT (plain ViT, no cat token, no head norm or UV PE, depth-only
+    # main head plus the sky head); the tiny one is also the nested metric branch of the
+    # tests, written with the m_vit.* / m_head.* layout.
+    "da3m-t": ModelSpec("da3m-t", "depthanything3", 128, 4, 2, 256, 32, (16, 32, 64, 64), (0, 1, 2, 3),
+                        cat_token=False, head_pos_embed=False, head_norm=False, output_dim=1, sky=True,
+                        pos_embed_grid=8, resize_mode="upper_bound", resize_target=112,
+                        checkpoint_name="da3-mono-tiny-random"),
+    "da3m-l": ModelSpec("da3m-l", "depthanything3", 1024, 24, 16, 4096, 256, (256, 512, 1024, 1024),
+                        (4, 11, 17, 23), cat_token=False, head_pos_embed=False, head_norm=False, output_dim=1,
+                        sky=True, resize_mode="upper_bound", resize_target=504,
+                        checkpoint_name="da3-mono-large-random"),
 }
 
 IMG_MEAN = (0.485, 0.456, 0.406)
@@ -182,7 +194,9 @@ def tensors_for(spec: ModelSpec, seed: int, stress: bool = False):
     add("head.scratch.out1.bias", n(F // 2))
     add("head.scratch.out2a.weight", lw(32, F // 2, 3, 3, fan_in=9 * F // 2, gain=1.4))
     add("head.scratch.out2a.bias", n(32))
-    add("head.scratch.out2b.weight", lw(spec.output_dim, 32, 1, 1, fan_in=32))
+    # a depth-only head (mono / metric DPT) keeps its single logit in a range where exp()
+    # gives depths of a few units rather than exp(15)
+    add("head.scratch.out2b.weight", lw(spec.output_dim, 32, 1, 1, fan_in=32, gain=0.1 if spec.sky else 1.0))
     add("head.scratch.out2b.bias", n(spec.output_dim))
     if spec.aux:
         pyramid("_aux")
@@ -210,48 +224,63 @@ def tensors_for(spec: ModelSpec, seed: int, stress: bool = False):
         add("cam.fc_q.bias", n(4) + np.array([0, 0, 0, 1], np.float32))
         add("cam.fc_fov.weight", _q8_0(lw(2, Ccam, fan_in=Ccam)), GGML_Q8_0)
         add("cam.fc_fov.bias", n(2) + np.float32(1.0))
+    if spec.sky:
+        # sky head (src/dpt_head.cpp:205-222): 3x3 feat/2 -> 32, relu, 1x1 32 -> 1
+        add("head.scratch.sky_out2a.weight", lw(32, F // 2, 3, 3, fan_in=9 * F // 2, gain=1.4))
+        add("head.scratch.sky_out2a.bias", n(32))
+        # scaled and shifted so that relu(logit) straddles the 0.3 sky threshold
+        add("head.scratch.sky_out2b.weight", lw(1, 32, 1, 1, fan_in=32, gain=0.1))
+        add("head.scratch.sky_out2b.bias", n(1) - np.float32(1.2 if stress else 0.0))
     return out
 
 
-def write_gguf(spec: ModelSpec, path: str, seed: int, stress: bool = False) -> str:
+def write_gguf(spec: ModelSpec, path: str, seed: int, stress: bool = False, metric_branch: bool = False) -> str:
+    """metric_branch=True writes the nested metric-branch layout: structure keys under
+    m_vit.* / m_head.* and tensors renamed vit.* -> m_vit.*, head.* -> m_head.*
+    (src/model_loader.cpp:84-127, :146-154); the head pos-embed key is omitted."""
     import gguf
     from gguf.constants import GGMLQuantizationType
 
     tmp = path + ".tmp"
     w = gguf.GGUFWriter(tmp, arch="depthanything3")
     P = "depthanything3."
+    V = P + ("m_vit." if metric_branch else "vit.")
+    Hd = P + ("m_head." if metric_branch else "head.")
     w.add_string(P + "arch", spec.arch)
     w.add_string(P + "checkpoint_name", spec.checkpoint_name or spec.name)
     w.add_uint32(P + "patch_size", 14)
-    w.add_uint32(P + "vit.embed_dim", spec.embed_dim)
-    w.add_uint32(P + "vit.depth", spec.depth)
-    w.add_uint32(P + "vit.num_heads", spec.num_heads)
-    w.add_uint32(P + "vit.head_dim", spec.head_dim)
-    w.add_uint32(P + "vit.mlp_hidden", spec.mlp_hidden)
-    w.add_string(P + "vit.ffn_type", "mlp")
-    w.add_uint32(P + "vit.num_register_tokens", 0)
-    w.add_int32(P + "vit.alt_start", spec.alt_start)
-    w.add_int32(P + "vit.rope_start", spec.rope_start)
-    w.add_int32(P + "vit.qknorm_start", spec.qknorm_start)
-    w.add_float32(P + "vit.rope_freq", 100.0)
-    w.add_bool(P + "vit.cat_token", spec.cat_token)
-    w.add_bool(P + "vit.qkv_bias", True)
-    w.add_float32(P + "vit.ln_eps", 1e-6)
-    w.add_float32(P + "vit.interpolate_offset", 0.1)
-    w.add_bool(P + "vit.interpolate_antialias", False)
-    w.add_uint32(P + "vit.pos_embed_grid", spec.pos_embed_grid)
-    w.add_array(P + "vit.out_layers", [int(v) for v in spec.out_layers])
+    w.add_uint32(V + "embed_dim", spec.embed_dim)
+    w.add_uint32(V + "depth", spec.depth)
+    w.add_uint32(V + "num_heads", spec.num_heads)
+    w.add_uint32(V + "head_dim", spec.head_dim)
+    w.add_uint32(V + "mlp_hidden", spec.mlp_hidden)
+    w.add_string(V + "ffn_type", "mlp")
+    w.add_uint32(V + "num_register_tokens", 0)
+    w.add_int32(V + "alt_start", spec.alt_start)
+    w.add_int32(V + "rope_start", spec.rope_start)
+    w.add_int32(V + "qknorm_start", spec.qknorm_start)
+    w.add_float32(V + "rope_freq", 100.0)
+    w.add_bool(V + "cat_token", spec.cat_token)
+    w.add_bool(V + "qkv_bias", True)
+    w.add_float32(V + "ln_eps", 1e-6)
+    w.add_float32(V + "interpolate_offset", 0.1)
+    w.add_bool(V + "interpolate_antialias", False)
+    w.add_uint32(V + "pos_embed_grid", spec.pos_embed_grid)
+    w.add_array(V + "out_layers", [int(v) for v in spec.out_layers])
     w.add_array(P + "img.mean", [float(v) for v in IMG_MEAN])
     w.add_array(P + "img.std", [float(v) for v in IMG_STD])
     w.add_string(P + "img.resize_mode", spec.resize_mode)
     w.add_uint32(P + "img.resize_target", spec.resize_target)
-    w.add_uint32(P + "head.features", spec.features)
-    w.add_array(P + "head.out_channels", [int(v) for v in spec.out_channels])
-    w.add_uint32(P + "head.output_dim", spec.output_dim)
-    w.add_bool(P + "head.pos_embed", spec.head_pos_embed)
+    w.add_uint32(Hd + "features", spec.features)
+    w.add_array(Hd + "out_channels", [int(v) for v in spec.out_channels])
+    w.add_uint32(Hd + "output_dim", spec.output_dim)
+    if not metric_branch:
+        w.add_bool(Hd + "pos_embed", spec.head_pos_embed)
     w.add_float32(P + "head.max_depth", float(spec.max_depth))
     w.add_bool(P + "head.has_aux", spec.aux)
     for name, arr, t in tensors_for(spec, seed, stress):
+        if metric_branch and name.startswith(("vit.", "head.")):
+            name = "m_" + name
         if t == GGML_Q8_0:
             w.add_tensor(name, arr, raw_dtype=GGMLQuantizationType.Q8_0)
         else:
@@ -268,15 +297,18 @@ def model_seed(name: str) -> int:
     return 20260101 + sorted(SPECS).index(name)
 
 
-def ensure_gguf(name: str, stress: bool = False, seed: int | None = None) -> str:
-    """Path of the cached random-init GGUF for SPECS[name] (generated on first use)."""
+def ensure_gguf(name: str, stress: bool = False, seed: int | None = None, metric_branch: bool = False) -> str:
+    """Path of the cached random-init GGUF for SPECS[name] (generated on first use);
+    metric_branch selects the nested metric-branch layout (m_vit.* / m_head.*)."""
     spec = SPECS[name]
     seed = model_seed(name) if seed is None else seed
-    key = hashlib.sha1(json.dumps([dataclasses.asdict(spec), seed, stress, 3]).encode()).hexdigest()[:10]
+    key_parts = [dataclasses.asdict(spec), seed, stress, 3] + ([1] if metric_branch else [])
+    key = hashlib.sha1(json.dumps(key_parts).encode()).hexdigest()[:10]
     os.makedirs(CACHE, exist_ok=True)
-    path = os.path.join(CACHE, f"{name}{'-stress' if stress else ''}-{key}.gguf")
+    tag = ("-stress" if stress else "") + ("-mbranch" if metric_branch else "")
+    path = os.path.join(CACHE, f"{name}{tag}-{key}.gguf")
     if not os.path.exists(path):
-        write_gguf(spec, path, seed, stress)
+        write_gguf(spec, path, seed, stress, metric_branch)
     return path
 
 

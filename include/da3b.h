@@ -183,6 +183,20 @@ DA3B_API int da3b_infer_prepared(da_ctx* ctx, const float* chw, int n_views, int
  * Host arrays, each may be NULL. */
 DA3B_API int da3b_last_pose(da_ctx* ctx, int n_views, float* pose_enc, float* ext, float* intr);
 
+/* Sky plane of the last run of a model with a sky head (DA3 mono / metric DPT,
+ * head.scratch.sky_out2a / sky_out2b; DptHead::depth_sky at src/dpt_head.cpp:396-400 with
+ * the relu of src/dpt_head.cpp:334-338): sky [n_views][H][W] host array. */
+DA3B_API int da3b_last_sky(da_ctx* ctx, int n_views, float* sky);
+
+/* Nested metric alignment on host arrays of n pixels (NestedAligner::process_mono_sky and
+ * ::align, src/nested.cpp:22-96, as Engine::depth_metric runs them at
+ * src/engine.cpp:446-449): metric_depth is sky-filled in place first; out_depth [n] and
+ * out_ext [12] receive the aligned depth and the translation-scaled anyview extrinsics.
+ * Returns the scale factor (negative on bad arguments). No GPU work. */
+DA3B_API float da3b_nested_align(const float* any_depth, const float* any_conf, const float* any_ext,
+                                 const float* any_intr, float* metric_depth, const float* sky, int64_t n,
+                                 float* out_depth, float* out_ext);
+
 /* Reference view chosen per scene by the last multi-view run (views_per_scene >= 3). */
 DA3B_API int da3b_ref_views(da_ctx* ctx, int* out, int n);
 /* Kernel launches of one forward of that shape (after one run of it). */
@@ -199,7 +213,8 @@ DA3B_API int da3b_set_act_quant(da_ctx* ctx, int on);
 /* 1 = the depth / confidence / ray outputs are the raw head logits (no output
  * activation), for parity checks against pre-activation reference values. */
 DA3B_API int da3b_set_raw_logits(da_ctx* ctx, int on);
-/* out[8] = {embed_dim, depth, num_heads, patch_size, cat_token, output_dim, has_aux, is_da2} */
+/* out[10] = {embed_dim, depth, num_heads, patch_size, cat_token, output_dim, has_aux, is_da2,
+ *            has_sky, has_camera} */
 DA3B_API int da3b_model_dims(da_ctx* ctx, int* out);
 
 #ifdef __cplusplus

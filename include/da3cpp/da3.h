@@ -1,6 +1,6 @@
 // da3.h — C++ API of libda3b, source-compatible with DA3cpplib's public header
-// (include/da3cpp/da3.h in DA3cpplib: Params :45-49, Image :58-62, ModelInfo :64-78,
-// Result :80-90, InferOptions :92-103, load_model :105, model_info :107,
+// (include/da3cpp/da3.h in DA3cpplib: Params :45-49, NestedParams :51-55, Image :58-62, ModelInfo :64-78,
+// Result :80-90, InferOptions :92-103, load_model :105, load_nested_model :106, model_info :107,
 // infer :109-110, infer_file :111-112, infer_preprocessed :119-126).
 //
 // Same types, names, argument meaning and error behaviour (bool false / nullptr,
@@ -58,6 +58,13 @@ struct Params {
   int device = -1;    // CUDA device ordinal; -1 = $DA3B_DEVICE or 0
 };
 
+// Nested metric model (reference :51-55): DA3 anyview model + metric branch.
+struct NestedParams {
+  std::string anyview_model_path;
+  std::string metric_model_path;
+  int n_threads = 4;  // host threads (unused by the GPU path)
+};
+
 // Interleaved RGB8 image (width * height * 3 bytes).
 struct Image {
   int width = 0;
@@ -100,6 +107,7 @@ struct InferOptions {
 };
 
 DA3_API std::shared_ptr<Model> load_model(const Params& params);
+DA3_API std::shared_ptr<Model> load_nested_model(const NestedParams& params);
 DA3_API ModelInfo model_info(const Model& model);
 
 DA3_API bool infer(Model& model, const Image& image, Result& result, const InferOptions& options = {});

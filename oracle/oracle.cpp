@@ -639,7 +639,10 @@ class Oracle {
   // DptHead::build_depth_graph (src/dpt_head.cpp:75-275) for one image. feats[s]:
   // [Npatch][C] token-major. Returns main logits [od][H][W]; aux logits [7][Ha][Wa]
   // when the aux tensors exist and want_aux.
-  Map head(const std::vector<const float*>& feats, int Cf, int H, int W, bool want_aux, Map* aux_out, const std::string& cap) {
+  // sky_out (when non-null and the sky tensors exist) receives the sky logits [1][H][W]
+  // of the metric / mono DPT (src/dpt_head.cpp:205-222).
+  Map head(const std::vector<const float*>& feats, int Cf, int H, int W, bool want_aux, Map* aux_out, const std::string& cap,
+           Map* sky_out = nullptr) {
     const int P = c.patch_size, pw = W / P, ph = H / P, N = pw * ph;
     const float aspect = static_cast<float>(W) / H;
     const bool hn = has("head.norm.weight");
@@ -673,6 +676,11 @@ class Oracle {
     caps[cap + "out1"] = out.v;
     out = interp_ac(out, W, H);
     if (c.head_pos_embed) add_inplace(out, uv_embed(W, H, out.C, aspect, 0.1f));
+    if (sky_out && has("head.scratch.sky_out2b.weight")) {
+      Map sk = conv2d(out, "head.scratch.sky_out2a.weight", "head.scratch.sky_out2a.bias", 1, 1);
+      relu_inplace(sk);
+      *sky_out = conv2d(sk, "head.scratch.sky_out2b.weight", "head.scratch.sky_out2b.bias", 1, 0);
+    }
     out = conv2d(out, "head.scratch.out2a.weight", "head.scratch.out2a.bias", 1, 1);
     relu_inplace(out);
     out = conv2d(out, "head.scratch.out2b.weight", "head.scratch.out2b.bias", 1, 0);
@@ -1077,7 +1085,7 @@ bool preprocess(const Img& img, const or_config& c, bool legacy, std::vector<flo
 
 struct Handle {
   Oracle o;
-  std::vector<float> depth, conf, logits, aux, chw, pose;
+  std::vector<float> depth, conf, logits, aux, chw, pose, sky;
   std::vector<std::vector<float>> feats;
   int H = 0, W = 0, od = 0, aux_h = 0, aux_w = 0, b_idx = 0;
 };
@@ -1173,15 +1181,12 @@ OR_API int or_uv_pos_embed(int pw, int ph, int C, float aspect, float* out) {
 // DA2 route: preprocess_real -> forward -> depth_relative (src/engine.cpp:121-130,
 // src/dpt_head.cpp:402-439); DA3 route: preprocess_real -> fused feats -> head ->
 // exp / exp+1 (src/engine.cpp:189-229). legacy=1 uses the floor-to-patch preprocess.
-OR_API int or_infer(void* p, const uint8_t* rgb, int w, int hgt, int legacy, int want_aux) {
-  auto* h = static_cast<Handle*>(p);
+namespace {
+// Forward + head + output activations of one normalised planar image held in h->chw
+// (src/engine.cpp:189-229; mono: src/engine.cpp:105-115 and the sky relu of
+// src/dpt_head.cpp:334-338).
+int infer_chw(Handle* h, int H, int W, int want_aux) {
   Oracle& o = h->o;
-  Img img;
-  img.w = w;
-  img.h = hgt;
-  img.rgb.assign(rgb, rgb + static_cast<size_t>(w) * hgt * 3);
-  int H = 0, W = 0;
-  if (!preprocess(img, o.c, legacy != 0, h->chw, H, W)) return -1;
   h->H = H;
   h->W = W;
   std::vector<std::vector<float>> views{h->chw};
@@ -1192,8 +1197,8 @@ OR_API int or_infer(void* p, const uint8_t* rgb, int w, int hgt, int legacy, int
   h->pose.assign(30, 0.f);
   if (!o.pose(cams[3].data(), Cf, H, W, h->pose.data())) h->pose.clear();
   std::vector<const float*> f4 = {h->feats[0].data(), h->feats[1].data(), h->feats[2].data(), h->feats[3].data()};
-  Oracle::Map aux;
-  Oracle::Map lg = o.head(f4, Cf, H, W, want_aux != 0, &aux, "");
+  Oracle::Map aux, sky;
+  Oracle::Map lg = o.head(f4, Cf, H, W, want_aux != 0, &aux, "", &sky);
   h->od = lg.C;
   h->logits = lg.v;
   const size_t HW = static_cast<size_t>(H) * W;
@@ -1209,10 +1214,41 @@ OR_API int or_infer(void* p, const uint8_t* rgb, int w, int hgt, int legacy, int
       for (size_t i = 0; i < HW; ++i) h->conf[i] = std::exp(lg.v[HW + i]) + 1.0f;
     }
   }
+  h->sky.clear();
+  if (sky.v.size() == HW) {
+    h->sky.resize(HW);
+    for (size_t i = 0; i < HW; ++i) h->sky[i] = std::max(0.0f, sky.v[i]);
+  }
   h->aux = aux.v;
   h->aux_h = aux.H;
   h->aux_w = aux.W;
   return 0;
+}
+}  // namespace
+
+// Single image: RGB8 HWC -> depth (+conf, +sky) at the processed size.
+// DA2 route: preprocess_real -> forward -> depth_relative (src/engine.cpp:121-130,
+// src/dpt_head.cpp:402-439); DA3 route: preprocess_real -> fused feats -> head ->
+// exp / exp+1 (src/engine.cpp:189-229). legacy=1 uses the floor-to-patch preprocess.
+OR_API int or_infer(void* p, const uint8_t* rgb, int w, int hgt, int legacy, int want_aux) {
+  auto* h = static_cast<Handle*>(p);
+  Img img;
+  img.w = w;
+  img.h = hgt;
+  img.rgb.assign(rgb, rgb + static_cast<size_t>(w) * hgt * 3);
+  int H = 0, W = 0;
+  if (!preprocess(img, h->o.c, legacy != 0, h->chw, H, W)) return -1;
+  return infer_chw(h, H, W, want_aux);
+}
+
+// The same from an already normalised planar f32 image [3][H][W] (the input the nested
+// path shares between its two branches, src/engine.cpp:418-421).
+OR_API int or_infer_chw(void* p, const float* chw, int H, int W, int want_aux) {
+  auto* h = static_cast<Handle*>(p);
+  const int P = h->o.c.patch_size;
+  if (H <= 0 || W <= 0 || H % P || W % P) return -1;
+  h->chw.assign(chw, chw + static_cast<size_t>(3) * H * W);
+  return infer_chw(h, H, W, want_aux);
 }
 
 // Multi-view (S views, same size): src/engine.cpp:352-384 + forward_mv
@@ -1301,6 +1337,7 @@ OR_API int64_t or_get(void* p, const char* name, const float** out) {
   else if (n == "aux") v = &h->aux;
   else if (n == "chw") v = &h->chw;
   else if (n == "pose") v = &h->pose;
+  else if (n == "sky") v = &h->sky;
   else if (n.size() == 5 && n.compare(0, 4, "feat") == 0) {
     const int l = n[4] - '0';
     if (l >= 0 && l < static_cast<int>(h->feats.size())) v = &h->feats[l];
@@ -1321,4 +1358,71 @@ OR_API void or_dims(void* p, int* H, int* W, int* od, int* aux_h, int* aux_w, in
   *aux_h = h->aux_h;
   *aux_w = h->aux_w;
   *b_idx = h->b_idx;
+}
+
+// ====================================================================== nested metric alignment
+// Restatement of NestedAligner (src/nested.cpp:7-96) for the checker: torch.quantile with
+// linear interpolation over a full sort, the mono sky fill, then the alignment.
+namespace {
+float or_quantile(std::vector<float> v, float q) {  // src/nested.cpp:7-20
+  if (v.empty()) return 0.0f;
+  std::sort(v.begin(), v.end());
+  const size_t n = v.size();
+  if (n == 1) return v[0];
+  const double pos = static_cast<double>(q) * static_cast<double>(n - 1);
+  const double fl = std::floor(pos);
+  const size_t i0 = static_cast<size_t>(fl);
+  const size_t i1 = std::min(static_cast<size_t>(std::ceil(pos)), n - 1);
+  return static_cast<float>(static_cast<double>(v[i0]) + (pos - fl) * (static_cast<double>(v[i1]) - static_cast<double>(v[i0])));
+}
+}  // namespace
+
+// metric_depth is sky-filled in place (src/nested.cpp:22-33) before the alignment
+// (src/nested.cpp:35-96); returns the scale factor.
+OR_API float or_nested_align(const float* any_depth, const float* any_conf, const float* any_ext, const float* any_intr,
+                             float* metric_depth, const float* sky, int64_t n, float* out_depth, float* out_ext) {
+  const size_t N = static_cast<size_t>(n);
+  {
+    std::vector<float> ns;
+    size_t n_sky = 0;
+    for (size_t i = 0; i < N; ++i) {
+      if (sky[i] < 0.3f) ns.push_back(metric_depth[i]);
+      else ++n_sky;
+    }
+    if (ns.size() > 10 && n_sky > 10) {
+      const float v = or_quantile(ns, 0.99f);
+      for (size_t i = 0; i < N; ++i)
+        if (!(sky[i] < 0.3f)) metric_depth[i] = v;
+    }
+  }
+  const float focal = (any_intr[0] + any_intr[4]) * 0.5f;
+  const float mscale = focal / 300.0f;
+  std::vector<float> conf_ns;
+  for (size_t i = 0; i < N; ++i)
+    if (sky[i] < 0.3f) conf_ns.push_back(any_conf[i]);
+  const float med = or_quantile(conf_ns, 0.5f);
+  double num = 0.0, den = 0.0;
+  for (size_t i = 0; i < N; ++i) {
+    const float md = metric_depth[i] * mscale;
+    if (sky[i] < 0.3f && any_conf[i] >= med && md > 1e-2f && any_depth[i] > 1e-3f) {
+      num += static_cast<double>(md) * static_cast<double>(any_depth[i]);
+      den += static_cast<double>(any_depth[i]) * static_cast<double>(any_depth[i]);
+    }
+  }
+  if (den < 1e-12) den = 1e-12;
+  const float sf = static_cast<float>(num / den);
+  for (int k = 0; k < 12; ++k) out_ext[k] = any_ext[k];
+  out_ext[3] *= sf;
+  out_ext[7] *= sf;
+  out_ext[11] *= sf;
+  std::vector<float> d_ns;
+  for (size_t i = 0; i < N; ++i) {
+    out_depth[i] = any_depth[i] * sf;
+    if (sky[i] < 0.3f) d_ns.push_back(out_depth[i]);
+  }
+  float cap = or_quantile(d_ns, 0.99f);
+  if (cap > 200.0f) cap = 200.0f;
+  for (size_t i = 0; i < N; ++i)
+    if (!(sky[i] < 0.3f)) out_depth[i] = cap;
+  return sf;
 }

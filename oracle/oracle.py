@@ -26,11 +26,11 @@ REF_SRC_DIR = os.environ.get("DA3_REFERENCE_SRC", "/root/reference/src")
 REF_DIR = os.path.join(HERE, "_ref")
 REF_LIB = os.path.join(REF_DIR, "libda3ref.so")
 # DA3cpplib's own host-only sources on the path, compiled unmodified (never copied).
-REF_SOURCES = ["preprocess.cpp", "uv_posembed.cpp"]
+REF_SOURCES = ["preprocess.cpp", "uv_posembed.cpp", "nested.cpp"]
 
 
 def build_ref(force: bool = False):
-    """Compile the reference's preprocess.cpp + uv_posembed.cpp with ref_wrap.cpp into
+    """Compile the reference's preprocess.cpp, uv_posembed.cpp and nested.cpp with ref_wrap.cpp into
     oracle/_ref/libda3ref.so. Returns the library path, or None when the reference
     checkout is absent (the prebuilt library, if shipped, is still used)."""
     srcs = [os.path.join(REF_SRC_DIR, f) for f in REF_SOURCES]
@@ -68,6 +68,8 @@ def ref_lib():
                                      ctypes.c_void_p, ctypes.c_int64]
         R.ref_resize.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 5 + [ctypes.c_void_p]
         R.ref_uv_pos_embed.argtypes = [ctypes.c_int] * 3 + [ctypes.c_float, ctypes.c_void_p]
+        R.ref_nested_align.restype = ctypes.c_float
+        R.ref_nested_align.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
         _ref = R
     return _ref
 
@@ -123,6 +125,9 @@ def lib():
                                         ctypes.c_int64, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]
         L.or_resize.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 5 + [ctypes.c_void_p]
         L.or_uv_pos_embed.argtypes = [ctypes.c_int] * 3 + [ctypes.c_float, ctypes.c_void_p]
+        L.or_infer_chw.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.or_nested_align.restype = ctypes.c_float
+        L.or_nested_align.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
         L.or_get.restype = ctypes.c_int64
         L.or_get.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.POINTER(ctypes.c_float))]
         L.or_dims.argtypes = [ctypes.c_void_p] + [ctypes.POINTER(ctypes.c_int)] * 6
@@ -158,9 +163,20 @@ def read_gguf(path):
 
 
 def config_from_kv(kv, act_quant=True, n_threads=0):
+    """or_config from GGUF keys; a nested metric-branch file (m_vit.* / m_head.* keys) is
+    read the way src/model_loader.cpp:84-127 reads it (head pos-embed off by default)."""
     P = "depthanything3."
     c = OrConfig()
-    g = lambda k, d: kv.get(P + k, d)
+    metric = (P + "m_vit.embed_dim") in kv
+
+    def g(k, d):
+        if metric and k.startswith("vit."):
+            k = "m_" + k
+        elif metric and k.startswith("head.") and k not in ("head.max_depth", "head.has_aux"):
+            k = "m_" + k
+            if k == "m_head.pos_embed":
+                d = False
+        return kv.get(P + k, d)
     c.patch_size = g("patch_size", 14)
     c.embed_dim = g("vit.embed_dim", 0)
     c.depth = g("vit.depth", 0)
@@ -199,9 +215,18 @@ def config_from_kv(kv, act_quant=True, n_threads=0):
 class Oracle:
     """CPU restatement of the reference depth path over a GGUF file."""
 
-    def __init__(self, gguf_path, act_quant=True, n_threads=0):
+    def __init__(self, gguf_path, act_quant=True, n_threads=0, swap=None):
+        """swap: optional {name_a: name_b} pairs whose tensors trade places (tests that
+        route one head's weights through another head's code)."""
         L = lib()
         self.kv, self._tensors = read_gguf(gguf_path)
+        if swap:
+            pairs = dict(swap)
+            pairs.update({b: a for a, b in swap.items()})
+            self._tensors = [(pairs.get(n, n), d, t, ne) for n, d, t, ne in self._tensors]
+        # metric-branch tensors are also reachable as vit.* / head.* (src/model_loader.cpp:146-154)
+        self._tensors = self._tensors + [(n[2:], d, t, ne) for n, d, t, ne in self._tensors
+                                         if n.startswith(("m_vit.", "m_head."))]
         self.cfg = config_from_kv(self.kv, act_quant, n_threads)
         arr = (OrTensor * len(self._tensors))()
         self._names = []
@@ -257,6 +282,9 @@ class Oracle:
         rc = lib().or_infer(self.h, rgb.ctypes.data, w, h, int(legacy), int(aux))
         if rc != 0:
             raise RuntimeError(f"oracle infer failed {rc}")
+        return self._outputs(aux)
+
+    def _outputs(self, aux):
         H, W, od, ah, aw, _ = self.dims()
         out = {"H": H, "W": W, "depth": self.get("depth").reshape(H, W), "logits": self.get("logits").reshape(od, H, W)}
         conf = self.get("conf")
@@ -267,7 +295,19 @@ class Oracle:
         pose = self.get("pose")
         if pose is not None and pose.size:  # [9 pose encoding | 12 extrinsics | 9 intrinsics]
             out["pose"] = pose.reshape(30)
+        sky = self.get("sky")
+        if sky is not None and sky.size:
+            out["sky"] = sky.reshape(H, W)
         return out
+
+    def infer_chw(self, chw, aux=False):
+        """Forward from a normalised planar f32 image [3][H][W] (no preprocessing)."""
+        chw = np.ascontiguousarray(chw, dtype=np.float32)
+        _, H, W = chw.shape
+        rc = lib().or_infer_chw(self.h, chw.ctypes.data, H, W, int(aux))
+        if rc != 0:
+            raise RuntimeError(f"oracle infer_chw failed {rc}")
+        return self._outputs(aux)
 
     def infer_mv(self, rgbs, legacy=True, aux=False):
         rgbs = [np.ascontiguousarray(r, dtype=np.uint8) for r in rgbs]
@@ -362,3 +402,24 @@ def uv_pos_embed(pw, ph, C, aspect, impl="oracle"):
     if rc != 0:
         raise RuntimeError(f"uv_pos_embed failed ({impl}): {rc}")
     return out
+
+
+def nested_align(any_depth, any_conf, any_ext, any_intr, metric_depth, sky, impl="oracle"):
+    """Nested metric alignment (src/nested.cpp:22-96: sky fill of the metric depth, then
+    the alignment). impl="oracle" runs the restatement, impl="ref" the reference's own
+    nested.cpp. Returns (depth, ext [12], scale)."""
+    a = [np.ascontiguousarray(x, dtype=np.float32).reshape(-1) for x in
+         (any_depth, any_conf, any_ext, any_intr, metric_depth, sky)]
+    a[4] = a[4].copy()
+    n = a[0].size
+    out = np.zeros(n, np.float32)
+    ext = np.zeros(12, np.float32)
+    if impl == "ref":
+        R = ref_lib()
+        if R is None:
+            raise RuntimeError("oracle/_ref is not built")
+        fn = R.ref_nested_align
+    else:
+        fn = lib().or_nested_align
+    scale = fn(*[x.ctypes.data for x in a], n, out.ctypes.data, ext.ctypes.data)
+    return out, ext, float(scale)

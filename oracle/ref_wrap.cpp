@@ -2,7 +2,8 @@
 // checkout into oracle/_ref/ — test infrastructure only, never part of libda3b.
 //
 // Only src/preprocess.cpp (the real/legacy preprocess and the uint8 cubic/area
-// resizers) and src/uv_posembed.cpp are compiled: they need nothing from ggml beyond
+// resizers), src/uv_posembed.cpp and src/nested.cpp (the nested metric alignment) are
+// compiled: they need nothing from ggml beyond
 // the opaque type names that model_loader.hpp mentions (oracle/ref_shim/). Everything
 // else on the depth path goes through ggml graphs, whose source is absent from the
 // reference checkout, so it cannot be built here.
@@ -10,6 +11,7 @@
 #include <cstring>
 #include <vector>
 
+#include "nested.hpp"
 #include "preprocess.hpp"
 #include "uv_posembed.hpp"
 
@@ -73,4 +75,27 @@ REF_API int ref_uv_pos_embed(int pw, int ph, int C, float aspect, float* out) {
   if (v.size() != static_cast<size_t>(pw) * ph * C) return -1;
   std::memcpy(out, v.data(), v.size() * sizeof(float));
   return 0;
+}
+
+// NestedAligner::process_mono_sky on metric_depth (in place), then NestedAligner::align.
+// Returns the scale factor.
+REF_API float ref_nested_align(const float* any_depth, const float* any_conf, const float* any_ext,
+                               const float* any_intr, float* metric_depth, const float* sky, int64_t n,
+                               float* out_depth, float* out_ext) {
+  const size_t N = static_cast<size_t>(n);
+  da::AnyviewOut any;
+  any.depth.assign(any_depth, any_depth + N);
+  any.depth_conf.assign(any_conf, any_conf + N);
+  for (int k = 0; k < 12; ++k) any.extrinsics[k] = any_ext[k];
+  for (int k = 0; k < 9; ++k) any.intrinsics[k] = any_intr[k];
+  da::MetricOut m;
+  m.depth.assign(metric_depth, metric_depth + N);
+  m.sky.assign(sky, sky + N);
+  da::NestedAligner::process_mono_sky(m.depth, m.sky);
+  std::memcpy(metric_depth, m.depth.data(), N * sizeof(float));
+  // align() takes H and W only for their product
+  const da::NestedOut r = da::NestedAligner::align(any, m, 1, static_cast<int>(N));
+  std::memcpy(out_depth, r.depth.data(), N * sizeof(float));
+  for (int k = 0; k < 12; ++k) out_ext[k] = r.extrinsics[k];
+  return r.scale_factor;
 }

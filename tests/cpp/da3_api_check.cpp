@@ -1,6 +1,6 @@
 // C++ API check of libda3b (include/da3cpp/da3.h), built and run by tests/test_cpp_api_gpu.py.
 //
-//   da3_api_check <da3 gguf> <da2 gguf> <size>
+//   da3_api_check <da3 gguf> <da2 gguf> <size> [<mono gguf> <metric-branch gguf>]
 //
 // 1. load_model + model_info on a DA3 checkpoint;
 // 2. infer() on a seeded RGB8 image at the processed size;
@@ -9,7 +9,11 @@
 //    the callback into the device buffer the library hands out: depth and confidence
 //    must be bit-identical to step 2;
 // 4. the reference's refusals: infer_preprocessed on a DA2 checkpoint, infer() on an
-//    image whose data size does not match, both return false with an empty Result.
+//    image whose data size does not match, both return false with an empty Result;
+// 5. (with the optional models) DA3 mono: kind, depth + sky and no confidence, refusal of
+//    with_pose and infer_preprocessed; nested: load_nested_model with the DA3 model as the
+//    anyview branch, kind / camera pose / metric flags, depth + pose without confidence or
+//    sky, and the infer_preprocessed refusal (src/api.cpp:95-161, :184).
 // Prints "OK" and exits 0 when every check holds.
 #include <cuda_runtime.h>
 
@@ -77,6 +81,38 @@ int main(int argc, char** argv) {
   bad.data.pop_back();
   CHECK(!da3::infer(*model, bad, c));
   CHECK(c.depth.empty());
+
+  if (argc >= 6) {
+    da3::Params pm;
+    pm.model_path = argv[4];
+    auto mono = da3::load_model(pm);
+    CHECK(mono);
+    const da3::ModelInfo mi = da3::model_info(*mono);
+    CHECK(mi.kind == da3::ModelKind::da3_mono && mi.is_metric && !mi.has_camera_pose);
+    da3::Result r;
+    CHECK(da3::infer(*mono, img, r));
+    CHECK(r.depth.size() == static_cast<size_t>(n) * n && r.sky.size() == r.depth.size() && r.confidence.empty());
+    CHECK(!r.has_pose && r.is_metric);
+    da3::InferOptions wp;
+    wp.with_pose = true;
+    CHECK(!da3::infer(*mono, img, r, wp) && r.depth.empty());
+    CHECK(!da3::infer_preprocessed(*mono, n, n, [&](const da3::UploadTarget&) {}, r));
+
+    da3::NestedParams np;
+    np.anyview_model_path = argv[1];
+    np.metric_model_path = argv[5];
+    auto nested = da3::load_nested_model(np);
+    CHECK(nested);
+    const da3::ModelInfo ni = da3::model_info(*nested);
+    CHECK(ni.kind == da3::ModelKind::da3_nested && ni.is_metric && ni.has_camera_pose);
+    da3::Result q;
+    CHECK(da3::infer(*nested, img, q));
+    CHECK(q.depth.size() == static_cast<size_t>(n) * n && q.confidence.empty() && q.sky.empty());
+    CHECK(q.has_pose && q.is_metric && q.intrinsics[8] == 1.f);
+    CHECK(!da3::infer_preprocessed(*nested, n, n, [&](const da3::UploadTarget&) {}, q));
+    np.metric_model_path.clear();
+    CHECK(!da3::load_nested_model(np));
+  }
   std::printf("OK\n");
   return 0;
 }

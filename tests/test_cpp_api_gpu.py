@@ -2,7 +2,8 @@
 compiled with g++ against the public headers and libda3b.so and run on the GPU. It checks
 load_model / model_info / infer, that infer_preprocessed with the reference's upload
 callback gives depth and confidence bit-identical to infer on the same image, and the
-reference's refusals (DA2 checkpoint on infer_preprocessed, malformed Image)."""
+reference's refusals (DA2 checkpoint on infer_preprocessed, malformed Image), and the DA3
+mono and nested metric model kinds through load_model / load_nested_model / infer."""
 import os
 import shutil
 import subprocess
@@ -33,5 +34,7 @@ def test_cpp_api(lib, tmp_path):
     assert r.returncode == 0, r.stderr
     da3 = synth.ensure_gguf("da3-t", stress=True)
     da2 = synth.ensure_gguf("da2-t", stress=True)
-    r = subprocess.run([str(exe), da3, da2, "112"], capture_output=True, text=True, timeout=300)
+    mono = synth.ensure_gguf("da3m-t", stress=True)
+    metric = synth.ensure_gguf("da3m-t", stress=True, metric_branch=True)
+    r = subprocess.run([str(exe), da3, da2, "112", mono, metric], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "OK" in r.stdout, r.stdout + r.stderr

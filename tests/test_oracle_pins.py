@@ -111,3 +111,32 @@ def test_da2_matches_transformers(orc, tag):
     ref = z[tag + "_depth"]
     assert np.abs(r["depth"] - ref).max() <= 1e-4 * np.abs(ref).max()
     assert (ref > 0).mean() > 0.3  # a live (not all-ReLU-zero) output
+
+
+def test_sky_head_is_the_out2_stack(orc):
+    """The sky head (src/dpt_head.cpp:205-222) is conv3x3 -> relu -> conv1x1 on the same
+    feature map as output_conv2, followed by relu (src/dpt_head.cpp:334-338): with the
+    sky and out2 weights swapped, the oracle's sky equals relu(main logits) of the swap,
+    tying the sky head to the output_conv2 code that the transformers pin covers."""
+    from da3cpplib_b200 import synth
+
+    path = synth.ensure_gguf("da3m-t", stress=True)
+    img = synth.image(synth.IMAGE_SEED, 43, 126, 112)
+    a = orc.Oracle(path, act_quant=False).infer(img)
+    swap = {f"head.scratch.out2{x}.{k}": f"head.scratch.sky_out2{x}.{k}" for x in "ab" for k in ("weight", "bias")}
+    b = orc.Oracle(path, act_quant=False, swap=swap).infer(img)
+    np.testing.assert_array_equal(a["sky"], np.maximum(b["logits"][0], 0))
+    np.testing.assert_array_equal(b["sky"], np.maximum(a["logits"][0], 0))
+    assert 0.2 < (a["sky"] < 0.3).mean() < 0.9  # both sides of the sky threshold occur
+
+
+def test_metric_branch_layout_oracle(orc):
+    """m_vit.* / m_head.* files read like the plain layout (src/model_loader.cpp:84-154)."""
+    from da3cpplib_b200 import synth
+
+    img = synth.image(synth.IMAGE_SEED, 44, 112, 112)
+    a = orc.Oracle(synth.ensure_gguf("da3m-t", stress=True)).infer(img)
+    b = orc.Oracle(synth.ensure_gguf("da3m-t", stress=True, metric_branch=True)).infer(img)
+    np.testing.assert_array_equal(a["depth"], b["depth"])
+    np.testing.assert_array_equal(a["sky"], b["sky"])
+    assert "conf" not in a
