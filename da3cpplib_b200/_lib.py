@@ -47,6 +47,8 @@ SIGNATURES = {
     "da3b_infer_prepared": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "da3b_last_pose": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "da3b_last_sky": (c_int, [c_void_p, c_int, c_void_p]),
+    "da3b_ray_pose": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                              c_void_p, c_void_p]),
     "da3b_nested_align": (ctypes.c_float, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_int64,
                                            c_void_p, c_void_p]),
     "da3b_ref_views": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int]),

@@ -27,6 +27,11 @@ NVCC_FLAGS = ARCH + [
 ]
 
 
+# Per-file extra flags. raypose.cu's double arithmetic must round like the reference's
+# host code, so no multiply-add contraction there.
+FILE_FLAGS = {"raypose.cu": ["-fmad=false"]}
+
+
 def _nvcc() -> str:
     for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
         if cand and os.path.exists(cand):
@@ -63,9 +68,10 @@ def build(verbose: bool = False, force: bool = False) -> str:
         obj = os.path.join(OBJDIR, os.path.basename(src) + ".o")
         objs.append(obj)
         if force or not os.path.exists(obj) or os.path.getmtime(obj) < max(os.path.getmtime(src), hdr):
-            cmd = [nvcc] + NVCC_FLAGS + ["-c", src, "-o", obj]
+            extra = FILE_FLAGS.get(os.path.basename(src), [])
+            cmd = [nvcc] + NVCC_FLAGS + extra + ["-c", src, "-o", obj]
             if src.endswith(".cpp"):
-                cmd = [nvcc] + NVCC_FLAGS + ["-x", "cu", "-c", src, "-o", obj]
+                cmd = [nvcc] + NVCC_FLAGS + extra + ["-x", "cu", "-c", src, "-o", obj]
             jobs.append(cmd)
 
     def run(cmd):

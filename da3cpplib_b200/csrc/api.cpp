@@ -21,6 +21,7 @@
 #include "nested.h"
 #include "pose.h"
 #include "preprocess.h"
+#include "raypose.h"
 
 #define DA_LOG(...)                     \
   do {                                  \
@@ -39,6 +40,8 @@ struct da_ctx {
   // preprocess_real on the GPU for inputs that need a resize: original image upload
   // buffer and processed-size output (grow-only), tap tables and scratch
   std::unique_ptr<da3b::Resizer> resizer;
+  // ray -> pose solver scratch (InferOptions::ray_pose, da3b_ray_pose)
+  std::unique_ptr<da3b::RaySolver> raysolver;
   uint8_t* in_dev = nullptr;
   size_t in_cap = 0;
   uint8_t* pre_dev = nullptr;
@@ -47,6 +50,7 @@ struct da_ctx {
     if (engine) cudaSetDevice(engine->device());
     if (stream) cudaStreamSynchronize(stream);
     resizer.reset();
+    raysolver.reset();
     if (in_dev) cudaFree(in_dev);
     if (pre_dev) cudaFree(pre_dev);
     if (stream) cudaStreamDestroy(stream);
@@ -164,9 +168,10 @@ bool run_legacy(da_ctx* c, const uint8_t* rgb, int n, int S, int w, int h, std::
   return true;
 }
 
-// Single-image inference at the processed size (H2D, forward, D2H).
+// Single-image inference at the processed size (H2D, forward, D2H). rays: also run the
+// aux ray head, leaving its planes on the device (Engine::last_rays).
 bool run_one(da_ctx* c, const uint8_t* rgb, int w, int h, bool legacy, std::vector<float>& depth,
-             std::vector<float>* conf, int* oh, int* ow) {
+             std::vector<float>* conf, int* oh, int* ow, bool rays = false) {
   da3b::Engine& e = *c->engine;
   int W = 0, H = 0;
   processed_size(e.config(), w, h, legacy, &W, &H);
@@ -206,7 +211,8 @@ bool run_one(da_ctx* c, const uint8_t* rgb, int w, int h, bool legacy, std::vect
   const bool want_conf = conf && e.output_dim() >= 2;
   if (want_conf) conf->resize(static_cast<size_t>(H) * W);
   cudaSetDevice(e.device());
-  const int rc = e.run(rgb, 1, 1, H, W, depth.data(), want_conf ? conf->data() : nullptr, nullptr, c->stream);
+  const int rc = rays ? e.run_with_rays(rgb, 1, 1, H, W, depth.data(), want_conf ? conf->data() : nullptr, c->stream)
+                      : e.run(rgb, 1, 1, H, W, depth.data(), want_conf ? conf->data() : nullptr, nullptr, c->stream);
   if (rc != 0 || cudaStreamSynchronize(c->stream) != cudaSuccess || e.status() != 0) {
     c->last_error = "depth: forward failed: " + e.last_error();
     return false;
@@ -370,17 +376,19 @@ bool infer(Model& model, const Image& image, Result& result, const InferOptions&
     result.has_pose = true;
     return !result.depth.empty();
   }
-  if (options.ray_pose) {
-    DA_LOG("infer: the ray-based pose solver is not part of this build");
+  // src/api.cpp:130-158: the ray solver only with with_pose, never with legacy_resize,
+  // and only for DA3 models with the aux ray head
+  if (options.ray_pose && (!options.with_pose || options.legacy_resize || e.config().is_da2() || is_mono(e) ||
+                           !e.has_aux()))
     return false;
-  }
-  if (options.with_pose && (e.config().is_da2() || is_mono(e) || !e.has_camera())) return false;
+  if (options.with_pose && !options.ray_pose && (e.config().is_da2() || is_mono(e) || !e.has_camera())) return false;
   // DA2 and mono always use preprocess_real (src/engine.cpp:105-130); DA3 uses it
   // unless legacy_resize (src/api.cpp:151-157).
   const bool mono = is_mono(e);
   const bool legacy = !e.config().is_da2() && !mono && options.legacy_resize;
   int H = 0, W = 0;
-  if (!run_one(c, image.data.data(), image.width, image.height, legacy, result.depth, &result.confidence, &H, &W) ||
+  if (!run_one(c, image.data.data(), image.width, image.height, legacy, result.depth, &result.confidence, &H, &W,
+               options.ray_pose) ||
       (mono && !fetch_sky(c, *c->engine, result.depth.size(), result.sky))) {
     DA_LOG("infer: %s", c->last_error.c_str());
     result = {};
@@ -389,7 +397,24 @@ bool infer(Model& model, const Image& image, Result& result, const InferOptions&
   result.height = H;
   result.width = W;
   result.is_metric = model_info(model).is_metric;
-  if (options.with_pose) {
+  if (options.ray_pose) {
+    // Engine::depth_pose_rays_native (src/engine.cpp:296-328): the solver on this
+    // forward's ray field; camera-to-world extrinsics
+    int nv = 0, rh = 0, rw = 0;
+    const float* rays = c->engine->last_rays(&nv, &rh, &rw);
+    if (!c->raysolver) c->raysolver.reset(new da3b::RaySolver());
+    da3b::RayPoseResult rp;
+    std::string err;
+    const int rc = rays ? c->raysolver->solve(rays, nv, 0, rh, rw, H, W, c->stream, &rp, &err) : -1;
+    if (rc != 0) {
+      DA_LOG("infer: ray->pose solver failed (%d) %s", rc, err.c_str());
+      result = {};
+      return false;
+    }
+    memcpy(result.extrinsics.data(), rp.ext, sizeof(rp.ext));
+    memcpy(result.intrinsics.data(), rp.intr, sizeof(rp.intr));
+    result.has_pose = true;
+  } else if (options.with_pose) {
     // CamPose::pose on this forward's camera token (src/api.cpp:136-150, src/engine.cpp:271-286)
     std::vector<float> pe;
     if (c->engine->poses(pe, c->stream) != 0) {
@@ -808,6 +833,38 @@ DA3B_API int da3b_last_pose(da_ctx* c, int n_views, float* pose_enc, float* ext,
     da3b::pose_to_ext_intr(&pe[static_cast<size_t>(v) * 9], H, W, e, k);
     if (ext) memcpy(ext + v * 12, e, sizeof(e));
     if (intr) memcpy(intr + v * 9, k, sizeof(k));
+  }
+  return 0;
+}
+
+DA3B_API int da3b_ray_pose(da_ctx* c, const float* rays_dev, int n_views, int view, int ray_h, int ray_w, int img_h,
+                           int img_w, float* ext, float* intr, double* diag, void* stream) {
+  if (!c || !c->engine || !rays_dev || !ext || !intr) return -1;
+  cudaSetDevice(c->engine->device());
+  if (!c->raysolver) c->raysolver.reset(new da3b::RaySolver());
+  da3b::RayPoseResult r;
+  std::string err;
+  const int rc = c->raysolver->solve(rays_dev, n_views, view, ray_h, ray_w, img_h, img_w,
+                                     stream ? static_cast<cudaStream_t>(stream) : c->stream, &r, &err);
+  if (rc < 0) {
+    c->last_error = err;
+    return rc;
+  }
+  if (rc > 0) {
+    c->last_error = "ray pose: degenerate ray field";
+    return rc;
+  }
+  memcpy(ext, r.ext, sizeof(r.ext));
+  memcpy(intr, r.intr, sizeof(r.intr));
+  if (diag) {
+    memcpy(diag, r.R, 9 * sizeof(double));
+    memcpy(diag + 9, r.T, 3 * sizeof(double));
+    diag[12] = r.focal[0];
+    diag[13] = r.focal[1];
+    diag[14] = r.pp[0];
+    diag[15] = r.pp[1];
+    memcpy(diag + 16, r.A, 9 * sizeof(double));
+    diag[25] = r.n_inlier_best;
   }
   return 0;
 }

@@ -772,6 +772,31 @@ int Engine::run(const uint8_t* rgb, int V, int S, int H, int W, float* depth, fl
   return rc ? rc : copy_out(p, depth, conf, rays, s);
 }
 
+int Engine::run_with_rays(const uint8_t* rgb, int V, int S, int H, int W, float* depth, float* conf, cudaStream_t s) {
+  if (!model_->head.aux) {
+    err_ = "this GGUF has no auxiliary ray head";
+    return -70;
+  }
+  int code = 0;
+  Plan* p = checked_plan(V, S, H, W, true, &code);
+  if (!p) return code;
+  const size_t HW = static_cast<size_t>(H) * W;
+  if (cudaMemcpyAsync(p->rgb, rgb, static_cast<size_t>(V) * HW * 3, cudaMemcpyDefault, s) != cudaSuccess) {
+    err_ = "input copy failed";
+    return -5;
+  }
+  const int rc = launch(p, false, s);
+  return rc ? rc : copy_out(p, depth, conf, nullptr, s);
+}
+
+const float* Engine::last_rays(int* n_views, int* ray_h, int* ray_w) const {
+  if (!last_ || !last_->rays || !last_->raysbuf) return nullptr;
+  if (n_views) *n_views = last_->V;
+  if (ray_h) *ray_h = 8 * last_->gh;
+  if (ray_w) *ray_w = 8 * last_->gw;
+  return last_->raysbuf;
+}
+
 Plan* Engine::checked_plan(int V, int S, int H, int W, bool rays, int* code) {
   const Config& c = model_->cfg;
   if (V <= 0 || S <= 0 || V % S || H <= 0 || W <= 0 || H % c.patch_size || W % c.patch_size) {

@@ -42,6 +42,12 @@ class Engine {
   int run(const uint8_t* rgb_dev, int n_views, int views_per_scene, int H, int W, float* depth_dev,
           float* conf_dev, float* rays_dev, cudaStream_t s);
 
+  // The same forward with the aux ray head, whose output stays on the device:
+  // last_rays() then gives its planes [7][n_views][8*gh][8*gw] (null without one).
+  int run_with_rays(const uint8_t* rgb, int n_views, int views_per_scene, int H, int W, float* depth, float* conf,
+                    cudaStream_t s);
+  const float* last_rays(int* n_views, int* ray_h, int* ray_w) const;
+
   // Prepared-input runs (infer_preprocessed, src/api.cpp:178-193 / src/engine.cpp:230-270;
   // the legacy preprocess): device buffer for V normalised planar f32 images [V][3][H][W]
   // (scenes of S views) of the plan of that shape (allocated on first use; *bytes its

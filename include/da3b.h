@@ -183,6 +183,17 @@ DA3B_API int da3b_infer_prepared(da_ctx* ctx, const float* chw, int n_views, int
  * Host arrays, each may be NULL. */
 DA3B_API int da3b_last_pose(da_ctx* ctx, int n_views, float* pose_enc, float* ext, float* intr);
 
+/* Ray -> pose solver (use_ray_pose: solve_ray_pose at src/ray_pose.cpp:95-252 with its
+ * production defaults, as Engine::depth_pose_rays_native runs it, src/engine.cpp:296-328)
+ * on view `view` of a device ray field rays_dev [7][n_views][ray_h][ray_w] f32 (direction
+ * xyz, origin xyz, confidence; the layout da3b_infer_device's rays output has). ext [12]
+ * camera-to-world 3x4 and intr [9] (host), for an image of img_h x img_w; diag (host, 26
+ * doubles, may be NULL) = R (9), T (3), focal (2), pp (2), refit homography (9), best
+ * inlier count. Returns 0, 1 for a degenerate field (the reference's false), or a negative
+ * error. Synchronises the stream (NULL: the context's). */
+DA3B_API int da3b_ray_pose(da_ctx* ctx, const float* rays_dev, int n_views, int view, int ray_h, int ray_w,
+                           int img_h, int img_w, float* ext, float* intr, double* diag, void* stream);
+
 /* Sky plane of the last run of a model with a sky head (DA3 mono / metric DPT,
  * head.scratch.sky_out2a / sky_out2b; DptHead::depth_sky at src/dpt_head.cpp:396-400 with
  * the relu of src/dpt_head.cpp:334-338): sky [n_views][H][W] host array. */

@@ -21,6 +21,7 @@
 #include <map>
 #include <memory>
 #include <string>
+#include <random>
 #include <vector>
 
 #ifdef _OPENMP
@@ -1425,4 +1426,292 @@ OR_API float or_nested_align(const float* any_depth, const float* any_conf, cons
   for (size_t i = 0; i < N; ++i)
     if (!(sky[i] < 0.3f)) out_depth[i] = cap;
   return sf;
+}
+
+// ====================================================================== ray -> pose solver
+// Restatement of the host ray->pose solver (src/ray_pose.cpp:11-252, src/linalg.cpp:8-203)
+// for the checker: dense double linear algebra on 3x3 / 9x9 matrices, a weighted
+// homography RANSAC over the aux ray field, QL of the refit homography. Operation order
+// follows the reference so the double results agree to the bit.
+namespace {
+namespace rp {
+
+double sgn(double x) { return static_cast<double>((x > 0.0) - (x < 0.0)); }
+
+double det3(const double* a) {  // src/linalg.cpp:10-14
+  return a[0] * (a[4] * a[8] - a[5] * a[7]) - a[1] * (a[3] * a[8] - a[5] * a[6]) + a[2] * (a[3] * a[7] - a[4] * a[6]);
+}
+
+// Householder QR of an n x n row-major matrix with n-1 reflectors (LAPACK sign
+// convention, last diagonal untouched) (src/linalg.cpp:45-90).
+void qr(const double* a, int n, double* q, double* r) {
+  std::copy(a, a + n * n, r);
+  for (int i = 0; i < n * n; ++i) q[i] = (i / n == i % n) ? 1.0 : 0.0;
+  std::vector<double> v(n);
+  for (int k = 0; k + 1 < n; ++k) {
+    double nx = 0;
+    for (int i = k; i < n; ++i) nx += r[i * n + k] * r[i * n + k];
+    nx = std::sqrt(nx);
+    if (nx < 1e-300) continue;
+    const double alpha = r[k * n + k] >= 0.0 ? -nx : nx;
+    std::fill(v.begin(), v.end(), 0.0);
+    for (int i = k; i < n; ++i) v[i] = r[i * n + k];
+    v[k] -= alpha;
+    double vv = 0;
+    for (int i = k; i < n; ++i) vv += v[i] * v[i];
+    if (vv < 1e-300) continue;
+    for (int j = 0; j < n; ++j) {  // R <- (I - 2vv'/vv) R
+      double d = 0;
+      for (int i = k; i < n; ++i) d += v[i] * r[i * n + j];
+      const double f = 2.0 * d / vv;
+      for (int i = k; i < n; ++i) r[i * n + j] -= f * v[i];
+    }
+    for (int row = 0; row < n; ++row) {  // Q <- Q (I - 2vv'/vv)
+      double d = 0;
+      for (int i = k; i < n; ++i) d += q[row * n + i] * v[i];
+      const double f = 2.0 * d / vv;
+      for (int i = k; i < n; ++i) q[row * n + i] -= f * v[i];
+    }
+  }
+  for (int i = 0; i < n; ++i)
+    for (int j = 0; j < i; ++j) r[i * n + j] = 0.0;
+}
+
+// QL through QR of the column-reversed matrix, sign-normalised so diag(L) >= 0
+// (src/linalg.cpp:96-126).
+void ql3(const double* a, double* q, double* l) {
+  double ar[9], qr_q[9], qr_r[9];
+  for (int i = 0; i < 3; ++i)
+    for (int j = 0; j < 3; ++j) ar[i * 3 + j] = a[i * 3 + 2 - j];
+  qr(ar, 3, qr_q, qr_r);
+  for (int i = 0; i < 3; ++i)
+    for (int j = 0; j < 3; ++j) {
+      q[i * 3 + j] = qr_q[i * 3 + 2 - j];
+      l[i * 3 + j] = qr_r[(2 - i) * 3 + 2 - j];
+    }
+  const double s[3] = {sgn(l[0]), sgn(l[4]), sgn(l[8])};
+  for (int i = 0; i < 3; ++i)
+    for (int j = 0; j < 3; ++j) {
+      q[i * 3 + j] *= s[j];
+      l[i * 3 + j] *= s[i];
+    }
+}
+
+// Cyclic Jacobi eigen-decomposition of a symmetric n x n matrix, eigenvectors in the
+// columns of vec (src/linalg.cpp:128-172).
+void jacobi(const double* m, int n, double* val, double* vec) {
+  std::vector<double> a(m, m + n * n);
+  for (int i = 0; i < n * n; ++i) vec[i] = (i / n == i % n) ? 1.0 : 0.0;
+  for (int sweep = 0; sweep < 100; ++sweep) {
+    double off = 0;
+    for (int p = 0; p < n; ++p)
+      for (int q = p + 1; q < n; ++q) off += a[p * n + q] * a[p * n + q];
+    if (off < 1e-30) break;
+    for (int p = 0; p < n; ++p)
+      for (int q = p + 1; q < n; ++q) {
+        const double apq = a[p * n + q];
+        if (std::fabs(apq) < 1e-300) continue;
+        const double theta = (a[q * n + q] - a[p * n + p]) / (2.0 * apq);
+        double t = sgn(theta) / (std::fabs(theta) + std::sqrt(theta * theta + 1.0));
+        if (theta == 0.0) t = 1.0;
+        const double c = 1.0 / std::sqrt(t * t + 1.0), s = t * c;
+        for (int i = 0; i < n; ++i) {
+          const double x = a[i * n + p], y = a[i * n + q];
+          a[i * n + p] = c * x - s * y;
+          a[i * n + q] = s * x + c * y;
+        }
+        for (int i = 0; i < n; ++i) {
+          const double x = a[p * n + i], y = a[q * n + i];
+          a[p * n + i] = c * x - s * y;
+          a[q * n + i] = s * x + c * y;
+        }
+        for (int i = 0; i < n; ++i) {
+          const double x = vec[i * n + p], y = vec[i * n + q];
+          vec[i * n + p] = c * x - s * y;
+          vec[i * n + q] = s * x + c * y;
+        }
+      }
+  }
+  for (int i = 0; i < n; ++i) val[i] = a[i * n + i];
+}
+
+void smallest_vec(const double* m, int n, double* v) {  // src/linalg.cpp:174-181
+  std::vector<double> val(n), vec(n * n);
+  jacobi(m, n, val.data(), vec.data());
+  int k = 0;
+  for (int i = 1; i < n; ++i)
+    if (val[i] < val[k]) k = i;
+  for (int i = 0; i < n; ++i) v[i] = vec[i * n + k];
+}
+
+// Weighted DLT homography: smallest eigenvector of A'A, normalised by H[2][2]
+// (src/linalg.cpp:183-203).
+bool homography(const double* src, const double* dst, const double* w, int M, double* H) {
+  double ata[81] = {0};
+  for (int m = 0; m < M; ++m) {
+    const double x = src[2 * m], y = src[2 * m + 1], u = dst[2 * m], v = dst[2 * m + 1];
+    const double sw = std::sqrt(w[m] < 0 ? 0.0 : w[m]);
+    const double a[9] = {-x * sw, -y * sw, -sw, 0, 0, 0, x * u * sw, y * u * sw, u * sw};
+    const double b[9] = {0, 0, 0, -x * sw, -y * sw, -sw, x * v * sw, y * v * sw, v * sw};
+    for (int i = 0; i < 9; ++i)
+      for (int j = 0; j < 9; ++j) ata[i * 9 + j] += a[i] * a[j] + b[i] * b[j];
+  }
+  double h[9];
+  smallest_vec(ata, 9, h);
+  if (std::fabs(h[8]) < 1e-300) return false;
+  const double inv = 1.0 / h[8];
+  for (int i = 0; i < 9; ++i) H[i] = h[i] * inv;
+  return true;
+}
+
+}  // namespace rp
+}  // namespace
+
+OR_API void or_qr(const double* a, int n, double* q, double* r) { rp::qr(a, n, q, r); }
+OR_API void or_ql3(const double* a, double* q, double* l) { rp::ql3(a, q, l); }
+OR_API void or_smallest_eigvec(const double* m, int n, double* v) { rp::smallest_vec(m, n, v); }
+OR_API int or_homography(const double* src, const double* dst, const double* w, int M, double* H) {
+  return rp::homography(src, dst, w, M, H) ? 0 : -1;
+}
+
+// Full solver on an interleaved ray field ray [Hy][Wx][6] (direction xyz, origin xyz)
+// and confidence [Hy][Wx] (src/ray_pose.cpp:95-252 with its production defaults: 100
+// iterations of 8 samples from the top 30 % by weight, reprojection threshold 0.2,
+// at most 8000 refit points, seed 1234). ext = camera-to-world 3x4, intr 3x3. diag
+// (optional, 26 doubles) = R (9), T (3), focal (2), pp (2), A (9), best inlier count.
+// Returns 0, or -1 on a degenerate field.
+OR_API int or_ray_pose(const float* ray, const float* conf, int Hy, int Wx, int img_h, int img_w, float* ext,
+                       float* intr, double* diag) {
+  const int N = Hy * Wx, n_iter = 100, n_pick = 8, max_refit = 8000;
+  const double thr = 0.2, zthr = 1e-4;
+  const uint32_t seed = 1234;
+  // ray cloud on the identity camera plane (src/ray_pose.cpp:11-59)
+  std::vector<double> src(2 * N), dst(2 * N), w(N), org(3 * N), craw(N);
+  const double dx = 1.0 / Wx, dy = 1.0 / Hy;
+  for (int i = 0; i < Hy; ++i) {
+    const double gy = Hy == 1 ? dy : dy + static_cast<double>(i) * ((2.0 - dy) - dy) / (Hy - 1);
+    for (int j = 0; j < Wx; ++j) {
+      const double gx = Wx == 1 ? dx : dx + static_cast<double>(j) * ((2.0 - dx) - dx) / (Wx - 1);
+      const int n = i * Wx + j;
+      const float* r = ray + static_cast<size_t>(n) * 6;
+      const double dz = r[2];
+      const bool ok = std::fabs(dz) > zthr;
+      src[2 * n] = gx - 1.0;
+      src[2 * n + 1] = gy - 1.0;
+      dst[2 * n] = ok ? r[0] / dz : static_cast<double>(r[0]);
+      dst[2 * n + 1] = ok ? r[1] / dz : static_cast<double>(r[1]);
+      craw[n] = conf[n];
+      w[n] = ok ? craw[n] : 0.0;
+      for (int c = 0; c < 3; ++c) org[3 * n + c] = r[3 + c];
+    }
+  }
+  const int n_cand = std::min(N, std::max(n_pick, static_cast<int>(static_cast<double>(N) * 0.3)));
+  std::vector<int> order(N);
+  for (int n = 0; n < N; ++n) order[n] = n;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return w[a] > w[b]; });
+  // sample draws: one persistent permutation, partially re-shuffled per iteration
+  std::vector<int> draws(static_cast<size_t>(n_iter) * n_pick), perm(n_cand);
+  {
+    std::mt19937 gen(seed);
+    for (int k = 0; k < n_cand; ++k) perm[k] = k;
+    for (int it = 0; it < n_iter; ++it)
+      for (int k = 0; k < n_pick; ++k) {
+        std::uniform_int_distribution<int> pick(k, n_cand - 1);
+        std::swap(perm[k], perm[pick(gen)]);
+        draws[static_cast<size_t>(it) * n_pick + k] = perm[k];
+      }
+  }
+  auto fit = [&](const int* idx, int M, double* H) {
+    std::vector<double> s(2 * M), d(2 * M), ww(M);
+    for (int k = 0; k < M; ++k) {
+      const int n = idx[k];
+      s[2 * k] = src[2 * n];
+      s[2 * k + 1] = src[2 * n + 1];
+      d[2 * k] = dst[2 * n];
+      d[2 * k + 1] = dst[2 * n + 1];
+      ww[k] = w[n];
+    }
+    return rp::homography(s.data(), d.data(), ww.data(), M, H);
+  };
+  std::vector<uint8_t> best(N, 0), cur(N, 0);
+  double best_score = -1.0;
+  std::vector<int> sample(n_pick);
+  for (int it = 0; it < n_iter; ++it) {
+    for (int k = 0; k < n_pick; ++k) sample[k] = order[draws[static_cast<size_t>(it) * n_pick + k]];
+    double H[9];
+    if (!fit(sample.data(), n_pick, H)) continue;
+    double score = 0;
+    for (int n = 0; n < N; ++n) {
+      const double x = src[2 * n], y = src[2 * n + 1];
+      const double pz = H[6] * x + H[7] * y + H[8];
+      const double ex = (H[0] * x + H[1] * y + H[2]) / pz - dst[2 * n];
+      const double ey = (H[3] * x + H[4] * y + H[5]) / pz - dst[2 * n + 1];
+      cur[n] = (ex * ex + ey * ey) < thr * thr;
+      if (cur[n]) score += w[n];
+    }
+    if (score > best_score) {
+      best_score = score;
+      best = cur;
+    }
+  }
+  std::vector<int> inl;
+  for (int n = 0; n < N; ++n)
+    if (best[n]) inl.push_back(n);
+  const int n_best = static_cast<int>(inl.size());
+  std::stable_sort(inl.begin(), inl.end(), [&](int a, int b) { return w[a] > w[b]; });
+  if (static_cast<int>(inl.size()) > max_refit) {
+    const int keep = std::max(static_cast<int>(inl.size() * 0.95), max_refit);
+    inl.resize(keep);
+    std::mt19937 gen(seed ^ 0x9e3779b9u);
+    std::shuffle(inl.begin(), inl.end(), gen);
+    inl.resize(max_refit);
+  }
+  if (inl.size() < 4) return -1;
+  double A[9];
+  if (!fit(inl.data(), static_cast<int>(inl.size()), A)) return -1;
+  if (rp::det3(A) < 0)
+    for (double& a : A) a = -a;
+  double R[9], L[9];
+  rp::ql3(A, R, L);
+  const double l22 = L[8];
+  if (std::fabs(l22) < 1e-12) return -1;
+  for (double& v : L) v /= l22;
+  if (std::fabs(L[0]) < 1e-12 || std::fabs(L[4]) < 1e-12) return -1;
+  double T[3] = {0, 0, 0}, cs = 0;
+  for (int n = 0; n < N; ++n) {
+    for (int c = 0; c < 3; ++c) T[c] += org[3 * n + c] * craw[n];
+    cs += craw[n];
+  }
+  if (std::fabs(cs) < 1e-12) return -1;
+  for (double& t : T) t /= cs;
+  const double focal[2] = {1.0 / L[0], 1.0 / L[4]}, pp[2] = {L[6] + 1.0, L[7] + 1.0};
+  for (int i = 0; i < 3; ++i) {
+    double t = 0;
+    for (int c = 0; c < 3; ++c) {
+      ext[i * 4 + c] = static_cast<float>(R[c * 3 + i]);  // rotation transposed: world from camera
+    }
+    t = -(R[0 * 3 + i] * T[0] + R[1 * 3 + i] * T[1] + R[2 * 3 + i] * T[2]);
+    ext[i * 4 + 3] = static_cast<float>(t);
+  }
+  for (int k = 0; k < 9; ++k) intr[k] = 0.0f;
+  intr[0] = static_cast<float>(focal[0] / 2.0 * img_w);
+  intr[4] = static_cast<float>(focal[1] / 2.0 * img_h);
+  intr[2] = static_cast<float>(pp[0] * img_w * 0.5);
+  intr[5] = static_cast<float>(pp[1] * img_h * 0.5);
+  intr[8] = 1.0f;
+  for (int k = 0; k < 12; ++k)
+    if (!std::isfinite(ext[k])) return -1;
+  for (int k = 0; k < 9; ++k)
+    if (!std::isfinite(intr[k])) return -1;
+  if (diag) {
+    std::copy(R, R + 9, diag);
+    std::copy(T, T + 3, diag + 9);
+    diag[12] = focal[0];
+    diag[13] = focal[1];
+    diag[14] = pp[0];
+    diag[15] = pp[1];
+    std::copy(A, A + 9, diag + 16);
+    diag[25] = n_best;
+  }
+  return 0;
 }

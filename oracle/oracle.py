@@ -26,11 +26,12 @@ REF_SRC_DIR = os.environ.get("DA3_REFERENCE_SRC", "/root/reference/src")
 REF_DIR = os.path.join(HERE, "_ref")
 REF_LIB = os.path.join(REF_DIR, "libda3ref.so")
 # DA3cpplib's own host-only sources on the path, compiled unmodified (never copied).
-REF_SOURCES = ["preprocess.cpp", "uv_posembed.cpp", "nested.cpp"]
+REF_SOURCES = ["preprocess.cpp", "uv_posembed.cpp", "nested.cpp", "ray_pose.cpp", "linalg.cpp"]
 
 
 def build_ref(force: bool = False):
-    """Compile the reference's preprocess.cpp, uv_posembed.cpp and nested.cpp with ref_wrap.cpp into
+    """Compile the reference's preprocess.cpp, uv_posembed.cpp, nested.cpp, ray_pose.cpp and
+    linalg.cpp with ref_wrap.cpp into
     oracle/_ref/libda3ref.so. Returns the library path, or None when the reference
     checkout is absent (the prebuilt library, if shipped, is still used)."""
     srcs = [os.path.join(REF_SRC_DIR, f) for f in REF_SOURCES]
@@ -68,6 +69,11 @@ def ref_lib():
                                      ctypes.c_void_p, ctypes.c_int64]
         R.ref_resize.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 5 + [ctypes.c_void_p]
         R.ref_uv_pos_embed.argtypes = [ctypes.c_int] * 3 + [ctypes.c_float, ctypes.c_void_p]
+        R.ref_ray_pose.argtypes = [ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 4 + [ctypes.c_void_p] * 3
+        R.ref_qr.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+        R.ref_ql3.argtypes = [ctypes.c_void_p] * 3
+        R.ref_smallest_eigvec.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        R.ref_homography.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_void_p]
         R.ref_nested_align.restype = ctypes.c_float
         R.ref_nested_align.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
         _ref = R
@@ -128,6 +134,11 @@ def lib():
         L.or_infer_chw.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.or_nested_align.restype = ctypes.c_float
         L.or_nested_align.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
+        L.or_ray_pose.argtypes = [ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 4 + [ctypes.c_void_p] * 3
+        L.or_qr.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+        L.or_ql3.argtypes = [ctypes.c_void_p] * 3
+        L.or_smallest_eigvec.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        L.or_homography.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_void_p]
         L.or_get.restype = ctypes.c_int64
         L.or_get.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.POINTER(ctypes.c_float))]
         L.or_dims.argtypes = [ctypes.c_void_p] + [ctypes.POINTER(ctypes.c_int)] * 6
@@ -423,3 +434,62 @@ def nested_align(any_depth, any_conf, any_ext, any_intr, metric_depth, sky, impl
         fn = lib().or_nested_align
     scale = fn(*[x.ctypes.data for x in a], n, out.ctypes.data, ext.ctypes.data)
     return out, ext, float(scale)
+
+
+def _impl(impl, name):
+    if impl == "ref":
+        R = ref_lib()
+        if R is None:
+            raise RuntimeError("oracle/_ref is not built")
+        return getattr(R, "ref_" + name)
+    return getattr(lib(), "or_" + name)
+
+
+def ray_pose(ray, conf, img_h, img_w, impl="oracle"):
+    """Ray->pose solver (src/ray_pose.cpp:95-252, production defaults) on an interleaved
+    ray field [Hy][Wx][6] and confidence [Hy][Wx]. Returns (ext [3][4] camera-to-world,
+    intr [3][3], diag dict) or None when the solver reports a degenerate field."""
+    ray = np.ascontiguousarray(ray, dtype=np.float32)
+    conf = np.ascontiguousarray(conf, dtype=np.float32)
+    Hy, Wx = conf.shape
+    ext = np.zeros(12, np.float32)
+    intr = np.zeros(9, np.float32)
+    diag = np.zeros(26, np.float64)
+    rc = _impl(impl, "ray_pose")(ray.ctypes.data, conf.ctypes.data, Hy, Wx, img_h, img_w, ext.ctypes.data,
+                                 intr.ctypes.data, diag.ctypes.data)
+    if rc != 0:
+        return None
+    d = {"R": diag[:9].reshape(3, 3), "T": diag[9:12], "focal": diag[12:14], "pp": diag[14:16],
+         "A": diag[16:25].reshape(3, 3), "n_inlier_best": int(diag[25])}
+    return ext.reshape(3, 4), intr.reshape(3, 3), d
+
+
+def qr(a, impl="oracle"):
+    a = np.ascontiguousarray(a, dtype=np.float64)
+    n = a.shape[0]
+    q = np.zeros((n, n)); r = np.zeros((n, n))
+    _impl(impl, "qr")(a.ctypes.data, n, q.ctypes.data, r.ctypes.data)
+    return q, r
+
+
+def ql3(a, impl="oracle"):
+    a = np.ascontiguousarray(a, dtype=np.float64)
+    q = np.zeros((3, 3)); l = np.zeros((3, 3))
+    _impl(impl, "ql3")(a.ctypes.data, q.ctypes.data, l.ctypes.data)
+    return q, l
+
+
+def smallest_eigvec(m, impl="oracle"):
+    m = np.ascontiguousarray(m, dtype=np.float64)
+    v = np.zeros(m.shape[0])
+    _impl(impl, "smallest_eigvec")(m.ctypes.data, m.shape[0], v.ctypes.data)
+    return v
+
+
+def homography(src, dst, w, impl="oracle"):
+    src = np.ascontiguousarray(src, dtype=np.float64)
+    dst = np.ascontiguousarray(dst, dtype=np.float64)
+    w = np.ascontiguousarray(w, dtype=np.float64)
+    H = np.zeros(9)
+    rc = _impl(impl, "homography")(src.ctypes.data, dst.ctypes.data, w.ctypes.data, w.size, H.ctypes.data)
+    return H.reshape(3, 3) if rc == 0 else None

@@ -2,8 +2,9 @@
 // checkout into oracle/_ref/ — test infrastructure only, never part of libda3b.
 //
 // Only src/preprocess.cpp (the real/legacy preprocess and the uint8 cubic/area
-// resizers), src/uv_posembed.cpp and src/nested.cpp (the nested metric alignment) are
-// compiled: they need nothing from ggml beyond
+// resizers), src/uv_posembed.cpp, src/nested.cpp (the nested metric alignment) and
+// src/ray_pose.cpp + src/linalg.cpp (the ray->pose solver) are compiled: they need
+// nothing from ggml beyond
 // the opaque type names that model_loader.hpp mentions (oracle/ref_shim/). Everything
 // else on the depth path goes through ggml graphs, whose source is absent from the
 // reference checkout, so it cannot be built here.
@@ -11,7 +12,9 @@
 #include <cstring>
 #include <vector>
 
+#include "linalg.hpp"
 #include "nested.hpp"
+#include "ray_pose.hpp"
 #include "preprocess.hpp"
 #include "uv_posembed.hpp"
 
@@ -98,4 +101,33 @@ REF_API float ref_nested_align(const float* any_depth, const float* any_conf, co
   std::memcpy(out_depth, r.depth.data(), N * sizeof(float));
   for (int k = 0; k < 12; ++k) out_ext[k] = r.extrinsics[k];
   return r.scale_factor;
+}
+
+// da::solve_ray_pose with its production defaults (no fed indices), as
+// Engine::depth_pose_rays_native calls it. diag as in the oracle's or_ray_pose.
+REF_API int ref_ray_pose(const float* ray, const float* conf, int Hy, int Wx, int img_h, int img_w, float* ext,
+                         float* intr, double* diag) {
+  da::RayPoseParams p;
+  da::RayPoseOut o;
+  if (!da::solve_ray_pose(ray, conf, Hy, Wx, img_h, img_w, nullptr, nullptr, nullptr, 0, p, o)) return -1;
+  std::memcpy(ext, o.extrinsics.data(), 12 * sizeof(float));
+  std::memcpy(intr, o.intrinsics.data(), 9 * sizeof(float));
+  if (diag) {
+    std::memcpy(diag, o.R, 9 * sizeof(double));
+    std::memcpy(diag + 9, o.T, 3 * sizeof(double));
+    diag[12] = o.focal[0];
+    diag[13] = o.focal[1];
+    diag[14] = o.pp[0];
+    diag[15] = o.pp[1];
+    std::memcpy(diag + 16, o.A, 9 * sizeof(double));
+    diag[25] = o.n_inlier_best;
+  }
+  return 0;
+}
+
+REF_API void ref_qr(const double* a, int n, double* q, double* r) { da::linalg::householder_qr(a, n, q, r); }
+REF_API void ref_ql3(const double* a, double* q, double* l) { da::linalg::ql_decomposition(a, q, l); }
+REF_API void ref_smallest_eigvec(const double* m, int n, double* v) { da::linalg::smallest_eigvec(m, n, v); }
+REF_API int ref_homography(const double* src, const double* dst, const double* w, int M, double* H) {
+  return da::linalg::homography_weighted(src, dst, w, M, H) ? 0 : -1;
 }

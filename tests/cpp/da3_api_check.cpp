@@ -10,7 +10,10 @@
 //    must be bit-identical to step 2;
 // 4. the reference's refusals: infer_preprocessed on a DA2 checkpoint, infer() on an
 //    image whose data size does not match, both return false with an empty Result;
-// 5. (with the optional models) DA3 mono: kind, depth + sky and no confidence, refusal of
+// 5. InferOptions::ray_pose with with_pose: the ray->pose solver's camera-to-world pose
+//    equals da3b_ray_pose on the ray field da3b_infer_device writes for the same image;
+//    ray_pose without with_pose, with legacy_resize, or on DA2 is refused;
+// 6. (with the optional models) DA3 mono: kind, depth + sky and no confidence, refusal of
 //    with_pose and infer_preprocessed; nested: load_nested_model with the DA3 model as the
 //    anyview branch, kind / camera pose / metric flags, depth + pose without confidence or
 //    sky, and the infer_preprocessed refusal (src/api.cpp:95-161, :184).
@@ -22,7 +25,9 @@
 #include <random>
 #include <vector>
 
+#include "da3b.h"
 #include "da3cpp/da3.h"
+#include "da3cpp/da3_c.h"
 
 #define CHECK(c)                                         \
   do {                                                   \
@@ -81,6 +86,43 @@ int main(int argc, char** argv) {
   bad.data.pop_back();
   CHECK(!da3::infer(*model, bad, c));
   CHECK(c.depth.empty());
+
+  {
+    da3::InferOptions rp;
+    rp.with_pose = true;
+    rp.ray_pose = true;
+    da3::Result rr;
+    CHECK(da3::infer(*model, img, rr, rp));
+    CHECK(rr.has_pose && rr.depth.size() == a.depth.size());
+    CHECK(std::memcmp(rr.depth.data(), a.depth.data(), a.depth.size() * 4) == 0);
+    da_ctx* ctx = da3b_load(argv[1], 0);
+    CHECK(ctx);
+    const int g = 8 * (n / 14);
+    void *d_img = nullptr, *d_depth = nullptr, *d_conf = nullptr, *d_rays = nullptr;
+    CHECK(cudaMalloc(&d_img, img.data.size()) == cudaSuccess);
+    CHECK(cudaMalloc(&d_depth, static_cast<size_t>(n) * n * 4) == cudaSuccess);
+    CHECK(cudaMalloc(&d_conf, static_cast<size_t>(n) * n * 4) == cudaSuccess);
+    CHECK(cudaMalloc(&d_rays, static_cast<size_t>(7) * g * g * 4) == cudaSuccess);
+    CHECK(cudaMemcpy(d_img, img.data.data(), img.data.size(), cudaMemcpyHostToDevice) == cudaSuccess);
+    CHECK(da3b_infer_device(ctx, d_img, 1, 1, n, n, d_depth, d_conf, d_rays, nullptr) == 0);
+    CHECK(cudaDeviceSynchronize() == cudaSuccess);
+    float ext[12], intr[9];
+    CHECK(da3b_ray_pose(ctx, static_cast<const float*>(d_rays), 1, 0, g, g, n, n, ext, intr, nullptr, nullptr) == 0);
+    CHECK(std::memcmp(ext, rr.extrinsics.data(), sizeof(ext)) == 0);
+    CHECK(std::memcmp(intr, rr.intrinsics.data(), sizeof(intr)) == 0);
+    cudaFree(d_img);
+    cudaFree(d_depth);
+    cudaFree(d_conf);
+    cudaFree(d_rays);
+    da_capi_free(ctx);
+    da3::InferOptions only_rays;
+    only_rays.ray_pose = true;
+    CHECK(!da3::infer(*model, img, rr, only_rays) && rr.depth.empty());
+    rp.legacy_resize = true;
+    CHECK(!da3::infer(*model, img, rr, rp) && rr.depth.empty());
+    rp.legacy_resize = false;
+    CHECK(!da3::infer(*da2, img, rr, rp) && rr.depth.empty());
+  }
 
   if (argc >= 6) {
     da3::Params pm;

@@ -23,6 +23,16 @@ Fixtures (all small):
                        published offset rule (bicubic, scale (g + 0.1) / grid, applied
                        at every grid), which is the rule src/dino_backbone.cpp:18-56
                        follows.
+  linalg_ref.json      The known answers of DA3cpplib's own tests/test_linalg.cpp (its
+                       fixed 3x3 matrix with torch.linalg.qr and the torch-derived QL
+                       factors, the 4x4 symmetric eigen case, the 12-point homography
+                       recovery), parsed from that file.
+  raypose_ref.npz      DA3cpplib's own src/ray_pose.cpp + src/linalg.cpp, compiled
+                       unmodified into oracle/_ref, on the seeded synthetic ray fields
+                       of tests/rayfield.py: extrinsics, intrinsics and the solver's
+                       double diagnostics.
+  nested_ref.npz       DA3cpplib's own src/nested.cpp (oracle/_ref) on seeded inputs:
+                       aligned depth, extrinsics and scale.
 """
 from __future__ import annotations
 
@@ -303,9 +313,81 @@ def make_hf():
     np.savez_compressed(os.path.join(HERE, "da2_hf_tiny.npz"), **out)
 
 
+REF_TESTS = os.path.join(os.path.dirname(orc.REF_SRC_DIR), "tests")
+RAY_CASES = [(1, 48, 64, 0.2), (2, 64, 64, 0.5), (3, 40, 56, 0.0), (4, 96, 72, 0.3)]
+
+
+def make_linalg():
+    import json
+    import re
+
+    src = open(os.path.join(REF_TESTS, "test_linalg.cpp")).read()
+
+    def arr(name):
+        m = re.search(r"\b" + name + r"\s*\[[^\]]*\](?:\[[^\]]*\])?\s*=\s*\{(.*?)\};", src, re.S)
+        return [float(v) for v in re.findall(r"-?\d+\.?\d*(?:e-?\d+)?", m.group(1))]
+
+    det = re.search(r"close\(det3\(A\),\s*([-\d.]+)", src).group(1)
+    out = {"source": "DA3cpplib tests/test_linalg.cpp", "A": arr("A"), "det": float(det), "QR_Q": arr("QR_Q"),
+           "QR_R": arr("QR_R"), "QL_Q": arr("QL_Q"), "QL_L": arr("QL_L"), "M4": arr("M"), "Htrue": arr("Htrue"),
+           "pts": arr("pts")}
+    assert len(out["A"]) == 9 and len(out["QL_L"]) == 9 and len(out["M4"]) == 16 and len(out["pts"]) == 24
+    with open(os.path.join(HERE, "linalg_ref.json"), "w") as f:
+        json.dump(out, f, indent=1)
+
+
+def make_raypose():
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import rayfield
+
+    out = {}
+    for seed, hy, wx, outl in RAY_CASES:
+        ray, conf, _ = rayfield.field(seed, hy, wx, outliers=outl)
+        ext, intr, d = orc.ray_pose(ray, conf, hy * 14 // 8, wx * 14 // 8, impl="ref")
+        out[f"s{seed}_ext"] = ext
+        out[f"s{seed}_intr"] = intr
+        out[f"s{seed}_diag"] = np.concatenate([d["R"].ravel(), d["T"], d["focal"], d["pp"], d["A"].ravel(),
+                                               [d["n_inlier_best"]]])
+    np.savez_compressed(os.path.join(HERE, "raypose_ref.npz"), **out)
+
+
+NESTED_CASES = [(21, 4096, 0.3), (22, 3000, 0.004), (23, 2500, 0.6)]
+
+
+def nested_inputs(seed, n, sky_frac):
+    rng = np.random.default_rng(seed)
+    ad = rng.uniform(0.0, 5.0, n).astype(np.float32)
+    ac = rng.uniform(1.0, 3.0, n).astype(np.float32)
+    ext = rng.standard_normal(12).astype(np.float32)
+    intr = np.array([rng.uniform(100, 400), 0, 56, 0, rng.uniform(100, 400), 56, 0, 0, 1], np.float32)
+    md = rng.uniform(0.0, 10.0, n).astype(np.float32)
+    sky = np.where(rng.random(n) < sky_frac, rng.uniform(0.3, 1.0, n), rng.uniform(0.0, 0.3, n)).astype(np.float32)
+    return ad, ac, ext, intr, md, sky
+
+
+def make_nested():
+    out = {}
+    for seed, n, frac in NESTED_CASES:
+        d, e, s = orc.nested_align(*nested_inputs(seed, n, frac), impl="ref")
+        out[f"s{seed}_depth"] = d
+        out[f"s{seed}_ext"] = e
+        out[f"s{seed}_scale"] = np.float32(s)
+    np.savez_compressed(os.path.join(HERE, "nested_ref.npz"), **out)
+
+
 if __name__ == "__main__":
-    make_preprocess()
-    make_q8()
-    make_hf()
+    which = sys.argv[1:] or ["preprocess", "q8", "hf", "linalg", "raypose", "nested"]
+    if "preprocess" in which:
+        make_preprocess()
+    if "q8" in which:
+        make_q8()
+    if "hf" in which:
+        make_hf()
+    if "linalg" in which:
+        make_linalg()
+    if "raypose" in which:
+        make_raypose()
+    if "nested" in which:
+        make_nested()
     for f in sorted(os.listdir(HERE)):
         print(f, os.path.getsize(os.path.join(HERE, f)))

@@ -82,3 +82,19 @@ def test_nested_align_empty_mask():
     if O.ref_lib() is not None:
         ref = O.nested_align(*args, impl="ref")
         assert ref[2] == ours[2] and np.array_equal(ref[0], ours[0])
+
+
+def test_nested_align_committed_outputs():
+    """The reference's outputs committed in tests/golden/nested_ref.npz (made from
+    oracle/_ref by tests/golden/make_golden.py) hold without the reference checkout."""
+    import os
+
+    from golden.make_golden import NESTED_CASES, nested_inputs
+
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "nested_ref.npz"))
+    for seed, n, frac in NESTED_CASES:
+        args = nested_inputs(seed, n, frac)
+        for got in (O.nested_align(*args, impl="oracle"), _ours(*args)):
+            assert np.array_equal(got[0], z[f"s{seed}_depth"])
+            assert np.array_equal(got[1], z[f"s{seed}_ext"])
+            assert np.float32(got[2]) == z[f"s{seed}_scale"]
