@@ -9,6 +9,8 @@ Part B: DPT-head 3x3 stride-1 pad-1 convs, NHWC f16, C_in = C_out in {64, 128, 2
 spatial 37..296, batch 8 (da3b_conv_nhwc).
 attn: da3b_attention at the C3 shape (64 x 1370 tokens, 16 heads) and the DA3
 multi-view global layer (8 views x 1297 tokens per scene).
+ray: da3b_ray_pose (the ray->pose solver, both host round trips included; wall time)
+on a synthetic 288 x 288 ray field, the aux resolution of a 504 x 504 image.
 
 Each line: {"part", "case", "ms", "tflops", "frac", "peak"}; frac is against the
 measured dense bf16 burst peak of this GPU pool (MEASURED_PEAKS.json, else the pool's
@@ -66,7 +68,7 @@ def main(argv=None):
     from . import _lib
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("--part", default="all", choices=["A", "B", "attn", "up", "pre", "all"])
+    ap.add_argument("--part", default="all", choices=["A", "B", "attn", "up", "pre", "ray", "all"])
     ap.add_argument("--m", type=int, default=0, help="Part A: only this M")
     ap.add_argument("--kn", default="", help="Part A: only this K,N (e.g. 1024,4096)")
     ap.add_argument("--act", type=int, default=0, help="Part A activation: 0 none, 2 erf-GELU")
@@ -205,6 +207,40 @@ def main(argv=None):
             ms = timeit(run)
             emit("attn", f"{tag}: nseq={nseq} seqlen={seqlen} heads={heads}", ms, 4.0 * nseq * seqlen * seqlen * D)
             del qkv, out
+
+    if args.part in ("ray", "all"):
+        import time
+
+        from . import synth
+
+        ctx = L.da3b_load(synth.ensure_gguf("da3-t").encode(), 0)
+        g = 288
+        rng = np.random.default_rng(7)
+        t = (np.arange(g) + 0.5) / g * 2 - 1
+        X, Y = np.meshgrid(t, t)
+        dirs = np.stack([X / 0.9, Y / 1.1, np.ones_like(X)], 0) + rng.standard_normal((3, g, g)) * 1e-3
+        bad = rng.random((g, g)) < 0.2
+        dirs[:, bad] = rng.standard_normal((3, int(bad.sum())))
+        planes = np.concatenate([dirs, np.ones((3, g, g)) * 0.5, rng.uniform(1, 3, (1, g, g))], 0).astype(np.float32)
+        d = torch.from_numpy(planes).cuda()
+        ext = np.zeros(12, np.float32)
+        intr = np.zeros(9, np.float32)
+        torch.cuda.synchronize()
+
+        def solve():
+            rc = L.da3b_ray_pose(ctx, P(d), 1, 0, g, g, 504, 504, ext.ctypes.data, intr.ctypes.data, None, S)
+            if rc:
+                raise RuntimeError(f"da3b_ray_pose rc={rc}")
+
+        for _ in range(3):
+            solve()
+        t0 = time.perf_counter()
+        for _ in range(args.reps):
+            solve()
+        ms = (time.perf_counter() - t0) * 1e3 / args.reps
+        print(json.dumps({"part": "ray", "case": f"ray->pose {g}x{g} points (504x504 image)", "ms": round(ms, 3),
+                          "timing": "wall clock per call, host round trips included"}), flush=True)
+        L.da_capi_free(ctx)
 
 
 if __name__ == "__main__":
