@@ -50,6 +50,9 @@ struct Level {
 struct Plan {
   int V = 0, S = 0, scenes = 0, H = 0, W = 0, gh = 0, gw = 0, Np = 0, Ntok = 0, M = 0;
   bool rays = false;
+  // true: upsample + output_conv2 run fused (up_out2, no full-resolution feature map);
+  // false ($DA3B_UNFUSED_UP=1 at plan creation): upsample_ac into O1u, then conv_nhwc
+  bool fused_up = true;
   int ho3 = 0, wo3 = 0;  // stride-2 stage grid
   int Cf = 0;            // feature channels (D or 2D)
   Arena arena;
@@ -276,6 +279,11 @@ Plan* Engine::plan_for(int V, int S, int H, int W, bool rays) {
   p->Ntok = 1 + p->Np;
   p->M = V * p->Ntok;
   p->rays = rays && hd.aux;
+  {
+    const char* u = getenv("DA3B_UNFUSED_UP");
+    const int Fh = (c.head_features > 0 ? c.head_features : hd.rn[0].OC) / 2;
+    p->fused_up = !(u && u[0] == '1') && Fh % 16 == 0 && Fh <= 128;
+  }
   p->ho3 = (p->gh + 2 - 3) / 2 + 1;
   p->wo3 = (p->gw + 2 - 3) / 2 + 1;
   p->Cf = (c.cat_token ? 2 : 1) * D;
@@ -350,7 +358,7 @@ Plan* Engine::plan_for(int V, int S, int H, int W, bool rays) {
     T(p->U[2], V_ * (4 * gh) * (4 * gw) * F);      // refinenet2 -> lv0
     T(p->U[3], V_ * (8 * gh) * (8 * gw) * F);      // refinenet1 -> 8gh
     T(p->O1, V_ * (8 * gh) * (8 * gw) * (F / 2));
-    T(p->O1u, V_ * H * W * (F / 2));
+    if (!p->fused_up) T(p->O1u, V_ * H * W * (F / 2));
     if (p->rays) {
       T(p->auxA, V_ * (8 * gh) * (8 * gw) * F);
       T(p->auxB, V_ * (8 * gh) * (8 * gw) * F);
@@ -668,7 +676,13 @@ int Engine::head(Plan& p, cudaStream_t s) {
   const int h8 = 8 * gh, w8 = 8 * gw;
   CK(conv_nhwc(p.U[3], V, h8, w8, F, h.out1.w, h.out1.OC, 3, 0, epi_f16(p.O1, h.out1.OC, h.out1.b, kActNone), status_,
                s));
-  CK(upsample_ac(p.O1, V, h8, w8, h.out1.OC, p.O1u, p.H, p.W, c.head_pos_embed ? p.pe_full : nullptr, s));
+  const __half* pe_full = c.head_pos_embed ? p.pe_full : nullptr;
+  if (!p.fused_up) CK(upsample_ac(p.O1, V, h8, w8, h.out1.OC, p.O1u, p.H, p.W, pe_full, s));
+  // output_conv2: 3x3 -> 32, relu, 1x1 -> output_dim, activation, on the upsampled map
+  auto out2 = [&](const Conv& cv, const EpiArgs& e) -> int {
+    if (p.fused_up) return up_out2(p.O1, V, h8, w8, h.out1.OC, pe_full, p.H, p.W, cv.w, conv_icp(cv.IC), e, status_, s);
+    return conv_nhwc(p.O1u, V, p.H, p.W, cv.IC, cv.w, 32, 3, 32, e, status_, s);
+  };
   {
     EpiArgs e = epi_default();
     e.kind = kEpiOut2;
@@ -689,7 +703,7 @@ int Engine::head(Plan& p, cudaStream_t s) {
       return -50;
     }
     e.o2_scale = c.head_max_depth;
-    CK(conv_nhwc(p.O1u, V, p.H, p.W, h.out2a.IC, h.out2a.w, 32, 3, 32, e, status_, s));
+    CK(out2(h.out2a, e));
   }
   // ---- sky head (metric / mono DPT, src/dpt_head.cpp:205-222 and the relu at
   // src/dpt_head.cpp:334-338) on the same upsampled feature map
@@ -702,7 +716,7 @@ int Engine::head(Plan& p, cudaStream_t s) {
     e.o2_dim = 1;
     e.o2_act[0] = raw_logits_ ? kOutIdentity : kOutRelu;
     e.o2_out[0] = p.sky;
-    CK(conv_nhwc(p.O1u, V, p.H, p.W, h.sky_out2a.IC, h.sky_out2a.w, 32, 3, 32, e, status_, s));
+    CK(out2(h.sky_out2a, e));
   }
   // ---- aux ray head (DualDPT, src/dpt_head.cpp:225-272)
   if (p.rays) {

@@ -87,16 +87,6 @@ __device__ __forceinline__ float apply_act(float v, int act) {
   return v;
 }
 
-__device__ __forceinline__ float out_act(float l, int a, float scale) {
-  switch (a) {
-    case kOutRelu: return fmaxf(l, 0.0f);
-    case kOutSigmoidScale: return scale / (1.0f + expf(-l));
-    case kOutExp: return expf(l);
-    case kOutExpP1: return expf(l) + 1.0f;
-    default: return l;
-  }
-}
-
 __device__ __forceinline__ void load_h8(const __half* p, float* v) {
   const uint4 u = *reinterpret_cast<const uint4*>(p);
   const __half2* h = reinterpret_cast<const __half2*>(&u);

@@ -89,4 +89,17 @@ struct EpiArgs {
   int vt_seqlen, vt_ld, vt_d;  // tokens per attention sequence, row pitch (>= seqlen, %8), model dim D
 };
 
+#ifdef __CUDACC__
+// Output activation of the fused out2b epilogue (src/dpt_head.cpp:327-338, :402-439).
+__device__ __forceinline__ float out_act(float l, int a, float scale) {
+  switch (a) {
+    case kOutRelu: return fmaxf(l, 0.0f);
+    case kOutSigmoidScale: return scale / (1.0f + expf(-l));
+    case kOutExp: return expf(l);
+    case kOutExpP1: return expf(l) + 1.0f;
+    default: return l;
+  }
+}
+#endif
+
 }  // namespace da3b

@@ -1,0 +1,336 @@
+// Fused DPT output stage: align-corners upsample of out1 to the image size (+ the
+// 0.1 UV pos-embed), output_conv2's 3x3 conv to 32 channels, relu, the 1x1 conv to
+// output_dim and the output activation (src/dpt_head.cpp:199-222 and :327-338; the
+// feature map `feat_map` of the reference is never written to memory).
+//
+// One CTA = a 128-pixel strip of up to kRows consecutive output rows of one image.
+// The upsampled rows the 3x3 taps need (128 + 2 halo pixels, all channels) are built
+// in shared memory in a ring of four row slots, laid out K-major without swizzle:
+// [16-byte channel chunk][pixel][8 halves]. In that layout an operand view shifted by
+// one pixel is a 16-byte move of the start address (8-row groups 128 B apart, channel
+// chunks one row-slot-plane apart), so the three horizontal taps read the same row
+// slot and each upsampled value is built once per strip instead of nine times.
+//   warps 0-7  build row j+2 while the tensor core works on row j (bilinear from the
+//              NHWC out1 map through L2, f32 weights as k_upsample_ac, PE added, f16);
+//              warps 0-3 also run the epilogue: TMEM -> bias, relu, 1x1 conv, activation;
+//   warp 8     one thread issues the 9 taps x C/16 tcgen05.mma (M=128, N=32, K=16)
+//              of a row into one of two TMEM accumulators.
+// The MMA order (tap-major, channels ascending) and every f32 expression equal the
+// unfused upsample + conv_nhwc path, so the outputs are bit-identical to it.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "gemm.h"
+#include "ops.h"
+#include "ptx.cuh"
+
+namespace da3b {
+namespace {
+
+constexpr int kTile = 128;             // output pixels per strip (MMA M)
+constexpr int kPx = kTile + 2;         // strip pixels with the 3x3 halo
+constexpr int kSlots = 4;              // upsampled-row ring
+constexpr int kRows = 74;              // output rows per CTA
+constexpr int kBuildWarps = 8;
+constexpr int kThreads = (kBuildWarps + 1) * 32;
+constexpr int kOC = 32;                // output_conv2 hidden channels
+constexpr int kConsts = 360;           // bias 32 | LN gamma 32 | LN beta 32 | out2b 8x32 | out2b bias 8
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// K-major operand without swizzle: 8-row core matrices of 16-byte rows, 8-row groups
+// `sbo` apart, 16-byte channel chunks `lbo` apart.
+__device__ __forceinline__ uint64_t desc_noswz(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100; swizzle field 0 = none
+  return d;
+}
+
+struct Layout {
+  uint32_t slot_bytes, w_bytes, total;
+};
+
+__host__ __device__ inline Layout layout_for(int C) {
+  Layout l;
+  l.slot_bytes = static_cast<uint32_t>(C / 8) * kPx * 16;
+  l.w_bytes = 9u * static_cast<uint32_t>(C / 8) * kOC * 16;
+  l.total = 1024 + kSlots * l.slot_bytes + l.w_bytes + kConsts * 4 + kPx * 12 + 16 * 8 + 16;
+  return l;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_up_out2(const __half* __restrict__ src, int hs, int ws, int C, const __half* __restrict__ pe, int H, int W,
+              const __half* __restrict__ wp, int icp, const EpiArgs e, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const Layout L = layout_for(C);
+  const int nkc = C >> 3;
+  uint8_t* sRows = smem;
+  uint8_t* sW = sRows + kSlots * L.slot_bytes;
+  float* sC = reinterpret_cast<float*>(sW + L.w_bytes);
+  int* sX0 = reinterpret_cast<int*>(sC + kConsts);
+  int* sX1 = sX0 + kPx;
+  float* sDX = reinterpret_cast<float*>(sX1 + kPx);
+  uint64_t* bars = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(sDX + kPx) + 7) & ~uintptr_t(7));
+  uint64_t* row_full = bars;       // [4] a row slot built (8 builder warps)
+  uint64_t* slot_free = bars + 4;  // [4] the last MMA reading a row slot completed
+  uint64_t* acc_full = bars + 8;   // [2] a row's accumulator complete
+  uint64_t* acc_empty = bars + 10; // [2] its epilogue drained it (4 warps)
+  uint64_t* drain = bars + 12;     // every issued MMA completed (teardown)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, xs0 = blockIdx.x * kTile, ya = blockIdx.y * kRows;
+  const int R = min(kRows, H - ya);
+  // align-corners source scale, as k_upsample_ac
+  const float sf0 = (W > 1 && ws > 1) ? static_cast<float>(W - 1) / (ws - 1) : static_cast<float>(W) / ws;
+  const float sf1 = (H > 1 && hs > 1) ? static_cast<float>(H - 1) / (hs - 1) : static_cast<float>(H) / hs;
+
+  // per-CTA tables: source columns of the strip pixels, epilogue constants, weights
+  for (int p = threadIdx.x; p < kPx; p += blockDim.x) {
+    const int xo = xs0 - 1 + p;
+    if (xo < 0 || xo >= W) {
+      sX0[p] = -1;
+      sX1[p] = -1;
+      sDX[p] = 0.f;
+    } else {
+      const float fx = static_cast<float>(xo) / sf0;
+      int x0 = static_cast<int>(floorf(fx));
+      int x1 = x0 + 1;
+      sDX[p] = fminf(fmaxf(fx - floorf(fx), 0.f), 1.f);
+      sX0[p] = max(0, min(x0, ws - 1));
+      sX1[p] = max(0, min(x1, ws - 1));
+    }
+  }
+  for (int i = threadIdx.x; i < kConsts; i += blockDim.x) {
+    float v = 0.f;
+    if (i < 32) v = e.bias ? e.bias[i] : 0.f;
+    else if (i < 64) v = e.o2_ln_g ? e.o2_ln_g[i - 32] : 1.f;
+    else if (i < 96) v = e.o2_ln_b ? e.o2_ln_b[i - 64] : 0.f;
+    else if (i < 352) v = (i - 96) < e.o2_dim * 32 ? e.o2_w[i - 96] : 0.f;
+    else v = (i - 352) < e.o2_dim ? e.o2_b[i - 352] : 0.f;
+    sC[i] = v;
+  }
+  // packed weights [32][9][icp] -> [tap * nkc + chunk][oc][8 halves]
+  for (int i = threadIdx.x; i < kOC * 9 * nkc; i += blockDim.x) {
+    const int c8 = i % nkc, t = (i / nkc) % 9, oc = i / (nkc * 9);
+    *reinterpret_cast<uint4*>(sW + ((t * nkc + c8) * kOC + oc) * 16) =
+        *reinterpret_cast<const uint4*>(wp + (static_cast<size_t>(oc) * 9 + t) * icp + c8 * 8);
+  }
+  fence_async_smem();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&row_full[s], kBuildWarps);
+      mbar_init(&slot_free[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == kBuildWarps) tmem_alloc(tmem_slot, 64);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kBuildWarps) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ MMA
+      // output row i reads row slots (i, i+1, i+2) & 3 = upsampled rows y-1, y, y+1
+      constexpr uint32_t idesc = umma_idesc_f16(128, kOC);
+      const uint32_t lbo_a = kPx * 16, lbo_b = kOC * 16;
+      const uint32_t rows0 = smem_u32(sRows), w0 = smem_u32(sW);
+      bool ok = true;
+      int issued = 0;
+      for (int i = 0; i < R && ok; ++i) {
+        for (int j = (i == 0 ? 0 : i + 2); j <= i + 2 && ok; ++j)
+          ok = mbar_wait(&row_full[j & 3], (j >> 2) & 1, status, kStatusTimeoutFull);
+        if (ok && i >= 2) ok = mbar_wait(&acc_empty[i & 1], ((i >> 1) - 1) & 1, status, kStatusTimeoutAccumFree);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t tAcc = tmem + (i & 1) * kOC;
+        uint32_t acc = 0;
+#pragma unroll 1
+        for (int dy = 0; dy < 3; ++dy) {
+          const uint32_t rb = rows0 + ((i + dy) & 3) * L.slot_bytes;
+#pragma unroll 1
+          for (int dx = 0; dx < 3; ++dx) {
+            const int t = dy * 3 + dx;
+            for (int k = 0; k < nkc / 2; ++k) {
+              const uint64_t a = desc_noswz(rb + (2 * k * kPx + dx) * 16, lbo_a, 128);
+              const uint64_t bw = desc_noswz(w0 + ((t * nkc + 2 * k) * kOC) * 16, lbo_b, 128);
+              umma_f16(tAcc, a, bw, idesc, acc);
+              acc = 1;
+            }
+          }
+        }
+        umma_commit(&acc_full[i & 1]);
+        umma_commit(&slot_free[i & 3]);
+        ++issued;
+      }
+      // every issued MMA has landed before the accumulator is freed (also on a timeout)
+      if (issued > 0) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, status, kStatusTimeoutAccum);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ builders
+    const int tb = threadIdx.x;  // 0 .. 255
+    const size_t img = static_cast<size_t>(b) * hs;
+    auto build = [&](int j) {
+      const int u = ya - 1 + j;  // upsampled row
+      uint8_t* dst = sRows + (j & 3) * L.slot_bytes;
+      const bool row_ok = u >= 0 && u < H;
+      float dy = 0.f;
+      const __half* s0 = src;
+      const __half* s1 = src;
+      const __half* prow = nullptr;
+      if (row_ok) {
+        const float fy = static_cast<float>(u) / sf1;
+        int y0 = static_cast<int>(floorf(fy));
+        int y1 = y0 + 1;
+        dy = fminf(fmaxf(fy - floorf(fy), 0.f), 1.f);
+        y0 = max(0, min(y0, hs - 1));
+        y1 = max(0, min(y1, hs - 1));
+        s0 = src + (img + y0) * ws * C;
+        s1 = src + (img + y1) * ws * C;
+        if (pe) prow = pe + static_cast<size_t>(u) * W * C;
+      }
+      for (int it = tb; it < kPx * nkc; it += kBuildWarps * 32) {
+        const int p = it / nkc, kc = it - p * nkc;
+        uint4 uo = make_uint4(0, 0, 0, 0);
+        const int x0 = sX0[p];
+        if (row_ok && x0 >= 0) {
+          const int x1 = sX1[p], c = kc * 8;
+          const float dx = sDX[p];
+          const float wa = (1 - dx) * (1 - dy), wb = dx * (1 - dy), wc = (1 - dx) * dy, wd = dx * dy;
+          const float2 wa2 = make_float2(wa, wa), wb2 = make_float2(wb, wb), wc2 = make_float2(wc, wc),
+                       wd2 = make_float2(wd, wd);
+          const uint4 ua = *reinterpret_cast<const uint4*>(s0 + x0 * C + c);
+          const uint4 ub = *reinterpret_cast<const uint4*>(s0 + x1 * C + c);
+          const uint4 uc = *reinterpret_cast<const uint4*>(s1 + x0 * C + c);
+          const uint4 ud = *reinterpret_cast<const uint4*>(s1 + x1 * C + c);
+          uint4 up = make_uint4(0, 0, 0, 0);
+          if (prow) up = *reinterpret_cast<const uint4*>(prow + (xs0 - 1 + p) * C + c);
+          const __half2* ha = reinterpret_cast<const __half2*>(&ua);
+          const __half2* hb = reinterpret_cast<const __half2*>(&ub);
+          const __half2* hc = reinterpret_cast<const __half2*>(&uc);
+          const __half2* hd = reinterpret_cast<const __half2*>(&ud);
+          const __half2* hp = reinterpret_cast<const __half2*>(&up);
+          __half2* ho = reinterpret_cast<__half2*>(&uo);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            float2 r = __fmul2_rn(__half22float2(ha[k]), wa2);
+            r = __ffma2_rn(__half22float2(hb[k]), wb2, r);
+            r = __ffma2_rn(__half22float2(hc[k]), wc2, r);
+            r = __ffma2_rn(__half22float2(hd[k]), wd2, r);
+            if (prow) r = __fadd2_rn(r, __half22float2(hp[k]));
+            ho[k] = __floats2half2_rn(r.x, r.y);
+          }
+        }
+        *reinterpret_cast<uint4*>(dst + (kc * kPx + p) * 16) = uo;
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&row_full[j & 3]);
+    };
+    const float* cb = sC;
+    auto epilogue = [&](int i) -> bool {
+      if (!mbar_wait_warp(&acc_full[i & 1], (i >> 1) & 1, status, kStatusTimeoutAccum)) return false;
+      tc_fence_after();
+      uint32_t raw[32];
+      tmem_ld32(tmem + (i & 1) * kOC + (static_cast<uint32_t>(warp * 32) << 16), raw);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[i & 1]);
+      const int xo = xs0 + warp * 32 + lane;
+      if (xo < W) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) + cb[j];
+        if (e.o2_ln_g) {
+          float mean = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) mean += v[j];
+          mean *= (1.0f / 32.0f);
+          float var = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float d = v[j] - mean;
+            var += d * d;
+          }
+          var *= (1.0f / 32.0f);
+          const float rstd = rsqrtf(var + e.o2_ln_eps);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = (v[j] - mean) * rstd * cb[32 + j] + cb[64 + j];
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+        const size_t pix = (static_cast<size_t>(b) * H + ya + i) * W + xo;
+        for (int od = 0; od < e.o2_dim; ++od) {
+          float l = cb[352 + od];
+          const float* w = cb + 96 + od * 32;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) l = fmaf(v[j], w[j], l);
+          e.o2_out[od][pix] = out_act(l, e.o2_act[od], e.o2_scale);
+        }
+      }
+      return true;
+    };
+    bool ok = true;
+    for (int j = 0; j <= R + 1 && ok; ++j) {
+      // slot j & 3 last held row j - 4, last read by MMA(j - 4)
+      if (j >= 4) ok = mbar_wait_warp(&slot_free[j & 3], ((j - 4) >> 2) & 1, status, kStatusTimeoutEmpty);
+      if (!ok) break;
+      build(j);
+      if (warp < 4 && j >= 3) ok = epilogue(j - 3);
+    }
+    if (ok && warp < 4 && R >= 1) epilogue(R - 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kBuildWarps) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
+  }
+}
+
+}  // namespace
+
+int up_out2(const __half* src, int B, int hs, int ws, int C, const __half* pe, int H, int W, const __half* wp,
+            int icp, const EpiArgs& e, int* status, cudaStream_t s) {
+  if (B <= 0 || hs <= 0 || ws <= 0 || H <= 0 || W <= 0) return 0;
+  if (C % 16 || C > 128 || icp < C || icp % 8 || e.kind != kEpiOut2 || e.o2_dim < 1 || e.o2_dim > 8) return -1;
+  for (int i = 0; i < e.o2_dim; ++i)
+    if (!e.o2_out[i]) return -1;
+  if ((reinterpret_cast<uintptr_t>(src) & 15) || (pe && (reinterpret_cast<uintptr_t>(pe) & 15)) ||
+      (reinterpret_cast<uintptr_t>(wp) & 15))
+    return -2;
+  const Layout L = layout_for(C);
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!((attr_set >> (dev & 63)) & 1)) {
+    if (cudaFuncSetAttribute(k_up_out2, cudaFuncAttributeMaxDynamicSharedMemorySize, layout_for(128).total) !=
+        cudaSuccess)
+      return -3;
+    attr_set |= uint64_t(1) << (dev & 63);
+  }
+  dim3 grid((W + kTile - 1) / kTile, (H + kRows - 1) / kRows, B);
+  k_up_out2<<<grid, kThreads, L.total, s>>>(src, hs, ws, C, pe, H, W, wp, icp, e, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+}  // namespace da3b

@@ -24,6 +24,11 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
 int conv_nhwc(const __half* X, int B, int H, int W, int IC, const __half* Wp, int OC, int ksize, int bn,
               const EpiArgs& e, int* status, cudaStream_t stream);
 int pick_bn(int N);
+// Fused align-corners upsample (+ UV pos-embed) -> 3x3 conv to 32 channels -> the
+// kEpiOut2 epilogue (head_fused.cu): src NHWC [B][hs][ws][C] f16, output grid H x W,
+// packed 3x3 weights [32][9][icp] (conv_nhwc layout), e.o2_* as for conv_nhwc.
+int up_out2(const __half* src, int B, int hs, int ws, int C, const __half* pe, int H, int W, const __half* wp,
+            int icp, const EpiArgs& e, int* status, cudaStream_t s);
 inline int conv_icp(int IC) { return (IC + 63) / 64 * 64; }
 
 EpiArgs epi_default();
