@@ -31,6 +31,8 @@ SIGNATURES = {
     "da3b_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "da3b_attention_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "da3b_upsample_nhwc": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p]),
+    "da3b_output_conv2": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p,
+                                  c_void_p, c_void_p, c_int, c_void_p, c_float, c_void_p, c_int, c_void_p]),
     "da3b_resize_u8": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_int, c_int, c_void_p]),
     "da3b_preprocess_legacy": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                        ctypes.POINTER(c_int), ctypes.POINTER(c_int), c_void_p]),

@@ -157,4 +157,36 @@ DA3B_API int da3b_conv_nhwc(const void* x, int B, int H, int W, int IC, const vo
                    st, static_cast<cudaStream_t>(stream));
 }
 
+DA3B_API int da3b_output_conv2(const void* feat, int B, int hs, int ws, int C, const void* pe, int H, int W,
+                               const void* w_packed, const float* out2a_bias, const float* out2b_w,
+                               const float* out2b_b, int od, const int* act, float scale, float* const* out,
+                               int fused, void* stream) {
+  if (!feat || !w_packed || !out2b_w || !out2b_b || !act || !out || od < 1 || od > 8) return -100;
+  int* st = device_status_word();
+  if (!st) return -101;
+  EpiArgs e = epi_default();
+  e.kind = kEpiOut2;
+  e.bias = out2a_bias;
+  e.o2_w = out2b_w;
+  e.o2_b = out2b_b;
+  e.o2_dim = od;
+  e.o2_scale = scale;
+  for (int i = 0; i < od; ++i) {
+    if (act[i] < 0 || act[i] > 4 || !out[i]) return -100;
+    e.o2_act[i] = act[i];
+    e.o2_out[i] = out[i];
+  }
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const __half* x = static_cast<const __half*>(feat);
+  const __half* wp = static_cast<const __half*>(w_packed);
+  if (fused) return up_out2(x, B, hs, ws, C, static_cast<const __half*>(pe), H, W, wp, conv_icp(C), e, st, s);
+  __half* up = nullptr;
+  if (cudaMallocAsync(reinterpret_cast<void**>(&up), static_cast<size_t>(B) * H * W * C * 2, s) != cudaSuccess)
+    return -102;
+  int rc = upsample_ac(x, B, hs, ws, C, up, H, W, static_cast<const __half*>(pe), s);
+  if (!rc) rc = conv_nhwc(up, B, H, W, C, wp, 32, 3, 32, e, st, s);
+  cudaFreeAsync(up, s);
+  return rc;
+}
+
 }  // extern "C"

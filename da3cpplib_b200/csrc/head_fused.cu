@@ -3,20 +3,23 @@
 // output_dim and the output activation (src/dpt_head.cpp:199-222 and :327-338; the
 // feature map `feat_map` of the reference is never written to memory).
 //
-// One CTA = a 128-pixel strip of up to kRows consecutive output rows of one image.
-// The upsampled rows the 3x3 taps need (128 + 2 halo pixels, all channels) are built
-// in shared memory in a ring of four row slots, laid out K-major without swizzle:
-// [16-byte channel chunk][pixel][8 halves]. In that layout an operand view shifted by
-// one pixel is a 16-byte move of the start address (8-row groups 128 B apart, channel
-// chunks one row-slot-plane apart), so the three horizontal taps read the same row
-// slot and each upsampled value is built once per strip instead of nine times.
+// One CTA = a strip of 120 output pixels of up to kRows consecutive output rows of one
+// image. The upsampled rows the 3x3 taps need are built once each in shared memory,
+// in a ring of four row slots laid out K-major without swizzle ([16-byte channel
+// chunk][row][8 halves]); slot row r = 32 w + l holds strip pixel 30 w + l, so each
+// 32-row block (one epilogue warp's TMEM lanes) carries its 30 pixels plus the 2 halo
+// pixels on its right. The three horizontal taps go into N: per row and vertical tap
+// dy, one tcgen05.mma (M = 128 rows, N = 96 = 3 taps x 32 channels, K = 16) per 16
+// input channels gives Z_dx[r] = sum_c A[r][c] W[dy][dx][c] for all three dx at once,
+// and lane l < 30 of an epilogue warp forms out = Z_0[l] + Z_1[l + 1] + Z_2[l + 2] with
+// shuffles inside the warp (a small-N MMA costs about as much per instruction as
+// N = 96, so one wide MMA replaces three narrow ones; no warp needs another's data).
 //   warps 0-7  build row j+2 while the tensor core works on row j (bilinear from the
-//              NHWC out1 map through L2, f32 weights as k_upsample_ac, PE added, f16);
-//              warps 0-3 also run the epilogue: TMEM -> bias, relu, 1x1 conv, activation;
-//   warp 8     one thread issues the 9 taps x C/16 tcgen05.mma (M=128, N=32, K=16)
-//              of a row into one of two TMEM accumulators.
-// The MMA order (tap-major, channels ascending) and every f32 expression equal the
-// unfused upsample + conv_nhwc path, so the outputs are bit-identical to it.
+//              NHWC out1 map, the f32 weights of k_upsample_ac, PE added, f16), after
+//              an L2 prefetch of the source rows two steps ahead; warps 0-3 also run
+//              the epilogue: TMEM -> tap sum, bias, relu, 1x1 conv, activation;
+//   warp 8     one thread issues the 3 x C/16 MMAs of a row into one of two TMEM
+//              accumulators of 96 columns.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -30,13 +33,14 @@
 namespace da3b {
 namespace {
 
-constexpr int kTile = 128;             // output pixels per strip (MMA M)
-constexpr int kPx = kTile + 2;         // strip pixels with the 3x3 halo
+constexpr int kPx = 128;               // slot rows per strip (MMA M)
+constexpr int kTile = 120;             // output pixels per strip: 4 warps x 30
 constexpr int kSlots = 4;              // upsampled-row ring
 constexpr int kRows = 74;              // output rows per CTA
 constexpr int kBuildWarps = 8;
 constexpr int kThreads = (kBuildWarps + 1) * 32;
 constexpr int kOC = 32;                // output_conv2 hidden channels
+constexpr int kN = 3 * kOC;            // MMA N: three horizontal taps x 32 channels
 constexpr int kConsts = 360;           // bias 32 | LN gamma 32 | LN beta 32 | out2b 8x32 | out2b bias 8
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -92,9 +96,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float sf0 = (W > 1 && ws > 1) ? static_cast<float>(W - 1) / (ws - 1) : static_cast<float>(W) / ws;
   const float sf1 = (H > 1 && hs > 1) ? static_cast<float>(H - 1) / (hs - 1) : static_cast<float>(H) / hs;
 
-  // per-CTA tables: source columns of the strip pixels, epilogue constants, weights
+  // per-CTA tables: source columns of the slot rows, epilogue constants, weights
   for (int p = threadIdx.x; p < kPx; p += blockDim.x) {
-    const int xo = xs0 - 1 + p;
+    const int xo = xs0 - 1 + 30 * (p >> 5) + (p & 31);  // slot row -> image column
     if (xo < 0 || xo >= W) {
       sX0[p] = -1;
       sX1[p] = -1;
@@ -117,10 +121,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     else v = (i - 352) < e.o2_dim ? e.o2_b[i - 352] : 0.f;
     sC[i] = v;
   }
-  // packed weights [32][9][icp] -> [tap * nkc + chunk][oc][8 halves]
+  // packed weights [32][9][icp] (tap = 3 dy + dx) -> [dy][chunk][dx * 32 + oc][8 halves]
   for (int i = threadIdx.x; i < kOC * 9 * nkc; i += blockDim.x) {
     const int c8 = i % nkc, t = (i / nkc) % 9, oc = i / (nkc * 9);
-    *reinterpret_cast<uint4*>(sW + ((t * nkc + c8) * kOC + oc) * 16) =
+    const int dy = t / 3, dx = t % 3;
+    *reinterpret_cast<uint4*>(sW + ((dy * nkc + c8) * kN + dx * kOC + oc) * 16) =
         *reinterpret_cast<const uint4*>(wp + (static_cast<size_t>(oc) * 9 + t) * icp + c8 * 8);
   }
   fence_async_smem();
@@ -136,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(drain, 1);
     fence_mbar_init();
   }
-  if (warp == kBuildWarps) tmem_alloc(tmem_slot, 64);
+  if (warp == kBuildWarps) tmem_alloc(tmem_slot, 256);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -146,8 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ------------------------------------------------------------------ MMA
       // output row i reads row slots (i, i+1, i+2) & 3 = upsampled rows y-1, y, y+1
-      constexpr uint32_t idesc = umma_idesc_f16(128, kOC);
-      const uint32_t lbo_a = kPx * 16, lbo_b = kOC * 16;
+      constexpr uint32_t idesc = umma_idesc_f16(128, kN);
+      const uint32_t lbo_a = kPx * 16, lbo_b = kN * 16;
       const uint32_t rows0 = smem_u32(sRows), w0 = smem_u32(sW);
       bool ok = true;
       int issued = 0;
@@ -157,20 +162,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok && i >= 2) ok = mbar_wait(&acc_empty[i & 1], ((i >> 1) - 1) & 1, status, kStatusTimeoutAccumFree);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t tAcc = tmem + (i & 1) * kOC;
+        const uint32_t tAcc = tmem + (i & 1) * 128;
         uint32_t acc = 0;
 #pragma unroll 1
         for (int dy = 0; dy < 3; ++dy) {
           const uint32_t rb = rows0 + ((i + dy) & 3) * L.slot_bytes;
-#pragma unroll 1
-          for (int dx = 0; dx < 3; ++dx) {
-            const int t = dy * 3 + dx;
-            for (int k = 0; k < nkc / 2; ++k) {
-              const uint64_t a = desc_noswz(rb + (2 * k * kPx + dx) * 16, lbo_a, 128);
-              const uint64_t bw = desc_noswz(w0 + ((t * nkc + 2 * k) * kOC) * 16, lbo_b, 128);
-              umma_f16(tAcc, a, bw, idesc, acc);
-              acc = 1;
-            }
+          for (int k = 0; k < nkc / 2; ++k) {
+            const uint64_t a = desc_noswz(rb + (2 * k * kPx) * 16, lbo_a, 128);
+            const uint64_t bw = desc_noswz(w0 + ((dy * nkc + 2 * k) * kN) * 16, lbo_b, 128);
+            umma_f16(tAcc, a, bw, idesc, acc);
+            acc = 1;
           }
         }
         umma_commit(&acc_full[i & 1]);
@@ -188,6 +189,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ builders
     const int tb = threadIdx.x;  // 0 .. 255
     const size_t img = static_cast<size_t>(b) * hs;
+    // first / last slot row inside the image (source column range of the strip)
+    const int xlo_row = xs0 == 0 ? 1 : 0;
+    int xhi_row = kPx - 1;
+    while (xhi_row > xlo_row && sX0[xhi_row] < 0) --xhi_row;
     auto build = [&](int j) {
       const int u = ya - 1 + j;  // upsampled row
       uint8_t* dst = sRows + (j & 3) * L.slot_bytes;
@@ -196,6 +201,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const __half* s0 = src;
       const __half* s1 = src;
       const __half* prow = nullptr;
+      {
+        // L2 prefetch of the source rows of upsampled row u + 2 (built two steps later)
+        const int u2 = u + 2;
+        if (u2 >= 0 && u2 < H) {
+          const float f2 = static_cast<float>(u2) / sf1;
+          const int r0 = max(0, min(static_cast<int>(floorf(f2)), hs - 1));
+          const int r1 = max(0, min(static_cast<int>(floorf(f2)) + 1, hs - 1));
+          const int xlo = sX0[xlo_row], xhi = sX1[xhi_row];
+          const int nl = ((xhi - xlo + 1) * C * 2 + 127) / 128;
+          for (int l = tb; l < 2 * nl; l += kBuildWarps * 32) {
+            const int row = l < nl ? r0 : r1;
+            const __half* a = src + ((img + row) * ws + xlo) * C + (l < nl ? l : l - nl) * 64;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+          }
+        }
+      }
       if (row_ok) {
         const float fy = static_cast<float>(u) / sf1;
         int y0 = static_cast<int>(floorf(fy));
@@ -207,39 +228,58 @@ __global__ void __launch_bounds__(kThreads, 1)
         s1 = src + (img + y1) * ws * C;
         if (pe) prow = pe + static_cast<size_t>(u) * W * C;
       }
-      for (int it = tb; it < kPx * nkc; it += kBuildWarps * 32) {
-        const int p = it / nkc, kc = it - p * nkc;
-        uint4 uo = make_uint4(0, 0, 0, 0);
-        const int x0 = sX0[p];
-        if (row_ok && x0 >= 0) {
-          const int x1 = sX1[p], c = kc * 8;
-          const float dx = sDX[p];
-          const float wa = (1 - dx) * (1 - dy), wb = dx * (1 - dy), wc = (1 - dx) * dy, wd = dx * dy;
-          const float2 wa2 = make_float2(wa, wa), wb2 = make_float2(wb, wb), wc2 = make_float2(wc, wc),
-                       wd2 = make_float2(wd, wd);
-          const uint4 ua = *reinterpret_cast<const uint4*>(s0 + x0 * C + c);
-          const uint4 ub = *reinterpret_cast<const uint4*>(s0 + x1 * C + c);
-          const uint4 uc = *reinterpret_cast<const uint4*>(s1 + x0 * C + c);
-          const uint4 ud = *reinterpret_cast<const uint4*>(s1 + x1 * C + c);
-          uint4 up = make_uint4(0, 0, 0, 0);
-          if (prow) up = *reinterpret_cast<const uint4*>(prow + (xs0 - 1 + p) * C + c);
-          const __half2* ha = reinterpret_cast<const __half2*>(&ua);
-          const __half2* hb = reinterpret_cast<const __half2*>(&ub);
-          const __half2* hc = reinterpret_cast<const __half2*>(&uc);
-          const __half2* hd = reinterpret_cast<const __half2*>(&ud);
-          const __half2* hp = reinterpret_cast<const __half2*>(&up);
-          __half2* ho = reinterpret_cast<__half2*>(&uo);
+      // kBatch items per thread in flight: their 4 * kBatch corner loads are issued
+      // before any is used (the loads, not the arithmetic, bound this loop)
+      constexpr int kBatch = 4;
+      const int total = kPx * nkc;
+      for (int base = tb; base < total; base += kBatch * kBuildWarps * 32) {
+        uint4 ua[kBatch], ub[kBatch], uc[kBatch], ud[kBatch], up[kBatch];
+        bool live[kBatch];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            float2 r = __fmul2_rn(__half22float2(ha[k]), wa2);
-            r = __ffma2_rn(__half22float2(hb[k]), wb2, r);
-            r = __ffma2_rn(__half22float2(hc[k]), wc2, r);
-            r = __ffma2_rn(__half22float2(hd[k]), wd2, r);
-            if (prow) r = __fadd2_rn(r, __half22float2(hp[k]));
-            ho[k] = __floats2half2_rn(r.x, r.y);
+        for (int q = 0; q < kBatch; ++q) {
+          const int it = base + q * kBuildWarps * 32;
+          const int p = it / nkc, kc = it - p * nkc;
+          const int x0 = it < total ? sX0[p] : -1;
+          live[q] = row_ok && x0 >= 0;
+          ua[q] = ub[q] = uc[q] = ud[q] = up[q] = make_uint4(0, 0, 0, 0);
+          if (live[q]) {
+            const int x1 = sX1[p], c = kc * 8;
+            ua[q] = *reinterpret_cast<const uint4*>(s0 + x0 * C + c);
+            ub[q] = *reinterpret_cast<const uint4*>(s0 + x1 * C + c);
+            uc[q] = *reinterpret_cast<const uint4*>(s1 + x0 * C + c);
+            ud[q] = *reinterpret_cast<const uint4*>(s1 + x1 * C + c);
+            if (prow) up[q] = *reinterpret_cast<const uint4*>(prow + (xs0 - 1 + 30 * (p >> 5) + (p & 31)) * C + c);
           }
         }
-        *reinterpret_cast<uint4*>(dst + (kc * kPx + p) * 16) = uo;
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+          const int it = base + q * kBuildWarps * 32;
+          if (it >= total) break;
+          const int p = it / nkc, kc = it - p * nkc;
+          uint4 uo = make_uint4(0, 0, 0, 0);
+          if (live[q]) {
+            const float dx = sDX[p];
+            const float wa = (1 - dx) * (1 - dy), wb = dx * (1 - dy), wc = (1 - dx) * dy, wd = dx * dy;
+            const float2 wa2 = make_float2(wa, wa), wb2 = make_float2(wb, wb), wc2 = make_float2(wc, wc),
+                         wd2 = make_float2(wd, wd);
+            const __half2* ha = reinterpret_cast<const __half2*>(&ua[q]);
+            const __half2* hb = reinterpret_cast<const __half2*>(&ub[q]);
+            const __half2* hc = reinterpret_cast<const __half2*>(&uc[q]);
+            const __half2* hd = reinterpret_cast<const __half2*>(&ud[q]);
+            const __half2* hp = reinterpret_cast<const __half2*>(&up[q]);
+            __half2* ho = reinterpret_cast<__half2*>(&uo);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              float2 r = __fmul2_rn(__half22float2(ha[k]), wa2);
+              r = __ffma2_rn(__half22float2(hb[k]), wb2, r);
+              r = __ffma2_rn(__half22float2(hc[k]), wc2, r);
+              r = __ffma2_rn(__half22float2(hd[k]), wd2, r);
+              if (prow) r = __fadd2_rn(r, __half22float2(hp[k]));
+              ho[k] = __floats2half2_rn(r.x, r.y);
+            }
+          }
+          *reinterpret_cast<uint4*>(dst + (kc * kPx + p) * 16) = uo;
+        }
       }
       fence_async_smem();
       __syncwarp();
@@ -249,17 +289,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto epilogue = [&](int i) -> bool {
       if (!mbar_wait_warp(&acc_full[i & 1], (i >> 1) & 1, status, kStatusTimeoutAccum)) return false;
       tc_fence_after();
-      uint32_t raw[32];
-      tmem_ld32(tmem + (i & 1) * kOC + (static_cast<uint32_t>(warp * 32) << 16), raw);
+      // lane l of warp w: slot row 32 w + l, Z_dx for dx = 0, 1, 2
+      const uint32_t ta = tmem + (i & 1) * 128 + (static_cast<uint32_t>(warp * 32) << 16);
+      uint32_t z0[32], z1[32], z2[32];
+      tmem_ld32(ta, z0);
+      tmem_ld32(ta + kOC, z1);
+      tmem_ld32(ta + 2 * kOC, z2);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[i & 1]);
-      const int xo = xs0 + warp * 32 + lane;
-      if (xo < W) {
-        float v[32];
+      float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) + cb[j];
+      for (int j = 0; j < 32; ++j) {
+        const float a1 = __shfl_down_sync(0xffffffffu, __uint_as_float(z1[j]), 1);
+        const float a2 = __shfl_down_sync(0xffffffffu, __uint_as_float(z2[j]), 2);
+        v[j] = ((__uint_as_float(z0[j]) + a1) + a2) + cb[j];
+      }
+      const int xo = xs0 + warp * 30 + lane;
+      if (lane < 30 && xo < W) {
         if (e.o2_ln_g) {
           float mean = 0.f;
 #pragma unroll
@@ -303,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == kBuildWarps) {
     tc_fence_after();
-    tmem_dealloc(tmem, 64);
+    tmem_dealloc(tmem, 256);
   }
 }
 

@@ -9,6 +9,8 @@ Part B: DPT-head 3x3 stride-1 pad-1 convs, NHWC f16, C_in = C_out in {64, 128, 2
 spatial 37..296, batch 8 (da3b_conv_nhwc).
 attn: da3b_attention at the C3 shape (64 x 1370 tokens, 16 heads) and the DA3
 multi-view global layer (8 views x 1297 tokens per scene).
+out2: da3b_output_conv2 (upsample 296 -> 518 + 3x3 conv 128 -> 32 + 1x1 -> depth) at the
+C3 head shape, fused and through a materialised upsampled map.
 ray: da3b_ray_pose (the ray->pose solver, both host round trips included; wall time)
 on a synthetic 288 x 288 ray field, the aux resolution of a 504 x 504 image.
 
@@ -68,7 +70,7 @@ def main(argv=None):
     from . import _lib
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("--part", default="all", choices=["A", "B", "attn", "up", "pre", "ray", "all"])
+    ap.add_argument("--part", default="all", choices=["A", "B", "attn", "up", "pre", "ray", "out2", "all"])
     ap.add_argument("--m", type=int, default=0, help="Part A: only this M")
     ap.add_argument("--kn", default="", help="Part A: only this K,N (e.g. 1024,4096)")
     ap.add_argument("--act", type=int, default=0, help="Part A activation: 0 none, 2 erf-GELU")
@@ -207,6 +209,31 @@ def main(argv=None):
             ms = timeit(run)
             emit("attn", f"{tag}: nseq={nseq} seqlen={seqlen} heads={heads}", ms, 4.0 * nseq * seqlen * seqlen * D)
             del qkv, out
+
+    if args.part in ("out2", "all"):
+        B, hs, C, H = args.batch if args.batch != 8 else 64, 296, 128, 518
+        feat = (torch.randn((B, hs, hs, C), generator=gen, device="cuda") * 0.5).half()
+        raw = torch.randn((32, C, 3, 3), generator=gen, device="cuda") / (9 * C) ** 0.5
+        wp = torch.zeros((32, 9, C), dtype=torch.float16, device="cuda")
+        if L.da3b_pack_conv_weight(P(raw), 32, C, 3, P(wp), S):
+            raise RuntimeError("pack failed")
+        b1 = torch.randn(32, generator=gen, device="cuda") * 0.1
+        w2 = torch.randn((1, 32), generator=gen, device="cuda") * 0.2
+        b2 = torch.zeros(1, device="cuda")
+        out = torch.empty((B, H, H), device="cuda")
+        act = (ctypes.c_int * 1)(3)
+        outs = (ctypes.c_void_p * 1)(out.data_ptr())
+        flops = 2.0 * B * H * H * C * 32 * 9
+        for fused in (1, 0):
+            def run():
+                rc = L.da3b_output_conv2(P(feat), B, hs, hs, C, None, H, H, P(wp), P(b1), P(w2), P(b2), 1, act,
+                                         ctypes.c_float(0.0), outs, fused, S)
+                if rc:
+                    raise RuntimeError(f"da3b_output_conv2 rc={rc}")
+
+            ms = timeit(run)
+            emit("out2", f"{'fused' if fused else 'unfused'} B={B} {hs}->{H} C={C}", ms, flops)
+        del feat, out
 
     if args.part in ("ray", "all"):
         import time

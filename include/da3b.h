@@ -116,6 +116,21 @@ DA3B_API int da3b_conv_nhwc(const void* x, int B, int H, int W, int IC, const vo
  * ggml_interpolate with GGML_SCALE_FLAG_ALIGN_CORNERS). */
 DA3B_API int da3b_upsample_nhwc(const void* in, int B, int hs, int ws, int C, void* out, int H, int W, void* stream);
 
+/* DPT output stage: output_conv2 on the align-corners upsample of out1, fused: feat NHWC
+ * f16 [B][hs][ws][C] (C a multiple of 16, at most 128) is upsampled to H x W (+ pe, NHWC
+ * f16 [H][W][C] or NULL: the 0.1 UV embedding of head_pos_embed), then the 3x3 conv
+ * (da3b_pack_conv_weight layout, 32 output channels, out2a_bias) -> relu -> 1x1 conv
+ * out2b_w [od][32] + out2b_b -> act[o] per output channel (0 identity, 1 relu, 2
+ * sigmoid * scale, 3 exp, 4 exp + 1) into out[o], f32 [B][H][W] device planes (od <= 8).
+ * Replaces interp_bilinear_ac + add_uv_input + the out2a / out2b convs of
+ * DptHead::build_depth_graph (src/dpt_head.cpp:199-222) and the activations of
+ * src/dpt_head.cpp:327-338 / :402-439. fused = 0 runs the same through a materialised
+ * f16 upsampled map (da3b_upsample_nhwc + the conv), for comparison. */
+DA3B_API int da3b_output_conv2(const void* feat, int B, int hs, int ws, int C, const void* pe, int H, int W,
+                               const void* w_packed, const float* out2a_bias, const float* out2b_w,
+                               const float* out2b_b, int od, const int* act, float scale, float* const* out,
+                               int fused, void* stream);
+
 /* uint8 HWC RGB resize of B images [B][sh][sw][3] -> [B][dh][dw][3], bit-exact with
  * DA3cpplib's resizers: mode 0 = resize_cubic (src/preprocess.cpp:61-99), mode 1 =
  * resize_area (:122-148, which falls back to its bilinear when both axes grow). src and

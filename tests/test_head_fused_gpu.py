@@ -3,11 +3,13 @@
 against the unfused path (upsample_ac into a f16 map, then conv_nhwc with the same
 fused out2b epilogue), selected with $DA3B_UNFUSED_UP=1 when a plan is created.
 
-Both paths round the upsampled values to f16 with the same f32 expressions and issue
-the tensor-core MMAs in the same order, so the outputs must be bit-identical: depth,
-confidence, the mono sky plane, raw logits, for widths that are and are not multiples
-of the 128-pixel strip and for batches of images. The parity of either path with the
-CPU oracle is covered by test_e2e_gpu.py / test_mono_nested_gpu.py.
+Both paths build the same f16 upsampled values; the fused kernel sums the three
+horizontal taps of the 3x3 conv in its epilogue (f32) instead of in the tensor-core
+accumulator, so the two differ only by f32 summation order: bound max|a - b| <=
+1e-4 * max(1, max|b|) on depth, confidence, the mono sky plane and the raw logits, for
+widths that are and are not multiples of the 126-pixel strip and for batches of
+images. The parity of either path with the CPU oracle is covered by test_e2e_gpu.py /
+test_mono_nested_gpu.py.
 """
 import os
 
@@ -52,7 +54,7 @@ CASES = [("da2-t", 112, 112, 2), ("da3-t", 126, 112, 3), ("da3-t", 140, 266, 1),
 
 
 @pytest.mark.parametrize("case", CASES, ids=[f"{c[0]}_{c[1]}x{c[2]}_b{c[3]}" for c in CASES])
-def test_fused_equals_unfused(cuda, case):
+def test_fused_matches_unfused(cuda, case):
     from da3cpplib_b200 import synth
 
     name, h, w, n = case
@@ -63,5 +65,6 @@ def test_fused_equals_unfused(cuda, case):
         b, lb = _run(path, imgs, unfused=True, raw=raw)
         assert a.keys() == b.keys()
         for k in a:
-            assert np.array_equal(a[k], b[k]), (k, raw, float(np.abs(a[k] - b[k]).max()))
+            err = float(np.abs(a[k] - b[k]).max())
+            assert err <= 1e-4 * max(1.0, float(np.abs(b[k]).max())), (k, raw, err)
         assert la == lb - 1  # one launch instead of upsample + conv
