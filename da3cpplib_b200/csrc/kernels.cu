@@ -117,12 +117,115 @@ __global__ void k_layernorm(const Tin* __restrict__ in, int ld_in, int rows, int
   }
 }
 
+// Same LayerNorm with 8 consecutive elements per lane (element e -> lane (e / 8) % 32,
+// slot (e / 256) * 8 + e % 8): 32-byte f32 / 16-byte f16 loads, gamma and beta as
+// float4 pairs, one 16-byte store per 8 outputs. For D a multiple of 256.
+template <typename Tin, int VPL>
+__global__ void k_layernorm8(const Tin* __restrict__ in, int ld_in, int rows, int D, const float* __restrict__ g,
+                             const float* __restrict__ bta, float eps, __half* __restrict__ out, int ld_out,
+                             int col_off, int rm_div, int rm_mul, int rm_add, int q8) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int in_row = rm_div > 0 ? (warp / rm_div) * rm_mul + rm_add + warp % rm_div : warp;
+  const Tin* src = in + static_cast<size_t>(in_row) * ld_in;
+  float v[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; j += 8) {
+    const int idx = (j / 8) * 256 + lane * 8;
+    if (sizeof(Tin) == 4) {
+      const float4 f0 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + idx);
+      const float4 f1 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + idx + 4);
+      v[j] = f0.x; v[j + 1] = f0.y; v[j + 2] = f0.z; v[j + 3] = f0.w;
+      v[j + 4] = f1.x; v[j + 5] = f1.y; v[j + 6] = f1.z; v[j + 7] = f1.w;
+    } else {
+      const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(src) + idx);
+      const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(h[k]);
+        v[j + 2 * k] = f.x;
+        v[j + 2 * k + 1] = f.y;
+      }
+    }
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) s += v[j];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / D;
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const float d = v[j] - mean;
+    q += d * d;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = rsqrtf(q / D + eps);
+  __half* dst = out + static_cast<size_t>(warp) * ld_out + col_off;
+#pragma unroll
+  for (int j = 0; j < VPL; j += 8) {
+    const int idx = (j / 8) * 256 + lane * 8;
+    const float4 g0 = __ldg(reinterpret_cast<const float4*>(g + idx));
+    const float4 g1 = __ldg(reinterpret_cast<const float4*>(g + idx + 4));
+    float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
+    if (bta) {
+      b0 = __ldg(reinterpret_cast<const float4*>(bta + idx));
+      b1 = __ldg(reinterpret_cast<const float4*>(bta + idx + 4));
+    }
+    const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    float r[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[i] = (v[j + i] - mean) * rstd * gg[i] + bb[i];
+    if (q8) {
+      // Q8_0 round trip over the 32-element block held by 4 consecutive lanes
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(r[i]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      const float d = amax / 127.0f;
+      const float id = d != 0.f ? 1.0f / d : 0.0f;
+      const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+      for (int i = 0; i < 8; ++i) r[i] = dh * roundf(r[i] * id);
+    }
+    uint4 u;
+    __half2* hu = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) hu[k] = __floats2half2_rn(r[2 * k], r[2 * k + 1]);
+    *reinterpret_cast<uint4*>(dst + idx) = u;
+  }
+}
+
 template <typename Tin>
 static int ln_dispatch(const Tin* in, int ld_in, int rows, int D, const float* g, const float* b, float eps,
                        __half* out, int ld_out, int col_off, int rm_div, int rm_mul, int rm_add, int q8,
                        cudaStream_t s) {
   if (rows <= 0) return 0;
   const unsigned blocks = static_cast<unsigned>((static_cast<long>(rows) * 32 + 255) / 256);
+  const bool wide = D % 256 == 0 && D <= 2048 && ld_in % 8 == 0 && ld_out % 8 == 0 && col_off % 8 == 0 &&
+                    (reinterpret_cast<uintptr_t>(in) & 31) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(g) & 15) == 0 && (reinterpret_cast<uintptr_t>(b) & 15) == 0;
+  if (wide) {
+#define DA3B_LN8(VPL)                                                                                          \
+  k_layernorm8<Tin, VPL><<<blocks, 256, 0, s>>>(in, ld_in, rows, D, g, b, eps, out, ld_out, col_off, rm_div, rm_mul, \
+                                                rm_add, q8)
+    switch (D) {
+      case 256: DA3B_LN8(8); break;
+      case 512: DA3B_LN8(16); break;
+      case 768: DA3B_LN8(24); break;
+      case 1024: DA3B_LN8(32); break;
+      case 1536: DA3B_LN8(48); break;
+      case 2048: DA3B_LN8(64); break;
+      default: return -1;
+    }
+#undef DA3B_LN8
+    return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  }
 #define DA3B_LN(VPL)                                                                                           \
   k_layernorm<Tin, VPL><<<blocks, 256, 0, s>>>(in, ld_in, rows, D, g, b, eps, out, ld_out, col_off, rm_div, rm_mul, \
                                                rm_add, q8)
@@ -297,11 +400,88 @@ __global__ void k_upsample_ac(const __half* __restrict__ in, int B, int hs, int 
     }
   }
 }
+// Slice-staged variant: one block per (output row, 64-channel slice). The two source
+// rows of the slice are read once, coalesced, into shared memory; every output pixel of
+// the row is then blended from there (the per-thread form above re-reads each source
+// value from L1/L2 about eight times). Same f32 expressions, so the same f16 results.
+constexpr int kUpCS = 64;
+__global__ void __launch_bounds__(256) k_upsample_staged(const __half* __restrict__ in, int hs, int ws, int C,
+                                                         __half* __restrict__ out, int H, int W,
+                                                         const __half* __restrict__ pe) {
+  extern __shared__ uint4 srow[];  // [2][ws][kUpCS / 8]
+  constexpr int nch = kUpCS / 8;
+  const int orow = blockIdx.x, cs0 = blockIdx.y * kUpCS;
+  const int y = orow % H, b = orow / H;
+  const float sf0 = (W > 1 && ws > 1) ? static_cast<float>(W - 1) / (ws - 1) : static_cast<float>(W) / ws;
+  const float sf1 = (H > 1 && hs > 1) ? static_cast<float>(H - 1) / (hs - 1) : static_cast<float>(H) / hs;
+  const float fy = static_cast<float>(y) / sf1;
+  int y0 = static_cast<int>(floorf(fy));
+  int y1 = y0 + 1;
+  const float dy = fminf(fmaxf(fy - floorf(fy), 0.f), 1.f);
+  y0 = max(0, min(y0, hs - 1));
+  y1 = max(0, min(y1, hs - 1));
+  const __half* s0 = in + (static_cast<size_t>(b) * hs + y0) * ws * C + cs0;
+  const __half* s1 = in + (static_cast<size_t>(b) * hs + y1) * ws * C + cs0;
+  for (int i = threadIdx.x; i < 2 * ws * nch; i += blockDim.x) {
+    const int r = i / (ws * nch), k = i - r * ws * nch, x = k / nch, c = k - x * nch;
+    srow[i] = *reinterpret_cast<const uint4*>((r ? s1 : s0) + static_cast<size_t>(x) * C + c * 8);
+  }
+  __syncthreads();
+  __half* dst = out + static_cast<size_t>(orow) * W * C + cs0;
+  const __half* prow = pe ? pe + static_cast<size_t>(y) * W * C + cs0 : nullptr;
+  for (int i = threadIdx.x; i < W * nch; i += blockDim.x) {
+    const int x = i / nch, c = i - x * nch;
+    const float fx = static_cast<float>(x) / sf0;
+    int x0 = static_cast<int>(floorf(fx));
+    int x1 = x0 + 1;
+    const float dx = fminf(fmaxf(fx - floorf(fx), 0.f), 1.f);
+    x0 = max(0, min(x0, ws - 1));
+    x1 = max(0, min(x1, ws - 1));
+    const float wa = (1 - dx) * (1 - dy), wb = dx * (1 - dy), wc = (1 - dx) * dy, wd = dx * dy;
+    const uint4 ua = srow[x0 * nch + c], ub = srow[x1 * nch + c];
+    const uint4 uc = srow[(ws + x0) * nch + c], ud = srow[(ws + x1) * nch + c];
+    uint4 up = make_uint4(0, 0, 0, 0);
+    if (prow) up = *reinterpret_cast<const uint4*>(prow + static_cast<size_t>(x) * C + c * 8);
+    const __half2* ha = reinterpret_cast<const __half2*>(&ua);
+    const __half2* hb = reinterpret_cast<const __half2*>(&ub);
+    const __half2* hc = reinterpret_cast<const __half2*>(&uc);
+    const __half2* hd = reinterpret_cast<const __half2*>(&ud);
+    const __half2* hp = reinterpret_cast<const __half2*>(&up);
+    uint4 uo;
+    __half2* ho = reinterpret_cast<__half2*>(&uo);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 r = __fmul2_rn(__half22float2(ha[k]), make_float2(wa, wa));
+      r = __ffma2_rn(__half22float2(hb[k]), make_float2(wb, wb), r);
+      r = __ffma2_rn(__half22float2(hc[k]), make_float2(wc, wc), r);
+      r = __ffma2_rn(__half22float2(hd[k]), make_float2(wd, wd), r);
+      if (prow) r = __fadd2_rn(r, __half22float2(hp[k]));
+      ho[k] = __floats2half2_rn(r.x, r.y);
+    }
+    *reinterpret_cast<uint4*>(dst + static_cast<size_t>(x) * C + c * 8) = uo;
+  }
+}
+
 int upsample_ac(const __half* in, int B, int hs, int ws, int C, __half* out, int H, int W, const __half* pe,
                 cudaStream_t s) {
   if (C % 8) return -1;
   const long rows = static_cast<long>(B) * H;
   if (rows <= 0 || W <= 0) return 0;
+  const int staged_smem = 2 * ws * kUpCS * 2;
+  if (C % kUpCS == 0 && staged_smem <= 96 * 1024 && rows <= 0x7fffffffL) {
+    static uint64_t attr_set = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!((attr_set >> (dev & 63)) & 1)) {
+      if (cudaFuncSetAttribute(k_upsample_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) !=
+          cudaSuccess)
+        return -3;
+      attr_set |= uint64_t(1) << (dev & 63);
+    }
+    k_upsample_staged<<<dim3(static_cast<unsigned>(rows), C / kUpCS), 256, staged_smem, s>>>(in, hs, ws, C, out, H, W,
+                                                                                               pe);
+    return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  }
   const unsigned gy = static_cast<unsigned>(rows < 65535 ? rows : 65535);
   if (C % 32 == 0) {
     const int per_row = W * (C / 32);
