@@ -35,6 +35,8 @@ namespace {
 
 constexpr int kPx = 128;               // slot rows per strip (MMA M)
 constexpr int kTile = 120;             // output pixels per strip: 4 warps x 30
+constexpr int kPitch = kPx + 1;        // rows per channel-chunk plane: the extra 16 B spread the
+                                       // builders' 16-byte stores over all banks (2048 B would not)
 constexpr int kSlots = 4;              // upsampled-row ring
 constexpr int kRows = 74;              // output rows per CTA
 constexpr int kBuildWarps = 8;
@@ -62,7 +64,7 @@ struct Layout {
 
 __host__ __device__ inline Layout layout_for(int C) {
   Layout l;
-  l.slot_bytes = static_cast<uint32_t>(C / 8) * kPx * 16;
+  l.slot_bytes = static_cast<uint32_t>(C / 8) * kPitch * 16;
   l.w_bytes = 9u * static_cast<uint32_t>(C / 8) * kOC * 16;
   l.total = 1024 + kSlots * l.slot_bytes + l.w_bytes + kConsts * 4 + kPx * 12 + 16 * 8 + 16;
   return l;
@@ -152,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ------------------------------------------------------------------ MMA
       // output row i reads row slots (i, i+1, i+2) & 3 = upsampled rows y-1, y, y+1
       constexpr uint32_t idesc = umma_idesc_f16(128, kN);
-      const uint32_t lbo_a = kPx * 16, lbo_b = kN * 16;
+      const uint32_t lbo_a = kPitch * 16, lbo_b = kN * 16;
       const uint32_t rows0 = smem_u32(sRows), w0 = smem_u32(sW);
       bool ok = true;
       int issued = 0;
@@ -168,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int dy = 0; dy < 3; ++dy) {
           const uint32_t rb = rows0 + ((i + dy) & 3) * L.slot_bytes;
           for (int k = 0; k < nkc / 2; ++k) {
-            const uint64_t a = desc_noswz(rb + (2 * k * kPx) * 16, lbo_a, 128);
+            const uint64_t a = desc_noswz(rb + (2 * k * kPitch) * 16, lbo_a, 128);
             const uint64_t bw = desc_noswz(w0 + ((dy * nkc + 2 * k) * kN) * 16, lbo_b, 128);
             umma_f16(tAcc, a, bw, idesc, acc);
             acc = 1;
@@ -278,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ho[k] = __floats2half2_rn(r.x, r.y);
             }
           }
-          *reinterpret_cast<uint4*>(dst + (kc * kPx + p) * 16) = uo;
+          *reinterpret_cast<uint4*>(dst + (kc * kPitch + p) * 16) = uo;
         }
       }
       fence_async_smem();
