@@ -282,7 +282,7 @@ Plan* Engine::plan_for(int V, int S, int H, int W, bool rays) {
   {
     const char* u = getenv("DA3B_UNFUSED_UP");
     const int Fh = (c.head_features > 0 ? c.head_features : hd.rn[0].OC) / 2;
-    p->fused_up = !(u && u[0] == '1') && Fh % 16 == 0 && Fh <= 128;
+    p->fused_up = !(u && u[0] == '1') && Fh >= 16 && Fh <= 128 && (Fh & (Fh - 1)) == 0;
   }
   p->ho3 = (p->gh + 2 - 3) / 2 + 1;
   p->wo3 = (p->gw + 2 - 3) / 2 + 1;

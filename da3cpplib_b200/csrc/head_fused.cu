@@ -70,13 +70,15 @@ __host__ __device__ inline Layout layout_for(int C) {
   return l;
 }
 
+// C (the out1 channel count) is a template parameter: 16, 32, 64 or 128.
+template <int C>
 __global__ void __launch_bounds__(kThreads, 1)
-    k_up_out2(const __half* __restrict__ src, int hs, int ws, int C, const __half* __restrict__ pe, int H, int W,
+    k_up_out2(const __half* __restrict__ src, int hs, int ws, const __half* __restrict__ pe, int H, int W,
               const __half* __restrict__ wp, int icp, const EpiArgs e, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const Layout L = layout_for(C);
-  const int nkc = C >> 3;
+  constexpr int nkc = C >> 3;
   uint8_t* sRows = smem;
   uint8_t* sW = sRows + kSlots * L.slot_bytes;
   float* sC = reinterpret_cast<float*>(sW + L.w_bytes);
@@ -230,57 +232,69 @@ __global__ void __launch_bounds__(kThreads, 1)
         s1 = src + (img + y1) * ws * C;
         if (pe) prow = pe + static_cast<size_t>(u) * W * C;
       }
-      // kBatch items per thread in flight: their 4 * kBatch corner loads are issued
-      // before any is used (the loads, not the arithmetic, bound this loop)
       constexpr int kBatch = 4;
-      const int total = kPx * nkc;
-      for (int base = tb; base < total; base += kBatch * kBuildWarps * 32) {
-        uint4 ua[kBatch], ub[kBatch], uc[kBatch], ud[kBatch], up[kBatch];
-        bool live[kBatch];
+      {
+        // C / 8 = nkc is a power of two (the launcher checks): thread tb owns one
+        // 16-byte channel chunk of every pstep-th slot row
+        constexpr int pstep = (kBuildWarps * 32) / nkc;  // slot rows covered per pass
+        constexpr int nit = kPx / pstep;                 // items per thread: nkc / 2
+        const int kc_own = tb & (nkc - 1);
+        const int p0 = tb / nkc;  // its slot rows: p0 + t * pstep, t < nit
+        // kBatch items' corner loads are in flight before any is used (zero-filled
+        // first, which also keeps the compiler from spilling)
+        uint8_t* dcol = dst + (kc_own * kPitch) * 16;
+        if (!row_ok) {
+          for (int t = 0; t < nit; ++t) *reinterpret_cast<uint4*>(dcol + (p0 + t * pstep) * 16) = make_uint4(0, 0, 0, 0);
+        } else {
+          const __half* s0c = s0 + kc_own * 8;
+          const __half* s1c = s1 + kc_own * 8;
+#pragma unroll 1
+          for (int t0 = 0; t0 < nit; t0 += kBatch) {
+            uint4 ua[kBatch], ub[kBatch], uc[kBatch], ud[kBatch], up[kBatch];
 #pragma unroll
-        for (int q = 0; q < kBatch; ++q) {
-          const int it = base + q * kBuildWarps * 32;
-          const int p = it / nkc, kc = it - p * nkc;
-          const int x0 = it < total ? sX0[p] : -1;
-          live[q] = row_ok && x0 >= 0;
-          ua[q] = ub[q] = uc[q] = ud[q] = up[q] = make_uint4(0, 0, 0, 0);
-          if (live[q]) {
-            const int x1 = sX1[p], c = kc * 8;
-            ua[q] = *reinterpret_cast<const uint4*>(s0 + x0 * C + c);
-            ub[q] = *reinterpret_cast<const uint4*>(s0 + x1 * C + c);
-            uc[q] = *reinterpret_cast<const uint4*>(s1 + x0 * C + c);
-            ud[q] = *reinterpret_cast<const uint4*>(s1 + x1 * C + c);
-            if (prow) up[q] = *reinterpret_cast<const uint4*>(prow + (xs0 - 1 + 30 * (p >> 5) + (p & 31)) * C + c);
-          }
-        }
+            for (int q = 0; q < kBatch; ++q) ua[q] = ub[q] = uc[q] = ud[q] = up[q] = make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int q = 0; q < kBatch; ++q) {
-          const int it = base + q * kBuildWarps * 32;
-          if (it >= total) break;
-          const int p = it / nkc, kc = it - p * nkc;
-          uint4 uo = make_uint4(0, 0, 0, 0);
-          if (live[q]) {
-            const float dx = sDX[p];
-            const float wa = (1 - dx) * (1 - dy), wb = dx * (1 - dy), wc = (1 - dx) * dy, wd = dx * dy;
-            const float2 wa2 = make_float2(wa, wa), wb2 = make_float2(wb, wb), wc2 = make_float2(wc, wc),
-                         wd2 = make_float2(wd, wd);
-            const __half2* ha = reinterpret_cast<const __half2*>(&ua[q]);
-            const __half2* hb = reinterpret_cast<const __half2*>(&ub[q]);
-            const __half2* hc = reinterpret_cast<const __half2*>(&uc[q]);
-            const __half2* hd = reinterpret_cast<const __half2*>(&ud[q]);
-            const __half2* hp = reinterpret_cast<const __half2*>(&up[q]);
-            __half2* ho = reinterpret_cast<__half2*>(&uo);
+            for (int q = 0; q < kBatch; ++q) {
+              const int p = p0 + (t0 + q) * pstep;
+              const int x0 = (t0 + q < nit) ? sX0[p] : -1;
+              if (x0 >= 0) {
+                const int x1 = sX1[p];
+                ua[q] = *reinterpret_cast<const uint4*>(s0c + x0 * C);
+                ub[q] = *reinterpret_cast<const uint4*>(s0c + x1 * C);
+                uc[q] = *reinterpret_cast<const uint4*>(s1c + x0 * C);
+                ud[q] = *reinterpret_cast<const uint4*>(s1c + x1 * C);
+                if (prow) up[q] = *reinterpret_cast<const uint4*>(prow + (xs0 - 1 + 30 * (p >> 5) + (p & 31)) * C + kc_own * 8);
+              }
+            }
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              float2 r = __fmul2_rn(__half22float2(ha[k]), wa2);
-              r = __ffma2_rn(__half22float2(hb[k]), wb2, r);
-              r = __ffma2_rn(__half22float2(hc[k]), wc2, r);
-              r = __ffma2_rn(__half22float2(hd[k]), wd2, r);
-              if (prow) r = __fadd2_rn(r, __half22float2(hp[k]));
-              ho[k] = __floats2half2_rn(r.x, r.y);
+            for (int q = 0; q < kBatch; ++q) {
+              if (t0 + q >= nit) break;
+              const int p = p0 + (t0 + q) * pstep;
+              uint4 uo = make_uint4(0, 0, 0, 0);
+              if (sX0[p] >= 0) {
+                const float dx = sDX[p];
+                const float wa = (1 - dx) * (1 - dy), wb = dx * (1 - dy), wc = (1 - dx) * dy, wd = dx * dy;
+                const float2 wa2 = make_float2(wa, wa), wb2 = make_float2(wb, wb), wc2 = make_float2(wc, wc),
+                             wd2 = make_float2(wd, wd);
+                const __half2* ha = reinterpret_cast<const __half2*>(&ua[q]);
+                const __half2* hb = reinterpret_cast<const __half2*>(&ub[q]);
+                const __half2* hc = reinterpret_cast<const __half2*>(&uc[q]);
+                const __half2* hd = reinterpret_cast<const __half2*>(&ud[q]);
+                const __half2* hp = reinterpret_cast<const __half2*>(&up[q]);
+                __half2* ho = reinterpret_cast<__half2*>(&uo);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  float2 r = __fmul2_rn(__half22float2(ha[k]), wa2);
+                  r = __ffma2_rn(__half22float2(hb[k]), wb2, r);
+                  r = __ffma2_rn(__half22float2(hc[k]), wc2, r);
+                  r = __ffma2_rn(__half22float2(hd[k]), wd2, r);
+                  if (prow) r = __fadd2_rn(r, __half22float2(hp[k]));
+                  ho[k] = __floats2half2_rn(r.x, r.y);
+                }
+              }
+              *reinterpret_cast<uint4*>(dcol + p * 16) = uo;
             }
           }
-          *reinterpret_cast<uint4*>(dst + (kc * kPitch + p) * 16) = uo;
         }
       }
       fence_async_smem();
@@ -362,7 +376,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 int up_out2(const __half* src, int B, int hs, int ws, int C, const __half* pe, int H, int W, const __half* wp,
             int icp, const EpiArgs& e, int* status, cudaStream_t s) {
   if (B <= 0 || hs <= 0 || ws <= 0 || H <= 0 || W <= 0) return 0;
-  if (C % 16 || C > 128 || icp < C || icp % 8 || e.kind != kEpiOut2 || e.o2_dim < 1 || e.o2_dim > 8) return -1;
+  // C = 16, 32, 64 or 128: the builders give each thread one 16-byte chunk of C / 8
+  if (C < 16 || C > 128 || (C & (C - 1)) || icp < C || icp % 8 || e.kind != kEpiOut2 || e.o2_dim < 1 ||
+      e.o2_dim > 8)
+    return -1;
   for (int i = 0; i < e.o2_dim; ++i)
     if (!e.o2_out[i]) return -1;
   if ((reinterpret_cast<uintptr_t>(src) & 15) || (pe && (reinterpret_cast<uintptr_t>(pe) & 15)) ||
@@ -373,13 +390,24 @@ int up_out2(const __half* src, int B, int hs, int ws, int C, const __half* pe, i
   int dev = 0;
   cudaGetDevice(&dev);
   if (!((attr_set >> (dev & 63)) & 1)) {
-    if (cudaFuncSetAttribute(k_up_out2, cudaFuncAttributeMaxDynamicSharedMemorySize, layout_for(128).total) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(k_up_out2<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, layout_for(16).total) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(k_up_out2<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, layout_for(32).total) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(k_up_out2<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, layout_for(64).total) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(k_up_out2<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, layout_for(128).total) !=
+            cudaSuccess)
       return -3;
     attr_set |= uint64_t(1) << (dev & 63);
   }
   dim3 grid((W + kTile - 1) / kTile, (H + kRows - 1) / kRows, B);
-  k_up_out2<<<grid, kThreads, L.total, s>>>(src, hs, ws, C, pe, H, W, wp, icp, e, status);
+  switch (C) {
+    case 16: k_up_out2<16><<<grid, kThreads, L.total, s>>>(src, hs, ws, pe, H, W, wp, icp, e, status); break;
+    case 32: k_up_out2<32><<<grid, kThreads, L.total, s>>>(src, hs, ws, pe, H, W, wp, icp, e, status); break;
+    case 64: k_up_out2<64><<<grid, kThreads, L.total, s>>>(src, hs, ws, pe, H, W, wp, icp, e, status); break;
+    default: k_up_out2<128><<<grid, kThreads, L.total, s>>>(src, hs, ws, pe, H, W, wp, icp, e, status); break;
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
