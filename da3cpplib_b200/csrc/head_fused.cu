@@ -16,8 +16,9 @@
 // N = 96, so one wide MMA replaces three narrow ones; no warp needs another's data).
 //   warps 0-7  build row j+2 while the tensor core works on row j (bilinear from the
 //              NHWC out1 map, the f32 weights of k_upsample_ac, PE added, f16), after
-//              an L2 prefetch of the source rows two steps ahead; warps 0-3 also run
-//              the epilogue: TMEM -> tap sum, bias, relu, 1x1 conv, activation;
+//              an L2 prefetch of the source rows two steps ahead; warps 0-3 (even
+//              rows) and 4-7 (odd rows) also run the epilogue: TMEM -> tap sum,
+//              bias, relu, 1x1 conv, activation;
 //   warp 8     one thread issues the 3 x C/16 MMAs of a row into one of two TMEM
 //              accumulators of 96 columns.
 #include <cuda.h>
@@ -125,12 +126,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     else v = (i - 352) < e.o2_dim ? e.o2_b[i - 352] : 0.f;
     sC[i] = v;
   }
-  // packed weights [32][9][icp] (tap = 3 dy + dx) -> [dy][chunk][dx * 32 + oc][8 halves]
-  for (int i = threadIdx.x; i < kOC * 9 * nkc; i += blockDim.x) {
-    const int c8 = i % nkc, t = (i / nkc) % 9, oc = i / (nkc * 9);
-    const int dy = t / 3, dx = t % 3;
-    *reinterpret_cast<uint4*>(sW + ((dy * nkc + c8) * kN + dx * kOC + oc) * 16) =
-        *reinterpret_cast<const uint4*>(wp + (static_cast<size_t>(oc) * 9 + t) * icp + c8 * 8);
+  // packed weights [32][9][icp] (tap = 3 dy + dx) -> [dy][chunk][dx * 32 + oc][8 halves],
+  // four loads in flight per thread
+  constexpr int kWItems = kOC * 9 * nkc;
+  for (int i0 = threadIdx.x; i0 < kWItems; i0 += 4 * kThreads) {
+    uint4 wv[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = i0 + q * kThreads;
+      const int c8 = i % nkc, t = (i / nkc) % 9, oc = i / (nkc * 9);
+      wv[q] = i < kWItems ? *reinterpret_cast<const uint4*>(wp + (static_cast<size_t>(oc) * 9 + t) * icp + c8 * 8)
+                          : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = i0 + q * kThreads;
+      if (i >= kWItems) break;
+      const int c8 = i % nkc, t = (i / nkc) % 9, oc = i / (nkc * 9);
+      const int dy = t / 3, dx = t % 3;
+      *reinterpret_cast<uint4*>(sW + ((dy * nkc + c8) * kN + dx * kOC + oc) * 16) = wv[q];
+    }
   }
   fence_async_smem();
   if (threadIdx.x == 0) {
@@ -305,8 +320,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto epilogue = [&](int i) -> bool {
       if (!mbar_wait_warp(&acc_full[i & 1], (i >> 1) & 1, status, kStatusTimeoutAccum)) return false;
       tc_fence_after();
-      // lane l of warp w: slot row 32 w + l, Z_dx for dx = 0, 1, 2
-      const uint32_t ta = tmem + (i & 1) * 128 + (static_cast<uint32_t>(warp * 32) << 16);
+      // lane l of warp w: slot row 32 (w mod 4) + l, Z_dx for dx = 0, 1, 2
+      const uint32_t ta = tmem + (i & 1) * 128 + (static_cast<uint32_t>((warp & 3) * 32) << 16);
       uint32_t z0[32], z1[32], z2[32];
       tmem_ld32(ta, z0);
       tmem_ld32(ta + kOC, z1);
@@ -322,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float a2 = __shfl_down_sync(0xffffffffu, __uint_as_float(z2[j]), 2);
         v[j] = ((__uint_as_float(z0[j]) + a1) + a2) + cb[j];
       }
-      const int xo = xs0 + warp * 30 + lane;
+      const int xo = xs0 + (warp & 3) * 30 + lane;
       if (lane < 30 && xo < W) {
         if (e.o2_ln_g) {
           float mean = 0.f;
@@ -359,9 +374,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j >= 4) ok = mbar_wait_warp(&slot_free[j & 3], ((j - 4) >> 2) & 1, status, kStatusTimeoutEmpty);
       if (!ok) break;
       build(j);
-      if (warp < 4 && j >= 3) ok = epilogue(j - 3);
+      // even rows' epilogues on warps 0-3, odd rows' on warps 4-7 (same TMEM lane
+      // quarters), so both halves of the builders carry the same load
+      if (j >= 3 && ((j - 3) & 1) == (warp >> 2)) ok = epilogue(j - 3);
     }
-    if (ok && warp < 4 && R >= 1) epilogue(R - 1);
+    if (ok && R >= 1 && ((R - 1) & 1) == (warp >> 2)) epilogue(R - 1);
   }
   tc_fence_before();
   __syncthreads();
