@@ -1,0 +1,313 @@
+// 3x3 NHWC convolution (stride 1, zero padding 1) with 128 output channels and one
+// input tile read per channel chunk. Replaces the implicit-GEMM conv for the DPT
+// head's output_conv1 (src/dpt_head.cpp:199-203; ggml_conv_2d of the features map,
+// 256 -> 128 channels at 8 x the patch grid).
+//
+// The implicit GEMM fetches the input once per tap (nine times per pixel). Here a CTA
+// owns a 16 x 16 output-pixel tile as two 8-wide halves, one TMEM accumulator
+// (M = 128 pixels, N = 128 channels) each. Per 64-channel chunk one TMA box of the
+// 18 x 18 input pixels around the tile lands in shared memory channel-chunk-major
+// ([chunk][y][x][8 halves], the K-major no-swizzle operand layout with a 16-byte
+// core-matrix row per pixel), and each of the nine taps is the same box read with a
+// descriptor whose start is shifted by (dy * 18 + dx) pixels: rows of one 8-pixel
+// output row are 16 bytes apart, output rows 18 pixels (288 bytes) apart. Each
+// 128 x 64 weight tile (SW128, TMA) feeds both accumulators.
+//   warp 0     TMA: per tile and chunk, the input box, then the nine weight tiles
+//   warp 1     one thread issues 2 halves x 9 taps x 4 K-steps of M = 128, N = 128,
+//              K = 16 per chunk into one of two double-buffered accumulator pairs
+//   warps 2-5  epilogue: TMEM -> + bias (+ res1 + res2, relu copy, activation) ->
+//              f16 NHWC; the accumulator pair is released after it is read
+// Persistent: grid = number of SMs, tiles assigned round-robin. Every wait is bounded
+// (ptx.cuh); on a timeout the kernel records a status, drains its MMAs and exits.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "gemm.h"
+#include "ops.h"
+#include "ptx.cuh"
+
+namespace da3b {
+namespace {
+
+constexpr int kOCh = 128;                 // output channels (MMA N)
+constexpr int kTw = 16, kTh = 16;         // output tile: two 8-wide halves
+constexpr int kBoxW = kTw + 2, kBoxH = kTh + 2;
+constexpr int kBoxPx = kBoxW * kBoxH;     // 324
+constexpr uint32_t kABytes = kBoxPx * 128;          // 64 channels x 324 pixels x 2 B = 41 472
+constexpr uint32_t kBBytes = kOCh * 128;            // 128 rows x 64 channels x 2 B = 16 384
+constexpr int kAStages = 2, kBStages = 6;
+constexpr uint32_t kLbo = kBoxPx * 16;    // channel-chunk plane stride
+constexpr uint32_t kSbo = kBoxW * 16;     // next output row (8-row group)
+constexpr int kThreads = 192;
+constexpr uint32_t kSmem = 1024 + kBStages * kBBytes + kAStages * kABytes + 256;
+
+__device__ __forceinline__ uint64_t desc_noswz(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100; swizzle field 0 = none
+  return d;
+}
+
+__device__ __forceinline__ void ld_h8(const __half* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 f = __half22float2(h[k]);
+    v[2 * k] = f.x;
+    v[2 * k + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ void st_h8(__half* p, const float (&v)[8]) {
+  uint4 u;
+  __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) h[k] = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_conv3_halo(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int B, int H, int W,
+                 int nck, int icp, const EpiArgs e, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sB = smem;                              // [kBStages][128][64] SW128
+  uint8_t* sA = sB + kBStages * kBBytes;           // [kAStages][8][18][18][8]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sA + kAStages * kABytes);
+  uint64_t* a_full = bars;                         // [2]
+  uint64_t* a_empty = bars + 2;                    // [2]
+  uint64_t* b_full = bars + 4;                     // [kBStages]
+  uint64_t* b_empty = b_full + kBStages;           // [kBStages]
+  uint64_t* acc_full = b_empty + kBStages;         // [2]
+  uint64_t* acc_empty = acc_full + 2;              // [2] (4 epilogue warps)
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_x = (W + kTw - 1) / kTw, tiles_y = (H + kTh - 1) / kTh;
+  const int n_tiles = B * tiles_x * tiles_y;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(&a_full[s], 1);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int s = 0; s < kBStages; ++s) {
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ TMA
+      uint32_t ia = 0, ib = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+        const int tx = t % tiles_x, ty = (t / tiles_x) % tiles_y, b = t / (tiles_x * tiles_y);
+        for (int c = 0; c < nck && ok; ++c) {
+          const uint32_t sa = ia % kAStages;
+          if (!mbar_wait(&a_empty[sa], ((ia / kAStages) & 1) ^ 1u, status, kStatusTimeoutEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&a_full[sa], kABytes);
+          tma_load_5d(sA + sa * kABytes, &tmA, &a_full[sa], 0, tx * kTw - 1, ty * kTh - 1, c * 8, b);
+          ++ia;
+          for (int tap = 0; tap < 9; ++tap) {
+            const uint32_t sb = ib % kBStages;
+            if (!mbar_wait(&b_empty[sb], ((ib / kBStages) & 1) ^ 1u, status, kStatusTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&b_full[sb], kBBytes);
+            tma_load_2d(sB + sb * kBBytes, &tmB, &b_full[sb], tap * icp + c * 64, 0);
+            ++ib;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ MMA
+      constexpr uint32_t idesc = umma_idesc_f16(128, kOCh);
+      const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+      uint32_t ia = 0, ib = 0, tc = 0;
+      bool ok = true;
+      int issued = 0;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++tc) {
+        const uint32_t ab = tc & 1;
+        if (tc >= 2 && !mbar_wait(&acc_empty[ab], ((tc >> 1) - 1) & 1, status, kStatusTimeoutAccumFree)) break;
+        tc_fence_after();
+        const uint32_t tAcc = tmem + ab * 256;
+        for (int c = 0; c < nck && ok; ++c) {
+          const uint32_t sa = ia % kAStages;
+          if (!mbar_wait(&a_full[sa], (ia / kAStages) & 1, status, kStatusTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t abox = a0 + sa * kABytes;
+          for (int tap = 0; tap < 9; ++tap) {
+            const uint32_t sb = ib % kBStages;
+            if (!mbar_wait(&b_full[sb], (ib / kBStages) & 1, status, kStatusTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const int dy = tap / 3, dx = tap - 3 * dy;
+            const uint64_t bd = umma_desc_sw128(b0 + sb * kBBytes);
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              const uint32_t start = abox + static_cast<uint32_t>((dy * kBoxW + 8 * half + dx) * 16);
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                umma_f16(tAcc + half * 128, desc_noswz(start + 2 * k * kLbo, kLbo, kSbo), bd + 2 * k, idesc,
+                         (c | tap | k) ? 1u : 0u);
+            }
+            umma_commit(&b_empty[sb]);
+            ++ib;
+            ++issued;
+          }
+          umma_commit(&a_empty[sa]);
+          ++ia;
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[ab]);
+      }
+      // every issued MMA has landed before TMEM is freed (also on a timeout)
+      if (issued > 0) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, status, kStatusTimeoutAccum);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;                 // TMEM lane quarter of this warp
+    const int m = q * 32 + lane;            // accumulator row: output pixel (m / 8, m % 8)
+    const int i = m >> 3, j = m & 7;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    uint32_t tc = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tc) {
+      const uint32_t ab = tc & 1;
+      if (!mbar_wait_warp(&acc_full[ab], (tc >> 1) & 1, status, kStatusTimeoutAccum)) break;
+      tc_fence_after();
+      const int tx = t % tiles_x, ty = (t / tiles_x) % tiles_y, b = t / (tiles_x * tiles_y);
+      const int y = ty * kTh + i;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        const int x = tx * kTw + 8 * half + j;
+        const bool valid = y < H && x < W;
+        const size_t pix = (static_cast<size_t>(b) * H + (valid ? y : 0)) * W + (valid ? x : 0);
+#pragma unroll 1
+        for (int cc = 0; cc < kOCh / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tmem + ab * 256 + half * 128 + cc * 32 + lane_off, r);
+          tmem_wait_ld();
+          if (valid) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const int n = cc * 32 + g * 8;
+              float v[8];
+#pragma unroll
+              for (int k = 0; k < 8; ++k) v[k] = __uint_as_float(r[g * 8 + k]);
+              if (e.bias) {
+                const float4 b0 = *reinterpret_cast<const float4*>(e.bias + n);
+                const float4 b1 = *reinterpret_cast<const float4*>(e.bias + n + 4);
+                v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+                v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+              }
+              if (e.res1) {
+                float s[8];
+                ld_h8(e.res1 + pix * e.ld_res1 + n, s);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] += s[k];
+              }
+              if (e.res2) {
+                float s[8];
+                ld_h8(e.res2 + pix * e.ld_res2 + n, s);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] += s[k];
+              }
+              if (e.out_relu) {
+                float rl[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) rl[k] = fmaxf(v[k], 0.0f);
+                st_h8(e.out_relu + pix * e.ld_out + n, rl);
+              }
+              if (e.act == kActRelu) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = fmaxf(v[k], 0.0f);
+              }
+              st_h8(e.out + pix * e.ld_out + n, v);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+// Returns 1 (nothing launched) when the shape or epilogue is not one this kernel
+// covers, so the caller can take the implicit-GEMM path; 0 on launch; < 0 on error.
+int conv3_halo(const __half* X, int B, int H, int W, int IC, const __half* Wp, int OC, const EpiArgs& e, int* status,
+               cudaStream_t s) {
+  if (OC != kOCh || IC % 64 || IC <= 0 || B <= 0 || H <= 0 || W <= 0) return 1;
+  if (e.kind != kEpiF16 || e.q8 || e.rm_div || (e.res1 && e.res1_mod) || e.ld_out != OC ||
+      (e.act != kActNone && e.act != kActRelu))
+    return 1;
+  if ((e.res1 && e.ld_res1 % 8) || (e.res2 && e.ld_res2 % 8)) return 1;
+  if ((reinterpret_cast<uintptr_t>(X) & 15) || (reinterpret_cast<uintptr_t>(e.out) & 15) ||
+      (e.out_relu && (reinterpret_cast<uintptr_t>(e.out_relu) & 15)) ||
+      (e.bias && (reinterpret_cast<uintptr_t>(e.bias) & 15)) || (e.res1 && (reinterpret_cast<uintptr_t>(e.res1) & 15)) ||
+      (e.res2 && (reinterpret_cast<uintptr_t>(e.res2) & 15)))
+    return 1;
+  const int icp = conv_icp(IC);
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_tmap_nhwc_planes(&ta, X, B, H, W, IC, kBoxW, kBoxH))) return rc - 100;
+  if ((rc = make_tmap_2d(&tb, Wp, OC, 9 * icp, 9 * icp, kOCh))) return rc - 200;
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!((attr_set >> (dev & 63)) & 1)) {
+    if (cudaFuncSetAttribute(k_conv3_halo, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+      return -3;
+    attr_set |= uint64_t(1) << (dev & 63);
+  }
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long n_tiles = static_cast<long>(B) * ((W + kTw - 1) / kTw) * ((H + kTh - 1) / kTh);
+  if (n_tiles > 0x7fffffffL) return 1;
+  const int grid = static_cast<int>(n_tiles < sms ? n_tiles : sms);
+  k_conv3_halo<<<grid, kThreads, kSmem, s>>>(ta, tb, B, H, W, IC / 64, icp, e, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+}  // namespace da3b

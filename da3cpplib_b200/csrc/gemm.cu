@@ -997,6 +997,27 @@ int make_tmap_nhwc(CUtensorMap* map, const void* ptr, int B, int H, int W, int C
   return r == CUDA_SUCCESS ? 0 : -3;
 }
 
+// 5-D f16 tensor map over an NHWC tensor [B][H][W][C] (C % 64 == 0) whose box lands
+// channel-chunk-major: dims (8 channels, W, H, C/8 chunks, B), box = 8 channels x bw x
+// bh x 8 chunks x 1, no swizzle, zero fill out of range. In shared memory a box is
+// [chunk][y][x][8 halves]: the K-major no-swizzle MMA operand layout with one 16-byte
+// core-matrix row per pixel, so a shifted pixel window is a shifted descriptor start.
+int make_tmap_nhwc_planes(CUtensorMap* map, const void* ptr, int B, int H, int W, int C, int bw, int bh) {
+  PFN_tmapEncodeTiled enc = tmap_encoder();
+  if (!enc) return -1;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || C % 64 || bw < 1 || bw > 256 || bh < 1 || bh > 256) return -2;
+  cuuint64_t dims[5] = {8, static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(C / 8),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[4] = {static_cast<cuuint64_t>(C) * 2, static_cast<cuuint64_t>(C) * 2 * W, 16,
+                           static_cast<cuuint64_t>(C) * 2 * W * H};
+  cuuint32_t box[5] = {8, static_cast<cuuint32_t>(bw), static_cast<cuuint32_t>(bh), 8, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -3;
+}
+
 static int g_num_sms = 0;
 static int num_sms() {
   if (g_num_sms == 0) {
@@ -1247,6 +1268,15 @@ int conv_nhwc(const __half* X, int B, int H, int W, int IC, const __half* Wp, in
   if (e.kind == kEpiOut2) bn = 32;
   int rc = check_epi(e, OC);
   if (rc) return rc;
+  if (ksize == 3) {
+    // 128 output channels: the halo-box kernel reads each input pixel once per chunk
+    // instead of once per tap ($DA3B_CONV_HALO=0 keeps the implicit GEMM)
+    const char* ev = getenv("DA3B_CONV_HALO");
+    if (!(ev && ev[0] == '0')) {
+      rc = conv3_halo(X, B, H, W, IC, Wp, OC, e, status, stream);
+      if (rc != 1) return rc;
+    }
+  }
   int bw = 16, bh = 8;
   pick_block(H, W, &bw, &bh);
   const int icp = conv_icp(IC);

@@ -12,6 +12,7 @@ namespace da3b {
 // ------------------------------------------------------------------ GEMM engine (gemm.cu)
 int make_tmap_2d(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows);
 int make_tmap_nhwc(CUtensorMap* map, const void* ptr, int B, int H, int W, int C, int bw, int bh);
+int make_tmap_nhwc_planes(CUtensorMap* map, const void* ptr, int B, int H, int W, int C, int bw, int bh);
 int gemm_launch(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeom& g, const EpiArgs& e,
                 int* status, cudaStream_t stream, int max_ctas);
 
@@ -27,6 +28,11 @@ int pick_bn(int N);
 // Fused align-corners upsample (+ UV pos-embed) -> 3x3 conv to 32 channels -> the
 // kEpiOut2 epilogue (head_fused.cu): src NHWC [B][hs][ws][C] f16, output grid H x W,
 // packed 3x3 weights [32][9][icp] (conv_nhwc layout), e.o2_* as for conv_nhwc.
+// 3x3 conv with 128 output channels and IC % 64 == 0 (one input box per channel chunk,
+// the nine taps as shifted descriptors); returns 1 without launching for other shapes
+// or epilogues.
+int conv3_halo(const __half* X, int B, int H, int W, int IC, const __half* Wp, int OC, const EpiArgs& e, int* status,
+               cudaStream_t s);
 int up_out2(const __half* src, int B, int hs, int ws, int C, const __half* pe, int H, int W, const __half* wp,
             int icp, const EpiArgs& e, int* status, cudaStream_t s);
 inline int conv_icp(int IC) { return (IC + 63) / 64 * 64; }

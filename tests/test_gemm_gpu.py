@@ -122,6 +122,49 @@ def test_conv_nhwc(lib, B, H, W, IC, OC, ks):
     close(outr, ref.clamp_min(0))
 
 
+def _conv3(lib, x, wp, OC, b, r1, r2, out, outr, act=0):
+    B, H, W, IC = x.shape
+    rc = lib.da3b_conv_nhwc(ptr(x), B, H, W, IC, ptr(wp), OC, 3, ptr(b), ptr(r1), ptr(r2), act, ptr(out), ptr(outr),
+                            stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert lib.da3b_device_status() == 0
+
+
+@pytest.mark.parametrize("B,H,W,IC", [(2, 37, 37, 256), (1, 5, 9, 64), (3, 17, 33, 128), (1, 16, 16, 64),
+                                      (2, 74, 74, 256)])
+def test_conv3_halo(lib, B, H, W, IC, monkeypatch):
+    """3x3 convs with 128 output channels take the halo-box kernel (one input box per
+    64-channel chunk, the nine taps as shifted no-swizzle descriptors): torch fp32
+    reference and the implicit-GEMM path ($DA3B_CONV_HALO=0) on the same inputs, with
+    bias, both residual addends, the relu copy, ragged tile edges and 1-5 chunks."""
+    OC = 128
+    g = torch.Generator(device="cuda").manual_seed(B * 7 + H + W + IC)
+    x = torch.randn(B, H, W, IC, device="cuda", generator=g).half()
+    w = torch.randn(OC, IC, 3, 3, device="cuda", generator=g).float() * 0.05
+    b = torch.randn(OC, device="cuda", generator=g).float()
+    r1 = torch.randn(B, H, W, OC, device="cuda", generator=g).half()
+    r2 = torch.randn(B, H, W, OC, device="cuda", generator=g).half()
+    wp = torch.empty(OC, 9, IC, dtype=torch.float16, device="cuda")
+    assert lib.da3b_pack_conv_weight(ptr(w), OC, IC, 3, ptr(wp), stream()) == 0
+    out, outr = (torch.full((B, H, W, OC), 7.0, dtype=torch.float16, device="cuda") for _ in range(2))
+    _conv3(lib, x, wp, OC, b, r1, r2, out, outr)
+    ref = torch.nn.functional.conv2d(x.permute(0, 3, 1, 2).float(), w.half().float(), b, padding=1)
+    ref = ref.permute(0, 2, 3, 1) + r1.float() + r2.float()
+    close(out, ref)
+    close(outr, ref.clamp_min(0))
+    monkeypatch.setenv("DA3B_CONV_HALO", "0")
+    gout, goutr = torch.empty_like(out), torch.empty_like(out)
+    _conv3(lib, x, wp, OC, b, r1, r2, gout, goutr)
+    close(out, gout.float(), rel=1e-3, abs_=1e-3)
+    # plain form (bias only, relu activation) as output_conv1 / layer convs use it
+    monkeypatch.delenv("DA3B_CONV_HALO")
+    out2 = torch.empty_like(out)
+    _conv3(lib, x, wp, OC, b, None, None, out2, None, act=1)
+    ref2 = torch.nn.functional.conv2d(x.permute(0, 3, 1, 2).float(), w.half().float(), b, padding=1)
+    close(out2, ref2.permute(0, 2, 3, 1).clamp_min(0))
+
+
 @pytest.mark.parametrize("nseq,seqlen,heads", [(1, 1, 1), (2, 37, 2), (3, 1370, 6), (1, 1297 * 3, 4), (2, 200, 16)])
 def test_attention(lib, nseq, seqlen, heads):
     g = torch.Generator(device="cuda").manual_seed(seqlen + heads)
