@@ -1,5 +1,5 @@
-// 3x3 NHWC convolution (stride 1, zero padding 1) with 128 output channels and one
-// input tile read per channel chunk. Replaces the implicit-GEMM conv for the DPT
+// 3x3 NHWC convolution (stride 1, zero padding 1), output channels in groups of 128,
+// with one input tile read per channel chunk. Replaces the implicit-GEMM conv for the DPT
 // head's output_conv1 (src/dpt_head.cpp:199-203; ggml_conv_2d of the features map,
 // 256 -> 128 channels at 8 x the patch grid).
 //
@@ -12,11 +12,14 @@
 // descriptor whose start is shifted by (dy * 18 + dx) pixels: rows of one 8-pixel
 // output row are 16 bytes apart, output rows 18 pixels (288 bytes) apart. Each
 // 128 x 64 weight tile (SW128, TMA) feeds both accumulators.
-//   warp 0     TMA: per tile and chunk, the input box, then the nine weight tiles
+//   warp 0     TMA: per chunk, the nine weight tiles, after the next chunk's input
+//              box (three box stages)
 //   warp 1     one thread issues 2 halves x 9 taps x 4 K-steps of M = 128, N = 128,
 //              K = 16 per chunk into one of two double-buffered accumulator pairs
 //   warps 2-5  epilogue: TMEM -> + bias (+ res1 + res2, relu copy, activation) ->
 //              f16 NHWC; the accumulator pair is released after it is read
+// A tile is (128-channel output group, 16 x 16 pixels), the group index fastest so the
+// groups of one pixel tile run side by side and share its input boxes in L2.
 // Persistent: grid = number of SMs, tiles assigned round-robin. Every wait is bounded
 // (ptx.cuh); on a timeout the kernel records a status, drains its MMAs and exits.
 #include <cuda.h>
@@ -38,7 +41,7 @@ constexpr int kBoxW = kTw + 2, kBoxH = kTh + 2;
 constexpr int kBoxPx = kBoxW * kBoxH;     // 324
 constexpr uint32_t kABytes = kBoxPx * 128;          // 64 channels x 324 pixels x 2 B = 41 472
 constexpr uint32_t kBBytes = kOCh * 128;            // 128 rows x 64 channels x 2 B = 16 384
-constexpr int kAStages = 2, kBStages = 6;
+constexpr int kAStages = 3, kBStages = 6;
 constexpr uint32_t kLbo = kBoxPx * 16;    // channel-chunk plane stride
 constexpr uint32_t kSbo = kBoxW * 16;     // next output row (8-row group)
 constexpr int kThreads = 192;
@@ -74,15 +77,15 @@ __device__ __forceinline__ void st_h8(__half* p, const float (&v)[8]) {
 
 __global__ void __launch_bounds__(kThreads, 1)
     k_conv3_halo(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int B, int H, int W,
-                 int nck, int icp, const EpiArgs e, int* status) {
+                 int nck, int icp, int n_oc, const EpiArgs e, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sB = smem;                              // [kBStages][128][64] SW128
   uint8_t* sA = sB + kBStages * kBBytes;           // [kAStages][8][18][18][8]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sA + kAStages * kABytes);
-  uint64_t* a_full = bars;                         // [2]
-  uint64_t* a_empty = bars + 2;                    // [2]
-  uint64_t* b_full = bars + 4;                     // [kBStages]
+  uint64_t* a_full = bars;                         // [kAStages]
+  uint64_t* a_empty = bars + kAStages;             // [kAStages]
+  uint64_t* b_full = a_empty + kAStages;           // [kBStages]
   uint64_t* b_empty = b_full + kBStages;           // [kBStages]
   uint64_t* acc_full = b_empty + kBStages;         // [2]
   uint64_t* acc_empty = acc_full + 2;              // [2] (4 epilogue warps)
@@ -91,7 +94,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_x = (W + kTw - 1) / kTw, tiles_y = (H + kTh - 1) / kTh;
-  const int n_tiles = B * tiles_x * tiles_y;
+  const int n_tiles = B * tiles_x * tiles_y * n_oc;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kAStages; ++s) {
@@ -120,26 +123,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------------ TMA
-      uint32_t ia = 0, ib = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
-        const int tx = t % tiles_x, ty = (t / tiles_x) % tiles_y, b = t / (tiles_x * tiles_y);
-        for (int c = 0; c < nck && ok; ++c) {
-          const uint32_t sa = ia % kAStages;
-          if (!mbar_wait(&a_empty[sa], ((ia / kAStages) & 1) ^ 1u, status, kStatusTimeoutEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&a_full[sa], kABytes);
-          tma_load_5d(sA + sa * kABytes, &tmA, &a_full[sa], 0, tx * kTw - 1, ty * kTh - 1, c * 8, b);
-          ++ia;
-          for (int tap = 0; tap < 9; ++tap) {
-            const uint32_t sb = ib % kBStages;
-            if (!mbar_wait(&b_empty[sb], ((ib / kBStages) & 1) ^ 1u, status, kStatusTimeoutEmpty)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(&b_full[sb], kBBytes);
-            tma_load_2d(sB + sb * kBBytes, &tmB, &b_full[sb], tap * icp + c * 64, 0);
-            ++ib;
+      // chunks g = tile-step * nck + c in order; the input box of chunk g + 1 is
+      // requested before the nine weight tiles of chunk g, a chunk ahead of its use
+      const int my_tiles = blockIdx.x < n_tiles ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+      const int n_chunks = my_tiles * nck;
+      auto load_box = [&](int g) -> bool {
+        const int t = blockIdx.x + (g / nck) * gridDim.x, c = g % nck;
+        const int tp = t / n_oc;
+        const int tx = tp % tiles_x, ty = (tp / tiles_x) % tiles_y, b = tp / (tiles_x * tiles_y);
+        const uint32_t sa = static_cast<uint32_t>(g) % kAStages;
+        if (!mbar_wait(&a_empty[sa], ((static_cast<uint32_t>(g) / kAStages) & 1) ^ 1u, status, kStatusTimeoutEmpty))
+          return false;
+        mbar_arrive_expect_tx(&a_full[sa], kABytes);
+        tma_load_5d(sA + sa * kABytes, &tmA, &a_full[sa], 0, tx * kTw - 1, ty * kTh - 1, c * 8, b);
+        return true;
+      };
+      uint32_t ib = 0;
+      bool ok = n_chunks == 0 || load_box(0);
+      for (int g = 0; g < n_chunks && ok; ++g) {
+        if (g + 1 < n_chunks && !load_box(g + 1)) break;
+        const int og = (blockIdx.x + (g / nck) * gridDim.x) % n_oc, c = g % nck;
+        for (int tap = 0; tap < 9; ++tap) {
+          const uint32_t sb = ib % kBStages;
+          if (!mbar_wait(&b_empty[sb], ((ib / kBStages) & 1) ^ 1u, status, kStatusTimeoutEmpty)) {
+            ok = false;
+            break;
           }
+          mbar_arrive_expect_tx(&b_full[sb], kBBytes);
+          tma_load_2d(sB + sb * kBBytes, &tmB, &b_full[sb], tap * icp + c * 64, og * kOCh);
+          ++ib;
         }
       }
     }
@@ -207,7 +219,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ab = tc & 1;
       if (!mbar_wait_warp(&acc_full[ab], (tc >> 1) & 1, status, kStatusTimeoutAccum)) break;
       tc_fence_after();
-      const int tx = t % tiles_x, ty = (t / tiles_x) % tiles_y, b = t / (tiles_x * tiles_y);
+      const int og = t % n_oc, tp = t / n_oc;
+      const int tx = tp % tiles_x, ty = (tp / tiles_x) % tiles_y, b = tp / (tiles_x * tiles_y);
       const int y = ty * kTh + i;
 #pragma unroll 1
       for (int half = 0; half < 2; ++half) {
@@ -222,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (valid) {
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
-              const int n = cc * 32 + g * 8;
+              const int n = og * kOCh + cc * 32 + g * 8;
               float v[8];
 #pragma unroll
               for (int k = 0; k < 8; ++k) v[k] = __uint_as_float(r[g * 8 + k]);
@@ -278,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // covers, so the caller can take the implicit-GEMM path; 0 on launch; < 0 on error.
 int conv3_halo(const __half* X, int B, int H, int W, int IC, const __half* Wp, int OC, const EpiArgs& e, int* status,
                cudaStream_t s) {
-  if (OC != kOCh || IC % 64 || IC <= 0 || B <= 0 || H <= 0 || W <= 0) return 1;
+  if (OC % kOCh || OC <= 0 || IC % 64 || IC <= 0 || B <= 0 || H <= 0 || W <= 0) return 1;
   if (e.kind != kEpiF16 || e.q8 || e.rm_div || (e.res1 && e.res1_mod) || e.ld_out != OC ||
       (e.act != kActNone && e.act != kActRelu))
     return 1;
@@ -303,10 +316,10 @@ int conv3_halo(const __half* X, int B, int H, int W, int IC, const __half* Wp, i
   }
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const long n_tiles = static_cast<long>(B) * ((W + kTw - 1) / kTw) * ((H + kTh - 1) / kTh);
+  const long n_tiles = static_cast<long>(B) * ((W + kTw - 1) / kTw) * ((H + kTh - 1) / kTh) * (OC / kOCh);
   if (n_tiles > 0x7fffffffL) return 1;
   const int grid = static_cast<int>(n_tiles < sms ? n_tiles : sms);
-  k_conv3_halo<<<grid, kThreads, kSmem, s>>>(ta, tb, B, H, W, IC / 64, icp, e, status);
+  k_conv3_halo<<<grid, kThreads, kSmem, s>>>(ta, tb, B, H, W, IC / 64, icp, OC / kOCh, e, status);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 

@@ -131,14 +131,16 @@ def _conv3(lib, x, wp, OC, b, r1, r2, out, outr, act=0):
     assert lib.da3b_device_status() == 0
 
 
-@pytest.mark.parametrize("B,H,W,IC", [(2, 37, 37, 256), (1, 5, 9, 64), (3, 17, 33, 128), (1, 16, 16, 64),
-                                      (2, 74, 74, 256)])
-def test_conv3_halo(lib, B, H, W, IC, monkeypatch):
-    """3x3 convs with 128 output channels take the halo-box kernel (one input box per
-    64-channel chunk, the nine taps as shifted no-swizzle descriptors): torch fp32
-    reference and the implicit-GEMM path ($DA3B_CONV_HALO=0) on the same inputs, with
-    bias, both residual addends, the relu copy, ragged tile edges and 1-5 chunks."""
-    OC = 128
+@pytest.mark.parametrize("B,H,W,IC,OC", [(2, 37, 37, 256, 128), (1, 5, 9, 64, 128), (3, 17, 33, 128, 128),
+                                         (1, 16, 16, 64, 128), (2, 74, 74, 256, 128), (1, 37, 37, 256, 256),
+                                         (2, 19, 21, 512, 256)])
+def test_conv3_halo(lib, B, H, W, IC, OC, monkeypatch):
+    """3x3 convs through the halo-box kernel ($DA3B_CONV_HALO=1; by default it serves 128
+    output channels): one input box per 64-channel chunk, the nine taps as shifted
+    no-swizzle descriptors, output channels in groups of 128. Checked against the
+    torch fp32 reference and the implicit-GEMM path ($DA3B_CONV_HALO=0) on the same
+    inputs, with bias, both residual addends, the relu copy, ragged tile edges, 1-8
+    chunks and one or two output groups."""
     g = torch.Generator(device="cuda").manual_seed(B * 7 + H + W + IC)
     x = torch.randn(B, H, W, IC, device="cuda", generator=g).half()
     w = torch.randn(OC, IC, 3, 3, device="cuda", generator=g).float() * 0.05
@@ -148,6 +150,7 @@ def test_conv3_halo(lib, B, H, W, IC, monkeypatch):
     wp = torch.empty(OC, 9, IC, dtype=torch.float16, device="cuda")
     assert lib.da3b_pack_conv_weight(ptr(w), OC, IC, 3, ptr(wp), stream()) == 0
     out, outr = (torch.full((B, H, W, OC), 7.0, dtype=torch.float16, device="cuda") for _ in range(2))
+    monkeypatch.setenv("DA3B_CONV_HALO", "1")  # also for 256 outputs, which default to the GEMM
     _conv3(lib, x, wp, OC, b, r1, r2, out, outr)
     ref = torch.nn.functional.conv2d(x.permute(0, 3, 1, 2).float(), w.half().float(), b, padding=1)
     ref = ref.permute(0, 2, 3, 1) + r1.float() + r2.float()
@@ -158,7 +161,7 @@ def test_conv3_halo(lib, B, H, W, IC, monkeypatch):
     _conv3(lib, x, wp, OC, b, r1, r2, gout, goutr)
     close(out, gout.float(), rel=1e-3, abs_=1e-3)
     # plain form (bias only, relu activation) as output_conv1 / layer convs use it
-    monkeypatch.delenv("DA3B_CONV_HALO")
+    monkeypatch.setenv("DA3B_CONV_HALO", "1")
     out2 = torch.empty_like(out)
     _conv3(lib, x, wp, OC, b, None, None, out2, None, act=1)
     ref2 = torch.nn.functional.conv2d(x.permute(0, 3, 1, 2).float(), w.half().float(), b, padding=1)
