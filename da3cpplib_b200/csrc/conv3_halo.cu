@@ -20,12 +20,14 @@
 //              f16 NHWC; the accumulator pair is released after it is read
 // A tile is (128-channel output group, 16 x 16 pixels), the group index fastest so the
 // groups of one pixel tile run side by side and share its input boxes in L2.
+// A CTA-pair form (k_conv3_halo2, below) serves output counts in groups of 256.
 // Persistent: grid = number of SMs, tiles assigned round-robin. Every wait is bounded
 // (ptx.cuh); on a timeout the kernel records a status, drains its MMAs and exits.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "gemm.h"
@@ -285,6 +287,291 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- CTA-pair form
+// The same scheme over a cluster of two CTAs (cta_group::2). Each CTA owns its own
+// 16-row pixel tile of kHalves 8-wide halves and loads its own input box, plus half of
+// the N weight rows of every tap; the leader's single thread issues M = 256 MMAs
+// whose rows 0-127 come from the leader's box and 128-255 from the peer's, leaving
+// each CTA's accumulators in its own TMEM. Per CTA this halves the weight bytes
+// written to and read from shared memory, which the 1-CTA form spends as much
+// shared-memory bandwidth on as the MMA itself. All loads complete on the leader's
+// barriers; MMA completions are multicast to both CTAs (tcgen05.commit), the peer's
+// epilogue releases an accumulator with a remote arrive on the leader's barrier.
+template <int N, int kHalves>
+struct Halo2Cfg {
+  static constexpr int kTw = 8 * kHalves, kTh = 16;
+  static constexpr int kBoxW = kTw + 2, kBoxH = kTh + 2, kBoxPx = kBoxW * kBoxH;
+  static constexpr uint32_t kABytes = kBoxPx * 128;
+  static constexpr uint32_t kBBytes = (N / 2) * 128;      // this CTA's N/2 weight rows x 64 channels
+  static constexpr int kAStages = 3, kBStages = 6;
+  static constexpr uint32_t kLbo = kBoxPx * 16, kSbo = kBoxW * 16;
+  static constexpr uint32_t kAccCols = kHalves * N;      // per accumulator buffer
+  static constexpr uint32_t kSmem = 1024 + kBStages * kBBytes + kAStages * kABytes + 256;
+  static_assert(2 * kAccCols <= 512, "two accumulator buffers must fit in TMEM");
+};
+
+template <int N, int kHalves>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_conv3_halo2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int B, int H,
+                  int W, int nck, int icp, int n_oc, const EpiArgs e, int* status) {
+  using Cfg = Halo2Cfg<N, kHalves>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sB = smem;
+  uint8_t* sA = sB + Cfg::kBStages * Cfg::kBBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sA + Cfg::kAStages * Cfg::kABytes);
+  uint64_t* a_full = bars;                            // [kAStages] (leader's used)
+  uint64_t* a_empty = a_full + Cfg::kAStages;         // [kAStages]
+  uint64_t* b_full = a_empty + Cfg::kAStages;         // [kBStages] (leader's used)
+  uint64_t* b_empty = b_full + Cfg::kBStages;         // [kBStages]
+  uint64_t* acc_full = b_empty + Cfg::kBStages;       // [2]
+  uint64_t* acc_empty = acc_full + 2;                 // [2] (leader's: 2 x 4 epilogue warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int tiles_x = (W + Cfg::kTw - 1) / Cfg::kTw, tiles_y = (H + Cfg::kTh - 1) / Cfg::kTh;
+  const int n_px = B * tiles_x * tiles_y;             // pixel tiles; a pair takes two
+  const int n_tiles = ((n_px + 1) / 2) * n_oc;        // pair tiles, output group fastest
+  const int my_tiles = pair < n_tiles ? (n_tiles - 1 - pair) / npairs + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kAStages; ++s) {
+      mbar_init(&a_full[s], 1);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int s = 0; s < Cfg::kBStages; ++s) {
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * 4);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) tmem_alloc2(tmem_slot, 512);
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // this CTA's pixel tile of pair tile t: (b, ty, tx); b == B past the last tile
+  auto px_tile = [&](int t, int& b, int& ty, int& tx) {
+    const int p = 2 * (t / n_oc) + static_cast<int>(rank);
+    b = p / (tiles_x * tiles_y);
+    const int rem = p - b * tiles_x * tiles_y;
+    ty = rem / tiles_x;
+    tx = rem - ty * tiles_x;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- TMA (both CTAs)
+      const int n_chunks = my_tiles * nck;
+      auto load_box = [&](int g) -> bool {
+        const int t = pair + (g / nck) * npairs, c = g % nck;
+        int b, ty, tx;
+        px_tile(t, b, ty, tx);
+        const uint32_t sa = static_cast<uint32_t>(g) % Cfg::kAStages;
+        if (!mbar_wait(&a_empty[sa], ((static_cast<uint32_t>(g) / Cfg::kAStages) & 1) ^ 1u, status,
+                       kStatusTimeoutEmpty))
+          return false;
+        if (rank == 0) mbar_arrive_expect_tx(&a_full[sa], 2 * Cfg::kABytes);
+        tma2_load_5d(sA + sa * Cfg::kABytes, &tmA, mapa_shared(smem_u32(&a_full[sa]), 0), 0, tx * Cfg::kTw - 1,
+                     ty * Cfg::kTh - 1, c * 8, b);
+        return true;
+      };
+      uint32_t ib = 0;
+      bool ok = n_chunks == 0 || load_box(0);
+      for (int g = 0; g < n_chunks && ok; ++g) {
+        if (g + 1 < n_chunks && !load_box(g + 1)) break;
+        const int og = (pair + (g / nck) * npairs) % n_oc, c = g % nck;
+        for (int tap = 0; tap < 9; ++tap) {
+          const uint32_t sb = ib % Cfg::kBStages;
+          if (!mbar_wait(&b_empty[sb], ((ib / Cfg::kBStages) & 1) ^ 1u, status, kStatusTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&b_full[sb], 2 * Cfg::kBBytes);
+          tma2_load_2d(sB + sb * Cfg::kBBytes, &tmB, mapa_shared(smem_u32(&b_full[sb]), 0), tap * icp + c * 64,
+                       og * N + static_cast<int>(rank) * (N / 2));
+          ++ib;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------------------------------------------------- MMA (leader only)
+      constexpr uint32_t idesc = umma_idesc_f16(256, N);
+      const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+      uint32_t ia = 0, ib = 0;
+      bool ok = true;
+      for (int it = 0; it < my_tiles && ok; ++it) {
+        const uint32_t ab = it & 1;
+        if (!mbar_wait(&acc_empty[ab], ((it >> 1) & 1) ^ 1u, status, kStatusTimeoutAccumFree)) break;
+        tc_fence_after();
+        const uint32_t tAcc = tmem + ab * Cfg::kAccCols;
+        for (int c = 0; c < nck && ok; ++c) {
+          const uint32_t sa = ia % Cfg::kAStages;
+          if (!mbar_wait(&a_full[sa], (ia / Cfg::kAStages) & 1, status, kStatusTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t abox = a0 + sa * Cfg::kABytes;
+          for (int tap = 0; tap < 9; ++tap) {
+            const uint32_t sb = ib % Cfg::kBStages;
+            if (!mbar_wait(&b_full[sb], (ib / Cfg::kBStages) & 1, status, kStatusTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const int dy = tap / 3, dx = tap - 3 * dy;
+            const uint64_t bd = umma_desc_sw128(b0 + sb * Cfg::kBBytes);
+#pragma unroll
+            for (int half = 0; half < kHalves; ++half) {
+              const uint32_t start = abox + static_cast<uint32_t>((dy * Cfg::kBoxW + 8 * half + dx) * 16);
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                umma2_f16(tAcc + half * N, desc_noswz(start + 2 * k * Cfg::kLbo, Cfg::kLbo, Cfg::kSbo), bd + 2 * k,
+                          idesc, (c | tap | k) ? 1u : 0u);
+            }
+            umma2_commit_mc(&b_empty[sb], 0x3);
+            ++ib;
+          }
+          umma2_commit_mc(&a_empty[sa], 0x3);
+          ++ia;
+        }
+        if (ok) umma2_commit_mc(&acc_full[ab], 0x3);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------- epilogue (both CTAs)
+    const int q = warp & 3;
+    const int m = q * 32 + lane;
+    const int i = m >> 3, j = m & 7;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t acc_empty_leader[2] = {mapa_shared(smem_u32(&acc_empty[0]), 0),
+                                          mapa_shared(smem_u32(&acc_empty[1]), 0)};
+    for (int it = 0; it < my_tiles; ++it) {
+      const uint32_t ab = it & 1;
+      const int t = pair + it * npairs;
+      if (!mbar_wait_warp(&acc_full[ab], (it >> 1) & 1, status, kStatusTimeoutAccum)) break;
+      tc_fence_after();
+      int b, ty, tx;
+      px_tile(t, b, ty, tx);
+      const int og = t % n_oc;
+      const int y = ty * Cfg::kTh + i;
+#pragma unroll 1
+      for (int half = 0; half < kHalves; ++half) {
+        const int x = tx * Cfg::kTw + 8 * half + j;
+        const bool valid = b < B && y < H && x < W;
+        const size_t pix = valid ? (static_cast<size_t>(b) * H + y) * W + x : 0;
+#pragma unroll 1
+        for (int cc = 0; cc < N / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tmem + ab * Cfg::kAccCols + half * N + cc * 32 + lane_off, r);
+          tmem_wait_ld();
+          if (valid) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const int n = og * N + cc * 32 + g * 8;
+              float v[8];
+#pragma unroll
+              for (int k = 0; k < 8; ++k) v[k] = __uint_as_float(r[g * 8 + k]);
+              if (e.bias) {
+                const float4 b0 = *reinterpret_cast<const float4*>(e.bias + n);
+                const float4 b1 = *reinterpret_cast<const float4*>(e.bias + n + 4);
+                v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+                v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+              }
+              if (e.res1) {
+                float s[8];
+                ld_h8(e.res1 + pix * e.ld_res1 + n, s);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] += s[k];
+              }
+              if (e.res2) {
+                float s[8];
+                ld_h8(e.res2 + pix * e.ld_res2 + n, s);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] += s[k];
+              }
+              if (e.out_relu) {
+                float rl[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) rl[k] = fmaxf(v[k], 0.0f);
+                st_h8(e.out_relu + pix * e.ld_out + n, rl);
+              }
+              if (e.act == kActRelu) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = fmaxf(v[k], 0.0f);
+              }
+              st_h8(e.out + pix * e.ld_out + n, v);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote_relaxed(acc_empty_leader[ab]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc2(tmem, 512);
+  }
+}
+
+template <int N, int kHalves>
+int launch_halo2(const __half* X, int B, int H, int W, int IC, const __half* Wp, int OC, const EpiArgs& e,
+                 int* status, cudaStream_t s, int sms) {
+  using Cfg = Halo2Cfg<N, kHalves>;
+  const int icp = conv_icp(IC);
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_tmap_nhwc_planes(&ta, X, B, H, W, IC, Cfg::kBoxW, Cfg::kBoxH))) return rc - 100;
+  if ((rc = make_tmap_2d(&tb, Wp, OC, 9 * icp, 9 * icp, N / 2))) return rc - 200;
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!((attr_set >> (dev & 63)) & 1)) {
+    if (cudaFuncSetAttribute(k_conv3_halo2<N, kHalves>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) !=
+        cudaSuccess)
+      return -3;
+    attr_set |= uint64_t(1) << (dev & 63);
+  }
+  const long n_px = static_cast<long>(B) * ((W + Cfg::kTw - 1) / Cfg::kTw) * ((H + Cfg::kTh - 1) / Cfg::kTh);
+  const long tiles = ((n_px + 1) / 2) * (OC / N);
+  if (tiles > 0x7fffffffL) return 1;
+  int pairs = sms / 2;
+  if (tiles < pairs) pairs = static_cast<int>(tiles);
+  if (pairs <= 0) return 0;
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, k_conv3_halo2<N, kHalves>, ta, tb, B, H, W, IC / 64, icp, OC / N, e, status) !=
+      cudaSuccess)
+    return -11;
+  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+}
+
 }  // namespace
 
 // Returns 1 (nothing launched) when the shape or epilogue is not one this kernel
@@ -301,6 +588,19 @@ int conv3_halo(const __half* X, int B, int H, int W, int IC, const __half* Wp, i
       (e.bias && (reinterpret_cast<uintptr_t>(e.bias) & 15)) || (e.res1 && (reinterpret_cast<uintptr_t>(e.res1) & 15)) ||
       (e.res2 && (reinterpret_cast<uintptr_t>(e.res2) & 15)))
     return 1;
+  int dev0 = 0, sms = 0;
+  cudaGetDevice(&dev0);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev0);
+  // Form: the CTA pair for output counts in groups of 256 (one 8-wide half of N = 256
+  // per CTA; measured 6-10% faster than the 2-SM implicit GEMM on the DPT head's
+  // shapes), one CTA for 128 outputs (the pair form, two halves of N = 128 per CTA,
+  // measured 4% slower there). $DA3B_CONV_HALO_PAIR=1 / =0 force one form.
+  const char* pe = getenv("DA3B_CONV_HALO_PAIR");
+  const int pmode = pe && pe[0] == '1' ? 1 : (pe && pe[0] == '0' ? 0 : -1);
+  if (sms >= 2 && pmode != 0) {
+    if (OC % 256 == 0) return launch_halo2<256, 1>(X, B, H, W, IC, Wp, OC, e, status, s, sms);
+    if (OC == 128 && pmode == 1) return launch_halo2<128, 2>(X, B, H, W, IC, Wp, OC, e, status, s, sms);
+  }
   const int icp = conv_icp(IC);
   CUtensorMap ta, tb;
   int rc;
@@ -314,8 +614,6 @@ int conv3_halo(const __half* X, int B, int H, int W, int IC, const __half* Wp, i
       return -3;
     attr_set |= uint64_t(1) << (dev & 63);
   }
-  int sms = 0;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const long n_tiles = static_cast<long>(B) * ((W + kTw - 1) / kTw) * ((H + kTh - 1) / kTh) * (OC / kOCh);
   if (n_tiles > 0x7fffffffL) return 1;
   const int grid = static_cast<int>(n_tiles < sms ? n_tiles : sms);

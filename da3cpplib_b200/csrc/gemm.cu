@@ -1270,13 +1270,11 @@ int conv_nhwc(const __half* X, int B, int H, int W, int IC, const __half* Wp, in
   if (rc) return rc;
   if (ksize == 3) {
     // The halo-box kernel reads each input pixel once per 64-channel chunk instead of
-    // once per tap. It is taken for 128 output channels, where the implicit GEMM's
-    // per-tap re-reads bound it; at 256 outputs the 2-SM implicit GEMM is faster (its
-    // CTA pair halves the weight traffic per SM). $DA3B_CONV_HALO=0 never takes it,
-    // =1 takes it for every output count that is a multiple of 128.
+    // once per tap: 128 output channels (one CTA), or groups of 256 (CTA pairs).
+    // $DA3B_CONV_HALO=0 never takes it, =1 also for other multiples of 128.
     const char* ev = getenv("DA3B_CONV_HALO");
     const int mode = ev && ev[0] == '0' ? 0 : (ev && ev[0] == '1' ? 2 : 1);
-    if (mode == 2 || (mode == 1 && OC == 128)) {
+    if (mode == 2 || (mode == 1 && (OC == 128 || OC % 256 == 0))) {
       rc = conv3_halo(X, B, H, W, IC, Wp, OC, e, status, stream);
       if (rc != 1) return rc;
     }
