@@ -44,6 +44,13 @@ constexpr float kRescaleLog2 = 8.0f;     // rescale O only when the row max grow
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// max(a, b, c) in one instruction (sm_100 three-input max.f32)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // 2^x of two values on the FMA/ALU pipes instead of the XU (MUFU) pipe, which one
 // exponential per score otherwise saturates. Cody-Waite reduction x = j + f with
 // j = round(x) (adding 1.5*2^23 leaves j in the low mantissa bits) and f in [-0.5, 0.5];
@@ -205,14 +212,17 @@ __global__ void __launch_bounds__(192, 2)
         for (int i = 0; i < kKT; ++i)
           if (i >= kvalid) sv[i] = -INFINITY;
       }
-      // row max as a tree of 8 independent chains (not one 63-deep dependency chain)
+      // row max: 8 independent chains of three-input maxima (32 instructions for 64
+      // scores instead of 63)
       float m8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) m8[i] = sv[i];
 #pragma unroll
-      for (int i = 8; i < kKT; ++i) m8[i & 7] = fmaxf(m8[i & 7], sv[i]);
-      const float mt = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      for (int i = 8; i < kKT; i += 16) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) m8[c] = fmax3(m8[c], sv[i + c], sv[i + 8 + c]);
+      }
+      const float mt = fmaxf(fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), m8[6]), m8[7]);
       // The running max of a row is raised only when a tile's max exceeds it by more
       // than 2^8; the accumulated O (and its row-sum column) is then rescaled in TMEM
       // once P V_{j-1} has landed. The TMEM read-modify-write is warp-collective, so the

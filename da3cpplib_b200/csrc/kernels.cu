@@ -408,7 +408,7 @@ constexpr int kUpCS = 64;
 __global__ void __launch_bounds__(256) k_upsample_staged(const __half* __restrict__ in, int hs, int ws, int C,
                                                          __half* __restrict__ out, int H, int W,
                                                          const __half* __restrict__ pe) {
-  extern __shared__ uint4 srow[];  // [2][ws][kUpCS / 8]
+  extern __shared__ uint4 srow[];  // [2][ws][kUpCS / 8], then the column table
   constexpr int nch = kUpCS / 8;
   const int orow = blockIdx.x, cs0 = blockIdx.y * kUpCS;
   const int y = orow % H, b = orow / H;
@@ -422,24 +422,36 @@ __global__ void __launch_bounds__(256) k_upsample_staged(const __half* __restric
   y1 = max(0, min(y1, hs - 1));
   const __half* s0 = in + (static_cast<size_t>(b) * hs + y0) * ws * C + cs0;
   const __half* s1 = in + (static_cast<size_t>(b) * hs + y1) * ws * C + cs0;
-  for (int i = threadIdx.x; i < 2 * ws * nch; i += blockDim.x) {
-    const int r = i / (ws * nch), k = i - r * ws * nch, x = k / nch, c = k - x * nch;
-    srow[i] = *reinterpret_cast<const uint4*>((r ? s1 : s0) + static_cast<size_t>(x) * C + c * 8);
-  }
-  __syncthreads();
-  __half* dst = out + static_cast<size_t>(orow) * W * C + cs0;
-  const __half* prow = pe ? pe + static_cast<size_t>(y) * W * C + cs0 : nullptr;
-  for (int i = threadIdx.x; i < W * nch; i += blockDim.x) {
-    const int x = i / nch, c = i - x * nch;
+  // per output column: source columns (x0 | x1 << 16) and weight, computed once per
+  // block instead of once per channel chunk
+  int2* xtab = reinterpret_cast<int2*>(srow + 2 * ws * nch);
+  for (int x = threadIdx.x; x < W; x += blockDim.x) {
     const float fx = static_cast<float>(x) / sf0;
     int x0 = static_cast<int>(floorf(fx));
     int x1 = x0 + 1;
     const float dx = fminf(fmaxf(fx - floorf(fx), 0.f), 1.f);
     x0 = max(0, min(x0, ws - 1));
     x1 = max(0, min(x1, ws - 1));
-    const float wa = (1 - dx) * (1 - dy), wb = dx * (1 - dy), wc = (1 - dx) * dy, wd = dx * dy;
+    xtab[x] = make_int2(x0 | (x1 << 16), __float_as_int(dx));
+  }
+  const int row_items = ws * nch;
+  for (int k = threadIdx.x; k < row_items; k += blockDim.x) {
+    const int x = k / nch, c = k % nch;  // nch is a power of two: shifts
+    srow[k] = *reinterpret_cast<const uint4*>(s0 + static_cast<size_t>(x) * C + c * 8);
+    srow[row_items + k] = *reinterpret_cast<const uint4*>(s1 + static_cast<size_t>(x) * C + c * 8);
+  }
+  __syncthreads();
+  __half* dst = out + static_cast<size_t>(orow) * W * C + cs0;
+  const __half* prow = pe ? pe + static_cast<size_t>(y) * W * C + cs0 : nullptr;
+  const float dy1 = 1 - dy;
+  for (int i = threadIdx.x; i < W * nch; i += blockDim.x) {
+    const int x = i / nch, c = i % nch;
+    const int2 t = xtab[x];
+    const int x0 = t.x & 0xffff, x1 = t.x >> 16;
+    const float dx = __int_as_float(t.y);
+    const float wa = (1 - dx) * dy1, wb = dx * dy1, wc = (1 - dx) * dy, wd = dx * dy;
     const uint4 ua = srow[x0 * nch + c], ub = srow[x1 * nch + c];
-    const uint4 uc = srow[(ws + x0) * nch + c], ud = srow[(ws + x1) * nch + c];
+    const uint4 uc = srow[row_items + x0 * nch + c], ud = srow[row_items + x1 * nch + c];
     uint4 up = make_uint4(0, 0, 0, 0);
     if (prow) up = *reinterpret_cast<const uint4*>(prow + static_cast<size_t>(x) * C + c * 8);
     const __half2* ha = reinterpret_cast<const __half2*>(&ua);
@@ -467,8 +479,8 @@ int upsample_ac(const __half* in, int B, int hs, int ws, int C, __half* out, int
   if (C % 8) return -1;
   const long rows = static_cast<long>(B) * H;
   if (rows <= 0 || W <= 0) return 0;
-  const int staged_smem = 2 * ws * kUpCS * 2;
-  if (C % kUpCS == 0 && staged_smem <= 96 * 1024 && rows <= 0x7fffffffL) {
+  const int staged_smem = 2 * ws * kUpCS * 2 + 8 * W;  // two source rows + the column table
+  if (C % kUpCS == 0 && staged_smem <= 96 * 1024 && ws <= 0xffff && rows <= 0x7fffffffL) {
     static uint64_t attr_set = 0;
     int dev = 0;
     cudaGetDevice(&dev);
