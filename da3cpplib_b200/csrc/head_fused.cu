@@ -16,7 +16,7 @@
 // N = 96, so one wide MMA replaces three narrow ones; no warp needs another's data).
 //   warps 0-7  build row j+2 while the tensor core works on row j (bilinear from the
 //              NHWC out1 map, the f32 weights of k_upsample_ac, PE added, f16), after
-//              an L2 prefetch of the source rows two steps ahead; warps 0-3 (even
+//              a bulk L2 prefetch of the source rows three steps ahead; warps 0-3 (even
 //              rows) and 4-7 (odd rows) also run the epilogue: TMEM -> tap sum,
 //              bias, relu, 1x1 conv, activation;
 //   warp 8     one thread issues the 3 x C/16 MMAs of a row into one of two TMEM
@@ -47,6 +47,11 @@ constexpr int kN = 3 * kOC;            // MMA N: three horizontal taps x 32 chan
 constexpr int kConsts = 360;           // bias 32 | LN gamma 32 | LN beta 32 | out2b 8x32 | out2b bias 8
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Bulk prefetch of [p, p + bytes) into L2 (16-byte aligned address, bytes % 16 == 0).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 // K-major operand without swizzle: 8-row core matrices of 16-byte rows, 8-row groups
 // `sbo` apart, 16-byte channel chunks `lbo` apart.
@@ -220,19 +225,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const __half* s0 = src;
       const __half* s1 = src;
       const __half* prow = nullptr;
-      {
-        // L2 prefetch of the source rows of upsampled row u + 2 (built two steps later)
-        const int u2 = u + 2;
-        if (u2 >= 0 && u2 < H) {
-          const float f2 = static_cast<float>(u2) / sf1;
+      // L2 prefetch, by one thread with bulk (TMA-unit) prefetches of whole row
+      // segments, of the source rows (and PE row) of upsampled row u + 3, built three
+      // steps later; the first build also covers rows u .. u + 2. A per-line
+      // prefetch.global.L2 left a third of the builders' loads missing L2.
+      if (tb == 0) {
+        for (int uu = (j == 0 ? u : u + 3); uu <= u + 3; ++uu) {
+          if (uu < 0 || uu >= H) continue;
+          const float f2 = static_cast<float>(uu) / sf1;
           const int r0 = max(0, min(static_cast<int>(floorf(f2)), hs - 1));
           const int r1 = max(0, min(static_cast<int>(floorf(f2)) + 1, hs - 1));
           const int xlo = sX0[xlo_row], xhi = sX1[xhi_row];
-          const int nl = ((xhi - xlo + 1) * C * 2 + 127) / 128;
-          for (int l = tb; l < 2 * nl; l += kBuildWarps * 32) {
-            const int row = l < nl ? r0 : r1;
-            const __half* a = src + ((img + row) * ws + xlo) * C + (l < nl ? l : l - nl) * 64;
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+          const uint32_t bytes = static_cast<uint32_t>(xhi - xlo + 1) * C * 2;
+          bulk_prefetch_l2(src + ((img + r0) * ws + xlo) * C, bytes);
+          if (r1 != r0) bulk_prefetch_l2(src + ((img + r1) * ws + xlo) * C, bytes);
+          if (pe) {
+            const int plo = max(0, xs0 - 1), phi = min(W, xs0 + kTile + 2);
+            bulk_prefetch_l2(pe + (static_cast<size_t>(uu) * W + plo) * C, static_cast<uint32_t>(phi - plo) * C * 2);
           }
         }
       }
