@@ -158,22 +158,25 @@ def main(argv=None):
                 del x, o
 
     if args.part in ("up", "all"):
-        # align-corners bilinear upsample of the DPT tail: 296x296 -> 518x518, 128 channels
-        B, C = args.batch, 128
-        x = torch.randn((B, 296, 296, C), generator=gen, device="cuda").half()
-        o = torch.empty((B, 518, 518, C), dtype=torch.float16, device="cuda")
+        # align-corners bilinear upsamples: the fusion pyramid's last step (148 -> 296,
+        # 256 channels) and the DPT tail without the fused output stage (296 -> 518, 128)
+        for hs, hd, C in ((148, 296, 256), (296, 518, 128)):
+            B = args.batch
+            x = torch.randn((B, hs, hs, C), generator=gen, device="cuda").half()
+            o = torch.empty((B, hd, hd, C), dtype=torch.float16, device="cuda")
 
-        def run():
-            rc = L.da3b_upsample_nhwc(P(x), B, 296, 296, C, P(o), 518, 518, S)
-            if rc:
-                raise RuntimeError(f"da3b_upsample_nhwc rc={rc}")
+            def run():
+                rc = L.da3b_upsample_nhwc(P(x), B, hs, hs, C, P(o), hd, hd, S)
+                if rc:
+                    raise RuntimeError(f"da3b_upsample_nhwc rc={rc}")
 
-        ms = timeit(run)
-        gbs = (x.numel() + o.numel()) * 2 / (ms / 1e3) / 1e9
-        hbm = peak_hbm()
-        print(json.dumps({"part": "up", "case": f"B={B} 296->518 C={C}", "ms": round(ms, 4), "GB/s": round(gbs, 1),
-                          "frac": round(gbs / hbm[0], 4), "peak": f"{hbm[0]} GB/s ({hbm[1]})"}), flush=True)
-        del x, o
+            ms = timeit(run)
+            gbs = (x.numel() + o.numel()) * 2 / (ms / 1e3) / 1e9
+            hbm = peak_hbm()
+            print(json.dumps({"part": "up", "case": f"B={B} {hs}->{hd} C={C}", "ms": round(ms, 4),
+                              "GB/s": round(gbs, 1), "frac": round(gbs / hbm[0], 4),
+                              "peak": f"{hbm[0]} GB/s ({hbm[1]})"}), flush=True)
+            del x, o
 
     if args.part in ("pre", "all"):
         # normalise + patchify of the C3 batch: 64 RGB8 images 518x518 -> f16 operand [64*1369][640]
