@@ -65,10 +65,10 @@ def _run_gpu(m, img, aux):
     return out, feats, lg
 
 
-def _check_single(name, size, aux=False):
+def _check_single(name, size, aux=False, stress=True):
     from da3cpplib_b200 import synth
 
-    path, m, oq, of = _models(name)
+    path, m, oq, of = _models(name, stress=stress)
     img = synth.image(synth.IMAGE_SEED, 0, size, size)
     refq = oq.infer(img, aux=aux)
     featq = [oq.get(f"feat{o}") for o in range(4)]
@@ -149,6 +149,16 @@ def test_da3_tiny_aux(cuda):
 def test_da2_small_518(cuda):
     """C1 shape: DA2-S at 518x518 (1370 tokens)."""
     _assert(_check_single("da2-s", 518))
+
+
+def test_da2_large_518(cuda):
+    """C3 model: DA2-L at 518x518, the bench's workload. Its DPT head has 256-channel
+    features, so this is the end-to-end check of the halo-box 3x3 convs (CTA pairs for
+    the 256-output layer and residual convs, one CTA for out1's 256 -> 128) and of the
+    fused output stage at C = 128, against the oracle on the bench's own GGUF. Its
+    depth (relu of random-init logits) is all zero, so the raw logits and the four
+    feature maps are what is compared."""
+    _assert(_check_single("da2-l", 518, stress=False), depth=False)
 
 
 def test_da3_tiny_multiview(cuda):
