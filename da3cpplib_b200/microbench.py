@@ -13,6 +13,13 @@ out2: da3b_output_conv2 (upsample 296 -> 518 + 3x3 conv 128 -> 32 + 1x1 -> depth
 C3 head shape, fused and through a materialised upsampled map.
 ray: da3b_ray_pose (the ray->pose solver, both host round trips included; wall time)
 on a synthetic 288 x 288 ray field, the aux resolution of a 504 x 504 image.
+c4: the C4 workload end to end on one GPU: a DA3-L random-init Q8_0 GGUF, --scenes
+scenes (default 16) x 8 views of 504 x 504 RGB8 already on the device, depth and
+confidence out (da3b_infer_device, views_per_scene = 8: local/global alternation,
+reference-view selection, camera token, UV pos-embed). One step = all scenes; the L2
+is flushed (256 MB write) before each timed step. Model work per scene is the
+algorithmic count of the scope table: linears 6.27 TF + attention 4.41 + pass A 2.21
++ depth head 2.26 = 15.15 TFLOP.
 
 Each line: {"part", "case", "ms", "tflops", "frac", "peak"}; frac is against the
 measured dense bf16 burst peak of this GPU pool (MEASURED_PEAKS.json, else the pool's
@@ -70,7 +77,8 @@ def main(argv=None):
     from . import _lib
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("--part", default="all", choices=["A", "B", "attn", "up", "pre", "ray", "out2", "all"])
+    ap.add_argument("--part", default="all", choices=["A", "B", "attn", "up", "pre", "ray", "out2", "c4", "all"])
+    ap.add_argument("--scenes", type=int, default=16, help="c4: scenes of 8 views")
     ap.add_argument("--m", type=int, default=0, help="Part A: only this M")
     ap.add_argument("--kn", default="", help="Part A: only this K,N (e.g. 1024,4096)")
     ap.add_argument("--act", type=int, default=0, help="Part A activation: 0 none, 2 erf-GELU")
@@ -237,6 +245,44 @@ def main(argv=None):
             ms = timeit(run)
             emit("out2", f"{'fused' if fused else 'unfused'} B={B} {hs}->{H} C={C}", ms, flops)
         del feat, out
+
+    if args.part == "c4":
+        from . import Model, synth
+
+        n_sc, V, HW = args.scenes, 8, 504
+        m = Model(synth.ensure_gguf("da3-l"), 0)
+        rgb = torch.randint(0, 256, (n_sc * V, HW, HW, 3), generator=gen, device="cuda", dtype=torch.uint8)
+        depth = torch.empty((n_sc * V, HW, HW), device="cuda")
+        conf = torch.empty_like(depth)
+        flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+
+        def step():
+            m.infer_device(rgb.data_ptr(), n_sc * V, HW, HW, depth.data_ptr(), conf.data_ptr(),
+                           views_per_scene=V, stream=s.cuda_stream)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(args.reps):
+            flush.fill_(1.0)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            step()
+            b.record(s)
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+        if L.da3b_device_status() != 0:
+            raise RuntimeError("device status set")
+        ms = sum(times) / len(times)
+        tf = 15.15e12 * n_sc / (ms / 1e3) / 1e12
+        print(json.dumps({"part": "c4", "case": f"DA3-L {n_sc} scenes x {V} views {HW}x{HW}", "ms": round(ms, 3),
+                          "scenes/s": round(n_sc / (ms / 1e3), 2), "views/s": round(n_sc * V / (ms / 1e3), 1),
+                          "model_tflops": round(tf, 1), "frac": round(tf / peak, 4),
+                          "peak": f"{peak} TFLOP/s ({src})", "launches": m.launches(n_sc * V, HW, HW, V),
+                          "l2": "flushed (256 MB write) before each step"}), flush=True)
+        m.close()
+        del rgb, depth, conf, flush
 
     if args.part in ("ray", "all"):
         import time
