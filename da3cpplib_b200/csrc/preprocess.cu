@@ -290,6 +290,23 @@ __global__ void __launch_bounds__(256) k_patchify14(const uint8_t* __restrict__ 
                                                     int gw, float m0, float m1, float m2, float s0, float s1, float s2,
                                                     __half* __restrict__ out, int ldk) {
   __shared__ __align__(16) uint8_t tile[kP * kRowBytes];
+  // Per-channel value table: lut[c][v] = f16((v / 255 - mean_c) / sd_c), built with the
+  // same f32 operations as the per-element formula, so the output bits are unchanged;
+  // and per operand column k < 3 * 14 * 14 the staged-tile byte offset of patch 0
+  // (ky * kRowBytes + kx * 3 + c) with the channel in bits 16+.
+  __shared__ unsigned short lut[3 * 256];
+  __shared__ int ktab[3 * kP * kP];
+  for (int i = threadIdx.x; i < 3 * 256; i += blockDim.x) {
+    const int c = i >> 8;
+    const float u = static_cast<float>(i & 255) / 255.f;
+    const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2);
+    const float sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
+    lut[i] = __half_as_ushort(__float2half_rn((u - mean) / sd));
+  }
+  for (int k = threadIdx.x; k < 3 * kP * kP; k += blockDim.x) {
+    const int c = k / (kP * kP), r = k - c * (kP * kP), ky = r / kP, kx = r - ky * kP;
+    ktab[k] = (ky * kRowBytes + kx * 3 + c) | (c << 16);
+  }
   const uintptr_t lo = reinterpret_cast<uintptr_t>(rgb);
   const uintptr_t hi = lo + static_cast<size_t>(B) * H * W * 3;
   const int px0 = blockIdx.x * kStrip, py = blockIdx.y, b = blockIdx.z;
@@ -324,26 +341,24 @@ __global__ void __launch_bounds__(256) k_patchify14(const uint8_t* __restrict__ 
   const int kk = 3 * kP * kP;
   for (int item = threadIdx.x; item < np * k8; item += blockDim.x) {
     const int pl = item / k8, k0 = (item - pl * k8) * 8;
-    float v[8];
+    const int poff = pl * kP * 3;
+    uint32_t w[4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int k = k0 + j;
-      if (k < kk) {
-        const int c = k / (kP * kP), r = k - c * (kP * kP), ky = r / kP, kx = r - ky * kP;
-        const float u = static_cast<float>(tile[ky * kRowBytes + (pl * kP + kx) * 3 + c]) / 255.f;
-        const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2);
-        const float sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
-        v[j] = (u - mean) / sd;
-      } else {
-        v[j] = 0.f;
+    for (int j = 0; j < 4; ++j) {
+      uint32_t h[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int k = k0 + 2 * j + q;
+        h[q] = 0u;  // operand columns past 3 * 14 * 14: zero padding
+        if (k < kk) {
+          const int e = ktab[k];
+          h[q] = lut[(e >> 16) * 256 + tile[(e & 0xffff) + poff]];
+        }
       }
+      w[j] = h[0] | (h[1] << 16);
     }
-    uint4 o;
-    __half2* h2 = reinterpret_cast<__half2*>(&o);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) h2[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
     const size_t row = (static_cast<size_t>(b) * gh + py) * gw + px0 + pl;
-    *reinterpret_cast<uint4*>(out + row * ldk + k0) = o;
+    *reinterpret_cast<uint4*>(out + row * ldk + k0) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
