@@ -151,6 +151,15 @@ def test_da2_small_518(cuda):
     _assert(_check_single("da2-s", 518))
 
 
+def test_da2_base_518(cuda):
+    """C2 model: DA2-B at 518x518. Its DPT head has 128-channel features, so the
+    layer_rn and residual-unit 3x3 convs run on the one-CTA halo-box kernel with 128
+    outputs (bias, residual addend and relu copy in the epilogue), and the fused output
+    stage at C = 64. Random-init depth is relu of mostly negative logits, so the logits
+    and features are compared."""
+    _assert(_check_single("da2-b", 518, stress=False), depth=False)
+
+
 def test_da2_large_518(cuda):
     """C3 model: DA2-L at 518x518, the bench's workload. Its DPT head has 256-channel
     features, so this is the end-to-end check of the halo-box 3x3 convs (CTA pairs for
