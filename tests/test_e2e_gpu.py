@@ -160,6 +160,14 @@ def test_da2_base_518(cuda):
     _assert(_check_single("da2-b", 518, stress=False), depth=False)
 
 
+def test_da3_large_504(cuda):
+    """C4's model, one view: DA3-L at 504x504 with the aux ray head. Covers RoPE and
+    QK-norm from layer 8, the camera token, the concatenated local/global out-layer
+    features, the head LayerNorm, the UV pos-embed inside the fused output stage (C = 128)
+    and the halo-box convs of both DPT pyramids, against the oracle."""
+    _assert(_check_single("da3-l", 504, aux=True, stress=False))
+
+
 def test_da2_large_518(cuda):
     """C3 model: DA2-L at 518x518, the bench's workload. Its DPT head has 256-channel
     features, so this is the end-to-end check of the halo-box 3x3 convs (CTA pairs for
