@@ -4,7 +4,8 @@
 Workload (the north-star metric): Depth Anything V2 Large
 (ViT-L/14, 24 layers, Q8_0 linears, DPT head with 256 features), a batch of 64
 seeded uniform RGB8 518x518 images sharded 64/N per GPU (strong scaling: the job is
-fixed at 64 images). Random-init GGUF weights in the reference layout (N(0, 0.02)).
+fixed at 64 images). Random-init GGUF weights in the reference layout (the parity
+tests' stress init, whose depth map is non-degenerate; see da3cpplib_b200/synth.py).
 
 One step = one forward of the rank's shard: RGB8 -> normalise/patchify -> 24 ViT
 blocks -> DPT head -> depth maps. `value` times steps with inputs resident in HBM;
@@ -123,7 +124,7 @@ def model_path(rank, world):
 
     path = None
     if rank == 0:
-        path = synth.ensure_gguf(MODEL)
+        path = synth.ensure_gguf(MODEL, stress=True)
     if world > 1:
         import torch.distributed as dist
 
@@ -140,7 +141,7 @@ def cpu_reference_step_seconds(n_images=1, warmup=0, steps=1, path=None):
     from oracle.oracle import Oracle
 
     if path is None:
-        path = synth.ensure_gguf(MODEL)
+        path = synth.ensure_gguf(MODEL, stress=True)
     orc = Oracle(path, act_quant=True, n_threads=os.cpu_count() or 1)
     img = synth.image(synth.IMAGE_SEED, 0, H, W)
     for _ in range(warmup):

@@ -143,6 +143,20 @@ class Model:
             raise RuntimeError(f"da3b_debug_feature failed ({rc})")
         return buf[: r.value * c.value].reshape(r.value, c.value).astype(np.float32)
 
+    def residual(self, layer, rows_cap=1 << 27):
+        """Residual stream after ViT block `layer` of the last run, f32 [rows][embed_dim]
+        (needs set_capture_residuals(True) before that run)."""
+        buf = np.empty(rows_cap, np.float32)
+        r, c = ctypes.c_int(), ctypes.c_int()
+        rc = self.lib.da3b_debug_residual(self.ctx, layer, buf.ctypes.data, buf.size, ctypes.byref(r),
+                                          ctypes.byref(c))
+        if rc != 0:
+            raise RuntimeError(f"da3b_debug_residual failed ({rc})")
+        return buf[: r.value * c.value].reshape(r.value, c.value).copy()
+
+    def set_capture_residuals(self, on: bool):
+        _lib.check(self.lib.da3b_set_capture_residuals(self.ctx, int(on)), "da3b_set_capture_residuals")
+
     def set_graphs(self, on: bool):
         _lib.check(self.lib.da3b_set_graphs(self.ctx, int(on)), "da3b_set_graphs")
 

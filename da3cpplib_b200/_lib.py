@@ -56,6 +56,8 @@ SIGNATURES = {
     "da3b_ref_views": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int]),
     "da3b_launches": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int]),
     "da3b_debug_feature": (c_int, [c_void_p, c_int, c_void_p, c_size_t, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    "da3b_set_capture_residuals": (c_int, [c_void_p, c_int]),
+    "da3b_debug_residual": (c_int, [c_void_p, c_int, c_void_p, c_size_t, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     "da3b_set_graphs": (c_int, [c_void_p, c_int]),
     "da3b_set_raw_logits": (c_int, [c_void_p, c_int]),
     "da3b_set_act_quant": (c_int, [c_void_p, c_int]),

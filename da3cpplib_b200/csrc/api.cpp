@@ -960,6 +960,26 @@ DA3B_API int da3b_debug_feature(da_ctx* c, int layer, void* out, size_t capacity
   return cudaMemcpy(out, p, n * 2, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -4;
 }
 
+DA3B_API int da3b_set_capture_residuals(da_ctx* c, int on) {
+  if (!c || !c->engine) return -1;
+  c->engine->set_capture_residuals(on != 0);
+  return 0;
+}
+
+DA3B_API int da3b_debug_residual(da_ctx* c, int layer, float* out, size_t capacity, int* rows, int* cols) {
+  if (!c || !c->engine || !out) return -1;
+  int r = 0, k = 0;
+  const float* p = c->engine->debug_resid(layer, &r, &k);
+  if (!p) return -2;
+  if (rows) *rows = r;
+  if (cols) *cols = k;
+  const size_t n = static_cast<size_t>(r) * k;
+  if (n > capacity) return -3;
+  cudaSetDevice(c->engine->device());
+  cudaStreamSynchronize(c->stream);
+  return cudaMemcpy(out, p, n * sizeof(float), cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -4;
+}
+
 DA3B_API int da3b_set_graphs(da_ctx* c, int on) {
   if (!c || !c->engine) return -1;
   c->engine->set_use_graph(on != 0);

@@ -17,6 +17,7 @@
 //              end. P V completions alternate between two barriers by tile parity.
 //              Keys past the sequence are masked; rows past it are not stored.
 // Every wait is bounded (ptx.cuh); on a timeout the kernel records a status and exits.
+#include <atomic>
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -341,8 +342,9 @@ __global__ void __launch_bounds__(192, 2)
 
 }  // namespace
 
-// qkv: [nseq*seqlen][3D] (q | k | v), vt: [nseq][H][64][ld_vt] (transposed v, zero
-// beyond seqlen within each row), out: [nseq*seqlen][D].
+// qkv: [nseq*seqlen][3D] (q | k | v), vt: [nseq][H][64][ld_vt] (transposed v), out:
+// [nseq*seqlen][D]. The columns of vt beyond seqlen are padding that is never read:
+// the V^T tensor map is seqlen wide, so the TMA fills out-of-range keys with zeros.
 int attention_tc(const __half* qkv, const __half* vt, int ld_vt, int nseq, int seqlen, int H, int D, __half* out,
                  int q8, int* status, cudaStream_t s) {
   if (nseq <= 0 || seqlen <= 0) return 0;
@@ -352,12 +354,14 @@ int attention_tc(const __half* qkv, const __half* vt, int ld_vt, int nseq, int s
   if ((rc = make_tmap_2d(&tq, qkv, nseq * seqlen, 3 * D, 3 * D, 128))) return rc - 100;
   if ((rc = make_tmap_2d(&tk, qkv, nseq * seqlen, 3 * D, 3 * D, kKT))) return rc - 100;
   if ((rc = make_tmap_2d(&tv, vt, nseq * H * 64, seqlen, ld_vt, 64))) return rc - 200;
-  static uint64_t attr_set = 0;
+  // per-device "attribute set" bits; host threads may make their first call at once
+  static std::atomic<uint64_t> attr_set{0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!((attr_set >> (dev & 63)) & 1)) {
+  const uint64_t bit = uint64_t(1) << (dev & 63);
+  if (!(attr_set.load(std::memory_order_acquire) & bit)) {
     if (cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess) return -3;
-    attr_set |= uint64_t(1) << (dev & 63);
+    attr_set.fetch_or(bit, std::memory_order_acq_rel);
   }
   dim3 grid((seqlen + 127) / 128, H, nseq);
   const float sl2 = 0.125f * 1.4426950408889634f;

@@ -23,6 +23,7 @@
 // A CTA-pair form (k_conv3_halo2, below) serves output counts in groups of 256.
 // Persistent: grid = number of SMs, tiles assigned round-robin. Every wait is bounded
 // (ptx.cuh); on a timeout the kernel records a status, drains its MMAs and exits.
+#include <atomic>
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -538,14 +539,14 @@ int launch_halo2(const __half* X, int B, int H, int W, int IC, const __half* Wp,
   int rc;
   if ((rc = make_tmap_nhwc_planes(&ta, X, B, H, W, IC, Cfg::kBoxW, Cfg::kBoxH))) return rc - 100;
   if ((rc = make_tmap_2d(&tb, Wp, OC, 9 * icp, 9 * icp, N / 2))) return rc - 200;
-  static uint64_t attr_set = 0;
+  static std::atomic<uint64_t> attr_set{0};  // one bit per device; first calls may race
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!((attr_set >> (dev & 63)) & 1)) {
+  if (!((attr_set.load() >> (dev & 63)) & 1)) {
     if (cudaFuncSetAttribute(k_conv3_halo2<N, kHalves>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) !=
         cudaSuccess)
       return -3;
-    attr_set |= uint64_t(1) << (dev & 63);
+    attr_set.fetch_or(uint64_t(1) << (dev & 63));
   }
   const long n_px = static_cast<long>(B) * ((W + Cfg::kTw - 1) / Cfg::kTw) * ((H + Cfg::kTh - 1) / Cfg::kTh);
   const long tiles = ((n_px + 1) / 2) * (OC / N);
@@ -606,13 +607,13 @@ int conv3_halo(const __half* X, int B, int H, int W, int IC, const __half* Wp, i
   int rc;
   if ((rc = make_tmap_nhwc_planes(&ta, X, B, H, W, IC, kBoxW, kBoxH))) return rc - 100;
   if ((rc = make_tmap_2d(&tb, Wp, OC, 9 * icp, 9 * icp, kOCh))) return rc - 200;
-  static uint64_t attr_set = 0;
+  static std::atomic<uint64_t> attr_set{0};  // one bit per device; first calls may race
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!((attr_set >> (dev & 63)) & 1)) {
+  if (!((attr_set.load() >> (dev & 63)) & 1)) {
     if (cudaFuncSetAttribute(k_conv3_halo, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
       return -3;
-    attr_set |= uint64_t(1) << (dev & 63);
+    attr_set.fetch_or(uint64_t(1) << (dev & 63));
   }
   const long n_tiles = static_cast<long>(B) * ((W + kTw - 1) / kTw) * ((H + kTh - 1) / kTh) * (OC / kOCh);
   if (n_tiles > 0x7fffffffL) return 1;

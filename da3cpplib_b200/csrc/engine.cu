@@ -69,6 +69,7 @@ struct Plan {
   __half* ftmp[4] = {nullptr, nullptr, nullptr, nullptr};
   __half* featn[4] = {nullptr, nullptr, nullptr, nullptr};  // head-LayerNormed features (DA3)
   int* b_idx = nullptr;
+  float* resid_cap = nullptr;  // [depth][M][D] residual after each block (capture mode only)
   // head
   __half* P[4] = {nullptr, nullptr, nullptr, nullptr};
   __half *L0 = nullptr, *L1 = nullptr, *L3 = nullptr, *A3 = nullptr;
@@ -131,6 +132,15 @@ std::unique_ptr<Engine> Engine::create(const std::string& path, int device, std:
 void Engine::set_act_quant(bool on) {
   if (on == act_quant_) return;
   act_quant_ = on;
+  cudaSetDevice(device_);
+  cudaDeviceSynchronize();
+  last_ = nullptr;
+  plans_.clear();
+}
+
+void Engine::set_capture_residuals(bool on) {
+  if (on == capture_resid_) return;
+  capture_resid_ = on;
   cudaSetDevice(device_);
   cudaDeviceSynchronize();
   last_ = nullptr;
@@ -328,6 +338,7 @@ Plan* Engine::plan_for(int V, int S, int H, int W, bool rays) {
     if (hd.norm_g)
       for (int o = 0; o < 4; ++o) T(p->featn[o], V_ * Np * p->Cf);
     T(p->b_idx, static_cast<size_t>(std::max(1, p->scenes)));
+    if (capture_resid_) T(p->resid_cap, static_cast<size_t>(c.depth) * M_ * D);
     if (model_->camdec.present) {
       T(p->cam, V_ * p->Cf);
       T(p->cam_h1, V_ * model_->camdec.bb0.N);
@@ -547,6 +558,12 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
       e.bias = b.fc2.b;
       e.scale = b.ls2;
       CK(gemm_linear(p.hid, M, b.fc2.K, b.fc2.K, b.fc2.w, D, b.fc2.ldw, 0, e, status_, s));
+    }
+    if (p.resid_cap &&
+        cudaMemcpyAsync(p.resid_cap + static_cast<size_t>(i) * M * D, p.x, static_cast<size_t>(M) * D * sizeof(float),
+                        cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+      err_ = "residual capture copy failed";
+      return -30;
     }
     if (!global)
       if (int rc = write_local(i)) return rc;
@@ -1003,6 +1020,13 @@ const float* Engine::debug_x(int* rows, int* cols) const {
   *rows = last_->M;
   *cols = model_->cfg.embed_dim;
   return last_x_;
+}
+
+const float* Engine::debug_resid(int layer, int* rows, int* cols) const {
+  if (!last_ || !last_->resid_cap || layer < 0 || layer >= model_->cfg.depth) return nullptr;
+  *rows = last_->M;
+  *cols = model_->cfg.embed_dim;
+  return last_->resid_cap + static_cast<size_t>(layer) * last_->M * model_->cfg.embed_dim;
 }
 
 }  // namespace da3b

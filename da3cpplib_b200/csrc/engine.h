@@ -83,11 +83,17 @@ class Engine {
   // which sit closer to the reference's outputs (two independent Q8_0 roundings
   // disagree by more than one rounding does). Drops the cached plans.
   void set_act_quant(bool on);
+  // true: every forward also copies the residual stream x after each ViT block into a
+  // per-plan buffer [depth][M][D] f32 (parity tests of every layer). Drops the cached plans.
+  void set_capture_residuals(bool on);
 
   // Debug captures for parity tests: feats of out-layer o ([n_views*Np][C] f16) of
   // the last run; returns nullptr if unavailable.
   const __half* debug_feat(int o, int* rows, int* cols) const;
   const float* debug_x(int* rows, int* cols) const;
+  // Residual stream after block `layer` of the last run ([M][D] f32, views in processing
+  // order), when residual capture is on; nullptr otherwise.
+  const float* debug_resid(int layer, int* rows, int* cols) const;
 
  private:
   Engine() = default;
@@ -106,6 +112,7 @@ class Engine {
   bool use_graph_ = true;
   bool raw_logits_ = false;
   bool act_quant_ = false;
+  bool capture_resid_ = false;
   std::string err_;
   std::map<std::tuple<int, int, int, int, bool>, std::unique_ptr<Plan>> plans_;
   Plan* last_ = nullptr;

@@ -12,6 +12,7 @@
 //                release the accumulator so the MMA of the next tile overlaps.
 // Tiles are visited m-major (all N tiles of one 128-row A panel back to back) so an
 // A panel is read from HBM about once while the weights stay resident in L2.
+#include <atomic>
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -1033,14 +1034,14 @@ template <int BN>
 static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeom& g, const EpiArgs& e, int* status,
                      cudaStream_t stream, int max_ctas) {
   using Cfg = GemmCfg<BN>;
-  static uint64_t attr_set = 0;  // one bit per device ordinal
+  static std::atomic<uint64_t> attr_set{0};  // one bit per device; first calls may race
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!((attr_set >> (dev & 63)) & 1)) {
+  if (!((attr_set.load() >> (dev & 63)) & 1)) {
     if (cudaFuncSetAttribute(k_tc_gemm<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
         cudaSuccess)
       return -10;
-    attr_set |= uint64_t(1) << (dev & 63);
+    attr_set.fetch_or(uint64_t(1) << (dev & 63));
   }
   const int tiles = g.num_m_tiles * g.num_n_tiles;
   int grid = num_sms();
@@ -1055,14 +1056,14 @@ template <int BN, bool kStaged>
 static int launch_bn2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmGeom& g,
                       const EpiArgs& e, int* status, cudaStream_t stream) {
   using Cfg = Gemm2Cfg<BN, kStaged>;
-  static uint64_t attr_set = 0;
+  static std::atomic<uint64_t> attr_set{0};  // one bit per device; first calls may race
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!((attr_set >> (dev & 63)) & 1)) {
+  if (!((attr_set.load() >> (dev & 63)) & 1)) {
     if (cudaFuncSetAttribute(k_tc_gemm2<BN, kStaged>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
         cudaSuccess)
       return -10;
-    attr_set |= uint64_t(1) << (dev & 63);
+    attr_set.fetch_or(uint64_t(1) << (dev & 63));
   }
   const int tiles = ((g.num_m_tiles + 1) / 2) * g.num_n_tiles;
   int pairs = num_sms() / 2;

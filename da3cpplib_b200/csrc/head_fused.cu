@@ -21,6 +21,7 @@
 //              bias, relu, 1x1 conv, activation;
 //   warp 8     one thread issues the 3 x C/16 MMAs of a row into one of two TMEM
 //              accumulators of 96 columns.
+#include <atomic>
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -412,10 +413,10 @@ int up_out2(const __half* src, int B, int hs, int ws, int C, const __half* pe, i
       (reinterpret_cast<uintptr_t>(wp) & 15))
     return -2;
   const Layout L = layout_for(C);
-  static uint64_t attr_set = 0;
+  static std::atomic<uint64_t> attr_set{0};  // one bit per device; first calls may race
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!((attr_set >> (dev & 63)) & 1)) {
+  if (!((attr_set.load() >> (dev & 63)) & 1)) {
     if (cudaFuncSetAttribute(k_up_out2<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, layout_for(16).total) !=
             cudaSuccess ||
         cudaFuncSetAttribute(k_up_out2<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, layout_for(32).total) !=
@@ -425,7 +426,7 @@ int up_out2(const __half* src, int B, int hs, int ws, int C, const __half* pe, i
         cudaFuncSetAttribute(k_up_out2<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, layout_for(128).total) !=
             cudaSuccess)
       return -3;
-    attr_set |= uint64_t(1) << (dev & 63);
+    attr_set.fetch_or(uint64_t(1) << (dev & 63));
   }
   dim3 grid((W + kTile - 1) / kTile, (H + kRows - 1) / kRows, B);
   switch (C) {

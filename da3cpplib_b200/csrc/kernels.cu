@@ -1,4 +1,5 @@
 // Memory-bound kernels of the depth path (coalesced, vectorised, one pass each).
+#include <atomic>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -481,14 +482,14 @@ int upsample_ac(const __half* in, int B, int hs, int ws, int C, __half* out, int
   if (rows <= 0 || W <= 0) return 0;
   const int staged_smem = 2 * ws * kUpCS * 2 + 8 * W;  // two source rows + the column table
   if (C % kUpCS == 0 && staged_smem <= 96 * 1024 && ws <= 0xffff && rows <= 0x7fffffffL) {
-    static uint64_t attr_set = 0;
+    static std::atomic<uint64_t> attr_set{0};  // one bit per device; first calls may race
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!((attr_set >> (dev & 63)) & 1)) {
+    if (!((attr_set.load() >> (dev & 63)) & 1)) {
       if (cudaFuncSetAttribute(k_upsample_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) !=
           cudaSuccess)
         return -3;
-      attr_set |= uint64_t(1) << (dev & 63);
+      attr_set.fetch_or(uint64_t(1) << (dev & 63));
     }
     k_upsample_staged<<<dim3(static_cast<unsigned>(rows), C / kUpCS), 256, staged_smem, s>>>(in, hs, ws, C, out, H, W,
                                                                                                pe);

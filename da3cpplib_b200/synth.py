@@ -15,8 +15,11 @@ would collapse every normalised activation to ~0.02 and make outputs degenerate)
 ``stress=True`` (parity tests) keeps every layer's output variance alive instead:
 linear and conv weights are N(0, 1/fan_in), QKV weights N(0, 2.25/fan_in) so that
 attention is sharp, and LayerScale 1 + N(0, std), so every block, the attention,
-RoPE and every head conv move the result measurably. The benchmark uses the plain
-N(0, 0.02) init (timing does not depend on the values).
+RoPE and every head conv move the result measurably; for DA2 relative models the
+output stage is drawn so that relu(logit) is positive on about half of the pixels
+(see the out2a/out2b comment in tensors_for). The benchmark uses the stress init of
+DA2-L too, so the timed model produces a non-degenerate depth map (timing does not
+depend on the values).
 """
 from __future__ import annotations
 
@@ -192,12 +195,29 @@ def tensors_for(spec: ModelSpec, seed: int, stress: bool = False):
     pyramid("")
     add("head.scratch.out1.weight", lw(F // 2, F, 3, 3, fan_in=9 * F))
     add("head.scratch.out1.bias", n(F // 2))
-    add("head.scratch.out2a.weight", lw(32, F // 2, 3, 3, fan_in=9 * F // 2, gain=1.4))
-    add("head.scratch.out2a.bias", n(32))
-    # a depth-only head (mono / metric DPT) keeps its single logit in a range where exp()
-    # gives depths of a few units rather than exp(15)
-    add("head.scratch.out2b.weight", lw(spec.output_dim, 32, 1, 1, fan_in=32, gain=0.1 if spec.sky else 1.0))
-    add("head.scratch.out2b.bias", n(spec.output_dim))
+    if stress and spec.arch == "depthanything2" and spec.max_depth <= 0.0:
+        # DA2 relative depth is relu(logit). Random out2a/out2b weights leave the logit's
+        # sign set by the large per-channel offsets of the head's features, so the depth
+        # map tends to be all zero. Here out2a's 32 outputs are 16 zero-DC 3x3 filters
+        # (taps summing to zero per input channel) and their negatives, and out2b weighs
+        # each pair by (v, -v): the logit is then a zero-mean high-pass of the features
+        # and about half the pixels have positive depth, while both relus still act
+        # (dropping one would double the logit).
+        w = rng.standard_normal((16, F // 2, 3, 3), dtype=np.float32) * np.float32(1.4 / np.sqrt(9 * F // 2))
+        w = (w - w.mean(axis=(2, 3), keepdims=True)).astype(np.float32)
+        b = n(16)
+        add("head.scratch.out2a.weight", np.concatenate([w, -w]).astype(np.float32))
+        add("head.scratch.out2a.bias", np.concatenate([b, -b]).astype(np.float32))
+        v = n(16, s=1.0 / np.sqrt(32))
+        add("head.scratch.out2b.weight", np.concatenate([v, -v]).reshape(1, 32, 1, 1).astype(np.float32))
+        add("head.scratch.out2b.bias", n(1))
+    else:
+        add("head.scratch.out2a.weight", lw(32, F // 2, 3, 3, fan_in=9 * F // 2, gain=1.4))
+        add("head.scratch.out2a.bias", n(32))
+        # a depth-only head (mono / metric DPT) keeps its single logit in a range where
+        # exp() gives depths of a few units rather than exp(15)
+        add("head.scratch.out2b.weight", lw(spec.output_dim, 32, 1, 1, fan_in=32, gain=0.1 if spec.sky else 1.0))
+        add("head.scratch.out2b.bias", n(spec.output_dim))
     if spec.aux:
         pyramid("_aux")
         chans = [F, F // 2, F, F // 2, F, F // 2]
@@ -302,7 +322,7 @@ def ensure_gguf(name: str, stress: bool = False, seed: int | None = None, metric
     metric_branch selects the nested metric-branch layout (m_vit.* / m_head.*)."""
     spec = SPECS[name]
     seed = model_seed(name) if seed is None else seed
-    key_parts = [dataclasses.asdict(spec), seed, stress, 3] + ([1] if metric_branch else [])
+    key_parts = [dataclasses.asdict(spec), seed, stress, 4] + ([1] if metric_branch else [])
     key = hashlib.sha1(json.dumps(key_parts).encode()).hexdigest()[:10]
     os.makedirs(CACHE, exist_ok=True)
     tag = ("-stress" if stress else "") + ("-mbranch" if metric_branch else "")

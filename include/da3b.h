@@ -229,6 +229,13 @@ DA3B_API int da3b_ref_views(da_ctx* ctx, int* out, int n);
 DA3B_API int da3b_launches(da_ctx* ctx, int n_views, int views_per_scene, int h, int w, int rays);
 /* Out-layer feature map of the last run (f16 [rows][cols], token 0 dropped) copied to host. */
 DA3B_API int da3b_debug_feature(da_ctx* ctx, int layer, void* out_f16, size_t capacity, int* rows, int* cols);
+/* 1 = every later forward also keeps the residual stream after each ViT block (f32
+ * [depth][rows][embed_dim] on the device, rows = views x tokens in processing order);
+ * 0 = off (default). Changing it drops the cached plans. For per-layer parity tests. */
+DA3B_API int da3b_set_capture_residuals(da_ctx* ctx, int on);
+/* Residual stream after block `layer` of the last run (f32 [rows][cols]) copied to
+ * host; -2 when residual capture was off for that run. */
+DA3B_API int da3b_debug_residual(da_ctx* ctx, int layer, float* out_f32, size_t capacity, int* rows, int* cols);
 /* 1 = replay captured CUDA graphs (default), 0 = eager launches. */
 DA3B_API int da3b_set_graphs(da_ctx* ctx, int on);
 /* 1 = activations entering each Q8_0 linear are rounded through Q8_0 the way ggml

@@ -4,9 +4,10 @@
  * Outputs are malloc'd and released with da_capi_free_floats / _bytes / _string;
  * failures return NULL or -1 and set da_capi_last_error (src/da_capi.cpp:97-176).
  *
- * Entry points that lie outside the depth path (camera pose, point clouds, GLB /
- * COLMAP export, nested metric models) are exported for link compatibility and fail
- * with a last_error that says so.
+ * Camera pose (camera-token decoder), nested metric models (da_capi_load_nested) and
+ * DA3 mono sky planes are implemented. Point clouds and the GLB / COLMAP exporters lie
+ * outside the depth path: they are exported for link compatibility and fail with a
+ * last_error that says so.
  */
 #ifndef DA3CPP_DA3_C_H
 #define DA3CPP_DA3_C_H
@@ -38,8 +39,10 @@ DA_CAPI const char* da_capi_last_error(da_ctx* ctx);
 /* Depth of one image file (binary PPM, P6) at the processed resolution. */
 DA_CAPI float* da_capi_depth_path(da_ctx* ctx, const char* image_path, int* out_h, int* out_w);
 DA_CAPI int da_capi_pose_path(da_ctx* ctx, const char* image_path, float out_ext[12], float out_intr[9]);
-/* Multi-view depth: all views share global attention (DA3). Returns n * h * w floats.
- * out_ext / out_intr are not written (camera pose is outside the depth path). */
+/* Multi-view depth: all views share global attention (DA3). Returns n * h * w floats in
+ * the input view order. When out_ext / out_intr are non-NULL they receive n * 12 and
+ * n * 9 floats: each view's camera-to-world extrinsics and intrinsics from the camera
+ * token decoder (fails, returning NULL, when the model has no camera decoder). */
 DA_CAPI float* da_capi_depth_pose_multi(da_ctx* ctx, const char** image_paths, int n_images, int* out_h,
                                         int* out_w, int* out_n, float* out_ext, float* out_intr);
 DA_CAPI int da_capi_depth_dense(da_ctx* ctx, const char* image_path, int* out_h, int* out_w, float** out_depth,

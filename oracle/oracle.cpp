@@ -140,6 +140,7 @@ class Oracle {
   std::map<std::string, Tensor> t;
   std::map<std::string, std::vector<float>> f32cache;
   std::map<std::string, std::vector<float>> caps;  // captures for parity tests
+  bool capture_resid = false;  // keep x after every block as caps["x<i>"]
 
   bool has(const std::string& n) const { return t.count(n) > 0; }
   const Tensor& T(const std::string& n) const {
@@ -762,6 +763,7 @@ class Oracle {
       const bool use_rope = c.rope_start >= 0 && i >= c.rope_start;
       if (global) vit_block(x.data(), 1, S * Nt, i, use_rope ? &r_global : nullptr);
       else vit_block(x.data(), S, Nt, i, use_rope ? &r_local : nullptr);
+      if (capture_resid && upto < 0) caps["x" + std::to_string(i)] = x;
       if (!global) local_x = x;
       for (int o = 0; o < NL; ++o)
         if (c.out_layers[o] == i) {
@@ -1111,6 +1113,47 @@ OR_API void* or_create(const or_config* cfg, const or_tensor* ts, int n) {
 }
 
 OR_API void or_destroy(void* p) { delete static_cast<Handle*>(p); }
+
+// Model-free entry points for the DA3 host-code pins: the RoPE tables for explicit
+// positions (src/rope2d.cpp:4-27), the offset bicubic pos-embed interpolation of an
+// explicit table [1 + grid^2][embed] (src/dino_backbone.cpp:18-56), and the saddle
+// reference-view choice from S CLS vectors [S][embed] (src/dino_backbone.cpp:372-412).
+OR_API int or_rope_tables(const float* pos_yx, int tokens, int head_dim, float freq, float* cos_out, float* sin_out) {
+  Oracle o;
+  o.c.head_dim = head_dim;
+  o.c.rope_freq = freq;
+  const std::vector<float> pos(pos_yx, pos_yx + static_cast<size_t>(tokens) * 2);
+  const Oracle::Rope r = o.rope_tables(pos, tokens);
+  memcpy(cos_out, r.cos.data(), r.cos.size() * sizeof(float));
+  memcpy(sin_out, r.sin.data(), r.sin.size() * sizeof(float));
+  return 0;
+}
+
+OR_API int or_interp_pos_embed(const float* pos_embed, int embed, int grid, float offset, int gh, int gw, float* out) {
+  Oracle o;
+  o.c.embed_dim = embed;
+  o.c.pos_embed_grid = grid;
+  o.c.interp_offset = offset;
+  Tensor t;
+  t.data = pos_embed;
+  t.type = 0;
+  t.ne[0] = embed;
+  t.ne[1] = 1 + grid * grid;
+  o.t["vit.pos_embed"] = t;
+  const std::vector<float> v = o.interp_pos_embed(gh, gw);
+  memcpy(out, v.data(), v.size() * sizeof(float));
+  return 0;
+}
+
+OR_API int or_select_saddle(const float* cls, int S, int embed) {
+  std::vector<std::vector<float>> c(S);
+  for (int s = 0; s < S; ++s) c[s].assign(cls + static_cast<size_t>(s) * embed, cls + static_cast<size_t>(s + 1) * embed);
+  return Oracle::select_saddle(c, embed);
+}
+
+// 1: later forwards keep the residual stream after every block (or_get "x<i>",
+// [S * tokens][embed] in processing order); 0: off.
+OR_API void or_set_capture_resid(void* p, int on) { static_cast<Handle*>(p)->o.capture_resid = on != 0; }
 
 OR_API void or_quantize_q8_0(const float* x, int64_t n, uint8_t* out) {
   for (int64_t b = 0; b < n / 32; ++b) {

@@ -22,29 +22,36 @@ CXXFLAGS = ["-O3", "-march=x86-64-v3", "-ffp-contract=off", "-fopenmp", "-fPIC",
             "-fvisibility=hidden"]
 
 
-REF_SRC_DIR = os.environ.get("DA3_REFERENCE_SRC", "/root/reference/src")
+# The DA3cpplib checkout's src/ folder: $DA3_REFERENCE_SRC, else a checkout named
+# "reference" beside this repository's root. Where neither exists (a machine without
+# the checkout), the prebuilt oracle/_ref library is used as shipped.
+REF_SRC_DIR = os.environ.get("DA3_REFERENCE_SRC") or os.path.join(os.path.dirname(os.path.dirname(HERE)),
+                                                                  "reference", "src")
 REF_DIR = os.path.join(HERE, "_ref")
 REF_LIB = os.path.join(REF_DIR, "libda3ref.so")
 # DA3cpplib's own host-only sources on the path, compiled unmodified (never copied).
-REF_SOURCES = ["preprocess.cpp", "uv_posembed.cpp", "nested.cpp", "ray_pose.cpp", "linalg.cpp"]
+REF_SOURCES = ["preprocess.cpp", "uv_posembed.cpp", "nested.cpp", "ray_pose.cpp", "linalg.cpp", "rope2d.cpp",
+               "dino_backbone.cpp"]
 
 
 def build_ref(force: bool = False):
-    """Compile the reference's preprocess.cpp, uv_posembed.cpp, nested.cpp, ray_pose.cpp and
-    linalg.cpp with ref_wrap.cpp into
+    """Compile the reference's preprocess.cpp, uv_posembed.cpp, nested.cpp, ray_pose.cpp,
+    linalg.cpp, rope2d.cpp and dino_backbone.cpp with ref_wrap.cpp and ref_stubs.cpp into
     oracle/_ref/libda3ref.so. Returns the library path, or None when the reference
     checkout is absent (the prebuilt library, if shipped, is still used)."""
     srcs = [os.path.join(REF_SRC_DIR, f) for f in REF_SOURCES]
     if not all(os.path.exists(s) for s in srcs):
         return REF_LIB if os.path.exists(REF_LIB) else None
     wrap = os.path.join(HERE, "ref_wrap.cpp")
-    newest = max(os.path.getmtime(s) for s in srcs + [wrap])
+    stubs = os.path.join(HERE, "ref_stubs.cpp")
+    shim = [os.path.join(HERE, "ref_shim", f) for f in os.listdir(os.path.join(HERE, "ref_shim"))]
+    newest = max(os.path.getmtime(s) for s in srcs + [wrap, stubs] + shim)
     if force or not os.path.exists(REF_LIB) or os.path.getmtime(REF_LIB) < newest:
         os.makedirs(REF_DIR, exist_ok=True)
         # x86-64 baseline ISA: no FMA, so no contraction; the reference's Release flags
         # (-O3, C++17) otherwise.
         cmd = (["g++", "-O3", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden",
-                "-I", os.path.join(HERE, "ref_shim"), "-I", REF_SRC_DIR] + srcs + [wrap, "-o", REF_LIB + ".tmp"])
+                "-I", os.path.join(HERE, "ref_shim"), "-I", REF_SRC_DIR] + srcs + [wrap, stubs, "-o", REF_LIB + ".tmp"])
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"reference build failed:\n{r.stderr}")
@@ -74,6 +81,11 @@ def ref_lib():
         R.ref_ql3.argtypes = [ctypes.c_void_p] * 3
         R.ref_smallest_eigvec.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
         R.ref_homography.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_void_p]
+        R.ref_rope_tables.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_void_p,
+                                      ctypes.c_void_p]
+        R.ref_interp_pos_embed.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int,
+                                           ctypes.c_int, ctypes.c_void_p]
+        R.ref_select_saddle.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
         R.ref_nested_align.restype = ctypes.c_float
         R.ref_nested_align.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
         _ref = R
@@ -139,6 +151,12 @@ def lib():
         L.or_ql3.argtypes = [ctypes.c_void_p] * 3
         L.or_smallest_eigvec.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
         L.or_homography.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_void_p]
+        L.or_set_capture_resid.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.or_rope_tables.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_void_p,
+                                     ctypes.c_void_p]
+        L.or_interp_pos_embed.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int,
+                                          ctypes.c_int, ctypes.c_void_p]
+        L.or_select_saddle.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
         L.or_get.restype = ctypes.c_int64
         L.or_get.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.POINTER(ctypes.c_float))]
         L.or_dims.argtypes = [ctypes.c_void_p] + [ctypes.POINTER(ctypes.c_int)] * 6
@@ -271,6 +289,15 @@ class Oracle:
         if n == 0:
             return np.zeros(0, dtype=np.float32)
         return np.ctypeslib.as_array(p, shape=(n,)).copy()
+
+    def set_capture_residuals(self, on=True):
+        """Keep the residual stream after every ViT block of later forwards ("x<i>")."""
+        lib().or_set_capture_resid(self.h, int(on))
+
+    def residual(self, layer):
+        """Residual stream after block `layer` of the last forward, [rows][embed_dim]."""
+        v = self.get(f"x{layer}")
+        return None if v is None else v.reshape(-1, self.cfg.embed_dim)
 
     def dims(self):
         v = [ctypes.c_int() for _ in range(6)]
@@ -493,3 +520,45 @@ def homography(src, dst, w, impl="oracle"):
     H = np.zeros(9)
     rc = _impl(impl, "homography")(src.ctypes.data, dst.ctypes.data, w.ctypes.data, w.size, H.ctypes.data)
     return H.reshape(3, 3) if rc == 0 else None
+
+
+# ---------------------------------------------------------------- DA3 host-code pins
+def _impl_lib(impl):
+    if impl == "ref":
+        R = ref_lib()
+        if R is None:
+            raise RuntimeError("oracle/_ref is not built")
+        return R, "ref_"
+    return lib(), "or_"
+
+
+def rope_tables(pos_yx, head_dim=64, freq=100.0, impl="oracle"):
+    """2-D RoPE cos / sin tables [tokens][head_dim] for positions pos_yx [tokens][2]."""
+    L, pre = _impl_lib(impl)
+    pos = np.ascontiguousarray(pos_yx, dtype=np.float32)
+    T = pos.shape[0]
+    c = np.zeros((T, head_dim), np.float32)
+    s = np.zeros((T, head_dim), np.float32)
+    rc = getattr(L, pre + "rope_tables")(pos.ctypes.data, T, head_dim, float(freq), c.ctypes.data, s.ctypes.data)
+    if rc != 0:
+        raise RuntimeError(f"rope_tables failed ({impl})")
+    return c, s
+
+
+def interp_pos_embed(pos_embed, grid, gh, gw, offset=0.1, impl="oracle"):
+    """Offset bicubic interpolation of a pos-embed table [1 + grid^2][embed] to gh x gw."""
+    L, pre = _impl_lib(impl)
+    pe = np.ascontiguousarray(pos_embed, dtype=np.float32)
+    E = pe.shape[1]
+    out = np.zeros((1 + gh * gw, E), np.float32)
+    rc = getattr(L, pre + "interp_pos_embed")(pe.ctypes.data, E, grid, float(offset), gh, gw, out.ctypes.data)
+    if rc != 0:
+        raise RuntimeError(f"interp_pos_embed failed ({impl})")
+    return out
+
+
+def select_saddle(cls, impl="oracle"):
+    """Index of the reference view chosen from S CLS vectors [S][embed]."""
+    L, pre = _impl_lib(impl)
+    c = np.ascontiguousarray(cls, dtype=np.float32)
+    return int(getattr(L, pre + "select_saddle")(c.ctypes.data, c.shape[0], c.shape[1]))

@@ -1,21 +1,31 @@
-// C ABI over DA3cpplib's own host-only sources, compiled unmodified from the reference
+// C ABI over DA3cpplib's own host-side sources, compiled unmodified from the reference
 // checkout into oracle/_ref/ — test infrastructure only, never part of libda3b.
 //
-// Only src/preprocess.cpp (the real/legacy preprocess and the uint8 cubic/area
-// resizers), src/uv_posembed.cpp, src/nested.cpp (the nested metric alignment) and
-// src/ray_pose.cpp + src/linalg.cpp (the ray->pose solver) are compiled: they need
-// nothing from ggml beyond
-// the opaque type names that model_loader.hpp mentions (oracle/ref_shim/). Everything
-// else on the depth path goes through ggml graphs, whose source is absent from the
-// reference checkout, so it cannot be built here.
+// Compiled: src/preprocess.cpp (the real/legacy preprocess and the uint8 cubic/area
+// resizers), src/uv_posembed.cpp, src/nested.cpp (the nested metric alignment),
+// src/ray_pose.cpp + src/linalg.cpp (the ray->pose solver), and src/rope2d.cpp +
+// src/dino_backbone.cpp for their host functions: the 2-D RoPE tables, the bicubic
+// pos-embed interpolation and the multi-view reference-view selection. The last two
+// files also build ggml graphs; ggml's source is absent from the checkout, so the ggml
+// names they use are declared in oracle/ref_shim/ and defined to abort in
+// oracle/ref_stubs.cpp. None of the functions called here reaches them.
 #include <cstdint>
 #include <cstring>
+#include <deque>
+#include <functional>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
 #include <vector>
 
+#include "dino_backbone.hpp"
 #include "linalg.hpp"
+#include "model_loader.hpp"
 #include "nested.hpp"
 #include "ray_pose.hpp"
 #include "preprocess.hpp"
+#include "rope2d.hpp"
 #include "uv_posembed.hpp"
 
 #define REF_API extern "C" __attribute__((visibility("default")))
@@ -130,4 +140,96 @@ REF_API void ref_ql3(const double* a, double* q, double* l) { da::linalg::ql_dec
 REF_API void ref_smallest_eigvec(const double* m, int n, double* v) { da::linalg::smallest_eigvec(m, n, v); }
 REF_API int ref_homography(const double* src, const double* dst, const double* w, int M, double* H) {
   return da::linalg::homography_weighted(src, dst, w, M, H) ? 0 : -1;
+}
+
+// ---------------------------------------------------------------- DA3 backbone host code
+// Access to private members of the reference's classes without editing its headers:
+// an explicit template instantiation may name a private member (the access rules do
+// not apply to explicit instantiations), and it exports the member pointer through a
+// friend function.
+namespace {
+template <typename Tag, typename Tag::type M>
+struct Expose {
+  friend typename Tag::type get(Tag) { return M; }
+};
+struct CfgTag {
+  typedef da::Config da::ModelLoader::*type;
+  friend type get(CfgTag);
+};
+struct InterpTag {
+  typedef std::vector<float> (da::DinoBackbone::*type)(int, int) const;
+  friend type get(InterpTag);
+};
+struct SaddleTag {
+  typedef int (da::DinoBackbone::*type)(const std::vector<std::vector<float>>&, int) const;
+  friend type get(SaddleTag);
+};
+}  // namespace
+template struct Expose<CfgTag, &da::ModelLoader::cfg_>;
+template struct Expose<InterpTag, &da::DinoBackbone::interp_pos_embed>;
+template struct Expose<SaddleTag, &da::DinoBackbone::select_reference_view_saddle>;
+
+// The checker's ModelLoader: model_loader.cpp (GGUF reading) is not compiled; tensor()
+// serves the tensors registered by the entry points below.
+namespace {
+std::mutex g_ml_mu;
+std::map<std::string, ggml_tensor> g_ml_tensors;
+// interp_pos_embed caches its result by the pos_embed data pointer, so every call gets
+// a buffer that stays alive (and therefore at a fresh address) until the library unloads.
+std::deque<std::vector<float>> g_pe_keep;
+}  // namespace
+da::ModelLoader::~ModelLoader() {}
+ggml_tensor* da::ModelLoader::tensor(const std::string& name) const {
+  auto it = g_ml_tensors.find(name);
+  return it == g_ml_tensors.end() ? nullptr : &it->second;
+}
+
+// build_rope_tables (src/rope2d.cpp:4-27): cos / sin [tokens][head_dim] for positions
+// pos_yx [tokens][2] (y, x).
+REF_API int ref_rope_tables(const float* pos_yx, int tokens, int head_dim, float freq, float* cos_out,
+                            float* sin_out) {
+  const std::vector<float> pos(pos_yx, pos_yx + static_cast<size_t>(tokens) * 2);
+  const da::RopeTables rt = da::build_rope_tables(pos, tokens, head_dim, freq);
+  const size_t n = static_cast<size_t>(tokens) * head_dim;
+  if (rt.cos.size() != n || rt.sin.size() != n) return -1;
+  std::memcpy(cos_out, rt.cos.data(), n * sizeof(float));
+  std::memcpy(sin_out, rt.sin.data(), n * sizeof(float));
+  return 0;
+}
+
+// DinoBackbone::interp_pos_embed (src/dino_backbone.cpp:18-56) of a pos-embed table
+// [1 + grid^2][embed] to gh x gw: out [1 + gh*gw][embed].
+REF_API int ref_interp_pos_embed(const float* pos_embed, int embed, int grid, float offset, int gh, int gw,
+                                 float* out) {
+  std::lock_guard<std::mutex> lk(g_ml_mu);
+  g_pe_keep.emplace_back(pos_embed, pos_embed + static_cast<size_t>(1 + grid * grid) * embed);
+  ggml_tensor t{};
+  t.type = GGML_TYPE_F32;
+  t.ne[0] = embed;
+  t.ne[1] = 1 + grid * grid;
+  t.ne[2] = t.ne[3] = 1;
+  t.data = g_pe_keep.back().data();
+  g_ml_tensors["vit.pos_embed"] = t;
+  da::ModelLoader ml;
+  da::Config& cfg = ml.*get(CfgTag());
+  cfg.embed_dim = static_cast<uint32_t>(embed);
+  cfg.pos_embed_grid = static_cast<uint32_t>(grid);
+  cfg.interp_offset = offset;
+  da::Backend be;
+  da::DinoBackbone bb(ml, be);
+  const std::vector<float> v = (bb.*get(InterpTag()))(gh, gw);
+  if (v.size() != static_cast<size_t>(1 + gh * gw) * embed) return -1;
+  std::memcpy(out, v.data(), v.size() * sizeof(float));
+  return 0;
+}
+
+// DinoBackbone::select_reference_view_saddle (src/dino_backbone.cpp:372-412) on S views'
+// CLS features cls [S][embed]; returns the selected view.
+REF_API int ref_select_saddle(const float* cls, int S, int embed) {
+  std::vector<std::vector<float>> c(S);
+  for (int s = 0; s < S; ++s) c[s].assign(cls + static_cast<size_t>(s) * embed, cls + static_cast<size_t>(s + 1) * embed);
+  da::ModelLoader ml;
+  da::Backend be;
+  da::DinoBackbone bb(ml, be);
+  return (bb.*get(SaddleTag()))(c, embed);
 }

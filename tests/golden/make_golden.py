@@ -33,6 +33,14 @@ Fixtures (all small):
                        double diagnostics.
   nested_ref.npz       DA3cpplib's own src/nested.cpp (oracle/_ref) on seeded inputs:
                        aligned depth, extrinsics and scale.
+  da3_host_ref.npz     DA3cpplib's own src/rope2d.cpp and src/dino_backbone.cpp host
+                       functions (oracle/_ref): build_rope_tables on the backbone's
+                       local and global ("no-diff") position grids and on random
+                       positions, DinoBackbone::interp_pos_embed (offset bicubic) from
+                       the 37-grid to the C1-C4 grids and odd grids, and
+                       select_reference_view_saddle on seeded CLS sets of 3-8 views.
+                       Small cases store the full outputs; the full-size C3/C4 tables
+                       store a SHA-256 of their bytes (da3_host_cases()).
 """
 from __future__ import annotations
 
@@ -375,8 +383,73 @@ def make_nested():
     np.savez_compressed(os.path.join(HERE, "nested_ref.npz"), **out)
 
 
+def backbone_positions(gh, gw, nodiff=False):
+    """Token positions (y, x) of the backbone's RoPE (src/dino_backbone.cpp:242-248):
+    token 0 at (0, 0); patch t at (row + 1, col + 1), or (1, 1) for the global layers'
+    position-free tables."""
+    pos = np.zeros((1 + gh * gw, 2), np.float32)
+    for t in range(gh * gw):
+        pos[1 + t] = (1, 1) if nodiff else (t // gw + 1, t % gw + 1)
+    return pos
+
+
+def da3_host_cases():
+    """(rope cases, interp cases, saddle cases) of da3_host_ref.npz, all seeded.
+    rope: (name, positions, head_dim, freq, full) ; interp: (name, pos_embed, grid, gh,
+    gw, offset, full) ; saddle: (name, cls [S][E])."""
+    rng = np.random.default_rng(SEED + 7)
+    rope = [("rl8x9", backbone_positions(8, 9), 64, 100.0, True),
+            ("rn8x9", backbone_positions(8, 9, nodiff=True), 64, 100.0, True),
+            ("rrand", rng.uniform(0, 60, size=(97, 2)).astype(np.float32), 64, 100.0, True),
+            ("rhd32", backbone_positions(5, 3), 32, 10.0, True),
+            ("rl36", backbone_positions(36, 36), 64, 100.0, False),
+            ("rl37", backbone_positions(37, 37), 64, 100.0, False)]
+    interp = []
+    for name, grid, gh, gw, E, full in (("p37to36", 37, 36, 36, 8, True), ("p37to37", 37, 37, 37, 8, True),
+                                        ("p8to5x7", 8, 5, 7, 16, True), ("p37to36w", 37, 36, 36, 1024, False),
+                                        ("p37to37w", 37, 37, 37, 1024, False), ("p4to9x2", 4, 9, 2, 4, True)):
+        pe = rng.standard_normal((1 + grid * grid, E)).astype(np.float32)
+        interp.append((name, pe, grid, gh, gw, 0.1, full))
+    saddle = []
+    for S in (3, 4, 5, 8):
+        for k in range(3):
+            base = rng.standard_normal(1024).astype(np.float32)
+            cls = base + rng.standard_normal((S, 1024)).astype(np.float32) * np.float32(0.3 + 0.4 * k)
+            cls *= rng.uniform(0.5, 2.0, size=(S, 1)).astype(np.float32)
+            saddle.append((f"s{S}_{k}", cls.astype(np.float32)))
+    return rope, interp, saddle
+
+
+def sha(a):
+    import hashlib
+
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def make_da3host():
+    if orc.ref_lib() is None:
+        raise SystemExit("oracle/_ref could not be built: the DA3cpplib checkout is required")
+    rope, interp, saddle = da3_host_cases()
+    out = {}
+    for name, pos, hd, freq, full in rope:
+        c, s = orc.rope_tables(pos, hd, freq, impl="ref")
+        if full:
+            out[name + "_cos"], out[name + "_sin"] = c, s
+        else:
+            out[name + "_sha"] = np.array([sha(c), sha(s)])
+    for name, pe, grid, gh, gw, off, full in interp:
+        r = orc.interp_pos_embed(pe, grid, gh, gw, off, impl="ref")
+        if full:
+            out[name + "_out"] = r
+        else:
+            out[name + "_sha"] = np.array([sha(r)])
+    for name, cls in saddle:
+        out[name + "_idx"] = np.int32(orc.select_saddle(cls, impl="ref"))
+    np.savez_compressed(os.path.join(HERE, "da3_host_ref.npz"), **out)
+
+
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["preprocess", "q8", "hf", "linalg", "raypose", "nested"]
+    which = sys.argv[1:] or ["preprocess", "q8", "hf", "linalg", "raypose", "nested", "da3host"]
     if "preprocess" in which:
         make_preprocess()
     if "q8" in which:
@@ -389,5 +462,7 @@ if __name__ == "__main__":
         make_raypose()
     if "nested" in which:
         make_nested()
+    if "da3host" in which:
+        make_da3host()
     for f in sorted(os.listdir(HERE)):
         print(f, os.path.getsize(os.path.join(HERE, f)))

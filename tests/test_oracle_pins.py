@@ -140,3 +140,62 @@ def test_metric_branch_layout_oracle(orc):
     np.testing.assert_array_equal(a["depth"], b["depth"])
     np.testing.assert_array_equal(a["sky"], b["sky"])
     assert "conf" not in a
+
+
+# ---------------------------------------------------------------- DA3 backbone host code
+def _da3_host():
+    import sys
+
+    if GOLD not in sys.path:
+        sys.path.insert(0, GOLD)
+    import make_golden
+
+    return make_golden
+
+
+def test_da3_host_code_matches_reference_fixture(orc):
+    """The oracle's RoPE tables, offset bicubic pos-embed interpolation and saddle
+    reference-view choice against DA3cpplib's own src/rope2d.cpp and
+    src/dino_backbone.cpp (compiled unmodified into oracle/_ref; committed outputs):
+    bit-exact, including the full-size C3/C4 tables (by SHA-256 of their bytes)."""
+    mg = _da3_host()
+    z = np.load(os.path.join(GOLD, "da3_host_ref.npz"))
+    rope, interp, saddle = mg.da3_host_cases()
+    for name, pos, hd, freq, full in rope:
+        c, s = orc.rope_tables(pos, hd, freq)
+        if full:
+            np.testing.assert_array_equal(c, z[name + "_cos"], err_msg=name)
+            np.testing.assert_array_equal(s, z[name + "_sin"], err_msg=name)
+        else:
+            assert [mg.sha(c), mg.sha(s)] == list(z[name + "_sha"]), name
+    for name, pe, grid, gh, gw, off, full in interp:
+        r = orc.interp_pos_embed(pe, grid, gh, gw, off)
+        if full:
+            np.testing.assert_array_equal(r, z[name + "_out"], err_msg=name)
+        else:
+            assert mg.sha(r) == z[name + "_sha"][0], name
+    for name, cls in saddle:
+        assert orc.select_saddle(cls) == int(z[name + "_idx"]), name
+
+
+def test_da3_host_code_matches_reference_live(orc):
+    """The same three functions against oracle/_ref on fresh seeded cases (skipped where
+    the reference library is not available)."""
+    if orc.ref_lib() is None:
+        pytest.skip("oracle/_ref not available")
+    rng = np.random.default_rng(77)
+    for _ in range(20):
+        T = int(rng.integers(1, 300))
+        pos = rng.uniform(0, 80, size=(T, 2)).astype(np.float32)
+        a, b = orc.rope_tables(pos), orc.rope_tables(pos, impl="ref")
+        np.testing.assert_array_equal(a[0], b[0])
+        np.testing.assert_array_equal(a[1], b[1])
+        grid = int(rng.integers(2, 40))
+        gh, gw = int(rng.integers(1, 45)), int(rng.integers(1, 45))
+        pe = rng.standard_normal((1 + grid * grid, 8)).astype(np.float32)
+        off = float(rng.choice([0.0, 0.1]))
+        np.testing.assert_array_equal(orc.interp_pos_embed(pe, grid, gh, gw, off),
+                                      orc.interp_pos_embed(pe, grid, gh, gw, off, impl="ref"))
+        S = int(rng.integers(2, 9))
+        cls = rng.standard_normal((S, 64)).astype(np.float32) * rng.uniform(0.1, 3.0, size=(S, 1)).astype(np.float32)
+        assert orc.select_saddle(cls) == orc.select_saddle(cls, impl="ref")

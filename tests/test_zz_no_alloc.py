@@ -82,3 +82,29 @@ def test_noalloc_argument_checks(lib, cuda):
     assert lib.da3b_attention_noalloc(ptr(qkv), 1, 16, 1, ptr(out), None, s) == -100   # no status word
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     assert lib.da3b_attention_noalloc(ptr(qkv), 0, 16, 1, ptr(out), ptr(status), s) == 0  # empty: no-op
+
+
+def test_noalloc_allocates_nothing(lib, cuda):
+    """After one warm-up call (which loads the kernels and resolves the scratch's
+    address), a larger call that the allocating entry point has never run leaves the
+    device's free memory unchanged: the no-alloc path takes no device memory."""
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s = V(torch.cuda.current_stream().cuda_stream)
+    small = _qkv(1, 300, 4, 6)
+    out_small = torch.empty(300, 4 * 64, dtype=torch.float16, device="cuda")
+    big_seq, big_heads = 2900, 16       # 2 * 1024 * 2904 * 2 B of V^T: within the scratch
+    big = _qkv(2, big_seq, big_heads, 7)
+    out_big = torch.empty(2 * big_seq, big_heads * 64, dtype=torch.float16, device="cuda")
+    assert lib.da3b_attention_noalloc(ptr(small), 1, 300, 4, ptr(out_small), ptr(status), s) == 0
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    assert lib.da3b_attention_noalloc(ptr(big), 2, big_seq, big_heads, ptr(out_big), ptr(status), s) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, f"free device memory changed by {free0 - free1} bytes"
+    assert int(status.item()) == 0
+    # and the result is the allocating entry point's
+    ref = torch.empty_like(out_big)
+    assert lib.da3b_attention(ptr(big), 2, big_seq, big_heads, ptr(ref), s) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(out_big, ref)
