@@ -12,6 +12,7 @@
 // ggml submodule is empty) and its tests ship no golden vectors for this path. The
 // Q8_0 quantiser is pinned bit-exactly against gguf-py's published quantiser, and the
 // DA2 architecture against an independent implementation (tests/test_oracle_*.py).
+#include <immintrin.h>
 #include <math.h>
 #include <stdint.h>
 #include <string.h>
@@ -78,6 +79,32 @@ uint16_t f2h(float f) {  // round to nearest even
   return sign | h;
 }
 
+// Optional per-op wall-clock totals ($DA3_ORACLE_PROFILE=1 prints them after each
+// forward); used to see where the checker's own time goes.
+struct Prof {
+  std::map<std::string, double> t;
+  bool on = getenv("DA3_ORACLE_PROFILE") != nullptr;
+};
+Prof& prof() {
+  static Prof p;
+  return p;
+}
+struct ProfScope {
+  const char* name;
+  double t0;
+  explicit ProfScope(const char* n) : name(n), t0(prof().on ? omp_get_wtime() : 0.0) {}
+  ~ProfScope() {
+    if (prof().on) prof().t[name] += omp_get_wtime() - t0;
+  }
+};
+void prof_dump(const char* what) {
+  if (!prof().on) return;
+  fprintf(stderr, "[oracle %s]", what);
+  for (auto& kv : prof().t) fprintf(stderr, " %s %.2fs", kv.first.c_str(), kv.second);
+  fprintf(stderr, "\n");
+  prof().t.clear();
+}
+
 struct Tensor {
   const void* data = nullptr;
   int type = 0;  // ggml type id: 0 f32, 1 f16, 8 q8_0
@@ -134,6 +161,49 @@ void quantize_row(const float* x, int K, float* d_out, int8_t* q_out) {
   }
 }
 
+// Exact int32 dot products of one 32-element int8 block of x (xb, its absolute value
+// ax) with the same block of eight weight rows (w0, rows ldw bytes apart), returned as
+// eight lanes. Products are formed as |x| * (w with x's sign), summed in pairs to int16
+// (|q| <= 127, so no pair exceeds 32 258) and then to int32; integer sums are exact in
+// any order, so each lane equals the scalar sum of x[i] * w[i].
+static inline __m256i q8_dot8(__m256i xb, __m256i ax, const int8_t* w0, size_t ldw) {
+  const __m256i ones = _mm256_set1_epi16(1);
+  __m256i p[8];
+  for (int j = 0; j < 8; ++j) {
+    const __m256i wj = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(w0 + j * ldw));
+    p[j] = _mm256_madd_epi16(_mm256_maddubs_epi16(ax, _mm256_sign_epi8(wj, xb)), ones);
+  }
+  const __m256i t0 = _mm256_hadd_epi32(p[0], p[1]), t1 = _mm256_hadd_epi32(p[2], p[3]);
+  const __m256i t2 = _mm256_hadd_epi32(p[4], p[5]), t3 = _mm256_hadd_epi32(p[6], p[7]);
+  const __m256i u0 = _mm256_hadd_epi32(t0, t1), u1 = _mm256_hadd_epi32(t2, t3);
+  return _mm256_add_epi32(_mm256_permute2x128_si256(u0, u1, 0x20), _mm256_permute2x128_si256(u0, u1, 0x31));
+}
+
+// rows (1 or 2) activation rows (int8 qx [rows][K], scales dx [rows][K/32]) against eight
+// Q8_0 weight rows (qw [8][K], scales dwT [K/32][ldd] at the first of the eight columns):
+// y[r][j] = sum over blocks b in order of float(isum_b) * (d_w * d_x) (+ bias[j]), the
+// scalar ggml vec_dot_q8_0_q8_0 accumulation, eight columns per vector.
+static void q8_rows_x8(const int8_t* qx, const float* dx, int rows, int K, const int8_t* qw, const float* dwT,
+                       int ldd, const float* bias, float* y, int ldy) {
+  const int nb = K / 32;
+  __m256 acc0 = _mm256_setzero_ps(), acc1 = _mm256_setzero_ps();
+  for (int b = 0; b < nb; ++b) {
+    const __m256 dwv = _mm256_loadu_ps(dwT + static_cast<size_t>(b) * ldd);
+    const __m256i x0 = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(qx + b * 32));
+    const __m256i i0 = q8_dot8(x0, _mm256_sign_epi8(x0, x0), qw + b * 32, K);
+    acc0 = _mm256_add_ps(acc0, _mm256_mul_ps(_mm256_cvtepi32_ps(i0), _mm256_mul_ps(dwv, _mm256_set1_ps(dx[b]))));
+    if (rows > 1) {
+      const __m256i x1 = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(qx + K + b * 32));
+      const __m256i i1 = q8_dot8(x1, _mm256_sign_epi8(x1, x1), qw + b * 32, K);
+      acc1 = _mm256_add_ps(acc1,
+                           _mm256_mul_ps(_mm256_cvtepi32_ps(i1), _mm256_mul_ps(dwv, _mm256_set1_ps(dx[nb + b]))));
+    }
+  }
+  const __m256 bv = bias ? _mm256_loadu_ps(bias) : _mm256_setzero_ps();
+  _mm256_storeu_ps(y, _mm256_add_ps(acc0, bv));
+  if (rows > 1) _mm256_storeu_ps(y + ldy, _mm256_add_ps(acc1, bv));
+}
+
 class Oracle {
  public:
   or_config c;
@@ -178,6 +248,7 @@ class Oracle {
   // Q8_0 W with act_quant: activations quantised to Q8_0, per-block int32 dot,
   // sumf += isum * (d_w * d_x) in block order (ggml vec_dot_q8_0_q8_0).
   void linear(const float* x, int M, int K, const std::string& wn, const std::string& bn, float* y) {
+    ProfScope ps_("linear");
     const Tensor& W = T(wn);
     const int N = static_cast<int>(W.ne[1]);
     const float* bias = bn.empty() ? nullptr : F(bn);
@@ -198,27 +269,35 @@ class Oracle {
           dw[static_cast<size_t>(n) * nb + b] = h2f(dh);
           memcpy(&qw[static_cast<size_t>(n) * K + b * 32], blk + 2, 32);
         }
-      const int NB = 16;
+      // per-block scales transposed to [nb][N] so eight output columns load together
+      std::vector<float> dwT(static_cast<size_t>(nb) * N);
+      for (int n = 0; n < N; ++n)
+        for (int b = 0; b < nb; ++b) dwT[static_cast<size_t>(b) * N + n] = dw[static_cast<size_t>(n) * nb + b];
+      const int N8 = N / 8 * 8;
 #pragma omp parallel for schedule(dynamic, 1) collapse(2)
-      for (int n0 = 0; n0 < N; n0 += NB)
+      for (int n0 = 0; n0 < N8; n0 += 8)
         for (int m0 = 0; m0 < M; m0 += 64)
-          for (int m = m0; m < std::min(M, m0 + 64); ++m) {
-            const int8_t* xq = &qx[static_cast<size_t>(m) * K];
-            const float* xd = &dx[static_cast<size_t>(m) * nb];
-            for (int n = n0; n < std::min(N, n0 + NB); ++n) {
-              const int8_t* wq = &qw[static_cast<size_t>(n) * K];
-              const float* wd = &dw[static_cast<size_t>(n) * nb];
-              float sumf = 0.f;
-              for (int b = 0; b < nb; ++b) {
-                int isum = 0;
-                const int8_t* a = wq + b * 32;
-                const int8_t* q = xq + b * 32;
-                for (int i = 0; i < 32; ++i) isum += static_cast<int>(a[i]) * static_cast<int>(q[i]);
-                sumf += static_cast<float>(isum) * (wd[b] * xd[b]);
-              }
-              y[static_cast<size_t>(m) * N + n] = sumf + (bias ? bias[n] : 0.f);
-            }
+          for (int m = m0; m < std::min(M, m0 + 64); m += 2) {
+            const int rows = std::min(2, M - m);
+            q8_rows_x8(&qx[static_cast<size_t>(m) * K], &dx[static_cast<size_t>(m) * nb], rows, K,
+                       &qw[static_cast<size_t>(n0) * K], &dwT[n0], N, bias ? bias + n0 : nullptr,
+                       y + static_cast<size_t>(m) * N + n0, N);
           }
+      // columns beyond the last multiple of 8: the same arithmetic, one column at a time
+      for (int n = N8; n < N; ++n)
+        for (int m = 0; m < M; ++m) {
+          const int8_t* xq = &qx[static_cast<size_t>(m) * K];
+          const float* xd = &dx[static_cast<size_t>(m) * nb];
+          const int8_t* wq = &qw[static_cast<size_t>(n) * K];
+          const float* wd = &dw[static_cast<size_t>(n) * nb];
+          float sumf = 0.f;
+          for (int b = 0; b < nb; ++b) {
+            int isum = 0;
+            for (int i = 0; i < 32; ++i) isum += static_cast<int>(wq[b * 32 + i]) * static_cast<int>(xq[b * 32 + i]);
+            sumf += static_cast<float>(isum) * (wd[b] * xd[b]);
+          }
+          y[static_cast<size_t>(m) * N + n] = sumf + (bias ? bias[n] : 0.f);
+        }
       return;
     }
     const float* w = F(wn);
@@ -228,19 +307,46 @@ class Oracle {
         for (int n = 0; n < N; ++n) y[static_cast<size_t>(m) * N + n] += bias[n];
   }
 
-  // y[M][N] = x[M][K] * w[N][K]^T in f32.
+  // y[M][N] = x[M][K] * w[N][K]^T in f32. Every output is the sum over k in order of
+  // x[m][k] * w[n][k] (separate multiply and add), computed for eight columns at once
+  // from w packed as [N/8][K][8].
   static void sgemm_nt(const float* x, int M, int K, const float* w, int N, float* y) {
+    const int N8 = N / 8 * 8;
+    std::vector<float> wp(static_cast<size_t>(N8) * K);
+#pragma omp parallel for schedule(static)
+    for (int nb = 0; nb < N8 / 8; ++nb)
+      for (int k = 0; k < K; ++k)
+        for (int j = 0; j < 8; ++j) wp[(static_cast<size_t>(nb) * K + k) * 8 + j] = w[static_cast<size_t>(nb * 8 + j) * K + k];
 #pragma omp parallel for schedule(dynamic, 1) collapse(2)
     for (int m0 = 0; m0 < M; m0 += 32)
-      for (int n0 = 0; n0 < N; n0 += 32)
-        for (int m = m0; m < std::min(M, m0 + 32); ++m)
-          for (int n = n0; n < std::min(N, n0 + 32); ++n) {
-            const float* a = x + static_cast<size_t>(m) * K;
-            const float* b = w + static_cast<size_t>(n) * K;
-            float s = 0.f;
-            for (int k = 0; k < K; ++k) s += a[k] * b[k];
-            y[static_cast<size_t>(m) * N + n] = s;
+      for (int n0 = 0; n0 < N8; n0 += 16)
+        for (int m = m0; m < std::min(M, m0 + 32); m += 4) {
+          const int rows = std::min(4, M - m);
+          const int nv = std::min(2, (N8 - n0) / 8);
+          __m256 acc[4][2];
+          for (int r = 0; r < 4; ++r) acc[r][0] = acc[r][1] = _mm256_setzero_ps();
+          const float* b0 = &wp[static_cast<size_t>(n0 / 8) * K * 8];
+          const float* b1 = b0 + static_cast<size_t>(K) * 8;
+          for (int k = 0; k < K; ++k) {
+            const __m256 w0 = _mm256_loadu_ps(b0 + static_cast<size_t>(k) * 8);
+            const __m256 w1 = nv > 1 ? _mm256_loadu_ps(b1 + static_cast<size_t>(k) * 8) : _mm256_setzero_ps();
+            for (int r = 0; r < rows; ++r) {
+              const __m256 a = _mm256_set1_ps(x[static_cast<size_t>(m + r) * K + k]);
+              acc[r][0] = _mm256_add_ps(acc[r][0], _mm256_mul_ps(a, w0));
+              acc[r][1] = _mm256_add_ps(acc[r][1], _mm256_mul_ps(a, w1));
+            }
           }
+          for (int r = 0; r < rows; ++r)
+            for (int v = 0; v < nv; ++v) _mm256_storeu_ps(y + static_cast<size_t>(m + r) * N + n0 + 8 * v, acc[r][v]);
+        }
+    for (int n = N8; n < N; ++n)
+      for (int m = 0; m < M; ++m) {
+        const float* a = x + static_cast<size_t>(m) * K;
+        const float* b = w + static_cast<size_t>(n) * K;
+        float s2 = 0.f;
+        for (int k = 0; k < K; ++k) s2 += a[k] * b[k];
+        y[static_cast<size_t>(m) * N + n] = s2;
+      }
   }
 
   // ggml_norm (double sums) * w + b  (src/ggml_extend.hpp:12-17).
@@ -354,6 +460,83 @@ class Oracle {
     }
     const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
     std::vector<float> o(static_cast<size_t>(M) * D);
+    ProfScope* ps_ = new ProfScope("attn_core");
+    if (hd % 8 == 0 && hd <= 256) {
+      // Keys of each (sequence, head) packed as [key block of 8][hd][8]: eight scores per
+      // vector, each lane summing q[d] * k[d] over d in order like the scalar loop below.
+      const int nkb = (seqlen + 7) / 8;
+      std::vector<float> kt(static_cast<size_t>(nseq) * H * nkb * hd * 8, 0.f);
+#pragma omp parallel for schedule(static) collapse(2)
+      for (int s = 0; s < nseq; ++s)
+        for (int h = 0; h < H; ++h) {
+          float* dst = &kt[(static_cast<size_t>(s) * H + h) * nkb * hd * 8];
+          for (int ki = 0; ki < seqlen; ++ki) {
+            const float* k = &qkv[(static_cast<size_t>(s) * seqlen + ki) * 3 * D + D + h * hd];
+            for (int d = 0; d < hd; ++d) dst[(static_cast<size_t>(ki / 8) * hd + d) * 8 + (ki % 8)] = k[d];
+          }
+        }
+      const int nv = hd / 8;
+      // two queries of one (sequence, head) at a time: independent online-softmax chains
+      // interleaved, sharing the key and value loads; each query's arithmetic and order are
+      // those of the scalar loop below
+      const int nqp = (seqlen + 1) / 2;
+#pragma omp parallel for schedule(dynamic, 4) collapse(2)
+      for (int s = 0; s < nseq; ++s)
+        for (int qp = 0; qp < nqp; ++qp)
+          for (int h = 0; h < H; ++h) {
+            const int nq = std::min(2, seqlen - 2 * qp);
+            const float* q[2];
+            for (int r = 0; r < 2; ++r)
+              q[r] = &qkv[(static_cast<size_t>(s) * seqlen + 2 * qp + std::min(r, nq - 1)) * 3 * D + h * hd];
+            const float* kth = &kt[(static_cast<size_t>(s) * H + h) * nkb * hd * 8];
+            __m256 acc[2][32];
+            for (int r = 0; r < 2; ++r)
+              for (int v = 0; v < nv; ++v) acc[r][v] = _mm256_setzero_ps();
+            float Mx[2] = {-INFINITY, -INFINITY}, S[2] = {0.f, 0.f};
+            alignas(32) float sc8[2][8];
+            for (int kb = 0; kb < nkb; ++kb) {
+              const float* kp = kth + static_cast<size_t>(kb) * hd * 8;
+              __m256 dot0 = _mm256_setzero_ps(), dot1 = _mm256_setzero_ps();
+              for (int d = 0; d < hd; ++d) {
+                const __m256 kv = _mm256_loadu_ps(kp + d * 8);
+                dot0 = _mm256_add_ps(dot0, _mm256_mul_ps(_mm256_set1_ps(q[0][d]), kv));
+                dot1 = _mm256_add_ps(dot1, _mm256_mul_ps(_mm256_set1_ps(q[1][d]), kv));
+              }
+              _mm256_store_ps(sc8[0], _mm256_mul_ps(dot0, _mm256_set1_ps(scale)));
+              _mm256_store_ps(sc8[1], _mm256_mul_ps(dot1, _mm256_set1_ps(scale)));
+              const int nk = std::min(8, seqlen - kb * 8);
+              for (int j = 0; j < nk; ++j) {
+                const float* vrow = &qkv[(static_cast<size_t>(s) * seqlen + kb * 8 + j) * 3 * D + 2 * D + h * hd];
+                for (int r = 0; r < 2; ++r) {
+                  const float sc = sc8[r][j];
+                  float ms = 1.f, vs = 1.f;
+                  if (sc > Mx[r]) {
+                    const float Mold = Mx[r];
+                    Mx[r] = sc;
+                    ms = expf(Mold - Mx[r]);
+                    const __m256 msv = _mm256_set1_ps(ms);
+                    for (int v = 0; v < nv; ++v) acc[r][v] = _mm256_mul_ps(acc[r][v], msv);
+                  } else {
+                    vs = expf(sc - Mx[r]);
+                  }
+                  const __m256 vsv = _mm256_set1_ps(vs);
+                  for (int v = 0; v < nv; ++v)
+                    acc[r][v] = _mm256_add_ps(acc[r][v], _mm256_mul_ps(_mm256_loadu_ps(vrow + 8 * v), vsv));
+                  S[r] = S[r] * ms + vs;
+                }
+              }
+            }
+            for (int r = 0; r < nq; ++r) {
+              float* od = &o[(static_cast<size_t>(s) * seqlen + 2 * qp + r) * D + h * hd];
+              const float inv = S[r] == 0.f ? 0.f : 1.0f / S[r];
+              const __m256 iv = _mm256_set1_ps(inv);
+              for (int v = 0; v < nv; ++v) _mm256_storeu_ps(od + 8 * v, _mm256_mul_ps(acc[r][v], iv));
+            }
+          }
+      delete ps_;
+      linear(o.data(), M, D, p + "attn_proj.weight", has(p + "attn_proj.bias") ? p + "attn_proj.bias" : "", out);
+      return;
+    }
 #pragma omp parallel for schedule(dynamic, 4) collapse(2)
     for (int s = 0; s < nseq; ++s)
       for (int qi = 0; qi < seqlen; ++qi)
@@ -384,6 +567,7 @@ class Oracle {
           const float inv = S == 0.f ? 0.f : 1.0f / S;
           for (int d = 0; d < hd; ++d) od[d] = acc[d] * inv;
         }
+    delete ps_;
     linear(o.data(), M, D, p + "attn_proj.weight", has(p + "attn_proj.bias") ? p + "attn_proj.bias" : "", out);
   }
 
@@ -484,48 +668,107 @@ class Oracle {
   // conv2d with ggml kernel [KW,KH,IC,OC] (= torch [OC][IC][KH][KW]) f32, stride s, pad p,
   // optional bias (src/dpt_blocks.cpp:18-66, direct f32 semantics).
   Map conv2d(const Map& x, const std::string& wn, const std::string& bn, int stride, int pad) {
+    ProfScope ps_("conv2d");
     const Tensor& Wt = T(wn);
     const int ks = static_cast<int>(Wt.ne[0]), IC = static_cast<int>(Wt.ne[2]), OC = static_cast<int>(Wt.ne[3]);
     const float* w = F(wn);
     const float* b = (!bn.empty() && has(bn)) ? F(bn) : nullptr;
     const int Ho = (x.H + 2 * pad - ks) / stride + 1, Wo = (x.W + 2 * pad - ks) / stride + 1;
     Map y(OC, Ho, Wo);
-#pragma omp parallel for schedule(dynamic, 1)
-    for (int oc = 0; oc < OC; ++oc) {
-      float* out = y.ch(oc);
-      for (int i = 0; i < Ho * Wo; ++i) out[i] = 0.f;
-      for (int ic = 0; ic < IC; ++ic) {
-        const float* in = x.ch(ic);
-        for (int ky = 0; ky < ks; ++ky)
-          for (int kx = 0; kx < ks; ++kx) {
-            const float wv = w[((static_cast<size_t>(oc) * IC + ic) * ks + ky) * ks + kx];
-            for (int oy = 0; oy < Ho; ++oy) {
-              const int iy = oy * stride + ky - pad;
-              if (iy < 0 || iy >= x.H) continue;
-              const float* row = in + static_cast<size_t>(iy) * x.W;
-              float* orow = out + static_cast<size_t>(oy) * Wo;
-              if (stride == 1) {
-                const int x0 = std::max(0, pad - kx), x1 = std::min(Wo, x.W + pad - kx);
-                const float* r2 = row + kx - pad;
-                for (int ox = x0; ox < x1; ++ox) orow[ox] += wv * r2[ox];
-              } else {
-                for (int ox = 0; ox < Wo; ++ox) {
-                  const int ix = ox * stride + kx - pad;
-                  if (ix >= 0 && ix < x.W) orow[ox] += wv * row[ix];
+    // Sixteen output channels per pair of vectors: weights packed [oc/16][ic][tap][16]
+    // (zero beyond OC), each output pixel's sixteen sums held in registers while its
+    // terms are added in the order ic, ky, kx (taps outside the input are skipped, as a
+    // direct convolution does), then the bias. Interior pixels go four at a time.
+    const int KK = ks * ks, nob = (OC + 15) / 16;
+    std::vector<float> wp(static_cast<size_t>(nob) * IC * KK * 16, 0.f);
+    for (int oc = 0; oc < OC; ++oc)
+      for (int ic = 0; ic < IC; ++ic)
+        for (int t = 0; t < KK; ++t)
+          wp[((static_cast<size_t>(oc / 16) * IC + ic) * KK + t) * 16 + oc % 16] =
+              w[(static_cast<size_t>(oc) * IC + ic) * KK + t];
+    const size_t plane = static_cast<size_t>(x.H) * x.W;
+#pragma omp parallel for schedule(dynamic, 1) collapse(2)
+    for (int ob = 0; ob < nob; ++ob)
+      for (int oy = 0; oy < Ho; ++oy) {
+        const float* wb = &wp[static_cast<size_t>(ob) * IC * KK * 16];
+        const int nlane = std::min(16, OC - ob * 16);
+        auto store = [&](int ox, __m256 lo, __m256 hi) {
+          alignas(32) float v[16];
+          _mm256_store_ps(v, lo);
+          _mm256_store_ps(v + 8, hi);
+          for (int j = 0; j < nlane; ++j) {
+            const int oc = ob * 16 + j;
+            y.v[(static_cast<size_t>(oc) * Ho + oy) * Wo + ox] = b ? v[j] + b[oc] : v[j];
+          }
+        };
+        const int iy0 = oy * stride - pad;
+        const bool rows_in = iy0 >= 0 && iy0 + ks <= x.H;
+        int ox = 0;
+        if (rows_in) {
+          // interior run: every tap of pixels ox..ox+3 inside the input
+          const int lo = (pad + stride - 1) / stride;  // first ox whose leftmost tap is >= 0
+          const int hi = (x.W - ks + pad) / stride;    // last ox whose rightmost tap is < W
+          for (; ox < Wo && ox < lo; ++ox) {
+            __m256 a0 = _mm256_setzero_ps(), a1 = _mm256_setzero_ps();
+            conv_pixel(x, wb, IC, ks, stride, pad, oy, ox, plane, a0, a1);
+            store(ox, a0, a1);
+          }
+          for (; ox + 3 <= hi && ox + 3 < Wo; ox += 4) {
+            __m256 a[4][2];
+            for (int r = 0; r < 4; ++r) a[r][0] = a[r][1] = _mm256_setzero_ps();
+            const int ix0 = ox * stride - pad;
+            for (int ic = 0; ic < IC; ++ic) {
+              const float* in = x.v.data() + ic * plane;
+              for (int ky = 0; ky < ks; ++ky) {
+                const float* row = in + static_cast<size_t>(iy0 + ky) * x.W + ix0;
+                for (int kx = 0; kx < ks; ++kx) {
+                  const float* wt = wb + (static_cast<size_t>(ic) * KK + ky * ks + kx) * 16;
+                  const __m256 w0 = _mm256_loadu_ps(wt), w1 = _mm256_loadu_ps(wt + 8);
+                  for (int r = 0; r < 4; ++r) {
+                    const __m256 v = _mm256_set1_ps(row[r * stride + kx]);
+                    a[r][0] = _mm256_add_ps(a[r][0], _mm256_mul_ps(v, w0));
+                    a[r][1] = _mm256_add_ps(a[r][1], _mm256_mul_ps(v, w1));
+                  }
                 }
               }
             }
+            for (int r = 0; r < 4; ++r) store(ox + r, a[r][0], a[r][1]);
           }
+        }
+        for (; ox < Wo; ++ox) {
+          __m256 a0 = _mm256_setzero_ps(), a1 = _mm256_setzero_ps();
+          conv_pixel(x, wb, IC, ks, stride, pad, oy, ox, plane, a0, a1);
+          store(ox, a0, a1);
+        }
       }
-      if (b)
-        for (int i = 0; i < Ho * Wo; ++i) out[i] += b[oc];
-    }
     return y;
+  }
+
+  // One output pixel of conv2d (sixteen output channels), skipping taps outside the input.
+  static void conv_pixel(const Map& x, const float* wb, int IC, int ks, int stride, int pad, int oy, int ox,
+                         size_t plane, __m256& a0, __m256& a1) {
+    const int KK = ks * ks;
+    for (int ic = 0; ic < IC; ++ic) {
+      const float* in = x.v.data() + ic * plane;
+      for (int ky = 0; ky < ks; ++ky) {
+        const int iy = oy * stride + ky - pad;
+        if (iy < 0 || iy >= x.H) continue;
+        for (int kx = 0; kx < ks; ++kx) {
+          const int ix = ox * stride + kx - pad;
+          if (ix < 0 || ix >= x.W) continue;
+          const float* wt = wb + (static_cast<size_t>(ic) * KK + ky * ks + kx) * 16;
+          const __m256 v = _mm256_set1_ps(in[static_cast<size_t>(iy) * x.W + ix]);
+          a0 = _mm256_add_ps(a0, _mm256_mul_ps(v, _mm256_loadu_ps(wt)));
+          a1 = _mm256_add_ps(a1, _mm256_mul_ps(v, _mm256_loadu_ps(wt + 8)));
+        }
+      }
+    }
   }
 
   // conv_transpose2d_p0 with stride == kernel; ggml kernel [KW,KH,OC,IC]
   // (= torch [IC][OC][KH][KW]) (src/dpt_blocks.cpp:68-85).
   Map convT(const Map& x, const std::string& wn, const std::string& bn, int S) {
+    ProfScope ps_("convT");
     const Tensor& Wt = T(wn);
     const int OC = static_cast<int>(Wt.ne[2]), IC = static_cast<int>(Wt.ne[3]);
     const float* w = F(wn);
@@ -1230,6 +1473,9 @@ namespace {
 // (src/engine.cpp:189-229; mono: src/engine.cpp:105-115 and the sky relu of
 // src/dpt_head.cpp:334-338).
 int infer_chw(Handle* h, int H, int W, int want_aux) {
+  struct Dump {
+    ~Dump() { prof_dump("infer"); }
+  } dump_;
   Oracle& o = h->o;
   h->H = H;
   h->W = W;
