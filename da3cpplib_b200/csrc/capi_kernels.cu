@@ -125,6 +125,23 @@ DA3B_API int da3b_attention(const void* qkv, int nseq, int seqlen, int heads, vo
                       st, s);
 }
 
+DA3B_API int da3b_transpose_v(const void* qkv, int nseq, int seqlen, int heads, void* vt, int ld_vt, void* stream) {
+  if (!qkv || !vt || heads <= 0 || nseq < 0 || seqlen < 0 || ld_vt < seqlen || ld_vt % 8) return -100;
+  if (nseq == 0 || seqlen == 0) return 0;
+  return transpose_v(static_cast<const __half*>(qkv), nseq, seqlen, heads, heads * 64, static_cast<__half*>(vt), ld_vt,
+                     static_cast<cudaStream_t>(stream));
+}
+
+DA3B_API int da3b_attention_vt(const void* qkv, const void* vt, int ld_vt, int nseq, int seqlen, int heads, void* out,
+                               void* stream) {
+  if (!qkv || !vt || !out || heads <= 0 || nseq < 0 || seqlen < 0) return -100;
+  if (nseq == 0 || seqlen == 0) return 0;
+  int* st = device_status_word();
+  if (!st) return -101;
+  return attention_tc(static_cast<const __half*>(qkv), static_cast<const __half*>(vt), ld_vt, nseq, seqlen, heads,
+                      heads * 64, static_cast<__half*>(out), 0, st, static_cast<cudaStream_t>(stream));
+}
+
 DA3B_API int da3b_upsample_nhwc(const void* in, int B, int hs, int ws, int C, void* out, int H, int W, void* stream) {
   if (!in || !out || B < 0 || hs <= 0 || ws <= 0 || H <= 0 || W <= 0 || C <= 0 || C % 8) return -100;
   return upsample_ac(static_cast<const __half*>(in), B, hs, ws, C, static_cast<__half*>(out), H, W, nullptr,

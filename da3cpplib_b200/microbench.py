@@ -250,7 +250,7 @@ def main(argv=None):
         from . import Model, synth
 
         n_sc, V, HW = args.scenes, 8, 504
-        m = Model(synth.ensure_gguf("da3-l"), 0)
+        m = Model(synth.ensure_gguf("da3-l", stress=True), 0)
         rgb = torch.randint(0, 256, (n_sc * V, HW, HW, 3), generator=gen, device="cuda", dtype=torch.uint8)
         depth = torch.empty((n_sc * V, HW, HW), device="cuda")
         conf = torch.empty_like(depth)
@@ -289,7 +289,7 @@ def main(argv=None):
 
         from . import synth
 
-        ctx = L.da3b_load(synth.ensure_gguf("da3-t").encode(), 0)
+        ctx = L.da3b_load(synth.ensure_gguf("da3-t", stress=True).encode(), 0)
         g = 288
         rng = np.random.default_rng(7)
         t = (np.arange(g) + 0.5) / g * 2 - 1

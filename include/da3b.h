@@ -66,6 +66,15 @@ DA3B_API int da3b_linear_resid_f32(const void* x, int M, int K, int lda, const v
  * the layout of the QKV linear's output), out: f16 [nseq*seqlen][heads*64]. */
 DA3B_API int da3b_attention(const void* qkv, int nseq, int seqlen, int heads, void* out, void* stream);
 
+/* The two halves of da3b_attention, for callers that keep V transposed (the engine's
+ * QKV GEMM epilogue writes it that way): da3b_transpose_v writes V^T f16
+ * [nseq][heads][64][ld_vt] (ld_vt >= seqlen, a multiple of 8; columns beyond seqlen are
+ * never read), and da3b_attention_vt runs the flash-attention kernel alone on q, k from
+ * qkv and that V^T. Same arithmetic as da3b_attention. */
+DA3B_API int da3b_transpose_v(const void* qkv, int nseq, int seqlen, int heads, void* vt, int ld_vt, void* stream);
+DA3B_API int da3b_attention_vt(const void* qkv, const void* vt, int ld_vt, int nseq, int seqlen, int heads, void* out,
+                               void* stream);
+
 /* Capacity of the fixed V^T scratch of da3b_attention_noalloc, in bytes (32 MiB):
  * nseq * heads*64 * round_up(seqlen, 8) * 2 must not exceed it, e.g. 11 ViT-L images
  * of 1370 tokens, or one 8-view scene of 1297 tokens per view at 16 heads. */
