@@ -8,6 +8,7 @@
 #include "da3b.h"
 #include "kernels.h"
 #include "ops.h"
+#include "ptx.cuh"
 
 namespace da3b {
 
@@ -33,6 +34,35 @@ int pack_conv_weight(const float* w, int OC, int IC, int ks, __half* out, cudaSt
   if (blocks > 65535) blocks = 65535;
   k_pack_conv<<<static_cast<unsigned>(blocks), threads, 0, s>>>(w, OC, IC, ks, icp, out);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// Wait-timeout probe: an mbarrier that nothing ever arrives on, waited on by both warps
+// with the given limit through the same bounded wait every pipeline uses. When
+// use_tmem is set, warp 0 first allocates 32 TMEM columns and frees them after the
+// failed wait, as the pipelined kernels do on their timeout path. elapsed (optional)
+// receives the nanoseconds thread 0 spent waiting.
+__global__ void k_wait_probe(int* status, uint64_t limit_ns, int use_tmem, unsigned long long* elapsed) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t slot;
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (use_tmem && warp == 0) tmem_alloc(&slot, 32);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint64_t t0 = globaltimer_ns();
+  const bool ok = mbar_wait_warp(&bar, 0, status, kStatusTimeoutFull, limit_ns);
+  const uint64_t t1 = globaltimer_ns();
+  tc_fence_before();
+  __syncthreads();
+  if (use_tmem && warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(slot, 32);
+  }
+  if (threadIdx.x == 0 && elapsed) *elapsed = ok ? 0ull : static_cast<unsigned long long>(t1 - t0);
 }
 
 }  // namespace da3b
@@ -123,6 +153,15 @@ DA3B_API int da3b_attention(const void* qkv, int nseq, int seqlen, int heads, vo
   if (rc) return rc;
   return attention_tc(static_cast<const __half*>(qkv), vt, ld, nseq, seqlen, heads, D, static_cast<__half*>(out), 0,
                       st, s);
+}
+
+DA3B_API int da3b_debug_wait_timeout(unsigned long long limit_ns, int use_tmem, int* status_dev,
+                                     unsigned long long* elapsed_dev, void* stream) {
+  if (limit_ns == 0 || limit_ns > 1000000000ull) return -100;  // at most 1 s
+  int* st = status_dev ? status_dev : device_status_word();
+  if (!st) return -101;
+  k_wait_probe<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(st, limit_ns, use_tmem ? 1 : 0, elapsed_dev);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 DA3B_API int da3b_transpose_v(const void* qkv, int nseq, int seqlen, int heads, void* vt, int ld_vt, void* stream) {

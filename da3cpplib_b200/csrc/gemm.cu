@@ -980,6 +980,24 @@ int make_tmap_2d(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, 
   return r == CUDA_SUCCESS ? 0 : -3;
 }
 
+// 2-D tensor map of any element type over a row-major [rows][cols] matrix (ld elements
+// between rows), box = box_cols x box_rows, the given swizzle, zero fill out of range.
+int make_tmap_2d_typed(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int elem_bytes, int rows,
+                       int cols, int ld, int box_cols, int box_rows, CUtensorMapSwizzle swz) {
+  PFN_tmapEncodeTiled enc = tmap_encoder();
+  if (!enc) return -1;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (static_cast<long>(ld) * elem_bytes) % 16 || box_rows > 256 ||
+      box_rows < 1 || box_cols > 256 || box_cols < 1 || (box_cols * elem_bytes) % 16)
+    return -2;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * elem_bytes};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -3;
+}
+
 // 4-D f16 tensor map over an NHWC tensor [B][H][W][C] (row pitch C), box =
 // 64 channels x bw x bh x 1, 128B swizzle, zero fill out of range (conv padding).
 int make_tmap_nhwc(CUtensorMap* map, const void* ptr, int B, int H, int W, int C, int bw, int bh) {

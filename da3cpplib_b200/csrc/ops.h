@@ -12,6 +12,8 @@ namespace da3b {
 // ------------------------------------------------------------------ GEMM engine (gemm.cu)
 int make_tmap_2d(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows);
 int make_tmap_nhwc(CUtensorMap* map, const void* ptr, int B, int H, int W, int C, int bw, int bh);
+int make_tmap_2d_typed(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int elem_bytes, int rows,
+                       int cols, int ld, int box_cols, int box_rows, CUtensorMapSwizzle swz);
 int make_tmap_nhwc_planes(CUtensorMap* map, const void* ptr, int B, int H, int W, int C, int bw, int bh);
 int gemm_launch(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeom& g, const EpiArgs& e,
                 int* status, cudaStream_t stream, int max_ctas);

@@ -66,15 +66,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete. Returns false
-// (after recording `code`) on timeout or when another role already failed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+// (after recording `code`) on timeout or when another role already failed. The limit
+// is kWaitNs except in the wait-timeout probe (da3b_debug_wait_timeout).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
+                                          uint64_t limit_ns = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (*reinterpret_cast<volatile int*>(status) != 0) return false;
-      if (globaltimer_ns() - t0 > kWaitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         atomicCAS(status, 0, code);
         return false;
       }
@@ -85,8 +87,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
 // Warp-uniform bounded wait for warps that issue warp-collective (.sync.aligned)
 // tcgen05 instructions afterwards: every lane waits, and the result is true only if
 // the wait succeeded in all lanes, so a failure can never leave a warp divergent.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code) {
-  const bool ok = mbar_wait(bar, parity, status, code);
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code,
+                                               uint64_t limit_ns = kWaitNs) {
+  const bool ok = mbar_wait(bar, parity, status, code, limit_ns);
   return __all_sync(0xffffffffu, ok);
 }
 

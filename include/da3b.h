@@ -66,6 +66,17 @@ DA3B_API int da3b_linear_resid_f32(const void* x, int M, int K, int lda, const v
  * the layout of the QKV linear's output), out: f16 [nseq*seqlen][heads*64]. */
 DA3B_API int da3b_attention(const void* qkv, int nseq, int seqlen, int heads, void* out, void* stream);
 
+/* Wait-timeout probe (tests of the failure path every pipelined kernel shares): one
+ * CTA waits, through the kernels' bounded mbarrier wait, on a barrier that nothing
+ * arrives on, with a limit of limit_ns (1 ns .. 1 s) instead of the kernels' 2 s.
+ * The wait runs out, the status word becomes 1 (a timed-out wait), and the kernel
+ * returns; with use_tmem it first allocates tensor memory and frees it after the
+ * failed wait, the way the kernels do. status_dev = NULL uses the library's status
+ * word (read and cleared by da3b_device_status); elapsed_dev (may be NULL) receives
+ * the nanoseconds waited. No GPU fault is involved: the context stays usable. */
+DA3B_API int da3b_debug_wait_timeout(unsigned long long limit_ns, int use_tmem, int* status_dev,
+                                     unsigned long long* elapsed_dev, void* stream);
+
 /* The two halves of da3b_attention, for callers that keep V transposed (the engine's
  * QKV GEMM epilogue writes it that way): da3b_transpose_v writes V^T f16
  * [nseq][heads][64][ld_vt] (ld_vt >= seqlen, a multiple of 8; columns beyond seqlen are

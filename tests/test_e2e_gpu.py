@@ -105,13 +105,21 @@ def _check_single(name, size, aux=False, stress=True, layers=False):
                 report[f"{tag}_feat{o}_localtok"] = token_rel(f[:, :E], rf[:, :E])
                 report[f"{tag}_feat{o}_localnmax"] = nmax(f[:, :E], rf[:, :E])
         if layers and tag != "q8":
+            # per-block residual stream, LayerNormed: the patch tokens (the rows whose
+            # normalised values become the head's features) are bounded in both pairings;
+            # the CLS row only against the f32-activation oracle. Its residual starts at
+            # cls_token + pos_embed[0] (~0.03) while the blocks add ~0.1, so after the
+            # normalisation the reference's own Q8_0 activation rounding of that one row
+            # is about 1% (printed as floor_x*_cls), which no f16 path can sit closer to.
             orc = oq if tag == "ref" else of
             worst = 0.0
             for i in range(m.depth):
                 g = _ln_rows(resid[i])
                 r = _ln_rows(orc.residual(i))
-                e = nmax(g, r)
+                e = nmax(g[1:], r[1:])
                 report[f"{tag}_x{i}_nmax"] = e
+                c = nmax(g[:1], r[:1])
+                report[f"{tag}_x{i}_" + ("clsnmax" if tag == "kern" else "clsinfo")] = c
                 worst = max(worst, e)
             report[f"{tag}_xworst_info"] = worst
         report[f"{tag}_depth"] = median_rel(out["depth"][0], ref["depth"])
@@ -130,6 +138,11 @@ def _check_single(name, size, aux=False, stress=True, layers=False):
         report["floor_conf"] = median_rel(reff["conf"], refq["conf"])
     if aux and "aux" in refq:
         report["floor_rays"] = median_rel(reff["aux"], refq["aux"])
+    if layers:
+        for i in range(m.depth):
+            a, b = _ln_rows(oq.residual(i)), _ln_rows(of.residual(i))
+            report[f"floor_x{i}_patch"] = nmax(b[1:], a[1:])
+            report[f"floor_x{i}_cls"] = nmax(b[:1], a[:1])
     for o in range(4):
         a, b = featq[o].reshape(feats[o].shape), featf[o].reshape(feats[o].shape)
         if m.cat_token:
@@ -172,7 +185,7 @@ def _assert(r, depth=True):
     checked = 0
     for k, v in r.items():
         lim = _limit(k, depth)
-        if lim is None:
+        if lim is None or k.startswith("floor"):
             continue
         checked += 1
         if not v <= lim:
