@@ -44,6 +44,38 @@ int dequant_q8_0(const void* q8, int rows, int K, __half* out, int ldo, cudaStre
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+// One launch dequantising up to four Q8_0 matrices (a ViT block's linears) into dense
+// f16 [rows][K]: one thread per 32-element block, f16(d * q) like k_dequant_q8_0.
+__global__ void k_dequant_q8_0_segs(Q8Segs g) {
+  for (long idx = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < g.total;
+       idx += static_cast<long>(gridDim.x) * blockDim.x) {
+    int k = 0;
+    while (k + 1 < g.n && idx >= g.s[k + 1].first) ++k;
+    const Q8Seg& sg = g.s[k];
+    const long li = idx - sg.first;
+    const int r = static_cast<int>(li / sg.nblk), b = static_cast<int>(li % sg.nblk);
+    const uint8_t* blk = sg.q8 + static_cast<size_t>(li) * 34;
+    const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(blk[0] | (blk[1] << 8))));
+    uint4 packed[4];
+    __half2* h = reinterpret_cast<__half2*>(packed);
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      h[i] = __floats2half2_rn(d * static_cast<float>(static_cast<int8_t>(blk[2 + 2 * i])),
+                               d * static_cast<float>(static_cast<int8_t>(blk[3 + 2 * i])));
+    uint4* o4 = reinterpret_cast<uint4*>(sg.out + static_cast<size_t>(r) * sg.nblk * 32 + b * 32);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o4[i] = packed[i];
+  }
+}
+
+int dequant_q8_0_segs(const Q8Segs& g, cudaStream_t s) {
+  if (g.n <= 0 || g.n > 4 || g.total <= 0) return -1;
+  long blocks = (g.total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  k_dequant_q8_0_segs<<<static_cast<unsigned>(blocks), 256, 0, s>>>(g);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
 __global__ void k_f32_to_f16(const float* __restrict__ in, __half* __restrict__ out, size_t n) {
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)

@@ -103,6 +103,7 @@ struct Plan {
 Engine::~Engine() {
   if (device_ >= 0) cudaSetDevice(device_);
   plans_.clear();
+  if (wstage_) cudaFree(wstage_);
   model_.reset();
 }
 
@@ -125,6 +126,12 @@ std::unique_ptr<Engine> Engine::create(const std::string& path, int device, std:
   }
   e->model_ = DeviceModel::load(path, err);
   if (!e->model_) return nullptr;
+  if (e->model_->q8_resident &&
+      cudaMalloc(&e->wstage_, e->model_->block_stage_elems * sizeof(__half)) != cudaSuccess) {
+    e->wstage_ = nullptr;
+    if (err) *err = "cannot allocate the block weight staging buffer";
+    return nullptr;
+  }
   if (const char* g = getenv("DA3B_GRAPH")) e->use_graph_ = strcmp(g, "0") != 0;
   return e;
 }
@@ -503,6 +510,25 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
 
   for (int i = 0; i < c.depth; ++i) {
     const Block& b = m.blk[i];
+    // this block's linears: the resident f16 planes, or its Q8_0 bytes dequantised into
+    // the staging buffer (in stream order after the previous block's last GEMM)
+    const __half *w_qkv = b.qkv.w, *w_proj = b.proj.w, *w_fc1 = b.fc1.w, *w_fc2 = b.fc2.w;
+    if (m.q8_resident) {
+      Q8Segs g;
+      const Lin* L4[4] = {&b.qkv, &b.proj, &b.fc1, &b.fc2};
+      const __half** ptrs[4] = {&w_qkv, &w_proj, &w_fc1, &w_fc2};
+      __half* dst = wstage_;
+      long first = 0;
+      for (int k = 0; k < 4; ++k) {
+        g.s[k] = Q8Seg{L4[k]->q8, dst, L4[k]->N, L4[k]->K / 32, first};
+        *ptrs[k] = dst;
+        first += static_cast<long>(L4[k]->N) * (L4[k]->K / 32);
+        dst += static_cast<size_t>(L4[k]->N) * L4[k]->K;
+      }
+      g.n = 4;
+      g.total = first;
+      CK(dequant_q8_0_segs(g, s));
+    }
     if (select && i == c.alt_start - 1) {
       // reference-view selection on the views' token 0 after blocks [0, alt_start-1)
       // (pass A, src/dino_backbone.cpp:427-441); the local blocks before are per view,
@@ -526,7 +552,7 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
       e.vt_seqlen = seqlen;
       e.vt_ld = ld_vt;
       e.vt_d = D;
-      CK(gemm_linear(p.xn, M, D, D, b.qkv.w, b.qkv.N, b.qkv.ldw, 0, e, status_, s));
+      CK(gemm_linear(p.xn, M, D, D, w_qkv, b.qkv.N, b.qkv.ldw, 0, e, status_, s));
     }
     if (b.qng || use_rope) {
       const float* cs = use_rope ? (global ? p.rn_cos : p.rl_cos) : nullptr;
@@ -541,14 +567,14 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
       e.ld_resid = D;
       e.bias = b.proj.b;
       e.scale = b.ls1;
-      CK(gemm_linear(p.attn, M, D, D, b.proj.w, D, b.proj.ldw, 0, e, status_, s));
+      CK(gemm_linear(p.attn, M, D, D, w_proj, D, b.proj.ldw, 0, e, status_, s));
     }
     // ---- MLP half
     CK(layernorm_f32(p.x, D, M, D, b.n2g, b.n2b, c.ln_eps, p.xn, D, 0, 0, 0, 0, s, q8));
     {
       EpiArgs e = epi_f16(p.hid, b.fc1.N, b.fc1.b, kActGelu);
       e.q8 = q8;
-      CK(gemm_linear(p.xn, M, D, D, b.fc1.w, b.fc1.N, b.fc1.ldw, 0, e, status_, s));
+      CK(gemm_linear(p.xn, M, D, D, w_fc1, b.fc1.N, b.fc1.ldw, 0, e, status_, s));
     }
     {
       EpiArgs e = epi_default();
@@ -557,7 +583,7 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
       e.ld_resid = D;
       e.bias = b.fc2.b;
       e.scale = b.ls2;
-      CK(gemm_linear(p.hid, M, b.fc2.K, b.fc2.K, b.fc2.w, D, b.fc2.ldw, 0, e, status_, s));
+      CK(gemm_linear(p.hid, M, b.fc2.K, b.fc2.K, w_fc2, D, b.fc2.ldw, 0, e, status_, s));
     }
     if (p.resid_cap &&
         cudaMemcpyAsync(p.resid_cap + static_cast<size_t>(i) * M * D, p.x, static_cast<size_t>(M) * D * sizeof(float),

@@ -107,6 +107,9 @@ class Engine {
   int pyramid(Plan& p, const void* fuse_weights, __half* u_out, cudaStream_t s);
 
   std::unique_ptr<DeviceModel> model_;
+  // f16 staging buffer of one ViT block's four linears (qkv | proj | fc1 | fc2), filled
+  // from the resident Q8_0 bytes ahead of each block when the model keeps them quantised
+  __half* wstage_ = nullptr;
   int device_ = 0;
   int* status_ = nullptr;
   bool use_graph_ = true;

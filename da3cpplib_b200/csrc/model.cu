@@ -5,6 +5,7 @@
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "ops.h"
@@ -142,7 +143,8 @@ float* DeviceModel::up_f32(const std::string& name, bool required, std::string* 
   return d;
 }
 
-bool DeviceModel::lin_q8(const std::string& wname, const std::string& bname, Lin& out, std::string* err) {
+bool DeviceModel::lin_q8(const std::string& wname, const std::string& bname, Lin& out, std::string* err,
+                         bool keep_q8) {
   const GgufTensor* t = file.tensor(wname);
   if (!t) { if (err) *err = "missing tensor " + wname; return false; }
   const int K = static_cast<int>(t->ne[0]), N = static_cast<int>(t->ne[1]);
@@ -150,6 +152,17 @@ bool DeviceModel::lin_q8(const std::string& wname, const std::string& bname, Lin
   out.K = K;
   out.ldw = K;
   if (K % 32) { if (err) *err = "K not a multiple of 32 in " + wname; return false; }
+  if (keep_q8 && t->type == 8) {
+    // resident as the GGUF's Q8_0 bytes; dequantised per forward into the staging buffer
+    uint8_t* q = static_cast<uint8_t*>(dalloc(t->nbytes));
+    if (!q || cudaMemcpy(q, t->data, t->nbytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+      if (err) *err = "Q8_0 upload failed for " + wname;
+      return false;
+    }
+    out.q8 = q;
+    if (!bname.empty()) out.b = up_f32(bname, false, err);
+    return true;
+  }
   out.w = static_cast<__half*>(dalloc(static_cast<size_t>(N) * K * 2));
   if (!out.w) { if (err) *err = "out of device memory"; return false; }
   if (t->type == 8) {
@@ -285,6 +298,11 @@ std::unique_ptr<DeviceModel> DeviceModel::load(const std::string& path, std::str
   if (!(m->norm_g = m->up_f32("vit.norm.weight", true, err))) return nullptr;
   m->norm_b = m->up_f32("vit.norm.bias", false, err);
   m->blk.resize(c.depth);
+  {
+    const GgufTensor* q0 = m->file.tensor("vit.blk.0.attn_qkv.weight");
+    const char* f16 = getenv("DA3B_F16_WEIGHTS");
+    m->q8_resident = q0 && q0->type == 8 && !(f16 && f16[0] == '1');
+  }
   for (int i = 0; i < c.depth; ++i) {
     const std::string p = "vit.blk." + std::to_string(i) + ".";
     Block& b = m->blk[i];
@@ -301,14 +319,25 @@ std::unique_ptr<DeviceModel> DeviceModel::load(const std::string& path, std::str
       b.knb = m->up_f32(p + "attn_knorm.bias", false, err);
       if (!b.qng || !b.kng) return nullptr;
     }
-    if (!m->lin_q8(p + "attn_qkv.weight", p + "attn_qkv.bias", b.qkv, err)) return nullptr;
-    if (!m->lin_q8(p + "attn_proj.weight", p + "attn_proj.bias", b.proj, err)) return nullptr;
-    if (!m->lin_q8(p + "mlp_fc1.weight", p + "mlp_fc1.bias", b.fc1, err)) return nullptr;
-    if (!m->lin_q8(p + "mlp_fc2.weight", p + "mlp_fc2.bias", b.fc2, err)) return nullptr;
-    if (b.qkv.N != 3 * D || b.qkv.K != D || b.fc1.K != D || b.fc2.N != D) {
+    const bool kq = m->q8_resident;
+    if (!m->lin_q8(p + "attn_qkv.weight", p + "attn_qkv.bias", b.qkv, err, kq)) return nullptr;
+    if (!m->lin_q8(p + "attn_proj.weight", p + "attn_proj.bias", b.proj, err, kq)) return nullptr;
+    if (!m->lin_q8(p + "mlp_fc1.weight", p + "mlp_fc1.bias", b.fc1, err, kq)) return nullptr;
+    if (!m->lin_q8(p + "mlp_fc2.weight", p + "mlp_fc2.bias", b.fc2, err, kq)) return nullptr;
+    if (b.qkv.N != 3 * D || b.qkv.K != D || b.fc1.K != D || b.fc2.N != D || b.proj.N != D || b.proj.K != D ||
+        b.fc2.K != b.fc1.N) {
       if (err) *err = "inconsistent block shapes in block " + std::to_string(i);
       return nullptr;
     }
+    // a model whose block linears are Q8_0 keeps all of them quantised; a block with
+    // another weight type there is rejected rather than mixed
+    if (kq && !(b.qkv.q8 && b.proj.q8 && b.fc1.q8 && b.fc2.q8)) {
+      if (err) *err = "block " + std::to_string(i) + " mixes Q8_0 and other linear weight types";
+      return nullptr;
+    }
+    const size_t st = static_cast<size_t>(b.qkv.N) * D + static_cast<size_t>(D) * D +
+                      static_cast<size_t>(b.fc1.N) * D * 2;
+    if (st > m->block_stage_elems) m->block_stage_elems = st;
   }
   if (m->file.tensor("cam.bb0.weight")) {
     CamDec& cd = m->camdec;

@@ -34,9 +34,12 @@ struct Config {
   bool is_da2() const { return arch == "depthanything2"; }
 };
 
-// f16 GEMM weight [N][K] (ld = ldw) with optional f32 bias [N].
+// f16 GEMM weight [N][K] (ld = ldw) with optional f32 bias [N]. A ViT block linear
+// kept quantised holds its GGUF Q8_0 bytes [N][K/32][34] in q8 instead (w == nullptr);
+// the engine dequantises it into its per-block staging buffer ahead of the block.
 struct Lin {
   __half* w = nullptr;
+  const uint8_t* q8 = nullptr;
   float* b = nullptr;
   int N = 0, K = 0, ldw = 0;
 };
@@ -109,6 +112,11 @@ class DeviceModel {
   Head head;
   CamDec camdec;
   size_t weight_bytes = 0;
+  // true: the ViT block linears stay resident as Q8_0 (Lin::q8) and block_stage_elems
+  // is the f16 element count of one block's four linears (the staging buffer size);
+  // false ($DA3B_F16_WEIGHTS=1 at load): they are dequantised once to resident f16.
+  bool q8_resident = false;
+  size_t block_stage_elems = 0;
 
   // host views used for per-resolution tables
   const float* pos_embed_host() const;
@@ -117,7 +125,8 @@ class DeviceModel {
   std::vector<void*> allocs_;
   void* dalloc(size_t bytes);
   float* up_f32(const std::string& name, bool required, std::string* err);
-  bool lin_q8(const std::string& wname, const std::string& bname, Lin& out, std::string* err);
+  bool lin_q8(const std::string& wname, const std::string& bname, Lin& out, std::string* err,
+              bool keep_q8 = false);
   bool lin_f32_1x1(const std::string& wname, const std::string& bname, Lin& out, std::string* err);
   bool conv(const std::string& wname, const std::string& bname, Conv& out, std::string* err);
   bool convT(const std::string& wname, const std::string& bname, int S, ConvT& out, std::string* err);

@@ -43,6 +43,20 @@ EpiArgs epi_default();
 
 // ------------------------------------------------------------------ elementwise (elementwise.cu)
 int dequant_q8_0(const void* q8, int rows, int K, __half* out, int ldo, cudaStream_t s);
+// Up to four Q8_0 matrices [rows][K/32][34 B] -> dense f16 [rows][K] in one launch;
+// `first` is each segment's first 32-element block in the launch's block numbering.
+struct Q8Seg {
+  const uint8_t* q8;
+  __half* out;
+  int rows, nblk;
+  long first;
+};
+struct Q8Segs {
+  Q8Seg s[4];
+  int n;
+  long total;
+};
+int dequant_q8_0_segs(const Q8Segs& g, cudaStream_t s);
 int f32_to_f16(const float* in, __half* out, size_t n, cudaStream_t s);
 
 // Per-device status word (allocated on first use for the current device).

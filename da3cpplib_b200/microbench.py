@@ -77,7 +77,7 @@ def main(argv=None):
     from . import _lib
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("--part", default="all", choices=["A", "B", "attn", "up", "pre", "ray", "out2", "c4", "all"])
+    ap.add_argument("--part", default="all", choices=["A", "A8", "B", "attn", "up", "pre", "ray", "out2", "c4", "all"])
     ap.add_argument("--scenes", type=int, default=16, help="c4: scenes of 8 views")
     ap.add_argument("--m", type=int, default=0, help="Part A: only this M")
     ap.add_argument("--kn", default="", help="Part A: only this K,N (e.g. 1024,4096)")
@@ -142,6 +142,39 @@ def main(argv=None):
                       "l2": "inputs exceed L2" if (M * K + M * N) * 2 > 126e6 else "inputs fit in L2"})
                 del x, y
             del raw, W
+
+    if args.part in ("A8", "all"):
+        # the int8 route (tcgen05.mma kind::i8, ggml-exact per-block rescale) against the
+        # f16 GEMM on the same shapes; TFLOP/s counts 2 M N K operations for both
+        kns = ((1024, 4096), (4096, 1024)) if not args.kn else (tuple(int(v) for v in args.kn.split(",")),)
+        ms_set = (10960, 87680) if not args.m else (args.m,)
+        for K, N in kns:
+            raw = q8_0_weights(torch, N, K, gen)
+            qw = torch.empty((N, K), dtype=torch.int8, device="cuda")
+            dwt = torch.empty((K // 32, N), dtype=torch.float32, device="cuda")
+            if L.da3b_repack_q8_0(P(raw), N, K, P(qw), P(dwt), S):
+                raise RuntimeError("repack failed")
+            for M in ms_set:
+                x = torch.randn((M, K), generator=gen, device="cuda")
+                q = torch.empty((M, K), dtype=torch.int8, device="cuda")
+                d = torch.empty((M, K // 32), dtype=torch.float32, device="cuda")
+                y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+
+                def quant():
+                    if L.da3b_quantize_q8_0(P(x), M, K, P(q), P(d), S):
+                        raise RuntimeError("quantize failed")
+
+                def run():
+                    rc = L.da3b_linear_q8q8_i8(P(q), P(d), M, K, P(qw), P(dwt), N, None, P(y), N, S)
+                    if rc:
+                        raise RuntimeError(f"da3b_linear_q8q8_i8 rc={rc}")
+
+                qms = timeit(quant)
+                ms = timeit(run)
+                emit("A8", f"M={M} K={K} N={N} int8 kind::i8", ms, 2.0 * M * K * N,
+                     {"quantize_ms": round(qms, 4)})
+                del x, q, d, y
+            del raw, qw, dwt
 
     if args.part in ("B", "all"):
         for C in (CONV_C if not args.c else (args.c,)):

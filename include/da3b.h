@@ -66,6 +66,22 @@ DA3B_API int da3b_linear_resid_f32(const void* x, int M, int K, int lda, const v
  * the layout of the QKV linear's output), out: f16 [nseq*seqlen][heads*64]. */
 DA3B_API int da3b_attention(const void* qkv, int nseq, int seqlen, int heads, void* out, void* stream);
 
+/* Q8_0 x Q8_0 linear on the int8 tensor cores (tcgen05.mma kind::i8), bit-exact with the
+ * reference's CPU ggml_mul_mat(W_q8_0, x) (src/ggml_extend.hpp:6-10): x quantised per
+ * 32-element block (da3b_quantize_q8_0), exact int32 block dot products, and
+ * y[m][n] = sum over blocks b in order of float(isum_b) * (d_w * d_x) (+ bias[n]) in
+ * explicitly rounded f32. The product path uses the f16 GEMM (da3b_linear_f16); this
+ * entry point is the measured int8 route and a reference-exact linear.
+ *   da3b_quantize_q8_0: x f32 [M][K] -> q int8 [M][K], d f32 [M][K/32] (the f16 scale).
+ *   da3b_repack_q8_0:   GGUF Q8_0 rows [N][K/32][34 B] -> qw int8 [N][K] and the scales
+ *                       transposed, dw_t f32 [K/32][N].
+ *   da3b_linear_q8q8_i8: K % 128 == 0, N % 128 == 0, y f32 [M][ldy] (16-byte aligned,
+ *                       ldy % 4 == 0), bias f32 [N] or NULL. */
+DA3B_API int da3b_quantize_q8_0(const float* x, int M, int K, void* q_int8, float* d, void* stream);
+DA3B_API int da3b_repack_q8_0(const void* q8, int N, int K, void* qw_int8, float* dw_t, void* stream);
+DA3B_API int da3b_linear_q8q8_i8(const void* qx, const float* dx, int M, int K, const void* qw, const float* dw_t,
+                                 int N, const float* bias, float* y, int ldy, void* stream);
+
 /* Wait-timeout probe (tests of the failure path every pipelined kernel shares): one
  * CTA waits, through the kernels' bounded mbarrier wait, on a barrier that nothing
  * arrives on, with a limit of limit_ns (1 ns .. 1 s) instead of the kernels' 2 s.

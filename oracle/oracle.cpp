@@ -1388,6 +1388,30 @@ OR_API int or_interp_pos_embed(const float* pos_embed, int embed, int grid, floa
   return 0;
 }
 
+// linear() (src/ggml_extend.hpp:6-10) of x f32 [M][K] with a Q8_0 weight given as GGUF
+// bytes [N][K/32][34] and an optional f32 bias [N]: act_quant = 1 follows ggml's Q8_0 x
+// Q8_0 CPU dot product, 0 the f32 path. y f32 [M][N].
+OR_API int or_linear_q8(const float* x, int M, int K, const uint8_t* wq8, int N, const float* bias, int act_quant,
+                        float* y) {
+  Oracle o;
+  o.c.act_quant = act_quant;
+  Tensor w;
+  w.data = wq8;
+  w.type = 8;
+  w.ne[0] = K;
+  w.ne[1] = N;
+  o.t["w"] = w;
+  if (bias) {
+    Tensor b;
+    b.data = bias;
+    b.type = 0;
+    b.ne[0] = N;
+    o.t["b"] = b;
+  }
+  o.linear(x, M, K, "w", bias ? "b" : "", y);
+  return 0;
+}
+
 OR_API int or_select_saddle(const float* cls, int S, int embed) {
   std::vector<std::vector<float>> c(S);
   for (int s = 0; s < S; ++s) c[s].assign(cls + static_cast<size_t>(s) * embed, cls + static_cast<size_t>(s + 1) * embed);

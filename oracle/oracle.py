@@ -157,6 +157,8 @@ def lib():
         L.or_interp_pos_embed.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int,
                                           ctypes.c_int, ctypes.c_void_p]
         L.or_select_saddle.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+        L.or_linear_q8.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                   ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
         L.or_get.restype = ctypes.c_int64
         L.or_get.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.POINTER(ctypes.c_float))]
         L.or_dims.argtypes = [ctypes.c_void_p] + [ctypes.POINTER(ctypes.c_int)] * 6
@@ -562,3 +564,16 @@ def select_saddle(cls, impl="oracle"):
     L, pre = _impl_lib(impl)
     c = np.ascontiguousarray(cls, dtype=np.float32)
     return int(getattr(L, pre + "select_saddle")(c.ctypes.data, c.shape[0], c.shape[1]))
+
+
+def linear_q8(x, wq8, N, bias=None, act_quant=True):
+    """linear() of x f32 [M][K] with a Q8_0 weight (GGUF bytes [N][K/32][34]); act_quant
+    follows ggml's Q8_0 x Q8_0 CPU dot product. Returns y f32 [M][N]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    w = np.ascontiguousarray(wq8, dtype=np.uint8)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    y = np.zeros((M, N), np.float32)
+    lib().or_linear_q8(x.ctypes.data, M, K, w.ctypes.data, N, b.ctypes.data if b is not None else None,
+                       int(act_quant), y.ctypes.data)
+    return y

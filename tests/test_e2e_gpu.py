@@ -351,3 +351,38 @@ def test_da2_matches_transformers(cuda, tag):
     assert median_rel(lg, z[tag + "_logits"]) <= 1e-2
     assert nmax(lg, z[tag + "_logits"]) <= 3e-2
     assert median_rel(out["depth"][0], z[tag + "_depth"]) <= 1e-2
+
+
+def test_q8_resident_weights_match_load_time_f16(cuda):
+    """ViT block linears resident as Q8_0 and dequantised ahead of each block (default)
+    give the same bits as the load-time f16 planes ($DA3B_F16_WEIGHTS=1): both round
+    d * q to f16 the same way. The device memory each model takes at load is printed."""
+    import os
+
+    import torch
+
+    from da3cpplib_b200 import Model, synth
+
+    path = synth.ensure_gguf("da3-t", stress=True)
+    imgs = np.stack([synth.image(synth.IMAGE_SEED, i, 112, 112) for i in range(3)])
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    a = Model(path, 0)
+    torch.cuda.synchronize()
+    used_q8 = free0 - torch.cuda.mem_get_info()[0]
+    out_a = a.infer(imgs, views_per_scene=3, rays=True)
+    a.close()
+    os.environ["DA3B_F16_WEIGHTS"] = "1"
+    try:
+        torch.cuda.synchronize()
+        free1 = torch.cuda.mem_get_info()[0]
+        b = Model(path, 0)
+        torch.cuda.synchronize()
+        used_f16 = free1 - torch.cuda.mem_get_info()[0]
+        out_b = b.infer(imgs, views_per_scene=3, rays=True)
+        b.close()
+    finally:
+        del os.environ["DA3B_F16_WEIGHTS"]
+    for k in out_a:
+        assert np.array_equal(out_a[k], out_b[k]), k
+    print(f"\n[weights] device bytes at load: Q8_0-resident {used_q8}, f16 {used_f16}")
