@@ -22,6 +22,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "kernels.h"
@@ -340,15 +341,372 @@ __global__ void __launch_bounds__(192, 2)
   }
 }
 
+// ---------------------------------------------------------------- ping-pong kernel
+// Two 128-query tiles per CTA share every 128-key K / V^T tile, and the two softmax
+// warpgroups alternate with the tensor core:
+//   warp 0     TMA: per key tile of 128 the K tile [128 keys][64] (128B swizzle) and
+//              V^T as two [64 dims][64 keys] halves, into a 4-stage ring;
+//   warp 1     one thread issues, per key tile j and query tile t, S_t = Q_t K_j^T
+//              (M=128, N=128, K=64; Q_t read from TMEM) and, once softmax t published
+//              P_t, O_t += P_t [V_j^T; 1; 0] (M=128, N=80, K=128; P_t read from TMEM);
+//   warps 2-5  softmax of query tile 0, warps 6-9 of query tile 1: thread = query row
+//              (its TMEM lane); S_t read into registers, p = 2^(s*c - m*c) written back
+//              as f16 over S_t's first 64 columns: the A operand of the P V product.
+// TMEM (512 columns): S_0 | S_1 (128 each, P_t aliases S_t), O_0 | O_1 (80 each: 64
+// dims, the row sums from the ones row of V^T, zeros), Q_0 | Q_1 (32 each: f16 pairs).
+// S_t of key tile j+1 is issued only after P_t V_j completed (it overwrites P_t), so O_t
+// is never being written while softmax t holds S_t: the lazy rescale of O_t needs no
+// extra wait. Shared memory carries only K and V^T (no Q or P reads): about 108 KB of
+// traffic per 256 x 128 block of scores instead of 268 KB with Q and P in shared memory.
+constexpr int kPKT = 128;                            // keys per tile
+constexpr int kPStages = 4;
+constexpr int kPKBytes = kPKT * 64 * 2;              // K tile [128 keys][64 dims]
+constexpr int kPVRows = 80;                          // V^T rows: 64 dims, ones, 15 zeros
+constexpr int kPVSub = kPVRows * 64 * 2;             // one 64-key half of the V^T tile
+constexpr int kPStageBytes = kPKBytes + 2 * kPVSub;  // 36 KB
+constexpr int kPSmem = 1024 + kPStages * kPStageBytes + 256;  // > 114 KB: one CTA per SM
+constexpr uint32_t kPTmemCols = 512;
+constexpr uint32_t kPColO = 256, kPColQ = 416;
+
+// D[tmem] (+)= A[tmem] * B[smem]^T (A: M rows in lanes, K along columns as f16 pairs,
+// low half first)
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 320 threads; capped at 200 registers so one CTA's 10 warps fit the register file
+// (the softmax threads hold a 128-score row).
+__global__ void __maxnreg__(200)
+    k_attn_pp(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+              const __half* __restrict__ qkv, int seqlen, int H, int D, __half* __restrict__ out, float sl2, int q8,
+              int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPStages * kPStageBytes);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = kv_full + kPStages;
+  uint64_t* q_ready = kv_empty + kPStages;  // [2] Q_t in TMEM (4 warps)
+  uint64_t* s_full = q_ready + 2;           // [2] S_t of the current key tile
+  uint64_t* p_ready = s_full + 2;           // [2] P_t written, O_t rescaled (4 warps)
+  uint64_t* pv_done = p_ready + 2;          // [2] P_t V_j complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y, sq = blockIdx.z;
+  const int q0 = blockIdx.x * 256;
+  const int nact = (seqlen - q0 > 128) ? 2 : 1;   // query tiles of this CTA inside the sequence
+  const int row_base = sq * seqlen;
+  const int nkt = (seqlen + kPKT - 1) / kPKT;
+
+  // rows 64..79 of every V^T half: a row of ones (its product with P is the row sum of
+  // P) and zeros; the TMA only writes rows 0..63. A constant row needs no swizzle.
+  for (int i = threadIdx.x; i < kPStages * 2 * 16 * 8; i += blockDim.x) {
+    const int st = i / 256, sub = (i / 128) & 1, r = 64 + (i % 128) / 8, c = i % 8;
+    const uint32_t v = (r == 64) ? 0x3C003C00u : 0u;
+    *reinterpret_cast<uint4*>(smem + st * kPStageBytes + kPKBytes + sub * kPVSub + r * 128 + c * 16) =
+        make_uint4(v, v, v, v);
+  }
+  fence_async_smem();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&q_ready[t], 4);
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_ready[t], 4);
+      mbar_init(&pv_done[t], 1);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kPTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- TMA
+      const int vrow = (sq * H + h) * 64;
+      for (int j = 0; j < nkt; ++j) {
+        const int st = j % kPStages;
+        if (!mbar_wait(&kv_empty[st], ((j / kPStages) & 1) ^ 1u, status, kStatusTimeoutEmpty)) break;
+        uint8_t* sb = smem + st * kPStageBytes;
+        mbar_arrive_expect_tx(&kv_full[st], kPKBytes + 2 * 64 * 64 * 2);
+        tma_load_2d(sb, &tmK, &kv_full[st], D + h * 64, row_base + j * kPKT);
+        tma_load_2d(sb + kPKBytes, &tmV, &kv_full[st], j * kPKT, vrow);
+        tma_load_2d(sb + kPKBytes + kPVSub, &tmV, &kv_full[st], j * kPKT + 64, vrow);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- MMA
+      constexpr uint32_t idS = umma_idesc_f16(128, kPKT);
+      constexpr uint32_t idO = umma_idesc_f16(128, kPVRows);
+      bool ok = true;
+      for (int t = 0; t < nact && ok; ++t) ok = mbar_wait(&q_ready[t], 0, status, kStatusTimeoutFull);
+      for (int j = 0; j < nkt && ok; ++j) {
+        const int st = j % kPStages;
+        if (!mbar_wait(&kv_full[st], (j / kPStages) & 1, status, kStatusTimeoutFull)) break;
+        tc_fence_after();
+        const uint8_t* sb = smem + st * kPStageBytes;
+        const uint64_t kdesc = umma_desc_sw128(smem_u32(sb));
+        for (int t = 0; t < nact; ++t) {
+          // S_t overwrites P_t of the previous key tile: wait until P_t V_{j-1} is done
+          if (j > 0 && !mbar_wait(&pv_done[t], (j - 1) & 1, status, kStatusTimeoutAccum)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tS = tmem + 128 * t, tQ = tmem + kPColQ + 32 * t;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) umma_f16_ts(tS, tQ + 8 * k, kdesc + 2 * k, idS, k > 0 ? 1u : 0u);
+          umma_commit(&s_full[t]);
+        }
+        if (!ok) break;
+        for (int t = 0; t < nact; ++t) {
+          if (!mbar_wait(&p_ready[t], j & 1, status, kStatusTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tO = tmem + kPColO + 80 * t, tP = tmem + 128 * t;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t vdesc = umma_desc_sw128(smem_u32(sb + kPKBytes + (kk >> 2) * kPVSub)) + 2 * (kk & 3);
+            umma_f16_ts(tO, tP + 8 * kk, vdesc, idO, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&pv_done[t]);
+        }
+        if (!ok) break;
+        umma_commit(&kv_empty[st]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ softmax
+    const int t = (warp - 2) >> 2;
+    const int qq = warp & 3;
+    const int r = qq * 32 + lane;                  // query row within tile t == TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(qq * 32) << 16;
+    const int qrow = q0 + 128 * t + r;             // query row within the sequence
+    if (t < nact) {
+      const uint32_t tS = tmem + 128 * t + lane_off;
+      const uint32_t tO = tmem + kPColO + 80 * t + lane_off;
+      const uint32_t tQ = tmem + kPColQ + 32 * t + lane_off;
+      {
+        // Q row -> TMEM lane r as 32 columns of f16 pairs (low half = even dimension)
+        uint32_t qv[32];
+        if (qrow < seqlen) {
+          const uint4* src = reinterpret_cast<const uint4*>(qkv + static_cast<size_t>(row_base + qrow) * 3 * D + h * 64);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint4 u = src[i];
+            qv[4 * i] = u.x;
+            qv[4 * i + 1] = u.y;
+            qv[4 * i + 2] = u.z;
+            qv[4 * i + 3] = u.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) qv[i] = 0u;
+        }
+        tmem_st32(tQ, qv);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_ready[t]);
+      }
+      float m = -INFINITY;
+      bool ok = true;
+      for (int j = 0; j < nkt; ++j) {
+        if (!mbar_wait_warp(&s_full[t], j & 1, status, kStatusTimeoutAccum)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float sv[kPKT];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ra[32];
+          tmem_ld32(tS + 32 * c, ra);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[32 * c + i] = __uint_as_float(ra[i]);
+        }
+        const int kvalid = seqlen - j * kPKT;       // keys of this tile inside the sequence (>= 1)
+        if (kvalid < kPKT) {
+#pragma unroll
+          for (int i = 0; i < kPKT; ++i)
+            if (i >= kvalid) sv[i] = -INFINITY;
+        }
+        // row max: 8 chains of three-input maxima over 128 scores
+        float m8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = fmax3(sv[i], sv[8 + i], sv[16 + i]);
+#pragma unroll
+        for (int i = 24; i + 16 <= kPKT; i += 16) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) m8[c] = fmax3(m8[c], sv[i + c], sv[i + 8 + c]);
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) m8[c] = fmaxf(m8[c], sv[120 + c]);
+        const float mt = fmaxf(fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), m8[6]), m8[7]);
+        // lazy rescale (the running max is raised only when a tile's max exceeds it by
+        // more than 2^8); O_t is stable here: P_t V_{j-1} completed before S_t was issued
+        const bool need = (j > 0) && ((mt - m) * sl2 > kRescaleLog2);
+        if (j == 0) m = mt;
+        if (__any_sync(0xffffffffu, need)) {
+          const float alpha = need ? ex2_approx((m - mt) * sl2) : 1.0f;
+          uint32_t ra[32], rb[32], rc;
+          tmem_ld32(tO, ra);
+          tmem_ld32(tO + 32, rb);
+          tmem_ld1(tO + 64, rc);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            ra[i] = __float_as_uint(__uint_as_float(ra[i]) * alpha);
+            rb[i] = __float_as_uint(__uint_as_float(rb[i]) * alpha);
+          }
+          rc = __float_as_uint(__uint_as_float(rc) * alpha);
+          tmem_st32(tO, ra);
+          tmem_st32(tO + 32, rb);
+          tmem_st1(tO + 64, rc);
+          if (need) m = mt;
+        }
+        const float mc = m * sl2;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int k = 64 * half + 2 * i;
+            const float2 a = __ffma2_rn(make_float2(sv[k], sv[k + 1]), make_float2(sl2, sl2), make_float2(-mc, -mc));
+            float p0, p1;
+            if ((i & 3) == 0) {  // a quarter of the exponentials on the FMA pipe, the rest on MUFU
+              const float2 e2 = exp2_poly2(a);
+              p0 = e2.x;
+              p1 = e2.y;
+            } else {
+              p0 = ex2_approx(a.x);
+              p1 = ex2_approx(a.y);
+            }
+            __half2 hp = __floats2half2_rn(p0, p1);
+            pk[i] = *reinterpret_cast<uint32_t*>(&hp);
+          }
+          tmem_st32(tS + 32 * half, pk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_ready[t]);
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) ok = mbar_wait_warp(&pv_done[t], (nkt - 1) & 1, status, kStatusTimeoutAccum);
+      if (ok) {
+        tc_fence_after();
+        float o[64];
+        uint32_t ra[32], rb[32], rc;
+        tmem_ld32(tO, ra);
+        tmem_ld32(tO + 32, rb);
+        tmem_ld1(tO + 64, rc);
+        tmem_wait_ld();
+        const float l = __uint_as_float(rc);
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          o[i] = __uint_as_float(ra[i]) * inv;
+          o[32 + i] = __uint_as_float(rb[i]) * inv;
+        }
+        if (qrow < seqlen) {
+          if (q8) {
+            // Q8_0 round trip per 32-dim block (ggml quantize_row_q8_0_ref semantics)
+#pragma unroll
+            for (int bb = 0; bb < 2; ++bb) {
+              float amax = 0.f;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[32 * bb + i]));
+              const float d = amax / 127.0f;
+              const float id = d != 0.f ? 1.0f / d : 0.0f;
+              const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[32 * bb + i] = dh * roundf(o[32 * bb + i] * id);
+            }
+          }
+          __half* dst = out + static_cast<size_t>(row_base + qrow) * D + h * 64;
+#pragma unroll
+          for (int i = 0; i < 64; i += 8) {
+            uint4 u;
+            __half2* hh = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) hh[k] = __floats2half2_rn(o[i + 2 * k], o[i + 2 * k + 1]);
+            *reinterpret_cast<uint4*>(dst + i) = u;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kPTmemCols);
+  }
+}
+
 }  // namespace
 
 // qkv: [nseq*seqlen][3D] (q | k | v), vt: [nseq][H][64][ld_vt] (transposed v), out:
 // [nseq*seqlen][D]. The columns of vt beyond seqlen are padding that is never read:
 // the V^T tensor map is seqlen wide, so the TMA fills out-of-range keys with zeros.
+// attention_tc runs the ping-pong kernel; $DA3B_ATTN_V1=1 (read once per process)
+// selects the 128-query kernel (2 CTAs per SM, P in shared memory) for comparisons.
+static bool attn_v1() {
+  static const bool v1 = [] {
+    const char* e = getenv("DA3B_ATTN_V1");
+    return e && e[0] == '1';
+  }();
+  return v1;
+}
+
+static int attention_pp(const __half* qkv, const __half* vt, int ld_vt, int nseq, int seqlen, int H, int D,
+                        __half* out, int q8, int* status, cudaStream_t s) {
+  CUtensorMap tk, tv;
+  int rc;
+  if ((rc = make_tmap_2d(&tk, qkv, nseq * seqlen, 3 * D, 3 * D, kPKT))) return rc - 100;
+  if ((rc = make_tmap_2d(&tv, vt, nseq * H * 64, seqlen, ld_vt, 64))) return rc - 200;
+  static std::atomic<uint64_t> attr_set{0};  // one bit per device; first calls may race
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = uint64_t(1) << (dev & 63);
+  if (!(attr_set.load(std::memory_order_acquire) & bit)) {
+    if (cudaFuncSetAttribute(k_attn_pp, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem) != cudaSuccess)
+      return -3;
+    attr_set.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  const int ntiles = (seqlen + 127) / 128;
+  dim3 grid((ntiles + 1) / 2, H, nseq);
+  const float sl2 = 0.125f * 1.4426950408889634f;
+  k_attn_pp<<<grid, 320, kPSmem, s>>>(tk, tv, qkv, seqlen, H, D, out, sl2, q8, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
 int attention_tc(const __half* qkv, const __half* vt, int ld_vt, int nseq, int seqlen, int H, int D, __half* out,
                  int q8, int* status, cudaStream_t s) {
   if (nseq <= 0 || seqlen <= 0) return 0;
   if (D != H * 64 || ld_vt < seqlen || ld_vt % 8 || (reinterpret_cast<uintptr_t>(out) & 15)) return -1;
+  if (!attn_v1()) return attention_pp(qkv, vt, ld_vt, nseq, seqlen, H, D, out, q8, status, s);
   CUtensorMap tq, tk, tv;
   int rc;
   if ((rc = make_tmap_2d(&tq, qkv, nseq * seqlen, 3 * D, 3 * D, 128))) return rc - 100;

@@ -4,6 +4,7 @@ Tolerance: |out - ref| <= 2e-3 * max|ref| + 2e-3 (f16 operands are exact in both
 paths; the difference is f32 summation order plus the f16 rounding of the output).
 """
 import ctypes
+import os
 
 import numpy as np
 import pytest
@@ -172,8 +173,13 @@ def test_conv3_halo(lib, B, H, W, IC, OC, pair, monkeypatch):
     close(out2, ref2.permute(0, 2, 3, 1).clamp_min(0))
 
 
-@pytest.mark.parametrize("nseq,seqlen,heads", [(1, 1, 1), (2, 37, 2), (3, 1370, 6), (1, 1297 * 3, 4), (2, 200, 16)])
+@pytest.mark.parametrize("nseq,seqlen,heads", [(1, 1, 1), (2, 37, 2), (3, 1370, 6), (1, 1297 * 3, 4), (2, 200, 16),
+                                               (2, 128, 2), (1, 129, 3), (3, 255, 1), (1, 256, 2), (2, 257, 2),
+                                               (1, 1297 * 8, 2)])
 def test_attention(lib, nseq, seqlen, heads):
+    """da3b_attention against torch fp32 softmax attention: sequence lengths on both sides
+    of the 128-query and 128-key tile edges (one or two query tiles per CTA, ragged last
+    key tile), several sequences and heads, and an 8-view global sequence."""
     g = torch.Generator(device="cuda").manual_seed(seqlen + heads)
     D = heads * 64
     qkv = (torch.randn(nseq * seqlen, 3 * D, device="cuda", generator=g) * 1.5).half()
@@ -200,3 +206,21 @@ def test_upsample_align_corners(lib, B, hs, ws, C, H, W):
     ref = torch.nn.functional.interpolate(x.permute(0, 3, 1, 2).float(), size=(H, W), mode="bilinear",
                                           align_corners=True).permute(0, 2, 3, 1)
     close(out, ref, rel=2e-3, abs_=2e-3)
+
+
+@pytest.mark.parametrize("nseq,seqlen,heads", [(2, 1370, 4), (1, 300, 2)])
+def test_attention_v1_kernel(nseq, seqlen, heads):
+    """The previous 128-query kernel, still selectable with DA3B_ATTN_V1=1 (read once per
+    process, so it runs in a fresh subprocess), against torch fp32."""
+    import subprocess
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    code = ("import sys; sys.path.insert(0, %r); sys.path.insert(0, %r)\n"
+            "from da3cpplib_b200 import _lib\n"
+            "import test_gemm_gpu as t\n"
+            "t.test_attention(_lib.load(), %d, %d, %d)\n"
+            "print('ok')\n" % (os.path.dirname(here), here, nseq, seqlen, heads))
+    env = dict(os.environ, DA3B_ATTN_V1="1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
