@@ -22,6 +22,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -380,9 +381,7 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
-// 320 threads; capped at 200 registers so one CTA's 10 warps fit the register file
-// (the softmax threads hold a 128-score row).
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(320, 1)
     k_attn_pp(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
               const __half* __restrict__ qkv, int seqlen, int H, int D, __half* __restrict__ out, float sl2, int q8,
               int* status) {
@@ -536,32 +535,28 @@ __global__ void __maxnreg__(200)
           break;
         }
         tc_fence_after();
-        float sv[kPKT];
+        // pass 1: the row max over the tile's 128 scores (32 columns at a time, so no
+        // thread holds the whole row); keys past the sequence are masked
+        const int kvalid = seqlen - j * kPKT;       // keys of this tile inside the sequence (>= 1)
+        float m8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t ra[32];
           tmem_ld32(tS + 32 * c, ra);
           tmem_wait_ld();
+          float sv[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) sv[32 * c + i] = __uint_as_float(ra[i]);
+          for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(ra[i]);
+          if (kvalid < kPKT) {  // the last tile of the sequence only (uniform branch)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (32 * c + i >= kvalid) sv[i] = -INFINITY;
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], fmax3(sv[i], sv[8 + i], sv[16 + i]), sv[24 + i]);
         }
-        const int kvalid = seqlen - j * kPKT;       // keys of this tile inside the sequence (>= 1)
-        if (kvalid < kPKT) {
-#pragma unroll
-          for (int i = 0; i < kPKT; ++i)
-            if (i >= kvalid) sv[i] = -INFINITY;
-        }
-        // row max: 8 chains of three-input maxima over 128 scores
-        float m8[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = fmax3(sv[i], sv[8 + i], sv[16 + i]);
-#pragma unroll
-        for (int i = 24; i + 16 <= kPKT; i += 16) {
-#pragma unroll
-          for (int c = 0; c < 8; ++c) m8[c] = fmax3(m8[c], sv[i + c], sv[i + 8 + c]);
-        }
-#pragma unroll
-        for (int c = 0; c < 8; ++c) m8[c] = fmaxf(m8[c], sv[120 + c]);
         const float mt = fmaxf(fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), m8[6]), m8[7]);
         // lazy rescale (the running max is raised only when a tile's max exceeds it by
         // more than 2^8); O_t is stable here: P_t V_{j-1} completed before S_t was issued
@@ -585,22 +580,42 @@ __global__ void __maxnreg__(200)
           tmem_st1(tO + 64, rc);
           if (need) m = mt;
         }
+        // pass 2: p = 2^(s*c - m*c) for 64 keys at a time, written as f16 pairs over the
+        // first 64 columns of S_t (keys 0..63 -> columns 0..31 once both of their S
+        // columns are in registers; keys 64..127 -> columns 32..63, already read)
         const float mc = m * sl2;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
+          float sv[64];
+          {
+            uint32_t ra[32], rb[32];
+            tmem_ld32(tS + 64 * half, ra);
+            tmem_ld32(tS + 64 * half + 32, rb);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              sv[i] = __uint_as_float(ra[i]);
+              sv[32 + i] = __uint_as_float(rb[i]);
+            }
+            if (kvalid < kPKT) {
+#pragma unroll
+              for (int i = 0; i < 64; ++i)
+                if (64 * half + i >= kvalid) sv[i] = -INFINITY;
+            }
+          }
           uint32_t pk[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const int k = 64 * half + 2 * i;
-            const float2 a = __ffma2_rn(make_float2(sv[k], sv[k + 1]), make_float2(sl2, sl2), make_float2(-mc, -mc));
+            const float2 a2 = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), make_float2(sl2, sl2),
+                                         make_float2(-mc, -mc));
             float p0, p1;
             if ((i & 3) == 0) {  // a quarter of the exponentials on the FMA pipe, the rest on MUFU
-              const float2 e2 = exp2_poly2(a);
+              const float2 e2 = exp2_poly2(a2);
               p0 = e2.x;
               p1 = e2.y;
             } else {
-              p0 = ex2_approx(a.x);
-              p1 = ex2_approx(a.y);
+              p0 = ex2_approx(a2.x);
+              p1 = ex2_approx(a2.y);
             }
             __half2 hp = __floats2half2_rn(p0, p1);
             pk[i] = *reinterpret_cast<uint32_t*>(&hp);
@@ -699,7 +714,16 @@ static int attention_pp(const __half* qkv, const __half* vt, int ld_vt, int nseq
   dim3 grid((ntiles + 1) / 2, H, nseq);
   const float sl2 = 0.125f * 1.4426950408889634f;
   k_attn_pp<<<grid, 320, kPSmem, s>>>(tk, tv, qkv, seqlen, H, D, out, sl2, q8, status);
-  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cudaFuncAttributes fa;
+    memset(&fa, 0, sizeof(fa));
+    cudaFuncGetAttributes(&fa, k_attn_pp);
+    fprintf(stderr, "[da3b] attention launch failed: %s (regs %d, max threads %d, smem %d)\n", cudaGetErrorString(e),
+            fa.numRegs, fa.maxThreadsPerBlock, kPSmem);
+    return -4;
+  }
+  return 0;
 }
 
 int attention_tc(const __half* qkv, const __half* vt, int ld_vt, int nseq, int seqlen, int H, int D, __half* out,
