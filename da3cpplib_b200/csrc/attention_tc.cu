@@ -685,14 +685,15 @@ __global__ void __launch_bounds__(320, 1)
 // qkv: [nseq*seqlen][3D] (q | k | v), vt: [nseq][H][64][ld_vt] (transposed v), out:
 // [nseq*seqlen][D]. The columns of vt beyond seqlen are padding that is never read:
 // the V^T tensor map is seqlen wide, so the TMA fills out-of-range keys with zeros.
-// attention_tc runs the ping-pong kernel; $DA3B_ATTN_V1=1 (read once per process)
-// selects the 128-query kernel (2 CTAs per SM, P in shared memory) for comparisons.
-static bool attn_v1() {
-  static const bool v1 = [] {
-    const char* e = getenv("DA3B_ATTN_V1");
+// attention_tc runs the 128-query kernel (2 CTAs per SM, P in shared memory);
+// $DA3B_ATTN_PP=1 (read once per process) selects the ping-pong kernel, which is
+// correct but measured slower (1.52 against 1.03 ms at the C3 shape).
+static bool attn_pp() {
+  static const bool pp = [] {
+    const char* e = getenv("DA3B_ATTN_PP");
     return e && e[0] == '1';
   }();
-  return v1;
+  return pp;
 }
 
 static int attention_pp(const __half* qkv, const __half* vt, int ld_vt, int nseq, int seqlen, int H, int D,
@@ -730,7 +731,7 @@ int attention_tc(const __half* qkv, const __half* vt, int ld_vt, int nseq, int s
                  int q8, int* status, cudaStream_t s) {
   if (nseq <= 0 || seqlen <= 0) return 0;
   if (D != H * 64 || ld_vt < seqlen || ld_vt % 8 || (reinterpret_cast<uintptr_t>(out) & 15)) return -1;
-  if (!attn_v1()) return attention_pp(qkv, vt, ld_vt, nseq, seqlen, H, D, out, q8, status, s);
+  if (attn_pp()) return attention_pp(qkv, vt, ld_vt, nseq, seqlen, H, D, out, q8, status, s);
   CUtensorMap tq, tk, tv;
   int rc;
   if ((rc = make_tmap_2d(&tq, qkv, nseq * seqlen, 3 * D, 3 * D, 128))) return rc - 100;

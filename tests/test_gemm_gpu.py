@@ -208,9 +208,9 @@ def test_upsample_align_corners(lib, B, hs, ws, C, H, W):
     close(out, ref, rel=2e-3, abs_=2e-3)
 
 
-@pytest.mark.parametrize("nseq,seqlen,heads", [(2, 1370, 4), (1, 300, 2)])
-def test_attention_v1_kernel(nseq, seqlen, heads):
-    """The previous 128-query kernel, still selectable with DA3B_ATTN_V1=1 (read once per
+@pytest.mark.parametrize("nseq,seqlen,heads", [(2, 1370, 4), (1, 300, 2), (3, 129, 2), (1, 2 * 1297, 3)])
+def test_attention_pp_kernel(nseq, seqlen, heads):
+    """The ping-pong attention kernel, selectable with DA3B_ATTN_PP=1 (read once per
     process, so it runs in a fresh subprocess), against torch fp32."""
     import subprocess
     import sys
@@ -221,6 +221,6 @@ def test_attention_v1_kernel(nseq, seqlen, heads):
             "import test_gemm_gpu as t\n"
             "t.test_attention(_lib.load(), %d, %d, %d)\n"
             "print('ok')\n" % (os.path.dirname(here), here, nseq, seqlen, heads))
-    env = dict(os.environ, DA3B_ATTN_V1="1")
+    env = dict(os.environ, DA3B_ATTN_PP="1")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
