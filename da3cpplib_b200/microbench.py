@@ -87,6 +87,7 @@ def main(argv=None):
     ap.add_argument("--cout", type=int, default=0, help="Part B: output channels (default = input channels)")
     ap.add_argument("--batch", type=int, default=8, help="Part B / up: images")
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--attn-nseq", type=int, default=0, help="attn: only the C3 shape with this many sequences")
     args = ap.parse_args(argv)
 
     L = _lib.load()
@@ -240,7 +241,10 @@ def main(argv=None):
         del img, o
 
     if args.part in ("attn", "all"):
-        for nseq, seqlen, heads, tag in ((64, 1370, 16, "C3 per-image"), (2, 8 * 1297, 16, "C4 global, 2 scenes")):
+        cases = ((64, 1370, 16, "C3 per-image"), (2, 8 * 1297, 16, "C4 global, 2 scenes"))
+        if args.attn_nseq:
+            cases = ((args.attn_nseq, 1370, 16, "C3 shape, fewer images"),)
+        for nseq, seqlen, heads, tag in cases:
             D = heads * 64
             qkv = torch.randn((nseq * seqlen, 3 * D), generator=gen, device="cuda").half()
             out = torch.empty((nseq * seqlen, D), dtype=torch.float16, device="cuda")
