@@ -89,7 +89,7 @@ DA3B_API int da3b_dequant_q8_0(const void* q8, int rows, int K, void* w_f16, int
 
 DA3B_API int da3b_linear_f16(const void* x, int M, int K, int lda, const void* w, int N, int ldw, const float* bias,
                              int act, void* out, int ldo, void* stream) {
-  if (!x || !w || !out || act < 0 || act > 2) return -100;
+  if (!x || !w || !out || act < 0 || act > 3) return -100;
   int* st = device_status_word();
   if (!st) return -101;
   EpiArgs e = epi_default();

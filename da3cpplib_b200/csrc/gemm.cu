@@ -82,9 +82,49 @@ __device__ __forceinline__ float2 gelu_erf2(float2 v) {
   return __fmul2_rn(__fmul2_rn(f2c(0.5f), v), __fadd2_rn(f2c(1.0f), r));
 }
 
+// Exact-form GELU with erf from Abramowitz & Stegun formula 7.1.28:
+// erf(z) = 1 - (1 + a1 z + a2 z^2 + ... + a6 z^6)^-16, z >= 0, |error| <= 3e-7. With
+// r = (1 + ...)^-16, 1 + erf(x / sqrt 2) is 2 - r for x >= 0 and r for x < 0 (no
+// cancellation for negative x); one reciprocal (MUFU) and no exponential per value.
+__device__ __forceinline__ float gelu_r(float v) {
+  const float z = fabsf(v * 0.70710678118654752f);
+  float p = fmaf(0.0000430638f, z, 0.0002765672f);
+  p = fmaf(p, z, 0.0001520143f);
+  p = fmaf(p, z, 0.0092705272f);
+  p = fmaf(p, z, 0.0422820123f);
+  p = fmaf(p, z, 0.0705230784f);
+  p = fmaf(p, z, 1.0f);
+  float r = __fdividef(1.0f, p);
+  r *= r;
+  r *= r;
+  r *= r;
+  r *= r;
+  return 0.5f * v * (v >= 0.0f ? 2.0f - r : r);
+}
+// gelu_r of two values with packed f32x2 arithmetic, the same operations in the same
+// order (bit-identical to the scalar form).
+__device__ __forceinline__ float2 gelu_r2(float2 v) {
+  const float2 zz = __fmul2_rn(v, f2c(0.70710678118654752f));
+  const float2 z = make_float2(fabsf(zz.x), fabsf(zz.y));
+  float2 p = __ffma2_rn(f2c(0.0000430638f), z, f2c(0.0002765672f));
+  p = __ffma2_rn(p, z, f2c(0.0001520143f));
+  p = __ffma2_rn(p, z, f2c(0.0092705272f));
+  p = __ffma2_rn(p, z, f2c(0.0422820123f));
+  p = __ffma2_rn(p, z, f2c(0.0705230784f));
+  p = __ffma2_rn(p, z, f2c(1.0f));
+  float2 r = make_float2(__fdividef(1.0f, p.x), __fdividef(1.0f, p.y));
+  r = __fmul2_rn(r, r);
+  r = __fmul2_rn(r, r);
+  r = __fmul2_rn(r, r);
+  r = __fmul2_rn(r, r);
+  const float2 t = make_float2(v.x >= 0.0f ? 2.0f - r.x : r.x, v.y >= 0.0f ? 2.0f - r.y : r.y);
+  return __fmul2_rn(__fmul2_rn(f2c(0.5f), v), t);
+}
+
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == kActRelu) return fmaxf(v, 0.0f);
   if (act == kActGelu) return gelu_erf(v);
+  if (act == kActGeluR) return gelu_r(v);
   return v;
 }
 
@@ -620,6 +660,15 @@ __device__ __forceinline__ void epi_transposed(const GemmGeom& g, const EpiArgs&
 #pragma unroll
           for (int i = 0; i < 8; i += 2) {
             const float2 gv = gelu_erf2(make_float2(t[k][i], t[k][i + 1]));
+            t[k][i] = gv.x;
+            t[k][i + 1] = gv.y;
+          }
+      } else if (e.act == kActGeluR) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) {
+            const float2 gv = gelu_r2(make_float2(t[k][i], t[k][i + 1]));
             t[k][i] = gv.x;
             t[k][i + 1] = gv.y;
           }
@@ -1254,7 +1303,8 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
   const int epi_mode = epi_mode_override();
   if ((e.kind == kEpiF16 && !e.q8) || e.kind == kEpiQKV) {
     if (epi_mode != 1) e2.tma_store = 3;
-    else if (bn >= 128 && e.rm_div == 0 && e.kind == kEpiF16 && e.act == kActGelu && !e.res1 && !e.res2 &&
+    else if (bn >= 128 && e.rm_div == 0 && e.kind == kEpiF16 && (e.act == kActGelu || e.act == kActGeluR) &&
+             !e.res1 && !e.res2 &&
              !e.out_relu && make_out_map(&tc, e.out, false, M, N, e.ld_out))
       e2.tma_store = 1;
   } else if (bn >= 128 && e.rm_div == 0 && e.kind == kEpiResid &&

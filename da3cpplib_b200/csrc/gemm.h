@@ -24,7 +24,10 @@ enum EpiKind : int {
                    // transposed per (sequence, head) to vt [seq][H][64][ld_vt] for attention
 };
 
-enum Act : int { kActNone = 0, kActRelu = 1, kActGelu = 2 };
+// kActGelu and kActGeluR are both the exact-form (erf) GELU, with different erf
+// approximations of published error bound (see gemm.cu): kActGeluR spends one MUFU
+// operation per value instead of two.
+enum Act : int { kActNone = 0, kActRelu = 1, kActGelu = 2, kActGeluR = 3 };
 
 // Output activation of the fused out2b stage (per output channel).
 enum OutAct : int {

@@ -49,7 +49,8 @@ DA3B_API int da3b_dequant_q8_0(const void* q8, int rows, int K, void* w_f16, int
 /* Linear layer y = act(x W^T + b) (+res): the replacement of `linear()`
  * (src/ggml_extend.hpp:6-10 -> ggml_mul_mat(W_q8_0, x) + bias) on the tcgen05 path.
  * x: f16 [M][K] (lda), W: f16 [N][K] (ldw, from da3b_dequant_q8_0), bias f32 [N]
- * or NULL, act: 0 none, 1 relu, 2 erf-GELU (src/ggml_extend.hpp:22-25),
+ * or NULL, act: 0 none, 1 relu, 2 erf-GELU (src/ggml_extend.hpp:22-25), 3 the same GELU
+ * with a one-reciprocal erf approximation (Abramowitz & Stegun 7.1.28),
  * out: f16 [M][N] (ldo). */
 DA3B_API int da3b_linear_f16(const void* x, int M, int K, int lda, const void* w, int N, int ldw,
                              const float* bias, int act, void* out, int ldo, void* stream);
