@@ -278,11 +278,10 @@ int Resizer::preprocess_real(const uint8_t* src, int B, int w, int h, int patch,
 // (v/255 - mean[c]) / std[c] in f32 (src/preprocess.cpp:192-196), stored as f16.
 namespace {
 
-// Patch size 14 (DINOv2): work item = (image, patch row, strip of up to kStrip patches);
-// each CTA builds its value and offset tables once and then walks items. The 14 image
-// rows of a strip are staged in shared memory with aligned 4-byte loads (the words that
-// straddle the ends of the image buffer are read byte by byte), then every thread
-// writes 8 consecutive f16 of one patch's operand row.
+// Patch size 14 (DINOv2): one CTA per (image, patch row, strip of up to kStrip patches).
+// The 14 image rows of the strip are staged in shared memory with aligned 4-byte loads
+// (the words that straddle the ends of the image buffer are read byte by byte), then
+// every thread writes 8 consecutive f16 of one patch's operand row.
 constexpr int kP = 14;
 constexpr int kStrip = 16;  // patches per CTA
 constexpr int kRowBytes = kStrip * kP * 3;
@@ -310,65 +309,56 @@ __global__ void __launch_bounds__(256) k_patchify14(const uint8_t* __restrict__ 
   }
   const uintptr_t lo = reinterpret_cast<uintptr_t>(rgb);
   const uintptr_t hi = lo + static_cast<size_t>(B) * H * W * 3;
-  const int nstrip = (gw + kStrip - 1) / kStrip;
-  const long items = static_cast<long>(nstrip) * gh * B;
+  const int px0 = blockIdx.x * kStrip, py = blockIdx.y, b = blockIdx.z;
+  const int np = min(kStrip, gw - px0);
+  const int row_bytes = np * kP * 3;
+  for (int ky = 0; ky < kP; ++ky) {
+    const uint8_t* base = rgb + ((static_cast<size_t>(b) * H + py * kP + ky) * W + px0 * kP) * 3;
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(base) & ~uintptr_t(3);
+    const int lead = static_cast<int>(reinterpret_cast<uintptr_t>(base) - a0);
+    const int nwords = (lead + row_bytes + 3) / 4;
+    uint8_t* dst = tile + ky * kRowBytes;
+    for (int wi = threadIdx.x; wi < nwords; wi += blockDim.x) {
+      const uintptr_t wa = a0 + 4 * static_cast<uintptr_t>(wi);
+      if (wa >= lo && wa + 4 <= hi) {
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(wa);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int o = wi * 4 + j - lead;  // byte offset within the staged row
+          if (o >= 0 && o < row_bytes) dst[o] = static_cast<uint8_t>(v >> (8 * j));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int o = wi * 4 + j - lead;
+          if (o >= 0 && o < row_bytes) dst[o] = base[o];
+        }
+      }
+    }
+  }
+  __syncthreads();
   const int k8 = ldk / 8;  // 8-column groups per operand row
   const int kk = 3 * kP * kP;
-  // the tables above are built once per CTA; the CTA then walks strips
-  for (long it = blockIdx.x; it < items; it += gridDim.x) {
-    const int sx = static_cast<int>(it % nstrip);
-    const int py = static_cast<int>((it / nstrip) % gh);
-    const int b = static_cast<int>(it / (static_cast<long>(nstrip) * gh));
-    const int px0 = sx * kStrip;
-    const int np = min(kStrip, gw - px0);
-    const int row_bytes = np * kP * 3;
-    __syncthreads();  // the previous strip's reads of the tile (and the tables) are done
-    for (int ky = 0; ky < kP; ++ky) {
-      const uint8_t* base = rgb + ((static_cast<size_t>(b) * H + py * kP + ky) * W + px0 * kP) * 3;
-      const uintptr_t a0 = reinterpret_cast<uintptr_t>(base) & ~uintptr_t(3);
-      const int lead = static_cast<int>(reinterpret_cast<uintptr_t>(base) - a0);
-      const int nwords = (lead + row_bytes + 3) / 4;
-      uint8_t* dst = tile + ky * kRowBytes;
-      for (int wi = threadIdx.x; wi < nwords; wi += blockDim.x) {
-        const uintptr_t wa = a0 + 4 * static_cast<uintptr_t>(wi);
-        if (wa >= lo && wa + 4 <= hi) {
-          const uint32_t v = *reinterpret_cast<const uint32_t*>(wa);
+  for (int item = threadIdx.x; item < np * k8; item += blockDim.x) {
+    const int pl = item / k8, k0 = (item - pl * k8) * 8;
+    const int poff = pl * kP * 3;
+    uint32_t w[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int o = wi * 4 + j - lead;  // byte offset within the staged row
-            if (o >= 0 && o < row_bytes) dst[o] = static_cast<uint8_t>(v >> (8 * j));
-          }
-        } else {
+    for (int j = 0; j < 4; ++j) {
+      uint32_t h[2];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int o = wi * 4 + j - lead;
-            if (o >= 0 && o < row_bytes) dst[o] = base[o];
-          }
+      for (int q = 0; q < 2; ++q) {
+        const int k = k0 + 2 * j + q;
+        h[q] = 0u;  // operand columns past 3 * 14 * 14: zero padding
+        if (k < kk) {
+          const int e = ktab[k];
+          h[q] = lut[(e >> 16) * 256 + tile[(e & 0xffff) + poff]];
         }
       }
+      w[j] = h[0] | (h[1] << 16);
     }
-    __syncthreads();
-    for (int item = threadIdx.x; item < np * k8; item += blockDim.x) {
-      const int pl = item / k8, k0 = (item - pl * k8) * 8;
-      const int poff = pl * kP * 3;
-      uint32_t w[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t h[2];
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int k = k0 + 2 * j + q;
-          h[q] = 0u;  // operand columns past 3 * 14 * 14: zero padding
-          if (k < kk) {
-            const int e = ktab[k];
-            h[q] = lut[(e >> 16) * 256 + tile[(e & 0xffff) + poff]];
-          }
-        }
-        w[j] = h[0] | (h[1] << 16);
-      }
-      const size_t row = (static_cast<size_t>(b) * gh + py) * gw + px0 + pl;
-      *reinterpret_cast<uint4*>(out + row * ldk + k0) = make_uint4(w[0], w[1], w[2], w[3]);
-    }
+    const size_t row = (static_cast<size_t>(b) * gh + py) * gw + px0 + pl;
+    *reinterpret_cast<uint4*>(out + row * ldk + k0) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -411,8 +401,7 @@ int patchify(const uint8_t* rgb, int B, int H, int W, int P, const float* mean, 
   const int gh = H / P, gw = W / P;
   if (B <= 0 || gh <= 0 || gw <= 0) return 0;
   if (P == kP && ldk % 8 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 && gh <= 65535 && B <= 65535) {
-    const long items = static_cast<long>((gw + kStrip - 1) / kStrip) * gh * B;
-    const unsigned grid = static_cast<unsigned>(items < 148L * 6 ? items : 148L * 6);
+    const dim3 grid((gw + kStrip - 1) / kStrip, gh, B);
     k_patchify14<<<grid, 256, 0, s>>>(rgb, B, H, W, gh, gw, mean[0], mean[1], mean[2], sd[0], sd[1], sd[2], out,
                                       ldk);
   } else {
