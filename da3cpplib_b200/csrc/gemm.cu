@@ -1277,7 +1277,8 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
                 int* status, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return M == 0 ? 0 : -30;
   if (lda < K || ldw < K || lda % 8 || ldw % 8) return -31;
-  if (bn <= 0) bn = pick_bn(N);
+  const bool auto_bn = bn <= 0;
+  if (auto_bn) bn = pick_bn(N);
   if (e.kind == kEpiOut2) bn = 32;
   int rc = check_epi(e, N);
   if (rc) return rc;
@@ -1291,6 +1292,13 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
   g.num_m_tiles = (M + 127) / 128;
   g.num_n_tiles = (N + bn - 1) / bn;
   const bool two = want_2sm(g, bn);
+  if (auto_bn && !two && e.kind != kEpiOut2) {
+    // Few rows (one image: M = 1370): with too few CTA-pair tiles for the SMs the GEMM
+    // runs on one-CTA tiles; narrower ones then keep more SMs busy (a ViT-B fc2 of
+    // N = 768 has 33 tiles of 128 x 256 but 132 of 128 x 64).
+    while (bn > 64 && static_cast<long>(g.num_m_tiles) * ((N + bn - 1) / bn) < num_sms()) bn /= 2;
+    g.num_n_tiles = (N + bn - 1) / bn;
+  }
   CUtensorMap ta, tb, tc;
   if ((rc = make_tmap_2d(&ta, A, M, K, lda, 128))) return rc - 100;
   if ((rc = make_tmap_2d(&tb, W, N, K, ldw, two ? bn / 2 : bn))) return rc - 200;
