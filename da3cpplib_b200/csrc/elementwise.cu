@@ -45,33 +45,55 @@ int dequant_q8_0(const void* q8, int rows, int K, __half* out, int ldo, cudaStre
 }
 
 // One launch dequantising up to four Q8_0 matrices (a ViT block's linears) into dense
-// f16 [rows][K]: one thread per 32-element block, f16(d * q) like k_dequant_q8_0.
-__global__ void k_dequant_q8_0_segs(Q8Segs g) {
-  for (long idx = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < g.total;
-       idx += static_cast<long>(gridDim.x) * blockDim.x) {
-    int k = 0;
-    while (k + 1 < g.n && idx >= g.s[k + 1].first) ++k;
+// f16 [rows][K], f16(d * q) like k_dequant_q8_0. A warp takes 32 consecutive blocks
+// of one matrix: their 1088 source bytes come in as 16-byte coalesced loads into shared
+// memory, then each lane converts one block and writes its 64 output bytes (the warp's
+// stores are one contiguous 2 KB run). A matrix's last partial chunk reads per lane.
+__device__ __forceinline__ void dequant_block32(const uint8_t* blk, __half* out) {
+  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(blk[0] | (blk[1] << 8))));
+  uint4 packed[4];
+  __half2* h = reinterpret_cast<__half2*>(packed);
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    h[i] = __floats2half2_rn(d * static_cast<float>(static_cast<int8_t>(blk[2 + 2 * i])),
+                             d * static_cast<float>(static_cast<int8_t>(blk[3 + 2 * i])));
+  uint4* o4 = reinterpret_cast<uint4*>(out);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o4[i] = packed[i];
+}
+
+__global__ void __launch_bounds__(256) k_dequant_q8_0_segs(Q8Segs g) {
+  __shared__ __align__(16) uint8_t stage[8][1088];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long gw = static_cast<long>(blockIdx.x) * 8 + warp, nw = static_cast<long>(gridDim.x) * 8;
+  for (int k = 0; k < g.n; ++k) {
     const Q8Seg& sg = g.s[k];
-    const long li = idx - sg.first;
-    const int r = static_cast<int>(li / sg.nblk), b = static_cast<int>(li % sg.nblk);
-    const uint8_t* blk = sg.q8 + static_cast<size_t>(li) * 34;
-    const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(blk[0] | (blk[1] << 8))));
-    uint4 packed[4];
-    __half2* h = reinterpret_cast<__half2*>(packed);
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-      h[i] = __floats2half2_rn(d * static_cast<float>(static_cast<int8_t>(blk[2 + 2 * i])),
-                               d * static_cast<float>(static_cast<int8_t>(blk[3 + 2 * i])));
-    uint4* o4 = reinterpret_cast<uint4*>(sg.out + static_cast<size_t>(r) * sg.nblk * 32 + b * 32);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) o4[i] = packed[i];
+    const long nblk = static_cast<long>(sg.rows) * sg.nblk;
+    const long nch = (nblk + 31) / 32;
+    for (long c = gw; c < nch; c += nw) {
+      const long b0 = c * 32;
+      const uint8_t* src = sg.q8 + static_cast<size_t>(b0) * 34;
+      if (b0 + 32 <= nblk) {
+        const uint4* s4 = reinterpret_cast<const uint4*>(src);
+        uint4* d4 = reinterpret_cast<uint4*>(stage[warp]);
+        for (int i = lane; i < 68; i += 32) d4[i] = s4[i];
+        __syncwarp();
+        dequant_block32(stage[warp] + lane * 34, sg.out + static_cast<size_t>(b0 + lane) * 32);
+        __syncwarp();  // the stage is reused by this warp's next chunk
+      } else if (b0 + lane < nblk) {
+        dequant_block32(src + lane * 34, sg.out + static_cast<size_t>(b0 + lane) * 32);
+      }
+    }
   }
 }
 
 int dequant_q8_0_segs(const Q8Segs& g, cudaStream_t s) {
   if (g.n <= 0 || g.n > 4 || g.total <= 0) return -1;
-  long blocks = (g.total + 255) / 256;
-  if (blocks > 148 * 16) blocks = 148 * 16;
+  for (int k = 0; k < g.n; ++k)
+    if (reinterpret_cast<uintptr_t>(g.s[k].q8) & 15 || reinterpret_cast<uintptr_t>(g.s[k].out) & 15) return -2;
+  const long chunks = (g.total + 31) / 32;
+  long blocks = (chunks + 7) / 8;
+  if (blocks > 148 * 8) blocks = 148 * 8;
   k_dequant_q8_0_segs<<<static_cast<unsigned>(blocks), 256, 0, s>>>(g);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
