@@ -8,10 +8,18 @@
 // reference's own host code for pos-embed interpolation, RoPE tables, UV embedding,
 // preprocessing and output activations. Citations are path:line in DA3cpplib.
 //
-// PARITY UNPINNED against the reference itself: DA3cpplib cannot be built here (its
-// ggml submodule is empty) and its tests ship no golden vectors for this path. The
-// Q8_0 quantiser is pinned bit-exactly against gguf-py's published quantiser, and the
-// DA2 architecture against an independent implementation (tests/test_oracle_*.py).
+// Pins. The reference's own host code compiles unmodified into oracle/_ref and this
+// restatement matches it bit for bit: preprocessing (src/preprocess.cpp), the UV
+// embedding (src/uv_posembed.cpp), the nested alignment (src/nested.cpp), the ray ->
+// pose solver (src/ray_pose.cpp, src/linalg.cpp), the 2-D RoPE tables
+// (src/rope2d.cpp), the pos-embed interpolation and the multi-view reference-view
+// selection (src/dino_backbone.cpp); see tests/test_oracle_pins.py and
+// tests/golden/. The Q8_0 quantiser is pinned bit-exactly against gguf-py's published
+// quantiser, and the DA2 architecture against an independent implementation
+// (transformers). The ggml graph arithmetic (matmul, norm, flash attention, conv,
+// interpolate) is a restatement only: ggml's source is absent from the reference's
+// checkout (its submodule is empty) and the reference ships no golden vectors for it.
+// The vectorised kernels (AVX2) keep the scalar operation order: same bits.
 #include <immintrin.h>
 #include <math.h>
 #include <stdint.h>
