@@ -34,6 +34,7 @@ SIGNATURES = {
     "da3b_linear_q8q8_i8": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
                                     c_int, c_void_p]),
     "da3b_debug_wait_timeout": (c_int, [ctypes.c_ulonglong, c_int, c_void_p, c_void_p, c_void_p]),
+    "da3b_debug_mma_cycles": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "da3b_transpose_v": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p]),
     "da3b_attention_vt": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "da3b_attention_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),

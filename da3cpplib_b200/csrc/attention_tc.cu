@@ -61,14 +61,16 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // relative-error minimax (Lawson-weighted least squares; max relative error 7.5e-5,
 // below the f16 rounding of P); 2^j is added to the exponent field. x is clamped at
 // -125 so the exponent stays normal (the result then rounds to 0 in f16).
+constexpr float kE2Shift = 12582912.0f;  // 1.5 * 2^23
+constexpr float kE2C3 = 0.05517166853f, kE2C2 = 0.24261112511f, kE2C1 = 0.69326096773f, kE2C0 = 0.99992805719f;
 __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   x = make_float2(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f));
-  const float2 t = __fadd2_rn(x, make_float2(12582912.0f, 12582912.0f));
-  const float2 jf = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+  const float2 t = __fadd2_rn(x, make_float2(kE2Shift, kE2Shift));
+  const float2 jf = __fadd2_rn(t, make_float2(-kE2Shift, -kE2Shift));
   const float2 f = __fadd2_rn(x, make_float2(-jf.x, -jf.y));
-  float2 p = __ffma2_rn(make_float2(0.05517166853f, 0.05517166853f), f, make_float2(0.24261112511f, 0.24261112511f));
-  p = __ffma2_rn(p, f, make_float2(0.69326096773f, 0.69326096773f));
-  p = __ffma2_rn(p, f, make_float2(0.99992805719f, 0.99992805719f));
+  float2 p = __ffma2_rn(make_float2(kE2C3, kE2C3), f, make_float2(kE2C2, kE2C2));
+  p = __ffma2_rn(p, f, make_float2(kE2C1, kE2C1));
+  p = __ffma2_rn(p, f, make_float2(kE2C0, kE2C0));
   return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
                      __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
@@ -215,13 +217,14 @@ __global__ void __launch_bounds__(192, 2)
         for (int i = 0; i < kKT; ++i)
           if (i >= kvalid) sv[i] = -INFINITY;
       }
-      // row max: 8 independent chains of three-input maxima (32 instructions for 64
-      // scores instead of 63)
+      // row max: 8 independent chains, each a two-input max of columns c and 56 + c and
+      // three three-input maxima over columns 8..55 (32 instructions for 64 scores
+      // instead of 63)
       float m8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = sv[i];
+      for (int c = 0; c < 8; ++c) m8[c] = fmaxf(sv[c], sv[56 + c]);
 #pragma unroll
-      for (int i = 8; i < kKT; i += 16) {
+      for (int i = 8; i < 56; i += 16) {
 #pragma unroll
         for (int c = 0; c < 8; ++c) m8[c] = fmax3(m8[c], sv[i + c], sv[i + 8 + c]);
       }
@@ -342,23 +345,31 @@ __global__ void __launch_bounds__(192, 2)
   }
 }
 
-// ---------------------------------------------------------------- ping-pong kernel
+// ------------------------------------------------------- warp-specialised kernel
 // Two 128-query tiles per CTA share every 128-key K / V^T tile, and the two softmax
-// warpgroups alternate with the tensor core:
+// warpgroups alternate with the tensor core (one CTA per SM, 12 warps):
 //   warp 0     TMA: per key tile of 128 the K tile [128 keys][64] (128B swizzle) and
 //              V^T as two [64 dims][64 keys] halves, into a 4-stage ring;
-//   warp 1     one thread issues, per key tile j and query tile t, S_t = Q_t K_j^T
-//              (M=128, N=128, K=64; Q_t read from TMEM) and, once softmax t published
-//              P_t, O_t += P_t [V_j^T; 1; 0] (M=128, N=80, K=128; P_t read from TMEM);
-//   warps 2-5  softmax of query tile 0, warps 6-9 of query tile 1: thread = query row
-//              (its TMEM lane); S_t read into registers, p = 2^(s*c - m*c) written back
-//              as f16 over S_t's first 64 columns: the A operand of the P V product.
+//   warp 1     one thread issues, per key tile j and query tile t, once softmax t
+//              published P_t(j): O_t += P_t(j) [V_j^T; 1; 0] (M=128, N=80, K=128; P_t
+//              read from TMEM) and at once S_t(j+1) = Q_t K_{j+1}^T (M=128, N=128,
+//              K=64; Q_t read from TMEM) into the same columns;
+//   warps 4-7  softmax of query tile 0, warps 8-11 of query tile 1: thread = query row
+//              (its TMEM lane); the whole 128-score row in registers (one pass), p =
+//              2^(s*c - m*c) written back as f16 over S_t's first 64 columns: the A
+//              operand of the P V product. Warps 2-3 are idle.
 // TMEM (512 columns): S_0 | S_1 (128 each, P_t aliases S_t), O_0 | O_1 (80 each: 64
 // dims, the row sums from the ones row of V^T, zeros), Q_0 | Q_1 (32 each: f16 pairs).
-// S_t of key tile j+1 is issued only after P_t V_j completed (it overwrites P_t), so O_t
-// is never being written while softmax t holds S_t: the lazy rescale of O_t needs no
-// extra wait. Shared memory carries only K and V^T (no Q or P reads): about 108 KB of
-// traffic per 256 x 128 block of scores instead of 268 KB with Q and P in shared memory.
+// The tcgen05.mma operations of one thread run in issue order, so S_t(j+1) overwrites
+// P_t(j) only after P_t(j) V_j read it, and S_t(j+1) completing implies P_t(j) V_j
+// completed: O_t is never being written while softmax t holds S_t, so the lazy rescale
+// of O_t needs no extra wait.
+// Measured on a B200 against k_attn_tc: 0.92 against 0.82 ms at the C3 shape, 1.19
+// against 1.18 ms at the C4 global shape. Each softmax warpgroup computes a 128-key tile
+// in about 1450 cycles and then waits about 1350 for its P V and next S products, whose
+// tensor-pipe latency (issue to completion about 1130 cycles for 736 cycles of MMA
+// work) this structure exposes once per tile; so it stays the alternative, not the
+// default.
 constexpr int kPKT = 128;                            // keys per tile
 constexpr int kPStages = 4;
 constexpr int kPKBytes = kPKT * 64 * 2;              // K tile [128 keys][64 dims]
@@ -369,20 +380,54 @@ constexpr int kPSmem = 1024 + kPStages * kPStageBytes + 256;  // > 114 KB: one C
 constexpr uint32_t kPTmemCols = 512;
 constexpr uint32_t kPColO = 256, kPColQ = 416;
 
-// D[tmem] (+)= A[tmem] * B[smem]^T (A: M rows in lanes, K along columns as f16 pairs,
-// low half first)
-__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+
+// Register split of the warp-specialised kernel: launched with 384 threads at 168
+// registers (64 512), warpgroup 0 (TMA, MMA, two idle warps) gives registers back down
+// to 56 and the two softmax warpgroups grow to 224, enough to hold a whole 128-score row
+// (one pass over S). setmaxnreg.inc waits until the registers are free, so the split
+// must not exceed the launch's total; the host checks the kernel's register count.
+constexpr int kWThreads = 384;
+constexpr int kWRegsLaunch = 168, kWRegsCtl = 56, kWRegsSoft = 224;
+static_assert(128 * kWRegsCtl + 256 * kWRegsSoft <= kWThreads * kWRegsLaunch, "register split exceeds the launch");
+
+// 2^a of 64 arguments as 32 f16 pairs (pair c = arguments 2c, 2c+1, low half first): a
+// quarter by exp2_poly2's polynomial (pairs 4i), staged across eight chains, the rest on
+// MUFU.
+__device__ __forceinline__ void exp2_pack64(const float* a, uint32_t (&pk)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    if ((i & 3) == 0) continue;
+    __half2 hp = __floats2half2_rn(ex2_approx(a[2 * i]), ex2_approx(a[2 * i + 1]));
+    pk[i] = *reinterpret_cast<uint32_t*>(&hp);
+  }
+  float2 x[8], t[8], q[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    x[c] = make_float2(fmaxf(a[8 * c], -125.0f), fmaxf(a[8 * c + 1], -125.0f));
+    t[c] = __fadd2_rn(x[c], make_float2(kE2Shift, kE2Shift));
+  }
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const float2 jf = __fadd2_rn(t[c], make_float2(-kE2Shift, -kE2Shift));
+    x[c] = __fadd2_rn(x[c], make_float2(-jf.x, -jf.y));
+  }
+#pragma unroll
+  for (int c = 0; c < 8; ++c) q[c] = __ffma2_rn(make_float2(kE2C3, kE2C3), x[c], make_float2(kE2C2, kE2C2));
+#pragma unroll
+  for (int c = 0; c < 8; ++c) q[c] = __ffma2_rn(q[c], x[c], make_float2(kE2C1, kE2C1));
+#pragma unroll
+  for (int c = 0; c < 8; ++c) q[c] = __ffma2_rn(q[c], x[c], make_float2(kE2C0, kE2C0));
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const float e0 = __uint_as_float(__float_as_uint(q[c].x) + (__float_as_uint(t[c].x) << 23));
+    const float e1 = __uint_as_float(__float_as_uint(q[c].y) + (__float_as_uint(t[c].y) << 23));
+    __half2 hp = __floats2half2_rn(e0, e1);
+    pk[4 * c] = *reinterpret_cast<uint32_t*>(&hp);
+  }
 }
 
-__global__ void __launch_bounds__(320, 1)
-    k_attn_pp(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+__global__ void __launch_bounds__(kWThreads, 1)
+    k_attn_ws(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
               const __half* __restrict__ qkv, int seqlen, int H, int D, __half* __restrict__ out, float sl2, int q8,
               int* status) {
   extern __shared__ uint8_t smem_raw[];
@@ -433,8 +478,9 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    if (lane == 0) {
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kWRegsCtl));
+    if (warp == 0 && lane == 0) {
       // ---------------------------------------------------------------- TMA
       const int vrow = (sq * H + h) * 64;
       for (int j = 0; j < nkt; ++j) {
@@ -446,34 +492,32 @@ __global__ void __launch_bounds__(320, 1)
         tma_load_2d(sb + kPKBytes, &tmV, &kv_full[st], j * kPKT, vrow);
         tma_load_2d(sb + kPKBytes + kPVSub, &tmV, &kv_full[st], j * kPKT + 64, vrow);
       }
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
       // ---------------------------------------------------------------- MMA
+      // Per key tile j and query tile t: O_t += P_t(j) [V_j^T; 1; 0] as soon as P_t(j) is
+      // published, then at once S_t(j+1) = Q_t K_{j+1}^T into the same TMEM columns.
+      // tcgen05.mma operations of one thread run in issue order, so P_t(j) is read before
+      // S_t(j+1) overwrites it, and S_t(j+1) completing implies P_t(j) V_j completed.
       constexpr uint32_t idS = umma_idesc_f16(128, kPKT);
       constexpr uint32_t idO = umma_idesc_f16(128, kPVRows);
       bool ok = true;
       for (int t = 0; t < nact && ok; ++t) ok = mbar_wait(&q_ready[t], 0, status, kStatusTimeoutFull);
-      for (int j = 0; j < nkt && ok; ++j) {
-        const int st = j % kPStages;
-        if (!mbar_wait(&kv_full[st], (j / kPStages) & 1, status, kStatusTimeoutFull)) break;
+      if (ok) ok = mbar_wait(&kv_full[0], 0, status, kStatusTimeoutFull);
+      if (ok) {
         tc_fence_after();
-        const uint8_t* sb = smem + st * kPStageBytes;
-        const uint64_t kdesc = umma_desc_sw128(smem_u32(sb));
+        const uint64_t kdesc = umma_desc_sw128(smem_u32(smem));
         for (int t = 0; t < nact; ++t) {
-          // S_t overwrites P_t of the previous key tile: wait until P_t V_{j-1} is done
-          if (j > 0 && !mbar_wait(&pv_done[t], (j - 1) & 1, status, kStatusTimeoutAccum)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t tS = tmem + 128 * t, tQ = tmem + kPColQ + 32 * t;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) umma_f16_ts(tS, tQ + 8 * k, kdesc + 2 * k, idS, k > 0 ? 1u : 0u);
+          for (int k = 0; k < 4; ++k)
+            umma_f16_tmem_a(tmem + 128 * t, tmem + kPColQ + 32 * t + 8 * k, kdesc + 2 * k, idS, k > 0 ? 1u : 0u);
           umma_commit(&s_full[t]);
         }
-        if (!ok) break;
+      }
+      for (int j = 0; j < nkt && ok; ++j) {
+        const int st = j % kPStages, st1 = (j + 1) % kPStages;
+        const uint8_t* sb = smem + st * kPStageBytes;
+        const uint64_t kdesc1 = umma_desc_sw128(smem_u32(smem + st1 * kPStageBytes));
+        bool next_ready = false;
         for (int t = 0; t < nact; ++t) {
           if (!mbar_wait(&p_ready[t], j & 1, status, kStatusTimeoutFull)) {
             ok = false;
@@ -484,9 +528,23 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint64_t vdesc = umma_desc_sw128(smem_u32(sb + kPKBytes + (kk >> 2) * kPVSub)) + 2 * (kk & 3);
-            umma_f16_ts(tO, tP + 8 * kk, vdesc, idO, (j > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_tmem_a(tO, tP + 8 * kk, vdesc, idO, (j > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&pv_done[t]);
+          if (j + 1 < nkt) {
+            if (!next_ready) {
+              if (!mbar_wait(&kv_full[st1], ((j + 1) / kPStages) & 1, status, kStatusTimeoutFull)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              next_ready = true;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              umma_f16_tmem_a(tmem + 128 * t, tmem + kPColQ + 32 * t + 8 * k, kdesc1 + 2 * k, idS, k > 0 ? 1u : 0u);
+            umma_commit(&s_full[t]);
+          }
         }
         if (!ok) break;
         umma_commit(&kv_empty[st]);
@@ -494,8 +552,9 @@ __global__ void __launch_bounds__(320, 1)
     }
     __syncwarp();
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kWRegsSoft));
     // ------------------------------------------------------------------ softmax
-    const int t = (warp - 2) >> 2;
+    const int t = (warp >> 2) - 1;
     const int qq = warp & 3;
     const int r = qq * 32 + lane;                  // query row within tile t == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(qq * 32) << 16;
@@ -535,31 +594,44 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         tc_fence_after();
-        // pass 1: the row max over the tile's 128 scores (32 columns at a time, so no
-        // thread holds the whole row); keys past the sequence are masked
+        // the whole 128-score row in registers
+        float sv[128];
+        {
+          uint32_t ra[32], rb[32], rc[32], rd[32];
+          tmem_ld32(tS, ra);
+          tmem_ld32(tS + 32, rb);
+          tmem_ld32(tS + 64, rc);
+          tmem_ld32(tS + 96, rd);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            sv[i] = __uint_as_float(ra[i]);
+            sv[32 + i] = __uint_as_float(rb[i]);
+            sv[64 + i] = __uint_as_float(rc[i]);
+            sv[96 + i] = __uint_as_float(rd[i]);
+          }
+        }
         const int kvalid = seqlen - j * kPKT;       // keys of this tile inside the sequence (>= 1)
+        if (kvalid < kPKT) {  // the last tile of the sequence only (uniform branch)
+#pragma unroll
+          for (int i = 0; i < kPKT; ++i)
+            if (i >= kvalid) sv[i] = -INFINITY;
+        }
+        // row max: 8 chains over columns 0..119 by three-input maxima, then 120..127
         float m8[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
+        for (int c = 0; c < 8; ++c) m8[c] = fmax3(sv[c], sv[8 + c], sv[16 + c]);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ra[32];
-          tmem_ld32(tS + 32 * c, ra);
-          tmem_wait_ld();
-          float sv[32];
+        for (int i = 24; i < 120; i += 16) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(ra[i]);
-          if (kvalid < kPKT) {  // the last tile of the sequence only (uniform branch)
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (32 * c + i >= kvalid) sv[i] = -INFINITY;
-          }
-#pragma unroll
-          for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], fmax3(sv[i], sv[8 + i], sv[16 + i]), sv[24 + i]);
+          for (int c = 0; c < 8; ++c) m8[c] = fmax3(m8[c], sv[i + c], sv[i + 8 + c]);
         }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) m8[c] = fmaxf(m8[c], sv[120 + c]);
         const float mt = fmaxf(fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), m8[6]), m8[7]);
         // lazy rescale (the running max is raised only when a tile's max exceeds it by
-        // more than 2^8); O_t is stable here: P_t V_{j-1} completed before S_t was issued
+        // more than 2^8); O_t is stable here: P_t V_{j-1} was issued before S_t(j), whose
+        // completion this thread waited for
         const bool need = (j > 0) && ((mt - m) * sl2 > kRescaleLog2);
         if (j == 0) m = mt;
         if (__any_sync(0xffffffffu, need)) {
@@ -580,46 +652,19 @@ __global__ void __launch_bounds__(320, 1)
           tmem_st1(tO + 64, rc);
           if (need) m = mt;
         }
-        // pass 2: p = 2^(s*c - m*c) for 64 keys at a time, written as f16 pairs over the
-        // first 64 columns of S_t (keys 0..63 -> columns 0..31 once both of their S
-        // columns are in registers; keys 64..127 -> columns 32..63, already read)
+        // p = 2^(s*c - m*c) as f16 pairs over the first 64 columns of S_t (the TMEM A
+        // operand of O_t += P_t V): keys 0..63 -> columns 0..31, 64..127 -> 32..63
         const float mc = m * sl2;
 #pragma unroll
+        for (int i = 0; i < kPKT; i += 2) {
+          const float2 a = __ffma2_rn(make_float2(sv[i], sv[i + 1]), make_float2(sl2, sl2), make_float2(-mc, -mc));
+          sv[i] = a.x;
+          sv[i + 1] = a.y;
+        }
+#pragma unroll
         for (int half = 0; half < 2; ++half) {
-          float sv[64];
-          {
-            uint32_t ra[32], rb[32];
-            tmem_ld32(tS + 64 * half, ra);
-            tmem_ld32(tS + 64 * half + 32, rb);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              sv[i] = __uint_as_float(ra[i]);
-              sv[32 + i] = __uint_as_float(rb[i]);
-            }
-            if (kvalid < kPKT) {
-#pragma unroll
-              for (int i = 0; i < 64; ++i)
-                if (64 * half + i >= kvalid) sv[i] = -INFINITY;
-            }
-          }
           uint32_t pk[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float2 a2 = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), make_float2(sl2, sl2),
-                                         make_float2(-mc, -mc));
-            float p0, p1;
-            if ((i & 3) == 0) {  // a quarter of the exponentials on the FMA pipe, the rest on MUFU
-              const float2 e2 = exp2_poly2(a2);
-              p0 = e2.x;
-              p1 = e2.y;
-            } else {
-              p0 = ex2_approx(a2.x);
-              p1 = ex2_approx(a2.y);
-            }
-            __half2 hp = __floats2half2_rn(p0, p1);
-            pk[i] = *reinterpret_cast<uint32_t*>(&hp);
-          }
+          exp2_pack64(sv + 64 * half, pk);
           tmem_st32(tS + 32 * half, pk);
         }
         tmem_wait_st();
@@ -686,8 +731,8 @@ __global__ void __launch_bounds__(320, 1)
 // [nseq*seqlen][D]. The columns of vt beyond seqlen are padding that is never read:
 // the V^T tensor map is seqlen wide, so the TMA fills out-of-range keys with zeros.
 // attention_tc runs the 128-query kernel (2 CTAs per SM, P in shared memory);
-// $DA3B_ATTN_PP=1 (read once per process) selects the ping-pong kernel, which is
-// correct but measured slower (1.52 against 1.03 ms at the C3 shape).
+// $DA3B_ATTN_PP=1 (read once per process) selects the warp-specialised kernel, which is
+// correct but measured slower at the C3 shape (0.92 against 0.82 ms).
 static bool attn_pp() {
   static const bool pp = [] {
     const char* e = getenv("DA3B_ATTN_PP");
@@ -707,19 +752,30 @@ static int attention_pp(const __half* qkv, const __half* vt, int ld_vt, int nseq
   cudaGetDevice(&dev);
   const uint64_t bit = uint64_t(1) << (dev & 63);
   if (!(attr_set.load(std::memory_order_acquire) & bit)) {
-    if (cudaFuncSetAttribute(k_attn_pp, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem) != cudaSuccess)
+    if (cudaFuncSetAttribute(k_attn_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem) != cudaSuccess)
       return -3;
     attr_set.fetch_or(bit, std::memory_order_acq_rel);
   }
   const int ntiles = (seqlen + 127) / 128;
   dim3 grid((ntiles + 1) / 2, H, nseq);
   const float sl2 = 0.125f * 1.4426950408889634f;
-  k_attn_pp<<<grid, 320, kPSmem, s>>>(tk, tv, qkv, seqlen, H, D, out, sl2, q8, status);
+  // the register split (setmaxnreg) needs the kernel to launch with its full share
+  static std::atomic<int> regs_fit{0};  // 0 = unchecked, 1 = fits, -1 = does not
+  if (regs_fit.load(std::memory_order_acquire) == 0) {
+    cudaFuncAttributes fa;
+    memset(&fa, 0, sizeof(fa));
+    if (cudaFuncGetAttributes(&fa, k_attn_ws) != cudaSuccess) return -5;
+    const bool fits = fa.numRegs * kWThreads >= 128 * kWRegsCtl + 256 * kWRegsSoft;
+    if (!fits) fprintf(stderr, "[da3b] attention: kernel has %d registers, the split needs %d\n", fa.numRegs, kWRegsLaunch);
+    regs_fit.store(fits ? 1 : -1, std::memory_order_release);
+  }
+  if (regs_fit.load(std::memory_order_acquire) < 0) return -5;
+  k_attn_ws<<<grid, kWThreads, kPSmem, s>>>(tk, tv, qkv, seqlen, H, D, out, sl2, q8, status);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     cudaFuncAttributes fa;
     memset(&fa, 0, sizeof(fa));
-    cudaFuncGetAttributes(&fa, k_attn_pp);
+    cudaFuncGetAttributes(&fa, k_attn_ws);
     fprintf(stderr, "[da3b] attention launch failed: %s (regs %d, max threads %d, smem %d)\n", cudaGetErrorString(e),
             fa.numRegs, fa.maxThreadsPerBlock, kPSmem);
     return -4;

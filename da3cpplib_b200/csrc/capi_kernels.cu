@@ -65,6 +65,70 @@ __global__ void k_wait_probe(int* status, uint64_t limit_ns, int use_tmem, unsig
   if (threadIdx.x == 0 && elapsed) *elapsed = ok ? 0ull : static_cast<unsigned long long>(t1 - t0);
 }
 
+// Tensor-pipe rate probe: one CTA per SM; thread 0 issues iters x 4 back-to-back
+// M = 128, K = 16 f16 MMAs (N columns) into one TMEM accumulator, A from shared memory
+// (A_TMEM = 0) or tensor memory (A_TMEM = 1), B from shared memory (zeros), and writes
+// the cycles from the first issue to the completion of the last to cycles[blockIdx.x].
+// The values in the A columns of tensor memory are whatever the allocation holds: the
+// probe times the pipe, not the arithmetic.
+template <int A_TMEM, int N>
+__global__ void __launch_bounds__(128, 1) k_mma_rate(int iters, unsigned long long* cycles, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;          // [128][64] f16, 128B swizzle
+  uint8_t* sB = smem + 16384;  // [256][64] f16
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 16384 + 32768);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 1);
+  for (int i = threadIdx.x; i < (16384 + 32768) / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0u, 0u, 0u, 0u);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (threadIdx.x < 32) tmem_alloc(slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  if (threadIdx.x == 0) {
+    constexpr uint32_t id = umma_idesc_f16(128, N);
+    const uint64_t ad = umma_desc_sw128(smem_u32(sA)), bd = umma_desc_sw128(smem_u32(sB));
+    for (int k = 0; k < 4; ++k) {
+      if (A_TMEM) umma_f16_tmem_a(tmem, tmem + 256 + 8 * k, bd + 2 * k, id, k > 0 ? 1u : 0u);
+      else umma_f16(tmem, ad + 2 * k, bd + 2 * k, id, k > 0 ? 1u : 0u);
+    }
+    umma_commit(bar);
+    bool ok = mbar_wait(bar, 0, status, kStatusTimeoutAccum);
+    const unsigned long long t0 = clock64();
+    for (int i = 0; i < iters && ok; ++i) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (A_TMEM) umma_f16_tmem_a(tmem, tmem + 256 + 8 * k, bd + 2 * k, id, 1u);
+        else umma_f16(tmem, ad + 2 * k, bd + 2 * k, id, 1u);
+      }
+    }
+    umma_commit(bar);
+    if (ok) ok = mbar_wait(bar, 1, status, kStatusTimeoutAccum);
+    cycles[blockIdx.x] = ok ? clock64() - t0 : 0ull;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int A_TMEM, int N>
+static int mma_rate(int ctas, int iters, unsigned long long* cycles, int* status, cudaStream_t s) {
+  const int smem = 120 * 1024;  // one CTA per SM
+  if (cudaFuncSetAttribute(k_mma_rate<A_TMEM, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return -3;
+  k_mma_rate<A_TMEM, N><<<ctas, 128, smem, s>>>(iters, cycles, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
 }  // namespace da3b
 
 using namespace da3b;
@@ -162,6 +226,21 @@ DA3B_API int da3b_debug_wait_timeout(unsigned long long limit_ns, int use_tmem, 
   if (!st) return -101;
   k_wait_probe<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(st, limit_ns, use_tmem ? 1 : 0, elapsed_dev);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+DA3B_API int da3b_debug_mma_cycles(int n, int a_tmem, int iters, int ctas, unsigned long long* cycles_dev, void* stream) {
+  if (!cycles_dev || iters <= 0 || iters > 100000 || ctas <= 0 || ctas > 1024) return -100;
+  int* st = device_status_word();
+  if (!st) return -101;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define DA3B_MMA_RATE(NN) \
+  if (n == NN) return a_tmem ? mma_rate<1, NN>(ctas, iters, cycles_dev, st, s) : mma_rate<0, NN>(ctas, iters, cycles_dev, st, s);
+  DA3B_MMA_RATE(64)
+  DA3B_MMA_RATE(80)
+  DA3B_MMA_RATE(128)
+  DA3B_MMA_RATE(256)
+#undef DA3B_MMA_RATE
+  return -100;
 }
 
 DA3B_API int da3b_transpose_v(const void* qkv, int nseq, int seqlen, int heads, void* vt, int ld_vt, void* stream) {

@@ -8,7 +8,11 @@ M in {1370, 8*1370, 64*1370} x (K, N) in {(384, 1152), (768, 3072), (1024, 4096)
 Part B: DPT-head 3x3 stride-1 pad-1 convs, NHWC f16, C_in = C_out in {64, 128, 256},
 spatial 37..296, batch 8 (da3b_conv_nhwc).
 attn: da3b_attention at the C3 shape (64 x 1370 tokens, 16 heads) and the DA3
-multi-view global layer (8 views x 1297 tokens per scene).
+multi-view global layer (8 views x 1297 tokens per scene), each with the V^T
+transpose and as the flash-attention kernel alone (da3b_attention_vt), next to cuDNN's
+fused attention through torch on the same tensors as a yardstick.
+mma: the tensor-pipe cost of one M=128, K=16 f16 tcgen05.mma for N = 64..256, A from
+shared or tensor memory (da3b_debug_mma_cycles, one CTA per SM, one accumulator).
 out2: da3b_output_conv2 (upsample 296 -> 518 + 3x3 conv 128 -> 32 + 1x1 -> depth) at the
 C3 head shape, fused and through a materialised upsampled map.
 ray: da3b_ray_pose (the ray->pose solver, both host round trips included; wall time)
@@ -25,7 +29,7 @@ Each line: {"part", "case", "ms", "tflops", "frac", "peak"}; frac is against the
 measured dense bf16 burst peak of this GPU pool (MEASURED_PEAKS.json, else the pool's
 fallback figure). Times are CUDA events around `reps` back-to-back launches on the
 launching stream after 3 warm-up launches. Usage:
-    python -m da3cpplib_b200.microbench [--part A|B|attn|all] [--m 87680] [--reps 20]
+    python -m da3cpplib_b200.microbench [--part A|B|attn|mma|all] [--m 87680] [--reps 20]
 """
 from __future__ import annotations
 
@@ -77,7 +81,7 @@ def main(argv=None):
     from . import _lib
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("--part", default="all", choices=["A", "A8", "B", "attn", "up", "pre", "ray", "out2", "c4", "all"])
+    ap.add_argument("--part", default="all", choices=["A", "A8", "B", "attn", "up", "pre", "ray", "out2", "c4", "mma", "all"])
     ap.add_argument("--scenes", type=int, default=16, help="c4: scenes of 8 views")
     ap.add_argument("--m", type=int, default=0, help="Part A: only this M")
     ap.add_argument("--kn", default="", help="Part A: only this K,N (e.g. 1024,4096)")
@@ -256,7 +260,52 @@ def main(argv=None):
 
             ms = timeit(run)
             emit("attn", f"{tag}: nseq={nseq} seqlen={seqlen} heads={heads}", ms, 4.0 * nseq * seqlen * seqlen * D)
+            # the flash-attention kernel alone, V^T prepared once (as the QKV GEMM epilogue
+            # provides it inside the engine)
+            ld = (seqlen + 7) // 8 * 8
+            vt = torch.empty(nseq * heads * 64 * ld, dtype=torch.float16, device="cuda")
+            assert L.da3b_transpose_v(P(qkv), nseq, seqlen, heads, P(vt), ld, S) == 0
+
+            def run_vt():
+                rc = L.da3b_attention_vt(P(qkv), P(vt), ld, nseq, seqlen, heads, P(out), S)
+                if rc:
+                    raise RuntimeError(f"da3b_attention_vt rc={rc}")
+
+            ms = timeit(run_vt)
+            emit("attn", f"{tag}, kernel only: nseq={nseq} seqlen={seqlen} heads={heads}", ms,
+                 4.0 * nseq * seqlen * seqlen * D)
+            del vt
+            # yardstick, not part of this library: cuDNN's fused attention through torch on
+            # the same q, k, v (f16, no mask, scale 1/8)
+            try:
+                from torch.nn.attention import SDPBackend, sdpa_kernel
+                q, k, v = (qkv.view(nseq, seqlen, 3, heads, 64)[:, :, i].transpose(1, 2).contiguous() for i in range(3))
+                with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+                    ms = timeit(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v))
+                emit("attn", f"{tag}, cuDNN SDPA via torch (reference): nseq={nseq} seqlen={seqlen} heads={heads}", ms,
+                     4.0 * nseq * seqlen * seqlen * D)
+            except Exception as e:  # noqa: BLE001 - a missing backend only drops the yardstick line
+                print(json.dumps({"part": "attn", "case": f"{tag}, cuDNN SDPA", "unavailable": str(e)[:200]}))
             del qkv, out
+
+    if args.part == "mma":
+        # tensor-pipe cost per M=128, K=16 f16 tcgen05.mma, one CTA per SM, one accumulator
+        nsm = torch.cuda.get_device_properties(0).multi_processor_count
+        cyc = torch.zeros(nsm, dtype=torch.int64, device="cuda")
+        iters = 2000
+        for a_tmem in (0, 1):
+            for n in (64, 80, 128, 256):
+                cyc.zero_()
+                rc = L.da3b_debug_mma_cycles(n, a_tmem, iters, nsm, P(cyc), S)
+                torch.cuda.synchronize()
+                if rc or L.da3b_device_status() != 0:
+                    raise RuntimeError(f"da3b_debug_mma_cycles rc={rc}")
+                c = cyc.float()
+                per = c[c > 0].median().item() / (iters * 4)
+                full = 128 * n * 16 / 4096  # cycles at 4096 f16 MAC per clock per SM
+                print(json.dumps({"part": "mma", "A": "tmem" if a_tmem else "smem", "M": 128, "N": n, "K": 16,
+                                  "cycles": round(per, 1), "full_rate_cycles": full,
+                                  "frac": round(full / per, 3)}), flush=True)
 
     if args.part in ("out2", "all"):
         B, hs, C, H = args.batch if args.batch != 8 else 64, 296, 128, 518

@@ -94,6 +94,14 @@ DA3B_API int da3b_linear_q8q8_i8(const void* qx, const float* dx, int M, int K, 
 DA3B_API int da3b_debug_wait_timeout(unsigned long long limit_ns, int use_tmem, int* status_dev,
                                      unsigned long long* elapsed_dev, void* stream);
 
+/* Tensor-pipe rate probe (no counterpart in the reference; measurement only): ctas CTAs
+ * of one per SM each issue iters x 4 back-to-back tcgen05.mma of M = 128, K = 16, N = n
+ * (64, 80, 128 or 256) f16 into one TMEM accumulator, A from shared memory
+ * or (a_tmem != 0) tensor memory, and write the cycles from the first issue to the
+ * completion of the last to cycles_dev[cta] (u64; 0 if a bounded wait gave up). */
+DA3B_API int da3b_debug_mma_cycles(int n, int a_tmem, int iters, int ctas, unsigned long long* cycles_dev,
+                                   void* stream);
+
 /* The two halves of da3b_attention, for callers that keep V transposed (the engine's
  * QKV GEMM epilogue writes it that way): da3b_transpose_v writes V^T f16
  * [nseq][heads][64][ld_vt] (ld_vt >= seqlen, a multiple of 8; columns beyond seqlen are

@@ -208,10 +208,13 @@ def test_upsample_align_corners(lib, B, hs, ws, C, H, W):
     close(out, ref, rel=2e-3, abs_=2e-3)
 
 
-@pytest.mark.parametrize("nseq,seqlen,heads", [(2, 1370, 4), (1, 300, 2), (3, 129, 2), (1, 2 * 1297, 3)])
+@pytest.mark.parametrize("nseq,seqlen,heads", [(2, 1370, 4), (1, 300, 2), (3, 129, 2), (2, 100, 2), (1, 257, 2),
+                                                (1, 2 * 1297, 3)])
 def test_attention_pp_kernel(nseq, seqlen, heads):
-    """The ping-pong attention kernel, selectable with DA3B_ATTN_PP=1 (read once per
-    process, so it runs in a fresh subprocess), against torch fp32."""
+    """The warp-specialised attention kernel (two query tiles per CTA, one-pass softmax
+    over 128-key tiles), selectable with DA3B_ATTN_PP=1 (read once per process, so it
+    runs in a fresh subprocess), against torch fp32. The sizes cover CTAs with one and
+    with two query tiles and ragged last key tiles."""
     import subprocess
     import sys
 
