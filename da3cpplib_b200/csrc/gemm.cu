@@ -565,8 +565,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // pieces XOR-swizzled by row & 7: conflict-free both ways) and read back so that lane
 // l holds columns 8*(l&3) .. +7 of row 8k + (l>>2), k = 0..3. All per-element work then
 // runs in that layout, and each global store instruction covers 8 rows x 64 contiguous
-// bytes. kEpiF16: bias, res1/res2, out_relu, activation; kEpiQKV: bias, q|k thirds
-// stored the same way, the v third transposed per (sequence, head) into vt.
+// bytes. kEpiF16 with res1/res2/out_relu: bias, residual addends, relu copy, activation
+// in that layout; kEpiF16 without them and the q|k thirds of kEpiQKV: the row-layout
+// path (bias and activation per row, f16 staging); the v third of kEpiQKV transposed per
+// (sequence, head) into vt.
 // bsm: this warp's bias slice [c_end - c_begin] in shared memory (zeros without bias).
 template <int BN>
 __device__ __forceinline__ void epi_transposed(const GemmGeom& g, const EpiArgs& e, uint32_t tbase, int c_begin,
@@ -581,6 +583,71 @@ __device__ __forceinline__ void epi_transposed(const GemmGeom& g, const EpiArgs&
     tmem_wait_ld();
     const int n_base = n_tile + c;
     if (n_base >= g.N) continue;  // warp-uniform
+    if (e.kind == kEpiQKV ? n_base < 2 * e.vt_d : (e.kind == kEpiF16 && !e.res1 && !e.res2 && !e.out_relu)) {
+      // Plain f16 output: bias and activation while the lane holds its own row (columns
+      // c .. c+31), then f16 staging: each lane writes its row's 64 bytes (16-byte pieces
+      // swizzled by (row >> 1) & 3) and reads back 8 consecutive columns of row
+      // 8k + (lane >> 2); both phases are conflict-free, and each store still covers
+      // 8 rows x 64 contiguous bytes. Half the staged bytes of the f32 path below and
+      // about a third of its shared-memory instructions: the tensor pipe runs measurably
+      // slower while epilogue warps issue, so the epilogue is kept short.
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 bb = *reinterpret_cast<const float4*>(bsm + (c - c_begin) + j);
+        v[j] = __uint_as_float(raw[j]) + bb.x;
+        v[j + 1] = __uint_as_float(raw[j + 1]) + bb.y;
+        v[j + 2] = __uint_as_float(raw[j + 2]) + bb.z;
+        v[j + 3] = __uint_as_float(raw[j + 3]) + bb.w;
+      }
+      if (e.kind == kEpiF16) {
+        if (e.act == kActGelu) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float2 gv = gelu_erf2(make_float2(v[i], v[i + 1]));
+            v[i] = gv.x;
+            v[i + 1] = gv.y;
+          }
+        } else if (e.act == kActGeluR) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float2 gv = gelu_r2(make_float2(v[i], v[i + 1]));
+            v[i] = gv.x;
+            v[i + 1] = gv.y;
+          }
+        } else if (e.act == kActRelu) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.0f);
+        }
+      }
+      uint32_t h[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        __half2 hh = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+        h[i] = *reinterpret_cast<uint32_t*>(&hh);
+      }
+      uint4* srow = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(stg) + lane * 64);
+      const int wsw = (lane >> 1) & 3;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) srow[q ^ wsw] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+      __syncwarp();
+      uint4 o[4];
+      int rr[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int r = 8 * k + rsub;
+        rr[k] = __shfl_sync(0xffffffffu, orow, r);
+        o[k] = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(stg) + r * 64)[s ^ ((r >> 1) & 3)];
+      }
+      __syncwarp();  // every lane has read the staging buffer before the next chunk overwrites it
+      const int n = n_base + 8 * s;
+      if (n < g.N) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (rr[k] >= 0) *reinterpret_cast<uint4*>(e.out + static_cast<size_t>(rr[k]) * e.ld_out + n) = o[k];
+      }
+      continue;
+    }
     if (e.kind == kEpiQKV && n_base >= 2 * e.vt_d) {
       // v third: lanes are consecutive tokens, so each of the 32 columns is one
       // contiguous run of the transposed row
