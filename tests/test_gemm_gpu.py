@@ -60,7 +60,8 @@ def test_dequant_q8_0_exact(lib):
 
 
 @pytest.mark.parametrize("M,K,N", [(1, 64, 32), (127, 384, 1152), (128, 128, 64), (300, 200, 48),
-                                   (1370, 768, 2304), (2740, 1024, 4096), (1370, 4096, 1024), (257, 640, 96)])
+                                   (1370, 768, 2304), (2740, 1024, 4096), (1370, 4096, 1024), (257, 640, 96),
+                                   (20000, 256, 1000)])
 @pytest.mark.parametrize("act", [0, 2, 3])
 def test_linear_f16(lib, M, K, N, act):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + K + N)
