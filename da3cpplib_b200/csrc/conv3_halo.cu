@@ -59,14 +59,13 @@ __device__ __forceinline__ uint64_t desc_noswz(uint32_t saddr, uint32_t lbo, uin
   return d;
 }
 
-__device__ __forceinline__ void ld_h8(const __half* p, float (&v)[8]) {
-  const uint4 u = *reinterpret_cast<const uint4*>(p);
+__device__ __forceinline__ void add_h8(const uint4& u, float (&v)[8]) {
   const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const float2 f = __half22float2(h[k]);
-    v[2 * k] = f.x;
-    v[2 * k + 1] = f.y;
+    v[2 * k] += f.x;
+    v[2 * k + 1] += f.y;
   }
 }
 
@@ -76,6 +75,71 @@ __device__ __forceinline__ void st_h8(__half* p, const float (&v)[8]) {
 #pragma unroll
   for (int k = 0; k < 4; ++k) h[k] = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
   *reinterpret_cast<uint4*>(p) = u;
+}
+
+// Epilogue of one accumulator buffer, this thread's pixel in each 8-wide half (pix,
+// valid): TMEM -> + bias (+ res1 + res2, relu copy, activation) -> f16 NHWC, 32
+// channels (one tcgen05.ld) per chunk. The residual reads of chunk k + kDist are issued
+// before chunk k's stores, and those of the first kDist chunks before the accumulator
+// is waited on: a load cannot be moved above an earlier store through a pointer of the
+// same type, so read one chunk at a time they each paid a full memory latency in turn
+// (about 2 us of a 25 us batch-1 conv). Returns false when the accumulator wait timed out.
+template <int kHalves, int kN, int kDist>
+__device__ __forceinline__ bool halo_epilogue(uint32_t tacc, uint64_t* full, uint32_t parity, int* status,
+                                              const EpiArgs& e, const size_t (&pix)[kHalves],
+                                              const bool (&valid)[kHalves], int n0) {
+  constexpr int kNc = kN / 32, kChunks = kHalves * kNc, kRing = kDist + 1;
+  uint4 ra[kRing][4], rb[kRing][4];
+  auto fetch = [&](int k) {
+    const int h = k / kNc, c = k % kNc;
+    if (!valid[h]) return;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int n = n0 + c * 32 + g * 8;
+      if (e.res1) ra[k % kRing][g] = *reinterpret_cast<const uint4*>(e.res1 + pix[h] * e.ld_res1 + n);
+      if (e.res2) rb[k % kRing][g] = *reinterpret_cast<const uint4*>(e.res2 + pix[h] * e.ld_res2 + n);
+    }
+  };
+#pragma unroll
+  for (int k = 0; k < kDist && k < kChunks; ++k) fetch(k);
+  if (!mbar_wait_warp(full, parity, status, kStatusTimeoutAccum)) return false;
+  tc_fence_after();
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k) {
+    if (k + kDist < kChunks) fetch(k + kDist);
+    const int h = k / kNc, c = k % kNc;
+    uint32_t r[32];
+    tmem_ld32(tacc + h * kN + c * 32, r);
+    tmem_wait_ld();
+    if (!valid[h]) continue;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int n = n0 + c * 32 + g * 8;
+      float v[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[q] = __uint_as_float(r[g * 8 + q]);
+      if (e.bias) {
+        const float4 b0 = __ldg(reinterpret_cast<const float4*>(e.bias + n));
+        const float4 b1 = __ldg(reinterpret_cast<const float4*>(e.bias + n + 4));
+        v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+        v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+      }
+      if (e.res1) add_h8(ra[k % kRing][g], v);
+      if (e.res2) add_h8(rb[k % kRing][g], v);
+      if (e.out_relu) {
+        float rl[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) rl[q] = fmaxf(v[q], 0.0f);
+        st_h8(e.out_relu + pix[h] * e.ld_out + n, rl);
+      }
+      if (e.act == kActRelu) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] = fmaxf(v[q], 0.0f);
+      }
+      st_h8(e.out + pix[h] * e.ld_out + n, v);
+    }
+  }
+  return true;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -220,61 +284,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t tc = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tc) {
       const uint32_t ab = tc & 1;
-      if (!mbar_wait_warp(&acc_full[ab], (tc >> 1) & 1, status, kStatusTimeoutAccum)) break;
-      tc_fence_after();
       const int og = t % n_oc, tp = t / n_oc;
       const int tx = tp % tiles_x, ty = (tp / tiles_x) % tiles_y, b = tp / (tiles_x * tiles_y);
       const int y = ty * kTh + i;
-#pragma unroll 1
+      size_t pix[2];
+      bool valid[2];
+#pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int x = tx * kTw + 8 * half + j;
-        const bool valid = y < H && x < W;
-        const size_t pix = (static_cast<size_t>(b) * H + (valid ? y : 0)) * W + (valid ? x : 0);
-#pragma unroll 1
-        for (int cc = 0; cc < kOCh / 32; ++cc) {
-          uint32_t r[32];
-          tmem_ld32(tmem + ab * 256 + half * 128 + cc * 32 + lane_off, r);
-          tmem_wait_ld();
-          if (valid) {
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              const int n = og * kOCh + cc * 32 + g * 8;
-              float v[8];
-#pragma unroll
-              for (int k = 0; k < 8; ++k) v[k] = __uint_as_float(r[g * 8 + k]);
-              if (e.bias) {
-                const float4 b0 = *reinterpret_cast<const float4*>(e.bias + n);
-                const float4 b1 = *reinterpret_cast<const float4*>(e.bias + n + 4);
-                v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
-                v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
-              }
-              if (e.res1) {
-                float s[8];
-                ld_h8(e.res1 + pix * e.ld_res1 + n, s);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] += s[k];
-              }
-              if (e.res2) {
-                float s[8];
-                ld_h8(e.res2 + pix * e.ld_res2 + n, s);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] += s[k];
-              }
-              if (e.out_relu) {
-                float rl[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) rl[k] = fmaxf(v[k], 0.0f);
-                st_h8(e.out_relu + pix * e.ld_out + n, rl);
-              }
-              if (e.act == kActRelu) {
-#pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] = fmaxf(v[k], 0.0f);
-              }
-              st_h8(e.out + pix * e.ld_out + n, v);
-            }
-          }
-        }
+        valid[half] = y < H && x < W;
+        pix[half] = valid[half] ? (static_cast<size_t>(b) * H + y) * W + x : 0;
       }
+      if (!halo_epilogue<2, kOCh, 2>(tmem + ab * 256 + lane_off, &acc_full[ab], (tc >> 1) & 1, status, e, pix,
+                                     valid, og * kOCh))
+        break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
@@ -460,62 +483,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int it = 0; it < my_tiles; ++it) {
       const uint32_t ab = it & 1;
       const int t = pair + it * npairs;
-      if (!mbar_wait_warp(&acc_full[ab], (it >> 1) & 1, status, kStatusTimeoutAccum)) break;
-      tc_fence_after();
       int b, ty, tx;
       px_tile(t, b, ty, tx);
       const int og = t % n_oc;
       const int y = ty * Cfg::kTh + i;
-#pragma unroll 1
+      size_t pix[kHalves];
+      bool valid[kHalves];
+#pragma unroll
       for (int half = 0; half < kHalves; ++half) {
         const int x = tx * Cfg::kTw + 8 * half + j;
-        const bool valid = b < B && y < H && x < W;
-        const size_t pix = valid ? (static_cast<size_t>(b) * H + y) * W + x : 0;
-#pragma unroll 1
-        for (int cc = 0; cc < N / 32; ++cc) {
-          uint32_t r[32];
-          tmem_ld32(tmem + ab * Cfg::kAccCols + half * N + cc * 32 + lane_off, r);
-          tmem_wait_ld();
-          if (valid) {
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              const int n = og * N + cc * 32 + g * 8;
-              float v[8];
-#pragma unroll
-              for (int k = 0; k < 8; ++k) v[k] = __uint_as_float(r[g * 8 + k]);
-              if (e.bias) {
-                const float4 b0 = *reinterpret_cast<const float4*>(e.bias + n);
-                const float4 b1 = *reinterpret_cast<const float4*>(e.bias + n + 4);
-                v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
-                v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
-              }
-              if (e.res1) {
-                float s[8];
-                ld_h8(e.res1 + pix * e.ld_res1 + n, s);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] += s[k];
-              }
-              if (e.res2) {
-                float s[8];
-                ld_h8(e.res2 + pix * e.ld_res2 + n, s);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] += s[k];
-              }
-              if (e.out_relu) {
-                float rl[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) rl[k] = fmaxf(v[k], 0.0f);
-                st_h8(e.out_relu + pix * e.ld_out + n, rl);
-              }
-              if (e.act == kActRelu) {
-#pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] = fmaxf(v[k], 0.0f);
-              }
-              st_h8(e.out + pix * e.ld_out + n, v);
-            }
-          }
-        }
+        valid[half] = b < B && y < H && x < W;
+        pix[half] = valid[half] ? (static_cast<size_t>(b) * H + y) * W + x : 0;
       }
+      if (!halo_epilogue<kHalves, N, 2>(tmem + ab * Cfg::kAccCols + lane_off, &acc_full[ab], (it >> 1) & 1,
+                                        status, e, pix, valid, og * N))
+        break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote_relaxed(acc_empty_leader[ab]);

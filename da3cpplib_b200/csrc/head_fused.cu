@@ -3,9 +3,10 @@
 // output_dim and the output activation (src/dpt_head.cpp:199-222 and :327-338; the
 // feature map `feat_map` of the reference is never written to memory).
 //
-// One CTA = a strip of 120 output pixels of up to kRows consecutive output rows of one
-// image. The upsampled rows the 3x3 taps need are built once each in shared memory,
-// in a ring of four row slots laid out K-major without swizzle ([16-byte channel
+// One CTA = a strip of 120 output pixels of a band of consecutive output rows of one
+// image (kRows rows, fewer when the batch would otherwise leave SMs idle). The
+// upsampled rows the 3x3 taps need are built once each in shared memory, in a ring of
+// four row slots laid out K-major without swizzle ([16-byte channel
 // chunk][row][8 halves]); slot row r = 32 w + l holds strip pixel 30 w + l, so each
 // 32-row block (one epilogue warp's TMEM lanes) carries its 30 pixels plus the 2 halo
 // pixels on its right. The three horizontal taps go into N: per row and vertical tap
@@ -21,6 +22,7 @@
 //              bias, relu, 1x1 conv, activation;
 //   warp 8     one thread issues the 3 x C/16 MMAs of a row into one of two TMEM
 //              accumulators of 96 columns.
+#include <algorithm>
 #include <atomic>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -40,7 +42,7 @@ constexpr int kTile = 120;             // output pixels per strip: 4 warps x 30
 constexpr int kPitch = kPx + 1;        // rows per channel-chunk plane: the extra 16 B spread the
                                        // builders' 16-byte stores over all banks (2048 B would not)
 constexpr int kSlots = 4;              // upsampled-row ring
-constexpr int kRows = 74;              // output rows per CTA
+constexpr int kRows = 74;              // output rows per CTA (at most)
 constexpr int kBuildWarps = 8;
 constexpr int kThreads = (kBuildWarps + 1) * 32;
 constexpr int kOC = 32;                // output_conv2 hidden channels
@@ -81,7 +83,7 @@ __host__ __device__ inline Layout layout_for(int C) {
 template <int C>
 __global__ void __launch_bounds__(kThreads, 1)
     k_up_out2(const __half* __restrict__ src, int hs, int ws, const __half* __restrict__ pe, int H, int W,
-              const __half* __restrict__ wp, int icp, const EpiArgs e, int* status) {
+              const __half* __restrict__ wp, int icp, int rows, const EpiArgs e, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const Layout L = layout_for(C);
@@ -101,8 +103,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.z, xs0 = blockIdx.x * kTile, ya = blockIdx.y * kRows;
-  const int R = min(kRows, H - ya);
+  const int b = blockIdx.z, xs0 = blockIdx.x * kTile, ya = blockIdx.y * rows;
+  const int R = min(rows, H - ya);
   // align-corners source scale, as k_upsample_ac
   const float sf0 = (W > 1 && ws > 1) ? static_cast<float>(W - 1) / (ws - 1) : static_cast<float>(W) / ws;
   const float sf1 = (H > 1 && hs > 1) ? static_cast<float>(H - 1) / (hs - 1) : static_cast<float>(H) / hs;
@@ -428,12 +430,21 @@ int up_out2(const __half* src, int B, int hs, int ws, int C, const __half* pe, i
       return -3;
     attr_set.fetch_or(uint64_t(1) << (dev & 63));
   }
-  dim3 grid((W + kTile - 1) / kTile, (H + kRows - 1) / kRows, B);
+  // Row bands of kRows, or shorter ones when that would give fewer CTAs than SMs (a
+  // band costs its two halo rows extra; one 518 x 518 image: 5 x 7 CTAs of 74 rows
+  // against 5 x 29 of 18). The rows per CTA do not change any output value.
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int gx = (W + kTile - 1) / kTile;
+  const long long per_band = static_cast<long long>(gx) * B;
+  const int bands = static_cast<int>(std::min<long long>(H, (sms + per_band - 1) / per_band));
+  const int rows = std::max(std::min(kRows, (H + bands - 1) / bands), 1);
+  dim3 grid(gx, (H + rows - 1) / rows, B);
   switch (C) {
-    case 16: k_up_out2<16><<<grid, kThreads, L.total, s>>>(src, hs, ws, pe, H, W, wp, icp, e, status); break;
-    case 32: k_up_out2<32><<<grid, kThreads, L.total, s>>>(src, hs, ws, pe, H, W, wp, icp, e, status); break;
-    case 64: k_up_out2<64><<<grid, kThreads, L.total, s>>>(src, hs, ws, pe, H, W, wp, icp, e, status); break;
-    default: k_up_out2<128><<<grid, kThreads, L.total, s>>>(src, hs, ws, pe, H, W, wp, icp, e, status); break;
+    case 16: k_up_out2<16><<<grid, kThreads, L.total, s>>>(src, hs, ws, pe, H, W, wp, icp, rows, e, status); break;
+    case 32: k_up_out2<32><<<grid, kThreads, L.total, s>>>(src, hs, ws, pe, H, W, wp, icp, rows, e, status); break;
+    case 64: k_up_out2<64><<<grid, kThreads, L.total, s>>>(src, hs, ws, pe, H, W, wp, icp, rows, e, status); break;
+    default: k_up_out2<128><<<grid, kThreads, L.total, s>>>(src, hs, ws, pe, H, W, wp, icp, rows, e, status); break;
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
