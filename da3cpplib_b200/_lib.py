@@ -35,6 +35,7 @@ SIGNATURES = {
                                     c_int, c_void_p]),
     "da3b_debug_wait_timeout": (c_int, [ctypes.c_ulonglong, c_int, c_void_p, c_void_p, c_void_p]),
     "da3b_debug_mma_cycles": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "da3b_set_attention_split": (c_int, [c_int]),
     "da3b_transpose_v": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p]),
     "da3b_attention_vt": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "da3b_attention_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),

@@ -17,6 +17,7 @@
 //              end. P V completions alternate between two barriers by tile parity.
 //              Keys past the sequence are masked; rows past it are not stored.
 // Every wait is bounded (ptx.cuh); on a timeout the kernel records a status and exits.
+#include <algorithm>
 #include <atomic>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -44,8 +45,25 @@ constexpr int kPBytes = 128 * kKT * 2;   // P tile [128][64 keys] (double buffer
 constexpr int kSmem = 1024 + kQBytes + kStagesKV * (kKBytes + kVBytes) + 2 * kPBytes + 256;
 constexpr uint32_t kTmemCols = 256;      // S[0..1]: cols [0,128), O (80 cols): [128,208)
 constexpr float kRescaleLog2 = 8.0f;     // rescale O only when the row max grows by > 2^8
+constexpr int kShareBytes = 128 * 64 * 4 + 128 * 8;  // a split share: O [16][128] float4, (max, sum) [128]
+static_assert(kShareBytes <= kStagesKV * (kKBytes + kVBytes), "a split share fits the K / V ring");
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// loads from another CTA's shared memory (a shared::cluster address, mapa_shared)
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t caddr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(caddr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ float2 ld_dsmem_f2(uint32_t caddr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(caddr) : "memory");
+  return v;
+}
 
 // max(a, b, c) in one instruction (sm_100 three-input max.f32)
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -78,7 +96,7 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
 __global__ void __launch_bounds__(192, 2)
     k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
               const __grid_constant__ CUtensorMap tmV, int seqlen, int H, int D, __half* __restrict__ out, float sl2,
-              int q8, int* status) {
+              int q8, int nsplit, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
@@ -95,10 +113,15 @@ __global__ void __launch_bounds__(192, 2)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, h = blockIdx.y, sq = blockIdx.z;
+  const int split = static_cast<int>(blockIdx.x) % nsplit, qt = static_cast<int>(blockIdx.x) / nsplit;
+  const int h = blockIdx.y, sq = blockIdx.z;
   const int q0 = qt * 128;
   const int row_base = sq * seqlen;               // first token row of this sequence
-  const int nkt = (seqlen + kKT - 1) / kKT;
+  // this CTA's key tiles [kt0, kt0 + nkt): all of them, or its share when the (query
+  // tile, head) is split over a cluster of nsplit CTAs (nsplit <= key tiles)
+  const int nkt_all = (seqlen + kKT - 1) / kKT;
+  const int kt0 = split * nkt_all / nsplit;
+  const int nkt = (split + 1) * nkt_all / nsplit - kt0;
 
   // rows 64..79 of every V^T stage: a row of ones (its product with P is the row sum
   // of P) and zeros; the TMA only ever writes rows 0..63. Swizzling permutes 16-byte
@@ -131,6 +154,50 @@ __global__ void __launch_bounds__(192, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tO = tmem + 128;
+  float o[64];                           // softmax warps: this thread's output row,
+  float lsum = 0.f, mrow = 0.f;          // its row sum and the max its exponentials used,
+  bool have = false;                     // once the last P V product has landed
+  const int r = (warp & 3) * 32 + lane;  // query row within the tile == TMEM lane
+  // O / l as f16 into out (rows past the sequence are not stored); with q8 the Q8_0
+  // round trip per 32-dim block (ggml quantize_row_q8_0_ref semantics). Warp-collective:
+  // the warp's 32 rows go out through shared memory (the Q tile, idle once the last
+  // product landed; 4 KB a warp, 16-byte chunks XOR-swizzled by row), four whole
+  // 128-byte rows per store instruction instead of 32 pieces of 16 bytes.
+  auto store_row = [&](float l) {
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) o[i] *= inv;
+    if (q8) {
+#pragma unroll
+      for (int bb = 0; bb < 2; ++bb) {
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[32 * bb + i]));
+        const float d = amax / 127.0f;
+        const float id = d != 0.f ? 1.0f / d : 0.0f;
+        const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[32 * bb + i] = dh * roundf(o[32 * bb + i] * id);
+      }
+    }
+    uint8_t* stg = sQ + (warp & 3) * 4096;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint4 u;
+      __half2* hh = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) hh[k] = __floats2half2_rn(o[8 * c + 2 * k], o[8 * c + 2 * k + 1]);
+      *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) = u;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int row = 4 * k + (lane >> 3), c = lane & 7;
+      const uint4 u = *reinterpret_cast<const uint4*>(stg + row * 128 + ((c ^ (row & 7)) << 4));
+      const int qrow = q0 + (warp & 3) * 32 + row;
+      if (qrow < seqlen) *reinterpret_cast<uint4*>(out + static_cast<size_t>(row_base + qrow) * D + h * 64 + c * 8) = u;
+    }
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -143,8 +210,8 @@ __global__ void __launch_bounds__(192, 2)
       for (int j = 0; j < nkt; ++j) {
         if (!mbar_wait(&kv_empty[stage], phase ^ 1u, status, kStatusTimeoutEmpty)) break;
         mbar_arrive_expect_tx(&kv_full[stage], kKBytes + 64 * kKT * 2);
-        tma_load_2d(sK + stage * kKBytes, &tmK, &kv_full[stage], D + h * 64, row_base + j * kKT);
-        tma_load_2d(sV + stage * kVBytes, &tmV, &kv_full[stage], j * kKT, vrow);
+        tma_load_2d(sK + stage * kKBytes, &tmK, &kv_full[stage], D + h * 64, row_base + (kt0 + j) * kKT);
+        tma_load_2d(sV + stage * kVBytes, &tmV, &kv_full[stage], (kt0 + j) * kKT, vrow);
         if (++stage == kStagesKV) { stage = 0; phase ^= 1u; }
       }
     }
@@ -189,9 +256,7 @@ __global__ void __launch_bounds__(192, 2)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax
-    const int qq = warp & 3;
-    const int r = qq * 32 + lane;                    // query row within the tile == TMEM lane
-    const uint32_t lane_off = static_cast<uint32_t>(qq * 32) << 16;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     float m = -INFINITY;                             // max used for the exponentials so far
     bool ok = true;
     for (int j = 0; j < nkt; ++j) {
@@ -211,7 +276,7 @@ __global__ void __launch_bounds__(192, 2)
           sv[32 + i] = __uint_as_float(rb[i]);
         }
       }
-      const int kvalid = seqlen - j * kKT;  // keys of this tile inside the sequence (>= 1)
+      const int kvalid = seqlen - (kt0 + j) * kKT;  // keys of this tile inside the sequence (>= 1)
       if (kvalid < kKT) {
 #pragma unroll
         for (int i = 0; i < kKT; ++i)
@@ -297,45 +362,81 @@ __global__ void __launch_bounds__(192, 2)
     if (ok) ok = mbar_wait_warp(&o_full[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1, status, kStatusTimeoutAccum);
     if (ok) {
       tc_fence_after();
-      float o[64];
       uint32_t ra[32], rb[32], rc;
       tmem_ld32(tO + lane_off, ra);
       tmem_ld32(tO + lane_off + 32, rb);
       tmem_ld1(tO + lane_off + 64, rc);
       tmem_wait_ld();
-      const float l = __uint_as_float(rc);
-      const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        o[i] = __uint_as_float(ra[i]) * inv;
-        o[32 + i] = __uint_as_float(rb[i]) * inv;
+        o[i] = __uint_as_float(ra[i]);
+        o[32 + i] = __uint_as_float(rb[i]);
       }
-      if (q0 + r < seqlen) {
-        if (q8) {
-          // Q8_0 round trip per 32-dim block (ggml quantize_row_q8_0_ref semantics)
-#pragma unroll
-          for (int bb = 0; bb < 2; ++bb) {
-            float amax = 0.f;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[32 * bb + i]));
-            const float d = amax / 127.0f;
-            const float id = d != 0.f ? 1.0f / d : 0.0f;
-            const float dh = __half2float(__float2half_rn(d));
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[32 * bb + i] = dh * roundf(o[32 * bb + i] * id);
-          }
-        }
-        __half* dst = out + static_cast<size_t>(row_base + q0 + r) * D + h * 64;
-#pragma unroll
-        for (int i = 0; i < 64; i += 8) {
-          uint4 u;
-          __half2* hh = reinterpret_cast<__half2*>(&u);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) hh[k] = __floats2half2_rn(o[i + 2 * k], o[i + 2 * k + 1]);
-          *reinterpret_cast<uint4*>(dst + i) = u;
-        }
-      }
+      lsum = __uint_as_float(rc);
+      mrow = m;
+      have = true;
     }
+    if (nsplit == 1) {
+      if (have) store_row(lsum);
+    } else if (split != 0) {
+      // this CTA's share: unnormalised O, its max and row sum, into its own (now idle)
+      // K / V ring for the cluster's first CTA to read, column-chunk-major (float4 chunk
+      // i of row r at [i][r], then (max, sum) pairs at [r]) so that each remote load of
+      // a warp reads 512 contiguous bytes
+      float4* dst = reinterpret_cast<float4*>(sK);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) dst[i * 128 + r] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+      reinterpret_cast<float2*>(dst + 16 * 128)[r] = make_float2(mrow, lsum);
+    }
+  }
+  if (nsplit > 1) {
+    // The cluster's first CTA merges the shares in rank order (so the result does not
+    // depend on which CTA finished first): with M the largest share max,
+    //   O = sum_s 2^((m_s - M) c) O_s / sum_s 2^((m_s - M) c) l_s.
+    cluster_sync();  // every share is in its CTA's shared memory
+    if (warp >= 2 && split == 0 && have) {
+      const uint32_t share = smem_u32(sK);
+      float pm[3], pl[3];
+      float mx = mrow;
+      float2 ml[3];
+#pragma unroll
+      for (int sp = 1; sp < 4; ++sp)
+        if (sp < nsplit) ml[sp - 1] = ld_dsmem_f2(mapa_shared(share + 16 * 128 * 16 + r * 8, static_cast<uint32_t>(sp)));
+#pragma unroll
+      for (int sp = 1; sp < 4; ++sp) {
+        if (sp >= nsplit) break;
+        pm[sp - 1] = ml[sp - 1].x;
+        pl[sp - 1] = ml[sp - 1].y;
+        mx = fmaxf(mx, ml[sp - 1].x);
+      }
+      const float w0 = ex2_approx((mrow - mx) * sl2);
+      float l = w0 * lsum;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) o[i] *= w0;
+#pragma unroll
+      for (int sp = 1; sp < 4; ++sp) {
+        if (sp >= nsplit) break;
+        const float w = ex2_approx((pm[sp - 1] - mx) * sl2);
+        l += w * pl[sp - 1];
+        // all 16 loads of the share in flight before the first use: a remote load takes
+        // a few hundred cycles, and the warp would wait out each one in turn
+        const uint32_t peer = mapa_shared(share + r * 16, static_cast<uint32_t>(sp));
+        float4 v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = ld_dsmem_f4(peer + static_cast<uint32_t>(i * 128 * 16));
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          o[4 * i] += w * v[i].x;
+          o[4 * i + 1] += w * v[i].y;
+          o[4 * i + 2] += w * v[i].z;
+          o[4 * i + 3] += w * v[i].w;
+        }
+      }
+      store_row(l);
+    }
+    // no CTA leaves while the first one may still read its share; relaxed, so the
+    // first CTA's output stores need not complete before the others may go
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
@@ -733,6 +834,18 @@ __global__ void __launch_bounds__(kWThreads, 1)
 // attention_tc runs the 128-query kernel (2 CTAs per SM, P in shared memory);
 // $DA3B_ATTN_PP=1 (read once per process) selects the warp-specialised kernel, which is
 // correct but measured slower at the C3 shape (0.92 against 0.82 ms).
+// Key-range split of the 128-query kernel: -1 = automatic; 1 = never; 2-4 = that many
+// shares wherever the sequence has that many key tiles (tests). Initial value from
+// $DA3B_ATTN_SPLIT (0 = never), read once per process.
+static std::atomic<int> g_attn_split{[] {
+  const char* e = getenv("DA3B_ATTN_SPLIT");
+  if (!e || !e[0]) return -1;
+  const int v = atoi(e);
+  return v <= 1 ? 1 : (v > 4 ? 4 : v);
+}()};
+
+void set_attention_split(int n) { g_attn_split.store(n < 0 ? -1 : (n <= 1 ? 1 : (n > 4 ? 4 : n))); }
+
 static bool attn_pp() {
   static const bool pp = [] {
     const char* e = getenv("DA3B_ATTN_PP");
@@ -802,9 +915,41 @@ int attention_tc(const __half* qkv, const __half* vt, int ld_vt, int nseq, int s
     if (cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess) return -3;
     attr_set.fetch_or(bit, std::memory_order_acq_rel);
   }
-  dim3 grid((seqlen + 127) / 128, H, nseq);
+  const int ntq = (seqlen + 127) / 128, nkt = (seqlen + kKT - 1) / kKT;
   const float sl2 = 0.125f * 1.4426950408889634f;
-  k_attn_tc<<<grid, 192, kSmem, s>>>(tq, tk, tv, seqlen, H, D, out, sl2, q8, status);
+  // When the (query tile, head, sequence) CTAs fill fewer than the SMs' two slots each
+  // (one image: 11 x 12 heads on 148 SMs), each one's key tiles are split over a
+  // cluster of up to four CTAs, which merge their shares through distributed shared
+  // memory: at batch 1 the softmax of one CTA per SM runs with one warp per SM
+  // sub-partition and nothing to hide its latencies behind. A share keeps at least six
+  // key tiles; below that the merge (about 2 us) costs more than the split saves.
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long ctas = static_cast<long long>(ntq) * H * nseq;
+  const int mode = g_attn_split.load(std::memory_order_relaxed);
+  int nsplit = 1;
+  if (mode < 0) nsplit = static_cast<int>(std::min<long long>({4LL, (2LL * sms) / ctas, nkt / 6}));
+  else if (mode > 1) nsplit = mode;
+  nsplit = std::max(1, std::min(nsplit, nkt));
+  if (nsplit == 1) {
+    k_attn_tc<<<dim3(ntq, H, nseq), 192, kSmem, s>>>(tq, tk, tv, seqlen, H, D, out, sl2, q8, 1, status);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+  }
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(ntq * nsplit, H, nseq);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(nsplit);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, k_attn_tc, tq, tk, tv, seqlen, H, D, out, sl2, q8, nsplit, status) != cudaSuccess)
+    return -4;
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 

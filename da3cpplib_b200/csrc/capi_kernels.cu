@@ -243,6 +243,11 @@ DA3B_API int da3b_debug_mma_cycles(int n, int a_tmem, int iters, int ctas, unsig
   return -100;
 }
 
+DA3B_API int da3b_set_attention_split(int n) {
+  set_attention_split(n);
+  return 0;
+}
+
 DA3B_API int da3b_transpose_v(const void* qkv, int nseq, int seqlen, int heads, void* vt, int ld_vt, void* stream) {
   if (!qkv || !vt || heads <= 0 || nseq < 0 || seqlen < 0 || ld_vt < seqlen || ld_vt % 8) return -100;
   if (nseq == 0 || seqlen == 0) return 0;

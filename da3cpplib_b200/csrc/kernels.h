@@ -42,6 +42,8 @@ int transpose_v(const __half* qkv, int nseq, int seqlen, int H, int D, __half* v
 // tcgen05 flash attention: q, k from qkv, v from vt (attention_tc.cu).
 int attention_tc(const __half* qkv, const __half* vt, int ld_vt, int nseq, int seqlen, int H, int D, __half* out,
                  int q8, int* status, cudaStream_t s);
+// Key-range split of attention_tc: -1 automatic (default), 1 never, 2-4 forced shares.
+void set_attention_split(int n);
 
 
 

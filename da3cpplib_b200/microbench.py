@@ -92,6 +92,7 @@ def main(argv=None):
     ap.add_argument("--batch", type=int, default=8, help="Part B / up: images")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--attn-nseq", type=int, default=0, help="attn: only the C3 shape with this many sequences")
+    ap.add_argument("--attn-heads", type=int, default=16, help="attn with --attn-nseq: heads (12: the C2 shape)")
     args = ap.parse_args(argv)
 
     L = _lib.load()
@@ -247,7 +248,7 @@ def main(argv=None):
     if args.part in ("attn", "all"):
         cases = ((64, 1370, 16, "C3 per-image"), (2, 8 * 1297, 16, "C4 global, 2 scenes"))
         if args.attn_nseq:
-            cases = ((args.attn_nseq, 1370, 16, "C3 shape, fewer images"),)
+            cases = ((args.attn_nseq, 1370, args.attn_heads, "1370 tokens"),)
         for nseq, seqlen, heads, tag in cases:
             D = heads * 64
             qkv = torch.randn((nseq * seqlen, 3 * D), generator=gen, device="cuda").half()

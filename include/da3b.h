@@ -102,6 +102,13 @@ DA3B_API int da3b_debug_wait_timeout(unsigned long long limit_ns, int use_tmem, 
 DA3B_API int da3b_debug_mma_cycles(int n, int a_tmem, int iters, int ctas, unsigned long long* cycles_dev,
                                    void* stream);
 
+/* Key-range split of the flash attention (process-wide): n < 0 automatic (default: when
+ * the (query tile, head, sequence) grid would leave SMs idle, each query tile's keys are
+ * shared out over a cluster of up to 4 CTAs, at least 6 key tiles each, which merge their
+ * partial softmax sums); n = 0 or 1 never; n = 2..4 that many shares wherever the
+ * sequence has that many 64-key tiles. For tests and measurement; returns 0. */
+DA3B_API int da3b_set_attention_split(int n);
+
 /* The two halves of da3b_attention, for callers that keep V transposed (the engine's
  * QKV GEMM epilogue writes it that way): da3b_transpose_v writes V^T f16
  * [nseq][heads][64][ld_vt] (ld_vt >= seqlen, a multiple of 8; columns beyond seqlen are

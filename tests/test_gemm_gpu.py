@@ -176,11 +176,13 @@ def test_conv3_halo(lib, B, H, W, IC, OC, pair, monkeypatch):
 
 @pytest.mark.parametrize("nseq,seqlen,heads", [(1, 1, 1), (2, 37, 2), (3, 1370, 6), (1, 1297 * 3, 4), (2, 200, 16),
                                                (2, 128, 2), (1, 129, 3), (3, 255, 1), (1, 256, 2), (2, 257, 2),
-                                               (1, 1297 * 8, 2)])
+                                               (1, 1297 * 8, 2), (1, 1370, 12), (1, 1370, 6)])
 def test_attention(lib, nseq, seqlen, heads):
     """da3b_attention against torch fp32 softmax attention: sequence lengths on both sides
     of the 128-query and 128-key tile edges (one or two query tiles per CTA, ragged last
-    key tile), several sequences and heads, and an 8-view global sequence."""
+    key tile), several sequences and heads, and an 8-view global sequence, with the
+    automatic key-range split: (1, 1370, 12) (one ViT-B image) runs 2 shares a query
+    tile, (1, 1370, 6) 3, (1, 1297 * 3, 4) 4, the others one."""
     g = torch.Generator(device="cuda").manual_seed(seqlen + heads)
     D = heads * 64
     qkv = (torch.randn(nseq * seqlen, 3 * D, device="cuda", generator=g) * 1.5).half()
@@ -192,6 +194,36 @@ def test_attention(lib, nseq, seqlen, heads):
     ref = torch.softmax(q @ k.transpose(-1, -2) / 8.0, dim=-1) @ v          # [nseq, heads, seqlen, 64]
     ref = ref.permute(0, 2, 1, 3).reshape(nseq * seqlen, D)
     close(out, ref, rel=5e-3, abs_=5e-3)
+
+
+@pytest.mark.parametrize("shares", [2, 3, 4])
+@pytest.mark.parametrize("nseq,seqlen,heads", [(1, 1370, 12), (2, 257, 2), (1, 129, 3), (3, 300, 1)])
+def test_attention_split_shares(lib, nseq, seqlen, heads, shares):
+    """Each query tile's keys shared out over a cluster of 2-4 CTAs (forced with
+    da3b_set_attention_split; by default only when the grid leaves SMs idle and every
+    share keeps 6 key tiles), merged through distributed shared memory in rank order:
+    against torch fp32 attention, ragged last key tiles and uneven shares included, and
+    against the unsplit kernel; two runs are bit-identical."""
+    g = torch.Generator(device="cuda").manual_seed(seqlen * 3 + heads + shares)
+    D = heads * 64
+    qkv = (torch.randn(nseq * seqlen, 3 * D, device="cuda", generator=g) * 1.5).half()
+    outs = []
+    try:
+        for n in (shares, shares, 1):
+            assert lib.da3b_set_attention_split(n) == 0
+            out = torch.empty(nseq * seqlen, D, dtype=torch.float16, device="cuda")
+            assert lib.da3b_attention(ptr(qkv), nseq, seqlen, heads, ptr(out), stream()) == 0
+            torch.cuda.synchronize()
+            assert lib.da3b_device_status() == 0
+            outs.append(out)
+    finally:
+        lib.da3b_set_attention_split(-1)
+    q, k, v = qkv.float().view(nseq, seqlen, 3, heads, 64).permute(2, 0, 3, 1, 4)
+    ref = torch.softmax(q @ k.transpose(-1, -2) / 8.0, dim=-1) @ v
+    ref = ref.permute(0, 2, 1, 3).reshape(nseq * seqlen, D)
+    close(outs[0], ref, rel=5e-3, abs_=5e-3)
+    assert torch.equal(outs[0], outs[1])
+    close(outs[0], outs[2].float(), rel=5e-3, abs_=5e-3)
 
 
 @pytest.mark.parametrize("B,hs,ws,C,H,W", [(2, 296, 296, 128, 518, 518), (1, 37, 37, 256, 74, 74), (3, 19, 19, 64, 37, 37),
