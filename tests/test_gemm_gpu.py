@@ -136,17 +136,22 @@ def _conv3(lib, x, wp, OC, b, r1, r2, out, outr, act=0):
 @pytest.mark.parametrize("B,H,W,IC,OC", [(2, 37, 37, 256, 128), (1, 5, 9, 64, 128), (3, 17, 33, 128, 128),
                                          (1, 16, 16, 64, 128), (2, 74, 74, 256, 128), (1, 37, 37, 256, 256),
                                          (2, 19, 21, 512, 256)])
-@pytest.mark.parametrize("pair", ["1", "0"], ids=["cta_pair", "one_cta"])
+@pytest.mark.parametrize("pair", ["1", "0", ""], ids=["cta_pair", "one_cta", "auto"])
 def test_conv3_halo(lib, B, H, W, IC, OC, pair, monkeypatch):
     """3x3 convs through the halo-box kernel ($DA3B_CONV_HALO=1; by default it serves 128
     output channels): one input box per 64-channel chunk, the nine taps as shifted
     no-swizzle descriptors, output channels in groups of 128. Checked against the
     torch fp32 reference and the implicit-GEMM path ($DA3B_CONV_HALO=0) on the same
     inputs, with bias, both residual addends, the relu copy, ragged tile edges, 1-8
-    chunks and one or two output groups; in the CTA-pair form (default, an odd number
-    of pixel tiles leaves the last pair's second tile empty) and the one-CTA form
-    ($DA3B_CONV_HALO_PAIR=0)."""
-    monkeypatch.setenv("DA3B_CONV_HALO_PAIR", pair)
+    chunks and one or two output groups; in the CTA-pair form with two 8-wide halves
+    per CTA for 128 outputs, one for 256 ($DA3B_CONV_HALO_PAIR=1; an odd number of pixel
+    tiles leaves the last pair's second tile empty), the one-CTA form (=0), and the
+    automatic choice, which runs 128-output maps of at most one 16 x 16 tile per SM
+    as CTA pairs of one half each."""
+    if pair:
+        monkeypatch.setenv("DA3B_CONV_HALO_PAIR", pair)
+    else:
+        monkeypatch.delenv("DA3B_CONV_HALO_PAIR", raising=False)
     g = torch.Generator(device="cuda").manual_seed(B * 7 + H + W + IC)
     x = torch.randn(B, H, W, IC, device="cuda", generator=g).half()
     w = torch.randn(OC, IC, 3, 3, device="cuda", generator=g).float() * 0.05
