@@ -36,6 +36,12 @@ SIGNATURES = {
     "da3b_debug_wait_timeout": (c_int, [ctypes.c_ulonglong, c_int, c_void_p, c_void_p, c_void_p]),
     "da3b_debug_mma_cycles": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "da3b_set_attention_split": (c_int, [c_int]),
+    "da3b_repack_q8_0_planar": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "da3b_dequant_q8p": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "da3b_linear_q8p_f16": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int,
+                                    c_void_p]),
+    "da3b_linear_q8p_resid_f32": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                          c_void_p, c_int, c_void_p]),
     "da3b_transpose_v": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p]),
     "da3b_attention_vt": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "da3b_attention_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),

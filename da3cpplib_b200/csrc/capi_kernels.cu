@@ -4,6 +4,7 @@
 #include <stdint.h>
 
 #include <mutex>
+#include <string.h>
 
 #include "da3b.h"
 #include "kernels.h"
@@ -179,6 +180,51 @@ DA3B_API int da3b_linear_resid_f32(const void* x, int M, int K, int lda, const v
   e.ld_resid = ldr;
   return gemm_linear(static_cast<const __half*>(x), M, K, lda, static_cast<const __half*>(w), N, ldw, 0, e, st,
                      static_cast<cudaStream_t>(stream));
+}
+
+DA3B_API int da3b_repack_q8_0_planar(const void* q8, int N, int K, void* planar, void* stream) {
+  if (!q8 || !planar) return -100;
+  return repack_q8_0_planar(q8, N, K, planar, static_cast<cudaStream_t>(stream));
+}
+
+DA3B_API int da3b_dequant_q8p(const void* planar, int N, int K, void* w_f16, void* stream) {
+  if (!planar || !w_f16 || N <= 0 || K <= 0 || K % 32) return -100;
+  Q8Segs g;
+  memset(&g, 0, sizeof(g));
+  g.s[0] = Q8Seg{static_cast<const uint8_t*>(planar), static_cast<__half*>(w_f16), N, K / 32, 0};
+  g.n = 1;
+  g.total = static_cast<long>(N) * (K / 32);
+  return dequant_q8p_segs(g, static_cast<cudaStream_t>(stream));
+}
+
+DA3B_API int da3b_linear_q8p_f16(const void* x, int M, int K, int lda, const void* planar, int N, const float* bias,
+                                 int act, void* out, int ldo, void* stream) {
+  if (!x || !planar || !out || act < 0 || act > 3) return -100;
+  int* st = device_status_word();
+  if (!st) return -101;
+  EpiArgs e = epi_default();
+  e.kind = kEpiF16;
+  e.act = act;
+  e.bias = bias;
+  e.out = static_cast<__half*>(out);
+  e.ld_out = ldo;
+  return gemm_linear_q8p(static_cast<const __half*>(x), M, K, lda, static_cast<const uint8_t*>(planar), N, e, st,
+                         static_cast<cudaStream_t>(stream));
+}
+
+DA3B_API int da3b_linear_q8p_resid_f32(const void* x, int M, int K, int lda, const void* planar, int N,
+                                       const float* bias, const float* scale, float* resid, int ldr, void* stream) {
+  if (!x || !planar || !resid) return -100;
+  int* st = device_status_word();
+  if (!st) return -101;
+  EpiArgs e = epi_default();
+  e.kind = kEpiResid;
+  e.bias = bias;
+  e.scale = scale;
+  e.resid = resid;
+  e.ld_resid = ldr;
+  return gemm_linear_q8p(static_cast<const __half*>(x), M, K, lda, static_cast<const uint8_t*>(planar), N, e, st,
+                         static_cast<cudaStream_t>(stream));
 }
 
 // Scratch for the transposed V of da3b_attention: one grow-only buffer per device,

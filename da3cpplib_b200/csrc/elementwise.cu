@@ -1,11 +1,14 @@
-// Memory-bound helper kernels: Q8_0 weight repack, casts, and the per-device status word.
+// Memory-bound helper kernels: Q8_0 weight repacks and dequantisation, casts, and the
+// per-device status word.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "ops.h"
+#include "q8planar.cuh"
 
 namespace da3b {
 
@@ -44,57 +47,69 @@ int dequant_q8_0(const void* q8, int rows, int K, __half* out, int ldo, cudaStre
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
-// One launch dequantising up to four Q8_0 matrices (a ViT block's linears) into dense
-// f16 [rows][K], f16(d * q) like k_dequant_q8_0. A warp takes 32 consecutive blocks
-// of one matrix: their 1088 source bytes come in as 16-byte coalesced loads into shared
-// memory, then each lane converts one block and writes its 64 output bytes (the warp's
-// stores are one contiguous 2 KB run). A matrix's last partial chunk reads per lane.
-__device__ __forceinline__ void dequant_block32(const uint8_t* blk, __half* out) {
-  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(blk[0] | (blk[1] << 8))));
-  uint4 packed[4];
-  __half2* h = reinterpret_cast<__half2*>(packed);
+// GGUF Q8_0 rows -> planar Q8_0 (q8planar.cuh), one thread per (row, block). Load time.
+__global__ void k_repack_q8_0_planar(const uint8_t* __restrict__ raw, int N, int K, uint8_t* __restrict__ planar) {
+  const int nb = K / 32;
+  const long blocks = static_cast<long>(N) * nb;
+  __half* dplane = reinterpret_cast<__half*>(planar + static_cast<size_t>(N) * K);
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < blocks;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int n = static_cast<int>(i / nb), b = static_cast<int>(i % nb);
+    const uint16_t* blk = reinterpret_cast<const uint16_t*>(raw + static_cast<size_t>(i) * 34);  // 2-byte aligned
+    dplane[static_cast<size_t>(b) * N + n] = __ushort_as_half(blk[0]);
+    uint32_t w[8];
 #pragma unroll
-  for (int i = 0; i < 16; ++i)
-    h[i] = __floats2half2_rn(d * static_cast<float>(static_cast<int8_t>(blk[2 + 2 * i])),
-                             d * static_cast<float>(static_cast<int8_t>(blk[3 + 2 * i])));
-  uint4* o4 = reinterpret_cast<uint4*>(out);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) o4[i] = packed[i];
+    for (int k = 0; k < 8; ++k) w[k] = static_cast<uint32_t>(blk[1 + 2 * k]) | (static_cast<uint32_t>(blk[2 + 2 * k]) << 16);
+    uint4* dst = reinterpret_cast<uint4*>(planar + static_cast<size_t>(n) * K + b * 32);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
 }
 
-__global__ void __launch_bounds__(256) k_dequant_q8_0_segs(Q8Segs g) {
-  __shared__ __align__(16) uint8_t stage[8][1088];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long gw = static_cast<long>(blockIdx.x) * 8 + warp, nw = static_cast<long>(gridDim.x) * 8;
+int repack_q8_0_planar(const void* raw, int N, int K, void* planar, cudaStream_t s) {
+  if (N <= 0 || K <= 0 || K % 32 || (reinterpret_cast<uintptr_t>(raw) & 1) || (reinterpret_cast<uintptr_t>(planar) & 15))
+    return -1;
+  const long n = static_cast<long>(N) * (K / 32);
+  long blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  k_repack_q8_0_planar<<<static_cast<unsigned>(blocks), 256, 0, s>>>(static_cast<const uint8_t*>(raw), N, K,
+                                                                      static_cast<uint8_t*>(planar));
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+// One launch dequantising up to four planar Q8_0 matrices (a ViT block's linears) into
+// dense f16 [rows][K]: a thread takes 16 consecutive weights of a row (one 16-byte load
+// of the q plane, its block's scale, two 16-byte stores), consecutive threads
+// consecutive pieces, so every load and store of a warp is one contiguous run.
+__global__ void __launch_bounds__(256) k_dequant_q8p_segs(Q8Segs g) {
+  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
   for (int k = 0; k < g.n; ++k) {
     const Q8Seg& sg = g.s[k];
-    const long nblk = static_cast<long>(sg.rows) * sg.nblk;
-    const long nch = (nblk + 31) / 32;
-    for (long c = gw; c < nch; c += nw) {
-      const long b0 = c * 32;
-      const uint8_t* src = sg.q8 + static_cast<size_t>(b0) * 34;
-      if (b0 + 32 <= nblk) {
-        const uint4* s4 = reinterpret_cast<const uint4*>(src);
-        uint4* d4 = reinterpret_cast<uint4*>(stage[warp]);
-        for (int i = lane; i < 68; i += 32) d4[i] = s4[i];
-        __syncwarp();
-        dequant_block32(stage[warp] + lane * 34, sg.out + static_cast<size_t>(b0 + lane) * 32);
-        __syncwarp();  // the stage is reused by this warp's next chunk
-      } else if (b0 + lane < nblk) {
-        dequant_block32(src + lane * 34, sg.out + static_cast<size_t>(b0 + lane) * 32);
-      }
+    const int K = sg.nblk * 32, per_row = K / 16;
+    const long units = static_cast<long>(sg.rows) * per_row;
+    const __half* dplane = reinterpret_cast<const __half*>(sg.q8 + static_cast<size_t>(sg.rows) * K);
+    for (long u = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; u < units; u += stride) {
+      const int n = static_cast<int>(u / per_row), j = static_cast<int>(u % per_row);
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(sg.q8 + static_cast<size_t>(n) * K + 16 * j));
+      const __half d = dplane[static_cast<size_t>(j >> 1) * sg.rows + n];
+      const __half2 d2 = __halves2half2(d, d);
+      uint4* dst = reinterpret_cast<uint4*>(sg.out + static_cast<size_t>(n) * K + 16 * j);
+      dst[0] = q8x8_to_f16x8(make_uint2(q.x, q.y), d2);
+      dst[1] = q8x8_to_f16x8(make_uint2(q.z, q.w), d2);
     }
   }
 }
 
-int dequant_q8_0_segs(const Q8Segs& g, cudaStream_t s) {
+int dequant_q8p_segs(const Q8Segs& g, cudaStream_t s) {
   if (g.n <= 0 || g.n > 4 || g.total <= 0) return -1;
-  for (int k = 0; k < g.n; ++k)
+  long units = 0;
+  for (int k = 0; k < g.n; ++k) {
     if (reinterpret_cast<uintptr_t>(g.s[k].q8) & 15 || reinterpret_cast<uintptr_t>(g.s[k].out) & 15) return -2;
-  const long chunks = (g.total + 31) / 32;
-  long blocks = (chunks + 7) / 8;
+    units = std::max(units, static_cast<long>(g.s[k].rows) * g.s[k].nblk * 2);
+  }
+  long blocks = (units + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
-  k_dequant_q8_0_segs<<<static_cast<unsigned>(blocks), 256, 0, s>>>(g);
+  k_dequant_q8p_segs<<<static_cast<unsigned>(blocks), 256, 0, s>>>(g);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

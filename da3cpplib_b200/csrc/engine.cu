@@ -13,6 +13,7 @@
 #include "engine.h"
 
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -133,6 +134,7 @@ std::unique_ptr<Engine> Engine::create(const std::string& path, int device, std:
     return nullptr;
   }
   if (const char* g = getenv("DA3B_GRAPH")) e->use_graph_ = strcmp(g, "0") != 0;
+  if (const char* q = getenv("DA3B_Q8_TILES")) e->q8_tiles_ = q[0] == '1';
   return e;
 }
 
@@ -510,10 +512,20 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
 
   for (int i = 0; i < c.depth; ++i) {
     const Block& b = m.blk[i];
-    // this block's linears: the resident f16 planes, or its Q8_0 bytes dequantised into
-    // the staging buffer (in stream order after the previous block's last GEMM)
+    // this block's linears: the resident f16 planes; or, resident as planar Q8_0,
+    // dequantised into the staging buffer (in stream order after the previous block's
+    // last GEMM) for the f16 GEMMs (default), or ($DA3B_Q8_TILES=1, few rows: every
+    // linear on one-CTA tiles) read by GEMMs that dequantise their weight tiles in
+    // shared memory. The two give the same bits; the staging route is the faster at
+    // one image (ViT-B: QKV 12.6 + 2.2 us against 18.1 us, fc1 14.6 + 2.7 against 20.3).
     const __half *w_qkv = b.qkv.w, *w_proj = b.proj.w, *w_fc1 = b.fc1.w, *w_fc2 = b.fc2.w;
-    if (m.q8_resident) {
+    const bool q8_tiles = m.q8_resident && q8_tiles_ && gemm_q8p_bn(M, b.qkv.N) && gemm_q8p_bn(M, b.proj.N) &&
+                          gemm_q8p_bn(M, b.fc1.N) && gemm_q8p_bn(M, b.fc2.N);
+    auto linear = [&](const __half* A, int lda, const Lin& L, const __half* w_f16, const EpiArgs& e) -> int {
+      if (q8_tiles) return gemm_linear_q8p(A, M, L.K, lda, L.q8, L.N, e, status_, s);
+      return gemm_linear(A, M, L.K, lda, w_f16, L.N, L.ldw, 0, e, status_, s);
+    };
+    if (m.q8_resident && !q8_tiles) {
       Q8Segs g;
       const Lin* L4[4] = {&b.qkv, &b.proj, &b.fc1, &b.fc2};
       const __half** ptrs[4] = {&w_qkv, &w_proj, &w_fc1, &w_fc2};
@@ -527,7 +539,7 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
       }
       g.n = 4;
       g.total = first;
-      CK(dequant_q8_0_segs(g, s));
+      CK(dequant_q8p_segs(g, s));
     }
     if (select && i == c.alt_start - 1) {
       // reference-view selection on the views' token 0 after blocks [0, alt_start-1)
@@ -552,7 +564,7 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
       e.vt_seqlen = seqlen;
       e.vt_ld = ld_vt;
       e.vt_d = D;
-      CK(gemm_linear(p.xn, M, D, D, w_qkv, b.qkv.N, b.qkv.ldw, 0, e, status_, s));
+      CK(linear(p.xn, D, b.qkv, w_qkv, e));
     }
     if (b.qng || use_rope) {
       const float* cs = use_rope ? (global ? p.rn_cos : p.rl_cos) : nullptr;
@@ -567,14 +579,14 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
       e.ld_resid = D;
       e.bias = b.proj.b;
       e.scale = b.ls1;
-      CK(gemm_linear(p.attn, M, D, D, w_proj, D, b.proj.ldw, 0, e, status_, s));
+      CK(linear(p.attn, D, b.proj, w_proj, e));
     }
     // ---- MLP half
     CK(layernorm_f32(p.x, D, M, D, b.n2g, b.n2b, c.ln_eps, p.xn, D, 0, 0, 0, 0, s, q8));
     {
       EpiArgs e = epi_f16(p.hid, b.fc1.N, b.fc1.b, kActGelu);
       e.q8 = q8;
-      CK(gemm_linear(p.xn, M, D, D, w_fc1, b.fc1.N, b.fc1.ldw, 0, e, status_, s));
+      CK(linear(p.xn, D, b.fc1, w_fc1, e));
     }
     {
       EpiArgs e = epi_default();
@@ -583,7 +595,7 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
       e.ld_resid = D;
       e.bias = b.fc2.b;
       e.scale = b.ls2;
-      CK(gemm_linear(p.hid, M, b.fc2.K, b.fc2.K, w_fc2, D, b.fc2.ldw, 0, e, status_, s));
+      CK(linear(p.hid, b.fc2.K, b.fc2, w_fc2, e));
     }
     if (p.resid_cap &&
         cudaMemcpyAsync(p.resid_cap + static_cast<size_t>(i) * M * D, p.x, static_cast<size_t>(M) * D * sizeof(float),

@@ -113,6 +113,10 @@ class Engine {
   int device_ = 0;
   int* status_ = nullptr;
   bool use_graph_ = true;
+  // $DA3B_Q8_TILES=1 at creation: resident Q8_0 block linears whose GEMMs all run on
+  // one-CTA tiles are read by GEMMs that dequantise their weight tiles in shared memory
+  // instead of through the f16 staging buffer (same bits; measured slower at batch 1)
+  bool q8_tiles_ = false;
   bool raw_logits_ = false;
   bool act_quant_ = false;
   bool capture_resid_ = false;

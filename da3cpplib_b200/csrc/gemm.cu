@@ -27,16 +27,22 @@
 #include "gemm.h"
 #include "ops.h"
 #include "ptx.cuh"
+#include "q8planar.cuh"
 
 namespace da3b {
 
 constexpr int kEpiWarps = 8;
 
-template <int BN>
+template <int BN, bool kQ8 = false>
 struct GemmCfg {
   static constexpr int kABytes = 128 * 64 * 2;
   static constexpr int kBBytes = BN * 64 * 2;
-  static constexpr int kStageBytes = kABytes + kBBytes;
+  // planar Q8_0 weights (kQ8): per stage the raw int8 tile [BN][64] and its two blocks'
+  // scales [2][BN] f16 land next to the f16 B tile the converter warps write
+  static constexpr int kQBytes = kQ8 ? BN * 64 : 0;
+  static constexpr int kSBytes = kQ8 ? 2 * BN * 2 : 0;
+  static constexpr int kTxBytes = kQ8 ? kABytes + kQBytes + kSBytes : kABytes + kBBytes;  // TMA bytes a stage
+  static constexpr int kStageBytes = kABytes + kBBytes + kQBytes + kSBytes;
   // per epilogue warp: a [32][32] f32 staging buffer and its bias slice (BN >= 64).
   // They cost one pipeline stage (two at BN = 64); the staged epilogue made the
   // M = 1370 GEMMs of a batch-1 ViT-B 1.14-2.1x faster on a B200 (QKV 27.6 -> 13.1 us,
@@ -44,7 +50,8 @@ struct GemmCfg {
   static constexpr int kEpiBufBytes = BN >= 64 ? 4096 : 0;
   static constexpr int kBiasFloats = BN >= 64 ? BN / 2 : 0;
   static constexpr int kEpiBytes = kEpiWarps * (kEpiBufBytes + kBiasFloats * 4);
-  static constexpr int kStages = (BN >= 256) ? 3 : (BN >= 128 ? 5 : (BN >= 64 ? 6 : 8));
+  static constexpr int kStages =
+      kQ8 ? (BN >= 128 ? 4 : 6) : ((BN >= 256) ? 3 : (BN >= 128 ? 5 : (BN >= 64 ? 6 : 8)));
   static constexpr int kAccCols = (BN < 32) ? 32 : BN;
   static constexpr int kTmemCols = (2 * kAccCols <= 64) ? 64 : (2 * kAccCols <= 128 ? 128 : (2 * kAccCols <= 256 ? 256 : 512));
   // epilogue constants of the fused out2a -> out2b stage (N == 32): bias, LayerNorm
@@ -175,6 +182,8 @@ __device__ __forceinline__ void q8_roundtrip32(float (&t)[32]) {
 }
 
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+constexpr int kConvWarps = 4;  // planar Q8_0 weight-tile converters (k_tc_gemm<BN, true>)
+constexpr int kGemmThreadsQ8 = kGemmThreads + 32 * kConvWarps;
 
 // 8 consecutive f32 (32-byte aligned) from global memory.
 __device__ __forceinline__ void load_f8(const float* p, float* v) {
@@ -652,22 +661,29 @@ __device__ __forceinline__ void epi_resid_transposed(const GemmGeom& g, const Ep
   }
 }
 
-template <int BN>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    k_tc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmGeom g,
-              const EpiArgs e, int* status) {
-  using Cfg = GemmCfg<BN>;
+// kQ8: the weights are planar Q8_0 (q8planar.cuh): tmB maps the int8 plane (box [BN][64],
+// no swizzle), tmS the f16 scale plane (box [2][BN]); four more warps (10-13) turn each
+// stage's raw tile into the f16 B tile, 128B-swizzled as a TMA would have written it,
+// and release it to the MMA warp. Otherwise tmB maps f16 weights and tmS is unused.
+template <int BN, bool kQ8>
+__global__ void __launch_bounds__(kQ8 ? kGemmThreadsQ8 : kGemmThreads, 1)
+    k_tc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const __grid_constant__ CUtensorMap tmS, const GemmGeom g, const EpiArgs e, int* status) {
+  using Cfg = GemmCfg<BN, kQ8>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + Cfg::kStages * Cfg::kABytes;
+  uint8_t* sQ = sB + Cfg::kStages * Cfg::kBBytes;  // kQ8: raw int8 tiles
+  uint8_t* sS = sQ + Cfg::kStages * Cfg::kQBytes;  // kQ8: their scales
   float* sConst = reinterpret_cast<float*>(smem + Cfg::kStages * Cfg::kStageBytes);
   uint8_t* sEpi = smem + Cfg::kStages * Cfg::kStageBytes + Cfg::kConstBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes + Cfg::kConstBytes + Cfg::kEpiBytes);
   uint64_t* empty = full + Cfg::kStages;
   uint64_t* tfull = empty + Cfg::kStages;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* conv = tempty + 2;  // kQ8: [kStages] the stage's f16 B tile is written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(conv + (kQ8 ? Cfg::kStages : 0));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -695,9 +711,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], Cfg::kSplitTiles ? kEpiWarps / 2 : kEpiWarps);
     }
+    if (kQ8)
+      for (int st = 0; st < Cfg::kStages; ++st) mbar_init(&conv[st], kConvWarps);
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (kQ8) prefetch_tmap(&tmS);
   }
   if (warp == 1) tmem_alloc(tmem_slot, Cfg::kTmemCols);
   tc_fence_before();
@@ -724,10 +743,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int kb = 0; kb < g.num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, status, kStatusTimeoutEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          mbar_arrive_expect_tx(&full[stage], Cfg::kTxBytes);
           uint8_t* a_dst = sA + stage * Cfg::kABytes;
           uint8_t* b_dst = sB + stage * Cfg::kBBytes;
-          if (g.mode == kModeConv) {
+          if (kQ8) {
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * 64, mt * 128);
+            tma_load_2d(sQ + stage * Cfg::kQBytes, &tmB, &full[stage], kb * 64, n0);
+            tma_load_2d(sS + stage * Cfg::kSBytes, &tmS, &full[stage], n0, kb * 2);
+          } else if (g.mode == kModeConv) {
             const int tap = kb / g.ic_chunks;
             const int ic0 = (kb % g.ic_chunks) * 64;
             const int dy = tap / g.ksize - g.pad, dx = tap % g.ksize - g.pad;
@@ -758,6 +781,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t d_tmem = tmem_base + acc * Cfg::kAccCols;
         for (int kb = 0; kb < g.num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, status, kStatusTimeoutFull)) { ok = false; break; }
+          if (kQ8 && !mbar_wait(&conv[stage], phase, status, kStatusTimeoutFull)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = umma_desc_sw128(smem_u32(sA + stage * Cfg::kABytes));
           const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * Cfg::kBBytes));
@@ -771,6 +795,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     __syncwarp();
+  } else if (kQ8 && warp >= 2 + kEpiWarps) {
+    // ------------------------------------------------------------ weight-tile dequantisation
+    // 128 threads, 16-byte pieces (8 weights): thread ct takes column chunk c = ct % 8 of
+    // rows ct / 8 + 16 i, so a warp reads 4 raw rows (256 contiguous bytes) and writes 4
+    // swizzled f16 rows (512 contiguous bytes) per step; chunk c of row n goes to
+    // 16-byte slot c ^ (n % 8) of the row, where the 128B swizzle of a TMA load puts it.
+    const int ct = threadIdx.x - 32 * (2 + kEpiWarps);
+    const int c = ct & 7, n_lo = ct >> 3;
+    const int swz = (c ^ (n_lo & 7)) << 4;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int kb = 0; kb < g.num_kb; ++kb) {
+        if (!mbar_wait_warp(&full[stage], phase, status, kStatusTimeoutFull)) { ok = false; break; }
+        const uint8_t* qt = sQ + stage * Cfg::kQBytes;
+        const __half* sc = reinterpret_cast<const __half*>(sS + stage * Cfg::kSBytes) + (c >> 2) * BN;
+        uint8_t* bt = sB + stage * Cfg::kBBytes;
+#pragma unroll
+        for (int i = 0; i < BN / 16; ++i) {
+          const int n = n_lo + 16 * i;
+          const uint2 raw = *reinterpret_cast<const uint2*>(qt + n * 64 + c * 8);
+          const __half d = sc[n];
+          *reinterpret_cast<uint4*>(bt + n * 128 + swz) = q8x8_to_f16x8(raw, __halves2half2(d, d));
+        }
+        fence_proxy_async_smem();  // the tensor core reads the tile through the async proxy
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[stage]);
+        if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
+      }
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
@@ -1255,15 +1310,16 @@ static int num_sms() {
   return g_num_sms;
 }
 
-template <int BN>
-static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeom& g, const EpiArgs& e, int* status,
-                     cudaStream_t stream, int max_ctas) {
-  using Cfg = GemmCfg<BN>;
+// kQ8: tb maps the planar Q8_0 int8 plane and ts its scale plane; otherwise ts is unused.
+template <int BN, bool kQ8>
+static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ts, const GemmGeom& g,
+                     const EpiArgs& e, int* status, cudaStream_t stream, int max_ctas) {
+  using Cfg = GemmCfg<BN, kQ8>;
   static std::atomic<uint64_t> attr_set{0};  // one bit per device; first calls may race
   int dev = 0;
   cudaGetDevice(&dev);
   if (!((attr_set.load() >> (dev & 63)) & 1)) {
-    if (cudaFuncSetAttribute(k_tc_gemm<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
+    if (cudaFuncSetAttribute(k_tc_gemm<BN, kQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
         cudaSuccess)
       return -10;
     attr_set.fetch_or(uint64_t(1) << (dev & 63));
@@ -1273,7 +1329,7 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeo
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
   if (tiles < grid) grid = tiles;
   if (grid <= 0) return 0;
-  k_tc_gemm<BN><<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, g, e, status);
+  k_tc_gemm<BN, kQ8><<<grid, kQ8 ? kGemmThreadsQ8 : kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, ts, g, e, status);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }
 
@@ -1381,11 +1437,13 @@ static bool want_2sm(const GemmGeom& g, int bn) {
 // Launch with a validated geometry. BN in {32, 64, 128, 256}.
 int gemm_launch(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmGeom& g, const EpiArgs& e,
                 int* status, cudaStream_t stream, int max_ctas) {
+  CUtensorMap unused;
+  memset(&unused, 0, sizeof(unused));
   switch (bn) {
-    case 32: return launch_bn<32>(ta, tb, g, e, status, stream, max_ctas);
-    case 64: return launch_bn<64>(ta, tb, g, e, status, stream, max_ctas);
-    case 128: return launch_bn<128>(ta, tb, g, e, status, stream, max_ctas);
-    case 256: return launch_bn<256>(ta, tb, g, e, status, stream, max_ctas);
+    case 32: return launch_bn<32, false>(ta, tb, unused, g, e, status, stream, max_ctas);
+    case 64: return launch_bn<64, false>(ta, tb, unused, g, e, status, stream, max_ctas);
+    case 128: return launch_bn<128, false>(ta, tb, unused, g, e, status, stream, max_ctas);
+    case 256: return launch_bn<256, false>(ta, tb, unused, g, e, status, stream, max_ctas);
     default: return -12;
   }
 }
@@ -1431,6 +1489,14 @@ static int check_epi(const EpiArgs& e, int N) {
   return 0;
 }
 
+// Few rows (one image: M = 1370): with too few CTA-pair tiles for the SMs the GEMM runs
+// on one-CTA tiles; narrower ones then keep more SMs busy (a ViT-B fc2 of N = 768 has 33
+// tiles of 128 x 256 but 132 of 128 x 64).
+static int narrow_1sm_bn(int m_tiles, int N, int bn) {
+  while (bn > 64 && static_cast<long>(m_tiles) * ((N + bn - 1) / bn) < num_sms()) bn /= 2;
+  return bn;
+}
+
 int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, int ldw, int bn, const EpiArgs& e,
                 int* status, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return M == 0 ? 0 : -30;
@@ -1451,10 +1517,7 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
   g.num_n_tiles = (N + bn - 1) / bn;
   const bool two = want_2sm(g, bn);
   if (auto_bn && !two && e.kind != kEpiOut2) {
-    // Few rows (one image: M = 1370): with too few CTA-pair tiles for the SMs the GEMM
-    // runs on one-CTA tiles; narrower ones then keep more SMs busy (a ViT-B fc2 of
-    // N = 768 has 33 tiles of 128 x 256 but 132 of 128 x 64).
-    while (bn > 64 && static_cast<long>(g.num_m_tiles) * ((N + bn - 1) / bn) < num_sms()) bn /= 2;
+    bn = narrow_1sm_bn(g.num_m_tiles, N, bn);
     g.num_n_tiles = (N + bn - 1) / bn;
   }
   CUtensorMap ta, tb, tc;
@@ -1478,6 +1541,50 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
     e2.tma_store = 2;
   }
   return gemm_launch2(bn, ta, tb, tc, g, e2, status, stream);
+}
+
+// Tile width the planar Q8_0 GEMM (k_tc_gemm<BN, true>) takes for an M x N linear, or 0
+// when the problem is one for the CTA-pair kernel (many rows), whose weights are then
+// better dequantised once per ViT block into f16 than once per 256-row tile pair.
+int gemm_q8p_bn(int M, int N) {
+  if (M <= 0 || N <= 0 || N % 8) return 0;
+  GemmGeom g;
+  memset(&g, 0, sizeof(g));
+  g.num_m_tiles = (M + 127) / 128;
+  int bn = pick_bn(N);
+  g.num_n_tiles = (N + bn - 1) / bn;
+  if (want_2sm(g, bn)) return 0;
+  bn = narrow_1sm_bn(g.num_m_tiles, N, bn);
+  return (bn == 64 || bn == 128) ? bn : 0;
+}
+
+int gemm_linear_q8p(const __half* A, int M, int K, int lda, const uint8_t* Wq, int N, const EpiArgs& e, int* status,
+                    cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return M == 0 ? 0 : -30;
+  if (lda < K || lda % 8 || K % 32 || N % 8 || (reinterpret_cast<uintptr_t>(Wq) & 15) || e.kind == kEpiOut2)
+    return -31;
+  const int bn = gemm_q8p_bn(M, N);
+  if (!bn) return 1;
+  int rc = check_epi(e, N);
+  if (rc) return rc;
+  GemmGeom g;
+  memset(&g, 0, sizeof(g));
+  g.mode = kModeLinear;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.num_kb = (K + 63) / 64;
+  g.num_m_tiles = (M + 127) / 128;
+  g.num_n_tiles = (N + bn - 1) / bn;
+  CUtensorMap ta, tq, ts;
+  if ((rc = make_tmap_2d(&ta, A, M, K, lda, 128))) return rc - 100;
+  if ((rc = make_tmap_2d_typed(&tq, Wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, 64, bn, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc - 200;
+  if ((rc = make_tmap_2d_typed(&ts, Wq + static_cast<size_t>(N) * K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K / 32, N, N,
+                               bn, 2, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc - 300;
+  return bn == 64 ? launch_bn<64, true>(ta, tq, ts, g, e, status, stream, 0)
+                  : launch_bn<128, true>(ta, tq, ts, g, e, status, stream, 0);
 }
 
 // Pixel block of one 128-row M tile: the (bw, bh) with bw * bh == 128 that wastes

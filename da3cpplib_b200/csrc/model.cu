@@ -9,6 +9,7 @@
 #include <string.h>
 
 #include "ops.h"
+#include "q8planar.cuh"
 
 namespace da3b {
 
@@ -153,9 +154,17 @@ bool DeviceModel::lin_q8(const std::string& wname, const std::string& bname, Lin
   out.ldw = K;
   if (K % 32) { if (err) *err = "K not a multiple of 32 in " + wname; return false; }
   if (keep_q8 && t->type == 8) {
-    // resident as the GGUF's Q8_0 bytes; dequantised per forward into the staging buffer
+    // resident as the GGUF's Q8_0 bytes in planar form (q8planar.cuh: the int8 plane and
+    // the transposed f16 scale plane, the same byte count); per forward either the GEMM
+    // dequantises its weight tiles itself or a staging kernel writes f16 ahead of a block
+    if (q8p_bytes(N, K) != t->nbytes) { if (err) *err = "unexpected Q8_0 size of " + wname; return false; }
     uint8_t* q = static_cast<uint8_t*>(dalloc(t->nbytes));
-    if (!q || cudaMemcpy(q, t->data, t->nbytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+    void* raw = nullptr;
+    bool ok = q && cudaMalloc(&raw, t->nbytes) == cudaSuccess &&
+              cudaMemcpy(raw, t->data, t->nbytes, cudaMemcpyHostToDevice) == cudaSuccess &&
+              repack_q8_0_planar(raw, N, K, q, nullptr) == 0 && cudaDeviceSynchronize() == cudaSuccess;
+    if (raw) cudaFree(raw);
+    if (!ok) {
       if (err) *err = "Q8_0 upload failed for " + wname;
       return false;
     }

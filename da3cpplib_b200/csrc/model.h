@@ -39,7 +39,7 @@ struct Config {
 // the engine dequantises it into its per-block staging buffer ahead of the block.
 struct Lin {
   __half* w = nullptr;
-  const uint8_t* q8 = nullptr;
+  const uint8_t* q8 = nullptr;  // planar Q8_0 (q8planar.cuh) when resident quantised
   float* b = nullptr;
   int N = 0, K = 0, ldw = 0;
 };

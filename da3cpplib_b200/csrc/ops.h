@@ -21,6 +21,13 @@ int gemm_launch(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
 // C[M][N] = A[M][K] * W[N][K]^T with a fused epilogue. bn <= 0 picks the N tile.
 int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, int ldw, int bn, const EpiArgs& e,
                 int* status, cudaStream_t stream);
+// The same with W planar Q8_0 [N][K] (q8planar.cuh; K % 32 == 0, N % 8 == 0): the GEMM
+// dequantises its weight tiles in shared memory, f16(d * q) as the staging dequantisation
+// gives. Serves the one-CTA tile regime only (gemm_q8p_bn(M, N) != 0, the tile width it
+// takes); returns 1 without launching otherwise.
+int gemm_q8p_bn(int M, int N);
+int gemm_linear_q8p(const __half* A, int M, int K, int lda, const uint8_t* Wq, int N, const EpiArgs& e, int* status,
+                    cudaStream_t stream);
 // Implicit-GEMM KxK stride-1 "same" convolution: X NHWC [B][H][W][IC] f16,
 // Wp packed [OC][ksize*ksize][icp] f16 (icp = IC rounded up to 64, zero padded).
 // The epilogue sees output pixel indices (b*H + y)*W + x as rows.
@@ -45,18 +52,21 @@ EpiArgs epi_default();
 int dequant_q8_0(const void* q8, int rows, int K, __half* out, int ldo, cudaStream_t s);
 // Up to four Q8_0 matrices [rows][K/32][34 B] -> dense f16 [rows][K] in one launch;
 // `first` is each segment's first 32-element block in the launch's block numbering.
+// GGUF Q8_0 [N][K] -> planar Q8_0 (q8planar.cuh), the same number of bytes.
+int repack_q8_0_planar(const void* raw, int N, int K, void* planar, cudaStream_t s);
+// Up to four planar Q8_0 matrices -> dense f16 [rows][nblk * 32], one launch.
 struct Q8Seg {
-  const uint8_t* q8;
+  const uint8_t* q8;  // planar Q8_0
   __half* out;
   int rows, nblk;
-  long first;
+  long first;  // blocks of the segments before this one
 };
 struct Q8Segs {
   Q8Seg s[4];
   int n;
-  long total;
+  long total;  // blocks of all segments
 };
-int dequant_q8_0_segs(const Q8Segs& g, cudaStream_t s);
+int dequant_q8p_segs(const Q8Segs& g, cudaStream_t s);
 int f32_to_f16(const float* in, __half* out, size_t n, cudaStream_t s);
 
 // Per-device status word (allocated on first use for the current device).

@@ -61,6 +61,27 @@ DA3B_API int da3b_linear_f16(const void* x, int M, int K, int lda, const void* w
 DA3B_API int da3b_linear_resid_f32(const void* x, int M, int K, int lda, const void* w, int N, int ldw,
                                    const float* bias, const float* scale, float* resid, int ldr, void* stream);
 
+/* Planar Q8_0, the resident form of the ViT block linears: the GGUF Q8_0 bytes of W
+ * [N][K] (K % 32 == 0, N % 8 == 0) as an int8 plane q [N][K] followed by the f16 block
+ * scales transposed, d [K/32][N] (the same byte count, rows a TMA can tile).
+ *   da3b_repack_q8_0_planar: GGUF Q8_0 rows on the device -> planar Q8_0.
+ *   da3b_dequant_q8p:        planar Q8_0 -> f16 w [N][K] = f16(d * q), bit-identical
+ *                            to da3b_dequant_q8_0.
+ *   da3b_linear_q8p_f16 / da3b_linear_q8p_resid_f32: da3b_linear_f16 /
+ *                            da3b_linear_resid_f32 with W planar Q8_0, the weight tiles
+ *                            dequantised in shared memory by the GEMM (the dequantisation
+ *                            inside ggml_mul_mat(W_q8_0, x), src/ggml_extend.hpp:6-10);
+ *                            bit-identical to the f16 route on da3b_dequant_q8p's
+ *                            weights. They serve the one-CTA tile regime (few rows, e.g.
+ *                            one image's 1370 tokens) and return 1 without launching
+ *                            when M x N is a problem for the CTA-pair kernel. */
+DA3B_API int da3b_repack_q8_0_planar(const void* q8, int N, int K, void* planar, void* stream);
+DA3B_API int da3b_dequant_q8p(const void* planar, int N, int K, void* w_f16, void* stream);
+DA3B_API int da3b_linear_q8p_f16(const void* x, int M, int K, int lda, const void* planar, int N,
+                                 const float* bias, int act, void* out, int ldo, void* stream);
+DA3B_API int da3b_linear_q8p_resid_f32(const void* x, int M, int K, int lda, const void* planar, int N,
+                                       const float* bias, const float* scale, float* resid, int ldr, void* stream);
+
 /* Bidirectional attention softmax(q k^T / 8) v over head_dim 64 — the replacement of
  * ggml_flash_attn_ext with F32 precision in attention() (src/attention.cpp:44-96).
  * qkv: f16 [nseq*seqlen][3*heads*64] (q | k | v, head h at columns h*64 of each third,

@@ -354,9 +354,11 @@ def test_da2_matches_transformers(cuda, tag):
 
 
 def test_q8_resident_weights_match_load_time_f16(cuda):
-    """ViT block linears resident as Q8_0 and dequantised ahead of each block (default)
-    give the same bits as the load-time f16 planes ($DA3B_F16_WEIGHTS=1): both round
-    d * q to f16 the same way. The device memory each model takes at load is printed."""
+    """ViT block linears resident as planar Q8_0 give the same bits as the load-time f16
+    planes ($DA3B_F16_WEIGHTS=1), both through the per-block f16 staging buffer (default)
+    and when the GEMMs dequantise their weight tiles in shared memory ($DA3B_Q8_TILES=1,
+    taken at these few rows): every route rounds d * q to f16 the same way. The device
+    memory each model takes at load is printed."""
     import os
 
     import torch
@@ -383,6 +385,14 @@ def test_q8_resident_weights_match_load_time_f16(cuda):
         b.close()
     finally:
         del os.environ["DA3B_F16_WEIGHTS"]
+    os.environ["DA3B_Q8_TILES"] = "1"
+    try:
+        c = Model(path, 0)
+        out_c = c.infer(imgs, views_per_scene=3, rays=True)
+        c.close()
+    finally:
+        del os.environ["DA3B_Q8_TILES"]
     for k in out_a:
         assert np.array_equal(out_a[k], out_b[k]), k
+        assert np.array_equal(out_c[k], out_b[k]), k
     print(f"\n[weights] device bytes at load: Q8_0-resident {used_q8}, f16 {used_f16}")

@@ -59,6 +59,91 @@ def test_dequant_q8_0_exact(lib):
     assert lib.da3b_device_status() == 0
 
 
+def _q8_0_raw(rng, N, K, tiny=False):
+    """GGUF Q8_0 bytes of an N x K matrix (q in [-128, 127], f16 scales), and the
+    reference f16(d * q) as numpy f16. tiny: a third of the scales near the bottom of the
+    f16 range, so some products are subnormal."""
+    q = rng.integers(-128, 128, size=(N, K // 32, 32), dtype=np.int8)
+    d = rng.uniform(1e-3, 1e-2, size=(N, K // 32)).astype(np.float16)
+    if tiny:
+        d[:, ::3] = rng.uniform(2.0 ** -23, 2.0 ** -14, size=d[:, ::3].shape).astype(np.float16)
+    raw = np.zeros((N, K // 32, 34), dtype=np.uint8)
+    raw[:, :, :2] = d.view(np.uint8).reshape(N, K // 32, 2)
+    raw[:, :, 2:] = q.view(np.uint8)
+    ref = (d.astype(np.float32)[:, :, None] * q.astype(np.float32)).reshape(N, K).astype(np.float16)
+    return raw.reshape(-1), ref
+
+
+@pytest.mark.parametrize("N,K", [(96, 384), (64, 96), (2304, 768)])
+def test_q8_planar_dequant_exact(lib, N, K):
+    """Planar Q8_0 (int8 plane + transposed f16 scale plane, the GGUF bytes): the repack,
+    then the staging dequantisation's f16(d * q) (exact int8 -> f16, one f16 multiply)
+    against numpy's rounding of the f32 product, subnormal products included, and
+    against da3b_dequant_q8_0 on the raw rows."""
+    rng = np.random.default_rng(N + K)
+    raw, ref = _q8_0_raw(rng, N, K, tiny=True)
+    q8 = torch.from_numpy(raw).cuda()
+    planar = torch.empty(N * K + (K // 32) * N * 2, dtype=torch.uint8, device="cuda")
+    assert lib.da3b_repack_q8_0_planar(ptr(q8), N, K, ptr(planar), stream()) == 0
+    w = torch.empty(N, K, dtype=torch.float16, device="cuda")
+    assert lib.da3b_dequant_q8p(ptr(planar), N, K, ptr(w), stream()) == 0
+    w0 = torch.empty(N, K, dtype=torch.float16, device="cuda")
+    assert lib.da3b_dequant_q8_0(ptr(q8), N, K, ptr(w0), K, stream()) == 0
+    torch.cuda.synchronize()
+    assert lib.da3b_device_status() == 0
+    got = w.cpu().numpy()
+    assert np.array_equal(got.view(np.uint16), ref.view(np.uint16))
+    assert torch.equal(w, w0)
+
+
+@pytest.mark.parametrize("M,K,N,kind", [(1370, 768, 2304, "f16"), (1370, 768, 3072, "gelu"), (1370, 768, 768, "resid"),
+                                        (1370, 3072, 768, "resid"), (100, 384, 1152, "f16"), (257, 96, 64, "gelu"),
+                                        (300, 160, 200, "f16"), (20000, 256, 1024, "f16")])
+def test_linear_q8_planar_tiles(lib, M, K, N, kind):
+    """The GEMM that dequantises planar Q8_0 weight tiles in shared memory (four converter
+    warps write each stage's f16 B tile in the 128B-swizzled layout) against the f16 GEMM
+    on the staging dequantisation's weights: bit-identical outputs (same f16 weights, same
+    MMA order, same epilogue), with tile widths 64 and 128, a ragged last K block (K = 96,
+    160) and ragged N; the CTA-pair regime (M = 20000) is declined (returns 1)."""
+    rng = np.random.default_rng(M + K + N)
+    raw, _ = _q8_0_raw(rng, N, K)
+    q8 = torch.from_numpy(raw).cuda()
+    planar = torch.empty(N * K + (K // 32) * N * 2, dtype=torch.uint8, device="cuda")
+    assert lib.da3b_repack_q8_0_planar(ptr(q8), N, K, ptr(planar), stream()) == 0
+    w = torch.empty(N, K, dtype=torch.float16, device="cuda")
+    assert lib.da3b_dequant_q8p(ptr(planar), N, K, ptr(w), stream()) == 0
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    b = torch.randn(N, device="cuda", generator=g).float()
+    if kind == "resid":
+        sc = torch.randn(N, device="cuda", generator=g).float()
+        r0 = torch.randn(M, N, device="cuda", generator=g).float()
+        ra, rb = r0.clone(), r0.clone()
+        rc = lib.da3b_linear_q8p_resid_f32(ptr(x), M, K, K, ptr(planar), N, ptr(b), ptr(sc), ptr(ra), N, stream())
+        assert rc == 0
+        assert lib.da3b_linear_resid_f32(ptr(x), M, K, K, ptr(w), N, K, ptr(b), ptr(sc), ptr(rb), N, stream()) == 0
+        torch.cuda.synchronize()
+        assert lib.da3b_device_status() == 0
+        assert torch.equal(ra, rb)
+        return
+    act = 2 if kind == "gelu" else 0
+    oa = torch.full((M, N), 7.0, dtype=torch.float16, device="cuda")
+    ob = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    rc = lib.da3b_linear_q8p_f16(ptr(x), M, K, K, ptr(planar), N, ptr(b), act, ptr(oa), N, stream())
+    if M >= 20000:
+        assert rc == 1
+        return
+    assert rc == 0
+    assert lib.da3b_linear_f16(ptr(x), M, K, K, ptr(w), N, K, ptr(b), act, ptr(ob), N, stream()) == 0
+    torch.cuda.synchronize()
+    assert lib.da3b_device_status() == 0
+    assert torch.equal(oa, ob)
+    ref = x.float() @ w.float().t() + b
+    if act:
+        ref = torch.nn.functional.gelu(ref)
+    close(oa, ref)
+
+
 @pytest.mark.parametrize("M,K,N", [(1, 64, 32), (127, 384, 1152), (128, 128, 64), (300, 200, 48),
                                    (1370, 768, 2304), (2740, 1024, 4096), (1370, 4096, 1024), (257, 640, 96),
                                    (20000, 256, 1000)])
