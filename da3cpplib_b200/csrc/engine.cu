@@ -105,6 +105,10 @@ Engine::~Engine() {
   if (device_ >= 0) cudaSetDevice(device_);
   plans_.clear();
   if (wstage_) cudaFree(wstage_);
+  for (auto& st : side_)
+    if (st) cudaStreamDestroy(st);
+  for (auto& ev : ev_)
+    if (ev) cudaEventDestroy(ev);
   model_.reset();
 }
 
@@ -135,6 +139,18 @@ std::unique_ptr<Engine> Engine::create(const std::string& path, int device, std:
   }
   if (const char* g = getenv("DA3B_GRAPH")) e->use_graph_ = strcmp(g, "0") != 0;
   if (const char* q = getenv("DA3B_Q8_TILES")) e->q8_tiles_ = q[0] == '1';
+  for (auto& st : e->side_)
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
+      st = nullptr;
+      if (err) *err = "cannot create the head's side streams";
+      return nullptr;
+    }
+  for (auto& ev : e->ev_)
+    if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
+      ev = nullptr;
+      if (err) *err = "cannot create the head's events";
+      return nullptr;
+    }
   return e;
 }
 
@@ -624,8 +640,11 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
 }
 
 // One fusion pyramid (refinenet4 .. refinenet1) over the layer_rn maps; writes the
-// x2-upsampled refinenet1 output into u_out (8gh x 8gw).
-int Engine::pyramid(Plan& p, const void* fw, __half* u_out, cudaStream_t s) {
+// x2-upsampled refinenet1 output into u_out (8gh x 8gw). lateral_ready (or null): per
+// level r < 3 an event after which RN[r] / RNr[r] and the first conv of the level's RCU1
+// (into lv[r].T) are done on another stream; the pyramid then waits for it before level
+// r and skips that conv.
+int Engine::pyramid(Plan& p, const void* fw, __half* u_out, cudaStream_t s, const cudaEvent_t* lateral_ready) {
   const Fusion* fu = static_cast<const Fusion*>(fw);
   const int V = p.V;
   const int F = fu[0].rc2c1.OC;
@@ -640,8 +659,15 @@ int Engine::pyramid(Plan& p, const void* fw, __half* u_out, cudaStream_t s) {
       y = p.RN[3];
     } else {
       // y1 = top + RCU1(lateral): relu -> conv1 -> relu -> conv2 + lateral (+ top)
-      EpiArgs e1 = epi_f16(L.T, F, f.rc1c1.b, kActRelu);
-      CK(conv_nhwc(p.RNr[r], V, hh, ww, f.rc1c1.IC, f.rc1c1.w, F, 3, 0, e1, status_, s));
+      if (lateral_ready) {
+        if (cudaStreamWaitEvent(s, lateral_ready[r], 0) != cudaSuccess) {
+          err_ = "stream wait failed";
+          return -51;
+        }
+      } else {
+        EpiArgs e1 = epi_f16(L.T, F, f.rc1c1.b, kActRelu);
+        CK(conv_nhwc(p.RNr[r], V, hh, ww, f.rc1c1.IC, f.rc1c1.w, F, 3, 0, e1, status_, s));
+      }
       EpiArgs e2 = epi_f16(L.Y1, F, f.rc1c2.b, kActNone);
       e2.res1 = p.RN[r];
       e2.ld_res1 = F;
@@ -687,47 +713,72 @@ int Engine::head(Plan& p, cudaStream_t s) {
       CK(layernorm_f16(p.feats[o], Cf, V * Np, Cf, h.norm_g, h.norm_b, 1e-5f, p.featn[o], Cf, 0, 0, 0, 0, s));
       fin[o] = p.featn[o];
     }
-  // ---- projections (+0.1 UV PE)
-  for (int st = 0; st < 4; ++st) {
-    const Lin& L = h.proj[st];
-    EpiArgs e = epi_f16(p.P[st], L.N, L.b, kActNone);
-    if (c.head_pos_embed) {
-      e.res1 = p.pe_proj[st];
-      e.ld_res1 = L.N;
-      e.res1_mod = Np;
+  // ---- the four lateral branches: projection (+0.1 UV PE) -> resize -> layer_rn (raw +
+  // relu copies) and, for levels 0-2, the first conv of the level's RCU1. They depend on
+  // nothing but the features, and only refinenet4 (level 3) needs its branch before the
+  // fusion chain starts, so branches 0-2 run on side streams (forked and joined by
+  // events, which a graph capture turns into parallel branches) while branch 3 and
+  // then the chain run on s; the chain waits for branch r just before level r. At one
+  // image these launches fill 6-148 of the SMs each.
+  const Fusion* fu = h.fu;
+  auto branch = [&](int st, cudaStream_t bs) -> int {
+    {
+      const Lin& L = h.proj[st];
+      EpiArgs e = epi_f16(p.P[st], L.N, L.b, kActNone);
+      if (c.head_pos_embed) {
+        e.res1 = p.pe_proj[st];
+        e.ld_res1 = L.N;
+        e.res1_mod = Np;
+      }
+      CK(gemm_linear(fin[st], V * Np, Cf, Cf, L.w, L.N, L.ldw, 0, e, status_, bs));
     }
-    CK(gemm_linear(fin[st], V * Np, Cf, Cf, L.w, L.N, L.ldw, 0, e, status_, s));
+    if (st == 0 || st == 1) {
+      const ConvT& rs = st == 0 ? h.rs0 : h.rs1;
+      const int sc = st == 0 ? 4 : 2;
+      EpiArgs e = epi_f16(st == 0 ? p.L0 : p.L1, rs.OC, rs.b, kActNone);
+      e.kind = kEpiConvT;
+      e.ct_hin = gh;
+      e.ct_win = gw;
+      e.ct_s = sc;
+      e.ct_oc = rs.OC;
+      CK(gemm_linear(p.P[st], V * Np, rs.IC, rs.IC, rs.w, sc * sc * rs.OC, rs.IC, 0, e, status_, bs));
+    } else if (st == 3) {
+      const int icp3 = conv_icp(h.rs3.IC);
+      CK(im2col_s2(p.P[3], V, gh, gw, h.rs3.IC, icp3, p.A3, bs));
+      CK(gemm_linear(p.A3, V * p.ho3 * p.wo3, 9 * icp3, 9 * icp3, h.rs3.w, h.rs3.OC, 9 * icp3, 0,
+                     epi_f16(p.L3, h.rs3.OC, h.rs3.b, kActNone), status_, bs));
+    }
+    const __half* Ls[4] = {p.L0, p.L1, p.P[2], p.L3};
+    {
+      EpiArgs e = epi_f16(p.RN[st], F, nullptr, kActNone);
+      e.out_relu = p.RNr[st];
+      CK(conv_nhwc(Ls[st], V, p.lv[st].h, p.lv[st].w, h.rn[st].IC, h.rn[st].w, F, 3, 0, e, status_, bs));
+    }
+    if (st < 3) {
+      const Fusion& f = fu[st];
+      EpiArgs e1 = epi_f16(p.lv[st].T, F, f.rc1c1.b, kActRelu);
+      CK(conv_nhwc(p.RNr[st], V, p.lv[st].h, p.lv[st].w, f.rc1c1.IC, f.rc1c1.w, F, 3, 0, e1, status_, bs));
+    }
+    return 0;
+  };
+  if (cudaEventRecord(ev_[0], s) != cudaSuccess) {
+    err_ = "event record failed";
+    return -52;
   }
-  // ---- resize layers
-  {
-    EpiArgs e = epi_f16(p.L0, h.rs0.OC, h.rs0.b, kActNone);
-    e.kind = kEpiConvT;
-    e.ct_hin = gh;
-    e.ct_win = gw;
-    e.ct_s = 4;
-    e.ct_oc = h.rs0.OC;
-    CK(gemm_linear(p.P[0], V * Np, h.rs0.IC, h.rs0.IC, h.rs0.w, 16 * h.rs0.OC, h.rs0.IC, 0, e, status_, s));
-    EpiArgs e1 = epi_f16(p.L1, h.rs1.OC, h.rs1.b, kActNone);
-    e1.kind = kEpiConvT;
-    e1.ct_hin = gh;
-    e1.ct_win = gw;
-    e1.ct_s = 2;
-    e1.ct_oc = h.rs1.OC;
-    CK(gemm_linear(p.P[1], V * Np, h.rs1.IC, h.rs1.IC, h.rs1.w, 4 * h.rs1.OC, h.rs1.IC, 0, e1, status_, s));
-    const int icp3 = conv_icp(h.rs3.IC);
-    CK(im2col_s2(p.P[3], V, gh, gw, h.rs3.IC, icp3, p.A3, s));
-    CK(gemm_linear(p.A3, V * p.ho3 * p.wo3, 9 * icp3, 9 * icp3, h.rs3.w, h.rs3.OC, 9 * icp3, 0,
-                   epi_f16(p.L3, h.rs3.OC, h.rs3.b, kActNone), status_, s));
+  for (int st = 0; st < 3; ++st) {
+    if (cudaStreamWaitEvent(side_[st], ev_[0], 0) != cudaSuccess) {
+      err_ = "stream wait failed";
+      return -52;
+    }
+    if (int rc = branch(st, side_[st])) return rc;
+    if (cudaEventRecord(ev_[1 + st], side_[st]) != cudaSuccess) {
+      err_ = "event record failed";
+      return -52;
+    }
   }
-  // ---- layer_rn (3x3, no bias): raw + relu copies
-  const __half* Ls[4] = {p.L0, p.L1, p.P[2], p.L3};
-  for (int st = 0; st < 4; ++st) {
-    EpiArgs e = epi_f16(p.RN[st], F, nullptr, kActNone);
-    e.out_relu = p.RNr[st];
-    CK(conv_nhwc(Ls[st], V, p.lv[st].h, p.lv[st].w, h.rn[st].IC, h.rn[st].w, F, 3, 0, e, status_, s));
-  }
+  if (int rc = branch(3, s)) return rc;
   // ---- main fusion pyramid -> out1 -> upsample(+PE) -> out2a + out2b + activation
-  if (int rc = pyramid(p, h.fu, p.U[3], s)) return rc;
+  if (int rc = pyramid(p, h.fu, p.U[3], s, ev_ + 1)) return rc;
   const int h8 = 8 * gh, w8 = 8 * gw;
   CK(conv_nhwc(p.U[3], V, h8, w8, F, h.out1.w, h.out1.OC, 3, 0, epi_f16(p.O1, h.out1.OC, h.out1.b, kActNone), status_,
                s));
@@ -775,7 +826,7 @@ int Engine::head(Plan& p, cudaStream_t s) {
   }
   // ---- aux ray head (DualDPT, src/dpt_head.cpp:225-272)
   if (p.rays) {
-    if (int rc = pyramid(p, h.fa, p.auxA, s)) return rc;
+    if (int rc = pyramid(p, h.fa, p.auxA, s, nullptr)) return rc;
     __half* a = p.auxA;
     __half* b = p.auxB;
     for (int i = 0; i < 5; ++i) {

@@ -104,7 +104,7 @@ class Engine {
   int forward(Plan& p, cudaStream_t s);
   int backbone(Plan& p, cudaStream_t s);
   int head(Plan& p, cudaStream_t s);
-  int pyramid(Plan& p, const void* fuse_weights, __half* u_out, cudaStream_t s);
+  int pyramid(Plan& p, const void* fuse_weights, __half* u_out, cudaStream_t s, const cudaEvent_t* lateral_ready);
 
   std::unique_ptr<DeviceModel> model_;
   // f16 staging buffer of one ViT block's four linears (qkv | proj | fc1 | fc2), filled
@@ -117,6 +117,11 @@ class Engine {
   // one-CTA tiles are read by GEMMs that dequantise their weight tiles in shared memory
   // instead of through the f16 staging buffer (same bits; measured slower at batch 1)
   bool q8_tiles_ = false;
+  // the DPT head's lateral branches 0-2 (projection -> resize -> layer_rn -> first RCU1
+  // conv) run on these side streams; ev_[0] forks them from the forward's stream,
+  // ev_[1 + r] marks branch r done
+  cudaStream_t side_[3] = {nullptr, nullptr, nullptr};
+  cudaEvent_t ev_[4] = {nullptr, nullptr, nullptr, nullptr};
   bool raw_logits_ = false;
   bool act_quant_ = false;
   bool capture_resid_ = false;
