@@ -50,20 +50,6 @@ static_assert(kShareBytes <= kStagesKV * (kKBytes + kVBytes), "a split share fit
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// loads from another CTA's shared memory (a shared::cluster address, mapa_shared)
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t caddr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(caddr)
-               : "memory");
-  return v;
-}
-__device__ __forceinline__ float2 ld_dsmem_f2(uint32_t caddr) {
-  float2 v;
-  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(caddr) : "memory");
-  return v;
-}
 
 // max(a, b, c) in one instruction (sm_100 three-input max.f32)
 __device__ __forceinline__ float fmax3(float a, float b, float c) {

@@ -576,19 +576,24 @@ int conv3_halo(const __half* X, int B, int H, int W, int IC, const __half* Wp, i
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev0);
   // Form: the CTA pair for output counts in groups of 256 (one 8-wide half of N = 256
   // per CTA; measured 6-10% faster than the 2-SM implicit GEMM on the DPT head's
-  // shapes). For 128 outputs: when the 16 x 16 tiles are no more than the SMs (one
-  // image's DPT maps up to 148 x 148), CTA pairs of one 8-wide half each: twice the
-  // CTAs, each with half the MMAs and half the epilogue (batch 1: 13.3-16.5 against
-  // 18.1-22.1 us at 19-74 px, 42.5 against 56.3 us for 768 inputs at 19 x 19; equal at
-  // 148 x 148); otherwise one CTA (the pair form with two halves of N = 128 per CTA was
-  // measured 4% slower on the batched maps). $DA3B_CONV_HALO_PAIR=1 / =0 force the pair
-  // form with two halves / the one-CTA form.
+  // shapes). For 128 outputs, by the number of 16 x 16 tiles (one image, batch 1):
+  //   at most half the SMs (maps up to about 128 x 128): none; the implicit GEMM on
+  //     one-CTA tiles, whose K split spreads the few tiles over more SMs, is faster
+  //     (13.1-14.6 against 15.3-15.8 us with a residual at 37-112 px; 19.0 against 42.4
+  //     us for 768 inputs at 19 x 19);
+  //   up to the SMs (148 x 148): CTA pairs of one 8-wide half each, twice the CTAs of
+  //     the one-CTA form, each with half the MMAs and half the epilogue (21.8 against
+  //     22.9 us for the implicit GEMM);
+  //   more: one CTA (the pair form with two halves of N = 128 per CTA was measured 4%
+  //     slower on the batched maps).
+  // $DA3B_CONV_HALO_PAIR=1 / =0 force the pair form with two halves / the one-CTA form.
   const char* pe = getenv("DA3B_CONV_HALO_PAIR");
   const int pmode = pe && pe[0] == '1' ? 1 : (pe && pe[0] == '0' ? 0 : -1);
   if (sms >= 2 && pmode != 0) {
     if (OC % 256 == 0) return launch_halo2<256, 1>(X, B, H, W, IC, Wp, OC, e, status, s, sms);
     if (OC == 128 && pmode == 1) return launch_halo2<128, 2>(X, B, H, W, IC, Wp, OC, e, status, s, sms);
     const long tiles16 = static_cast<long>(B) * ((W + 15) / 16) * ((H + 15) / 16);
+    if (OC == 128 && 2 * tiles16 <= sms) return 1;
     if (OC == 128 && tiles16 <= sms) return launch_halo2<128, 1>(X, B, H, W, IC, Wp, OC, e, status, s, sms);
   }
   const int icp = conv_icp(IC);

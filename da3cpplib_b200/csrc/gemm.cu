@@ -16,6 +16,7 @@
 //                row.
 // Tiles are visited m-major (all N tiles of one 128-row A panel back to back) so an
 // A panel is read from HBM about once while the weights stay resident in L2.
+#include <algorithm>
 #include <atomic>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -688,6 +689,14 @@ __global__ void __launch_bounds__(kQ8 ? kGemmThreadsQ8 : kGemmThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_tiles = g.num_m_tiles * g.num_n_tiles;
+  // K split (g.ksplit > 1, BN >= 64): a cluster of ks CTAs shares one tile, CTA `split`
+  // (its cluster rank) taking k-blocks [kb0, kb1); the partial accumulators are summed
+  // into the first CTA's TMEM in rank order before its epilogue. Otherwise the grid is
+  // persistent over tiles and one CTA takes all k-blocks.
+  const int ks = (!kQ8 && g.ksplit > 1) ? g.ksplit : 1;  // not with the Q8_0 converters
+  const int split = static_cast<int>(blockIdx.x) % ks;
+  const int t_first = static_cast<int>(blockIdx.x) / ks, t_step = static_cast<int>(gridDim.x) / ks;
+  const int kb0 = split * g.num_kb / ks, kb1 = (split + 1) * g.num_kb / ks;
 
   if (e.kind == kEpiOut2) {
     // [0,32) bias, [32,64) LN gamma, [64,96) LN beta, [96,352) out2b weights, [352,360) out2b bias
@@ -730,7 +739,7 @@ __global__ void __launch_bounds__(kQ8 ? kGemmThreadsQ8 : kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = t_first; t < num_tiles && ok; t += t_step) {
         const int mt = t / g.num_n_tiles, nt = t % g.num_n_tiles;
         const int n0 = nt * BN;
         int cb = 0, cx = 0, cy = 0;
@@ -741,7 +750,7 @@ __global__ void __launch_bounds__(kQ8 ? kGemmThreadsQ8 : kGemmThreads, 1)
           cy = (rem / g.tiles_x) * g.bh;
           cx = (rem % g.tiles_x) * g.bw;
         }
-        for (int kb = 0; kb < g.num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, status, kStatusTimeoutEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[stage], Cfg::kTxBytes);
           uint8_t* a_dst = sA + stage * Cfg::kABytes;
@@ -773,13 +782,13 @@ __global__ void __launch_bounds__(kQ8 ? kGemmThreadsQ8 : kGemmThreads, 1)
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+      for (int t = t_first; t < num_tiles && ok; t += t_step, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, status, kStatusTimeoutAccumFree)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * Cfg::kAccCols;
-        for (int kb = 0; kb < g.num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, status, kStatusTimeoutFull)) { ok = false; break; }
           if (kQ8 && !mbar_wait(&conv[stage], phase, status, kStatusTimeoutFull)) { ok = false; break; }
           tc_fence_after();
@@ -787,7 +796,7 @@ __global__ void __launch_bounds__(kQ8 ? kGemmThreadsQ8 : kGemmThreads, 1)
           const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * Cfg::kBBytes));
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           umma_commit(&empty[stage]);
           if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
         }
@@ -807,8 +816,8 @@ __global__ void __launch_bounds__(kQ8 ? kGemmThreadsQ8 : kGemmThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-      for (int kb = 0; kb < g.num_kb; ++kb) {
+    for (int t = t_first; t < num_tiles && ok; t += t_step) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait_warp(&full[stage], phase, status, kStatusTimeoutFull)) { ok = false; break; }
         const uint8_t* qt = sQ + stage * Cfg::kQBytes;
         const __half* sc = reinterpret_cast<const __half*>(sS + stage * Cfg::kSBytes) + (c >> 2) * BN;
@@ -834,11 +843,9 @@ __global__ void __launch_bounds__(kQ8 ? kGemmThreadsQ8 : kGemmThreads, 1)
     const int half = (warp - 2) / 4;
     const int c_begin = Cfg::kSplitTiles ? 0 : half * (BN / 2);
     const int c_end = Cfg::kSplitTiles ? BN : c_begin + BN / 2;
-    int it = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
-      if (Cfg::kSplitTiles && (it & 1) != half) continue;  // the other half takes this tile
-      const int acc = it & 1;
-      const uint32_t acc_phase = (it >> 1) & 1;
+    bool split_ok = false;
+    // the epilogue of tile t from accumulator buffer acc (after tfull when wait_full)
+    auto epi_tile = [&](int t, int acc, bool wait_full, uint32_t acc_phase) -> bool {
       const int mt = t / g.num_n_tiles, nt = t % g.num_n_tiles;
       int row = -1;
       if (g.mode == kModeConv) {
@@ -856,7 +863,7 @@ __global__ void __launch_bounds__(kQ8 ? kGemmThreadsQ8 : kGemmThreads, 1)
       const int bcol = nt * BN + c_begin + 4 * lane;
       if (staged && e.kind != kEpiResid && e.bias && 4 * lane < c_end - c_begin && bcol < g.N)
         bq = __ldg(reinterpret_cast<const float4*>(e.bias + bcol));
-      if (!mbar_wait_warp(&tfull[acc], acc_phase, status, kStatusTimeoutAccum)) break;
+      if (wait_full && !mbar_wait_warp(&tfull[acc], acc_phase, status, kStatusTimeoutAccum)) return false;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
       if (staged) {
@@ -883,10 +890,80 @@ __global__ void __launch_bounds__(kQ8 ? kGemmThreadsQ8 : kGemmThreads, 1)
           else epilogue32(g, e, row, nt * BN + c, v);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      return true;
+    };
+    if (ks > 1) {
+      // one tile per cluster: the other CTAs hand their partial accumulator (this
+      // warp's columns) to the first through their idle A / B ring, column-chunk-major
+      // (float4 chunk j of row r at [j][r]), so that a warp's remote load reads 512
+      // contiguous bytes
+      if (t_first < num_tiles && mbar_wait_warp(&tfull[0], 0, status, kStatusTimeoutAccum)) {
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+        if (split != 0) {
+          float4* share = reinterpret_cast<float4*>(smem);
+#pragma unroll 1
+          for (int c = c_begin; c < c_end; c += 32) {
+            uint32_t raw[32];
+            tmem_ld32(tbase + c, raw);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              share[((c >> 2) + i) * 128 + r] = make_float4(__uint_as_float(raw[4 * i]), __uint_as_float(raw[4 * i + 1]),
+                                                            __uint_as_float(raw[4 * i + 2]), __uint_as_float(raw[4 * i + 3]));
+          }
+        }
+        split_ok = true;
+      }
+    } else {
+      int it = 0;
+      for (int t = t_first; t < num_tiles; t += t_step, ++it) {
+        if (Cfg::kSplitTiles && (it & 1) != half) continue;  // the other half takes this tile
+        const int acc = it & 1;
+        if (!epi_tile(t, acc, true, (it >> 1) & 1)) break;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+      }
     }
+    if (ks > 1) {
+      cluster_sync();  // every partial accumulator is in its CTA's shared memory
+      if (split == 0 && split_ok) {
+        // sum the shares into this CTA's accumulator in rank order, then the epilogue
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+        const uint32_t share = smem_u32(smem);
+#pragma unroll 1
+        for (int c = c_begin; c < c_end; c += 32) {
+          uint32_t raw[32];
+          tmem_ld32(tbase + c, raw);
+          tmem_wait_ld();
+          for (int sp = 1; sp < ks; ++sp) {
+            float4 v[8];
+            const uint32_t peer = mapa_shared(share + static_cast<uint32_t>(((c >> 2) * 128 + r) * 16), static_cast<uint32_t>(sp));
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = ld_dsmem_f4(peer + static_cast<uint32_t>(i * 128 * 16));
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              raw[4 * i] = __float_as_uint(__uint_as_float(raw[4 * i]) + v[i].x);
+              raw[4 * i + 1] = __float_as_uint(__uint_as_float(raw[4 * i + 1]) + v[i].y);
+              raw[4 * i + 2] = __float_as_uint(__uint_as_float(raw[4 * i + 2]) + v[i].z);
+              raw[4 * i + 3] = __float_as_uint(__uint_as_float(raw[4 * i + 3]) + v[i].w);
+            }
+          }
+          tmem_st32(tbase + c, raw);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        epi_tile(t_first, 0, false, 0);
+      }
+    }
+  }
+  // the K-split cluster's second barrier: no CTA leaves while the first may still read
+  // its share (every thread of every CTA of the cluster takes both barriers)
+  if (ks > 1) {
+    if (warp < 2 || (kQ8 && warp >= 2 + kEpiWarps)) cluster_sync();
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
   }
 
   tc_fence_before();
@@ -1325,6 +1402,24 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
     attr_set.fetch_or(uint64_t(1) << (dev & 63));
   }
   const int tiles = g.num_m_tiles * g.num_n_tiles;
+  if (g.ksplit > 1) {
+    // one tile per cluster of g.ksplit CTAs
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>(tiles * g.ksplit), 1, 1);
+    cfg.blockDim = dim3(kQ8 ? kGemmThreadsQ8 : kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(g.ksplit);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, k_tc_gemm<BN, kQ8>, ta, tb, ts, g, e, status) != cudaSuccess) return -11;
+    return cudaGetLastError() == cudaSuccess ? 0 : -11;
+  }
   int grid = num_sms();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
   if (tiles < grid) grid = tiles;
@@ -1497,6 +1592,28 @@ static int narrow_1sm_bn(int m_tiles, int N, int bn) {
   return bn;
 }
 
+// $DA3B_GEMM_KSPLIT=0 (read once per process) keeps every 1-SM launch at one CTA per tile.
+static bool ksplit_enabled() {
+  static const bool on = [] {
+    const char* s = getenv("DA3B_GEMM_KSPLIT");
+    return !(s && s[0] == '0');
+  }();
+  return on;
+}
+
+// K split of the 1-SM kernel: when the tiles fill at most half the SMs and the reduction
+// is long, a cluster of up to 4 CTAs takes each tile, each at least 8 k-blocks, and the
+// first sums the others' partial accumulators (one image's stride-2 conv: 36 tiles of
+// 108 k-blocks).
+static int pick_ksplit(long tiles, int num_kb, int bn) {
+  if (bn < 64 || tiles <= 0 || !ksplit_enabled()) return 1;
+  const int sms = num_sms();
+  if (tiles * 2 > sms) return 1;
+  long ks = std::min<long>(4, sms / tiles);
+  ks = std::min<long>(ks, num_kb / 8);
+  return ks >= 2 ? static_cast<int>(ks) : 1;
+}
+
 int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, int ldw, int bn, const EpiArgs& e,
                 int* status, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return M == 0 ? 0 : -30;
@@ -1520,6 +1637,7 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
     bn = narrow_1sm_bn(g.num_m_tiles, N, bn);
     g.num_n_tiles = (N + bn - 1) / bn;
   }
+  if (!two && e.kind != kEpiOut2) g.ksplit = pick_ksplit(static_cast<long>(g.num_m_tiles) * g.num_n_tiles, g.num_kb, bn);
   CUtensorMap ta, tb, tc;
   if ((rc = make_tmap_2d(&ta, A, M, K, lda, 128))) return rc - 100;
   if ((rc = make_tmap_2d(&tb, W, N, K, ldw, two ? bn / 2 : bn))) return rc - 200;
@@ -1645,6 +1763,7 @@ int conv_nhwc(const __half* X, int B, int H, int W, int IC, const __half* Wp, in
   g.num_m_tiles = B * g.tiles_x * g.tiles_y;
   g.num_n_tiles = (OC + bn - 1) / bn;
   const bool two = want_2sm(g, bn);
+  if (!two && e.kind != kEpiOut2) g.ksplit = pick_ksplit(static_cast<long>(g.num_m_tiles) * g.num_n_tiles, g.num_kb, bn);
   CUtensorMap ta, tb, tc;
   if ((rc = make_tmap_nhwc(&ta, X, B, H, W, IC, bw, bh))) return rc - 100;
   if ((rc = make_tmap_2d(&tb, Wp, OC, ksize * ksize * icp, ksize * ksize * icp, two ? bn / 2 : bn))) return rc - 200;

@@ -51,6 +51,7 @@ struct GemmGeom {
   int ksize, pad;   // kernel size, padding (stride 1)
   int ic_chunks;    // ceil(IC / 64)
   int icp;          // padded per-tap channel stride of the packed weight (ic_chunks * 64)
+  int ksplit;       // 1-SM kernel: > 1 = a cluster of ksplit CTAs per tile, each a share of the k-blocks
 };
 
 struct EpiArgs {

@@ -209,6 +209,67 @@ def test_conv_nhwc(lib, B, H, W, IC, OC, ks):
     close(outr, ref.clamp_min(0))
 
 
+@pytest.mark.parametrize("case", ["linear", "gelu", "resid", "conv19", "conv37"])
+def test_gemm_ksplit(lib, case, monkeypatch):
+    """The 1-SM GEMM's K split: with few tiles and a long reduction a cluster of up to 4
+    CTAs takes each tile, and the first adds the others' partial accumulators (read over
+    distributed shared memory) into its own in rank order before the epilogue. Shapes of
+    one image's DPT head: the stride-2 conv as a GEMM (M = 361, K = 6912, N = 768: 36
+    tiles, 4 shares), and 3x3 convs through the implicit GEMM ($DA3B_CONV_HALO=0) at 19 x
+    19 from 768 channels and 37 x 37 from 384. Against torch fp32, and two runs are
+    bit-identical."""
+    g = torch.Generator(device="cuda").manual_seed(len(case))
+    outs = []
+    if case in ("linear", "gelu", "resid"):
+        M, K, N = 361, 6912, 768
+        x = torch.randn(M, K, device="cuda", generator=g).half()
+        w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+        b = torch.randn(N, device="cuda", generator=g).float()
+        ref = x.float() @ w.float().t() + b
+        if case == "resid":
+            sc = torch.randn(N, device="cuda", generator=g).float()
+            r0 = torch.randn(M, N, device="cuda", generator=g).float()
+            for _ in range(2):
+                r = r0.clone()
+                assert lib.da3b_linear_resid_f32(ptr(x), M, K, K, ptr(w), N, K, ptr(b), ptr(sc), ptr(r), N, stream()) == 0
+                outs.append(r)
+            ref = r0 + sc * ref
+            torch.cuda.synchronize()
+            assert lib.da3b_device_status() == 0
+            err = (outs[0] - ref).abs().max().item()
+            assert err <= 1e-3 * ref.abs().max().item() + 1e-4
+        else:
+            act = 2 if case == "gelu" else 0
+            for _ in range(2):
+                out = torch.empty(M, N, dtype=torch.float16, device="cuda")
+                assert lib.da3b_linear_f16(ptr(x), M, K, K, ptr(w), N, K, ptr(b), act, ptr(out), N, stream()) == 0
+                outs.append(out)
+            if act:
+                ref = torch.nn.functional.gelu(ref)
+            torch.cuda.synchronize()
+            assert lib.da3b_device_status() == 0
+            close(outs[0], ref)
+    else:
+        monkeypatch.setenv("DA3B_CONV_HALO", "0")
+        H, IC = (19, 768) if case == "conv19" else (37, 384)
+        OC = 128
+        x = torch.randn(1, H, H, IC, device="cuda", generator=g).half()
+        w = torch.randn(OC, IC, 3, 3, device="cuda", generator=g).float() * 0.02
+        b = torch.randn(OC, device="cuda", generator=g).float()
+        r1 = torch.randn(1, H, H, OC, device="cuda", generator=g).half()
+        wp = torch.empty(OC, 9, IC, dtype=torch.float16, device="cuda")
+        assert lib.da3b_pack_conv_weight(ptr(w), OC, IC, 3, ptr(wp), stream()) == 0
+        for _ in range(2):
+            out, outr = (torch.empty(1, H, H, OC, dtype=torch.float16, device="cuda") for _ in range(2))
+            _conv3(lib, x, wp, OC, b, r1, None, out, outr)
+            outs.append(out)
+        ref = torch.nn.functional.conv2d(x.permute(0, 3, 1, 2).float(), w.half().float(), b, padding=1)
+        ref = ref.permute(0, 2, 3, 1) + r1.float()
+        close(outs[0], ref)
+        close(outr, ref.clamp_min(0))
+    assert torch.equal(outs[0], outs[1])
+
+
 def _conv3(lib, x, wp, OC, b, r1, r2, out, outr, act=0):
     B, H, W, IC = x.shape
     rc = lib.da3b_conv_nhwc(ptr(x), B, H, W, IC, ptr(wp), OC, 3, ptr(b), ptr(r1), ptr(r2), act, ptr(out), ptr(outr),
@@ -220,7 +281,7 @@ def _conv3(lib, x, wp, OC, b, r1, r2, out, outr, act=0):
 
 @pytest.mark.parametrize("B,H,W,IC,OC", [(2, 37, 37, 256, 128), (1, 5, 9, 64, 128), (3, 17, 33, 128, 128),
                                          (1, 16, 16, 64, 128), (2, 74, 74, 256, 128), (1, 37, 37, 256, 256),
-                                         (2, 19, 21, 512, 256)])
+                                         (2, 19, 21, 512, 256), (1, 148, 148, 64, 128)])
 @pytest.mark.parametrize("pair", ["1", "0", ""], ids=["cta_pair", "one_cta", "auto"])
 def test_conv3_halo(lib, B, H, W, IC, OC, pair, monkeypatch):
     """3x3 convs through the halo-box kernel ($DA3B_CONV_HALO=1; by default it serves 128
@@ -231,8 +292,9 @@ def test_conv3_halo(lib, B, H, W, IC, OC, pair, monkeypatch):
     chunks and one or two output groups; in the CTA-pair form with two 8-wide halves
     per CTA for 128 outputs, one for 256 ($DA3B_CONV_HALO_PAIR=1; an odd number of pixel
     tiles leaves the last pair's second tile empty), the one-CTA form (=0), and the
-    automatic choice, which runs 128-output maps of at most one 16 x 16 tile per SM
-    as CTA pairs of one half each."""
+    automatic choice, which runs 128-output maps of between half and one 16 x 16 tile
+    per SM as CTA pairs of one half each (148 x 148) and leaves smaller ones to the
+    implicit GEMM."""
     if pair:
         monkeypatch.setenv("DA3B_CONV_HALO_PAIR", pair)
     else:
