@@ -535,8 +535,9 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
     // shared memory. The two give the same bits; the staging route is the faster at
     // one image (ViT-B: QKV 12.6 + 2.2 us against 18.1 us, fc1 14.6 + 2.7 against 20.3).
     const __half *w_qkv = b.qkv.w, *w_proj = b.proj.w, *w_fc1 = b.fc1.w, *w_fc2 = b.fc2.w;
-    const bool q8_tiles = m.q8_resident && q8_tiles_ && gemm_q8p_bn(M, b.qkv.N) && gemm_q8p_bn(M, b.proj.N) &&
-                          gemm_q8p_bn(M, b.fc1.N) && gemm_q8p_bn(M, b.fc2.N);
+    const bool q8_tiles = m.q8_resident && q8_tiles_ && gemm_q8p_bn(M, b.qkv.N, b.qkv.K) &&
+                          gemm_q8p_bn(M, b.proj.N, b.proj.K) && gemm_q8p_bn(M, b.fc1.N, b.fc1.K) &&
+                          gemm_q8p_bn(M, b.fc2.N, b.fc2.K);
     auto linear = [&](const __half* A, int lda, const Lin& L, const __half* w_f16, const EpiArgs& e) -> int {
       if (q8_tiles) return gemm_linear_q8p(A, M, L.K, lda, L.q8, L.N, e, status_, s);
       return gemm_linear(A, M, L.K, lda, w_f16, L.N, L.ldw, 0, e, status_, s);

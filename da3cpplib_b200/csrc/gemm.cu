@@ -17,6 +17,7 @@
 // Tiles are visited m-major (all N tiles of one 128-row A panel back to back) so an
 // A panel is read from HBM about once while the weights stay resident in L2.
 #include <algorithm>
+#include <cmath>
 #include <atomic>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -1614,6 +1615,57 @@ static int pick_ksplit(long tiles, int num_kb, int bn) {
   return ks >= 2 ? static_cast<int>(ks) : 1;
 }
 
+// Tile width and K split of a long-K linear on the 1-SM kernel (at least 32 k-blocks):
+// the candidates (64, 1), (128, 1) and (128, 2) scored by a model fitted to B200
+// measurements of such GEMMs at a few images' rows: waves x the larger of a CTA's
+// operand bytes at 75 GB/s and its share of all operand bytes at 7.5 TB/s (L2 -> SM
+// reads bound these shapes), plus about 2.9 us for summing a 128 x 128 f32 share. ViT-B
+// fc2 at one image (K = 3072, N = 768): (128, 2) 16.7 us against 20.4 for (64, 1);
+// ViT-L fc2 (K = 4096, N = 1024): (128, 1) 27.1 against 44.3; two ViT-B images: (128, 1)
+// 22.9 against 35.2.
+static void long_k_tile(int m_tiles, int N, int num_kb, int* bn_out, int* ks_out) {
+  const int cand[3][2] = {{64, 1}, {128, 1}, {128, 2}};
+  const double sms = num_sms();
+  double best = 1e30;
+  for (const auto& c : cand) {
+    const int bn = c[0], ks = c[1];
+    if (ks > 1 && !ksplit_enabled()) continue;
+    const double ctas = static_cast<double>(m_tiles) * ((N + bn - 1) / bn) * ks;
+    const double waves = std::ceil(ctas / sms);
+    const double cta_bytes = static_cast<double>(num_kb / ks) * (16384.0 + 128.0 * bn);
+    double t = std::max(waves * cta_bytes / 75e9, ctas * cta_bytes / 7.5e12);
+    if (ks > 1) t += 2.9e-6 * (bn / 128.0) * (ks - 1);
+    if (t < best * 0.98) {
+      best = t;
+      *bn_out = bn;
+      *ks_out = ks;
+    }
+  }
+}
+
+// The automatic tiles of a linear (f16 or fused-Q8_0 weights, not the out2 stage):
+// false for the CTA-pair kernel (bn = its tile width), true for the 1-SM kernel with
+// tile width bn and K split ks.
+static bool auto_linear_tile(int M, int N, int K, int* bn_out, int* ks_out) {
+  GemmGeom g;
+  memset(&g, 0, sizeof(g));
+  g.num_kb = (K + 63) / 64;
+  g.num_m_tiles = (M + 127) / 128;
+  int bn = pick_bn(N);
+  g.num_n_tiles = (N + bn - 1) / bn;
+  *ks_out = 1;
+  if (want_2sm(g, bn)) {
+    *bn_out = bn;
+    return false;
+  }
+  bn = narrow_1sm_bn(g.num_m_tiles, N, bn);
+  int ks = pick_ksplit(static_cast<long>(g.num_m_tiles) * ((N + bn - 1) / bn), g.num_kb, bn);
+  if (g.num_kb >= 32 && bn <= 128 && ks <= 1) long_k_tile(g.num_m_tiles, N, g.num_kb, &bn, &ks);
+  *bn_out = bn;
+  *ks_out = ks;
+  return true;
+}
+
 int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, int ldw, int bn, const EpiArgs& e,
                 int* status, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return M == 0 ? 0 : -30;
@@ -1632,12 +1684,17 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
   g.num_kb = (K + 63) / 64;
   g.num_m_tiles = (M + 127) / 128;
   g.num_n_tiles = (N + bn - 1) / bn;
-  const bool two = want_2sm(g, bn);
-  if (auto_bn && !two && e.kind != kEpiOut2) {
-    bn = narrow_1sm_bn(g.num_m_tiles, N, bn);
+  bool two = want_2sm(g, bn);
+  if (e.kind != kEpiOut2) {
+    if (auto_bn) {
+      int ks = 1;
+      two = !auto_linear_tile(M, N, K, &bn, &ks);
+      g.ksplit = ks;
+    } else if (!two) {
+      g.ksplit = pick_ksplit(static_cast<long>(g.num_m_tiles) * g.num_n_tiles, g.num_kb, bn);
+    }
     g.num_n_tiles = (N + bn - 1) / bn;
   }
-  if (!two && e.kind != kEpiOut2) g.ksplit = pick_ksplit(static_cast<long>(g.num_m_tiles) * g.num_n_tiles, g.num_kb, bn);
   CUtensorMap ta, tb, tc;
   if ((rc = make_tmap_2d(&ta, A, M, K, lda, 128))) return rc - 100;
   if ((rc = make_tmap_2d(&tb, W, N, K, ldw, two ? bn / 2 : bn))) return rc - 200;
@@ -1664,16 +1721,12 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
 // Tile width the planar Q8_0 GEMM (k_tc_gemm<BN, true>) takes for an M x N linear, or 0
 // when the problem is one for the CTA-pair kernel (many rows), whose weights are then
 // better dequantised once per ViT block into f16 than once per 256-row tile pair.
-int gemm_q8p_bn(int M, int N) {
-  if (M <= 0 || N <= 0 || N % 8) return 0;
-  GemmGeom g;
-  memset(&g, 0, sizeof(g));
-  g.num_m_tiles = (M + 127) / 128;
-  int bn = pick_bn(N);
-  g.num_n_tiles = (N + bn - 1) / bn;
-  if (want_2sm(g, bn)) return 0;
-  bn = narrow_1sm_bn(g.num_m_tiles, N, bn);
-  return (bn == 64 || bn == 128) ? bn : 0;
+int gemm_q8p_bn(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0 || N % 8) return 0;
+  int bn = 0, ks = 1;
+  if (!auto_linear_tile(M, N, K, &bn, &ks)) return 0;  // CTA pairs
+  // the same tiles as the f16 route (so the two give the same bits); no K split there
+  return ks == 1 && (bn == 64 || bn == 128) ? bn : 0;
 }
 
 int gemm_linear_q8p(const __half* A, int M, int K, int lda, const uint8_t* Wq, int N, const EpiArgs& e, int* status,
@@ -1681,7 +1734,7 @@ int gemm_linear_q8p(const __half* A, int M, int K, int lda, const uint8_t* Wq, i
   if (M <= 0 || N <= 0 || K <= 0) return M == 0 ? 0 : -30;
   if (lda < K || lda % 8 || K % 32 || N % 8 || (reinterpret_cast<uintptr_t>(Wq) & 15) || e.kind == kEpiOut2)
     return -31;
-  const int bn = gemm_q8p_bn(M, N);
+  const int bn = gemm_q8p_bn(M, N, K);
   if (!bn) return 1;
   int rc = check_epi(e, N);
   if (rc) return rc;

@@ -23,9 +23,10 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
                 int* status, cudaStream_t stream);
 // The same with W planar Q8_0 [N][K] (q8planar.cuh; K % 32 == 0, N % 8 == 0): the GEMM
 // dequantises its weight tiles in shared memory, f16(d * q) as the staging dequantisation
-// gives. Serves the one-CTA tile regime only (gemm_q8p_bn(M, N) != 0, the tile width it
-// takes); returns 1 without launching otherwise.
-int gemm_q8p_bn(int M, int N);
+// gives. Serves the one-CTA tile regime without K split only (gemm_q8p_bn(M, N, K) != 0,
+// the tile width it takes, the same as the f16 route's); returns 1 without launching
+// otherwise.
+int gemm_q8p_bn(int M, int N, int K);
 int gemm_linear_q8p(const __half* A, int M, int K, int lda, const uint8_t* Wq, int N, const EpiArgs& e, int* status,
                     cudaStream_t stream);
 // Implicit-GEMM KxK stride-1 "same" convolution: X NHWC [B][H][W][IC] f16,
