@@ -1615,25 +1615,28 @@ static int pick_ksplit(long tiles, int num_kb, int bn) {
   return ks >= 2 ? static_cast<int>(ks) : 1;
 }
 
-// Tile width and K split of a long-K linear on the 1-SM kernel (at least 32 k-blocks):
-// the candidates (64, 1), (128, 1) and (128, 2) scored by a model fitted to B200
-// measurements of such GEMMs at a few images' rows: waves x the larger of a CTA's
-// operand bytes at 75 GB/s and its share of all operand bytes at 7.5 TB/s (L2 -> SM
-// reads bound these shapes), plus about 2.9 us for summing a 128 x 128 f32 share. ViT-B
-// fc2 at one image (K = 3072, N = 768): (128, 2) 16.7 us against 20.4 for (64, 1);
-// ViT-L fc2 (K = 4096, N = 1024): (128, 1) 27.1 against 44.3; two ViT-B images: (128, 1)
-// 22.9 against 35.2.
-static void long_k_tile(int m_tiles, int N, int num_kb, int* bn_out, int* ks_out) {
-  const int cand[3][2] = {{64, 1}, {128, 1}, {128, 2}};
+// Tile width and K split of a linear on the 1-SM kernel: the candidates (64, 1),
+// (128, 1), (256, 1) and, with at least 32 k-blocks, (128, 2), scored by a model fitted
+// to B200 measurements at a few images' rows, where reading the operands from L2 bounds
+// these GEMMs: waves x the larger of a CTA's operand bytes at 75 GB/s and its MMA time,
+// against all operand bytes at 7.5 TB/s, plus about 2.9 us for summing a 128 x 128 f32
+// share. One ViT-B image: QKV (N = 2304) 256-wide tiles 10.4 us against 13.2 for 128 (198
+// tiles are two waves), fc1 + GELU 13.6 against 15.2, proj 64-wide 8.1 against 10.2 for
+// 256; fc2 (K = 3072) (128, 2) 16.7 against 20.4 for (64, 1); ViT-L fc2 (K = 4096) (128,
+// 1) 27.1 against 44.3; two ViT-B images' fc2 (128, 1) 22.9 against 35.2.
+static void model_1sm_tile(int m_tiles, int N, int num_kb, int* bn_out, int* ks_out) {
+  const int cand[4][2] = {{64, 1}, {128, 1}, {256, 1}, {128, 2}};
   const double sms = num_sms();
   double best = 1e30;
   for (const auto& c : cand) {
     const int bn = c[0], ks = c[1];
-    if (ks > 1 && !ksplit_enabled()) continue;
+    if (ks > 1 && (num_kb < 32 || !ksplit_enabled())) continue;
     const double ctas = static_cast<double>(m_tiles) * ((N + bn - 1) / bn) * ks;
     const double waves = std::ceil(ctas / sms);
-    const double cta_bytes = static_cast<double>(num_kb / ks) * (16384.0 + 128.0 * bn);
-    double t = std::max(waves * cta_bytes / 75e9, ctas * cta_bytes / 7.5e12);
+    const double kbs = static_cast<double>(num_kb / ks);
+    const double cta_bytes = kbs * (16384.0 + 128.0 * bn);
+    const double mma = kbs * 4 * (bn >= 256 ? 128 : 64) / 1.9e9;
+    double t = std::max(waves * std::max(cta_bytes / 75e9, mma), ctas * cta_bytes / 7.5e12);
     if (ks > 1) t += 2.9e-6 * (bn / 128.0) * (ks - 1);
     if (t < best * 0.98) {
       best = t;
@@ -1658,9 +1661,11 @@ static bool auto_linear_tile(int M, int N, int K, int* bn_out, int* ks_out) {
     *bn_out = bn;
     return false;
   }
+  // few tiles with a long reduction: the narrowest tiles and the cluster K split
+  // (measured on one image's stride-2 conv); otherwise the fitted model
   bn = narrow_1sm_bn(g.num_m_tiles, N, bn);
   int ks = pick_ksplit(static_cast<long>(g.num_m_tiles) * ((N + bn - 1) / bn), g.num_kb, bn);
-  if (g.num_kb >= 32 && bn <= 128 && ks <= 1) long_k_tile(g.num_m_tiles, N, g.num_kb, &bn, &ks);
+  if (ks <= 1) model_1sm_tile(g.num_m_tiles, N, g.num_kb, &bn, &ks);
   *bn_out = bn;
   *ks_out = ks;
   return true;
