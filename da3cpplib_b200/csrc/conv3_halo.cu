@@ -561,7 +561,7 @@ int launch_halo2(const __half* X, int B, int H, int W, int IC, const __half* Wp,
 // covers, so the caller can take the implicit-GEMM path; 0 on launch; < 0 on error.
 int conv3_halo(const __half* X, int B, int H, int W, int IC, const __half* Wp, int OC, const EpiArgs& e, int* status,
                cudaStream_t s) {
-  if (OC % kOCh || OC <= 0 || IC % 64 || IC <= 0 || B <= 0 || H <= 0 || W <= 0) return 1;
+  if ((OC % kOCh && OC != 64) || OC <= 0 || IC % 64 || IC <= 0 || B <= 0 || H <= 0 || W <= 0) return 1;
   if (e.kind != kEpiF16 || e.q8 || e.rm_div || (e.res1 && e.res1_mod) || e.ld_out != OC ||
       (e.act != kActNone && e.act != kActRelu))
     return 1;
@@ -592,10 +592,17 @@ int conv3_halo(const __half* X, int B, int H, int W, int IC, const __half* Wp, i
   if (sms >= 2 && pmode != 0) {
     if (OC % 256 == 0) return launch_halo2<256, 1>(X, B, H, W, IC, Wp, OC, e, status, s, sms);
     if (OC == 128 && pmode == 1) return launch_halo2<128, 2>(X, B, H, W, IC, Wp, OC, e, status, s, sms);
+    // 64 outputs (one image's out1, 128 -> 64 at 296 x 296): CTA pairs with two halves
+    // of N = 64 per CTA on maps of more 16 x 16 tiles than SMs
+    if (OC == 64) {
+      const long t16 = static_cast<long>(B) * ((W + 15) / 16) * ((H + 15) / 16);
+      return (t16 > sms || pmode == 1) ? launch_halo2<64, 2>(X, B, H, W, IC, Wp, OC, e, status, s, sms) : 1;
+    }
     const long tiles16 = static_cast<long>(B) * ((W + 15) / 16) * ((H + 15) / 16);
     if (OC == 128 && 2 * tiles16 <= sms) return 1;
     if (OC == 128 && tiles16 <= sms) return launch_halo2<128, 1>(X, B, H, W, IC, Wp, OC, e, status, s, sms);
   }
+  if (OC % kOCh) return 1;  // the one-CTA form serves groups of 128 outputs only
   const int icp = conv_icp(IC);
   CUtensorMap ta, tb;
   int rc;

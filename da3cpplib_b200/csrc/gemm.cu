@@ -1792,7 +1792,7 @@ int conv_nhwc(const __half* X, int B, int H, int W, int IC, const __half* Wp, in
     // $DA3B_CONV_HALO=0 never takes it, =1 also for other multiples of 128.
     const char* ev = getenv("DA3B_CONV_HALO");
     const int mode = ev && ev[0] == '0' ? 0 : (ev && ev[0] == '1' ? 2 : 1);
-    if (mode == 2 || (mode == 1 && (OC == 128 || OC % 256 == 0))) {
+    if (mode == 2 || (mode == 1 && (OC == 64 || OC == 128 || OC % 256 == 0))) {
       rc = conv3_halo(X, B, H, W, IC, Wp, OC, e, status, stream);
       if (rc != 1) return rc;
     }

@@ -287,7 +287,8 @@ def _conv3(lib, x, wp, OC, b, r1, r2, out, outr, act=0):
 
 @pytest.mark.parametrize("B,H,W,IC,OC", [(2, 37, 37, 256, 128), (1, 5, 9, 64, 128), (3, 17, 33, 128, 128),
                                          (1, 16, 16, 64, 128), (2, 74, 74, 256, 128), (1, 37, 37, 256, 256),
-                                         (2, 19, 21, 512, 256), (1, 148, 148, 64, 128)])
+                                         (2, 19, 21, 512, 256), (1, 148, 148, 64, 128), (1, 296, 296, 128, 64),
+                                         (2, 150, 150, 64, 64), (1, 37, 37, 128, 64)])
 @pytest.mark.parametrize("pair", ["1", "0", ""], ids=["cta_pair", "one_cta", "auto"])
 def test_conv3_halo(lib, B, H, W, IC, OC, pair, monkeypatch):
     """3x3 convs through the halo-box kernel ($DA3B_CONV_HALO=1; by default it serves 128
@@ -300,7 +301,9 @@ def test_conv3_halo(lib, B, H, W, IC, OC, pair, monkeypatch):
     tiles leaves the last pair's second tile empty), the one-CTA form (=0), and the
     automatic choice, which runs 128-output maps of between half and one 16 x 16 tile
     per SM as CTA pairs of one half each (148 x 148) and leaves smaller ones to the
-    implicit GEMM."""
+    implicit GEMM. 64 outputs: CTA pairs with two halves of N = 64 per CTA on maps of
+    more tiles than SMs (one image's out1 at 296 x 296) or when forced, the implicit
+    GEMM otherwise."""
     if pair:
         monkeypatch.setenv("DA3B_CONV_HALO_PAIR", pair)
     else:
