@@ -82,33 +82,14 @@ int repack_q8_0_planar(const void* raw, int N, int K, void* planar, cudaStream_t
 // of the q plane, its block's scale, two 16-byte stores), consecutive threads
 // consecutive pieces, so every load and store of a warp is one contiguous run.
 __global__ void __launch_bounds__(256) k_dequant_q8p_segs(Q8Segs g) {
-  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
-  for (int k = 0; k < g.n; ++k) {
-    const Q8Seg& sg = g.s[k];
-    const int K = sg.nblk * 32, per_row = K / 16;
-    const long units = static_cast<long>(sg.rows) * per_row;
-    const __half* dplane = reinterpret_cast<const __half*>(sg.q8 + static_cast<size_t>(sg.rows) * K);
-    for (long u = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; u < units; u += stride) {
-      const int n = static_cast<int>(u / per_row), j = static_cast<int>(u % per_row);
-      const uint4 q = __ldg(reinterpret_cast<const uint4*>(sg.q8 + static_cast<size_t>(n) * K + 16 * j));
-      const __half d = dplane[static_cast<size_t>(j >> 1) * sg.rows + n];
-      const __half2 d2 = __halves2half2(d, d);
-      uint4* dst = reinterpret_cast<uint4*>(sg.out + static_cast<size_t>(n) * K + 16 * j);
-      dst[0] = q8x8_to_f16x8(make_uint2(q.x, q.y), d2);
-      dst[1] = q8x8_to_f16x8(make_uint2(q.z, q.w), d2);
-    }
-  }
+  q8p_segs_dequant(g, static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x, static_cast<long>(gridDim.x) * blockDim.x);
 }
 
 int dequant_q8p_segs(const Q8Segs& g, cudaStream_t s) {
   if (g.n <= 0 || g.n > 4 || g.total <= 0) return -1;
-  long units = 0;
-  for (int k = 0; k < g.n; ++k) {
+  for (int k = 0; k < g.n; ++k)
     if (reinterpret_cast<uintptr_t>(g.s[k].q8) & 15 || reinterpret_cast<uintptr_t>(g.s[k].out) & 15) return -2;
-    units = std::max(units, static_cast<long>(g.s[k].rows) * g.s[k].nblk * 2);
-  }
-  long blocks = (units + 255) / 256;
-  if (blocks > 148 * 8) blocks = 148 * 8;
+  const long blocks = q8p_segs_blocks(g);
   k_dequant_q8p_segs<<<static_cast<unsigned>(blocks), 256, 0, s>>>(g);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

@@ -529,8 +529,8 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
   for (int i = 0; i < c.depth; ++i) {
     const Block& b = m.blk[i];
     // this block's linears: the resident f16 planes; or, resident as planar Q8_0,
-    // dequantised into the staging buffer (in stream order after the previous block's
-    // last GEMM) for the f16 GEMMs (default), or ($DA3B_Q8_TILES=1, few rows: every
+    // dequantised into the staging buffer by the LN1 launch (in stream order after the
+    // previous block's last GEMM) for the f16 GEMMs (default), or ($DA3B_Q8_TILES=1, few rows: every
     // linear on one-CTA tiles) read by GEMMs that dequantise their weight tiles in
     // shared memory. The two give the same bits; the staging route is the faster at
     // one image (ViT-B: QKV 12.6 + 2.2 us against 18.1 us, fc1 14.6 + 2.7 against 20.3).
@@ -542,8 +542,9 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
       if (q8_tiles) return gemm_linear_q8p(A, M, L.K, lda, L.q8, L.N, e, status_, s);
       return gemm_linear(A, M, L.K, lda, w_f16, L.N, L.ldw, 0, e, status_, s);
     };
+    Q8Segs g;
+    memset(&g, 0, sizeof(g));
     if (m.q8_resident && !q8_tiles) {
-      Q8Segs g;
       const Lin* L4[4] = {&b.qkv, &b.proj, &b.fc1, &b.fc2};
       const __half** ptrs[4] = {&w_qkv, &w_proj, &w_fc1, &w_fc2};
       __half* dst = wstage_;
@@ -556,7 +557,6 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
       }
       g.n = 4;
       g.total = first;
-      CK(dequant_q8p_segs(g, s));
     }
     if (select && i == c.alt_start - 1) {
       // reference-view selection on the views' token 0 after blocks [0, alt_start-1)
@@ -571,7 +571,8 @@ int Engine::backbone(Plan& p, cudaStream_t s) {
     const bool use_rope = c.rope_start >= 0 && i >= c.rope_start;
     // ---- attention half
     const int q8 = act_quant_ ? 1 : 0;
-    CK(layernorm_f32(p.x, D, M, D, b.n1g, b.n1b, c.ln_eps, p.xn, D, 0, 0, 0, 0, s, q8));
+    // LN1, with this block's staging dequantisation in the same launch
+    CK(layernorm_f32(p.x, D, M, D, b.n1g, b.n1b, c.ln_eps, p.xn, D, 0, 0, 0, 0, s, q8, g.n ? &g : nullptr));
     const int seqlen = global ? p.S * Nt : Nt, nseq = global ? p.scenes : V;
     const int ld_vt = global ? p.ld_vt_global : p.ld_vt_local;
     {

@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include "kernels.h"
+#include "q8planar.cuh"
 
 namespace da3b {
 
@@ -122,10 +123,10 @@ __global__ void k_layernorm(const Tin* __restrict__ in, int ld_in, int rows, int
 // slot (e / 256) * 8 + e % 8): 32-byte f32 / 16-byte f16 loads, gamma and beta as
 // float4 pairs, one 16-byte store per 8 outputs. For D a multiple of 256.
 template <typename Tin, int VPL>
-__global__ void k_layernorm8(const Tin* __restrict__ in, int ld_in, int rows, int D, const float* __restrict__ g,
-                             const float* __restrict__ bta, float eps, __half* __restrict__ out, int ld_out,
-                             int col_off, int rm_div, int rm_mul, int rm_add, int q8) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+__device__ __forceinline__ void ln8_row(int warp, const Tin* __restrict__ in, int ld_in, int rows, int D,
+                                        const float* __restrict__ g, const float* __restrict__ bta, float eps,
+                                        __half* __restrict__ out, int ld_out, int col_off, int rm_div, int rm_mul,
+                                        int rm_add, int q8) {
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const int in_row = rm_div > 0 ? (warp / rm_div) * rm_mul + rm_add + warp % rm_div : warp;
@@ -202,15 +203,63 @@ __global__ void k_layernorm8(const Tin* __restrict__ in, int ld_in, int rows, in
   }
 }
 
+template <typename Tin, int VPL>
+__global__ void k_layernorm8(const Tin* __restrict__ in, int ld_in, int rows, int D, const float* __restrict__ g,
+                             const float* __restrict__ bta, float eps, __half* __restrict__ out, int ld_out,
+                             int col_off, int rm_div, int rm_mul, int rm_add, int q8) {
+  ln8_row<Tin, VPL>((blockIdx.x * blockDim.x + threadIdx.x) >> 5, in, ld_in, rows, D, g, bta, eps, out, ld_out,
+                    col_off, rm_div, rm_mul, rm_add, q8);
+}
+
+// The same LayerNorm in blocks [0, ln_blocks) and the staging dequantisation of a ViT
+// block's planar Q8_0 linears in the blocks after: two independent memory-bound passes
+// that each take a few microseconds at one image, in one launch.
+template <int VPL>
+__global__ void k_layernorm8_dq(const float* __restrict__ in, int ld_in, int rows, int D, const float* __restrict__ g,
+                                const float* __restrict__ bta, float eps, __half* __restrict__ out, int ld_out,
+                                int col_off, int rm_div, int rm_mul, int rm_add, int q8, const Q8Segs dq,
+                                unsigned ln_blocks) {
+  if (blockIdx.x < ln_blocks) {
+    ln8_row<float, VPL>((blockIdx.x * blockDim.x + threadIdx.x) >> 5, in, ld_in, rows, D, g, bta, eps, out, ld_out,
+                        col_off, rm_div, rm_mul, rm_add, q8);
+  } else {
+    q8p_segs_dequant(dq, static_cast<long>(blockIdx.x - ln_blocks) * blockDim.x + threadIdx.x,
+                     static_cast<long>(gridDim.x - ln_blocks) * blockDim.x);
+  }
+}
+
 template <typename Tin>
 static int ln_dispatch(const Tin* in, int ld_in, int rows, int D, const float* g, const float* b, float eps,
                        __half* out, int ld_out, int col_off, int rm_div, int rm_mul, int rm_add, int q8,
-                       cudaStream_t s) {
-  if (rows <= 0) return 0;
+                       cudaStream_t s, const Q8Segs* dq = nullptr) {
+  if (rows <= 0) return dq ? dequant_q8p_segs(*dq, s) : 0;
   const unsigned blocks = static_cast<unsigned>((static_cast<long>(rows) * 32 + 255) / 256);
   const bool wide = D % 256 == 0 && D <= 2048 && ld_in % 8 == 0 && ld_out % 8 == 0 && col_off % 8 == 0 &&
                     (reinterpret_cast<uintptr_t>(in) & 31) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
                     (reinterpret_cast<uintptr_t>(g) & 15) == 0 && (reinterpret_cast<uintptr_t>(b) & 15) == 0;
+  if (wide && dq && sizeof(Tin) == 4) {
+    for (int k = 0; k < dq->n; ++k)
+      if (reinterpret_cast<uintptr_t>(dq->s[k].q8) & 15 || reinterpret_cast<uintptr_t>(dq->s[k].out) & 15) return -3;
+    const unsigned total = blocks + static_cast<unsigned>(q8p_segs_blocks(*dq));
+    const float* fin = reinterpret_cast<const float*>(in);
+#define DA3B_LN8DQ(VPL)                                                                                           \
+  k_layernorm8_dq<VPL><<<total, 256, 0, s>>>(fin, ld_in, rows, D, g, b, eps, out, ld_out, col_off, rm_div, rm_mul, \
+                                            rm_add, q8, *dq, blocks)
+    switch (D) {
+      case 256: DA3B_LN8DQ(8); break;
+      case 512: DA3B_LN8DQ(16); break;
+      case 768: DA3B_LN8DQ(24); break;
+      case 1024: DA3B_LN8DQ(32); break;
+      case 1536: DA3B_LN8DQ(48); break;
+      case 2048: DA3B_LN8DQ(64); break;
+      default: return -1;
+    }
+#undef DA3B_LN8DQ
+    return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  }
+  if (dq) {
+    if (int rc = dequant_q8p_segs(*dq, s)) return rc;
+  }
   if (wide) {
 #define DA3B_LN8(VPL)                                                                                          \
   k_layernorm8<Tin, VPL><<<blocks, 256, 0, s>>>(in, ld_in, rows, D, g, b, eps, out, ld_out, col_off, rm_div, rm_mul, \
@@ -246,8 +295,9 @@ static int ln_dispatch(const Tin* in, int ld_in, int rows, int D, const float* g
 }
 
 int layernorm_f32(const float* in, int ld_in, int rows, int D, const float* g, const float* b, float eps, __half* out,
-                  int ld_out, int col_off, int rm_div, int rm_mul, int rm_add, cudaStream_t s, int q8) {
-  return ln_dispatch<float>(in, ld_in, rows, D, g, b, eps, out, ld_out, col_off, rm_div, rm_mul, rm_add, q8, s);
+                  int ld_out, int col_off, int rm_div, int rm_mul, int rm_add, cudaStream_t s, int q8,
+                  const Q8Segs* dq) {
+  return ln_dispatch<float>(in, ld_in, rows, D, g, b, eps, out, ld_out, col_off, rm_div, rm_mul, rm_add, q8, s, dq);
 }
 int layernorm_f16(const __half* in, int ld_in, int rows, int D, const float* g, const float* b, float eps,
                   __half* out, int ld_out, int col_off, int rm_div, int rm_mul, int rm_add, cudaStream_t s) {

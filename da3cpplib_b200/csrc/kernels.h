@@ -21,8 +21,12 @@ int cam_rows(float* x, int nviews_total, int views_per_scene, int ntok, int D, c
 // is (r / rm_div) * rm_mul + rm_add + r % rm_div when rm_div > 0.
 // q8 = 1: Q8_0 round trip of each 32-element block of the output (ggml activation
 // quantisation ahead of a Q8_0 matmul).
+// dq (or null): a ViT block's planar Q8_0 staging dequantisation (ops.h), run by the
+// same launch as the LayerNorm where the wide kernel serves it, else just before it.
+struct Q8Segs;
 int layernorm_f32(const float* in, int ld_in, int rows, int D, const float* g, const float* b, float eps, __half* out,
-                  int ld_out, int col_off, int rm_div, int rm_mul, int rm_add, cudaStream_t s, int q8 = 0);
+                  int ld_out, int col_off, int rm_div, int rm_mul, int rm_add, cudaStream_t s, int q8 = 0,
+                  const Q8Segs* dq = nullptr);
 int layernorm_f16(const __half* in, int ld_in, int rows, int D, const float* g, const float* b, float eps,
                   __half* out, int ld_out, int col_off, int rm_div, int rm_mul, int rm_add, cudaStream_t s);
 int cast_rows(const float* in, int ld_in, int rows, int D, __half* out, int ld_out, int col_off, int rm_div, int rm_mul,

@@ -15,6 +15,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "ops.h"
+
 namespace da3b {
 
 // Bytes of a planar Q8_0 matrix (the same as its GGUF Q8_0 bytes).
@@ -42,6 +44,39 @@ __device__ __forceinline__ uint4 q8x8_to_f16x8(uint2 raw, __half2 d2) {
     o[i] = *reinterpret_cast<const uint32_t*>(&v);
   }
   return out;
+}
+
+// Up to four planar Q8_0 matrices -> dense f16, thread `tid` of `nthreads` (grid-stride):
+// a thread takes 16 consecutive weights of a row (one 16-byte load of the q plane, its
+// block's scale, two 16-byte stores), consecutive threads consecutive pieces, so every
+// load and store of a warp is one contiguous run.
+__device__ __forceinline__ void q8p_segs_dequant(const Q8Segs& g, long tid, long nthreads) {
+  for (int k = 0; k < g.n; ++k) {
+    const Q8Seg& sg = g.s[k];
+    const int K = sg.nblk * 32, per_row = K / 16;
+    const long units = static_cast<long>(sg.rows) * per_row;
+    const __half* dplane = reinterpret_cast<const __half*>(sg.q8 + static_cast<size_t>(sg.rows) * K);
+    for (long u = tid; u < units; u += nthreads) {
+      const int n = static_cast<int>(u / per_row), j = static_cast<int>(u % per_row);
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(sg.q8 + static_cast<size_t>(n) * K + 16 * j));
+      const __half d = dplane[static_cast<size_t>(j >> 1) * sg.rows + n];
+      const __half2 d2 = __halves2half2(d, d);
+      uint4* dst = reinterpret_cast<uint4*>(sg.out + static_cast<size_t>(n) * K + 16 * j);
+      dst[0] = q8x8_to_f16x8(make_uint2(q.x, q.y), d2);
+      dst[1] = q8x8_to_f16x8(make_uint2(q.z, q.w), d2);
+    }
+  }
+}
+
+// Grid blocks of the staging dequantisation of g (256 threads each).
+inline long q8p_segs_blocks(const Q8Segs& g) {
+  long units = 0;
+  for (int k = 0; k < g.n; ++k) {
+    const long u = static_cast<long>(g.s[k].rows) * g.s[k].nblk * 2;
+    units = u > units ? u : units;
+  }
+  long blocks = (units + 255) / 256;
+  return blocks > 148 * 8 ? 148 * 8 : blocks;
 }
 
 }  // namespace da3b
