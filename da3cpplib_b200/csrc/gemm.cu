@@ -1617,10 +1617,11 @@ static int pick_ksplit(long tiles, int num_kb, int bn) {
 
 // Tile width and K split of a linear on the 1-SM kernel: the candidates (64, 1),
 // (128, 1), (256, 1) and, with at least 32 k-blocks, (128, 2), scored by a model fitted
-// to B200 measurements at a few images' rows, where reading the operands from L2 bounds
-// these GEMMs: waves x the larger of a CTA's operand bytes at 75 GB/s and its MMA time,
-// against all operand bytes at 7.5 TB/s, plus about 2.9 us for summing a 128 x 128 f32
-// share. One ViT-B image: QKV (N = 2304) 256-wide tiles 10.4 us against 13.2 for 128 (198
+// to B200 measurements at a few images' rows, where each SM's operand stream (its TMA
+// ring against the latency of L2 reads) bounds these GEMMs: waves x the larger of a
+// CTA's operand bytes at 75 GB/s and its MMA time, against all operand bytes at 7.5
+// TB/s, plus about 2.9 us for summing a 128 x 128 f32 share. The rates are fitted to
+// timings, not hardware limits (ncu at fc2's shape: L2 throughput 17%, tensor pipe 14%). One ViT-B image: QKV (N = 2304) 256-wide tiles 10.4 us against 13.2 for 128 (198
 // tiles are two waves), fc1 + GELU 13.6 against 15.2, proj 64-wide 8.1 against 10.2 for
 // 256; fc2 (K = 3072) (128, 2) 16.7 against 20.4 for (64, 1); ViT-L fc2 (K = 4096) (128,
 // 1) 27.1 against 44.3; two ViT-B images' fc2 (128, 1) 22.9 against 35.2.
