@@ -36,6 +36,7 @@ SIGNATURES = {
     "da3b_debug_wait_timeout": (c_int, [ctypes.c_ulonglong, c_int, c_void_p, c_void_p, c_void_p]),
     "da3b_debug_mma_cycles": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "da3b_set_attention_split": (c_int, [c_int]),
+    "da3b_linear_tiles": (c_int, [c_int, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     "da3b_repack_q8_0_planar": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "da3b_dequant_q8p": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "da3b_linear_q8p_f16": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int,

@@ -289,6 +289,10 @@ DA3B_API int da3b_debug_mma_cycles(int n, int a_tmem, int iters, int ctas, unsig
   return -100;
 }
 
+DA3B_API int da3b_linear_tiles(int M, int N, int K, int* bn, int* ksplit) {
+  return gemm_linear_tiles(M, N, K, bn, ksplit);
+}
+
 DA3B_API int da3b_set_attention_split(int n) {
   set_attention_split(n);
   return 0;

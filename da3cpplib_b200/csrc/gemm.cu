@@ -1727,6 +1727,11 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
 // Tile width the planar Q8_0 GEMM (k_tc_gemm<BN, true>) takes for an M x N linear, or 0
 // when the problem is one for the CTA-pair kernel (many rows), whose weights are then
 // better dequantised once per ViT block into f16 than once per 256-row tile pair.
+int gemm_linear_tiles(int M, int N, int K, int* bn, int* ksplit) {
+  if (M <= 0 || N <= 0 || K <= 0 || !bn || !ksplit) return -1;
+  return auto_linear_tile(M, N, K, bn, ksplit) ? 1 : 0;
+}
+
 int gemm_q8p_bn(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0 || N % 8) return 0;
   int bn = 0, ks = 1;

@@ -27,6 +27,9 @@ int gemm_linear(const __half* A, int M, int K, int lda, const __half* W, int N, 
 // the tile width it takes, the same as the f16 route's); returns 1 without launching
 // otherwise.
 int gemm_q8p_bn(int M, int N, int K);
+// The automatic tiles of an M x N x K linear: 1 = the one-CTA kernel with tile width bn
+// and K split ksplit, 0 = CTA pairs with tile width bn, < 0 = bad arguments. Host only.
+int gemm_linear_tiles(int M, int N, int K, int* bn, int* ksplit);
 int gemm_linear_q8p(const __half* A, int M, int K, int lda, const uint8_t* Wq, int N, const EpiArgs& e, int* status,
                     cudaStream_t stream);
 // Implicit-GEMM KxK stride-1 "same" convolution: X NHWC [B][H][W][IC] f16,

@@ -130,6 +130,14 @@ DA3B_API int da3b_debug_mma_cycles(int n, int a_tmem, int iters, int ctas, unsig
  * sequence has that many 64-key tiles. For tests and measurement; returns 0. */
 DA3B_API int da3b_set_attention_split(int n);
 
+/* The tiles da3b_linear_f16 / da3b_linear_resid_f32 choose for an M x N x K linear (host
+ * only, no GPU work): returns 1 for the one-CTA kernel with tile width *bn and K split
+ * *ksplit (a cluster of that many CTAs per tile), 0 for CTA pairs of tile width *bn,
+ * negative for bad arguments. The one-CTA choice comes from a cost model fitted to B200
+ * timings at a few images' rows (one ViT-B image: QKV and fc1 on 256-wide tiles, fc2 on
+ * 128-wide tiles split in two, attn proj on 64-wide tiles). */
+DA3B_API int da3b_linear_tiles(int M, int N, int K, int* bn, int* ksplit);
+
 /* The two halves of da3b_attention, for callers that keep V transposed (the engine's
  * QKV GEMM epilogue writes it that way): da3b_transpose_v writes V^T f16
  * [nseq][heads][64][ld_vt] (ld_vt >= seqlen, a multiple of 8; columns beyond seqlen are
