@@ -1586,8 +1586,8 @@ static int check_epi(const EpiArgs& e, int N) {
 }
 
 // Few rows (one image: M = 1370): with too few CTA-pair tiles for the SMs the GEMM runs
-// on one-CTA tiles; narrower ones then keep more SMs busy (a ViT-B fc2 of N = 768 has 33
-// tiles of 128 x 256 but 132 of 128 x 64).
+// on one-CTA tiles, narrowed until they outnumber the SMs or are 64 wide. The K split's
+// few-tile rule starts from this width; otherwise the fitted model below picks the tiles.
 static int narrow_1sm_bn(int m_tiles, int N, int bn) {
   while (bn > 64 && static_cast<long>(m_tiles) * ((N + bn - 1) / bn) < num_sms()) bn /= 2;
   return bn;
